@@ -1,0 +1,90 @@
+// hb_arith.cuh -- 64-bit RNS modular arithmetic for sm_100a.
+//
+// Every residue is a uint64 in [0, q) with q < 2^61.  Multiplication by a
+// precomputed constant uses Shoup's method (Shoup, NTL; Harvey 2014);
+// products of two variable residues are formed exactly as 128-bit values
+// and reduced with the fold x = hi*2^64 + lo -> hi*(2^64 mod q) + lo, each
+// half reduced by a Shoup multiplication.  Sums of up to 32 products of
+// residues below 2^61 stay below 2^127, so multiply-accumulate loops add
+// 128-bit products lazily and reduce once.
+#pragma once
+#include <cstdint>
+
+namespace hb {
+
+typedef unsigned long long u64;
+
+#define HB_MAX_PRIMES 64
+
+// Per-prime constants, one entry per prime index (main primes first, then
+// the special primes).  Kept in __constant__ memory: every thread of a
+// warp reads the same entry, which the constant cache broadcasts.
+struct PrimeConst {
+    u64 q;
+    u64 r64;      // 2^64 mod q
+    u64 r64p;     // Shoup companion of r64
+    u64 onep;     // floor(2^64 / q) (Shoup companion of 1)
+    u64 ninv;     // N^-1 mod q
+    u64 ninvp;
+};
+
+__device__ __forceinline__ u64 add_mod(u64 a, u64 b, u64 q) {
+    u64 s = a + b;
+    return s >= q ? s - q : s;
+}
+__device__ __forceinline__ u64 sub_mod(u64 a, u64 b, u64 q) {
+    return a >= b ? a - b : a + (q - b);
+}
+__device__ __forceinline__ u64 neg_mod(u64 a, u64 q) { return a ? q - a : 0; }
+
+// a * w mod q for any a < 2^64, w < q, wp = floor(w 2^64 / q).
+__device__ __forceinline__ u64 mul_shoup(u64 a, u64 w, u64 wp, u64 q) {
+    u64 hi = __umul64hi(a, wp);
+    u64 r = a * w - hi * q;
+    return r >= q ? r - q : r;
+}
+// same, result left in [0, 2q)
+__device__ __forceinline__ u64 mul_shoup_lazy(u64 a, u64 w, u64 wp, u64 q) {
+    u64 hi = __umul64hi(a, wp);
+    return a * w - hi * q;
+}
+
+struct u128 {
+    u64 lo, hi;
+};
+
+__device__ __forceinline__ void mac128(u128 &acc, u64 a, u64 b) {
+    u64 lo = a * b;
+    u64 hi = __umul64hi(a, b);
+    acc.lo += lo;
+    acc.hi += hi + (acc.lo < lo ? 1ull : 0ull);
+}
+
+// (hi*2^64 + lo) mod q
+__device__ __forceinline__ u64 reduce128(u64 hi, u64 lo, const PrimeConst &pc) {
+    u64 h = mul_shoup(hi, pc.r64, pc.r64p, pc.q);
+    u64 l = mul_shoup(lo, 1ull, pc.onep, pc.q);
+    return add_mod(h, l, pc.q);
+}
+__device__ __forceinline__ u64 reduce128(const u128 &x, const PrimeConst &pc) {
+    return reduce128(x.hi, x.lo, pc);
+}
+__device__ __forceinline__ u64 mul_mod(u64 a, u64 b, const PrimeConst &pc) {
+    return reduce128(__umul64hi(a, b), a * b, pc);
+}
+
+// bit reversal of the low `bits` bits
+__device__ __forceinline__ unsigned brev_bits(unsigned x, int bits) {
+    return __brev(x) >> (32 - bits);
+}
+
+// Automorphism X -> X^g in the bit-reversed NTT domain: the value at
+// position t after the automorphism is the input value at tau_g(t).
+__device__ __forceinline__ unsigned aut_index(unsigned t, u64 g, int logN) {
+    const u64 mask = (2ull << logN) - 1;  // 2N - 1
+    u64 e = 2ull * brev_bits(t, logN) + 1ull;
+    u64 e2 = (e * g) & mask;
+    return brev_bits((unsigned)((e2 - 1) >> 1), logN);
+}
+
+}  // namespace hb

@@ -1,0 +1,1843 @@
+// hb_context.cu -- scheme state, object registries, the CKKS operations
+// built from the kernels in hb_kernels.cu, and the extern "C" boundary
+// declared in include/helrm_b200.h.
+//
+// Ownership follows the reference backends: the library owns every
+// ciphertext, plaintext and transform; callers hold int handles
+// (orion/backend/cheddar/ext/cheddar_pybind.cu:73-236).  All device work
+// goes to one non-blocking stream; memory comes from CUDA's stream-ordered
+// pool (cudaMallocAsync), which keeps freed blocks cached for reuse.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <set>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/helrm_b200.h"
+#include "hb_host.hpp"
+#include "hb_kernels.cuh"
+
+namespace hb {
+
+struct HbError : std::runtime_error {
+    int code;
+    HbError(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+#define HB_THROW(code, msg) throw HbError(code, msg)
+
+static void cuda_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) {
+        if (e == cudaErrorMemoryAllocation) HB_THROW(HB_ENOMEM, std::string(what) + ": out of device memory");
+        HB_THROW(HB_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+enum : u64 {
+    DOM_SK_POS = 1, DOM_SK_SIGN = 2, DOM_ENC_A = 3, DOM_ENC_E = 4,
+    DOM_SWK_A = 5, DOM_SWK_E = 6, DOM_KEYSEED = 7, DOM_PK_A = 8, DOM_PK_E = 9
+};
+
+static inline u64 hmix(u64 z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static inline u64 hrand64(u64 seed, u64 dom, u64 idx) { return hmix(hmix(seed ^ hmix(dom)) ^ idx); }
+
+struct Ct {
+    u64 *d = nullptr;
+    int nq = 0;
+    int npoly = 2;
+    double scale = 1.0;
+    int slots = 0;
+};
+struct Pt {
+    u64 *d = nullptr;
+    int nq = 0;      // q rows
+    bool ext = false;  // K special-prime rows follow
+    double scale = 1.0;
+    int slots = 0;
+};
+
+struct LevelTabs {
+    // device blob; pointers into it
+    u64 *blob = nullptr;
+    ModUpTab mu{};
+    ModDownTab md{};
+    const u64 *qlinv = nullptr, *qlinvp = nullptr;
+    int beta = 0;
+};
+
+struct LinTrans {
+    int level = 0;
+    int bs = 1;
+    bool use_bsgs = false;
+    std::vector<int> ks;
+    std::map<int, Pt> pts;                        // k -> extended plaintext
+    std::map<int, std::vector<std::pair<int, int>>> groups;  // g -> (b, k)
+    // device plans, rebuilt when the rotation-key set changes
+    int plan_keygen = -1;
+    int plan_nq = -1;
+    std::vector<BabyDesc *> plan_dev;
+    std::vector<BsgsChunk> plan_chunks;
+    std::vector<int> giant_of_slot;   // slot -> g
+};
+
+class Context {
+public:
+    int device = 0;
+    int logN = 0, N = 0, L = 0, K = 0, P = 0, alpha = 1, dnum = 1, logscale = 0, h = 0, slots = 0;
+    u64 seed = 0;
+    double default_scale = 1.0;
+    std::vector<u64> primes;
+    cudaStream_t stream = nullptr;
+    NttTables ntt{};
+    u64 *d_tables = nullptr;
+    u64 *d_pmod = nullptr;     // P mod q_p, [P]
+    std::vector<LevelTabs> lv; // index nq (1..L)
+    std::vector<PrimeConst> pcs;
+    // keys
+    u64 *d_sk = nullptr;
+    u64 *d_rlk = nullptr;
+    std::map<u64, u64 *> rot_keys;  // galois -> [dnum][2][P][N]
+    int keygen_counter = 0;
+    // registries
+    std::unordered_map<int, Ct> cts;
+    std::unordered_map<int, Pt> pts;
+    std::unordered_map<int, std::unique_ptr<LinTrans>> lts;
+    int next_id = 1;
+    u64 enc_counter = 0;
+    // memory accounting
+    std::unordered_map<void *, size_t> alloc_sizes;
+    size_t live = 0, peak = 0, key_bytes = 0;
+
+    size_t limb_bytes() const { return (size_t)N * sizeof(u64); }
+    size_t key_words() const { return (size_t)dnum * 2 * P * N; }
+
+    // ---------------------------------------------------------- memory
+    u64 *alloc(size_t words) {
+        void *p = nullptr;
+        if (words == 0) words = 1;
+        cuda_check(cudaMallocAsync(&p, words * sizeof(u64), stream), "cudaMallocAsync");
+        alloc_sizes[p] = words * sizeof(u64);
+        live += words * sizeof(u64);
+        peak = std::max(peak, live);
+        return (u64 *)p;
+    }
+    void release(void *p) {
+        if (!p) return;
+        auto it = alloc_sizes.find(p);
+        if (it != alloc_sizes.end()) {
+            live -= it->second;
+            alloc_sizes.erase(it);
+        }
+        cudaFreeAsync(p, stream);
+    }
+    void zero(u64 *p, size_t words) { cuda_check(cudaMemsetAsync(p, 0, words * 8, stream), "memset"); }
+    void d2d(u64 *dst, const u64 *src, size_t words) {
+        cuda_check(cudaMemcpyAsync(dst, src, words * 8, cudaMemcpyDeviceToDevice, stream), "d2d");
+    }
+    void sync() { cuda_check(cudaStreamSynchronize(stream), "sync"); }
+
+    RowMap qmap(int nq) const { return rowmap(nq, nq, L); }
+    RowMap extmap(int nq) const { return rowmap(nq + K, nq, L); }
+    int beta_of(int nq) const { return (nq + alpha - 1) / alpha; }
+
+    // ---------------------------------------------------------- setup
+    void setup(int logn, const std::vector<int> &logq, const std::vector<int> &logp, int lscale, int hw, int dn,
+               u64 sd, int dev) {
+        if (logn < 10 || logn > 17) HB_THROW(HB_EINVAL, "LogN must be in [10, 17]");
+        if (logq.empty() || logp.empty()) HB_THROW(HB_EINVAL, "LogQ and LogP must be non-empty");
+        if ((int)(logq.size() + logp.size()) > HB_MAX_PRIMES) HB_THROW(HB_EINVAL, "too many primes");
+        if (logp.size() > 8) HB_THROW(HB_EINVAL, "at most 8 special primes");
+        for (int b : logq)
+            if (b > 60) HB_THROW(HB_EINVAL, "prime sizes above 60 bits are not supported (lazy 128-bit sums)");
+        for (int b : logp)
+            if (b > 60) HB_THROW(HB_EINVAL, "prime sizes above 60 bits are not supported (lazy 128-bit sums)");
+        device = dev;
+        cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+        logN = logn;
+        N = 1 << logn;
+        slots = N / 2;
+        L = (int)logq.size();
+        K = (int)logp.size();
+        P = L + K;
+        logscale = lscale;
+        default_scale = std::ldexp(1.0, lscale);
+        h = hw;
+        seed = sd;
+        std::vector<u64> used;
+        primes = gen_primes(logq, logn, used);
+        std::vector<u64> aux = gen_primes(logp, logn, used);
+        primes.insert(primes.end(), aux.begin(), aux.end());
+        // digits: dnum given, or Lattigo's default of |P| primes per digit
+        alpha = dn > 0 ? (L + dn - 1) / dn : K;
+        if (alpha < 1) alpha = 1;
+        if (alpha > 16) HB_THROW(HB_EINVAL, "digits of more than 16 primes are not supported");
+        dnum = (L + alpha - 1) / alpha;
+
+        cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+        cudaMemPool_t pool;
+        cuda_check(cudaDeviceGetDefaultMemPool(&pool, dev), "mempool");
+        u64 thr = ~0ull;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+
+        // per-prime constants
+        pcs.resize(P);
+        for (int p = 0; p < P; p++) {
+            u64 q = primes[p];
+            PrimeConst c;
+            c.q = q;
+            c.r64 = (u64)(((hu128)1 << 64) % q);
+            c.r64p = h_shoup(c.r64, q);
+            c.onep = (u64)(((hu128)1 << 64) / q);
+            c.ninv = h_invm((u64)N, q);
+            c.ninvp = h_shoup(c.ninv, q);
+            pcs[p] = c;
+        }
+        upload_prime_consts(pcs.data(), P);
+
+        // twiddles
+        std::vector<u64> tw((size_t)4 * P * N);
+        for (int p = 0; p < P; p++) {
+            u64 q = primes[p];
+            u64 psi = find_psi(q, logN), ipsi = h_invm(psi, q);
+            u64 *T = &tw[(size_t)(0 * P + p) * N], *Tp = &tw[(size_t)(1 * P + p) * N];
+            u64 *I = &tw[(size_t)(2 * P + p) * N], *Ip = &tw[(size_t)(3 * P + p) * N];
+            u64 w = 1, iw = 1;
+            for (int i = 0; i < N; i++) {
+                unsigned r = h_brv((unsigned)i, logN);
+                T[r] = w;
+                I[r] = iw;
+                w = h_mulm(w, psi, q);
+                iw = h_mulm(iw, ipsi, q);
+            }
+            for (int i = 0; i < N; i++) {
+                Tp[i] = h_shoup(T[i], q);
+                Ip[i] = h_shoup(I[i], q);
+            }
+        }
+        d_tables = alloc(tw.size());
+        cuda_check(cudaMemcpyAsync(d_tables, tw.data(), tw.size() * 8, cudaMemcpyHostToDevice, stream), "tw upload");
+        ntt.tw = d_tables;
+        ntt.twp = d_tables + (size_t)P * N;
+        ntt.itw = d_tables + (size_t)2 * P * N;
+        ntt.itwp = d_tables + (size_t)3 * P * N;
+        ntt.logN = logN;
+
+        std::vector<u64> pm(P);
+        for (int p = 0; p < P; p++) {
+            u64 q = primes[p], v = 1 % q;
+            for (int k = 0; k < K; k++) v = h_mulm(v, primes[L + k] % q, q);
+            pm[p] = v;
+        }
+        d_pmod = alloc(P);
+        cuda_check(cudaMemcpyAsync(d_pmod, pm.data(), P * 8, cudaMemcpyHostToDevice, stream), "pmod");
+
+        build_level_tables();
+        sync();
+    }
+
+    void build_level_tables() {
+        lv.assign(L + 1, LevelTabs{});
+        for (int nq = 1; nq <= L; nq++) {
+            const int ne = nq + K, beta = beta_of(nq);
+            std::vector<u64> qhinv((size_t)beta * alpha, 0), qhinvp((size_t)beta * alpha, 0);
+            std::vector<u64> qhat((size_t)beta * alpha * ne, 0), qjneg((size_t)beta * ne, 0);
+            for (int j = 0; j < beta; j++) {
+                int lo = j * alpha, hi = std::min(lo + alpha, nq), na = hi - lo;
+                for (int e = 0; e < ne; e++) {
+                    int pe = e < nq ? e : L + (e - nq);
+                    u64 t = primes[pe], v = 1 % t;
+                    for (int m = 0; m < na; m++) v = h_mulm(v, primes[lo + m] % t, t);
+                    qjneg[(size_t)j * ne + e] = v ? t - v : 0;
+                }
+                for (int m = 0; m < na; m++) {
+                    u64 qm = primes[lo + m], v = 1 % qm;
+                    for (int m2 = 0; m2 < na; m2++)
+                        if (m2 != m) v = h_mulm(v, primes[lo + m2] % qm, qm);
+                    qhinv[(size_t)j * alpha + m] = h_invm(v, qm);
+                    qhinvp[(size_t)j * alpha + m] = h_shoup(qhinv[(size_t)j * alpha + m], qm);
+                    for (int e = 0; e < ne; e++) {
+                        int pe = e < nq ? e : L + (e - nq);
+                        if (pe >= lo && pe < hi) continue;
+                        u64 t = primes[pe], w = 1 % t;
+                        for (int m2 = 0; m2 < na; m2++)
+                            if (m2 != m) w = h_mulm(w, primes[lo + m2] % t, t);
+                        qhat[((size_t)j * alpha + m) * ne + e] = w;
+                    }
+                }
+            }
+            std::vector<u64> phinv(K), phinvp(K), phat((size_t)K * nq), pinv(nq), pinvp(nq), pneg(nq);
+            for (int k = 0; k < K; k++) {
+                u64 pk = primes[L + k], v = 1 % pk;
+                for (int k2 = 0; k2 < K; k2++)
+                    if (k2 != k) v = h_mulm(v, primes[L + k2] % pk, pk);
+                phinv[k] = h_invm(v, pk);
+                phinvp[k] = h_shoup(phinv[k], pk);
+                for (int i = 0; i < nq; i++) {
+                    u64 q = primes[i], w = 1 % q;
+                    for (int k2 = 0; k2 < K; k2++)
+                        if (k2 != k) w = h_mulm(w, primes[L + k2] % q, q);
+                    phat[(size_t)k * nq + i] = w;
+                }
+            }
+            for (int i = 0; i < nq; i++) {
+                u64 q = primes[i], v = 1 % q;
+                for (int k = 0; k < K; k++) v = h_mulm(v, primes[L + k] % q, q);
+                pinv[i] = h_invm(v, q);
+                pinvp[i] = h_shoup(pinv[i], q);
+                pneg[i] = v ? q - v : 0;
+            }
+            std::vector<u64> qlinv(nq, 0), qlinvp(nq, 0);
+            if (nq >= 2) {
+                u64 ql = primes[nq - 1];
+                for (int i = 0; i < nq - 1; i++) {
+                    qlinv[i] = h_invm(ql % primes[i], primes[i]);
+                    qlinvp[i] = h_shoup(qlinv[i], primes[i]);
+                }
+            }
+            std::vector<u64> blob;
+            auto put = [&](const std::vector<u64> &v) {
+                size_t off = blob.size();
+                blob.insert(blob.end(), v.begin(), v.end());
+                return off;
+            };
+            size_t o_qhinv = put(qhinv), o_qhinvp = put(qhinvp), o_qhat = put(qhat), o_qjneg = put(qjneg),
+                   o_pneg = put(pneg);
+            size_t o_phinv = put(phinv), o_phinvp = put(phinvp), o_phat = put(phat), o_pinv = put(pinv),
+                   o_pinvp = put(pinvp), o_qlinv = put(qlinv), o_qlinvp = put(qlinvp);
+            LevelTabs &T = lv[nq];
+            T.blob = alloc(blob.size());
+            cuda_check(cudaMemcpyAsync(T.blob, blob.data(), blob.size() * 8, cudaMemcpyHostToDevice, stream),
+                       "level tables");
+            T.beta = beta;
+            T.mu.qhinv = T.blob + o_qhinv;
+            T.mu.qhinvp = T.blob + o_qhinvp;
+            T.mu.qhat = T.blob + o_qhat;
+            T.mu.qjneg = T.blob + o_qjneg;
+            T.md.pneg = T.blob + o_pneg;
+            T.md.phinv = T.blob + o_phinv;
+            T.md.phinvp = T.blob + o_phinvp;
+            T.md.phat = T.blob + o_phat;
+            T.md.pinv = T.blob + o_pinv;
+            T.md.pinvp = T.blob + o_pinvp;
+            T.qlinv = T.blob + o_qlinv;
+            T.qlinvp = T.blob + o_qlinvp;
+        }
+    }
+
+    ~Context() {
+        if (stream) {
+            cudaStreamSynchronize(stream);
+            for (auto &kv : cts) release(kv.second.d);
+            for (auto &kv : pts) release(kv.second.d);
+            for (auto &kv : lts) free_lt(*kv.second);
+            for (auto &kv : rot_keys) release(kv.second);
+            release(d_rlk);
+            release(d_sk);
+            for (auto &t : lv) release(t.blob);
+            release(d_pmod);
+            release(d_tables);
+            cudaStreamSynchronize(stream);
+            cudaStreamDestroy(stream);
+        }
+    }
+
+    // ---------------------------------------------------------- registries
+    int put_ct(const Ct &c) {
+        int id = next_id++;
+        cts[id] = c;
+        return id;
+    }
+    int put_pt(const Pt &p) {
+        int id = next_id++;
+        pts[id] = p;
+        return id;
+    }
+    Ct &ct(int id) {
+        auto it = cts.find(id);
+        if (it == cts.end()) HB_THROW(HB_ENOENT, "unknown ciphertext id " + std::to_string(id));
+        return it->second;
+    }
+    Pt &pt(int id) {
+        auto it = pts.find(id);
+        if (it == pts.end()) HB_THROW(HB_ENOENT, "unknown plaintext id " + std::to_string(id));
+        return it->second;
+    }
+    LinTrans &lt(int id) {
+        auto it = lts.find(id);
+        if (it == lts.end()) HB_THROW(HB_ENOENT, "unknown linear transform id " + std::to_string(id));
+        return *it->second;
+    }
+    void del_ct(int id) {
+        auto it = cts.find(id);
+        if (it == cts.end()) return;
+        release(it->second.d);
+        cts.erase(it);
+    }
+    void del_pt(int id) {
+        auto it = pts.find(id);
+        if (it == pts.end()) return;
+        release(it->second.d);
+        pts.erase(it);
+    }
+    void free_lt(LinTrans &t) {
+        for (auto &kv : t.pts) release(kv.second.d);
+        t.pts.clear();
+        for (auto *p : t.plan_dev) release(p);
+        t.plan_dev.clear();
+    }
+    // move the content of `from` into `id`
+    void replace_ct(int id, int from) {
+        Ct &dst = ct(id);
+        Ct src = ct(from);
+        release(dst.d);
+        dst = src;
+        cts.erase(from);
+    }
+
+    Ct new_ct(int nq, int npoly, double scale) {
+        Ct c;
+        c.nq = nq;
+        c.npoly = npoly;
+        c.scale = scale;
+        c.slots = slots;
+        c.d = alloc((size_t)npoly * nq * N);
+        return c;
+    }
+    int level_of(const Ct &c) const { return c.nq - 1; }
+
+    // ---------------------------------------------------------- keys
+    void require_sk() const {
+        if (!d_sk) HB_THROW(HB_ESTATE, "secret key not generated (call GenerateSecretKey)");
+    }
+
+    void gen_secret() {
+        // ternary secret of Hamming weight h (all coefficients when h >= N)
+        std::vector<int8_t> s(N, 0);
+        if (h >= N) {
+            for (int n = 0; n < N; n++) s[n] = (hrand64(seed, DOM_SK_SIGN, n) >> 63) ? 1 : -1;
+        } else {
+            std::vector<unsigned> perm(N);
+            for (int i = 0; i < N; i++) perm[i] = i;
+            for (int i = 0; i < h; i++) {
+                u64 r = hrand64(seed, DOM_SK_POS, i);
+                unsigned j = i + (unsigned)(((hu128)r * (u64)(N - i)) >> 64);
+                std::swap(perm[i], perm[j]);
+                s[perm[i]] = (hrand64(seed, DOM_SK_SIGN, i) >> 63) ? 1 : -1;
+            }
+        }
+        std::vector<u64> rows((size_t)P * N);
+        for (int p = 0; p < P; p++)
+            for (int n = 0; n < N; n++) rows[(size_t)p * N + n] = s[n] >= 0 ? (u64)s[n] : primes[p] - 1;
+        if (!d_sk) d_sk = alloc((size_t)P * N);
+        cuda_check(cudaMemcpyAsync(d_sk, rows.data(), rows.size() * 8, cudaMemcpyHostToDevice, stream), "sk");
+        ntt_forward(d_sk, P, rowmap(P, L, L), ntt, stream);
+        sync();
+    }
+
+    // switching key from `target` (NTT, [P][N]) to s
+    u64 *gen_swk(const u64 *target, u64 kseed) {
+        u64 *key = alloc(key_words());
+        u64 *e = alloc((size_t)P * N);
+        const RowMap all = rowmap(P, L, L);
+        for (int j = 0; j < dnum; j++) {
+            u64 *b = key + ((size_t)j * 2 + 0) * P * N;
+            u64 *a = key + ((size_t)j * 2 + 1) * P * N;
+            sample_uniform(a, P, nullptr, all, kseed, DOM_SWK_A, (u64)j * P * N, 0, logN, stream);
+            sample_cbd(e, P, all, kseed, DOM_SWK_E, (u64)j * N, logN, stream);
+            ntt_forward(e, P, all, ntt, stream);
+            int lo = j * alpha, hi = std::min(lo + alpha, L);
+            swk_combine(b, a, e, d_sk, target, d_pmod, P, lo, hi, logN, stream);
+        }
+        release(e);
+        key_bytes += key_words() * 8;
+        keygen_counter++;
+        return key;
+    }
+
+    u64 galois_of(int k) const {
+        int kn = ((k % slots) + slots) % slots;
+        return h_powm(5, (u64)kn, 2ull * N);
+    }
+
+    u64 *rotation_key(u64 g) {
+        auto it = rot_keys.find(g);
+        if (it != rot_keys.end()) return it->second;
+        require_sk();
+        u64 *t = alloc((size_t)P * N);
+        ew_automorphism(t, d_sk, P, g, logN, stream);
+        u64 *key = gen_swk(t, hrand64(seed, DOM_KEYSEED, g));
+        release(t);
+        rot_keys[g] = key;
+        return key;
+    }
+
+    void gen_relin() {
+        require_sk();
+        if (d_rlk) return;
+        u64 *t = alloc((size_t)P * N);
+        // s^2 over all primes: tensor-free elementwise square
+        MacArgs m{};
+        m.ct[0] = d_sk;
+        m.pt[0] = d_sk;
+        m.n = 1;
+        // ew_mac treats rows as q rows of one poly; P rows map to primes 0..P-1
+        ew_mac(t, m, 1, P, logN, stream);
+        d_rlk = gen_swk(t, hrand64(seed, DOM_KEYSEED, 0));
+        release(t);
+    }
+
+    // ---------------------------------------------------------- encode
+    // integer coefficients -> NTT residues on `rows` rows (q rows then aux)
+    void upload_coeffs(const std::vector<hi128> &co, int nq, bool ext, u64 *dst) {
+        const int rows = nq + (ext ? K : 0);
+        std::vector<u64> host((size_t)rows * N);
+        auto work = [&](int r0, int r1) {
+            for (int r = r0; r < r1; r++) {
+                const int p = r < nq ? r : L + (r - nq);
+                const u64 q = primes[p];
+                u64 *row = &host[(size_t)r * N];
+                for (int n = 0; n < N; n++) {
+                    hi128 x = co[n];
+                    if (x >= 0)
+                        row[n] = x < ((hi128)1 << 63) ? (u64)x % q : (u64)((hu128)x % q);
+                    else {
+                        u64 m = (-x) < ((hi128)1 << 63) ? (u64)(-x) % q : (u64)((hu128)(-x) % q);
+                        row[n] = m ? q - m : 0;
+                    }
+                }
+            }
+        };
+        work(0, rows);
+        cuda_check(cudaMemcpyAsync(dst, host.data(), host.size() * 8, cudaMemcpyHostToDevice, stream), "encode upload");
+        ntt_forward(dst, rows, rowmap(rows, nq, L), ntt, stream);
+        sync();  // host buffer lifetime
+    }
+
+    int encode(const double *inter, int n, int level, double scale, bool ext) {
+        if (level < 0 || level >= L) HB_THROW(HB_EINVAL, "encode: level out of range");
+        if (n > slots) HB_THROW(HB_EINVAL, "encode: more values than slots");
+        if (!(scale > 0)) scale = default_scale;
+        std::vector<hi128> co;
+        encode_coeffs(logN, inter, n, (long double)scale, co);
+        Pt p;
+        p.nq = level + 1;
+        p.ext = ext;
+        p.scale = scale;
+        p.slots = slots;
+        p.d = alloc((size_t)(p.nq + (ext ? K : 0)) * N);
+        upload_coeffs(co, p.nq, ext, p.d);
+        return put_pt(p);
+    }
+
+    // decode (NTT) plaintext rows -> interleaved values
+    void decode_rows(const u64 *d, int nq, double scale, std::vector<double> &out) {
+        const int nc = std::min(nq, 4);
+        u64 *tmp = alloc((size_t)nc * N);
+        d2d(tmp, d, (size_t)nc * N);
+        ntt_inverse(tmp, nc, qmap(nc), ntt, stream);
+        std::vector<u64> host((size_t)nc * N);
+        cuda_check(cudaMemcpyAsync(host.data(), tmp, host.size() * 8, cudaMemcpyDeviceToHost, stream), "decode");
+        release(tmp);
+        sync();
+        CrtPlan plan(primes.data(), nc);
+        std::vector<long double> co(N);
+        std::vector<u64> res(nc);
+        for (int n = 0; n < N; n++) {
+            for (int i = 0; i < nc; i++) res[i] = host[(size_t)i * N + n];
+            co[n] = crt_centered(res.data(), plan);
+        }
+        out.resize((size_t)2 * slots);
+        decode_coeffs(logN, co, (long double)scale, out.data());
+    }
+
+    // ---------------------------------------------------------- encrypt
+    Ct encrypt_rows(const u64 *m, int nq, double scale, u64 ct_seed) {
+        require_sk();
+        Ct c = new_ct(nq, 2, scale);
+        u64 *c0 = c.d, *c1 = c.d + (size_t)nq * N;
+        u64 *e = alloc((size_t)nq * N);
+        sample_uniform(c1, nq, nullptr, qmap(nq), ct_seed, DOM_ENC_A, 0, 0, logN, stream);
+        sample_cbd(e, nq, qmap(nq), ct_seed, DOM_ENC_E, 0, logN, stream);
+        ntt_forward(e, nq, qmap(nq), ntt, stream);
+        enc_combine(c0, c1, e, d_sk, m, nq, logN, stream);
+        release(e);
+        return c;
+    }
+
+    // ---------------------------------------------------------- key switching pieces
+    // ModUp of nb polys (nq rows each, NTT) -> D [nb][beta][ne][N]
+    void modup(u64 *D, const u64 *a, int nq, int nb, size_t a_stride) {
+        const int ne = nq + K, beta = beta_of(nq);
+        u64 *X = alloc((size_t)nb * nq * N);
+        for (int b = 0; b < nb; b++) d2d(X + (size_t)b * nq * N, a + b * a_stride, (size_t)nq * N);
+        ntt_inverse(X, nb * nq, qmap(nq), ntt, stream);
+        modup_bconv(D, X, a, nq, K, L, alpha, beta, lv[nq].mu, logN, nb, (size_t)nq * N, (size_t)beta * ne * N,
+                    a_stride, stream);
+        RowMap m = extmap(nq);
+        m.alpha = alpha;
+        m.ndig = beta;
+        ntt_forward(D, nb * beta * ne, m, ntt, stream);
+        release(X);
+    }
+
+    // ModDown of nb extended polys x (ne rows, item stride xs) -> out (nq rows, stride os),
+    // optionally + addend[tau_g] (stride as)
+    void moddown(u64 *out, const u64 *x, int nq, int nb, size_t xs, size_t os, const u64 *addend = nullptr,
+                 u64 add_g = 1, size_t as = 0) {
+        u64 *Y = alloc((size_t)nb * K * N);
+        for (int b = 0; b < nb; b++) d2d(Y + (size_t)b * K * N, x + b * xs + (size_t)nq * N, (size_t)K * N);
+        RowMap pm = rowmap(K, 0, L);
+        ntt_inverse(Y, nb * K, pm, ntt, stream);
+        u64 *Z = alloc((size_t)nb * nq * N);
+        moddown_bconv(Z, Y, nq, K, L, lv[nq].md, logN, nb, (size_t)K * N, (size_t)nq * N, stream);
+        ntt_forward(Z, nb * nq, qmap(nq), ntt, stream);
+        moddown_combine(out, x, Z, nq, lv[nq].md, addend, add_g, logN, nb, xs, (size_t)nq * N, os, as, stream);
+        release(Y);
+        release(Z);
+    }
+
+    // rotations of nb ciphertexts (contiguous [nb][2][nq][N] at `in`) by
+    // Galois g into `out` (same layout): one ModUp per ciphertext.
+    void rotate_batch(u64 *out, const u64 *in, int nq, int nb, u64 g, const u64 *key) {
+        const int ne = nq + K, beta = beta_of(nq);
+        const size_t cts_ = (size_t)2 * nq * N;
+        u64 *D = alloc((size_t)nb * beta * ne * N);
+        modup(D, in + (size_t)nq * N, nq, nb, cts_);
+        u64 *acc = alloc((size_t)nb * 2 * ne * N);
+        keymult(acc, D, key, g, nq, K, L, beta, P, nullptr, false, logN, nb, (size_t)beta * ne * N,
+                (size_t)2 * ne * N, 0, stream);
+        release(D);
+        moddown(out, acc, nq, nb, (size_t)2 * ne * N, cts_, in, g, cts_);
+        moddown(out + (size_t)nq * N, acc + (size_t)ne * N, nq, nb, (size_t)2 * ne * N, cts_);
+        release(acc);
+    }
+
+    // hoisted: one ciphertext, many Galois elements
+    void rotate_hoisted(const u64 *in, int nq, int nb, const std::vector<u64> &gs, const std::vector<u64 *> &outs,
+                        size_t out_stride) {
+        const int ne = nq + K, beta = beta_of(nq);
+        const size_t cts_ = (size_t)2 * nq * N;
+        u64 *D = alloc((size_t)nb * beta * ne * N);
+        modup(D, in + (size_t)nq * N, nq, nb, cts_);
+        u64 *acc = alloc((size_t)nb * 2 * ne * N);
+        for (size_t r = 0; r < gs.size(); r++) {
+            u64 *key = rotation_key(gs[r]);
+            keymult(acc, D, key, gs[r], nq, K, L, beta, P, nullptr, false, logN, nb, (size_t)beta * ne * N,
+                    (size_t)2 * ne * N, 0, stream);
+            moddown(outs[r], acc, nq, nb, (size_t)2 * ne * N, out_stride, in, gs[r], cts_);
+            moddown(outs[r] + (size_t)nq * N, acc + (size_t)ne * N, nq, nb, (size_t)2 * ne * N, out_stride);
+        }
+        release(acc);
+        release(D);
+    }
+
+    void relinearize(u64 *out, const u64 *in3, int nq) {
+        const int ne = nq + K, beta = beta_of(nq);
+        u64 *D = alloc((size_t)beta * ne * N);
+        modup(D, in3 + (size_t)2 * nq * N, nq, 1, 0);
+        u64 *acc = alloc((size_t)2 * ne * N);
+        keymult(acc, D, d_rlk, 1, nq, K, L, beta, P, nullptr, false, logN, 1, 0, 0, 0, stream);
+        release(D);
+        moddown(out, acc, nq, 1, 0, 0, in3, 1, 0);
+        moddown(out + (size_t)nq * N, acc + (size_t)ne * N, nq, 1, 0, 0, in3 + (size_t)nq * N, 1, 0);
+        release(acc);
+    }
+
+    // rescale nb ciphertexts [nb][npoly][nq] -> [nb][npoly][nq-1]
+    void rescale(u64 *out, const u64 *in, int npoly, int nq, int nb, size_t in_stride, size_t out_stride) {
+        if (nq < 2) HB_THROW(HB_ESTATE, "rescale: ciphertext already at level 0");
+        const int l = nq - 1;
+        u64 *R = alloc((size_t)nb * npoly * N);
+        for (int b = 0; b < nb; b++)
+            for (int pl = 0; pl < npoly; pl++)
+                d2d(R + ((size_t)b * npoly + pl) * N, in + b * in_stride + ((size_t)pl * nq + l) * N, N);
+        RowMap rm = rowmap(1, 1, L);
+        rm.pbase = l;
+        ntt_inverse(R, nb * npoly, rm, ntt, stream);
+        u64 *W = alloc((size_t)nb * npoly * l * N);
+        rescale_prep(W, R, npoly, l, primes[l], logN, nb, (size_t)npoly * N, (size_t)npoly * l * N, stream);
+        ntt_forward(W, nb * npoly * l, qmap(l), ntt, stream);
+        rescale_combine(out, in, W, npoly, nq, lv[nq].qlinv, lv[nq].qlinvp, logN, nb, in_stride,
+                        (size_t)npoly * l * N, out_stride, stream);
+        release(R);
+        release(W);
+    }
+
+    // ---------------------------------------------------------- level / scale alignment
+    Ct drop_to(const Ct &c, int nq) {
+        Ct o = new_ct(nq, c.npoly, c.scale);
+        o.slots = c.slots;
+        for (int pl = 0; pl < c.npoly; pl++)
+            d2d(o.d + (size_t)pl * nq * N, c.d + (size_t)pl * c.nq * N, (size_t)nq * N);
+        return o;
+    }
+
+    // absorbs scale drift below 1e-4 relative like the reference
+    // (cheddar_pybind.cu:277-307); larger mismatches are errors.
+    void check_scales(double a, double b, const char *op) {
+        double diff = std::fabs(a - b);
+        if (diff < 1e-12 * a) return;
+        if (!(diff < 1e-4 * a))
+            HB_THROW(HB_ESTATE, std::string(op) + ": scale mismatch beyond drift tolerance (" + std::to_string(a) +
+                                    " vs " + std::to_string(b) + ")");
+    }
+
+    int add_sub(int a, int b, bool sub) {
+        const Ct &ca = ct(a), &cb = ct(b);
+        if (ca.npoly != cb.npoly) HB_THROW(HB_ESTATE, "add: ciphertext degrees differ");
+        check_scales(ca.scale, cb.scale, sub ? "SubCiphertextNew" : "AddCiphertextNew");
+        int nq = std::min(ca.nq, cb.nq);
+        Ct o = new_ct(nq, ca.npoly, ca.scale);
+        o.slots = std::max(ca.slots, cb.slots);
+        for (int pl = 0; pl < ca.npoly; pl++) {
+            if (sub)
+                ew_sub(o.d + (size_t)pl * nq * N, ca.d + (size_t)pl * ca.nq * N, cb.d + (size_t)pl * cb.nq * N, nq,
+                       qmap(nq), logN, stream);
+            else
+                ew_add(o.d + (size_t)pl * nq * N, ca.d + (size_t)pl * ca.nq * N, cb.d + (size_t)pl * cb.nq * N, nq,
+                       qmap(nq), logN, stream);
+        }
+        return put_ct(o);
+    }
+
+    // constant value per prime (signed integer v, possibly beyond 64 bits)
+    std::vector<u64> const_residues(long double v) {
+        long double r = v >= 0 ? floorl(v + 0.5L) : -floorl(-v + 0.5L);
+        if (!(fabsl(r) < 1.6e38L)) HB_THROW(HB_EINVAL, "scalar too large to encode");
+        hi128 x = (hi128)r;
+        std::vector<u64> res(P);
+        for (int p = 0; p < P; p++) {
+            u64 q = primes[p];
+            if (x >= 0)
+                res[p] = (u64)((hu128)x % q);
+            else {
+                u64 m = (u64)((hu128)(-x) % q);
+                res[p] = m ? q - m : 0;
+            }
+        }
+        return res;
+    }
+
+    int scalar_op(int id, long double value, int kind) {  // 0 add, 1 sub, 2 mul(int), 3 mul(float)
+        const Ct &c = ct(id);
+        Ct o = new_ct(c.nq, c.npoly, c.scale);
+        o.slots = c.slots;
+        std::vector<u64> res;
+        if (kind == 0 || kind == 1) res = const_residues(value * (long double)c.scale);
+        else if (kind == 2) res = const_residues(value);
+        else res = const_residues(value * (long double)c.scale);
+        if (kind == 1)
+            for (int p = 0; p < P; p++) res[p] = res[p] ? primes[p] - res[p] : 0;
+        u64 *dc = alloc((size_t)2 * P);
+        std::vector<u64> hc(2 * P);
+        for (int p = 0; p < P; p++) {
+            hc[p] = res[p];
+            hc[P + p] = h_shoup(res[p], primes[p]);
+        }
+        cuda_check(cudaMemcpyAsync(dc, hc.data(), hc.size() * 8, cudaMemcpyHostToDevice, stream), "const");
+        if (kind <= 1) {
+            ew_add_const(o.d, c.d, dc, c.nq, qmap(c.nq), logN, stream);
+            if (c.npoly > 1) d2d(o.d + (size_t)c.nq * N, c.d + (size_t)c.nq * N, (size_t)(c.npoly - 1) * c.nq * N);
+        } else {
+            ew_mul_const(o.d, c.d, dc, dc + P, c.npoly * c.nq, qmap(c.nq), logN, stream);
+            if (kind == 3) o.scale = c.scale * c.scale;
+        }
+        sync();  // host constant buffer
+        release(dc);
+        return put_ct(o);
+    }
+
+    int mul_plain(int ctid, int ptid) {
+        const Ct &c = ct(ctid);
+        const Pt &p = pt(ptid);
+        int nq = std::min(c.nq, p.nq);
+        Ct o = new_ct(nq, c.npoly, c.scale * p.scale);
+        o.slots = c.slots;
+        for (int pl = 0; pl < c.npoly; pl++)
+            ew_mul_bcast(o.d + (size_t)pl * nq * N, c.d + (size_t)pl * c.nq * N, p.d, 1, nq, 0, logN, stream);
+        return put_ct(o);
+    }
+
+    int add_plain(int ctid, int ptid, bool sub) {
+        const Ct &c = ct(ctid);
+        Pt p = pt(ptid);
+        int tmp_pt = 0;
+        if (std::fabs(p.scale - c.scale) > 1e-12 * c.scale) {
+            // re-encode the plaintext at the ciphertext's scale (cheddar_pybind.cu:775-788)
+            std::vector<double> vals;
+            decode_rows(p.d, p.nq, p.scale, vals);
+            tmp_pt = encode(vals.data(), slots, p.nq - 1, c.scale, false);
+            p = pt(tmp_pt);
+        }
+        int nq = std::min(c.nq, p.nq);
+        Ct o = new_ct(nq, c.npoly, c.scale);
+        o.slots = c.slots;
+        if (sub)
+            ew_sub(o.d, c.d, p.d, nq, qmap(nq), logN, stream);
+        else
+            ew_add(o.d, c.d, p.d, nq, qmap(nq), logN, stream);
+        for (int pl = 1; pl < c.npoly; pl++) d2d(o.d + (size_t)pl * nq * N, c.d + (size_t)pl * c.nq * N, (size_t)nq * N);
+        if (tmp_pt) del_pt(tmp_pt);
+        return put_ct(o);
+    }
+
+    int mac(const std::vector<int> &cids, const std::vector<int> &pids) {
+        if (cids.empty() || cids.size() != pids.size())
+            HB_THROW(HB_EINVAL, "MulPlaintextAccumNew: ct_ids/pt_ids must be equal-length and non-empty");
+        int nq = 1 << 30;
+        for (int id : cids) nq = std::min(nq, ct(id).nq);
+        for (int id : pids) nq = std::min(nq, pt(id).nq);
+        const double s0 = ct(cids[0]).scale * pt(pids[0]).scale;
+        int sl = 0;
+        for (size_t i = 0; i < cids.size(); i++) {
+            const Ct &c = ct(cids[i]);
+            if (c.npoly != 2) HB_THROW(HB_ESTATE, "MulPlaintextAccumNew: operand is degree-2; relinearize first");
+            double s = c.scale * pt(pids[i]).scale;
+            if (std::fabs(s - s0) > 1e-9 * s0)
+                HB_THROW(HB_ESTATE, "MulPlaintextAccumNew: inconsistent ct*pt scale products across pairs");
+            sl = std::max(sl, c.slots);
+        }
+        Ct o = new_ct(nq, 2, s0);
+        o.slots = sl;
+        // operands at a higher level are used through their first nq rows
+        std::vector<u64 *> tmps;
+        size_t done = 0;
+        u64 *acc = nullptr;
+        while (done < cids.size()) {
+            size_t n = std::min((size_t)HB_MAC_MAX, cids.size() - done);
+            MacArgs m{};
+            for (size_t t = 0; t < n; t++) {
+                const Ct &c = ct(cids[done + t]);
+                const u64 *src = c.d;
+                if (c.nq != nq) {
+                    Ct dd = drop_to(c, nq);
+                    tmps.push_back(dd.d);
+                    src = dd.d;
+                }
+                m.ct[t] = src;
+                m.pt[t] = pt(pids[done + t]).d;
+            }
+            m.n = (int)n;
+            if (!acc) {
+                ew_mac(o.d, m, 2, nq, logN, stream);
+                acc = o.d;
+            } else {
+                u64 *part = alloc((size_t)2 * nq * N);
+                ew_mac(part, m, 2, nq, logN, stream);
+                ew_add(o.d, o.d, part, 2 * nq, qmap(nq), logN, stream);
+                release(part);
+            }
+            done += n;
+        }
+        for (auto *p : tmps) release(p);
+        return put_ct(o);
+    }
+
+    // ---------------------------------------------------------- linear transforms
+    int generate_lt(const int *idxs, int n, const double *data, int width, int level, double ratio) {
+        if (n <= 0) HB_THROW(HB_EINVAL, "GenerateLinearTransform: no diagonals");
+        if (width <= 0 || width > slots) HB_THROW(HB_EINVAL, "GenerateLinearTransform: bad diagonal width");
+        if (level < 0 || level >= L) HB_THROW(HB_EINVAL, "GenerateLinearTransform: level out of range");
+        auto t = std::make_unique<LinTrans>();
+        t->level = level;
+        t->use_bsgs = ratio > 0 && n > 1;
+        int bs;
+        const char *env = std::getenv("HELRM_B200_BS");
+        if (t->use_bsgs) {
+            bs = std::max(1, (int)std::ceil(std::sqrt((double)n * ratio)));
+            if (env && *env) bs = std::max(1, std::atoi(env));
+        } else {
+            bs = slots;  // one giant group: every diagonal is a baby step
+        }
+        t->bs = bs;
+        std::set<int> seen;
+        for (int i = 0; i < n; i++) {
+            int k = idxs[i];
+            if (k < 0 || k >= slots) HB_THROW(HB_EINVAL, "GenerateLinearTransform: diagonal index out of range");
+            if (!seen.insert(k).second) HB_THROW(HB_EINVAL, "GenerateLinearTransform: duplicate diagonal index");
+            t->ks.push_back(k);
+        }
+        // encode every diagonal once (pre-rolled by g*bs), host FFTs in parallel
+        std::vector<std::vector<hi128>> coeffs(n);
+        int nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+        auto worker = [&](int tid) {
+            std::vector<double> inter((size_t)2 * width);
+            for (int i = tid; i < n; i += nthreads) {
+                const int k = idxs[i], g = t->use_bsgs ? k / bs : 0, shift = g * bs;
+                const double *vals = data + (size_t)i * width;
+                for (int s = 0; s < width; s++) {
+                    // numpy roll to the right by shift over the diagonal's own width
+                    int src = ((s - shift) % width + width) % width;
+                    inter[2 * s] = vals[src];
+                    inter[2 * s + 1] = 0.0;
+                }
+                encode_coeffs(logN, inter.data(), width, (long double)default_scale, coeffs[i]);
+            }
+        };
+        std::vector<std::thread> th;
+        for (int tid = 0; tid < nthreads; tid++) th.emplace_back(worker, tid);
+        for (auto &x : th) x.join();
+        for (int i = 0; i < n; i++) {
+            Pt p;
+            p.nq = level + 1;
+            p.ext = true;
+            p.scale = default_scale;
+            p.slots = slots;
+            p.d = alloc((size_t)(p.nq + K) * N);
+            upload_coeffs(coeffs[i], p.nq, true, p.d);
+            t->pts[idxs[i]] = p;
+            int k = idxs[i], g = t->use_bsgs ? k / bs : 0, b = t->use_bsgs ? k % bs : k;
+            t->groups[g].push_back({b, k});
+        }
+        int id = next_id++;
+        lts[id] = std::move(t);
+        return id;
+    }
+
+    std::vector<int> lt_rotation_keys(const LinTrans &t) {
+        std::set<int> d;
+        for (auto &kv : t.groups) {
+            int g = kv.first;
+            for (auto &bk : kv.second)
+                if (bk.first != 0) d.insert(bk.first);
+            if (g != 0) d.insert(g * t.bs);
+        }
+        return std::vector<int>(d.begin(), d.end());
+    }
+
+    void build_plan(LinTrans &t, int nq) {
+        if (t.plan_keygen == keygen_counter && t.plan_nq == nq) return;
+        for (auto *p : t.plan_dev) release(p);
+        t.plan_dev.clear();
+        t.plan_chunks.clear();
+        t.giant_of_slot.clear();
+        for (auto &kv : t.groups) t.giant_of_slot.push_back(kv.first);
+        const int nslots = (int)t.giant_of_slot.size();
+        for (int s0 = 0; s0 < nslots; s0 += HB_GCH) {
+            const int cnt = std::min(HB_GCH, nslots - s0);
+            std::map<int, BabyDesc> babies;
+            for (int gi = 0; gi < cnt; gi++) {
+                int g = t.giant_of_slot[s0 + gi];
+                for (auto &bk : t.groups[g]) {
+                    int b = bk.first;
+                    auto it = babies.find(b);
+                    if (it == babies.end()) {
+                        BabyDesc bd{};
+                        if (b == 0) {
+                            bd.galois = 1;
+                            bd.key = nullptr;
+                        } else {
+                            bd.galois = galois_of(b);
+                            auto kit = rot_keys.find(bd.galois);
+                            if (kit == rot_keys.end()) bd.key = rotation_key(bd.galois);
+                            else bd.key = kit->second;
+                        }
+                        it = babies.emplace(b, bd).first;
+                    }
+                    it->second.pt[gi] = t.pts[bk.second].d;
+                }
+            }
+            std::vector<BabyDesc> host;
+            for (auto &kv : babies) host.push_back(kv.second);
+            BabyDesc *dev = (BabyDesc *)alloc(host.size() * sizeof(BabyDesc) / 8 + 1);
+            cuda_check(cudaMemcpyAsync(dev, host.data(), host.size() * sizeof(BabyDesc), cudaMemcpyHostToDevice,
+                                       stream),
+                       "plan");
+            t.plan_dev.push_back(dev);
+            BsgsChunk ch;
+            ch.babies = dev;
+            ch.nbabies = (int)host.size();
+            ch.gbase = s0;
+            ch.gcount = cnt;
+            t.plan_chunks.push_back(ch);
+            sync();
+        }
+        // giant keys
+        for (int g : t.giant_of_slot)
+            if (g != 0) rotation_key(galois_of(g * t.bs));
+        t.plan_keygen = keygen_counter;
+        t.plan_nq = nq;
+    }
+
+    // Double-hoisted BSGS over nb ciphertexts packed at `in` ([nb][2][nq][N]);
+    // output [nb][2][nq][N] at `out`, scale ct*pt, not rescaled.
+    void lt_eval_packed(LinTrans &t, const u64 *in, int nq, int nb, u64 *out) {
+        build_plan(t, nq);
+        const int ne = nq + K, beta = beta_of(nq);
+        const size_t cts_ = (size_t)2 * nq * N, es = (size_t)ne * N;
+        const int nslots = (int)t.giant_of_slot.size();
+        u64 *D = alloc((size_t)nb * beta * es);
+        modup(D, in + (size_t)nq * N, nq, nb, cts_);
+        u64 *inner = alloc((size_t)nb * nslots * 2 * es);
+        for (auto &ch : t.plan_chunks)
+            bsgs_baby_mac(inner, in, D, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, nb, cts_,
+                          (size_t)beta * es, (size_t)nslots * 2 * es, stream);
+        release(D);
+        u64 *acc = alloc((size_t)nb * 2 * es);
+        bool acc_init = false;
+        for (int s = 0; s < nslots; s++) {
+            if (t.giant_of_slot[s] == 0) {
+                for (int b = 0; b < nb; b++)
+                    d2d(acc + (size_t)b * 2 * es, inner + ((size_t)b * nslots + s) * 2 * es, 2 * es);
+                acc_init = true;
+            }
+        }
+        if (!acc_init) zero(acc, (size_t)nb * 2 * es);
+        u64 *aq = alloc((size_t)nb * nq * N);
+        u64 *D2 = alloc((size_t)nb * beta * es);
+        for (int s = 0; s < nslots; s++) {
+            const int g = t.giant_of_slot[s];
+            if (g == 0) continue;
+            const u64 gal = galois_of(g * t.bs);
+            const u64 *key = rot_keys.at(gal);
+            const u64 *Ia = inner + (size_t)s * 2 * es + es;
+            moddown(aq, Ia, nq, nb, (size_t)nslots * 2 * es, (size_t)nq * N);
+            modup(D2, aq, nq, nb, (size_t)nq * N);
+            keymult(acc, D2, key, gal, nq, K, L, beta, P, inner + (size_t)s * 2 * es, true, logN, nb,
+                    (size_t)beta * es, 2 * es, (size_t)nslots * 2 * es, stream);
+        }
+        release(aq);
+        release(D2);
+        release(inner);
+        moddown(out, acc, nq, nb, 2 * es, cts_);
+        moddown(out + (size_t)nq * N, acc + es, nq, nb, 2 * es, cts_);
+        release(acc);
+    }
+
+    size_t lt_bytes_per_ct(const LinTrans &t, int nq) {
+        const int ne = nq + K, beta = beta_of(nq);
+        const size_t es = (size_t)ne * N * 8;
+        return (size_t)t.groups.size() * 2 * es + 3 * beta * es + 2 * es + (size_t)6 * nq * N * 8;
+    }
+
+    void eval_lt_batch(int ltid, const std::vector<int> &ids, std::vector<int> &outs) {
+        LinTrans &t = lt(ltid);
+        outs.assign(ids.size(), 0);
+        // group ciphertexts by the level they run at
+        std::map<int, std::vector<size_t>> bylevel;
+        for (size_t i = 0; i < ids.size(); i++) {
+            const Ct &c = ct(ids[i]);
+            if (c.npoly != 2) HB_THROW(HB_ESTATE, "EvaluateLinearTransform: input is degree-2; relinearize first");
+            bylevel[std::min(c.nq, t.level + 1)].push_back(i);
+        }
+        size_t free_b = 0, tot_b = 0;
+        cudaMemGetInfo(&free_b, &tot_b);
+        for (auto &kv : bylevel) {
+            const int nq = kv.first;
+            const auto &idx = kv.second;
+            size_t per = lt_bytes_per_ct(t, nq);
+            size_t budget = std::min<size_t>(free_b / 2, (size_t)48 << 30);
+            int chunk = (int)std::max<size_t>(1, std::min<size_t>(idx.size(), budget / std::max<size_t>(per, 1)));
+            const size_t cts_ = (size_t)2 * nq * N;
+            for (size_t c0 = 0; c0 < idx.size(); c0 += chunk) {
+                int nb = (int)std::min<size_t>(chunk, idx.size() - c0);
+                u64 *in = alloc((size_t)nb * cts_);
+                for (int b = 0; b < nb; b++) {
+                    const Ct &c = ct(ids[idx[c0 + b]]);
+                    d2d(in + (size_t)b * cts_, c.d, (size_t)nq * N);
+                    d2d(in + (size_t)b * cts_ + (size_t)nq * N, c.d + (size_t)c.nq * N, (size_t)nq * N);
+                }
+                u64 *out = alloc((size_t)nb * cts_);
+                lt_eval_packed(t, in, nq, nb, out);
+                release(in);
+                for (int b = 0; b < nb; b++) {
+                    const Ct &c = ct(ids[idx[c0 + b]]);
+                    Ct o = new_ct(nq, 2, c.scale * default_scale);
+                    o.slots = c.slots;
+                    d2d(o.d, out + (size_t)b * cts_, cts_);
+                    outs[idx[c0 + b]] = put_ct(o);
+                }
+                release(out);
+            }
+        }
+    }
+
+    void hybrid_fold(const std::vector<int> &ids, int rotations) {
+        if (ids.empty() || rotations <= 0) return;
+        std::map<int, std::vector<int>> bylevel;
+        for (int id : ids) bylevel[ct(id).nq].push_back(id);
+        for (auto &kv : bylevel) {
+            const int nq = kv.first;
+            const auto &v = kv.second;
+            const size_t cts_ = (size_t)2 * nq * N;
+            const int nb = (int)v.size();
+            u64 *buf = alloc((size_t)nb * cts_), *rot = alloc((size_t)nb * cts_);
+            for (int b = 0; b < nb; b++) d2d(buf + (size_t)b * cts_, ct(v[b]).d, cts_);
+            for (int i = 1; i <= rotations; i++) {
+                int k = slots >> i;
+                u64 g = galois_of(k);
+                u64 *key = rotation_key(g);
+                rotate_batch(rot, buf, nq, nb, g, key);
+                ew_add(buf, buf, rot, nb * 2 * nq, qmap(nq), logN, stream);
+            }
+            for (int b = 0; b < nb; b++) d2d(ct(v[b]).d, buf + (size_t)b * cts_, cts_);
+            release(buf);
+            release(rot);
+        }
+    }
+};
+
+static std::unique_ptr<Context> g_ctx;
+static std::string g_err;
+
+static Context &C() {
+    if (!g_ctx) HB_THROW(HB_ESTATE, "B200 backend not initialised. Call NewScheme first.");
+    return *g_ctx;
+}
+
+}  // namespace hb
+
+using namespace hb;
+
+#define HB_API extern "C" __attribute__((visibility("default")))
+
+template <class F>
+static int guard(F &&f) {
+    try {
+        f();
+        return HB_OK;
+    } catch (const HbError &e) {
+        g_err = e.what();
+        return e.code;
+    } catch (const std::invalid_argument &e) {
+        g_err = e.what();
+        return HB_EINVAL;
+    } catch (const std::out_of_range &e) {
+        g_err = e.what();
+        return HB_ENOENT;
+    } catch (const std::bad_alloc &e) {
+        g_err = "host allocation failed";
+        return HB_ENOMEM;
+    } catch (const std::exception &e) {
+        g_err = e.what();
+        return HB_ECUDA;
+    }
+}
+
+#define OUT(p) \
+    if (!(p)) HB_THROW(HB_EINVAL, "null output pointer")
+
+HB_API const char *helrm_LastError(void) { return g_err.c_str(); }
+
+HB_API int helrm_NewScheme(int logn, const int *logq, int nlogq, const int *logp, int nlogp, int logscale,
+                           int hamming_weight, int dnum, uint64_t seed, int device) {
+    return guard([&] {
+        if (!logq || !logp || nlogq <= 0 || nlogp <= 0) HB_THROW(HB_EINVAL, "LogQ/LogP required");
+        g_ctx.reset();
+        auto c = std::make_unique<Context>();
+        c->setup(logn, std::vector<int>(logq, logq + nlogq), std::vector<int>(logp, logp + nlogp), logscale,
+                 hamming_weight, dnum, seed, device);
+        g_ctx = std::move(c);
+    });
+}
+
+HB_API int helrm_DeleteScheme(void) {
+    return guard([&] { g_ctx.reset(); });
+}
+
+HB_API int helrm_GetModuliChain(uint64_t *out, int cap, int *n) {
+    return guard([&] {
+        Context &c = C();
+        OUT(n);
+        *n = c.L;
+        for (int i = 0; i < c.L && i < cap; i++) out[i] = c.primes[i];
+    });
+}
+HB_API int helrm_GetAuxModuliChain(uint64_t *out, int cap, int *n) {
+    return guard([&] {
+        Context &c = C();
+        OUT(n);
+        *n = c.K;
+        for (int i = 0; i < c.K && i < cap; i++) out[i] = c.primes[c.L + i];
+    });
+}
+HB_API int helrm_GetSchemeInfo(int *logn, int *slots, int *max_level, int *alpha, int *dnum) {
+    return guard([&] {
+        Context &c = C();
+        if (logn) *logn = c.logN;
+        if (slots) *slots = c.slots;
+        if (max_level) *max_level = c.L - 1;
+        if (alpha) *alpha = c.alpha;
+        if (dnum) *dnum = c.dnum;
+    });
+}
+
+HB_API int helrm_GenPrimes(int logn, const int *bits, int n, const uint64_t *used, int nused, uint64_t *out) {
+    return guard([&] {
+        if (!bits || !out || n < 0 || nused < 0 || (nused > 0 && !used)) HB_THROW(HB_EINVAL, "GenPrimes: bad arguments");
+        std::vector<u64> u(used, used + nused);
+        std::vector<u64> p = gen_primes(std::vector<int>(bits, bits + n), logn, u);
+        for (int i = 0; i < n; i++) out[i] = p[i];
+    });
+}
+
+HB_API int helrm_GenerateSecretKey(void) {
+    return guard([&] { C().gen_secret(); });
+}
+HB_API int helrm_GeneratePublicKey(void) {
+    return guard([&] { C().require_sk(); });
+}
+HB_API int helrm_GenerateRelinearizationKey(void) {
+    return guard([&] {
+        C().gen_relin();
+        C().sync();
+    });
+}
+HB_API int helrm_GenerateEvaluationKeys(void) {
+    return guard([&] {
+        Context &c = C();
+        c.rotation_key(2ull * c.N - 1);
+        c.sync();
+    });
+}
+HB_API int helrm_AddRotationKey(int k) {
+    return guard([&] {
+        Context &c = C();
+        u64 g = c.galois_of(k);
+        if (g == 1) return;
+        c.rotation_key(g);
+        c.sync();
+    });
+}
+
+HB_API int helrm_Encode(const double *values, int n, int level, double scale, int *out_pt) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out_pt);
+        if (n < 0 || (n > 0 && !values)) HB_THROW(HB_EINVAL, "encode: bad values");
+        std::vector<double> inter((size_t)2 * n);
+        for (int i = 0; i < n; i++) {
+            inter[2 * i] = values[i];
+            inter[2 * i + 1] = 0.0;
+        }
+        *out_pt = c.encode(inter.data(), n, level, scale, false);
+    });
+}
+HB_API int helrm_EncodeComplex(const double *inter, int n, int level, double scale, int *out_pt) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out_pt);
+        if (n < 0 || (n > 0 && !inter)) HB_THROW(HB_EINVAL, "encode: bad values");
+        *out_pt = c.encode(inter, n, level, scale, false);
+    });
+}
+static void decode_impl(int pt, double *out, int cap, int *n, bool cplx) {
+    Context &c = C();
+    OUT(n);
+    const Pt &p = c.pt(pt);
+    std::vector<double> vals;
+    c.decode_rows(p.d, p.nq, p.scale, vals);
+    int cnt = std::min(cap, c.slots);
+    if (cplx) {
+        for (int i = 0; i < cnt; i++) {
+            out[2 * i] = vals[2 * i];
+            out[2 * i + 1] = vals[2 * i + 1];
+        }
+    } else {
+        for (int i = 0; i < cnt; i++) out[i] = vals[2 * i];
+    }
+    *n = cnt;
+}
+HB_API int helrm_Decode(int pt, double *out, int cap, int *n) {
+    return guard([&] { decode_impl(pt, out, cap, n, false); });
+}
+HB_API int helrm_DecodeComplex(int pt, double *out, int cap, int *n) {
+    return guard([&] { decode_impl(pt, out, cap, n, true); });
+}
+
+HB_API int helrm_Encrypt(int pt, int *out_ct) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out_ct);
+        const Pt &p = c.pt(pt);
+        u64 ct_seed = hrand64(c.seed, 1000, c.enc_counter++);
+        Ct o = c.encrypt_rows(p.d, p.nq, p.scale, ct_seed);
+        o.slots = p.slots;
+        *out_ct = c.put_ct(o);
+    });
+}
+HB_API int helrm_EncryptSeeded(int pt, uint64_t seed, int *out_ct) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out_ct);
+        const Pt &p = c.pt(pt);
+        Ct o = c.encrypt_rows(p.d, p.nq, p.scale, seed);
+        o.slots = p.slots;
+        *out_ct = c.put_ct(o);
+    });
+}
+HB_API int helrm_DropAx(int ct) {
+    return guard([&] {
+        Context &c = C();
+        Ct &x = c.ct(ct);
+        c.zero(x.d + (size_t)x.nq * c.N, (size_t)x.nq * c.N);
+    });
+}
+HB_API int helrm_ExpandSeededAx(int ct, uint64_t seed) {
+    return guard([&] {
+        Context &c = C();
+        Ct &x = c.ct(ct);
+        sample_uniform(x.d + (size_t)x.nq * c.N, x.nq, nullptr, c.qmap(x.nq), seed, DOM_ENC_A, 0, 0, c.logN,
+                       c.stream);
+    });
+}
+HB_API int helrm_Decrypt(int ct, int *out_pt) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out_pt);
+        c.require_sk();
+        const Ct &x = c.ct(ct);
+        const u64 *src = x.d;
+        u64 *tmp = nullptr;
+        if (x.npoly == 3) {
+            if (!c.d_rlk) c.gen_relin();
+            tmp = c.alloc((size_t)2 * x.nq * c.N);
+            c.relinearize(tmp, x.d, x.nq);
+            src = tmp;
+        }
+        Pt p;
+        p.nq = x.nq;
+        p.scale = x.scale;
+        p.slots = x.slots;
+        p.d = c.alloc((size_t)x.nq * c.N);
+        ew_decrypt(p.d, src, c.d_sk, x.nq, c.logN, c.stream);
+        if (tmp) c.release(tmp);
+        *out_pt = c.put_pt(p);
+    });
+}
+
+#define NEW_AND_INPLACE2(NAME, EXPR)                                           \
+    HB_API int helrm_##NAME##New(int a, int b, int *out) {                     \
+        return guard([&] {                                                     \
+            Context &c = C();                                                  \
+            OUT(out);                                                          \
+            *out = (EXPR);                                                     \
+        });                                                                    \
+    }                                                                          \
+    HB_API int helrm_##NAME(int a, int b) {                                    \
+        return guard([&] {                                                     \
+            Context &c = C();                                                  \
+            int o = (EXPR);                                                    \
+            c.replace_ct(a, o);                                                \
+        });                                                                    \
+    }
+
+NEW_AND_INPLACE2(AddCiphertext, c.add_sub(a, b, false))
+NEW_AND_INPLACE2(SubCiphertext, c.add_sub(a, b, true))
+NEW_AND_INPLACE2(AddPlaintext, c.add_plain(a, b, false))
+NEW_AND_INPLACE2(SubPlaintext, c.add_plain(a, b, true))
+NEW_AND_INPLACE2(MulPlaintext, c.mul_plain(a, b))
+
+static int mul_relin(Context &c, int a, int b) {
+    if (!c.d_rlk) c.gen_relin();
+    const Ct &ca = c.ct(a), &cb = c.ct(b);
+    if (ca.npoly != 2 || cb.npoly != 2) HB_THROW(HB_ESTATE, "MulRelinCiphertext: operand is degree-2");
+    int nq = std::min(ca.nq, cb.nq);
+    Ct x = ca.nq == nq ? ca : c.drop_to(ca, nq);
+    Ct y = cb.nq == nq ? cb : c.drop_to(cb, nq);
+    u64 *t3 = c.alloc((size_t)3 * nq * c.N);
+    ew_tensor(t3, x.d, y.d, nq, c.logN, c.stream);
+    Ct o = c.new_ct(nq, 2, ca.scale * cb.scale);
+    o.slots = std::max(ca.slots, cb.slots);
+    c.relinearize(o.d, t3, nq);
+    c.release(t3);
+    if (x.d != ca.d) c.release(x.d);
+    if (y.d != cb.d) c.release(y.d);
+    return c.put_ct(o);
+}
+NEW_AND_INPLACE2(MulRelinCiphertext, mul_relin(c, a, b))
+
+HB_API int helrm_Negate(int ct) {
+    return guard([&] {
+        Context &c = C();
+        Ct &x = c.ct(ct);
+        ew_neg(x.d, x.d, x.npoly * x.nq, c.qmap(x.nq), c.logN, c.stream);
+    });
+}
+
+HB_API int helrm_MulPlaintextAccumNew(const int *cts, const int *pts, int n, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        if (n <= 0 || !cts || !pts) HB_THROW(HB_EINVAL, "MulPlaintextAccumNew: empty input");
+        *out = c.mac(std::vector<int>(cts, cts + n), std::vector<int>(pts, pts + n));
+    });
+}
+
+#define SCALAR_OPS(NAME, KIND, T)                                              \
+    HB_API int helrm_##NAME##New(int ct, T s, int *out) {                      \
+        return guard([&] {                                                     \
+            Context &c = C();                                                  \
+            OUT(out);                                                          \
+            *out = c.scalar_op(ct, (long double)s, KIND);                      \
+        });                                                                    \
+    }                                                                          \
+    HB_API int helrm_##NAME(int ct, T s) {                                     \
+        return guard([&] {                                                     \
+            Context &c = C();                                                  \
+            int o = c.scalar_op(ct, (long double)s, KIND);                     \
+            c.replace_ct(ct, o);                                               \
+        });                                                                    \
+    }
+SCALAR_OPS(AddScalar, 0, double)
+SCALAR_OPS(SubScalar, 1, double)
+SCALAR_OPS(MulScalarInt, 2, int64_t)
+SCALAR_OPS(MulScalarFloat, 3, double)
+
+static int rescale_new(Context &c, int id) {
+    const Ct &x = c.ct(id);
+    if (x.nq < 2) HB_THROW(HB_ESTATE, "RescaleNew: ciphertext already at level 0.");
+    Ct o = c.new_ct(x.nq - 1, x.npoly, x.scale / (double)c.primes[x.nq - 1]);
+    o.slots = x.slots;
+    c.rescale(o.d, x.d, x.npoly, x.nq, 1, 0, 0);
+    return c.put_ct(o);
+}
+HB_API int helrm_RescaleNew(int ct, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        *out = rescale_new(c, ct);
+    });
+}
+HB_API int helrm_Rescale(int ct) {
+    return guard([&] {
+        Context &c = C();
+        int o = rescale_new(c, ct);
+        c.replace_ct(ct, o);
+    });
+}
+HB_API int helrm_RescaleBatch(const int *cts, int n) {
+    return guard([&] {
+        Context &c = C();
+        for (int i = 0; i < n; i++) {
+            int o = rescale_new(c, cts[i]);
+            c.replace_ct(cts[i], o);
+        }
+    });
+}
+
+HB_API int helrm_AlignToLevelNew(int ct, int level, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        const Ct &x = c.ct(ct);
+        if (x.nq - 1 < level)
+            HB_THROW(HB_ESTATE, "AlignToLevelNew: input level " + std::to_string(x.nq - 1) + " below target " +
+                                    std::to_string(level) + ".");
+        if (level < 0) HB_THROW(HB_EINVAL, "AlignToLevelNew: negative level");
+        *out = c.put_ct(c.drop_to(x, level + 1));
+    });
+}
+
+static int rotate_new(Context &c, int id, int k) {
+    const Ct &x = c.ct(id);
+    if (x.npoly != 2) HB_THROW(HB_ESTATE, "RotateNew: input is degree-2; relinearize first.");
+    u64 g = c.galois_of(k);
+    if (g == 1) return c.put_ct(c.drop_to(x, x.nq));
+    u64 *key = c.rotation_key(g);
+    Ct o = c.new_ct(x.nq, 2, x.scale);
+    o.slots = x.slots;
+    c.rotate_batch(o.d, x.d, x.nq, 1, g, key);
+    return c.put_ct(o);
+}
+HB_API int helrm_RotateNew(int ct, int k, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        *out = rotate_new(c, ct, k);
+    });
+}
+HB_API int helrm_Rotate(int ct, int k) {
+    return guard([&] {
+        Context &c = C();
+        int o = rotate_new(c, ct, k);
+        c.replace_ct(ct, o);
+    });
+}
+static int conj_new(Context &c, int id) {
+    const Ct &x = c.ct(id);
+    if (x.npoly != 2) HB_THROW(HB_ESTATE, "ConjugateNew: input is degree-2; relinearize first.");
+    u64 g = 2ull * c.N - 1;
+    u64 *key = c.rotation_key(g);
+    Ct o = c.new_ct(x.nq, 2, x.scale);
+    o.slots = x.slots;
+    c.rotate_batch(o.d, x.d, x.nq, 1, g, key);
+    return c.put_ct(o);
+}
+HB_API int helrm_ConjugateNew(int ct, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        *out = conj_new(c, ct);
+    });
+}
+HB_API int helrm_Conjugate(int ct) {
+    return guard([&] {
+        Context &c = C();
+        int o = conj_new(c, ct);
+        c.replace_ct(ct, o);
+    });
+}
+
+HB_API int helrm_RotateBatchNew(int ct, const int *ks, int n, int *outs) {
+    return guard([&] {
+        Context &c = C();
+        if (n <= 0) return;
+        if (!ks || !outs) HB_THROW(HB_EINVAL, "RotateBatchNew: null array");
+        const Ct &x = c.ct(ct);
+        if (x.npoly != 2) HB_THROW(HB_ESTATE, "RotateBatchNew: input is degree-2; relinearize first.");
+        std::vector<u64> gs;
+        std::vector<int> pos;
+        std::vector<u64 *> bufs;
+        std::vector<int> ids(n, 0);
+        for (int i = 0; i < n; i++) {
+            u64 g = c.galois_of(ks[i]);
+            if (g == 1) {
+                ids[i] = c.put_ct(c.drop_to(x, x.nq));
+                continue;
+            }
+            Ct o = c.new_ct(x.nq, 2, x.scale);
+            o.slots = x.slots;
+            ids[i] = c.put_ct(o);
+            gs.push_back(g);
+            bufs.push_back(o.d);
+        }
+        if (!gs.empty()) c.rotate_hoisted(x.d, x.nq, 1, gs, bufs, 0);
+        for (int i = 0; i < n; i++) outs[i] = ids[i];
+    });
+}
+
+HB_API int helrm_GenerateLinearTransform(const int *diag_idxs, int n, const double *data, int width, int level,
+                                         double bsgs_ratio, int *out_lt) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out_lt);
+        if (!diag_idxs || !data) HB_THROW(HB_EINVAL, "GenerateLinearTransform: null input");
+        *out_lt = c.generate_lt(diag_idxs, n, data, width, level, bsgs_ratio);
+    });
+}
+HB_API int helrm_EvaluateLinearTransformBatch(int lt, const int *cts, int n, int *outs) {
+    return guard([&] {
+        Context &c = C();
+        if (n <= 0) return;
+        if (!cts || !outs) HB_THROW(HB_EINVAL, "EvaluateLinearTransformBatch: null array");
+        std::vector<int> o;
+        c.eval_lt_batch(lt, std::vector<int>(cts, cts + n), o);
+        for (int i = 0; i < n; i++) outs[i] = o[i];
+    });
+}
+HB_API int helrm_EvaluateLinearTransform(int lt, int ct, int *out) {
+    return helrm_EvaluateLinearTransformBatch(lt, &ct, 1, out);
+}
+HB_API int helrm_DeleteLinearTransform(int lt) {
+    return guard([&] {
+        Context &c = C();
+        auto it = c.lts.find(lt);
+        if (it == c.lts.end()) return;
+        c.sync();
+        c.free_lt(*it->second);
+        c.lts.erase(it);
+    });
+}
+HB_API int helrm_GetLinearTransformRotationKeys(int lt, int *out, int cap, int *n) {
+    return guard([&] {
+        Context &c = C();
+        OUT(n);
+        auto v = c.lt_rotation_keys(c.lt(lt));
+        *n = (int)v.size();
+        for (int i = 0; i < (int)v.size() && i < cap; i++) out[i] = v[i];
+    });
+}
+HB_API int helrm_GetLinearTransformInfo(int lt, int *bs, int *ndiag, int *ngiant, int *level) {
+    return guard([&] {
+        Context &c = C();
+        LinTrans &t = c.lt(lt);
+        if (bs) *bs = t.use_bsgs ? t.bs : 0;
+        if (ndiag) *ndiag = (int)t.ks.size();
+        if (ngiant) *ngiant = (int)t.groups.size();
+        if (level) *level = t.level;
+    });
+}
+HB_API int helrm_HybridFoldBatch(const int *cts, int n, int rotations) {
+    return guard([&] {
+        Context &c = C();
+        if (n <= 0) return;
+        c.hybrid_fold(std::vector<int>(cts, cts + n), rotations);
+    });
+}
+
+HB_API int helrm_DeleteCiphertext(int ct) {
+    return guard([&] {
+        if (g_ctx) g_ctx->del_ct(ct);
+    });
+}
+HB_API int helrm_DeletePlaintext(int pt) {
+    return guard([&] {
+        if (g_ctx) g_ctx->del_pt(pt);
+    });
+}
+HB_API int helrm_GetCiphertextLevel(int ct, int *level) {
+    return guard([&] {
+        OUT(level);
+        *level = C().ct(ct).nq - 1;
+    });
+}
+HB_API int helrm_GetPlaintextLevel(int pt, int *level) {
+    return guard([&] {
+        OUT(level);
+        *level = C().pt(pt).nq - 1;
+    });
+}
+HB_API int helrm_GetCiphertextScale(int ct, double *scale) {
+    return guard([&] {
+        OUT(scale);
+        *scale = C().ct(ct).scale;
+    });
+}
+HB_API int helrm_GetPlaintextScale(int pt, double *scale) {
+    return guard([&] {
+        OUT(scale);
+        *scale = C().pt(pt).scale;
+    });
+}
+HB_API int helrm_SetCiphertextScale(int ct, double scale) {
+    return guard([&] { C().ct(ct).scale = scale; });
+}
+HB_API int helrm_SetPlaintextScale(int pt, double scale) {
+    return guard([&] { C().pt(pt).scale = scale; });
+}
+HB_API int helrm_GetCiphertextSlots(int ct, int *s) {
+    return guard([&] {
+        OUT(s);
+        *s = C().ct(ct).slots;
+    });
+}
+HB_API int helrm_GetPlaintextSlots(int pt, int *s) {
+    return guard([&] {
+        OUT(s);
+        *s = C().pt(pt).slots;
+    });
+}
+HB_API int helrm_SetCiphertextSlots(int ct, int slots) {
+    return guard([&] {
+        Context &c = C();
+        Ct &x = c.ct(ct);
+        if (slots <= 0 || slots > x.slots || x.slots % slots != 0)
+            HB_THROW(HB_EINVAL, "SetCiphertextSlots: narrowing retag only (divisor of the current width)");
+        x.slots = slots;
+    });
+}
+HB_API int helrm_GetCiphertextDegree(int ct, int *d) {
+    return guard([&] {
+        OUT(d);
+        *d = C().ct(ct).npoly - 1;
+    });
+}
+HB_API int helrm_GetLiveCounts(int *cts, int *pts) {
+    return guard([&] {
+        Context &c = C();
+        if (cts) *cts = (int)c.cts.size();
+        if (pts) *pts = (int)c.pts.size();
+    });
+}
+HB_API int helrm_GetCiphertextBytes(int ct, double *bytes) {
+    return guard([&] {
+        Context &c = C();
+        OUT(bytes);
+        const Ct &x = c.ct(ct);
+        *bytes = (double)x.npoly * x.nq * c.N * 8;
+    });
+}
+HB_API int helrm_GetMemoryMB(double *live, double *peak, double *keys) {
+    return guard([&] {
+        Context &c = C();
+        if (live) *live = c.live / 1048576.0;
+        if (peak) *peak = c.peak / 1048576.0;
+        if (keys) *keys = c.key_bytes / 1048576.0;
+    });
+}
+
+HB_API int helrm_GetCiphertextData(int ct, uint64_t *out, size_t words) {
+    return guard([&] {
+        Context &c = C();
+        const Ct &x = c.ct(ct);
+        size_t need = (size_t)x.npoly * x.nq * c.N;
+        if (!out || words < need) HB_THROW(HB_EINVAL, "GetCiphertextData: buffer too small");
+        cuda_check(cudaMemcpyAsync(out, x.d, need * 8, cudaMemcpyDeviceToHost, c.stream), "d2h");
+        c.sync();
+    });
+}
+HB_API int helrm_NewCiphertextFromData(const uint64_t *data, int level, int npoly, double scale, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        if (level < 0 || level >= c.L || npoly < 2 || npoly > 3 || !data)
+            HB_THROW(HB_EINVAL, "NewCiphertextFromData: bad level/degree");
+        Ct o = c.new_ct(level + 1, npoly, scale);
+        cuda_check(cudaMemcpyAsync(o.d, data, (size_t)npoly * (level + 1) * c.N * 8, cudaMemcpyHostToDevice,
+                                   c.stream),
+                   "h2d");
+        c.sync();
+        *out = c.put_ct(o);
+    });
+}
+HB_API int helrm_GetPlaintextData(int pt, uint64_t *out, size_t words) {
+    return guard([&] {
+        Context &c = C();
+        const Pt &p = c.pt(pt);
+        size_t need = (size_t)(p.nq + (p.ext ? c.K : 0)) * c.N;
+        if (!out || words < need) HB_THROW(HB_EINVAL, "GetPlaintextData: buffer too small");
+        cuda_check(cudaMemcpyAsync(out, p.d, need * 8, cudaMemcpyDeviceToHost, c.stream), "d2h");
+        c.sync();
+    });
+}
+HB_API int helrm_NewPlaintextFromData(const uint64_t *data, int level, int ext, double scale, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        if (level < 0 || level >= c.L || !data) HB_THROW(HB_EINVAL, "NewPlaintextFromData: bad level");
+        Pt p;
+        p.nq = level + 1;
+        p.ext = ext != 0;
+        p.scale = scale;
+        p.slots = c.slots;
+        size_t words = (size_t)(p.nq + (p.ext ? c.K : 0)) * c.N;
+        p.d = c.alloc(words);
+        cuda_check(cudaMemcpyAsync(p.d, data, words * 8, cudaMemcpyHostToDevice, c.stream), "h2d");
+        c.sync();
+        *out = c.put_pt(p);
+    });
+}
+HB_API int helrm_GetKeyData(uint64_t galois, uint64_t *out, size_t words) {
+    return guard([&] {
+        Context &c = C();
+        if (!out || words < c.key_words()) HB_THROW(HB_EINVAL, "GetKeyData: buffer too small");
+        const u64 *k = nullptr;
+        if (galois == 0) {
+            if (!c.d_rlk) HB_THROW(HB_ENOENT, "no relinearisation key");
+            k = c.d_rlk;
+        } else {
+            auto it = c.rot_keys.find(galois);
+            if (it == c.rot_keys.end()) HB_THROW(HB_ENOENT, "no key for this Galois element");
+            k = it->second;
+        }
+        cuda_check(cudaMemcpyAsync(out, k, c.key_words() * 8, cudaMemcpyDeviceToHost, c.stream), "d2h");
+        c.sync();
+    });
+}
+HB_API int helrm_GetSecretKeyData(uint64_t *out, size_t words) {
+    return guard([&] {
+        Context &c = C();
+        c.require_sk();
+        if (!out || words < (size_t)c.P * c.N) HB_THROW(HB_EINVAL, "GetSecretKeyData: buffer too small");
+        cuda_check(cudaMemcpyAsync(out, c.d_sk, (size_t)c.P * c.N * 8, cudaMemcpyDeviceToHost, c.stream), "d2h");
+        c.sync();
+    });
+}
+HB_API int helrm_GetLinearTransformPlaintext(int lt, int k, uint64_t *out, size_t words) {
+    return guard([&] {
+        Context &c = C();
+        LinTrans &t = c.lt(lt);
+        auto it = t.pts.find(k);
+        if (it == t.pts.end()) HB_THROW(HB_ENOENT, "no such diagonal");
+        size_t need = (size_t)(it->second.nq + c.K) * c.N;
+        if (!out || words < need) HB_THROW(HB_EINVAL, "buffer too small");
+        cuda_check(cudaMemcpyAsync(out, it->second.d, need * 8, cudaMemcpyDeviceToHost, c.stream), "d2h");
+        c.sync();
+    });
+}
+
+HB_API int helrm_kernel_ntt(uint64_t *d, int nrows, int per, int nq, int inverse, void *stream) {
+    return guard([&] {
+        Context &c = C();
+        if (!d || nrows <= 0 || per <= 0 || nq < 0 || nq > c.L || per - nq > c.K)
+            HB_THROW(HB_EINVAL, "kernel_ntt: bad arguments");
+        cudaStream_t s = stream ? (cudaStream_t)stream : c.stream;
+        if (inverse)
+            ntt_inverse((u64 *)d, nrows, rowmap(per, nq, c.L), c.ntt, s);
+        else
+            ntt_forward((u64 *)d, nrows, rowmap(per, nq, c.L), c.ntt, s);
+    });
+}
+HB_API int helrm_kernel_automorphism(const uint64_t *in, uint64_t *out, int nrows, uint64_t galois, void *stream) {
+    return guard([&] {
+        Context &c = C();
+        if (!in || !out || nrows <= 0 || (galois & 1) == 0) HB_THROW(HB_EINVAL, "kernel_automorphism: bad arguments");
+        ew_automorphism((u64 *)out, (const u64 *)in, nrows, galois % (2ull * c.N), c.logN,
+                        stream ? (cudaStream_t)stream : c.stream);
+    });
+}
+HB_API int helrm_kernel_rescale(const uint64_t *in, uint64_t *out, int nq, int nbatch, void *stream) {
+    return guard([&] {
+        Context &c = C();
+        if (!in || !out || nq < 2 || nq > c.L || nbatch <= 0) HB_THROW(HB_EINVAL, "kernel_rescale: bad arguments");
+        cudaStream_t old = c.stream;
+        if (stream) c.stream = (cudaStream_t)stream;
+        try {
+            c.rescale((u64 *)out, (const u64 *)in, 2, nq, nbatch, (size_t)2 * nq * c.N, (size_t)2 * (nq - 1) * c.N);
+        } catch (...) {
+            c.stream = old;
+            throw;
+        }
+        c.stream = old;
+    });
+}
+HB_API int helrm_kernel_mac(const uint64_t *const *cts, const uint64_t *const *pts, int nterms, int nq, uint64_t *out,
+                            void *stream) {
+    return guard([&] {
+        Context &c = C();
+        if (!cts || !pts || !out || nterms <= 0 || nterms > HB_MAC_MAX || nq <= 0 || nq > c.L)
+            HB_THROW(HB_EINVAL, "kernel_mac: bad arguments");
+        MacArgs m{};
+        for (int t = 0; t < nterms; t++) {
+            m.ct[t] = (const u64 *)cts[t];
+            m.pt[t] = (const u64 *)pts[t];
+        }
+        m.n = nterms;
+        ew_mac((u64 *)out, m, 2, nq, c.logN, stream ? (cudaStream_t)stream : c.stream);
+    });
+}
+HB_API int helrm_kernel_rotate_hoisted(const uint64_t *in, int nq, int nbatch, const int *ks, int nrot, uint64_t *out,
+                                       void *stream) {
+    return guard([&] {
+        Context &c = C();
+        if (!in || !out || !ks || nq <= 0 || nq > c.L || nbatch <= 0 || nrot <= 0)
+            HB_THROW(HB_EINVAL, "kernel_rotate_hoisted: bad arguments");
+        std::vector<u64> gs;
+        std::vector<u64 *> outs;
+        const size_t per = (size_t)nbatch * 2 * nq * c.N;
+        for (int r = 0; r < nrot; r++) {
+            u64 g = c.galois_of(ks[r]);
+            if (g == 1) HB_THROW(HB_EINVAL, "kernel_rotate_hoisted: zero shift");
+            if (!c.rot_keys.count(g)) HB_THROW(HB_ESTATE, "kernel_rotate_hoisted: missing rotation key");
+            gs.push_back(g);
+            outs.push_back((u64 *)out + r * per);
+        }
+        cudaStream_t old = c.stream;
+        if (stream) c.stream = (cudaStream_t)stream;
+        try {
+            c.rotate_hoisted((const u64 *)in, nq, nbatch, gs, outs, (size_t)2 * nq * c.N);
+        } catch (...) {
+            c.stream = old;
+            throw;
+        }
+        c.stream = old;
+    });
+}
+HB_API int helrm_Synchronize(void) {
+    return guard([&] { C().sync(); });
+}

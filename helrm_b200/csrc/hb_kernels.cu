@@ -1,0 +1,800 @@
+// hb_kernels.cu -- sm_100a kernels of the B200 CKKS backend.
+//
+// All residues are 64-bit words below q < 2^61, limb-major in HBM.  The
+// kernels are integer CUDA-core code: modular arithmetic is not a dense
+// MMA, so no tensor cores are involved.  Data that a kernel reads more
+// than once per thread block (NTT twiddle tiles, the per-chunk baby-step
+// descriptors) is staged in shared memory; everything else streams with
+// 16-byte vector accesses.
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "hb_kernels.cuh"
+
+namespace hb {
+
+__constant__ PrimeConst c_pc[HB_MAX_PRIMES];
+
+static void check_launch(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void upload_prime_consts(const PrimeConst *pc, int n) {
+    cudaError_t e = cudaMemcpyToSymbol(c_pc, pc, sizeof(PrimeConst) * n);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("prime constants: ") + cudaGetErrorString(e));
+}
+
+static inline unsigned grid1d(size_t work, int block) {
+    size_t g = (work + block - 1) / block;
+    return (unsigned)(g ? g : 1);
+}
+
+// =====================================================================
+// NTT.  N = N1 * N2.  Forward (Cooley-Tukey, bit-reversed output): the
+// first log2(N1) stages pair elements N2 apart and stay inside a column
+// {k*N2 + c}; the last log2(N2) stages stay inside a contiguous block of
+// N2.  Pass 1 runs the column stages on a tile of C columns, pass 2 the
+// block stages on RB blocks; each pass stages its tile in shared memory.
+// The inverse (Gentleman-Sande) runs the block stages first.
+// =====================================================================
+static inline int split_log1(int logN) { return logN / 2; }
+
+template <bool INV>
+__global__ void __launch_bounds__(256) k_ntt_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+                                                   const u64 *__restrict__ twp, int logN, int logN1, int logC,
+                                                   int row0) {
+    extern __shared__ u64 sm[];
+    const int row = row0 + blockIdx.y;
+    if (map.skip(row)) return;
+    const int p = map.prime(row);
+    const u64 q = c_pc[p].q;
+    const int N = 1 << logN, N1 = 1 << logN1, N2 = N >> logN1, C = 1 << logC;
+    const int c0 = blockIdx.x << logC;
+    u64 *a = data + (size_t)row * N;
+    const u64 *W = tw + (size_t)p * N, *Wp = twp + (size_t)p * N;
+    for (int idx = threadIdx.x; idx < (N1 << logC); idx += blockDim.x) {
+        int k = idx >> logC, c = idx & (C - 1);
+        sm[idx] = a[(size_t)k * N2 + c0 + c];
+    }
+    __syncthreads();
+    const int nbf = (N1 >> 1) << logC;
+    if (!INV) {
+        for (int m = 1, lt = logN1 - 1; m < N1; m <<= 1, lt--) {
+            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
+                int c = bf & (C - 1), j = bf >> logC;
+                int i = j >> lt, jj = j & ((1 << lt) - 1);
+                int k1 = (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
+                u64 w = __ldg(W + m + i), wp = __ldg(Wp + m + i);
+                u64 U = sm[(k1 << logC) + c];
+                u64 V = mul_shoup(sm[(k2 << logC) + c], w, wp, q);
+                sm[(k1 << logC) + c] = add_mod(U, V, q);
+                sm[(k2 << logC) + c] = sub_mod(U, V, q);
+            }
+            __syncthreads();
+        }
+        for (int idx = threadIdx.x; idx < (N1 << logC); idx += blockDim.x) {
+            int k = idx >> logC, c = idx & (C - 1);
+            a[(size_t)k * N2 + c0 + c] = sm[idx];
+        }
+    } else {
+        for (int h = N1 >> 1, lt = 0; h >= 1; h >>= 1, lt++) {
+            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
+                int c = bf & (C - 1), j = bf >> logC;
+                int i = j >> lt, jj = j & ((1 << lt) - 1);
+                int k1 = (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
+                u64 w = __ldg(W + h + i), wp = __ldg(Wp + h + i);
+                u64 U = sm[(k1 << logC) + c], V = sm[(k2 << logC) + c];
+                sm[(k1 << logC) + c] = add_mod(U, V, q);
+                sm[(k2 << logC) + c] = mul_shoup(sub_mod(U, V, q), w, wp, q);
+            }
+            __syncthreads();
+        }
+        const u64 ni = c_pc[p].ninv, nip = c_pc[p].ninvp;
+        for (int idx = threadIdx.x; idx < (N1 << logC); idx += blockDim.x) {
+            int k = idx >> logC, c = idx & (C - 1);
+            a[(size_t)k * N2 + c0 + c] = mul_shoup(sm[idx], ni, nip, q);
+        }
+    }
+}
+
+template <bool INV>
+__global__ void __launch_bounds__(256) k_ntt_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+                                                   const u64 *__restrict__ twp, int logN, int logN1, int logRB,
+                                                   int row0) {
+    extern __shared__ u64 sm[];
+    const int row = row0 + blockIdx.y;
+    if (map.skip(row)) return;
+    const int p = map.prime(row);
+    const u64 q = c_pc[p].q;
+    const int N = 1 << logN, N1 = 1 << logN1, logN2 = logN - logN1, N2 = 1 << logN2;
+    const int rb0 = blockIdx.x << logRB;
+    const int tile = N2 << logRB;
+    u64 *a = data + (size_t)row * N + (size_t)rb0 * N2;
+    const u64 *W = tw + (size_t)p * N, *Wp = twp + (size_t)p * N;
+    {
+        const ulonglong2 *src = reinterpret_cast<const ulonglong2 *>(a);
+        ulonglong2 *dst = reinterpret_cast<ulonglong2 *>(sm);
+        for (int idx = threadIdx.x; idx < (tile >> 1); idx += blockDim.x) dst[idx] = src[idx];
+    }
+    __syncthreads();
+    const int nbf = (N2 >> 1) << logRB;
+    const int halfmask = (N2 >> 1) - 1;
+    if (!INV) {
+        for (int mp = 1, lt = logN2 - 1; mp < N2; mp <<= 1, lt--) {
+            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
+                int blk = bf >> (logN2 - 1), j = bf & halfmask;
+                int i = j >> lt, jj = j & ((1 << lt) - 1);
+                int k1 = (blk << logN2) + (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
+                int widx = mp * (N1 + rb0 + blk) + i;
+                u64 w = __ldg(W + widx), wp = __ldg(Wp + widx);
+                u64 U = sm[k1];
+                u64 V = mul_shoup(sm[k2], w, wp, q);
+                sm[k1] = add_mod(U, V, q);
+                sm[k2] = sub_mod(U, V, q);
+            }
+            __syncthreads();
+        }
+    } else {
+        for (int hp = N2 >> 1, lt = 0; hp >= 1; hp >>= 1, lt++) {
+            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
+                int blk = bf >> (logN2 - 1), j = bf & halfmask;
+                int i = j >> lt, jj = j & ((1 << lt) - 1);
+                int k1 = (blk << logN2) + (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
+                int widx = hp * (N1 + rb0 + blk) + i;
+                u64 w = __ldg(W + widx), wp = __ldg(Wp + widx);
+                u64 U = sm[k1], V = sm[k2];
+                sm[k1] = add_mod(U, V, q);
+                sm[k2] = mul_shoup(sub_mod(U, V, q), w, wp, q);
+            }
+            __syncthreads();
+        }
+    }
+    {
+        const ulonglong2 *src = reinterpret_cast<const ulonglong2 *>(sm);
+        ulonglong2 *dst = reinterpret_cast<ulonglong2 *>(a);
+        for (int idx = threadIdx.x; idx < (tile >> 1); idx += blockDim.x) dst[idx] = src[idx];
+    }
+}
+
+static void ntt_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bool inv, cudaStream_t s) {
+    if (nrows <= 0) return;
+    const int logN = t.logN, logN1 = split_log1(logN), logN2 = logN - logN1;
+    const int logC = logN2 < 4 ? logN2 : 4;                    // columns per tile
+    int logRB = 12 - logN2;                                     // 4096-word row tiles
+    if (logRB < 0) logRB = 0;
+    if (logRB > logN1) logRB = logN1;
+    const size_t smc = ((size_t)1 << (logN1 + logC)) * sizeof(u64);
+    const size_t smr = ((size_t)1 << (logN2 + logRB)) * sizeof(u64);
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaFuncSetAttribute(k_ntt_cols<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        cudaFuncSetAttribute(k_ntt_cols<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        cudaFuncSetAttribute(k_ntt_rows<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        cudaFuncSetAttribute(k_ntt_rows<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        attr_done = true;
+    }
+    for (int r0 = 0; r0 < nrows; r0 += 65535) {
+        int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
+        dim3 gc(1u << (logN2 - logC), nr), gr(1u << (logN1 - logRB), nr);
+        if (!inv) {
+            k_ntt_cols<false><<<gc, 256, smc, s>>>(data, map, t.tw, t.twp, logN, logN1, logC, r0);
+            k_ntt_rows<false><<<gr, 256, smr, s>>>(data, map, t.tw, t.twp, logN, logN1, logRB, r0);
+        } else {
+            k_ntt_rows<true><<<gr, 256, smr, s>>>(data, map, t.itw, t.itwp, logN, logN1, logRB, r0);
+            k_ntt_cols<true><<<gc, 256, smc, s>>>(data, map, t.itw, t.itwp, logN, logN1, logC, r0);
+        }
+    }
+    check_launch("ntt");
+}
+
+void ntt_forward(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s) {
+    ntt_impl(data, nrows, map, t, false, s);
+}
+void ntt_inverse(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s) {
+    ntt_impl(data, nrows, map, t, true, s);
+}
+
+// =====================================================================
+// elementwise
+// =====================================================================
+struct OpAdd {
+    __device__ u64 operator()(u64 a, u64 b, const PrimeConst &pc) const { return add_mod(a, b, pc.q); }
+};
+struct OpSub {
+    __device__ u64 operator()(u64 a, u64 b, const PrimeConst &pc) const { return sub_mod(a, b, pc.q); }
+};
+struct OpMul {
+    __device__ u64 operator()(u64 a, u64 b, const PrimeConst &pc) const { return mul_mod(a, b, pc); }
+};
+
+template <class Op>
+__global__ void k_ew2(u64 *__restrict__ out, const u64 *__restrict__ a, const u64 *__restrict__ b, size_t npairs,
+                      RowMap map, int logN, Op op) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < npairs; i += (size_t)gridDim.x * blockDim.x) {
+        const int row = (int)((2 * i) >> logN);
+        const PrimeConst &pc = c_pc[map.prime(row)];
+        ulonglong2 x = reinterpret_cast<const ulonglong2 *>(a)[i];
+        ulonglong2 y = reinterpret_cast<const ulonglong2 *>(b)[i];
+        ulonglong2 r;
+        r.x = op(x.x, y.x, pc);
+        r.y = op(x.y, y.y, pc);
+        reinterpret_cast<ulonglong2 *>(out)[i] = r;
+    }
+}
+
+template <class Op>
+static void launch_ew2(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap map, int logN, cudaStream_t s, Op op) {
+    size_t npairs = ((size_t)nrows << logN) / 2;
+    if (!npairs) return;
+    unsigned g = grid1d(npairs, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_ew2<Op><<<g, 256, 0, s>>>(out, a, b, npairs, map, logN, op);
+    check_launch("elementwise");
+}
+
+void ew_add(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap map, int logN, cudaStream_t s) {
+    launch_ew2(out, a, b, nrows, map, logN, s, OpAdd());
+}
+void ew_sub(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap map, int logN, cudaStream_t s) {
+    launch_ew2(out, a, b, nrows, map, logN, s, OpSub());
+}
+
+__global__ void k_neg(u64 *out, const u64 *a, size_t n, RowMap map, int logN) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i >> logN);
+        out[i] = neg_mod(a[i], c_pc[map.prime(row)].q);
+    }
+}
+void ew_neg(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cudaStream_t s) {
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_neg<<<g, 256, 0, s>>>(out, a, n, map, logN);
+    check_launch("neg");
+}
+
+// out[pl][i] = a[pl][i] * b[i]
+__global__ void k_mul_bcast(u64 *out, const u64 *a, const u64 *b, size_t n, int nq, int logN) {
+    const size_t per = (size_t)nq << logN;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t off = i % per;
+        const int row = (int)(off >> logN);
+        out[i] = mul_mod(a[i], b[off], c_pc[row]);
+    }
+}
+void ew_mul_bcast(u64 *out, const u64 *a, const u64 *b, int npoly, int nq, int, int logN, cudaStream_t s) {
+    size_t n = ((size_t)npoly * nq) << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_mul_bcast<<<g, 256, 0, s>>>(out, a, b, n, nq, logN);
+    check_launch("mul_bcast");
+}
+
+__global__ void k_mul_const(u64 *out, const u64 *a, const u64 *c, const u64 *cp, size_t n, RowMap map, int logN) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int p = map.prime((int)(i >> logN));
+        out[i] = mul_shoup(a[i], c[p], cp[p], c_pc[p].q);
+    }
+}
+void ew_mul_const(u64 *out, const u64 *a, const u64 *c, const u64 *cp, int nrows, RowMap map, int logN,
+                  cudaStream_t s) {
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_mul_const<<<g, 256, 0, s>>>(out, a, c, cp, n, map, logN);
+    check_launch("mul_const");
+}
+
+__global__ void k_add_const(u64 *out, const u64 *a, const u64 *c, size_t n, RowMap map, int logN) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int p = map.prime((int)(i >> logN));
+        out[i] = add_mod(a[i], c[p], c_pc[p].q);
+    }
+}
+void ew_add_const(u64 *out, const u64 *a, const u64 *c, int nrows, RowMap map, int logN, cudaStream_t s) {
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_add_const<<<g, 256, 0, s>>>(out, a, c, n, map, logN);
+    check_launch("add_const");
+}
+
+__global__ void k_tensor(u64 *out, const u64 *a, const u64 *b, int nq, int logN) {
+    const size_t n = (size_t)nq << logN;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const PrimeConst &pc = c_pc[i >> logN];
+        u64 a0 = a[i], a1 = a[n + i], b0 = b[i], b1 = b[n + i];
+        out[i] = mul_mod(a0, b0, pc);
+        u128 acc = {0, 0};
+        mac128(acc, a0, b1);
+        mac128(acc, a1, b0);
+        out[n + i] = reduce128(acc, pc);
+        out[2 * n + i] = mul_mod(a1, b1, pc);
+    }
+}
+void ew_tensor(u64 *out, const u64 *a, const u64 *b, int nq, int logN, cudaStream_t s) {
+    size_t n = (size_t)nq << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_tensor<<<g, 256, 0, s>>>(out, a, b, nq, logN);
+    check_launch("tensor");
+}
+
+__global__ void k_decrypt(u64 *out, const u64 *ct, const u64 *sk, int nq, int logN) {
+    const size_t n = (size_t)nq << logN;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const PrimeConst &pc = c_pc[i >> logN];
+        out[i] = add_mod(ct[i], mul_mod(ct[n + i], sk[i], pc), pc.q);
+    }
+}
+void ew_decrypt(u64 *out, const u64 *ct, const u64 *sk, int nq, int logN, cudaStream_t s) {
+    size_t n = (size_t)nq << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_decrypt<<<g, 256, 0, s>>>(out, ct, sk, nq, logN);
+    check_launch("decrypt");
+}
+
+__global__ void k_automorphism(u64 *__restrict__ out, const u64 *__restrict__ in, size_t n, u64 g, int logN) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t rowbase = (i >> logN) << logN;
+        const unsigned t = (unsigned)(i - rowbase);
+        out[i] = in[rowbase + aut_index(t, g, logN)];
+    }
+}
+void ew_automorphism(u64 *out, const u64 *in, int nrows, u64 galois, int logN, cudaStream_t s) {
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_automorphism<<<g, 256, 0, s>>>(out, in, n, galois, logN);
+    check_launch("automorphism");
+}
+
+__global__ void k_mac(u64 *out, MacArgs args, int npoly, int nq, int logN) {
+    const size_t per = (size_t)nq << logN;
+    const size_t n = per * npoly;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t off = i % per;
+        const PrimeConst &pc = c_pc[off >> logN];
+        u128 acc = {0, 0};
+        u64 partial = 0;
+        for (int t = 0; t < args.n; t++) {
+            mac128(acc, args.ct[t][i], args.pt[t][off]);
+            if ((t & 15) == 15) {
+                partial = add_mod(partial, reduce128(acc, pc), pc.q);
+                acc.lo = acc.hi = 0;
+            }
+        }
+        out[i] = add_mod(partial, reduce128(acc, pc), pc.q);
+    }
+}
+void ew_mac(u64 *out, const MacArgs &args, int npoly, int nq, int logN, cudaStream_t s) {
+    size_t n = ((size_t)npoly * nq) << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_mac<<<g, 256, 0, s>>>(out, args, npoly, nq, logN);
+    check_launch("mac");
+}
+
+// =====================================================================
+// counter-based sampler (SplitMix64 finaliser, Steele-Lea-Flood 2014)
+// rand64(seed, domain, idx) = mix(mix(seed ^ mix(domain)) ^ idx); uniform
+// residues by Lemire's multiply-shift with rejection (retry counters in
+// the top byte of idx); errors centred binomial, eta = 21.
+// =====================================================================
+__device__ __forceinline__ u64 mix64(u64 z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void k_uniform(u64 *out, size_t n, RowMap map, u64 kseed, u64 idx_base, int logN) {
+    const int N = 1 << logN;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i >> logN);
+        const int p = map.prime(row);
+        const u64 q = c_pc[p].q;
+        const u64 thr = (0ull - q) % q;
+        const u64 idx = idx_base + (u64)p * N + (i & (N - 1));
+        u64 v = 0;
+        for (u64 att = 0; att < 64; att++) {
+            u64 r = mix64(kseed ^ (idx + (att << 56)));
+            u64 lo = r * q, hi = __umul64hi(r, q);
+            if (lo >= thr) { v = hi; break; }
+        }
+        out[i] = v;
+    }
+}
+void sample_uniform(u64 *out, int nrows, const int *, RowMap map, u64 seed, u64 domain, u64 idx_base, u64,
+                    int logN, cudaStream_t s) {
+    // host-side part of rand64: mix(seed ^ mix(domain))
+    auto hmix = [](u64 z) {
+        z += 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    u64 kseed = hmix(seed ^ hmix(domain));
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_uniform<<<g, 256, 0, s>>>(out, n, map, kseed, idx_base, logN);
+    check_launch("uniform");
+}
+
+__global__ void k_cbd(u64 *out, size_t n, RowMap map, u64 kseed, u64 idx_base, int logN) {
+    const int N = 1 << logN;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i >> logN);
+        const u64 q = c_pc[map.prime(row)].q;
+        u64 r = mix64(kseed ^ (idx_base + (i & (N - 1))));
+        int e = __popcll(r & 0x1FFFFFull) - __popcll((r >> 21) & 0x1FFFFFull);
+        out[i] = e >= 0 ? (u64)e : q - (u64)(-e);
+    }
+}
+void sample_cbd(u64 *out, int nrows, RowMap map, u64 seed, u64 domain, u64 idx_base, int logN, cudaStream_t s) {
+    auto hmix = [](u64 z) {
+        z += 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    u64 kseed = hmix(seed ^ hmix(domain));
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_cbd<<<g, 256, 0, s>>>(out, n, map, kseed, idx_base, logN);
+    check_launch("cbd");
+}
+
+__global__ void k_swk_combine(u64 *b, const u64 *a, const u64 *e, const u64 *sk, const u64 *target, const u64 *pmod,
+                              size_t n, int lo, int hi, int logN) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i >> logN);
+        const PrimeConst &pc = c_pc[p];
+        u64 v = sub_mod(e[i], mul_mod(a[i], sk[i], pc), pc.q);
+        if (p >= lo && p < hi) v = add_mod(v, mul_mod(pmod[p], target[i], pc), pc.q);
+        b[i] = v;
+    }
+}
+void swk_combine(u64 *b, const u64 *a, const u64 *e, const u64 *sk, const u64 *target, const u64 *pmod, int nrows,
+                 int digit_lo, int digit_hi, int logN, cudaStream_t s) {
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_swk_combine<<<g, 256, 0, s>>>(b, a, e, sk, target, pmod, n, digit_lo, digit_hi, logN);
+    check_launch("swk_combine");
+}
+
+__global__ void k_enc_combine(u64 *c0, const u64 *a, const u64 *e, const u64 *sk, const u64 *m, size_t n, int logN) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const PrimeConst &pc = c_pc[i >> logN];
+        u64 v = sub_mod(e[i], mul_mod(a[i], sk[i], pc), pc.q);
+        if (m) v = add_mod(v, m[i], pc.q);
+        c0[i] = v;
+    }
+}
+void enc_combine(u64 *c0, const u64 *a, const u64 *e, const u64 *sk, const u64 *m, int nq, int logN, cudaStream_t s) {
+    size_t n = (size_t)nq << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    k_enc_combine<<<g, 256, 0, s>>>(c0, a, e, sk, m, n, logN);
+    check_launch("enc_combine");
+}
+
+// =====================================================================
+// basis conversion
+// =====================================================================
+#define HB_MAX_ALPHA 16
+
+// grid: x over N, y over digits j, z over batch.
+__global__ void k_modup_bconv(u64 *__restrict__ D, const u64 *__restrict__ X, const u64 *__restrict__ c1ntt,
+                              int nq, int K, int L, int alpha, int beta, ModUpTab tab, int logN, size_t in_stride,
+                              size_t out_stride, size_t c1_stride) {
+    const int N = 1 << logN;
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const int j = blockIdx.y, b = blockIdx.z;
+    const int ne = nq + K;
+    const int lo = j * alpha, hi = lo + alpha < nq ? lo + alpha : nq, na = hi - lo;
+    const u64 *Xb = X + b * in_stride;
+    u64 *Db = D + b * out_stride + (size_t)j * ne * N;
+    u64 y[HB_MAX_ALPHA];
+    int nneg = 0;
+#pragma unroll
+    for (int m = 0; m < HB_MAX_ALPHA; m++) {
+        if (m < na) {
+            const int pm = lo + m;
+            const u64 qm = c_pc[pm].q;
+            y[m] = mul_shoup(Xb[(size_t)pm * N + n], tab.qhinv[j * alpha + m], tab.qhinvp[j * alpha + m], qm);
+            nneg += y[m] > (qm >> 1);
+        }
+    }
+    const u64 *qhat = tab.qhat + (size_t)j * alpha * ne;
+    for (int e = 0; e < ne; e++) {
+        if (e >= lo && e < hi) {
+            Db[(size_t)e * N + n] = c1ntt[b * c1_stride + (size_t)e * N + n];
+            continue;
+        }
+        const int p = e < nq ? e : L + (e - nq);
+        const PrimeConst &pc = c_pc[p];
+        u128 acc = {0, 0};
+#pragma unroll
+        for (int m = 0; m < HB_MAX_ALPHA; m++)
+            if (m < na) mac128(acc, y[m], qhat[(size_t)m * ne + e]);
+        if (nneg) mac128(acc, (u64)nneg, tab.qjneg[(size_t)j * ne + e]);
+        Db[(size_t)e * N + n] = reduce128(acc, pc);
+    }
+}
+
+void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
+                  const ModUpTab &tab, int logN, int nbatch, size_t in_stride, size_t out_stride, size_t c1_stride,
+                  cudaStream_t s) {
+    if (alpha > HB_MAX_ALPHA) throw std::invalid_argument("alpha exceeds HB_MAX_ALPHA");
+    const int N = 1 << logN;
+    dim3 grid((N + 255) / 256, beta, nbatch);
+    k_modup_bconv<<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, beta, tab, logN, in_stride, out_stride,
+                                       c1_stride);
+    check_launch("modup_bconv");
+}
+
+__global__ void k_moddown_bconv(u64 *__restrict__ Z, const u64 *__restrict__ Y, int nq, int K, int L, ModDownTab tab,
+                                int logN, size_t in_stride, size_t out_stride) {
+    const int N = 1 << logN;
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const int b = blockIdx.y;
+    const u64 *Yb = Y + b * in_stride;
+    u64 *Zb = Z + b * out_stride;
+    u64 y[8];
+    int nneg = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+        if (k < K) {
+            const u64 pk = c_pc[L + k].q;
+            y[k] = mul_shoup(Yb[(size_t)k * N + n], tab.phinv[k], tab.phinvp[k], pk);
+            nneg += y[k] > (pk >> 1);
+        }
+    for (int i = 0; i < nq; i++) {
+        u128 acc = {0, 0};
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if (k < K) mac128(acc, y[k], tab.phat[(size_t)k * nq + i]);
+        if (nneg) mac128(acc, (u64)nneg, tab.pneg[i]);
+        Zb[(size_t)i * N + n] = reduce128(acc, c_pc[i]);
+    }
+}
+void moddown_bconv(u64 *Z, const u64 *Y, int nq, int K, int L, const ModDownTab &tab, int logN, int nbatch,
+                   size_t in_stride, size_t out_stride, cudaStream_t s) {
+    if (K > 8) throw std::invalid_argument("at most 8 special primes");
+    const int N = 1 << logN;
+    dim3 grid((N + 255) / 256, nbatch);
+    k_moddown_bconv<<<grid, 256, 0, s>>>(Z, Y, nq, K, L, tab, logN, in_stride, out_stride);
+    check_launch("moddown_bconv");
+}
+
+__global__ void k_moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, ModDownTab tab, const u64 *addend,
+                                  u64 g, int logN, size_t x_stride, size_t z_stride, size_t out_stride,
+                                  size_t add_stride) {
+    const int N = 1 << logN;
+    const size_t n = (size_t)nq << logN;
+    const int b = blockIdx.y;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i >> logN);
+        const u64 q = c_pc[row].q;
+        u64 v = mul_shoup(sub_mod(x[b * x_stride + i], Z[b * z_stride + i], q), tab.pinv[row], tab.pinvp[row], q);
+        if (addend) {
+            const unsigned t = (unsigned)(i & (N - 1));
+            const unsigned src = g == 1 ? t : aut_index(t, g, logN);
+            v = add_mod(v, addend[b * add_stride + ((size_t)row << logN) + src], q);
+        }
+        out[b * out_stride + i] = v;
+    }
+}
+void moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, const ModDownTab &tab, const u64 *addend,
+                     u64 add_galois, int logN, int nbatch, size_t x_stride, size_t z_stride, size_t out_stride,
+                     size_t add_stride, cudaStream_t s) {
+    size_t n = (size_t)nq << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 4096) g = 4096;
+    dim3 grid(g, nbatch);
+    k_moddown_combine<<<grid, 256, 0, s>>>(out, x, Z, nq, tab, addend, add_galois, logN, x_stride, z_stride,
+                                           out_stride, add_stride);
+    check_launch("moddown_combine");
+}
+
+// =====================================================================
+// rescale
+// =====================================================================
+__global__ void k_rescale_prep(u64 *W, const u64 *R, int npoly, int nq_out, u64 ql, int logN, size_t r_stride,
+                               size_t w_stride) {
+    const size_t n = ((size_t)npoly * nq_out) << logN;
+    const int N = 1 << logN;
+    const int b = blockIdx.y;
+    const u64 h = ql >> 1;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int rowall = (int)(i >> logN);
+        const int pl = rowall / nq_out, row = rowall % nq_out;
+        const PrimeConst &pc = c_pc[row];
+        u64 r = R[b * r_stride + (size_t)pl * N + (i & (N - 1))];
+        r = add_mod(r, h, ql);
+        u64 rq = mul_shoup(r, 1ull, pc.onep, pc.q);
+        u64 hq = mul_shoup(h, 1ull, pc.onep, pc.q);
+        W[b * w_stride + i] = sub_mod(hq, rq, pc.q);
+    }
+}
+void rescale_prep(u64 *W, const u64 *R, int npoly, int nq_out, u64 ql, int logN, int nbatch, size_t r_stride,
+                  size_t w_stride, cudaStream_t s) {
+    size_t n = ((size_t)npoly * nq_out) << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 4096) g = 4096;
+    k_rescale_prep<<<dim3(g, nbatch), 256, 0, s>>>(W, R, npoly, nq_out, ql, logN, r_stride, w_stride);
+    check_launch("rescale_prep");
+}
+
+__global__ void k_rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in, const u64 *qlinv,
+                                  const u64 *qlinvp, int logN, size_t c_stride, size_t w_stride, size_t out_stride) {
+    const int nq_out = nq_in - 1;
+    const size_t n = ((size_t)npoly * nq_out) << logN;
+    const int N = 1 << logN;
+    const int b = blockIdx.y;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int rowall = (int)(i >> logN);
+        const int pl = rowall / nq_out, row = rowall % nq_out;
+        const u64 q = c_pc[row].q;
+        const u64 cv = c[b * c_stride + ((size_t)pl * nq_in + row) * N + (i & (N - 1))];
+        out[b * out_stride + i] = mul_shoup(add_mod(cv, W[b * w_stride + i], q), qlinv[row], qlinvp[row], q);
+    }
+}
+void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in, const u64 *qlinv, const u64 *qlinvp,
+                     int logN, int nbatch, size_t c_stride, size_t w_stride, size_t out_stride, cudaStream_t s) {
+    size_t n = ((size_t)npoly * (nq_in - 1)) << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 4096) g = 4096;
+    k_rescale_combine<<<dim3(g, nbatch), 256, 0, s>>>(out, c, W, npoly, nq_in, qlinv, qlinvp, logN, c_stride,
+                                                      w_stride, out_stride);
+    check_launch("rescale_combine");
+}
+
+// =====================================================================
+// key switching: key multiplication with the automorphism folded into the
+// digit gather.
+// =====================================================================
+__global__ void __launch_bounds__(256) k_keymult(u64 *__restrict__ acc, const u64 *__restrict__ D,
+                                                 const u64 *__restrict__ key, u64 g, int nq, int K, int L, int beta,
+                                                 int keyP, const u64 *__restrict__ addb, int accumulate, int logN,
+                                                 size_t d_stride, size_t acc_stride, size_t add_stride) {
+    const int N = 1 << logN;
+    const int ne = nq + K;
+    const size_t n_all = (size_t)ne << logN;
+    const int b = blockIdx.y;
+    const u64 *Db = D + b * d_stride;
+    u64 *Ab = acc + b * acc_stride;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_all; i += (size_t)gridDim.x * blockDim.x) {
+        const int e = (int)(i >> logN);
+        const unsigned t = (unsigned)(i & (N - 1));
+        const unsigned src = g == 1 ? t : aut_index(t, g, logN);
+        const int p = e < nq ? e : L + (e - nq);
+        const PrimeConst &pc = c_pc[p];
+        u128 sb = {0, 0}, sa = {0, 0};
+        for (int j = 0; j < beta; j++) {
+            const u64 d = Db[((size_t)j * ne + e) * N + src];
+            const u64 *kb = key + (((size_t)j * 2 + 0) * keyP + p) * N;
+            const u64 *ka = key + (((size_t)j * 2 + 1) * keyP + p) * N;
+            mac128(sb, d, kb[t]);
+            mac128(sa, d, ka[t]);
+        }
+        u64 vb = reduce128(sb, pc), va = reduce128(sa, pc);
+        if (addb) vb = add_mod(vb, addb[b * add_stride + ((size_t)e << logN) + src], pc.q);
+        if (accumulate) {
+            vb = add_mod(vb, Ab[i], pc.q);
+            va = add_mod(va, Ab[n_all + i], pc.q);
+        }
+        Ab[i] = vb;
+        Ab[n_all + i] = va;
+    }
+}
+void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,
+             const u64 *addb, bool accumulate, int logN, int nbatch, size_t d_stride, size_t acc_stride,
+             size_t add_stride, cudaStream_t s) {
+    size_t n = (size_t)(nq + K) << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 4096) g = 4096;
+    k_keymult<<<dim3(g, nbatch), 256, 0, s>>>(acc, D, key, galois, nq, K, L, beta, keyP, addb, accumulate ? 1 : 0,
+                                              logN, d_stride, acc_stride, add_stride);
+    check_launch("keymult");
+}
+
+// =====================================================================
+// fused baby steps + diagonal MAC (double hoisting)
+// =====================================================================
+__global__ void __launch_bounds__(256) k_bsgs_baby_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct,
+                                                       const u64 *__restrict__ D, BsgsChunk ch, int nq, int K, int L,
+                                                       int beta, int keyP, int pt_nq, const u64 *__restrict__ pmod_q,
+                                                       int logN, size_t ct_stride, size_t d_stride,
+                                                       size_t inner_stride) {
+    extern __shared__ BabyDesc sdesc[];
+    for (int i = threadIdx.x; i < ch.nbabies * (int)(sizeof(BabyDesc) / 8); i += blockDim.x)
+        reinterpret_cast<u64 *>(sdesc)[i] = reinterpret_cast<const u64 *>(ch.babies)[i];
+    __syncthreads();
+    const int N = 1 << logN;
+    const int ne = nq + K;
+    const size_t n_all = (size_t)ne << logN;
+    const int b = blockIdx.y;
+    const u64 *c0 = ct + b * ct_stride;
+    const u64 *c1 = c0 + ((size_t)nq << logN);
+    const u64 *Db = D + b * d_stride;
+    u64 *Ib = inner + b * inner_stride;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_all; i += (size_t)gridDim.x * blockDim.x) {
+        const int e = (int)(i >> logN);
+        const unsigned t = (unsigned)(i & (N - 1));
+        const int p = e < nq ? e : L + (e - nq);
+        const PrimeConst &pc = c_pc[p];
+        const size_t pt_off = ((size_t)(e < nq ? e : pt_nq + (e - nq)) << logN) + t;
+        u64 acc[HB_GCH][2];
+#pragma unroll
+        for (int gi = 0; gi < HB_GCH; gi++) acc[gi][0] = acc[gi][1] = 0;
+        for (int bi = 0; bi < ch.nbabies; bi++) {
+            const BabyDesc &bd = sdesc[bi];
+            u64 rb, ra;
+            if (bd.key == nullptr) {
+                rb = e < nq ? mul_mod(pmod_q[e], c0[((size_t)e << logN) + t], pc) : 0;
+                ra = e < nq ? mul_mod(pmod_q[e], c1[((size_t)e << logN) + t], pc) : 0;
+            } else {
+                const unsigned src = aut_index(t, bd.galois, logN);
+                u128 sb = {0, 0}, sa = {0, 0};
+                for (int j = 0; j < beta; j++) {
+                    const u64 d = Db[((size_t)j * ne + e) * N + src];
+                    mac128(sb, d, bd.key[(((size_t)j * 2 + 0) * keyP + p) * N + t]);
+                    mac128(sa, d, bd.key[(((size_t)j * 2 + 1) * keyP + p) * N + t]);
+                }
+                if (e < nq) mac128(sb, pmod_q[e], c0[((size_t)e << logN) + src]);
+                rb = reduce128(sb, pc);
+                ra = reduce128(sa, pc);
+            }
+#pragma unroll
+            for (int gi = 0; gi < HB_GCH; gi++) {
+                if (gi < ch.gcount && bd.pt[gi] != nullptr) {
+                    const u64 pv = bd.pt[gi][pt_off];
+                    acc[gi][0] = add_mod(acc[gi][0], mul_mod(pv, rb, pc), pc.q);
+                    acc[gi][1] = add_mod(acc[gi][1], mul_mod(pv, ra, pc), pc.q);
+                }
+            }
+        }
+#pragma unroll
+        for (int gi = 0; gi < HB_GCH; gi++) {
+            if (gi < ch.gcount) {
+                u64 *o = Ib + (size_t)(ch.gbase + gi) * 2 * n_all;
+                o[i] = acc[gi][0];
+                o[n_all + i] = acc[gi][1];
+            }
+        }
+    }
+}
+
+void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, int nq, int K, int L, int beta,
+                   int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride, size_t d_stride,
+                   size_t inner_stride, cudaStream_t s) {
+    size_t n = (size_t)(nq + K) << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 2048) g = 2048;
+    size_t smem = sizeof(BabyDesc) * (size_t)ch.nbabies;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_bsgs_baby_mac, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        attr = true;
+    }
+    k_bsgs_baby_mac<<<dim3(g, nbatch), 256, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN,
+                                                       ct_stride, d_stride, inner_stride);
+    check_launch("bsgs_baby_mac");
+}
+
+void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, nwords * sizeof(u64), cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("copy: ") + cudaGetErrorString(e));
+}
+
+}  // namespace hb

@@ -1,0 +1,176 @@
+// hb_kernels.cuh -- device kernels of the B200 CKKS backend and their
+// host-side launchers.  Data layout (HBM): a polynomial is a stack of
+// limbs, each limb N contiguous uint64 residues in the bit-reversed NTT
+// order.  A ciphertext at level l is [2][l+1][N]; an extended-basis (PQ)
+// polynomial is [l+1+K][N] with the q rows first and the K special-prime
+// rows after them.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "hb_arith.cuh"
+
+namespace hb {
+
+// Maps row r of a batched launch to its prime index.  Rows come in blocks
+// of `per` rows; row e of a block is main prime e when e < nq and special
+// prime L + (e - nq) otherwise.  With alpha > 0, rows of block b that
+// belong to digit b ([b*alpha, min(b*alpha+alpha, nq))) are skipped (the
+// ModUp output keeps the input limbs of its own digit).
+struct RowMap {
+    int per;
+    int nq;
+    int L;
+    int alpha = 0;   // > 0: skip the rows of the block's own digit
+    int ndig = 1;    // digit of block b is (b % ndig)
+    int pbase = 0;   // main-prime rows start at prime pbase
+    __host__ __device__ int prime(int r) const {
+        int e = r % per;
+        return e < nq ? pbase + e : L + (e - nq);
+    }
+    __host__ __device__ bool skip(int r) const {
+        if (alpha <= 0) return false;
+        int b = (r / per) % ndig, e = r % per;
+        int lo = b * alpha, hi = lo + alpha < nq ? lo + alpha : nq;
+        return e >= lo && e < hi;
+    }
+};
+inline RowMap rowmap(int per, int nq, int L) {
+    RowMap m;
+    m.per = per;
+    m.nq = nq;
+    m.L = L;
+    return m;
+}
+
+struct NttTables {
+    const u64 *tw, *twp;    // [P][N] psi^brv(i) and Shoup companions
+    const u64 *itw, *itwp;  // [P][N] psi^-brv(i)
+    int logN;
+};
+
+void upload_prime_consts(const PrimeConst *pc, int n);
+
+// ---- NTT -----------------------------------------------------------------
+void ntt_forward(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s);
+void ntt_inverse(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s);
+
+// ---- elementwise ---------------------------------------------------------
+// out = a op b on nrows rows (rows map to primes with `map`)
+void ew_add(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap map, int logN, cudaStream_t s);
+void ew_sub(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap map, int logN, cudaStream_t s);
+void ew_neg(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cudaStream_t s);
+// out[pl][i] = a[pl][i] * b[i]   (b broadcast over npoly blocks of nq rows)
+void ew_mul_bcast(u64 *out, const u64 *a, const u64 *b, int npoly, int nq, int b_rows_stride_nq,
+                  int logN, cudaStream_t s);
+// out[r] = a[r] * c[prime(r)] (+ add[prime(r)] if add != null), constants per prime with Shoup
+void ew_mul_const(u64 *out, const u64 *a, const u64 *c, const u64 *cp, int nrows, RowMap map, int logN,
+                  cudaStream_t s);
+void ew_add_const(u64 *out, const u64 *a, const u64 *c, int nrows, RowMap map, int logN, cudaStream_t s);
+// ct x ct tensor: out[0]=a0b0, out[1]=a0b1+a1b0, out[2]=a1b1 (nq rows each)
+void ew_tensor(u64 *out, const u64 *a, const u64 *b, int nq, int logN, cudaStream_t s);
+// out = c0 + c1 * sk (nq rows)
+void ew_decrypt(u64 *out, const u64 *ct, const u64 *sk, int nq, int logN, cudaStream_t s);
+// automorphism: out[r][t] = in[r][tau_g(t)]
+void ew_automorphism(u64 *out, const u64 *in, int nrows, u64 galois, int logN, cudaStream_t s);
+
+#define HB_MAC_MAX 64
+struct MacArgs {
+    const u64 *ct[HB_MAC_MAX];
+    const u64 *pt[HB_MAC_MAX];
+    int n;
+};
+// out[pl][i] = sum_t ct_t[pl][i] * pt_t[i]
+void ew_mac(u64 *out, const MacArgs &args, int npoly, int nq, int logN, cudaStream_t s);
+
+// ---- sampling (counter-based; see hb_kernels.cu) ---------------------------
+void sample_uniform(u64 *out, int nrows, const int *row_prime_host_unused, RowMap map, u64 seed, u64 domain,
+                    u64 idx_base, u64 idx_row_stride, int logN, cudaStream_t s);
+// centred-binomial error, the same integer written modulo every row's prime
+void sample_cbd(u64 *out, int nrows, RowMap map, u64 seed, u64 domain, u64 idx_base, int logN,
+                cudaStream_t s);
+
+// ---- key generation / encryption combines ------------------------------------
+// b = e - a*s (+ pmod[p] * target if addmask row), rows in [0, P)
+void swk_combine(u64 *b, const u64 *a, const u64 *e, const u64 *sk, const u64 *target, const u64 *pmod,
+                 int nrows, int digit_lo, int digit_hi, int logN, cudaStream_t s);
+// c0 = e - a*s + m over nq rows (m may be null)
+void enc_combine(u64 *c0, const u64 *a, const u64 *e, const u64 *sk, const u64 *m, int nq, int logN,
+                 cudaStream_t s);
+
+// ---- basis conversion --------------------------------------------------------
+// ModUp basis conversion for digits [0, beta): X holds the coefficient form
+// of the nq input limbs, c1ntt their NTT form.  For every digit j and
+// extended row e outside the digit: D[j][e] = sum_m (X_m * qhinv_m mod q_m)
+// * qhat_m mod t_e (coefficient form, NTT'd afterwards); rows of the digit
+// itself are copied from c1ntt.  The lift is centred: a term y_m above
+// q_m/2 stands for y_m - q_m, which adds -Q_j (keeps the digit zero-mean).
+// tab: per-level tables in device memory.
+struct ModUpTab {
+    const u64 *qhinv;   // [beta][alpha]            (and Shoup companions in qhinvp)
+    const u64 *qhinvp;
+    const u64 *qhat;    // [beta][alpha][ne]        qhat_m mod t_e
+    const u64 *qjneg;   // [beta][ne]               t_e - (Q_j mod t_e)
+};
+void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
+                 const ModUpTab &tab, int logN, int nbatch, size_t in_stride, size_t out_stride, size_t c1_stride,
+                 cudaStream_t s);
+
+struct ModDownTab {
+    const u64 *phinv;   // [K] (P/p_k)^-1 mod p_k, with Shoup
+    const u64 *phinvp;
+    const u64 *phat;    // [K][nq]  (P/p_k) mod q_i
+    const u64 *pinv;    // [nq] P^-1 mod q_i, with Shoup
+    const u64 *pinvp;
+    const u64 *pneg;    // [nq] q_i - (P mod q_i)
+};
+// Z[i] = sum_k (Y_k * phinv_k mod p_k) * phat_k mod q_i  (coefficient form),
+// with the same centred lift as ModUp.
+void moddown_bconv(u64 *Z, const u64 *Y, int nq, int K, int L, const ModDownTab &tab, int logN, int nbatch,
+                   size_t in_stride, size_t out_stride, cudaStream_t s);
+// out[i] = (x[i] - Z[i]) * pinv_i (+ addend[i][tau_g(n)] if addend)
+void moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, const ModDownTab &tab, const u64 *addend,
+                     u64 add_galois, int logN, int nbatch, size_t x_stride, size_t z_stride,
+                     size_t out_stride, size_t add_stride, cudaStream_t s);
+
+// ---- rescale ---------------------------------------------------------------
+// prep: W[pl][i] = (h mod q_i) - ((R[pl] + h) mod q_l mod q_i), R = INTT of last limb (coef)
+void rescale_prep(u64 *W, const u64 *R, int npoly, int nq_out, u64 ql, int logN, int nbatch,
+                  size_t r_stride, size_t w_stride, cudaStream_t s);
+// out[pl][i] = (c[pl][i] + W[pl][i]) * qlinv_i
+void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in, const u64 *qlinv,
+                     const u64 *qlinvp, int logN, int nbatch, size_t c_stride, size_t w_stride,
+                     size_t out_stride, cudaStream_t s);
+
+// ---- key switching -------------------------------------------------------------
+// acc[pl][e][n] (+)= sum_{j<beta} D[j][e][tau(n)] * key[j][pl][prime(e)][n]
+//                 (+ addb[e][tau(n)] on pl = 0 when addb != null)
+// key layout [dnum][2][P][N].  nbatch ciphertexts: D, acc, addb advance by
+// their strides, key shared.
+void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,
+             const u64 *addb, bool accumulate, int logN, int nbatch, size_t d_stride, size_t acc_stride,
+             size_t add_stride, cudaStream_t s);
+
+// ---- fused double-hoisted baby steps + plaintext MAC --------------------------
+#define HB_GCH 16
+struct BabyDesc {
+    u64 galois;        // 1 for the identity baby (b = 0)
+    const u64 *key;    // null for b = 0
+    const u64 *pt[HB_GCH];  // plaintext (ext basis) of (giant slot, this baby) or null
+};
+struct BsgsChunk {
+    const BabyDesc *babies;  // device array
+    int nbabies;
+    int gbase;               // first output giant slot of this chunk
+    int gcount;              // giant slots in this chunk (<= HB_GCH)
+};
+// inner[g][pl][e][n] for g in [gbase, gbase+gcount): sum over babies of
+// pt(g, b) * R_b, R_b = baby rotation of the input kept in the PQ basis:
+// R_b.b = P*c0[tau] + sum_j D_j[tau] key.b,  R_b.a = sum_j D_j[tau] key.a.
+void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, int nq, int K, int L,
+                   int beta, int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride,
+                   size_t d_stride, size_t inner_stride, cudaStream_t s);
+
+// copy rows with optional automorphism (used to place P*c parts etc.)
+void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s);
+
+}  // namespace hb

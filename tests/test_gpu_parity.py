@@ -1,0 +1,256 @@
+"""Bit-exact parity of the sm_100a path with the CPU oracle, through the C ABI.
+
+Every residue the GPU produces -- secret key, switching keys,
+encryptions, NTT/INTT, automorphism, MAC, rescale, hoisted key switching,
+relinearisation and the double-hoisted BSGS linear transform -- must equal
+the oracle's on the same primes, keys and ciphertexts.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from gpu_helpers import Pair
+from helrm_b200 import CKKSConfig
+from helrm_b200 import workload as W
+
+pytestmark = pytest.mark.gpu
+
+# P = 2^120 exceeds every 3-prime digit (<= 2^112), as hybrid key switching needs
+CFG = CKKSConfig(logn=12, logq=[40, 36, 36, 36, 36], logp=[60, 60], logscale=36, h=64)
+
+
+@pytest.fixture(scope="module")
+def pair(oracle_mod):
+    p = Pair(CFG, dnum=2, seed=20261201, oracle_mod=oracle_mod)
+    yield p
+    p.close()
+
+
+def test_secret_key_bit_exact(pair):
+    assert np.array_equal(pair.lib.GetSecretKeyData(), pair.sk)
+
+
+def test_encryption_bit_exact(pair):
+    vals = np.linspace(-1, 1, pair.slots)
+    pt = pair.lib.Encode(list(vals), 4, pair.scale)
+    pt_res = pair.lib.GetPlaintextData(pt)
+    seed = pair.next_ct_seed()
+    ct = pair.lib.Encrypt(pt)
+    pair.enc_count += 1
+    want = pair.o.encrypt(pair.sk, pt_res, seed)
+    assert np.array_equal(pair.ct_data(ct), want)
+    # decrypt on the GPU == oracle decrypt
+    dp = pair.lib.Decrypt(ct)
+    assert np.array_equal(pair.lib.GetPlaintextData(dp), pair.o.decrypt(pair.sk, want))
+
+
+def test_encode_matches_oracle(pair):
+    rng = np.random.default_rng(1)
+    vals = rng.uniform(-1, 1, pair.slots)
+    pt = pair.lib.Encode(list(vals), 4, pair.scale)
+    got = pair.lib.GetPlaintextData(pt)
+    want = pair.o.encode(vals, 5, pair.scale)
+    # same canonical-embedding spec; two FFT implementations may round a
+    # coefficient sitting at .5 differently: allow |delta| <= 1 per coefficient
+    for i in range(5):
+        q = pair.o.primes[i]
+        d = (pair.o.intt(i, got[i]).astype(object) - pair.o.intt(i, want[i]).astype(object)) % q
+        d = np.where(d > q // 2, d - q, d)
+        assert np.abs(d.astype(np.int64)).max() <= 1
+    assert np.abs(np.array(pair.lib.Decode(pt)) - vals).max() < 1e-8
+
+
+@pytest.mark.parametrize("k", [1, 5, -3, 1000, 2047])
+def test_rotation_keys_and_rotation_bit_exact(pair, k):
+    ct = pair.encrypt(np.cos(np.arange(pair.slots)))
+    out = pair.lib.RotateNew(ct, k)
+    g = pair.o.galois(k)
+    key = pair.key(g)
+    assert np.array_equal(key, pair.o.rotation_key(pair.sk, pair.seed, g))
+    assert np.array_equal(pair.ct_data(out), pair.o.rotate(pair.ct_data(ct), key, g))
+    vals = pair.decrypt(out)
+    assert np.abs(vals - np.roll(np.cos(np.arange(pair.slots)), -k)).max() < 1e-5
+
+
+def test_conjugation_bit_exact(pair):
+    ct = pair.encrypt(np.sin(np.arange(pair.slots)))
+    out = pair.lib.ConjugateNew(ct)
+    g = 2 * pair.N - 1
+    key = pair.key(g)
+    assert np.array_equal(key, pair.o.rotation_key(pair.sk, pair.seed, g))
+    assert np.array_equal(pair.ct_data(out), pair.o.rotate(pair.ct_data(ct), key, g))
+
+
+def test_hoisted_rotation_batch_bit_exact(pair):
+    ct = pair.encrypt(np.arange(pair.slots) / pair.slots)
+    ks = [1, 2, 3, 17, 0, 2]
+    outs = pair.lib.RotateBatchNew(ct, ks)
+    data = pair.ct_data(ct)
+    for k, o in zip(ks, outs):
+        if k == 0:
+            assert np.array_equal(pair.ct_data(o), data)
+            continue
+        g = pair.o.galois(k)
+        assert np.array_equal(pair.ct_data(o), pair.o.rotate(data, pair.key(g), g))
+
+
+def test_rescale_bit_exact(pair):
+    ct = pair.encrypt(np.linspace(0, 1, pair.slots))
+    out = pair.lib.RescaleNew(ct)
+    assert pair.lib.GetCiphertextLevel(out) == 3
+    assert np.array_equal(pair.ct_data(out), pair.o.rescale(pair.ct_data(ct)))
+
+
+def test_mac_bit_exact(pair):
+    rng = np.random.default_rng(4)
+    cts = [pair.encrypt(rng.uniform(-1, 1, pair.slots)) for _ in range(5)]
+    pts = [pair.lib.Encode(list(rng.uniform(-1, 1, pair.slots)), 4, pair.scale) for _ in range(5)]
+    out = pair.lib.MulPlaintextAccumNew(cts, pts)
+    want = pair.o.mac([pair.ct_data(c) for c in cts], [pair.lib.GetPlaintextData(p) for p in pts])
+    assert np.array_equal(pair.ct_data(out), want)
+
+
+def test_relinearized_product_bit_exact(pair):
+    a = pair.encrypt(np.linspace(-1, 1, pair.slots))
+    b = pair.encrypt(np.linspace(1, -1, pair.slots))
+    rlk = pair.key(0)
+    assert np.array_equal(rlk, pair.o.relin_key(pair.sk, pair.seed))
+    out = pair.lib.MulRelinCiphertextNew(a, b)
+    want = pair.o.relinearize(pair.o.tensor(pair.ct_data(a), pair.ct_data(b)), rlk)
+    assert np.array_equal(pair.ct_data(out), want)
+
+
+def test_add_sub_negate_bit_exact(pair):
+    a = pair.encrypt(np.linspace(-1, 1, pair.slots))
+    b = pair.encrypt(np.linspace(1, -1, pair.slots))
+    da, db = pair.ct_data(a), pair.ct_data(b)
+    q = np.array(pair.o.primes[:5], dtype=object)[None, :, None]
+    s = pair.ct_data(pair.lib.AddCiphertextNew(a, b)).astype(object)
+    d = pair.ct_data(pair.lib.SubCiphertextNew(a, b)).astype(object)
+    assert ((s - (da.astype(object) + db.astype(object))) % q == 0).all()
+    assert ((d - (da.astype(object) - db.astype(object))) % q == 0).all()
+    pair.lib.Negate(a)
+    assert ((pair.ct_data(a).astype(object) + da.astype(object)) % q == 0).all()
+
+
+LT_CASES = [
+    ("identity", [0], 1.0),
+    ("permute", [3], 1.0),
+    ("multi", [0, 1], 1.0),
+    ("bsgs5", [0, 1, 2, 5, 8], 2.0),
+    ("naive3", [0, 2, 7], "none"),
+    ("wide", [0, 1, 2, 3, 40, 41, 77, 512, 1000, 2047], 2.0),
+]
+
+
+@pytest.mark.parametrize("name,ks,ratio", LT_CASES)
+def test_linear_transform_bit_exact(pair, golden_bsgs, name, ks, ratio):
+    rng = np.random.default_rng(len(ks))
+    slots = pair.slots
+    diags = {k: rng.uniform(-0.5, 0.5, slots) for k in ks}
+    data = np.concatenate([diags[k] for k in ks])
+    lt = pair.lib.GenerateLinearTransform(ks, data, 4, ratio, "none")
+    plan = W.bsgs_plan(ks, ratio, slots)
+    assert pair.lib.GetLinearTransformRotationKeys(lt) == plan["rotation_keys"]
+    assert pair.lib.GetLinearTransformInfo(lt)["bs"] == plan["bs"]
+    for kk in pair.lib.GetLinearTransformRotationKeys(lt):
+        pair.lib.GenerateLinearTransformRotationKey(kk)
+    x = rng.uniform(-1, 1, slots)
+    ct = pair.encrypt(x)
+    out = pair.lib.EvaluateLinearTransform(lt, ct)
+    pts = [pair.lib.GetLinearTransformPlaintext(lt, k) for k in ks]
+    keys = {pair.o.galois(d): pair.key(pair.o.galois(d)) for d in plan["rotation_keys"]}
+    want = pair.o.bsgs_lt(pair.ct_data(ct), ks, pts, plan["stride"], keys)
+    assert np.array_equal(pair.ct_data(out), want), name
+    got = pair.decrypt(pair.lib.RescaleNew(out))
+    ref = W.cleartext_lt(x, diags, slots)
+    assert np.abs(got - ref).max() < 1e-4, name
+    pair.lib.DeleteLinearTransform(lt)
+
+
+def test_golden_bsgs_plans(pair, golden_bsgs):
+    """bs and key sets of the reference's own orchestration (64-slot cases
+    replayed at this scheme's width keep the same split)."""
+    for c in golden_bsgs:
+        data = np.ones(len(c["ks"]) * pair.slots)
+        lt = pair.lib.GenerateLinearTransform(c["ks"], data, 4, c["ratio"], "none")
+        assert pair.lib.GetLinearTransformInfo(lt)["bs"] == c["bs"], c["name"]
+        assert pair.lib.GetLinearTransformRotationKeys(lt) == c["rotation_keys"], c["name"]
+        pair.lib.DeleteLinearTransform(lt)
+
+
+def test_lt_batch_equals_single(pair):
+    rng = np.random.default_rng(8)
+    ks = [0, 1, 2, 5, 8, 13, 100]
+    data = rng.uniform(-0.5, 0.5, len(ks) * pair.slots)
+    lt = pair.lib.GenerateLinearTransform(ks, data, 4, 2.0, "none")
+    for kk in pair.lib.GetLinearTransformRotationKeys(lt):
+        pair.lib.GenerateLinearTransformRotationKey(kk)
+    cts = [pair.encrypt(rng.uniform(-1, 1, pair.slots)) for _ in range(3)]
+    batch = pair.lib.EvaluateLinearTransformBatch(lt, cts)
+    for c, b in zip(cts, batch):
+        assert np.array_equal(pair.ct_data(pair.lib.EvaluateLinearTransform(lt, c)), pair.ct_data(b))
+
+
+def test_input_above_transform_level_bit_exact(pair):
+    rng = np.random.default_rng(9)
+    ks = [0, 1, 2, 5, 8]
+    data = rng.uniform(-0.5, 0.5, len(ks) * pair.slots)
+    lt = pair.lib.GenerateLinearTransform(ks, data, 2, 2.0, "none")
+    for kk in pair.lib.GetLinearTransformRotationKeys(lt):
+        pair.lib.GenerateLinearTransformRotationKey(kk)
+    ct = pair.encrypt(rng.uniform(-1, 1, pair.slots))
+    out = pair.lib.EvaluateLinearTransform(lt, ct)
+    assert pair.lib.GetCiphertextLevel(out) == 2
+    aligned = pair.lib.AlignToLevelNew(ct, 2)
+    plan = W.bsgs_plan(ks, 2.0, pair.slots)
+    pts = [pair.lib.GetLinearTransformPlaintext(lt, k) for k in ks]
+    keys = {pair.o.galois(d): pair.key(pair.o.galois(d)) for d in plan["rotation_keys"]}
+    want = pair.o.bsgs_lt(pair.ct_data(aligned), ks, pts, plan["stride"], keys)
+    assert np.array_equal(pair.ct_data(out), want)
+
+
+def test_hybrid_fold_bit_exact(pair):
+    ct = pair.encrypt(np.arange(pair.slots) % 7 / 7.0)
+    before = pair.ct_data(ct)
+    pair.lib.HybridFoldBatch([ct], 3)
+    x = before
+    for i in range(1, 4):
+        k = pair.slots >> i
+        g = pair.o.galois(k)
+        r = pair.o.rotate(x, pair.key(g), g)
+        q = np.array(pair.o.primes[:5], dtype=np.uint64)[None, :, None]
+        x = ((x.astype(object) + r.astype(object)) % q.astype(object)).astype(np.uint64)
+    assert np.array_equal(pair.ct_data(ct), x)
+
+
+def test_kernel_entry_points_bit_exact(pair):
+    """helrm_kernel_* on device pointers (torch only allocates the memory)."""
+    import torch
+    from helrm_b200 import _capi
+    lib = _capi.load()
+    rng = np.random.default_rng(2)
+    nq, N = 5, pair.N
+    host = np.stack([rng.integers(0, pair.o.primes[i], N, dtype=np.uint64) for i in range(nq)] * 2)
+    dev = torch.from_numpy(host.view(np.int64).copy()).cuda()
+    _capi.check(lib.helrm_kernel_ntt(ctypes.c_void_p(dev.data_ptr()), 2 * nq, nq, nq, 0, None))
+    _capi.check(lib.helrm_Synchronize())
+    fwd = dev.cpu().numpy().view(np.uint64)
+    for r in range(2 * nq):
+        assert np.array_equal(fwd[r], pair.o.ntt(r % nq, host[r]))
+    _capi.check(lib.helrm_kernel_ntt(ctypes.c_void_p(dev.data_ptr()), 2 * nq, nq, nq, 1, None))
+    _capi.check(lib.helrm_Synchronize())
+    assert np.array_equal(dev.cpu().numpy().view(np.uint64), host)
+    out = torch.empty_like(dev)
+    g = pair.o.galois(9)
+    _capi.check(lib.helrm_kernel_automorphism(ctypes.c_void_p(dev.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                              2 * nq, g, None))
+    _capi.check(lib.helrm_Synchronize())
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), pair.o.automorphism(host, g))
+    rs = torch.empty((2 * (nq - 1), N), dtype=torch.int64, device="cuda")
+    _capi.check(lib.helrm_kernel_rescale(ctypes.c_void_p(dev.data_ptr()), ctypes.c_void_p(rs.data_ptr()), nq, 1,
+                                         None))
+    _capi.check(lib.helrm_Synchronize())
+    assert np.array_equal(rs.cpu().numpy().view(np.uint64).reshape(2, nq - 1, N),
+                          pair.o.rescale(host.reshape(2, nq, N)))
