@@ -1,0 +1,435 @@
+#!/usr/bin/env python
+"""bench.py -- the HE-LRM embedding PCMM on B200.
+
+One step = one batch of 64 encrypted Criteo-shaped queries through the
+embedding layer, the reference's hot path (examples/criteo/dlrm.py:226-229
+-> orion/nn/linear.py:99-140): the BSGS diagonal linear transform of the
+26-table block-diagonal 416 x 4224 matrix (512 diagonals, bs 32, 16 giant
+groups) on ciphertexts at LogN 16 with 24 limbs + 4 special primes
+(dnum 4), then the rescale and the 6 hybrid-fold rotations.  Inputs are
+seeded synthetic data with the reference's shapes (the Criteo dataset is
+not available), weights N(0, 0.05), queries Zipf(1.05).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Under torchrun each rank runs its own batch (query-batch data parallelism,
+keys and diagonals replicated, no data-path collective): weak scaling.
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "HE-LRM encrypted inferences/sec; embedding PCMM ms; key-switch HBM GB/s"
+UNIT = "inferences/s"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--level", type=int, default=23, help="PCMM input level (23 = all 24 limbs)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-threads", type=int, default=0, help="oracle threads (0 = all host cores)")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------- distributed plumbing
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            sel = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            sel = str(device_index)
+        self.sel = sel
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_r{device_index}.csv") \
+            if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.sel, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
+        if self.path:
+            with open(self.path, "w") as f:
+                f.write(out)
+        sm = [float(r[0]) for r in rows if len(r) >= 8 and r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if len(r) >= 8 and r[1].replace(".", "").isdigit()]
+        pw = [float(r[2]) for r in rows if len(r) >= 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 8 for i in range(4) if r[4 + i].strip() == "Active"})
+        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 0)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "samples": len(rows), "reasons": reasons}
+
+
+# --------------------------------------------------------------------------- workload
+def build_workload(batch: int, seed: int):
+    from helrm_b200 import workload as W
+    V = W.cfg2_vocab()
+    M = W.block_diag_matrix(V, 64, 16, 0.05, seed=0)
+    d, rot = W.diagonalize(M, 32768, "hybrid")
+    diags = d[(0, 0)]
+    ks = sorted(diags)
+    q = W.zipf_queries(V, batch, seed=seed)
+    xs = [W.selector(qq, V) for qq in q]
+    return M, ks, diags, rot, xs
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def ncu_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            t = json.load(f)
+        return t.get(kernel)
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------------------- CPU baseline (oracle)
+def cpu_pcmm_seconds(ks, diags, rot, x, level, threads, reps=1):
+    """The same PCMM for one ciphertext on the CPU restatement (oracle/),
+    with `threads` host threads.  Returns (seconds per ciphertext, setup s)."""
+    from oracle import oracle as om
+    from helrm_b200 import workload as W
+    from helrm_b200.params import CFG2, CFG2_DNUM
+    from concurrent.futures import ThreadPoolExecutor
+    t0 = time.time()
+    main, aux = om.scheme_primes(CFG2.logq, CFG2.logp, CFG2.logn)
+    o = om.Oracle(CFG2.logn, main, aux, CFG2_DNUM)
+    plan = W.bsgs_plan(ks, 2.0, o.N // 2)
+    nq = level + 1
+    scale = float(1 << CFG2.logscale)
+    # untimed setup: one task per diagonal / key, each single-threaded inside
+    # the oracle (ctypes releases the GIL, so the pool runs them in parallel)
+    om.set_threads(1)
+    sk = o.secret_ntt(o.sample_secret(4242, CFG2.h))
+    gal = sorted({o.galois(dd) for dd in plan["rotation_keys"]} |
+                 {o.galois((o.N // 2) >> i) for i in range(1, rot + 1)})
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        pts = list(ex.map(lambda k: o.encode(W.preroll(diags[k], k // plan["stride"], plan["stride"]), nq, scale,
+                                             ext=True), ks))
+        keys = dict(zip(gal, ex.map(lambda g: o.rotation_key(sk, 4242, g), gal)))
+    om.set_threads(threads)
+    v = np.zeros(o.N // 2)
+    v[:len(x)] = x
+    ct = o.encrypt(sk, o.encode(v, nq, scale), 7)
+    setup = time.time() - t0
+    times = []
+    for _ in range(reps):
+        t1 = time.time()
+        out = o.rescale(o.bsgs_lt(ct, ks, pts, plan["stride"], keys))
+        for i in range(1, rot + 1):
+            g = o.galois((o.N // 2) >> i)
+            r = o.rotate(out, keys[g], g)
+            qs = np.array(o.primes[:out.shape[1]], dtype=np.uint64)[None, :, None]
+            s = out + r  # residues < 2^60, no uint64 overflow
+            out = np.where(s >= qs, s - qs, s)
+        times.append(time.time() - t1)
+    return min(times), setup, times
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args, dist):
+    """The reference's CPU implementation of the path cannot be built here
+    (Lattigo is Go, absent with its module cache; Cheddar is not vendored),
+    so the arm times the oracle port on all host cores: one ciphertext of
+    the same PCMM per step."""
+    if dist.rank != 0:
+        return
+    threads = args.cpu_threads or os.cpu_count() or 1
+    M, ks, diags, rot, xs = build_workload(1, seed=100)
+    # one oracle setup (keys, diagonals; untimed), then warmup + timed steps
+    _, setup, times_all = cpu_pcmm_seconds(ks, diags, rot, xs[0], args.level, threads,
+                                           reps=args.warmup + args.steps)
+    times = times_all[args.warmup:]
+    ms = 1000.0 * sum(times) / len(times)
+    value = 1000.0 / ms
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+        "config": cfg_dict(args, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "1 ciphertext of the cfg2 PCMM per step (LT + rescale + 6 fold rotations), "
+                                   f"oracle port on {threads} threads; Lattigo (Go) is not buildable here"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_s": setup,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cfg_dict(args, batch):
+    return {"workload": "cfg2: 26-table block-diagonal embedding PCMM (BASELINE configs[1])",
+            "logN": 16, "slots": 32768, "q_limbs": 24, "q_bits": 36, "special_primes": 4, "p_bits": 60,
+            "dnum": 4, "pcmm_level": args.level, "matrix": "416x4224 block-diagonal", "diagonals": 512,
+            "bs": 32, "giant_groups": 16, "fold_rotations": 6, "batch_ciphertexts": batch,
+            "queries_per_ciphertext": 1, "parallelism": f"dp{args.gpus} (query batch)",
+            "l2": "inputs larger than L2 (1.5 GiB ciphertexts, 7 GiB diagonals, 5.7 GiB keys per step)"}
+
+
+# --------------------------------------------------------------------------- B200 arm
+def run_b200(args, dist):
+    import torch
+
+    from helrm_b200 import B200Library, _capi
+    from helrm_b200.params import CFG2, CFG2_DNUM
+
+    dev = dist.local
+    torch.cuda.set_device(dev)
+    lib = B200Library(dnum=CFG2_DNUM, seed=1000 + dist.rank, device=dev)
+    lib.setup_bindings(CFG2)
+    lib.GenerateSecretKey()
+    M, ks, diags, rot, xs = build_workload(args.batch, seed=100 + dist.rank)
+    info = lib.scheme_info()
+    slots, N = info["slots"], info["N"]
+    data = np.concatenate([diags[k].astype(np.float64) for k in ks])
+    lt = lib.GenerateLinearTransform(ks, data, args.level, 2.0, "none")
+    for k in lib.GetLinearTransformRotationKeys(lt):
+        lib.GenerateLinearTransformRotationKey(k)
+    for i in range(1, rot + 1):
+        lib.AddRotationKey(slots >> i)
+    scale = float(1 << CFG2.logscale)
+    cts = []
+    for x in xs:
+        v = np.zeros(slots)
+        v[:len(x)] = x
+        pt = lib.Encode(list(v), args.level, scale)
+        cts.append(lib.Encrypt(pt))
+        lib.DeletePlaintext(pt)
+    capi = _capi.load()
+
+    def step(ids):
+        outs = lib.EvaluateLinearTransformBatch(lt, ids)
+        lib.RescaleBatch(outs)
+        lib.HybridFoldBatch(outs, rot)
+        return outs
+
+    # correctness spot check outside the timed region: first ciphertext
+    o = step(cts[:1])[0]
+    got = np.array(lib.Decode(lib.Decrypt(o)))[:416]
+    ref = M.astype(np.float64) @ xs[0]
+    max_err = float(np.abs(got - ref).max())
+    lib.DeleteCiphertext(o)
+
+    for _ in range(args.warmup):
+        for o in step(cts):
+            lib.DeleteCiphertext(o)
+    lib.Synchronize()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region
+    clocks = ClockSampler(dev)
+    dist.barrier()
+    torch.cuda.synchronize()
+    lib.Synchronize()
+    clocks.start()
+    _capi.check(capi.helrm_ProfileEnable(1))
+    n0 = ctypes.c_uint64(0)
+    _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n0)))
+    _capi.check(capi.helrm_TimerStart())
+    for _ in range(args.steps):
+        for o in step(cts):
+            lib.DeleteCiphertext(o)
+    ms = ctypes.c_double(0)
+    _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+    n1 = ctypes.c_uint64(0)
+    _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n1)))
+    K = 16
+    pms, pby, pwk = (ctypes.c_double * K)(), (ctypes.c_double * K)(), (ctypes.c_double * K)()
+    pl = (ctypes.c_uint64 * K)()
+    ncls = ctypes.c_int(0)
+    _capi.check(capi.helrm_ProfileRead(pms, pby, pwk, pl, K, ctypes.byref(ncls)))
+    _capi.check(capi.helrm_ProfileEnable(0))
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t_dev = dist.max(ms.value / 1000.0)
+    value = dist.world * args.batch * args.steps / t_dev
+    ms_step = 1000.0 * t_dev / args.steps
+
+    names = []
+    buf = ctypes.create_string_buffer(64)
+    for i in range(ncls.value):
+        capi.helrm_KernelClassName(i, buf, 64)
+        names.append(buf.value.decode())
+    kern = {}
+    for i, nm in enumerate(names):
+        if pl[i] == 0:
+            continue
+        kern[nm] = {"ms_per_step": pms[i] / args.steps, "launches_per_step": pl[i] / args.steps,
+                    "share": None, "GBps": pby[i] / (pms[i] * 1e6) if pms[i] else None,
+                    "Gops": pwk[i] / (pms[i] * 1e6) if pms[i] else None}
+    tot = sum(v["ms_per_step"] for v in kern.values()) or 1.0
+    for v in kern.values():
+        v["share"] = v["ms_per_step"] / tot
+    dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
+    di = names.index(dom)
+    hbm, src = peaks()
+    achieved = pby[di] / (pms[di] * 1e6)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured"
+                else "fallback 6.65 TB/s", "bytes_per_launch": pby[di] / pl[di],
+                "avg_launch_ms": pms[di] / pl[di],
+                "traffic": ncu_traffic(dom)}
+    ksi = names.index("keymult")
+    keyswitch_gbps = pby[ksi] / (pms[ksi] * 1e6) if pl[ksi] else None
+
+    # ---- end to end through the C ABI with host buffers
+    e2e = None
+    if not args.no_e2e:
+        nq_in, nq_out = args.level + 1, args.level
+        words_in, words_out = 2 * nq_in * N, 2 * nq_out * N
+        hin = torch.empty((args.batch, words_in), dtype=torch.int64, pin_memory=True)
+        hout = torch.empty((args.batch, words_out), dtype=torch.int64, pin_memory=True)
+        for i, c in enumerate(cts):
+            hin[i].copy_(torch.from_numpy(lib.GetCiphertextData(c).reshape(-1).view(np.int64)))
+        u64p = ctypes.POINTER(ctypes.c_uint64)
+
+        def e2e_step():
+            ids = []
+            for i in range(args.batch):
+                out = ctypes.c_int(0)
+                _capi.check(capi.helrm_NewCiphertextFromData(ctypes.cast(hin[i].data_ptr(), u64p), args.level, 2,
+                                                             scale, ctypes.byref(out)))
+                ids.append(out.value)
+            outs = step(ids)
+            for i, o in enumerate(outs):
+                _capi.check(capi.helrm_GetCiphertextData(o, ctypes.cast(hout[i].data_ptr(), u64p), words_out))
+            for x in ids + outs:
+                lib.DeleteCiphertext(x)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        dist.barrier()
+        lib.Synchronize()
+        _capi.check(capi.helrm_TimerStart())
+        for _ in range(args.steps):
+            e2e_step()
+        ms2 = ctypes.c_double(0)
+        _capi.check(capi.helrm_TimerStop(ctypes.byref(ms2)))
+        t_e2e = dist.max(ms2.value / 1000.0)
+        e2e = {"value": dist.world * args.batch * args.steps / t_e2e, "unit": UNIT,
+               "h2d_bytes_per_step": args.batch * words_in * 8, "d2h_bytes_per_step": args.batch * words_out * 8,
+               "ms_per_step": 1000.0 * t_e2e / args.steps}
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        threads = args.cpu_threads or os.cpu_count() or 1
+        try:
+            s, setup, _ = cpu_pcmm_seconds(ks, diags, rot, xs[0], args.level, threads)
+            cpu = {"value": 1.0 / s, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"1 ciphertext of the same PCMM (LT + rescale + {rot} fold rotations) on the oracle "
+                             f"port, {threads} threads, {s:.2f} s (setup {setup:.1f} s untimed)"}
+        except Exception as ex:  # the baseline must not sink the GPU line
+            cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "port", "sample": f"failed: {ex}"}
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64", "data": "synthetic (seeded Criteo-shaped queries; dataset absent)",
+            "config": cfg_dict(args, args.batch),
+            "pcmm_ms_per_batch": ms_step, "keyswitch_GBps": keyswitch_gbps,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": int(n1.value - n0.value), "clocks": clk, "kernels": kern,
+            "max_abs_err_embedding": max_err,
+        }
+        print(json.dumps(line), flush=True)
+    lib.DeleteScheme()
+
+
+def main():
+    args = parse()
+    dist = Dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, dist)
+        else:
+            run_b200(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -103,6 +103,12 @@ SIGNATURES = {
     "helrm_kernel_mac": [P(c_void), P(c_void), c_int, c_int, c_void, c_void],
     "helrm_kernel_rotate_hoisted": [c_void, c_int, c_int, P(c_int), c_int, c_void, c_void],
     "helrm_Synchronize": [],
+    "helrm_TimerStart": [],
+    "helrm_TimerStop": [P(c_double)],
+    "helrm_ProfileEnable": [c_int],
+    "helrm_ProfileRead": [P(c_double), P(c_double), P(c_double), P(c_u64), c_int, P(c_int)],
+    "helrm_KernelClassName": [c_int, ctypes.c_char_p, c_int],
+    "helrm_GetLaunchCount": [P(c_u64)],
 }
 
 ERRORS = {

@@ -963,6 +963,12 @@ public:
             ch.nbabies = (int)host.size();
             ch.gbase = s0;
             ch.gcount = cnt;
+            ch.nkeys = 0;
+            ch.npts = 0;
+            for (auto &bd : host) {
+                ch.nkeys += bd.key != nullptr;
+                for (int gi = 0; gi < HB_GCH; gi++) ch.npts += bd.pt[gi] != nullptr;
+            }
             t.plan_chunks.push_back(ch);
             sync();
         }
@@ -1840,4 +1846,62 @@ HB_API int helrm_kernel_rotate_hoisted(const uint64_t *in, int nq, int nbatch, c
 }
 HB_API int helrm_Synchronize(void) {
     return guard([&] { C().sync(); });
+}
+
+// ---- measurement ----------------------------------------------------------
+static cudaEvent_t g_t0 = nullptr, g_t1 = nullptr;
+
+HB_API int helrm_TimerStart(void) {
+    return guard([&] {
+        Context &c = C();
+        if (!g_t0) {
+            cuda_check(cudaEventCreate(&g_t0), "event");
+            cuda_check(cudaEventCreate(&g_t1), "event");
+        }
+        cuda_check(cudaEventRecord(g_t0, c.stream), "event record");
+    });
+}
+HB_API int helrm_TimerStop(double *ms) {
+    return guard([&] {
+        Context &c = C();
+        OUT(ms);
+        if (!g_t0) HB_THROW(HB_ESTATE, "TimerStop without TimerStart");
+        cuda_check(cudaEventRecord(g_t1, c.stream), "event record");
+        cuda_check(cudaEventSynchronize(g_t1), "event sync");
+        float f = 0.f;
+        cuda_check(cudaEventElapsedTime(&f, g_t0, g_t1), "elapsed");
+        *ms = f;
+    });
+}
+HB_API int helrm_ProfileEnable(int on) {
+    return guard([&] {
+        C().sync();
+        prof_enable(on != 0);
+    });
+}
+HB_API int helrm_ProfileRead(double *ms, double *bytes, double *work, uint64_t *launches, int cap, int *nclasses) {
+    return guard([&] {
+        C().sync();
+        ProfStats st;
+        prof_collect(&st);
+        if (nclasses) *nclasses = KC_COUNT;
+        for (int i = 0; i < KC_COUNT && i < cap; i++) {
+            if (ms) ms[i] = st.ms[i];
+            if (bytes) bytes[i] = st.bytes[i];
+            if (work) work[i] = st.work[i];
+            if (launches) launches[i] = st.launches[i];
+        }
+    });
+}
+HB_API int helrm_KernelClassName(int cls, char *out, int cap) {
+    return guard([&] {
+        if (!out || cap <= 0) HB_THROW(HB_EINVAL, "KernelClassName: bad buffer");
+        std::snprintf(out, (size_t)cap, "%s", kclass_name(cls));
+    });
+}
+HB_API int helrm_GetLaunchCount(uint64_t *n) {
+    return guard([&] {
+        OUT(n);
+        *n = launch_count();
+    });
 }

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "hb_kernels.cuh"
 
@@ -24,6 +25,85 @@ static void check_launch(const char *what) {
 void upload_prime_consts(const PrimeConst *pc, int n) {
     cudaError_t e = cudaMemcpyToSymbol(c_pc, pc, sizeof(PrimeConst) * n);
     if (e != cudaSuccess) throw std::runtime_error(std::string("prime constants: ") + cudaGetErrorString(e));
+}
+
+// =====================================================================
+// Launch accounting.  Every launcher counts the kernels it launches and,
+// while profiling is on, brackets them with CUDA events on the stream it
+// launches on, tagged with the launch's algorithmic bytes (each operand
+// read or written once) and integer work (modular products, or NTT
+// butterflies).  prof_collect() resolves the events.
+// =====================================================================
+static unsigned long long g_launches = 0;
+static bool g_prof_on = false;
+struct ProfRec {
+    cudaEvent_t a, b;
+    int cls;
+    double bytes, work;
+};
+static std::vector<ProfRec> g_pending;
+static std::vector<cudaEvent_t> g_event_pool;
+static ProfStats g_stats;
+
+static cudaEvent_t pool_event() {
+    if (!g_event_pool.empty()) {
+        cudaEvent_t e = g_event_pool.back();
+        g_event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    return e;
+}
+
+struct ProfScope {
+    int cls;
+    double bytes, work;
+    cudaStream_t s;
+    cudaEvent_t a = nullptr;
+    ProfScope(int c, double by, double wk, cudaStream_t st, int nlaunch) : cls(c), bytes(by), work(wk), s(st) {
+        g_launches += (unsigned long long)nlaunch;
+        if (g_prof_on) {
+            a = pool_event();
+            cudaEventRecord(a, s);
+        }
+    }
+    ~ProfScope() {
+        if (a) {
+            cudaEvent_t b = pool_event();
+            cudaEventRecord(b, s);
+            g_pending.push_back({a, b, cls, bytes, work});
+        }
+    }
+};
+
+static const char *kClassNames[KC_COUNT] = {
+    "ntt_forward", "ntt_inverse", "modup_bconv", "moddown_bconv", "moddown_combine", "keymult",
+    "bsgs_baby_mac", "rescale", "elementwise", "automorphism", "sampling"};
+
+const char *kclass_name(int c) { return (c >= 0 && c < KC_COUNT) ? kClassNames[c] : ""; }
+unsigned long long launch_count() { return g_launches; }
+
+void prof_collect(ProfStats *out) {
+    for (auto &r : g_pending) {
+        cudaEventSynchronize(r.b);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, r.a, r.b);
+        g_stats.ms[r.cls] += ms;
+        g_stats.bytes[r.cls] += r.bytes;
+        g_stats.work[r.cls] += r.work;
+        g_stats.launches[r.cls] += 1;
+        g_event_pool.push_back(r.a);
+        g_event_pool.push_back(r.b);
+    }
+    g_pending.clear();
+    if (out) *out = g_stats;
+}
+
+void prof_enable(bool on) {
+    prof_collect(nullptr);
+    g_stats = ProfStats{};
+    g_prof_on = on;
 }
 
 static inline unsigned grid1d(size_t work, int block) {
@@ -175,6 +255,12 @@ static void ntt_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bool 
         cudaFuncSetAttribute(k_ntt_rows<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
         attr_done = true;
     }
+    int active = nrows;
+    if (map.alpha > 0)
+        for (int r = 0; r < nrows; r++) active -= map.skip(r) ? 1 : 0;
+    const double nwords = (double)active * (double)(1 << logN);
+    ProfScope ps(inv ? KC_NTT_INV : KC_NTT_FWD, 16.0 * nwords, nwords / 2 * logN, s,
+                 2 * ((nrows + 65534) / 65535));
     for (int r0 = 0; r0 < nrows; r0 += 65535) {
         int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
         dim3 gc(1u << (logN2 - logC), nr), gr(1u << (logN1 - logRB), nr);
@@ -230,6 +316,7 @@ static void launch_ew2(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap m
     if (!npairs) return;
     unsigned g = grid1d(npairs, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 48.0 * npairs, 2.0 * npairs, s, 1);
     k_ew2<Op><<<g, 256, 0, s>>>(out, a, b, npairs, map, logN, op);
     check_launch("elementwise");
 }
@@ -251,6 +338,7 @@ void ew_neg(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cudaStream_
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * n, 0, s, 1);
     k_neg<<<g, 256, 0, s>>>(out, a, n, map, logN);
     check_launch("neg");
 }
@@ -268,6 +356,7 @@ void ew_mul_bcast(u64 *out, const u64 *a, const u64 *b, int npoly, int nq, int, 
     size_t n = ((size_t)npoly * nq) << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 8.0 * (2.0 * n + ((double)nq * (1 << logN))), (double)n, s, 1);
     k_mul_bcast<<<g, 256, 0, s>>>(out, a, b, n, nq, logN);
     check_launch("mul_bcast");
 }
@@ -283,6 +372,7 @@ void ew_mul_const(u64 *out, const u64 *a, const u64 *c, const u64 *cp, int nrows
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * n, (double)n, s, 1);
     k_mul_const<<<g, 256, 0, s>>>(out, a, c, cp, n, map, logN);
     check_launch("mul_const");
 }
@@ -297,6 +387,7 @@ void ew_add_const(u64 *out, const u64 *a, const u64 *c, int nrows, RowMap map, i
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * n, 0, s, 1);
     k_add_const<<<g, 256, 0, s>>>(out, a, c, n, map, logN);
     check_launch("add_const");
 }
@@ -318,6 +409,7 @@ void ew_tensor(u64 *out, const u64 *a, const u64 *b, int nq, int logN, cudaStrea
     size_t n = (size_t)nq << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 56.0 * n, 4.0 * n, s, 1);
     k_tensor<<<g, 256, 0, s>>>(out, a, b, nq, logN);
     check_launch("tensor");
 }
@@ -333,6 +425,7 @@ void ew_decrypt(u64 *out, const u64 *ct, const u64 *sk, int nq, int logN, cudaSt
     size_t n = (size_t)nq << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 32.0 * n, (double)n, s, 1);
     k_decrypt<<<g, 256, 0, s>>>(out, ct, sk, nq, logN);
     check_launch("decrypt");
 }
@@ -348,6 +441,7 @@ void ew_automorphism(u64 *out, const u64 *in, int nrows, u64 galois, int logN, c
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_AUTOMORPHISM, 16.0 * n, 0, s, 1);
     k_automorphism<<<g, 256, 0, s>>>(out, in, n, galois, logN);
     check_launch("automorphism");
 }
@@ -374,6 +468,8 @@ void ew_mac(u64 *out, const MacArgs &args, int npoly, int nq, int logN, cudaStre
     size_t n = ((size_t)npoly * nq) << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    const double words = (double)nq * (1 << logN);
+    ProfScope ps(KC_ELEMENTWISE, 8.0 * words * (args.n * (npoly + 1) + npoly), words * npoly * args.n, s, 1);
     k_mac<<<g, 256, 0, s>>>(out, args, npoly, nq, logN);
     check_launch("mac");
 }
@@ -421,6 +517,7 @@ void sample_uniform(u64 *out, int nrows, const int *, RowMap map, u64 seed, u64 
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_SAMPLE, 8.0 * n, 0, s, 1);
     k_uniform<<<g, 256, 0, s>>>(out, n, map, kseed, idx_base, logN);
     check_launch("uniform");
 }
@@ -446,6 +543,7 @@ void sample_cbd(u64 *out, int nrows, RowMap map, u64 seed, u64 domain, u64 idx_b
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_SAMPLE, 8.0 * n, 0, s, 1);
     k_cbd<<<g, 256, 0, s>>>(out, n, map, kseed, idx_base, logN);
     check_launch("cbd");
 }
@@ -465,6 +563,7 @@ void swk_combine(u64 *b, const u64 *a, const u64 *e, const u64 *sk, const u64 *t
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_SAMPLE, 40.0 * n, 2.0 * n, s, 1);
     k_swk_combine<<<g, 256, 0, s>>>(b, a, e, sk, target, pmod, n, digit_lo, digit_hi, logN);
     check_launch("swk_combine");
 }
@@ -481,6 +580,7 @@ void enc_combine(u64 *c0, const u64 *a, const u64 *e, const u64 *sk, const u64 *
     size_t n = (size_t)nq << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_SAMPLE, 40.0 * n, (double)n, s, 1);
     k_enc_combine<<<g, 256, 0, s>>>(c0, a, e, sk, m, n, logN);
     check_launch("enc_combine");
 }
@@ -536,6 +636,9 @@ void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, i
     if (alpha > HB_MAX_ALPHA) throw std::invalid_argument("alpha exceeds HB_MAX_ALPHA");
     const int N = 1 << logN;
     dim3 grid((N + 255) / 256, beta, nbatch);
+    const int ne = nq + K;
+    ProfScope ps(KC_MODUP_BCONV, 8.0 * nbatch * (double)N * (nq + (double)beta * ne),
+                 (double)nbatch * N * ((double)nq + (double)alpha * ((double)beta * ne - nq)), s, 1);
     k_modup_bconv<<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, beta, tab, logN, in_stride, out_stride,
                                        c1_stride);
     check_launch("modup_bconv");
@@ -572,6 +675,8 @@ void moddown_bconv(u64 *Z, const u64 *Y, int nq, int K, int L, const ModDownTab 
     if (K > 8) throw std::invalid_argument("at most 8 special primes");
     const int N = 1 << logN;
     dim3 grid((N + 255) / 256, nbatch);
+    ProfScope ps(KC_MODDOWN_BCONV, 8.0 * nbatch * (double)N * (K + nq), (double)nbatch * N * (K + (double)K * nq), s,
+                 1);
     k_moddown_bconv<<<grid, 256, 0, s>>>(Z, Y, nq, K, L, tab, logN, in_stride, out_stride);
     check_launch("moddown_bconv");
 }
@@ -601,6 +706,7 @@ void moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, const ModDown
     unsigned g = grid1d(n, 256);
     if (g > 4096) g = 4096;
     dim3 grid(g, nbatch);
+    ProfScope ps(KC_MODDOWN_COMBINE, 8.0 * nbatch * (double)n * (addend ? 4 : 3), (double)nbatch * n, s, 1);
     k_moddown_combine<<<grid, 256, 0, s>>>(out, x, Z, nq, tab, addend, add_galois, logN, x_stride, z_stride,
                                            out_stride, add_stride);
     check_launch("moddown_combine");
@@ -631,6 +737,7 @@ void rescale_prep(u64 *W, const u64 *R, int npoly, int nq_out, u64 ql, int logN,
     size_t n = ((size_t)npoly * nq_out) << logN;
     unsigned g = grid1d(n, 256);
     if (g > 4096) g = 4096;
+    ProfScope ps(KC_RESCALE, 8.0 * nbatch * ((double)n + (double)((size_t)npoly << logN)), 0, s, 1);
     k_rescale_prep<<<dim3(g, nbatch), 256, 0, s>>>(W, R, npoly, nq_out, ql, logN, r_stride, w_stride);
     check_launch("rescale_prep");
 }
@@ -654,6 +761,7 @@ void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in,
     size_t n = ((size_t)npoly * (nq_in - 1)) << logN;
     unsigned g = grid1d(n, 256);
     if (g > 4096) g = 4096;
+    ProfScope ps(KC_RESCALE, 24.0 * nbatch * (double)n, (double)nbatch * n, s, 1);
     k_rescale_combine<<<dim3(g, nbatch), 256, 0, s>>>(out, c, W, npoly, nq_in, qlinv, qlinvp, logN, c_stride,
                                                       w_stride, out_stride);
     check_launch("rescale_combine");
@@ -703,6 +811,11 @@ void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, 
     size_t n = (size_t)(nq + K) << logN;
     unsigned g = grid1d(n, 256);
     if (g > 4096) g = 4096;
+    // digits per ciphertext + the key once per launch + accumulator traffic
+    const double nd = (double)n;
+    ProfScope ps(KC_KEYMULT,
+                 8.0 * (nbatch * nd * (beta + 2.0 + (addb ? 1.0 : 0.0) + (accumulate ? 2.0 : 0.0)) + 2.0 * beta * nd),
+                 2.0 * beta * nbatch * nd, s, 1);
     k_keymult<<<dim3(g, nbatch), 256, 0, s>>>(acc, D, key, galois, nq, K, L, beta, keyP, addb, accumulate ? 1 : 0,
                                               logN, d_stride, acc_stride, add_stride);
     check_launch("keymult");
@@ -787,6 +900,13 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
         cudaFuncSetAttribute(k_bsgs_baby_mac, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
         attr = true;
     }
+    // per ciphertext: c0/c1 rows, the digits, the inner sums written; per
+    // launch: every baby key and plaintext of the chunk once
+    const double nd = (double)n, nqw = (double)nq * (1 << logN);
+    ProfScope ps(KC_BSGS_MAC,
+                 8.0 * (nbatch * (2.0 * nqw + beta * nd + 2.0 * ch.gcount * nd) + 2.0 * beta * ch.nkeys * nd +
+                        ch.npts * nd),
+                 (double)nbatch * nd * (2.0 * beta * ch.nkeys + 2.0 * ch.npts), s, 1);
     k_bsgs_baby_mac<<<dim3(g, nbatch), 256, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN,
                                                        ct_stride, d_stride, inner_stride);
     check_launch("bsgs_baby_mac");

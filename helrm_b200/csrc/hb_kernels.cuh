@@ -50,6 +50,22 @@ struct NttTables {
 
 void upload_prime_consts(const PrimeConst *pc, int n);
 
+// ---- launch accounting ------------------------------------------------------
+enum KernelClass {
+    KC_NTT_FWD, KC_NTT_INV, KC_MODUP_BCONV, KC_MODDOWN_BCONV, KC_MODDOWN_COMBINE, KC_KEYMULT,
+    KC_BSGS_MAC, KC_RESCALE, KC_ELEMENTWISE, KC_AUTOMORPHISM, KC_SAMPLE, KC_COUNT
+};
+struct ProfStats {
+    double ms[KC_COUNT] = {};
+    double bytes[KC_COUNT] = {};      // algorithmic bytes
+    double work[KC_COUNT] = {};       // modular products (NTT: butterflies)
+    unsigned long long launches[KC_COUNT] = {};
+};
+void prof_enable(bool on);             // resets the statistics
+void prof_collect(ProfStats *out);     // waits for the recorded events
+const char *kclass_name(int c);
+unsigned long long launch_count();     // kernels launched since load
+
 // ---- NTT -----------------------------------------------------------------
 void ntt_forward(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s);
 void ntt_inverse(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s);
@@ -162,6 +178,8 @@ struct BsgsChunk {
     int nbabies;
     int gbase;               // first output giant slot of this chunk
     int gcount;              // giant slots in this chunk (<= HB_GCH)
+    int nkeys;               // babies with a key (b != 0), for accounting
+    int npts;                // plaintexts referenced by the chunk, for accounting
 };
 // inner[g][pl][e][n] for g in [gbase, gbase+gcount): sum over babies of
 // pt(g, b) * R_b, R_b = baby rotation of the input kept in the PQ basis:

@@ -207,6 +207,20 @@ int helrm_kernel_rotate_hoisted(const uint64_t *d_in, int nq, int nbatch, const 
 /* synchronise the library stream */
 int helrm_Synchronize(void);
 
+/* ---- measurement (no reference counterpart; the reference times with
+ * torch.cuda.synchronize + wall clock, examples/criteo/bench_sweep.py:192-222) -- */
+/* CUDA events on the library stream around a region of work. */
+int helrm_TimerStart(void);
+int helrm_TimerStop(double *ms);
+/* Per-kernel-class CUDA-event timing on the launching stream, with each
+ * launch's algorithmic bytes and modular products (NTT: butterflies).
+ * Enabling resets the statistics. */
+int helrm_ProfileEnable(int on);
+int helrm_ProfileRead(double *ms, double *bytes, double *work, uint64_t *launches, int cap, int *nclasses);
+int helrm_KernelClassName(int cls, char *out, int cap);
+/* number of kernels this library has launched since it was loaded */
+int helrm_GetLaunchCount(uint64_t *n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,15 +52,45 @@
 #include <string.h>
 #include <math.h>
 
-#ifdef _OPENMP
-#include <omp.h>
-#endif
+#include <pthread.h>
 
 typedef unsigned __int128 u128;
 typedef __int128 i128;
 typedef uint64_t u64;
 
 #define ORA_MAXP 64
+
+/* ------------------------------------------------------------------ */
+/* parallel for over independent limbs (plain pthreads, no shared state  */
+/* beyond an atomic work counter)                                       */
+/* ------------------------------------------------------------------ */
+static int g_threads = 1;
+typedef void (*par_fn)(void *ctx, int i);
+typedef struct { par_fn fn; void *ctx; int n; int next; } par_job;
+
+static void *par_worker(void *arg) {
+    par_job *j = (par_job *)arg;
+    for (;;) {
+        int i = __atomic_fetch_add(&j->next, 1, __ATOMIC_RELAXED);
+        if (i >= j->n) break;
+        j->fn(j->ctx, i);
+    }
+    return NULL;
+}
+
+static void par_for(int n, par_fn fn, void *ctx) {
+    int nt = g_threads < n ? g_threads : n;
+    if (nt <= 1) { for (int i = 0; i < n; i++) fn(ctx, i); return; }
+    par_job job = {fn, ctx, n, 0};
+    pthread_t th[512];
+    if (nt > 512) nt = 512;
+    for (int t = 0; t < nt - 1; t++) pthread_create(&th[t], NULL, par_worker, &job);
+    par_worker(&job);
+    for (int t = 0; t < nt - 1; t++) pthread_join(th[t], NULL);
+}
+
+void ora_set_threads(int n) { g_threads = n < 1 ? 1 : n; }
+int ora_num_threads(void) { return g_threads; }
 
 /* ------------------------------------------------------------------ */
 /* modular helpers                                                     */
@@ -379,34 +409,37 @@ u64 ora_key_seed(u64 master, u64 galois) { return ora_rand64(master, DOM_KEYSEED
 
 /* switching key from target t (NTT, all L+K primes) to s.
  * swk layout [dnum][2 (b, a)][L+K][N];  b = -a s + e + [p in digit j] P t */
-void ora_gen_swk(const ora_ctx *c, const u64 *sk, const u64 *target, u64 kseed, u64 *swk) {
-    const int N = c->N, np = c->L + c->K;
-    int64_t *ev = (int64_t *)malloc(sizeof(int64_t) * N);
+typedef struct { const ora_ctx *c; const u64 *sk, *target; u64 kseed; u64 *swk; } swk_job;
+
+static void swk_row(void *p_, int k) {
+    swk_job *J = (swk_job *)p_;
+    const ora_ctx *c = J->c;
+    const int N = c->N, np = c->L + c->K, j = k / np, p = k % np;
+    const u64 q = c->q[p], kseed = J->kseed;
+    u64 *b = J->swk + (((size_t)j * 2 + 0) * np + p) * N;
+    u64 *a = J->swk + (((size_t)j * 2 + 1) * np + p) * N;
     u64 *erow = (u64 *)malloc(sizeof(u64) * N);
-    for (int j = 0; j < c->dnum; j++) {
-        for (int n = 0; n < N; n++) ev[n] = ora_cbd(kseed, DOM_SWK_E, (u64)j * N + n);
-        for (int p = 0; p < np; p++) {
-            u64 q = c->q[p];
-            u64 *b = swk + (((size_t)j * 2 + 0) * np + p) * N;
-            u64 *a = swk + (((size_t)j * 2 + 1) * np + p) * N;
-            for (int n = 0; n < N; n++)
-                a[n] = ora_uniform(kseed, DOM_SWK_A, ((u64)j * np + p) * N + n, q);
-            for (int n = 0; n < N; n++) {
-                int64_t x = ev[n];
-                erow[n] = x >= 0 ? (u64)x % q : q - ((u64)(-x) % q);
-            }
-            ora_ntt(c, p, erow);
-            int in_digit = (p < c->L) && (p / c->alpha == j);
-            u64 Pq = in_digit ? pmod(c, q) : 0;
-            const u64 *sp = sk + (size_t)p * N, *tp = target + (size_t)p * N;
-            for (int n = 0; n < N; n++) {
-                u64 v = subm(erow[n], mulm(a[n], sp[n], q), q);
-                if (in_digit) v = addm(v, mulm(Pq, tp[n], q), q);
-                b[n] = v;
-            }
-        }
+    for (int n = 0; n < N; n++)
+        a[n] = ora_uniform(kseed, DOM_SWK_A, ((u64)j * np + p) * N + n, q);
+    for (int n = 0; n < N; n++) {
+        int64_t x = ora_cbd(kseed, DOM_SWK_E, (u64)j * N + n);
+        erow[n] = x >= 0 ? (u64)x % q : q - ((u64)(-x) % q);
     }
-    free(ev); free(erow);
+    ora_ntt(c, p, erow);
+    int in_digit = (p < c->L) && (p / c->alpha == j);
+    u64 Pq = in_digit ? pmod(c, q) : 0;
+    const u64 *sp = J->sk + (size_t)p * N, *tp = J->target + (size_t)p * N;
+    for (int n = 0; n < N; n++) {
+        u64 v = subm(erow[n], mulm(a[n], sp[n], q), q);
+        if (in_digit) v = addm(v, mulm(Pq, tp[n], q), q);
+        b[n] = v;
+    }
+    free(erow);
+}
+
+void ora_gen_swk(const ora_ctx *c, const u64 *sk, const u64 *target, u64 kseed, u64 *swk) {
+    swk_job J = {c, sk, target, kseed, swk};
+    par_for(c->dnum * (c->L + c->K), swk_row, &J);
 }
 
 /* rotation key for Galois element g: encrypts sigma_g(s) under s */
@@ -518,17 +551,24 @@ void ora_encode_coeffs(const ora_ctx *c, const double *vals, int nvals, long dou
 }
 
 /* integer coefficients -> NTT residues on the given prime rows */
-void ora_coeffs_to_ntt(const ora_ctx *c, const i128 *coeffs, const int *prime_idx, int np, u64 *out) {
-    for (int r = 0; r < np; r++) {
-        int p = prime_idx[r]; u64 q = c->q[p];
-        u64 *row = out + (size_t)r * c->N;
-        for (int n = 0; n < c->N; n++) {
-            i128 x = coeffs[n];
-            u64 m = x >= 0 ? (u64)((u128)x % q) : (u64)((q - (u64)((u128)(-x) % q)) % q);
-            row[n] = m;
-        }
-        ora_ntt(c, p, row);
+typedef struct { const ora_ctx *c; const i128 *coeffs; const int *prime_idx; u64 *out; } c2n_job;
+
+static void c2n_row(void *p_, int r) {
+    c2n_job *J = (c2n_job *)p_;
+    const ora_ctx *c = J->c;
+    int p = J->prime_idx[r]; u64 q = c->q[p];
+    u64 *row = J->out + (size_t)r * c->N;
+    for (int n = 0; n < c->N; n++) {
+        i128 x = J->coeffs[n];
+        u64 m = x >= 0 ? (u64)((u128)x % q) : (u64)((q - (u64)((u128)(-x) % q)) % q);
+        row[n] = m;
     }
+    ora_ntt(c, p, row);
+}
+
+void ora_coeffs_to_ntt(const ora_ctx *c, const i128 *coeffs, const int *prime_idx, int np, u64 *out) {
+    c2n_job J = {c, coeffs, prime_idx, out};
+    par_for(np, c2n_row, &J);
 }
 
 /* encode real/complex values at level (nq = level+1 limbs); if ext != 0
@@ -599,24 +639,35 @@ void ora_decode(const ora_ctx *c, const u64 *pt, int nq, double scale, double *v
 /* rescale (rounded division by the last prime), both polys             */
 /* ct: [npoly][nq][N] -> out: [npoly][nq-1][N]                         */
 /* ------------------------------------------------------------------ */
+typedef struct { const ora_ctx *c; const u64 *ct; u64 *out; const u64 *r; int nq; } rescale_job;
+
+static void rescale_row(void *p, int k) {
+    rescale_job *J = (rescale_job *)p;
+    const ora_ctx *c = J->c;
+    const int N = c->N, nq = J->nq, l = nq - 1, pl = k / l, i = k % l;
+    const u64 ql = c->q[l], h = ql >> 1, q = c->q[i], hq = h % q, inv = invm(ql % q, q);
+    const u64 *r = J->r + (size_t)pl * N;
+    u64 *w = (u64 *)malloc(sizeof(u64) * N);
+    for (int n = 0; n < N; n++) w[n] = subm(hq, r[n] % q, q);
+    ora_ntt(c, i, w);
+    u64 *o = J->out + ((size_t)pl * l + i) * N;
+    const u64 *x = J->ct + ((size_t)pl * nq + i) * N;
+    for (int n = 0; n < N; n++) o[n] = mulm(addm(x[n], w[n], q), inv, q);
+    free(w);
+}
+
 void ora_rescale(const ora_ctx *c, const u64 *ct, int npoly, int nq, u64 *out) {
     const int N = c->N, l = nq - 1; const u64 ql = c->q[l], h = ql >> 1;
-    u64 *r = (u64 *)malloc(sizeof(u64) * N), *w = (u64 *)malloc(sizeof(u64) * N);
+    u64 *r = (u64 *)malloc(sizeof(u64) * (size_t)npoly * N);
     for (int pl = 0; pl < npoly; pl++) {
-        const u64 *in = ct + (size_t)pl * nq * N;
-        memcpy(r, in + (size_t)l * N, sizeof(u64) * N);
-        ora_intt(c, l, r);
-        for (int n = 0; n < N; n++) r[n] = addm(r[n], h, ql);   /* (c + h) mod q_l */
-        for (int i = 0; i < l; i++) {
-            u64 q = c->q[i], hq = h % q, inv = invm(ql % q, q);
-            for (int n = 0; n < N; n++) w[n] = subm(hq, r[n] % q, q);
-            ora_ntt(c, i, w);
-            u64 *o = out + ((size_t)pl * l + i) * N;
-            const u64 *x = in + (size_t)i * N;
-            for (int n = 0; n < N; n++) o[n] = mulm(addm(x[n], w[n], q), inv, q);
-        }
+        u64 *rp = r + (size_t)pl * N;
+        memcpy(rp, ct + ((size_t)pl * nq + l) * N, sizeof(u64) * N);
+        ora_intt(c, l, rp);
+        for (int n = 0; n < N; n++) rp[n] = addm(rp[n], h, ql);   /* (c + h) mod q_l */
     }
-    free(r); free(w);
+    rescale_job J = {c, ct, out, r, nq};
+    par_for(npoly * l, rescale_row, &J);
+    free(r);
 }
 
 /* ------------------------------------------------------------------ */
@@ -624,27 +675,51 @@ void ora_rescale(const ora_ctx *c, const u64 *ct, int npoly, int nq, u64 *out) {
 /* ------------------------------------------------------------------ */
 /* ModUp of one poly a (NTT, nq rows) into beta digits over the extended
  * basis: D[j][e][N], e in [0, nq+K). */
+typedef struct { const ora_ctx *c; const u64 *a; int nq; u64 *y; u64 *D; } modup_job;
+
+/* phase 1: y_m = INTT(a_m) * (Q_j/q_m)^-1 mod q_m for every input limb m */
+static void modup_in(void *p, int pm) {
+    modup_job *J = (modup_job *)p;
+    const ora_ctx *c = J->c;
+    const int N = c->N, alpha = c->alpha, nq = J->nq;
+    const int lo = (pm / alpha) * alpha, hi = lo + alpha < nq ? lo + alpha : nq;
+    const u64 qm = c->q[pm];
+    u64 *y = J->y + (size_t)pm * N;
+    memcpy(y, J->a + (size_t)pm * N, sizeof(u64) * N);
+    ora_intt(c, pm, y);
+    u64 qhat = 1 % qm;
+    for (int m2 = lo; m2 < hi; m2++) if (m2 != pm) qhat = mulm(qhat, c->q[m2] % qm, qm);
+    u64 qhinv = invm(qhat, qm);
+    for (int n = 0; n < N; n++) y[n] = mulm(y[n], qhinv, qm);
+}
+
+static void modup_out(void *p, int k);
+
 void ora_modup(const ora_ctx *c, const u64 *a, int nq, u64 *D) {
     const int N = c->N, K = c->K, ne = nq + K, alpha = c->alpha;
     const int beta = (nq + alpha - 1) / alpha;
-    #pragma omp parallel for schedule(dynamic)
-    for (int j = 0; j < beta; j++) {
-        int lo = j * alpha, hi = (j + 1) * alpha < nq ? (j + 1) * alpha : nq, na = hi - lo;
-        u64 *y = (u64 *)malloc(sizeof(u64) * (size_t)na * N);
-        u64 *z = (u64 *)malloc(sizeof(u64) * N);
-        for (int m = 0; m < na; m++) {
-            int pm = lo + m; u64 qm = c->q[pm];
-            memcpy(y + (size_t)m * N, a + (size_t)pm * N, sizeof(u64) * N);
-            ora_intt(c, pm, y + (size_t)m * N);
-            u64 qhat = 1 % qm;
-            for (int m2 = 0; m2 < na; m2++) if (m2 != m) qhat = mulm(qhat, c->q[lo + m2] % qm, qm);
-            u64 qhinv = invm(qhat, qm);
-            for (int n = 0; n < N; n++) y[(size_t)m * N + n] = mulm(y[(size_t)m * N + n], qhinv, qm);
-        }
-        for (int e = 0; e < ne; e++) {
+    modup_job J = {c, a, nq, (u64 *)malloc(sizeof(u64) * (size_t)nq * N), D};
+    par_for(nq, modup_in, &J);
+    par_for(beta * ne, modup_out, &J);
+    free(J.y);
+}
+
+/* phase 2: digit j, extended row e */
+static void modup_out(void *p, int k) {
+    modup_job *J = (modup_job *)p;
+    const ora_ctx *c = J->c;
+    const int N = c->N, K = c->K, nq = J->nq, ne = nq + K, alpha = c->alpha;
+    const int j = k / ne, e = k % ne;
+    const int lo = j * alpha, hi = (j + 1) * alpha < nq ? (j + 1) * alpha : nq, na = hi - lo;
+    const u64 *y = J->y + (size_t)lo * N;
+    const u64 *a = J->a;
+    u64 *D = J->D;
+    {
+        {
             int pt = ext_prime(c, nq, e);
             u64 *dst = D + ((size_t)j * ne + e) * N;
-            if (pt >= lo && pt < hi) { memcpy(dst, a + (size_t)pt * N, sizeof(u64) * N); continue; }
+            if (pt >= lo && pt < hi) { memcpy(dst, a + (size_t)pt * N, sizeof(u64) * N); return; }
+            u64 *z = (u64 *)malloc(sizeof(u64) * N);
             u64 t = c->q[pt];
             u64 cm[ORA_MAXP];
             u64 Qj = 1 % t;   /* Q_j mod t */
@@ -668,26 +743,34 @@ void ora_modup(const ora_ctx *c, const u64 *a, int nq, u64 *D) {
             }
             ora_ntt(c, pt, z);
             memcpy(dst, z, sizeof(u64) * N);
+            free(z);
         }
-        free(y); free(z);
     }
 }
 
-/* ModDown of x (NTT, extended basis nq+K rows) -> out (nq rows) */
-void ora_moddown(const ora_ctx *c, const u64 *x, int nq, u64 *out) {
+typedef struct { const ora_ctx *c; const u64 *x; int nq; u64 *y; u64 *out; } moddown_job;
+
+static void moddown_in(void *p, int k) {
+    moddown_job *J = (moddown_job *)p;
+    const ora_ctx *c = J->c;
     const int N = c->N, K = c->K, L = c->L;
-    u64 *y = (u64 *)malloc(sizeof(u64) * (size_t)K * N);
-    for (int k = 0; k < K; k++) {
-        u64 pk = c->q[L + k];
-        memcpy(y + (size_t)k * N, x + ((size_t)nq + k) * N, sizeof(u64) * N);
-        ora_intt(c, L + k, y + (size_t)k * N);
-        u64 phat = 1 % pk;
-        for (int k2 = 0; k2 < K; k2++) if (k2 != k) phat = mulm(phat, c->q[L + k2] % pk, pk);
-        u64 inv = invm(phat, pk);
-        for (int n = 0; n < N; n++) y[(size_t)k * N + n] = mulm(y[(size_t)k * N + n], inv, pk);
-    }
-    #pragma omp parallel for schedule(dynamic)
-    for (int i = 0; i < nq; i++) {
+    u64 pk = c->q[L + k];
+    u64 *y = J->y + (size_t)k * N;
+    memcpy(y, J->x + ((size_t)J->nq + k) * N, sizeof(u64) * N);
+    ora_intt(c, L + k, y);
+    u64 phat = 1 % pk;
+    for (int k2 = 0; k2 < K; k2++) if (k2 != k) phat = mulm(phat, c->q[L + k2] % pk, pk);
+    u64 inv = invm(phat, pk);
+    for (int n = 0; n < N; n++) y[n] = mulm(y[n], inv, pk);
+}
+
+static void moddown_out(void *p, int i) {
+    moddown_job *J = (moddown_job *)p;
+    const ora_ctx *c = J->c;
+    const int N = c->N, K = c->K, L = c->L;
+    const u64 *y = J->y, *x = J->x;
+    u64 *out = J->out;
+    {
         u64 q = c->q[i];
         u64 cm[ORA_MAXP];
         for (int k = 0; k < K; k++) {
@@ -713,30 +796,44 @@ void ora_moddown(const ora_ctx *c, const u64 *x, int nq, u64 *out) {
         for (int n = 0; n < N; n++) out[(size_t)i * N + n] = mulm(subm(x[(size_t)i * N + n], z[n], q), pinv, q);
         free(z);
     }
-    free(y);
+}
+
+/* ModDown of x (NTT, extended basis nq+K rows) -> out (nq rows) */
+void ora_moddown(const ora_ctx *c, const u64 *x, int nq, u64 *out) {
+    moddown_job J = {c, x, nq, (u64 *)malloc(sizeof(u64) * (size_t)c->K * c->N), out};
+    par_for(c->K, moddown_in, &J);
+    par_for(nq, moddown_out, &J);
+    free(J.y);
 }
 
 /* KeyMult with the automorphism folded into the digit index:
  * acc[pl][e][n] = sum_j D[j][e][tau(n)] * swk[j][pl][prime(e)][n] */
-void ora_keymult(const ora_ctx *c, const u64 *D, int nq, const u64 *swk, u64 g, u64 *acc) {
-    const int N = c->N, K = c->K, ne = nq + K, np = c->L + c->K;
+typedef struct { const ora_ctx *c; const u64 *D; int nq; const u64 *swk; const unsigned *idx; u64 *acc; } keymult_job;
+
+static void keymult_row(void *p, int e) {
+    keymult_job *J = (keymult_job *)p;
+    const ora_ctx *c = J->c;
+    const int N = c->N, nq = J->nq, ne = nq + c->K, np = c->L + c->K;
     const int beta = (nq + c->alpha - 1) / c->alpha;
-    unsigned *idx = (unsigned *)malloc(sizeof(unsigned) * N);
-    aut_index(c, g, idx);
-    #pragma omp parallel for schedule(dynamic)
-    for (int e = 0; e < ne; e++) {
-        int p = ext_prime(c, nq, e); u64 q = c->q[p];
-        for (int pl = 0; pl < 2; pl++) {
-            u64 *o = acc + ((size_t)pl * ne + e) * N;
-            for (int n = 0; n < N; n++) {
-                u128 s = 0;
-                for (int j = 0; j < beta; j++)
-                    s += (u128)mulm(D[((size_t)j * ne + e) * N + idx[n]],
-                                    swk[(((size_t)j * 2 + pl) * np + p) * N + n], q);
-                o[n] = (u64)(s % q);
-            }
+    const int pr = ext_prime(c, nq, e);
+    const u64 q = c->q[pr];
+    for (int pl = 0; pl < 2; pl++) {
+        u64 *o = J->acc + ((size_t)pl * ne + e) * N;
+        for (int n = 0; n < N; n++) {
+            u128 s = 0;
+            for (int j = 0; j < beta; j++)
+                s += (u128)mulm(J->D[((size_t)j * ne + e) * N + J->idx[n]],
+                                J->swk[(((size_t)j * 2 + pl) * np + pr) * N + n], q);
+            o[n] = (u64)(s % q);
         }
     }
+}
+
+void ora_keymult(const ora_ctx *c, const u64 *D, int nq, const u64 *swk, u64 g, u64 *acc) {
+    unsigned *idx = (unsigned *)malloc(sizeof(unsigned) * c->N);
+    aut_index(c, g, idx);
+    keymult_job J = {c, D, nq, swk, idx, acc};
+    par_for(nq + c->K, keymult_row, &J);
     free(idx);
 }
 
@@ -849,6 +946,72 @@ static const u64 *find_key(const u64 *gal, const u64 *const *ptr, int nkeys, u64
     return NULL;
 }
 
+typedef struct {
+    const ora_ctx *c; const u64 *ct; int nq; const u64 *D; const int *diag_k; const u64 *const *pts;
+    int ndiag; int bs; int nbab; const int *bab_b; const u64 *const *bab_key; const unsigned *bab_idx;
+    int ng; u64 *inner; const u64 *Pq;
+} bsgs_job;
+
+/* one extended limb e: baby rotations R_b (PQ basis) and their products
+ * with the plaintexts, summed per giant group with lazy 128-bit sums */
+static void bsgs_row(void *p, int e) {
+    bsgs_job *J = (bsgs_job *)p;
+    const ora_ctx *c = J->c;
+    const int N = c->N, nq = J->nq, ne = nq + c->K, np = c->L + c->K;
+    const int beta = (nq + c->alpha - 1) / c->alpha;
+    const int pr = ext_prime(c, nq, e);
+    const u64 q = c->q[pr];
+    const size_t esz = (size_t)ne * N;
+    const u64 *c0 = J->ct, *c1 = J->ct + (size_t)nq * N;
+    u128 *acc = (u128 *)calloc((size_t)J->ng * 2 * N, sizeof(u128));
+    int *cnt = (int *)calloc(J->ng, sizeof(int));
+    u64 *rb = (u64 *)malloc(sizeof(u64) * N), *ra = (u64 *)malloc(sizeof(u64) * N);
+    for (int bi = 0; bi < J->nbab; bi++) {
+        const int b = J->bab_b[bi];
+        if (b == 0) {
+            for (int n = 0; n < N; n++) {
+                rb[n] = e < nq ? mulm(J->Pq[e], c0[(size_t)e * N + n], q) : 0;
+                ra[n] = e < nq ? mulm(J->Pq[e], c1[(size_t)e * N + n], q) : 0;
+            }
+        } else {
+            const unsigned *idx = J->bab_idx + (size_t)bi * N;
+            const u64 *swk = J->bab_key[bi];
+            for (int n = 0; n < N; n++) {
+                u128 sb = 0, sa = 0;
+                for (int j = 0; j < beta; j++) {
+                    u64 d = J->D[((size_t)j * ne + e) * N + idx[n]];
+                    sb += (u128)mulm(d, swk[(((size_t)j * 2 + 0) * np + pr) * N + n], q);
+                    sa += (u128)mulm(d, swk[(((size_t)j * 2 + 1) * np + pr) * N + n], q);
+                }
+                if (e < nq) sb += (u128)mulm(J->Pq[e], c0[(size_t)e * N + idx[n]], q);
+                rb[n] = (u64)(sb % q);
+                ra[n] = (u64)(sa % q);
+            }
+        }
+        for (int t = 0; t < J->ndiag; t++) {
+            if (J->diag_k[t] % J->bs != b) continue;
+            const int g = J->diag_k[t] / J->bs;
+            const u64 *pt = J->pts[t] + (size_t)e * N;
+            u128 *a = acc + (size_t)g * 2 * N;
+            for (int n = 0; n < N; n++) {
+                a[n] += (u128)rb[n] * pt[n];
+                a[N + n] += (u128)ra[n] * pt[n];
+            }
+            if (++cnt[g] % 16 == 0)
+                for (int n = 0; n < 2 * N; n++) a[n] %= q;
+        }
+    }
+    for (int g = 0; g < J->ng; g++) {
+        u64 *I = J->inner + (size_t)g * 2 * esz + (size_t)e * N;
+        const u128 *a = acc + (size_t)g * 2 * N;
+        for (int n = 0; n < N; n++) {
+            I[n] = (u64)(a[n] % q);
+            I[esz + n] = (u64)(a[N + n] % q);
+        }
+    }
+    free(acc); free(cnt); free(rb); free(ra);
+}
+
 int ora_bsgs_lt(const ora_ctx *c, const u64 *ct, int nq, const int *diag_k, const u64 *const *pts,
                 int ndiag, int bs, const u64 *key_gal, const u64 *const *key_ptr, int nkeys, u64 *out) {
     const int N = c->N, K = c->K, ne = nq + K, L = c->L;
@@ -869,44 +1032,35 @@ int ora_bsgs_lt(const ora_ctx *c, const u64 *ct, int nq, const int *diag_k, cons
     int *used = (int *)calloc(ng, sizeof(int));
     u64 *R = (u64 *)malloc(sizeof(u64) * 2 * esz);
     unsigned *idx = (unsigned *)malloc(sizeof(unsigned) * N);
+    for (int t = 0; t < ndiag; t++) used[diag_k[t] / bs] = 1;
 
-    /* babies in increasing b; each baby rotated once (in PQ) then MAC'd */
+    /* babies in increasing b, each rotated in the PQ basis (never ModDown'd)
+     * and multiplied into every giant group that uses it; independent per
+     * extended limb e */
+    int nbab = 0;
+    int *bab_b = (int *)malloc(sizeof(int) * (bs < ndiag ? bs : ndiag));
+    const u64 **bab_key = (const u64 **)malloc(sizeof(u64 *) * (bs < ndiag ? bs : ndiag));
     for (int b = 0; b < bs; b++) {
         int any = 0;
         for (int t = 0; t < ndiag; t++) if (diag_k[t] % bs == b) { any = 1; break; }
         if (!any) continue;
-        if (b == 0) {
-            for (int pl = 0; pl < 2; pl++)
-                for (int e = 0; e < ne; e++)
-                    for (int n = 0; n < N; n++)
-                        R[(size_t)pl * esz + (size_t)e * N + n] =
-                            e < nq ? mulm(Pq[e], ct[((size_t)pl * nq + e) * N + n], c->q[e]) : 0;
-        } else {
-            u64 g = ora_galois_rotation(c, b);
-            const u64 *swk = find_key(key_gal, key_ptr, nkeys, g);
-            if (!swk) { free(D); free(inner); free(used); free(R); free(idx); return -1; }
-            ora_keymult(c, D, nq, swk, g, R);
-            aut_index(c, g, idx);
-            for (int e = 0; e < nq; e++)
-                for (int n = 0; n < N; n++) {
-                    size_t x = (size_t)e * N + n;
-                    R[x] = addm(R[x], mulm(Pq[e], ct[(size_t)e * N + idx[n]], c->q[e]), c->q[e]);
-                }
+        bab_b[nbab] = b;
+        bab_key[nbab] = NULL;
+        if (b != 0) {
+            bab_key[nbab] = find_key(key_gal, key_ptr, nkeys, ora_galois_rotation(c, b));
+            if (!bab_key[nbab]) {
+                free(D); free(inner); free(used); free(R); free(idx); free(bab_b); free(bab_key);
+                return -1;
+            }
         }
-        for (int t = 0; t < ndiag; t++) {
-            if (diag_k[t] % bs != b) continue;
-            int g = diag_k[t] / bs; used[g] = 1;
-            u64 *I = inner + (size_t)g * 2 * esz;
-            for (int pl = 0; pl < 2; pl++)
-                for (int e = 0; e < ne; e++) {
-                    u64 q = c->q[ext_prime(c, nq, e)];
-                    for (int n = 0; n < N; n++) {
-                        size_t x = (size_t)pl * esz + (size_t)e * N + n;
-                        I[x] = addm(I[x], mulm(R[x], pts[t][(size_t)e * N + n], q), q);
-                    }
-                }
-        }
+        nbab++;
     }
+    unsigned *bab_idx = (unsigned *)malloc(sizeof(unsigned) * (size_t)nbab * N);
+    for (int bi = 0; bi < nbab; bi++)
+        aut_index(c, bab_b[bi] ? ora_galois_rotation(c, bab_b[bi]) : 1, bab_idx + (size_t)bi * N);
+    bsgs_job BJ = {c, ct, nq, D, diag_k, pts, ndiag, bs, nbab, bab_b, bab_key, bab_idx, ng, inner, Pq};
+    par_for(ne, bsgs_row, &BJ);
+    free(bab_b); free(bab_key); free(bab_idx);
 
     /* giant steps in the PQ basis, accumulated, then one ModDown */
     u64 *acc = (u64 *)calloc(2 * esz, sizeof(u64));
@@ -946,17 +1100,3 @@ int ora_bsgs_lt(const ora_ctx *c, const u64 *ct, int nq, const int *diag_k, cons
     return 0;
 }
 
-int ora_num_threads(void) {
-#ifdef _OPENMP
-    return omp_get_max_threads();
-#else
-    return 1;
-#endif
-}
-void ora_set_threads(int n) {
-#ifdef _OPENMP
-    omp_set_num_threads(n);
-#else
-    (void)n;
-#endif
-}

@@ -76,6 +76,8 @@ def _load():
         "ora_tensor": ([ctypes.c_void_p, _u64p, _u64p, ctypes.c_int, _u64p], None),
         "ora_mac": ([ctypes.c_void_p, ctypes.POINTER(_u64p), ctypes.POINTER(_u64p), ctypes.c_int,
                      ctypes.c_int, _u64p], None),
+        "ora_set_threads": ([ctypes.c_int], None),
+        "ora_num_threads": ([], ctypes.c_int),
         "ora_bsgs_lt": ([ctypes.c_void_p, _u64p, ctypes.c_int, _i32p, ctypes.POINTER(_u64p), ctypes.c_int,
                          ctypes.c_int, _u64p, ctypes.POINTER(_u64p), ctypes.c_int, _u64p], ctypes.c_int),
     }
@@ -345,3 +347,8 @@ class Oracle:
         if rc != 0:
             raise KeyError("missing rotation key for the BSGS linear transform")
         return out
+
+
+def set_threads(n: int) -> None:
+    """Worker threads for the oracle's limb-parallel loops (default 1)."""
+    lib().ora_set_threads(int(n))
