@@ -304,6 +304,7 @@ def run_b200(args, dist):
     torch.cuda.synchronize()
     lib.Synchronize()
     clocks.start()
+    _capi.check(capi.helrm_ProfilerRange(1))
     _capi.check(capi.helrm_ProfileEnable(1))
     n0 = ctypes.c_uint64(0)
     _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n0)))
@@ -321,6 +322,7 @@ def run_b200(args, dist):
     ncls = ctypes.c_int(0)
     _capi.check(capi.helrm_ProfileRead(pms, pby, pwk, pl, K, ctypes.byref(ncls)))
     _capi.check(capi.helrm_ProfileEnable(0))
+    _capi.check(capi.helrm_ProfilerRange(0))
     clk = clocks.stop()
     torch.cuda.synchronize()
     dist.barrier()

@@ -26,7 +26,27 @@ struct PrimeConst {
     u64 onep;     // floor(2^64 / q) (Shoup companion of 1)
     u64 ninv;     // N^-1 mod q
     u64 ninvp;
+    u64 c30, c30p;  // 2^30 mod q (split-product recombination)
+    u64 c60, c60p;  // 2^60 mod q
 };
+
+// Split-30 products for residues below 2^40: a = ah*2^30 + al (al < 2^30,
+// ah < 2^10).  A sum of products is kept as S0 + S1*2^30 + S2*2^60 with
+// S0 = sum al*bl (< 2^60 per term, at most 16 terms), S1 = sum al*bh +
+// ah*bl (< 2^41 per term), S2 = sum ah*bh (< 2^20 per term); each term is
+// four 32x32 multiply-adds instead of a 64x64->128 product.
+#define HB_SPLIT_MASK 0x3FFFFFFFull
+struct Split3 {
+    u64 s0, s1;
+    unsigned s2;
+};
+__device__ __forceinline__ void split_mac(Split3 &acc, unsigned al, unsigned ah, unsigned bl, unsigned bh) {
+    acc.s0 += (u64)al * bl;
+    acc.s1 += (u64)al * bh;
+    acc.s1 += (u64)ah * bl;
+    acc.s2 += ah * bh;
+}
+__device__ __forceinline__ u64 split_pack(u64 v) { return ((v >> 30) << 32) | (v & HB_SPLIT_MASK); }
 
 __device__ __forceinline__ u64 add_mod(u64 a, u64 b, u64 q) {
     u64 s = a + b;
@@ -71,6 +91,12 @@ __device__ __forceinline__ u64 reduce128(const u128 &x, const PrimeConst &pc) {
 }
 __device__ __forceinline__ u64 mul_mod(u64 a, u64 b, const PrimeConst &pc) {
     return reduce128(__umul64hi(a, b), a * b, pc);
+}
+// (S0 + S1 2^30 + S2 2^60) mod q
+__device__ __forceinline__ u64 split_reduce(const Split3 &s, const PrimeConst &pc) {
+    u64 r = mul_shoup(s.s0, 1ull, pc.onep, pc.q);
+    r = add_mod(r, mul_shoup(s.s1, pc.c30, pc.c30p, pc.q), pc.q);
+    return add_mod(r, mul_shoup((u64)s.s2, pc.c60, pc.c60p, pc.q), pc.q);
 }
 
 // bit reversal of the low `bits` bits

@@ -1,0 +1,182 @@
+// hb_bsgs.cu -- the fused baby-step + diagonal-MAC kernel of the
+// double-hoisted BSGS linear transform (the embedding PCMM's hot loop).
+//
+// For one extended limb e and a tile of HB_BT coefficients, over every
+// ciphertext of the batch:
+//   phase A  R_b = baby rotation of the input, kept in the PQ basis:
+//              R_b.b = P*c0[tau_b] + sum_j D_j[tau_b] key_b[j].b,
+//              R_b.a = sum_j D_j[tau_b] key_b[j].a        (b = 0: R = P*c)
+//   phase B  inner[g] += pt(g, b) * R_b for every giant slot g of the chunk
+// The thread block keeps the evaluation-key tiles of its babies in shared
+// memory and each thread its plaintext values in registers, so keys and
+// diagonals stream from HBM once per batch while the ciphertext data
+// (digits D, c0, inner sums) streams once per ciphertext.  Residues below
+// 2^40 (the 36-bit q limbs) multiply with the split-30 form, four 32-bit
+// multiply-adds per product; the 60-bit special-prime limbs use 64x64->128
+// products.  Accumulation is lazy and reduced once per 16 terms.
+// Included by hb_kernels.cu (it reads the per-prime __constant__ table).
+#pragma once
+
+namespace hb {
+
+namespace {
+
+constexpr int kThreads = HB_GCH * HB_BT;  // 512: one warp per giant slot
+
+__device__ __forceinline__ void mac_split_packed(Split3 &s, u64 a_packed, u64 b_packed) {
+    split_mac(s, (unsigned)a_packed, (unsigned)(a_packed >> 32), (unsigned)b_packed, (unsigned)(b_packed >> 32));
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
+               int K, int L, int beta, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch,
+               size_t ct_stride, size_t d_stride, size_t inner_stride) {
+    extern __shared__ u64 sm[];
+    const int N = 1 << logN;
+    const int e = blockIdx.y;
+    const int n0 = blockIdx.x * HB_BT;
+    const int ne = nq + K;
+    const int p = e < nq ? e : L + (e - nq);
+    const PrimeConst pc = c_pc[p];
+    const bool fast = pc.q < (1ull << 40);
+    const int tid = threadIdx.x;
+    const int nb = ch.nbabies;
+
+    // shared memory: descriptors | key tiles [nb][beta][2][BT] | R [nb][2][BT]
+    BabyDesc *sdesc = reinterpret_cast<BabyDesc *>(sm);
+    u64 *skey = sm + (size_t)HB_BCH * (sizeof(BabyDesc) / 8);
+    u64 *sR = skey + (size_t)HB_BCH * beta * 2 * HB_BT;
+
+    for (int i = tid; i < nb * (int)(sizeof(BabyDesc) / 8); i += kThreads)
+        sm[i] = reinterpret_cast<const u64 *>(ch.babies)[i];
+    __syncthreads();
+    // key tiles (split form on fast limbs)
+    {
+        const int per = beta * 2 * HB_BT;
+        for (int i = tid; i < nb * per; i += kThreads) {
+            const int bb = i / per, r = i % per, jp = r / HB_BT, n = r % HB_BT;
+            const u64 *key = sdesc[bb].key;
+            u64 v = 0;
+            if (key) v = key[((size_t)jp * keyP + p) * N + n0 + n];
+            skey[i] = fast ? split_pack(v) : v;
+        }
+    }
+    // plaintexts of (giant slot gi, baby bb) at this thread's coefficient
+    const int gi = tid / HB_BT, nl = tid % HB_BT;
+    const bool gactive = gi < ch.gcount;
+    const size_t pt_off = ((size_t)(e < nq ? e : pt_nq + (e - nq)) << logN) + n0 + nl;
+    u64 ptv[HB_BCH];
+#pragma unroll
+    for (int bb = 0; bb < HB_BCH; bb++) {
+        u64 v = 0;
+        if (bb < nb && gactive) {
+            const u64 *pp = sdesc[bb].pt[gi];
+            if (pp) v = pp[pt_off];
+        }
+        ptv[bb] = fast ? split_pack(v) : v;
+    }
+    u64 pq_packed = 0, pq = 0;
+    if (e < nq) {
+        pq = pmod_q[e];
+        pq_packed = split_pack(pq);
+    }
+    __syncthreads();
+
+    const size_t nall = (size_t)ne << logN;
+    for (int b = 0; b < nbatch; b++) {
+        const u64 *c0 = ct + b * ct_stride;
+        const u64 *c1 = c0 + ((size_t)nq << logN);
+        const u64 *Db = D + b * d_stride;
+        // ---- phase A: baby rotations of this tile
+        for (int it = tid; it < nb * HB_BT; it += kThreads) {
+            const int bb = it / HB_BT, n = it % HB_BT;
+            const unsigned t = (unsigned)(n0 + n);
+            const BabyDesc &bd = sdesc[bb];
+            u64 rb, ra;
+            if (bd.key == nullptr) {
+                rb = e < nq ? mul_mod(pq, c0[((size_t)e << logN) + t], pc) : 0;
+                ra = e < nq ? mul_mod(pq, c1[((size_t)e << logN) + t], pc) : 0;
+            } else {
+                const unsigned src = aut_index(t, bd.galois, logN);
+                const u64 *kt = skey + (size_t)bb * beta * 2 * HB_BT + n;
+                if (fast) {
+                    Split3 sb = {0, 0, 0}, sa = {0, 0, 0};
+                    for (int j = 0; j < beta; j++) {
+                        const u64 d = split_pack(Db[((size_t)j * ne + e) * N + src]);
+                        mac_split_packed(sb, d, kt[(j * 2 + 0) * HB_BT]);
+                        mac_split_packed(sa, d, kt[(j * 2 + 1) * HB_BT]);
+                    }
+                    if (e < nq) mac_split_packed(sb, pq_packed, split_pack(c0[((size_t)e << logN) + src]));
+                    rb = split_reduce(sb, pc);
+                    ra = split_reduce(sa, pc);
+                } else {
+                    u128 sb = {0, 0}, sa = {0, 0};
+                    for (int j = 0; j < beta; j++) {
+                        const u64 d = Db[((size_t)j * ne + e) * N + src];
+                        mac128(sb, d, kt[(j * 2 + 0) * HB_BT]);
+                        mac128(sa, d, kt[(j * 2 + 1) * HB_BT]);
+                    }
+                    if (e < nq) mac128(sb, pq, c0[((size_t)e << logN) + src]);
+                    rb = reduce128(sb, pc);
+                    ra = reduce128(sa, pc);
+                }
+            }
+            sR[(bb * 2 + 0) * HB_BT + n] = fast ? split_pack(rb) : rb;
+            sR[(bb * 2 + 1) * HB_BT + n] = fast ? split_pack(ra) : ra;
+        }
+        __syncthreads();
+        // ---- phase B: inner[g] += pt(g, b) * R_b
+        if (gactive) {
+            u64 vb, va;
+            if (fast) {
+                Split3 ab = {0, 0, 0}, aa = {0, 0, 0};
+                u64 tb = 0, ta = 0;
+#pragma unroll
+                for (int bb = 0; bb < HB_BCH; bb++) {
+                    if (bb < nb) {
+                        mac_split_packed(ab, ptv[bb], sR[(bb * 2 + 0) * HB_BT + nl]);
+                        mac_split_packed(aa, ptv[bb], sR[(bb * 2 + 1) * HB_BT + nl]);
+                        if ((bb & 15) == 15) {
+                            tb = add_mod(tb, split_reduce(ab, pc), pc.q);
+                            ta = add_mod(ta, split_reduce(aa, pc), pc.q);
+                            ab = {0, 0, 0};
+                            aa = {0, 0, 0};
+                        }
+                    }
+                }
+                vb = add_mod(tb, split_reduce(ab, pc), pc.q);
+                va = add_mod(ta, split_reduce(aa, pc), pc.q);
+            } else {
+                u128 ab = {0, 0}, aa = {0, 0};
+                u64 tb = 0, ta = 0;
+#pragma unroll
+                for (int bb = 0; bb < HB_BCH; bb++) {
+                    if (bb < nb) {
+                        mac128(ab, ptv[bb], sR[(bb * 2 + 0) * HB_BT + nl]);
+                        mac128(aa, ptv[bb], sR[(bb * 2 + 1) * HB_BT + nl]);
+                        if ((bb & 15) == 15) {
+                            tb = add_mod(tb, reduce128(ab, pc), pc.q);
+                            ta = add_mod(ta, reduce128(aa, pc), pc.q);
+                            ab = {0, 0};
+                            aa = {0, 0};
+                        }
+                    }
+                }
+                vb = add_mod(tb, reduce128(ab, pc), pc.q);
+                va = add_mod(ta, reduce128(aa, pc), pc.q);
+            }
+            u64 *o = inner + b * inner_stride + (size_t)(ch.gbase + gi) * 2 * nall + ((size_t)e << logN) + n0 + nl;
+            if (ch.accumulate) {
+                vb = add_mod(vb, o[0], pc.q);
+                va = add_mod(va, o[nall], pc.q);
+            }
+            o[0] = vb;
+            o[nall] = va;
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace hb

@@ -7,6 +7,7 @@
 // (orion/backend/cheddar/ext/cheddar_pybind.cu:73-236).  All device work
 // goes to one non-blocking stream; memory comes from CUDA's stream-ordered
 // pool (cudaMallocAsync), which keeps freed blocks cached for reuse.
+#include <cuda_profiler_api.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -204,6 +205,10 @@ public:
             c.onep = (u64)(((hu128)1 << 64) / q);
             c.ninv = h_invm((u64)N, q);
             c.ninvp = h_shoup(c.ninv, q);
+            c.c30 = (1ull << 30) % q;
+            c.c30p = h_shoup(c.c30, q);
+            c.c60 = (1ull << 60) % q;
+            c.c60p = h_shoup(c.c60, q);
             pcs[p] = c;
         }
         upload_prime_consts(pcs.data(), P);
@@ -951,26 +956,33 @@ public:
                     it->second.pt[gi] = t.pts[bk.second].d;
                 }
             }
-            std::vector<BabyDesc> host;
-            for (auto &kv : babies) host.push_back(kv.second);
-            BabyDesc *dev = (BabyDesc *)alloc(host.size() * sizeof(BabyDesc) / 8 + 1);
-            cuda_check(cudaMemcpyAsync(dev, host.data(), host.size() * sizeof(BabyDesc), cudaMemcpyHostToDevice,
-                                       stream),
-                       "plan");
-            t.plan_dev.push_back(dev);
-            BsgsChunk ch;
-            ch.babies = dev;
-            ch.nbabies = (int)host.size();
-            ch.gbase = s0;
-            ch.gcount = cnt;
-            ch.nkeys = 0;
-            ch.npts = 0;
-            for (auto &bd : host) {
-                ch.nkeys += bd.key != nullptr;
-                for (int gi = 0; gi < HB_GCH; gi++) ch.npts += bd.pt[gi] != nullptr;
+            std::vector<BabyDesc> all;
+            for (auto &kv : babies) all.push_back(kv.second);
+            // babies in groups of HB_BCH; later groups accumulate into the
+            // inner sums the first group wrote
+            for (size_t b0 = 0; b0 < all.size(); b0 += HB_BCH) {
+                std::vector<BabyDesc> host(all.begin() + b0,
+                                           all.begin() + std::min(all.size(), b0 + (size_t)HB_BCH));
+                BabyDesc *dev = (BabyDesc *)alloc(host.size() * sizeof(BabyDesc) / 8 + 1);
+                cuda_check(cudaMemcpyAsync(dev, host.data(), host.size() * sizeof(BabyDesc),
+                                           cudaMemcpyHostToDevice, stream),
+                           "plan");
+                t.plan_dev.push_back(dev);
+                BsgsChunk ch;
+                ch.babies = dev;
+                ch.nbabies = (int)host.size();
+                ch.gbase = s0;
+                ch.gcount = cnt;
+                ch.nkeys = 0;
+                ch.npts = 0;
+                ch.accumulate = b0 > 0;
+                for (auto &bd : host) {
+                    ch.nkeys += bd.key != nullptr;
+                    for (int gi = 0; gi < HB_GCH; gi++) ch.npts += bd.pt[gi] != nullptr;
+                }
+                t.plan_chunks.push_back(ch);
+                sync();
             }
-            t.plan_chunks.push_back(ch);
-            sync();
         }
         // giant keys
         for (int g : t.giant_of_slot)
@@ -1897,6 +1909,12 @@ HB_API int helrm_KernelClassName(int cls, char *out, int cap) {
     return guard([&] {
         if (!out || cap <= 0) HB_THROW(HB_EINVAL, "KernelClassName: bad buffer");
         std::snprintf(out, (size_t)cap, "%s", kclass_name(cls));
+    });
+}
+HB_API int helrm_ProfilerRange(int on) {
+    return guard([&] {
+        C().sync();
+        cuda_check(on ? cudaProfilerStart() : cudaProfilerStop(), "profiler range");
     });
 }
 HB_API int helrm_GetLaunchCount(uint64_t *n) {

@@ -16,6 +16,11 @@
 namespace hb {
 
 __constant__ PrimeConst c_pc[HB_MAX_PRIMES];
+}  // namespace hb
+
+#include "hb_bsgs.cuh"
+
+namespace hb {
 
 static void check_launch(const char *what) {
     cudaError_t e = cudaGetLastError();
@@ -121,6 +126,35 @@ static inline unsigned grid1d(size_t work, int block) {
 // =====================================================================
 static inline int split_log1(int logN) { return logN / 2; }
 
+// Radix-4 rounds: a thread owns the four elements {j, j+t/2, j+t, j+3t/2}
+// of a group of 2t and applies two consecutive stages to them in registers
+// (one shared-memory round trip per two stages).  Forward butterflies are
+// Harvey's lazy form with values in [0, 4q); the inverse keeps [0, 2q); the
+// store reduces fully.
+__device__ __forceinline__ void ct_bfly(u64 &x, u64 &y, u64 w, u64 wp, u64 q) {
+    const u64 two_q = 2 * q;
+    if (x >= two_q) x -= two_q;
+    const u64 t = mul_shoup_lazy(y, w, wp, q);
+    y = x + two_q - t;
+    x = x + t;
+}
+__device__ __forceinline__ void gs_bfly(u64 &x, u64 &y, u64 w, u64 wp, u64 q) {
+    const u64 two_q = 2 * q;
+    u64 s = x + y;
+    if (s >= two_q) s -= two_q;
+    const u64 d = x + two_q - y;
+    x = s;
+    y = mul_shoup_lazy(d, w, wp, q);
+}
+__device__ __forceinline__ u64 reduce4q(u64 x, u64 q) {
+    if (x >= 2 * q) x -= 2 * q;
+    if (x >= q) x -= q;
+    return x;
+}
+
+// Stage s of an n-point transform on a shared-memory tile addressed by
+// idx(k): forward stage with m groups pairs k and k + n/(2m); twiddle of
+// group i is tw[wbase(m) + i].
 template <bool INV>
 __global__ void __launch_bounds__(256) k_ntt_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
                                                    const u64 *__restrict__ twp, int logN, int logN1, int logC,
@@ -135,48 +169,95 @@ __global__ void __launch_bounds__(256) k_ntt_cols(u64 *__restrict__ data, RowMap
     u64 *a = data + (size_t)row * N;
     const u64 *W = tw + (size_t)p * N, *Wp = twp + (size_t)p * N;
     for (int idx = threadIdx.x; idx < (N1 << logC); idx += blockDim.x) {
-        int k = idx >> logC, c = idx & (C - 1);
-        sm[idx] = a[(size_t)k * N2 + c0 + c];
+        int kk = idx >> logC, c = idx & (C - 1);
+        sm[idx] = a[(size_t)kk * N2 + c0 + c];
     }
     __syncthreads();
-    const int nbf = (N1 >> 1) << logC;
+#define SMC(kk) sm[((kk) << logC) + c]
     if (!INV) {
-        for (int m = 1, lt = logN1 - 1; m < N1; m <<= 1, lt--) {
-            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
-                int c = bf & (C - 1), j = bf >> logC;
-                int i = j >> lt, jj = j & ((1 << lt) - 1);
-                int k1 = (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
-                u64 w = __ldg(W + m + i), wp = __ldg(Wp + m + i);
-                u64 U = sm[(k1 << logC) + c];
-                u64 V = mul_shoup(sm[(k2 << logC) + c], w, wp, q);
-                sm[(k1 << logC) + c] = add_mod(U, V, q);
-                sm[(k2 << logC) + c] = sub_mod(U, V, q);
+        int lt = logN1 - 1;  // log2 of the half distance t at the current stage
+        int m = 1;
+        for (; lt >= 1; lt -= 2, m <<= 2) {
+            const int nq4 = (N1 >> 2) << logC;
+            for (int u = threadIdx.x; u < nq4; u += blockDim.x) {
+                const int c = u & (C - 1), j = u >> logC;
+                const int t = 1 << lt, h = t >> 1;
+                const int i = j >> (lt - 1), jj = j & (h - 1);
+                const int k0 = (i << (lt + 1)) + jj;
+                u64 x0 = SMC(k0), x1 = SMC(k0 + h), x2 = SMC(k0 + t), x3 = SMC(k0 + t + h);
+                const u64 w1 = __ldg(W + m + i), w1p = __ldg(Wp + m + i);
+                ct_bfly(x0, x2, w1, w1p, q);
+                ct_bfly(x1, x3, w1, w1p, q);
+                const u64 w2 = __ldg(W + 2 * m + 2 * i), w2p = __ldg(Wp + 2 * m + 2 * i);
+                const u64 w3 = __ldg(W + 2 * m + 2 * i + 1), w3p = __ldg(Wp + 2 * m + 2 * i + 1);
+                ct_bfly(x0, x1, w2, w2p, q);
+                ct_bfly(x2, x3, w3, w3p, q);
+                SMC(k0) = x0;
+                SMC(k0 + h) = x1;
+                SMC(k0 + t) = x2;
+                SMC(k0 + t + h) = x3;
+            }
+            __syncthreads();
+        }
+        if (lt == 0) {  // odd number of stages: one radix-2 round
+            const int nb2 = (N1 >> 1) << logC;
+            for (int u = threadIdx.x; u < nb2; u += blockDim.x) {
+                const int c = u & (C - 1), i = u >> logC;
+                u64 x0 = SMC(2 * i), x1 = SMC(2 * i + 1);
+                ct_bfly(x0, x1, __ldg(W + m + i), __ldg(Wp + m + i), q);
+                SMC(2 * i) = x0;
+                SMC(2 * i + 1) = x1;
             }
             __syncthreads();
         }
         for (int idx = threadIdx.x; idx < (N1 << logC); idx += blockDim.x) {
-            int k = idx >> logC, c = idx & (C - 1);
-            a[(size_t)k * N2 + c0 + c] = sm[idx];
+            int kk = idx >> logC, c = idx & (C - 1);
+            a[(size_t)kk * N2 + c0 + c] = reduce4q(sm[idx], q);
         }
     } else {
-        for (int h = N1 >> 1, lt = 0; h >= 1; h >>= 1, lt++) {
-            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
-                int c = bf & (C - 1), j = bf >> logC;
-                int i = j >> lt, jj = j & ((1 << lt) - 1);
-                int k1 = (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
-                u64 w = __ldg(W + h + i), wp = __ldg(Wp + h + i);
-                u64 U = sm[(k1 << logC) + c], V = sm[(k2 << logC) + c];
-                sm[(k1 << logC) + c] = add_mod(U, V, q);
-                sm[(k2 << logC) + c] = mul_shoup(sub_mod(U, V, q), w, wp, q);
+        int lt = 0;
+        int h = N1 >> 1;  // groups at the current stage
+        if (logN1 & 1) {  // odd: one radix-2 round first (t = 1)
+            const int nb2 = (N1 >> 1) << logC;
+            for (int u = threadIdx.x; u < nb2; u += blockDim.x) {
+                const int c = u & (C - 1), i = u >> logC;
+                u64 x0 = SMC(2 * i), x1 = SMC(2 * i + 1);
+                gs_bfly(x0, x1, __ldg(W + h + i), __ldg(Wp + h + i), q);
+                SMC(2 * i) = x0;
+                SMC(2 * i + 1) = x1;
+            }
+            __syncthreads();
+            lt = 1;
+            h >>= 1;
+        }
+        for (; lt < logN1; lt += 2, h >>= 2) {
+            const int nq4 = (N1 >> 2) << logC;
+            for (int u = threadIdx.x; u < nq4; u += blockDim.x) {
+                const int c = u & (C - 1), j = u >> logC;
+                const int t = 1 << lt;  // first stage half distance
+                const int i2 = j >> lt, jj = j & (t - 1);  // group of the second stage (distance 2t)
+                const int k0 = (i2 << (lt + 2)) + jj;
+                u64 x0 = SMC(k0), x1 = SMC(k0 + t), x2 = SMC(k0 + 2 * t), x3 = SMC(k0 + 3 * t);
+                const int i1 = 2 * i2;  // groups of the first stage: i1, i1+1
+                gs_bfly(x0, x1, __ldg(W + h + i1), __ldg(Wp + h + i1), q);
+                gs_bfly(x2, x3, __ldg(W + h + i1 + 1), __ldg(Wp + h + i1 + 1), q);
+                const int hh = h >> 1;
+                gs_bfly(x0, x2, __ldg(W + hh + i2), __ldg(Wp + hh + i2), q);
+                gs_bfly(x1, x3, __ldg(W + hh + i2), __ldg(Wp + hh + i2), q);
+                SMC(k0) = x0;
+                SMC(k0 + t) = x1;
+                SMC(k0 + 2 * t) = x2;
+                SMC(k0 + 3 * t) = x3;
             }
             __syncthreads();
         }
         const u64 ni = c_pc[p].ninv, nip = c_pc[p].ninvp;
         for (int idx = threadIdx.x; idx < (N1 << logC); idx += blockDim.x) {
-            int k = idx >> logC, c = idx & (C - 1);
-            a[(size_t)k * N2 + c0 + c] = mul_shoup(sm[idx], ni, nip, q);
+            int kk = idx >> logC, c = idx & (C - 1);
+            a[(size_t)kk * N2 + c0 + c] = mul_shoup(sm[idx], ni, nip, q);
         }
     }
+#undef SMC
 }
 
 template <bool INV>
@@ -199,42 +280,96 @@ __global__ void __launch_bounds__(256) k_ntt_rows(u64 *__restrict__ data, RowMap
         for (int idx = threadIdx.x; idx < (tile >> 1); idx += blockDim.x) dst[idx] = src[idx];
     }
     __syncthreads();
-    const int nbf = (N2 >> 1) << logRB;
-    const int halfmask = (N2 >> 1) - 1;
+    const int nq4 = (N2 >> 2) << logRB;
     if (!INV) {
-        for (int mp = 1, lt = logN2 - 1; mp < N2; mp <<= 1, lt--) {
-            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
-                int blk = bf >> (logN2 - 1), j = bf & halfmask;
-                int i = j >> lt, jj = j & ((1 << lt) - 1);
-                int k1 = (blk << logN2) + (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
-                int widx = mp * (N1 + rb0 + blk) + i;
-                u64 w = __ldg(W + widx), wp = __ldg(Wp + widx);
-                u64 U = sm[k1];
-                u64 V = mul_shoup(sm[k2], w, wp, q);
-                sm[k1] = add_mod(U, V, q);
-                sm[k2] = sub_mod(U, V, q);
+        // forward stage with mp groups per block: twiddle of (block rb, group i) at mp*(N1 + rb) + i
+        int lt = logN2 - 1, mp = 1;
+        for (; lt >= 1; lt -= 2, mp <<= 2) {
+            for (int u = threadIdx.x; u < nq4; u += blockDim.x) {
+                const int blk = u >> (logN2 - 2), j = u & ((N2 >> 2) - 1);
+                const int t = 1 << lt, h = t >> 1;
+                const int i = j >> (lt - 1), jj = j & (h - 1);
+                const int k0 = (blk << logN2) + (i << (lt + 1)) + jj;
+                const int rb = rb0 + blk;
+                u64 x0 = sm[k0], x1 = sm[k0 + h], x2 = sm[k0 + t], x3 = sm[k0 + t + h];
+                const int w1i = mp * (N1 + rb) + i;
+                ct_bfly(x0, x2, __ldg(W + w1i), __ldg(Wp + w1i), q);
+                ct_bfly(x1, x3, __ldg(W + w1i), __ldg(Wp + w1i), q);
+                const int w2i = 2 * mp * (N1 + rb) + 2 * i;
+                ct_bfly(x0, x1, __ldg(W + w2i), __ldg(Wp + w2i), q);
+                ct_bfly(x2, x3, __ldg(W + w2i + 1), __ldg(Wp + w2i + 1), q);
+                sm[k0] = x0;
+                sm[k0 + h] = x1;
+                sm[k0 + t] = x2;
+                sm[k0 + t + h] = x3;
+            }
+            __syncthreads();
+        }
+        if (lt == 0) {
+            const int nb2 = (N2 >> 1) << logRB;
+            for (int u = threadIdx.x; u < nb2; u += blockDim.x) {
+                const int blk = u >> (logN2 - 1), i = u & ((N2 >> 1) - 1);
+                const int k0 = (blk << logN2) + 2 * i;
+                const int wi = mp * (N1 + rb0 + blk) + i;
+                u64 x0 = sm[k0], x1 = sm[k0 + 1];
+                ct_bfly(x0, x1, __ldg(W + wi), __ldg(Wp + wi), q);
+                sm[k0] = x0;
+                sm[k0 + 1] = x1;
             }
             __syncthreads();
         }
     } else {
-        for (int hp = N2 >> 1, lt = 0; hp >= 1; hp >>= 1, lt++) {
-            for (int bf = threadIdx.x; bf < nbf; bf += blockDim.x) {
-                int blk = bf >> (logN2 - 1), j = bf & halfmask;
-                int i = j >> lt, jj = j & ((1 << lt) - 1);
-                int k1 = (blk << logN2) + (i << (lt + 1)) + jj, k2 = k1 + (1 << lt);
-                int widx = hp * (N1 + rb0 + blk) + i;
-                u64 w = __ldg(W + widx), wp = __ldg(Wp + widx);
-                u64 U = sm[k1], V = sm[k2];
-                sm[k1] = add_mod(U, V, q);
-                sm[k2] = mul_shoup(sub_mod(U, V, q), w, wp, q);
+        int lt = 0, hp = N2 >> 1;
+        if (logN2 & 1) {
+            const int nb2 = (N2 >> 1) << logRB;
+            for (int u = threadIdx.x; u < nb2; u += blockDim.x) {
+                const int blk = u >> (logN2 - 1), i = u & ((N2 >> 1) - 1);
+                const int k0 = (blk << logN2) + 2 * i;
+                const int wi = hp * (N1 + rb0 + blk) + i;
+                u64 x0 = sm[k0], x1 = sm[k0 + 1];
+                gs_bfly(x0, x1, __ldg(W + wi), __ldg(Wp + wi), q);
+                sm[k0] = x0;
+                sm[k0 + 1] = x1;
+            }
+            __syncthreads();
+            lt = 1;
+            hp >>= 1;
+        }
+        for (; lt < logN2; lt += 2, hp >>= 2) {
+            for (int u = threadIdx.x; u < nq4; u += blockDim.x) {
+                const int blk = u >> (logN2 - 2), j = u & ((N2 >> 2) - 1);
+                const int t = 1 << lt;
+                const int i2 = j >> lt, jj = j & (t - 1);
+                const int k0 = (blk << logN2) + (i2 << (lt + 2)) + jj;
+                const int rb = rb0 + blk;
+                u64 x0 = sm[k0], x1 = sm[k0 + t], x2 = sm[k0 + 2 * t], x3 = sm[k0 + 3 * t];
+                const int i1 = 2 * i2;
+                const int wa = hp * (N1 + rb) + i1;
+                gs_bfly(x0, x1, __ldg(W + wa), __ldg(Wp + wa), q);
+                gs_bfly(x2, x3, __ldg(W + wa + 1), __ldg(Wp + wa + 1), q);
+                const int wb = (hp >> 1) * (N1 + rb) + i2;
+                gs_bfly(x0, x2, __ldg(W + wb), __ldg(Wp + wb), q);
+                gs_bfly(x1, x3, __ldg(W + wb), __ldg(Wp + wb), q);
+                sm[k0] = x0;
+                sm[k0 + t] = x1;
+                sm[k0 + 2 * t] = x2;
+                sm[k0 + 3 * t] = x3;
             }
             __syncthreads();
         }
+        // the column pass reduces fully; values here stay in [0, 2q)
     }
     {
         const ulonglong2 *src = reinterpret_cast<const ulonglong2 *>(sm);
         ulonglong2 *dst = reinterpret_cast<ulonglong2 *>(a);
-        for (int idx = threadIdx.x; idx < (tile >> 1); idx += blockDim.x) dst[idx] = src[idx];
+        for (int idx = threadIdx.x; idx < (tile >> 1); idx += blockDim.x) {
+            ulonglong2 v = src[idx];
+            if (!INV) {  // forward output fully reduced
+                v.x = reduce4q(v.x, q);
+                v.y = reduce4q(v.y, q);
+            }
+            dst[idx] = v;
+        }
     }
 }
 
@@ -822,94 +957,31 @@ void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, 
 }
 
 // =====================================================================
-// fused baby steps + diagonal MAC (double hoisting)
+// fused baby steps + diagonal MAC (double hoisting): see hb_bsgs.cuh
 // =====================================================================
-__global__ void __launch_bounds__(256) k_bsgs_baby_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct,
-                                                       const u64 *__restrict__ D, BsgsChunk ch, int nq, int K, int L,
-                                                       int beta, int keyP, int pt_nq, const u64 *__restrict__ pmod_q,
-                                                       int logN, size_t ct_stride, size_t d_stride,
-                                                       size_t inner_stride) {
-    extern __shared__ BabyDesc sdesc[];
-    for (int i = threadIdx.x; i < ch.nbabies * (int)(sizeof(BabyDesc) / 8); i += blockDim.x)
-        reinterpret_cast<u64 *>(sdesc)[i] = reinterpret_cast<const u64 *>(ch.babies)[i];
-    __syncthreads();
-    const int N = 1 << logN;
-    const int ne = nq + K;
-    const size_t n_all = (size_t)ne << logN;
-    const int b = blockIdx.y;
-    const u64 *c0 = ct + b * ct_stride;
-    const u64 *c1 = c0 + ((size_t)nq << logN);
-    const u64 *Db = D + b * d_stride;
-    u64 *Ib = inner + b * inner_stride;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_all; i += (size_t)gridDim.x * blockDim.x) {
-        const int e = (int)(i >> logN);
-        const unsigned t = (unsigned)(i & (N - 1));
-        const int p = e < nq ? e : L + (e - nq);
-        const PrimeConst &pc = c_pc[p];
-        const size_t pt_off = ((size_t)(e < nq ? e : pt_nq + (e - nq)) << logN) + t;
-        u64 acc[HB_GCH][2];
-#pragma unroll
-        for (int gi = 0; gi < HB_GCH; gi++) acc[gi][0] = acc[gi][1] = 0;
-        for (int bi = 0; bi < ch.nbabies; bi++) {
-            const BabyDesc &bd = sdesc[bi];
-            u64 rb, ra;
-            if (bd.key == nullptr) {
-                rb = e < nq ? mul_mod(pmod_q[e], c0[((size_t)e << logN) + t], pc) : 0;
-                ra = e < nq ? mul_mod(pmod_q[e], c1[((size_t)e << logN) + t], pc) : 0;
-            } else {
-                const unsigned src = aut_index(t, bd.galois, logN);
-                u128 sb = {0, 0}, sa = {0, 0};
-                for (int j = 0; j < beta; j++) {
-                    const u64 d = Db[((size_t)j * ne + e) * N + src];
-                    mac128(sb, d, bd.key[(((size_t)j * 2 + 0) * keyP + p) * N + t]);
-                    mac128(sa, d, bd.key[(((size_t)j * 2 + 1) * keyP + p) * N + t]);
-                }
-                if (e < nq) mac128(sb, pmod_q[e], c0[((size_t)e << logN) + src]);
-                rb = reduce128(sb, pc);
-                ra = reduce128(sa, pc);
-            }
-#pragma unroll
-            for (int gi = 0; gi < HB_GCH; gi++) {
-                if (gi < ch.gcount && bd.pt[gi] != nullptr) {
-                    const u64 pv = bd.pt[gi][pt_off];
-                    acc[gi][0] = add_mod(acc[gi][0], mul_mod(pv, rb, pc), pc.q);
-                    acc[gi][1] = add_mod(acc[gi][1], mul_mod(pv, ra, pc), pc.q);
-                }
-            }
-        }
-#pragma unroll
-        for (int gi = 0; gi < HB_GCH; gi++) {
-            if (gi < ch.gcount) {
-                u64 *o = Ib + (size_t)(ch.gbase + gi) * 2 * n_all;
-                o[i] = acc[gi][0];
-                o[n_all + i] = acc[gi][1];
-            }
-        }
-    }
-}
-
 void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, int nq, int K, int L, int beta,
                    int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride, size_t d_stride,
                    size_t inner_stride, cudaStream_t s) {
-    size_t n = (size_t)(nq + K) << logN;
-    unsigned g = grid1d(n, 256);
-    if (g > 2048) g = 2048;
-    size_t smem = sizeof(BabyDesc) * (size_t)ch.nbabies;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_bsgs_baby_mac, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        attr = true;
+    if (ch.nbabies > HB_BCH || ch.gcount > HB_GCH) throw std::invalid_argument("bsgs chunk too large");
+    const size_t smem = HB_BCH * sizeof(BabyDesc) + (size_t)HB_BCH * beta * 2 * HB_BT * 8 + (size_t)HB_BCH * 2 * HB_BT * 8;
+    if (smem > 227 * 1024) throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaFuncSetAttribute(k_bsgs_mac, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
     }
+    const size_t n = (size_t)(nq + K) << logN;
     // per ciphertext: c0/c1 rows, the digits, the inner sums written; per
     // launch: every baby key and plaintext of the chunk once
     const double nd = (double)n, nqw = (double)nq * (1 << logN);
     ProfScope ps(KC_BSGS_MAC,
-                 8.0 * (nbatch * (2.0 * nqw + beta * nd + 2.0 * ch.gcount * nd) + 2.0 * beta * ch.nkeys * nd +
-                        ch.npts * nd),
+                 8.0 * (nbatch * (2.0 * nqw + beta * nd + 2.0 * ch.gcount * nd * (ch.accumulate ? 2 : 1)) +
+                        2.0 * beta * ch.nkeys * nd + ch.npts * nd),
                  (double)nbatch * nd * (2.0 * beta * ch.nkeys + 2.0 * ch.npts), s, 1);
-    k_bsgs_baby_mac<<<dim3(g, nbatch), 256, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN,
-                                                       ct_stride, d_stride, inner_stride);
-    check_launch("bsgs_baby_mac");
+    dim3 grid((1u << logN) / HB_BT, nq + K);
+    k_bsgs_mac<<<grid, HB_GCH * HB_BT, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN, nbatch,
+                                                  ct_stride, d_stride, inner_stride);
+    check_launch("bsgs_mac");
 }
 
 void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s) {

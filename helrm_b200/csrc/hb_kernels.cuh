@@ -167,7 +167,9 @@ void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, 
              size_t add_stride, cudaStream_t s);
 
 // ---- fused double-hoisted baby steps + plaintext MAC --------------------------
-#define HB_GCH 16
+#define HB_GCH 16   // giant slots per chunk (one warp each)
+#define HB_BCH 32   // babies per chunk (plaintexts held in registers)
+#define HB_BT 32    // coefficients per thread block tile
 struct BabyDesc {
     u64 galois;        // 1 for the identity baby (b = 0)
     const u64 *key;    // null for b = 0
@@ -180,6 +182,7 @@ struct BsgsChunk {
     int gcount;              // giant slots in this chunk (<= HB_GCH)
     int nkeys;               // babies with a key (b != 0), for accounting
     int npts;                // plaintexts referenced by the chunk, for accounting
+    int accumulate;          // add into inner (later baby chunks of the same giant slots)
 };
 // inner[g][pl][e][n] for g in [gbase, gbase+gcount): sum over babies of
 // pt(g, b) * R_b, R_b = baby rotation of the input kept in the PQ basis:

@@ -218,6 +218,9 @@ int helrm_TimerStop(double *ms);
 int helrm_ProfileEnable(int on);
 int helrm_ProfileRead(double *ms, double *bytes, double *work, uint64_t *launches, int cap, int *nclasses);
 int helrm_KernelClassName(int cls, char *out, int cap);
+/* cudaProfilerStart / cudaProfilerStop around a region (for an external
+ * profiler started with profiling off) */
+int helrm_ProfilerRange(int on);
 /* number of kernels this library has launched since it was loaded */
 int helrm_GetLaunchCount(uint64_t *n);
 
