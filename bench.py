@@ -48,7 +48,13 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-threads", type=int, default=0, help="oracle threads (0 = all host cores)")
-    return ap.parse_args()
+    ap.add_argument("--small", action="store_true",
+                    help="profiling case: same 512-diagonal PCMM on 6 q limbs + 2 special primes (dnum 3), "
+                         "so an ncu capture keeps a few GB on the device")
+    args = ap.parse_args()
+    if args.small:
+        args.level = min(args.level, 5)
+    return args
 
 
 # --------------------------------------------------------------------------- distributed plumbing
@@ -240,12 +246,16 @@ def run_reference(args, dist):
 
 
 def cfg_dict(args, batch):
-    return {"workload": "cfg2: 26-table block-diagonal embedding PCMM (BASELINE configs[1])",
-            "logN": 16, "slots": 32768, "q_limbs": 24, "q_bits": 36, "special_primes": 4, "p_bits": 60,
-            "dnum": 4, "pcmm_level": args.level, "matrix": "416x4224 block-diagonal", "diagonals": 512,
-            "bs": 32, "giant_groups": 16, "fold_rotations": 6, "batch_ciphertexts": batch,
-            "queries_per_ciphertext": 1, "parallelism": f"dp{args.gpus} (query batch)",
-            "l2": "inputs larger than L2 (1.5 GiB ciphertexts, 7 GiB diagonals, 5.7 GiB keys per step)"}
+    d = {"workload": "cfg2: 26-table block-diagonal embedding PCMM (BASELINE configs[1])",
+         "logN": 16, "slots": 32768, "q_limbs": 24, "q_bits": 36, "special_primes": 4, "p_bits": 60,
+         "dnum": 4, "pcmm_level": args.level, "matrix": "416x4224 block-diagonal", "diagonals": 512,
+         "bs": 32, "giant_groups": 16, "fold_rotations": 6, "batch_ciphertexts": batch,
+         "queries_per_ciphertext": 1, "parallelism": f"dp{args.gpus} (query batch)",
+         "l2": "inputs larger than L2 (1.5 GiB ciphertexts, 7 GiB diagonals, 5.7 GiB keys per step)"}
+    if getattr(args, "small", False):
+        d.update({"workload": "profiling case (NOT the headline): cfg2 PCMM on 6 q limbs + 2 special primes",
+                  "q_limbs": 6, "special_primes": 2, "dnum": 3})
+    return d
 
 
 # --------------------------------------------------------------------------- B200 arm
@@ -255,10 +265,15 @@ def run_b200(args, dist):
     from helrm_b200 import B200Library, _capi
     from helrm_b200.params import CFG2, CFG2_DNUM
 
+    from helrm_b200 import CKKSConfig
     dev = dist.local
     torch.cuda.set_device(dev)
-    lib = B200Library(dnum=CFG2_DNUM, seed=1000 + dist.rank, device=dev)
-    lib.setup_bindings(CFG2)
+    if args.small:
+        cfg, dnum = CKKSConfig(logn=16, logq=[36] * 6, logp=[60] * 2, logscale=36, h=192), 3
+    else:
+        cfg, dnum = CFG2, CFG2_DNUM
+    lib = B200Library(dnum=dnum, seed=1000 + dist.rank, device=dev)
+    lib.setup_bindings(cfg)
     lib.GenerateSecretKey()
     M, ks, diags, rot, xs = build_workload(args.batch, seed=100 + dist.rank)
     info = lib.scheme_info()

@@ -21,7 +21,7 @@ namespace hb {
 
 namespace {
 
-constexpr int kThreads = HB_GCH * HB_BT;  // 512: one warp per giant slot
+constexpr int kThreads = HB_GCH * HB_BT;  // 256: half a warp per giant slot
 
 __device__ __forceinline__ void mac_split_packed(Split3 &s, u64 a_packed, u64 b_packed) {
     split_mac(s, (unsigned)a_packed, (unsigned)(a_packed >> 32), (unsigned)b_packed, (unsigned)(b_packed >> 32));
@@ -29,7 +29,7 @@ __device__ __forceinline__ void mac_split_packed(Split3 &s, u64 a_packed, u64 b_
 
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
                int K, int L, int beta, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch,
                size_t ct_stride, size_t d_stride, size_t inner_stride) {
@@ -89,7 +89,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const u64 *c0 = ct + b * ct_stride;
         const u64 *c1 = c0 + ((size_t)nq << logN);
         const u64 *Db = D + b * d_stride;
-        // ---- phase A: baby rotations of this tile
+        // ---- phase A: baby rotations of this tile.  The gathers of an item
+        // (beta digits at the rotated index, and c0) are all issued before
+        // any of them is used, so their latencies overlap.
         for (int it = tid; it < nb * HB_BT; it += kThreads) {
             const int bb = it / HB_BT, n = it % HB_BT;
             const unsigned t = (unsigned)(n0 + n);
@@ -101,24 +103,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 const unsigned src = aut_index(t, bd.galois, logN);
                 const u64 *kt = skey + (size_t)bb * beta * 2 * HB_BT + n;
+                u64 dv[HB_MAX_BETA];
+#pragma unroll
+                for (int j = 0; j < HB_MAX_BETA; j++)
+                    if (j < beta) dv[j] = Db[((size_t)j * ne + e) * N + src];
+                const u64 cv = e < nq ? c0[((size_t)e << logN) + src] : 0;
                 if (fast) {
                     Split3 sb = {0, 0, 0}, sa = {0, 0, 0};
-                    for (int j = 0; j < beta; j++) {
-                        const u64 d = split_pack(Db[((size_t)j * ne + e) * N + src]);
-                        mac_split_packed(sb, d, kt[(j * 2 + 0) * HB_BT]);
-                        mac_split_packed(sa, d, kt[(j * 2 + 1) * HB_BT]);
-                    }
-                    if (e < nq) mac_split_packed(sb, pq_packed, split_pack(c0[((size_t)e << logN) + src]));
+#pragma unroll
+                    for (int j = 0; j < HB_MAX_BETA; j++)
+                        if (j < beta) {
+                            const u64 d = split_pack(dv[j]);
+                            mac_split_packed(sb, d, kt[(j * 2 + 0) * HB_BT]);
+                            mac_split_packed(sa, d, kt[(j * 2 + 1) * HB_BT]);
+                        }
+                    if (e < nq) mac_split_packed(sb, pq_packed, split_pack(cv));
                     rb = split_reduce(sb, pc);
                     ra = split_reduce(sa, pc);
                 } else {
                     u128 sb = {0, 0}, sa = {0, 0};
-                    for (int j = 0; j < beta; j++) {
-                        const u64 d = Db[((size_t)j * ne + e) * N + src];
-                        mac128(sb, d, kt[(j * 2 + 0) * HB_BT]);
-                        mac128(sa, d, kt[(j * 2 + 1) * HB_BT]);
-                    }
-                    if (e < nq) mac128(sb, pq, c0[((size_t)e << logN) + src]);
+#pragma unroll
+                    for (int j = 0; j < HB_MAX_BETA; j++)
+                        if (j < beta) {
+                            mac128(sb, dv[j], kt[(j * 2 + 0) * HB_BT]);
+                            mac128(sa, dv[j], kt[(j * 2 + 1) * HB_BT]);
+                        }
+                    if (e < nq) mac128(sb, pq, cv);
                     rb = reduce128(sb, pc);
                     ra = reduce128(sa, pc);
                 }

@@ -187,6 +187,9 @@ public:
         if (alpha < 1) alpha = 1;
         if (alpha > 16) HB_THROW(HB_EINVAL, "digits of more than 16 primes are not supported");
         dnum = (L + alpha - 1) / alpha;
+        if (dnum > HB_MAX_BETA)
+            HB_THROW(HB_EINVAL, "more than " + std::to_string(HB_MAX_BETA) +
+                                    " key-switching digits; pass a smaller dnum or more special primes");
 
         cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
         cudaMemPool_t pool;
@@ -319,8 +322,12 @@ public:
                 blob.insert(blob.end(), v.begin(), v.end());
                 return off;
             };
+            auto packed = [](std::vector<u64> v) {  // split-30 form: (v >> 30) << 32 | (v & (2^30 - 1))
+                for (auto &x : v) x = ((x >> 30) << 32) | (x & ((1ull << 30) - 1));
+                return v;
+            };
             size_t o_qhinv = put(qhinv), o_qhinvp = put(qhinvp), o_qhat = put(qhat), o_qjneg = put(qjneg),
-                   o_pneg = put(pneg);
+                   o_pneg = put(pneg), o_qhat_s = put(packed(qhat)), o_qjneg_s = put(packed(qjneg));
             size_t o_phinv = put(phinv), o_phinvp = put(phinvp), o_phat = put(phat), o_pinv = put(pinv),
                    o_pinvp = put(pinvp), o_qlinv = put(qlinv), o_qlinvp = put(qlinvp);
             LevelTabs &T = lv[nq];
@@ -332,6 +339,8 @@ public:
             T.mu.qhinvp = T.blob + o_qhinvp;
             T.mu.qhat = T.blob + o_qhat;
             T.mu.qjneg = T.blob + o_qjneg;
+            T.mu.qhat_s = T.blob + o_qhat_s;
+            T.mu.qjneg_s = T.blob + o_qjneg_s;
             T.md.pneg = T.blob + o_pneg;
             T.md.phinv = T.blob + o_phinv;
             T.md.phinvp = T.blob + o_phinvp;

@@ -373,8 +373,192 @@ __global__ void __launch_bounds__(256) k_ntt_rows(u64 *__restrict__ data, RowMap
     }
 }
 
+// ---------------------------------------------------------------------
+// N = 2^16 = 256 x 256: radix-16 passes.  A thread block owns 16
+// sub-transforms of 256 points (16 columns in the column pass, 16
+// contiguous blocks in the block pass) and 16 threads per sub-transform;
+// each thread holds 16 elements in registers and runs 4 stages on them,
+// the sub-transform is transposed through shared memory, and the thread
+// runs the remaining 4 stages.  Twiddle of a stage with g groups per
+// sub-transform, sub-transform sb of S: tw[g * (S + sb) + i].
+//   layout A: the thread's elements are e = c + 16k (k = 0..15)
+//   layout B: e = 16c + k
+// ---------------------------------------------------------------------
+// forward, layout A, groups 1, 2, 4, 8 (distances 128..16)
+__device__ __forceinline__ void fwd_a(u64 (&x)[16], const u64 *W, const u64 *Wp, int base, u64 q) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 1 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int i = k >> (4 - s);
+            const int wi = g * base + i;
+            ct_bfly(x[k], x[k + d], __ldg(W + wi), __ldg(Wp + wi), q);
+        }
+    }
+}
+// forward, layout B, groups 16, 32, 64, 128 (distances 8..1)
+__device__ __forceinline__ void fwd_b(u64 (&x)[16], const u64 *W, const u64 *Wp, int base, int c, u64 q) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 16 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int i = (c << s) + (k >> (4 - s));
+            const int wi = g * base + i;
+            ct_bfly(x[k], x[k + d], __ldg(W + wi), __ldg(Wp + wi), q);
+        }
+    }
+}
+// inverse, layout B, groups 128, 64, 32, 16 (distances 1..8)
+__device__ __forceinline__ void inv_b(u64 (&x)[16], const u64 *W, const u64 *Wp, int base, int c, u64 q) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 16 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int i = (c << s) + (k >> (4 - s));
+            const int wi = g * base + i;
+            gs_bfly(x[k], x[k + d], __ldg(W + wi), __ldg(Wp + wi), q);
+        }
+    }
+}
+// inverse, layout A, groups 8, 4, 2, 1 (distances 16..128)
+__device__ __forceinline__ void inv_a(u64 (&x)[16], const u64 *W, const u64 *Wp, int base, u64 q) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 1 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int i = k >> (4 - s);
+            const int wi = g * base + i;
+            gs_bfly(x[k], x[k + d], __ldg(W + wi), __ldg(Wp + wi), q);
+        }
+    }
+}
+
+// Column pass: the 16 columns c0..c0+15, element (r, col) at r*256 + c0 + col.
+template <bool INV>
+__global__ void __launch_bounds__(256) k_ntt256_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+                                                      const u64 *__restrict__ twp, int row0) {
+    __shared__ u64 sm[256 * 17];
+    const int row = row0 + blockIdx.y;
+    if (map.skip(row)) return;
+    const int p = map.prime(row);
+    const u64 q = c_pc[p].q;
+    const int col = threadIdx.x & 15, c = threadIdx.x >> 4;
+    const int c0 = blockIdx.x << 4;
+    u64 *a = data + ((size_t)row << 16) + c0 + col;
+    const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
+    u64 x[16];
+    if (!INV) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = a[(size_t)(c + 16 * k) << 8];
+        fwd_a(x, W, Wp, 1, q);
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[(c + 16 * k) * 17 + col] = x[k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sm[(16 * c + k) * 17 + col];
+        fwd_b(x, W, Wp, 1, c, q);
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = reduce4q(x[k], q);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = a[(size_t)(16 * c + k) << 8];
+        inv_b(x, W, Wp, 1, c, q);
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[(16 * c + k) * 17 + col] = x[k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sm[(c + 16 * k) * 17 + col];
+        inv_a(x, W, Wp, 1, q);
+        const u64 ni = c_pc[p].ninv, nip = c_pc[p].ninvp;
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[(size_t)(c + 16 * k) << 8] = mul_shoup(x[k], ni, nip, q);
+    }
+}
+
+// Block pass: blocks rb0..rb0+15 of 256 contiguous elements.
+template <bool INV>
+__global__ void __launch_bounds__(256) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+                                                      const u64 *__restrict__ twp, int row0) {
+    __shared__ u64 sm[16 * 272];
+    const int row = row0 + blockIdx.y;
+    if (map.skip(row)) return;
+    const int p = map.prime(row);
+    const u64 q = c_pc[p].q;
+    const int c = threadIdx.x & 15, blk = threadIdx.x >> 4;
+    const int rb = (blockIdx.x << 4) + blk;
+    u64 *a = data + ((size_t)row << 16) + ((size_t)rb << 8);
+    const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
+    u64 *sb = sm + blk * 272;  // 256 elements of this block, 17-word rows of 16 (padding)
+    u64 x[16];
+    if (!INV) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = a[c + 16 * k];
+        fwd_a(x, W, Wp, 256 + rb, q);
+#pragma unroll
+        for (int k = 0; k < 16; k++) sb[k * 17 + c] = x[k];  // element c + 16k at (k, c)
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];  // element 16c + k
+        fwd_b(x, W, Wp, 256 + rb, c, q);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) sb[c * 17 + k] = reduce4q(x[k], q);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[c + 16 * k] = sb[k * 17 + c];
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; k++) sb[k * 17 + c] = a[c + 16 * k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];
+        inv_b(x, W, Wp, 256 + rb, c, q);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) sb[c * 17 + k] = x[k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sb[k * 17 + c];
+        inv_a(x, W, Wp, 256 + rb, q);
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[c + 16 * k] = x[k];  // [0, 2q): the column pass reduces
+    }
+}
+
+static void ntt256_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bool inv, cudaStream_t s) {
+    for (int r0 = 0; r0 < nrows; r0 += 65535) {
+        const int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
+        const dim3 grid(16, nr);
+        if (!inv) {
+            k_ntt256_cols<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, r0);
+            k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, r0);
+        } else {
+            k_ntt256_rows<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, r0);
+            k_ntt256_cols<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, r0);
+        }
+    }
+}
+
 static void ntt_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bool inv, cudaStream_t s) {
     if (nrows <= 0) return;
+    if (t.logN == 16) {
+        int active = nrows;
+        if (map.alpha > 0)
+            for (int r = 0; r < nrows; r++) active -= map.skip(r) ? 1 : 0;
+        const double nwords = (double)active * 65536.0;
+        ProfScope ps(inv ? KC_NTT_INV : KC_NTT_FWD, 16.0 * nwords, nwords / 2 * 16, s, 2 * ((nrows + 65534) / 65535));
+        ntt256_impl(data, nrows, map, t, inv, s);
+        check_launch("ntt256");
+        return;
+    }
     const int logN = t.logN, logN1 = split_log1(logN), logN2 = logN - logN1;
     const int logC = logN2 < 4 ? logN2 : 4;                    // columns per tile
     int logRB = 12 - logN2;                                     // 4096-word row tiles
@@ -922,14 +1106,22 @@ __global__ void __launch_bounds__(256) k_keymult(u64 *__restrict__ acc, const u6
         const unsigned src = g == 1 ? t : aut_index(t, g, logN);
         const int p = e < nq ? e : L + (e - nq);
         const PrimeConst &pc = c_pc[p];
+        // issue every digit gather and key load before the products
+        u64 dv[HB_MAX_BETA], kbv[HB_MAX_BETA], kav[HB_MAX_BETA];
+#pragma unroll
+        for (int j = 0; j < HB_MAX_BETA; j++)
+            if (j < beta) {
+                dv[j] = Db[((size_t)j * ne + e) * N + src];
+                kbv[j] = key[(((size_t)j * 2 + 0) * keyP + p) * N + t];
+                kav[j] = key[(((size_t)j * 2 + 1) * keyP + p) * N + t];
+            }
         u128 sb = {0, 0}, sa = {0, 0};
-        for (int j = 0; j < beta; j++) {
-            const u64 d = Db[((size_t)j * ne + e) * N + src];
-            const u64 *kb = key + (((size_t)j * 2 + 0) * keyP + p) * N;
-            const u64 *ka = key + (((size_t)j * 2 + 1) * keyP + p) * N;
-            mac128(sb, d, kb[t]);
-            mac128(sa, d, ka[t]);
-        }
+#pragma unroll
+        for (int j = 0; j < HB_MAX_BETA; j++)
+            if (j < beta) {
+                mac128(sb, dv[j], kbv[j]);
+                mac128(sa, dv[j], kav[j]);
+            }
         u64 vb = reduce128(sb, pc), va = reduce128(sa, pc);
         if (addb) vb = add_mod(vb, addb[b * add_stride + ((size_t)e << logN) + src], pc.q);
         if (accumulate) {
@@ -943,6 +1135,7 @@ __global__ void __launch_bounds__(256) k_keymult(u64 *__restrict__ acc, const u6
 void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,
              const u64 *addb, bool accumulate, int logN, int nbatch, size_t d_stride, size_t acc_stride,
              size_t add_stride, cudaStream_t s) {
+    if (beta > HB_MAX_BETA) throw std::invalid_argument("keymult: more digits than HB_MAX_BETA");
     size_t n = (size_t)(nq + K) << logN;
     unsigned g = grid1d(n, 256);
     if (g > 4096) g = 4096;
@@ -964,7 +1157,8 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
                    size_t inner_stride, cudaStream_t s) {
     if (ch.nbabies > HB_BCH || ch.gcount > HB_GCH) throw std::invalid_argument("bsgs chunk too large");
     const size_t smem = HB_BCH * sizeof(BabyDesc) + (size_t)HB_BCH * beta * 2 * HB_BT * 8 + (size_t)HB_BCH * 2 * HB_BT * 8;
-    if (smem > 227 * 1024) throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
+    if (smem > 227 * 1024 || beta > HB_MAX_BETA)
+        throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
     static size_t attr = 0;
     if (smem > attr) {
         cudaFuncSetAttribute(k_bsgs_mac, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -126,6 +126,8 @@ struct ModUpTab {
     const u64 *qhinvp;
     const u64 *qhat;    // [beta][alpha][ne]        qhat_m mod t_e
     const u64 *qjneg;   // [beta][ne]               t_e - (Q_j mod t_e)
+    const u64 *qhat_s;  // qhat in split-30 packed form (targets below 2^40)
+    const u64 *qjneg_s; // qjneg in split-30 packed form
 };
 void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
                  const ModUpTab &tab, int logN, int nbatch, size_t in_stride, size_t out_stride, size_t c1_stride,
@@ -167,9 +169,10 @@ void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, 
              size_t add_stride, cudaStream_t s);
 
 // ---- fused double-hoisted baby steps + plaintext MAC --------------------------
+#define HB_MAX_BETA 8  // key-switching digits handled by the fused kernels
 #define HB_GCH 16   // giant slots per chunk (one warp each)
 #define HB_BCH 32   // babies per chunk (plaintexts held in registers)
-#define HB_BT 32    // coefficients per thread block tile
+#define HB_BT 16    // coefficients per thread block tile
 struct BabyDesc {
     u64 galois;        // 1 for the identity baby (b = 0)
     const u64 *key;    // null for b = 0
