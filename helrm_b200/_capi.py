@@ -100,6 +100,7 @@ SIGNATURES = {
     "helrm_kernel_ntt": [c_void, c_int, c_int, c_int, c_int, c_void],
     "helrm_kernel_automorphism": [c_void, c_void, c_int, c_u64, c_void],
     "helrm_kernel_rescale": [c_void, c_void, c_int, c_int, c_void],
+    "helrm_kernel_rescale_noalloc": [c_void, c_void, c_int, c_int, c_void],
     "helrm_kernel_mac": [P(c_void), P(c_void), c_int, c_int, c_void, c_void],
     "helrm_kernel_rotate_hoisted": [c_void, c_int, c_int, P(c_int), c_int, c_void, c_void],
     "helrm_Synchronize": [],

@@ -690,6 +690,25 @@ public:
         release(R);
         release(W);
     }
+    // the same rescale with both temporaries carved from caller-owned
+    // scratch of nb*npoly*nq*N words (R first, then W); nothing is allocated
+    void rescale_scratch(u64 *out, const u64 *in, int npoly, int nq, int nb, size_t in_stride,
+                         size_t out_stride, u64 *scratch) {
+        if (nq < 2) HB_THROW(HB_ESTATE, "rescale: ciphertext already at level 0");
+        const int l = nq - 1;
+        u64 *R = scratch;
+        u64 *W = scratch + (size_t)nb * npoly * N;
+        for (int b = 0; b < nb; b++)
+            for (int pl = 0; pl < npoly; pl++)
+                d2d(R + ((size_t)b * npoly + pl) * N, in + b * in_stride + ((size_t)pl * nq + l) * N, N);
+        RowMap rm = rowmap(1, 1, L);
+        rm.pbase = l;
+        ntt_inverse(R, nb * npoly, rm, ntt, stream);
+        rescale_prep(W, R, npoly, l, primes[l], logN, nb, (size_t)npoly * N, (size_t)npoly * l * N, stream);
+        ntt_forward(W, nb * npoly * l, qmap(l), ntt, stream);
+        rescale_combine(out, in, W, npoly, nq, lv[nq].qlinv, lv[nq].qlinvp, logN, nb, in_stride,
+                        (size_t)npoly * l * N, out_stride, stream);
+    }
 
     // ---------------------------------------------------------- level / scale alignment
     Ct drop_to(const Ct &c, int nq) {
@@ -1816,6 +1835,65 @@ HB_API int helrm_kernel_rescale(const uint64_t *in, uint64_t *out, int nq, int n
         if (stream) c.stream = (cudaStream_t)stream;
         try {
             c.rescale((u64 *)out, (const u64 *)in, 2, nq, nbatch, (size_t)2 * nq * c.N, (size_t)2 * (nq - 1) * c.N);
+        } catch (...) {
+            c.stream = old;
+            throw;
+        }
+        c.stream = old;
+    });
+}
+
+// ---- rescale without device allocation ---------------------------------------
+// Some callers must not allocate device memory at all: a host runtime that
+// reserves the whole HBM budget up front through its own allocator (an
+// allocation behind its back can fail or push its pool out of memory), and
+// serving loops where the first request of a new batch size would otherwise
+// grow the stream-ordered pool with a blocking cudaMalloc in the middle of a
+// latency-critical step.  For them the rescale temporaries come from this
+// fixed array, part of the library's device image.  Every word the call
+// reads from it is written earlier in the same call, so nothing in it has to
+// start at zero and it is never cleared.
+static __device__ __align__(256) u64 g_rescale_scratch[HELRM_RESCALE_SCRATCH_WORDS];
+
+#define HB_SCRATCH_DEVICES 64
+static std::mutex g_rescale_scratch_mu;
+static u64 *g_rescale_scratch_ptr[HB_SCRATCH_DEVICES] = {};
+
+// The array's address on `device`, looked up once per device with that
+// device current (the lookup loads the library's device image there).
+static u64 *rescale_scratch_on(int device) {
+    if (device < 0 || device >= HB_SCRATCH_DEVICES) HB_THROW(HB_EINVAL, "rescale scratch: device out of range");
+    std::lock_guard<std::mutex> lk(g_rescale_scratch_mu);
+    if (!g_rescale_scratch_ptr[device]) {
+        int cur = -1;
+        cuda_check(cudaGetDevice(&cur), "cudaGetDevice");
+        if (cur != device) cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_rescale_scratch);
+        if (cur != device) cudaSetDevice(cur);
+        cuda_check(e, "cudaGetSymbolAddress(rescale scratch)");
+        if (!p) HB_THROW(HB_ECUDA, "cudaGetSymbolAddress(rescale scratch) returned null");
+        g_rescale_scratch_ptr[device] = (u64 *)p;
+    }
+    return g_rescale_scratch_ptr[device];
+}
+
+HB_API int helrm_kernel_rescale_noalloc(const uint64_t *in, uint64_t *out, int nq, int nbatch, void *stream) {
+    return guard([&] {
+        Context &c = C();
+        if (!in || !out || nq < 2 || nq > c.L || nbatch <= 0)
+            HB_THROW(HB_EINVAL, "kernel_rescale_noalloc: bad arguments");
+        const size_t need = (size_t)nbatch * 2 * nq * c.N;
+        if (need > (size_t)HELRM_RESCALE_SCRATCH_WORDS)
+            HB_THROW(HB_EINVAL, "kernel_rescale_noalloc: needs " + std::to_string(need) +
+                                    " scratch words (nbatch*2*nq*N), above the static limit of " +
+                                    std::to_string((size_t)HELRM_RESCALE_SCRATCH_WORDS));
+        u64 *scratch = rescale_scratch_on(c.device);
+        cudaStream_t old = c.stream;
+        if (stream) c.stream = (cudaStream_t)stream;
+        try {
+            c.rescale_scratch((u64 *)out, (const u64 *)in, 2, nq, nbatch, (size_t)2 * nq * c.N,
+                              (size_t)2 * (nq - 1) * c.N, scratch);
         } catch (...) {
             c.stream = old;
             throw;

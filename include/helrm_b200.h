@@ -204,6 +204,18 @@ int helrm_kernel_mac(const uint64_t *const *d_cts, const uint64_t *const *d_pts,
  * (helrm_AddRotationKey).  d_out: [nrot][nbatch][2][nq][N]. */
 int helrm_kernel_rotate_hoisted(const uint64_t *d_in, int nq, int nbatch, const int *ks, int nrot,
                                 uint64_t *d_out, void *stream);
+/* Same result as helrm_kernel_rescale, but the call allocates no device
+ * memory.  No counterpart in the reference, whose Python operators allocate
+ * freely.  Its temporaries (the INTT of the last limb and the correction
+ * term, nbatch*2*nq*N words in all) come from one fixed array compiled into
+ * the library, HELRM_RESCALE_SCRATCH_WORDS words (32 MiB) per device: one
+ * ciphertext of N = 2^16 at 24 limbs fits.  Larger requests fail with
+ * HB_EINVAL before any work is issued.  The first call on a device looks up
+ * that array's address; make it before any stream capture.  All calls on a
+ * device share the array: calls whose GPU work overlaps (unordered streams,
+ * several host threads) race and corrupt each other's output. */
+#define HELRM_RESCALE_SCRATCH_WORDS (4u << 20)
+int helrm_kernel_rescale_noalloc(const uint64_t *d_in, uint64_t *d_out, int nq, int nbatch, void *stream);
 /* synchronise the library stream */
 int helrm_Synchronize(void);
 
