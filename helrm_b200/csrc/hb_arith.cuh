@@ -41,10 +41,17 @@ struct Split3 {
     unsigned s2;
 };
 __device__ __forceinline__ void split_mac(Split3 &acc, unsigned al, unsigned ah, unsigned bl, unsigned bh) {
-    acc.s0 += (u64)al * bl;
-    acc.s1 += (u64)al * bh;
-    acc.s1 += (u64)ah * bl;
+    // one 32x32+64 multiply-add each (mad.wide.u32)
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s0) : "r"(al), "r"(bl));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s1) : "r"(al), "r"(bh));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s1) : "r"(ah), "r"(bl));
     acc.s2 += ah * bh;
+}
+// Moves the bits of S0 above 2^30 into S1 (same value), so S0 can take 16
+// more terms.  S1 gains < 2^34 per call.
+__device__ __forceinline__ void split_normalize(Split3 &acc) {
+    acc.s1 += acc.s0 >> 30;
+    acc.s0 &= 0x3FFFFFFFull;
 }
 __device__ __forceinline__ u64 split_pack(u64 v) { return ((v >> 30) << 32) | (v & HB_SPLIT_MASK); }
 
@@ -92,11 +99,16 @@ __device__ __forceinline__ u64 reduce128(const u128 &x, const PrimeConst &pc) {
 __device__ __forceinline__ u64 mul_mod(u64 a, u64 b, const PrimeConst &pc) {
     return reduce128(__umul64hi(a, b), a * b, pc);
 }
-// (S0 + S1 2^30 + S2 2^60) mod q
+// (S0 + S1 2^30 + S2 2^60) mod q, for S1 < 2^62 and S2 < 2^32: the value is
+// first rewritten as lo + hi 2^60 with lo < 2^60 (carries of S0 into S1 and
+// of S1 into S2), then hi 2^60 is folded with 2^60 mod q (a lazy Shoup
+// product, < 2q) and the sum (< 2^61) reduced once with floor(2^64/q).
 __device__ __forceinline__ u64 split_reduce(const Split3 &s, const PrimeConst &pc) {
-    u64 r = mul_shoup(s.s0, 1ull, pc.onep, pc.q);
-    r = add_mod(r, mul_shoup(s.s1, pc.c30, pc.c30p, pc.q), pc.q);
-    return add_mod(r, mul_shoup((u64)s.s2, pc.c60, pc.c60p, pc.q), pc.q);
+    const u64 s1 = s.s1 + (s.s0 >> 30);
+    const u64 lo = (s.s0 & HB_SPLIT_MASK) | ((s1 & HB_SPLIT_MASK) << 30);
+    const u64 hi = (u64)s.s2 + (s1 >> 30);
+    const u64 v = lo + mul_shoup_lazy(hi, pc.c60, pc.c60p, pc.q);
+    return mul_shoup(v, 1ull, pc.onep, pc.q);
 }
 
 // bit reversal of the low `bits` bits

@@ -13,7 +13,7 @@
 // (digits D, c0, inner sums) streams once per ciphertext.  Residues below
 // 2^40 (the 36-bit q limbs) multiply with the split-30 form, four 32-bit
 // multiply-adds per product; the 60-bit special-prime limbs use 64x64->128
-// products.  Accumulation is lazy and reduced once per 16 terms.
+// products.  Accumulation is lazy: one modular reduction per output.
 // Included by hb_kernels.cu (it reads the per-prime __constant__ table).
 #pragma once
 
@@ -29,6 +29,9 @@ __device__ __forceinline__ void mac_split_packed(Split3 &s, u64 a_packed, u64 b_
 
 }  // namespace
 
+// NBF = HB_BCH: a full chunk, the baby count is a compile-time constant and
+// the unrolled loops carry no guards; NBF = 0: the count is read at run time.
+template <int NBF>
 __global__ void __launch_bounds__(kThreads, 2)
     k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
                int K, int L, int beta, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch,
@@ -42,7 +45,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const PrimeConst pc = c_pc[p];
     const bool fast = pc.q < (1ull << 40);
     const int tid = threadIdx.x;
-    const int nb = ch.nbabies;
+    const int nb = NBF ? NBF : ch.nbabies;
 
     // shared memory: descriptors | key tiles [nb][beta][2][BT] | R [nb][2][BT]
     BabyDesc *sdesc = reinterpret_cast<BabyDesc *>(sm);
@@ -84,30 +87,37 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();
 
+    // 32-bit element offsets inside one ciphertext's digits / c0 (the whole
+    // extended digit stack of one ciphertext stays far below 2^32 words)
+    const unsigned dstride = (unsigned)ne << logN;
+    const unsigned erow = (unsigned)e << logN;
     const size_t nall = (size_t)ne << logN;
     for (int b = 0; b < nbatch; b++) {
         const u64 *c0 = ct + b * ct_stride;
         const u64 *c1 = c0 + ((size_t)nq << logN);
-        const u64 *Db = D + b * d_stride;
+        const u64 *Dbe = D + b * d_stride + erow;
         // ---- phase A: baby rotations of this tile.  The gathers of an item
         // (beta digits at the rotated index, and c0) are all issued before
         // any of them is used, so their latencies overlap.
-        for (int it = tid; it < nb * HB_BT; it += kThreads) {
+#pragma unroll
+        for (int it0 = 0; it0 < (NBF ? NBF * HB_BT : HB_BCH * HB_BT); it0 += kThreads) {
+            const int it = it0 + tid;
+            if (!NBF && it >= nb * HB_BT) break;
             const int bb = it / HB_BT, n = it % HB_BT;
             const unsigned t = (unsigned)(n0 + n);
             const BabyDesc &bd = sdesc[bb];
             u64 rb, ra;
             if (bd.key == nullptr) {
-                rb = e < nq ? mul_mod(pq, c0[((size_t)e << logN) + t], pc) : 0;
-                ra = e < nq ? mul_mod(pq, c1[((size_t)e << logN) + t], pc) : 0;
+                rb = e < nq ? mul_mod(pq, c0[erow + t], pc) : 0;
+                ra = e < nq ? mul_mod(pq, c1[erow + t], pc) : 0;
             } else {
                 const unsigned src = aut_index(t, bd.galois, logN);
                 const u64 *kt = skey + (size_t)bb * beta * 2 * HB_BT + n;
                 u64 dv[HB_MAX_BETA];
 #pragma unroll
                 for (int j = 0; j < HB_MAX_BETA; j++)
-                    if (j < beta) dv[j] = Db[((size_t)j * ne + e) * N + src];
-                const u64 cv = e < nq ? c0[((size_t)e << logN) + src] : 0;
+                    if (j < beta) dv[j] = Dbe[(unsigned)j * dstride + src];
+                const u64 cv = e < nq ? c0[erow + src] : 0;
                 if (fast) {
                     Split3 sb = {0, 0, 0}, sa = {0, 0, 0};
 #pragma unroll
@@ -137,47 +147,40 @@ __global__ void __launch_bounds__(kThreads, 2)
             sR[(bb * 2 + 1) * HB_BT + n] = fast ? split_pack(ra) : ra;
         }
         __syncthreads();
-        // ---- phase B: inner[g] += pt(g, b) * R_b
+        // ---- phase B: inner[g] += pt(g, b) * R_b.  Split sums: S0 takes 16
+        // terms below 2^60 before it is normalised (exact, three
+        // instructions); one reduction per output.  128-bit sums of at most
+        // 32 products below 2^122 need no intermediate reduction.
         if (gactive) {
             u64 vb, va;
             if (fast) {
                 Split3 ab = {0, 0, 0}, aa = {0, 0, 0};
-                u64 tb = 0, ta = 0;
 #pragma unroll
                 for (int bb = 0; bb < HB_BCH; bb++) {
-                    if (bb < nb) {
+                    if (NBF || bb < nb) {
                         mac_split_packed(ab, ptv[bb], sR[(bb * 2 + 0) * HB_BT + nl]);
                         mac_split_packed(aa, ptv[bb], sR[(bb * 2 + 1) * HB_BT + nl]);
-                        if ((bb & 15) == 15) {
-                            tb = add_mod(tb, split_reduce(ab, pc), pc.q);
-                            ta = add_mod(ta, split_reduce(aa, pc), pc.q);
-                            ab = {0, 0, 0};
-                            aa = {0, 0, 0};
+                        if (bb == 15) {
+                            split_normalize(ab);
+                            split_normalize(aa);
                         }
                     }
                 }
-                vb = add_mod(tb, split_reduce(ab, pc), pc.q);
-                va = add_mod(ta, split_reduce(aa, pc), pc.q);
+                vb = split_reduce(ab, pc);
+                va = split_reduce(aa, pc);
             } else {
                 u128 ab = {0, 0}, aa = {0, 0};
-                u64 tb = 0, ta = 0;
 #pragma unroll
                 for (int bb = 0; bb < HB_BCH; bb++) {
-                    if (bb < nb) {
+                    if (NBF || bb < nb) {
                         mac128(ab, ptv[bb], sR[(bb * 2 + 0) * HB_BT + nl]);
                         mac128(aa, ptv[bb], sR[(bb * 2 + 1) * HB_BT + nl]);
-                        if ((bb & 15) == 15) {
-                            tb = add_mod(tb, reduce128(ab, pc), pc.q);
-                            ta = add_mod(ta, reduce128(aa, pc), pc.q);
-                            ab = {0, 0};
-                            aa = {0, 0};
-                        }
                     }
                 }
-                vb = add_mod(tb, reduce128(ab, pc), pc.q);
-                va = add_mod(ta, reduce128(aa, pc), pc.q);
+                vb = reduce128(ab, pc);
+                va = reduce128(aa, pc);
             }
-            u64 *o = inner + b * inner_stride + (size_t)(ch.gbase + gi) * 2 * nall + ((size_t)e << logN) + n0 + nl;
+            u64 *o = inner + b * inner_stride + (size_t)(ch.gbase + gi) * 2 * nall + erow + n0 + nl;
             if (ch.accumulate) {
                 vb = add_mod(vb, o[0], pc.q);
                 va = add_mod(va, o[nall], pc.q);

@@ -1161,7 +1161,8 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
         throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
     static size_t attr = 0;
     if (smem > attr) {
-        cudaFuncSetAttribute(k_bsgs_mac, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = smem;
     }
     const size_t n = (size_t)(nq + K) << logN;
@@ -1173,8 +1174,12 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
                         2.0 * beta * ch.nkeys * nd + ch.npts * nd),
                  (double)nbatch * nd * (2.0 * beta * ch.nkeys + 2.0 * ch.npts), s, 1);
     dim3 grid((1u << logN) / HB_BT, nq + K);
-    k_bsgs_mac<<<grid, HB_GCH * HB_BT, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN, nbatch,
-                                                  ct_stride, d_stride, inner_stride);
+    if (ch.nbabies == HB_BCH)
+        k_bsgs_mac<HB_BCH><<<grid, HB_GCH * HB_BT, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q,
+                                                              logN, nbatch, ct_stride, d_stride, inner_stride);
+    else
+        k_bsgs_mac<0><<<grid, HB_GCH * HB_BT, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN,
+                                                         nbatch, ct_stride, d_stride, inner_stride);
     check_launch("bsgs_mac");
 }
 
