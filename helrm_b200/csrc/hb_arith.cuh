@@ -111,6 +111,46 @@ __device__ __forceinline__ u64 split_reduce(const Split3 &s, const PrimeConst &p
     return mul_shoup(v, 1ull, pc.onep, pc.q);
 }
 
+// Split-30 sums of products a*b with one factor below 2^40 and the other
+// below 2^61 (basis conversion: a main-prime residue times a constant modulo
+// any prime, or a special-prime residue times a constant modulo a main
+// prime).  Per term al*bl < 2^60 goes to S0, al*bh + ah*bl < 2^61 + 2^40 to
+// S1 and ah*bh < 2^41 to S2.  After at most 4 terms the sums are normalised
+// (carries of S0 into S1 and of S1 into S2; the value is unchanged), which
+// keeps S0 and S1 below 2^64.
+struct SplitW {
+    u64 s0, s1, s2;
+};
+__device__ __forceinline__ void splitw_mac(SplitW &acc, u64 a_packed, u64 b_packed) {
+    const unsigned al = (unsigned)a_packed, ah = (unsigned)(a_packed >> 32);
+    const unsigned bl = (unsigned)b_packed, bh = (unsigned)(b_packed >> 32);
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s0) : "r"(al), "r"(bl));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s1) : "r"(al), "r"(bh));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s1) : "r"(ah), "r"(bl));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s2) : "r"(ah), "r"(bh));
+}
+// a * b for a small count a < 2^32 (no high half)
+__device__ __forceinline__ void splitw_mac_small(SplitW &acc, unsigned a, u64 b_packed) {
+    const unsigned bl = (unsigned)b_packed, bh = (unsigned)(b_packed >> 32);
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s0) : "r"(a), "r"(bl));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s1) : "r"(a), "r"(bh));
+}
+__device__ __forceinline__ void splitw_normalize(SplitW &acc) {
+    acc.s1 += acc.s0 >> 30;
+    acc.s0 &= HB_SPLIT_MASK;
+    acc.s2 += acc.s1 >> 30;
+    acc.s1 &= HB_SPLIT_MASK;
+}
+// (S0 + S1 2^30 + S2 2^60) mod q for S0 < 2^64, S1 < 2^64 - 2^34, S2 < 2^63
+// and any q < 2^62: lo + hi 2^60 with lo < 2^60 as in split_reduce.
+__device__ __forceinline__ u64 splitw_reduce(const SplitW &s, const PrimeConst &pc) {
+    const u64 s1 = s.s1 + (s.s0 >> 30);
+    const u64 lo = (s.s0 & HB_SPLIT_MASK) | ((s1 & HB_SPLIT_MASK) << 30);
+    const u64 hi = s.s2 + (s1 >> 30);
+    const u64 v = lo + mul_shoup_lazy(hi, pc.c60, pc.c60p, pc.q);
+    return mul_shoup(v, 1ull, pc.onep, pc.q);
+}
+
 // bit reversal of the low `bits` bits
 __device__ __forceinline__ unsigned brev_bits(unsigned x, int bits) {
     return __brev(x) >> (32 - bits);

@@ -329,7 +329,10 @@ public:
             size_t o_qhinv = put(qhinv), o_qhinvp = put(qhinvp), o_qhat = put(qhat), o_qjneg = put(qjneg),
                    o_pneg = put(pneg), o_qhat_s = put(packed(qhat)), o_qjneg_s = put(packed(qjneg));
             size_t o_phinv = put(phinv), o_phinvp = put(phinvp), o_phat = put(phat), o_pinv = put(pinv),
-                   o_pinvp = put(pinvp), o_qlinv = put(qlinv), o_qlinvp = put(qlinvp);
+                   o_pinvp = put(pinvp), o_qlinv = put(qlinv), o_qlinvp = put(qlinvp), o_phat_s = put(packed(phat)),
+                   o_pneg_s = put(packed(pneg));
+            bool small_main = true;  // split-30 basis conversion needs main primes below 2^40
+            for (int i = 0; i < L; i++) small_main = small_main && primes[i] < (1ull << 40);
             LevelTabs &T = lv[nq];
             T.blob = alloc(blob.size());
             cuda_check(cudaMemcpyAsync(T.blob, blob.data(), blob.size() * 8, cudaMemcpyHostToDevice, stream),
@@ -341,7 +344,11 @@ public:
             T.mu.qjneg = T.blob + o_qjneg;
             T.mu.qhat_s = T.blob + o_qhat_s;
             T.mu.qjneg_s = T.blob + o_qjneg_s;
+            T.mu.split = small_main ? 1 : 0;
             T.md.pneg = T.blob + o_pneg;
+            T.md.phat_s = T.blob + o_phat_s;
+            T.md.pneg_s = T.blob + o_pneg_s;
+            T.md.split = small_main ? 1 : 0;
             T.md.phinv = T.blob + o_phinv;
             T.md.phinvp = T.blob + o_phinvp;
             T.md.phat = T.blob + o_phat;

@@ -949,17 +949,100 @@ __global__ void k_modup_bconv(u64 *__restrict__ D, const u64 *__restrict__ X, co
     }
 }
 
+// The same conversion with split-30 products (every main prime below 2^40;
+// the digit values y_m are then below 2^40 and every table entry below
+// 2^61).  NA = digits size, a compile-time constant; blockIdx.y + j0 is the
+// digit.  The digit's qhat and qjneg rows are staged in shared memory.
+template <int NA>
+__global__ void __launch_bounds__(256)
+    k_modup_bconv_split(u64 *__restrict__ D, const u64 *__restrict__ X, const u64 *__restrict__ c1ntt, int nq, int K,
+                        int L, int alpha, int j0, ModUpTab tab, int logN, size_t in_stride, size_t out_stride,
+                        size_t c1_stride) {
+    __shared__ u64 st[(NA + 1) * HB_MAX_PRIMES];  // qhat [m][e], then qjneg [e]
+    const int N = 1 << logN;
+    const int j = j0 + blockIdx.y, b = blockIdx.z;
+    const int ne = nq + K;
+    const int lo = j * alpha;
+    for (int i = threadIdx.x; i < NA * ne; i += blockDim.x) st[i] = tab.qhat_s[(size_t)j * alpha * ne + i];
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) st[NA * ne + i] = tab.qjneg_s[(size_t)j * ne + i];
+    __syncthreads();
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const u64 *Xb = X + b * in_stride;
+    u64 *Db = D + b * out_stride + (size_t)j * ne * N;
+    u64 y[NA];
+    unsigned nneg = 0;
+#pragma unroll
+    for (int m = 0; m < NA; m++) {
+        const int pm = lo + m;
+        const u64 qm = c_pc[pm].q;
+        const u64 v = mul_shoup(Xb[(size_t)pm * N + n], tab.qhinv[j * alpha + m], tab.qhinvp[j * alpha + m], qm);
+        nneg += v > (qm >> 1);
+        y[m] = split_pack(v);
+    }
+    for (int e = 0; e < ne; e++) {
+        if (e >= lo && e < lo + NA) {
+            Db[(size_t)e * N + n] = c1ntt[b * c1_stride + (size_t)e * N + n];
+            continue;
+        }
+        const int p = e < nq ? e : L + (e - nq);
+        SplitW acc = {0, 0, 0};
+#pragma unroll
+        for (int m = 0; m < NA; m++) {
+            splitw_mac(acc, y[m], st[m * ne + e]);
+            if ((m & 3) == 3 && m + 1 < NA) splitw_normalize(acc);
+        }
+        splitw_mac_small(acc, nneg, st[NA * ne + e]);
+        Db[(size_t)e * N + n] = splitw_reduce(acc, c_pc[p]);
+    }
+}
+
+template <int NA>
+static void modup_split_launch(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int j0,
+                               int ndig, const ModUpTab &tab, int logN, int nbatch, size_t in_stride,
+                               size_t out_stride, size_t c1_stride, cudaStream_t s) {
+    dim3 grid(((1 << logN) + 255) / 256, ndig, nbatch);
+    k_modup_bconv_split<NA><<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, j0, tab, logN, in_stride, out_stride,
+                                                  c1_stride);
+}
+static void modup_split_dispatch(int na, u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha,
+                                 int j0, int ndig, const ModUpTab &tab, int logN, int nbatch, size_t in_stride,
+                                 size_t out_stride, size_t c1_stride, cudaStream_t s) {
+#define HB_MU_CASE(A)                                                                                             \
+    case A:                                                                                                        \
+        modup_split_launch<A>(D, X, c1ntt, nq, K, L, alpha, j0, ndig, tab, logN, nbatch, in_stride, out_stride,    \
+                              c1_stride, s);                                                                       \
+        break;
+    switch (na) {
+        HB_MU_CASE(1) HB_MU_CASE(2) HB_MU_CASE(3) HB_MU_CASE(4) HB_MU_CASE(5) HB_MU_CASE(6) HB_MU_CASE(7)
+        HB_MU_CASE(8)
+        default: throw std::invalid_argument("modup_bconv: split digit size out of range");
+    }
+#undef HB_MU_CASE
+}
+
 void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
                   const ModUpTab &tab, int logN, int nbatch, size_t in_stride, size_t out_stride, size_t c1_stride,
                   cudaStream_t s) {
     if (alpha > HB_MAX_ALPHA) throw std::invalid_argument("alpha exceeds HB_MAX_ALPHA");
     const int N = 1 << logN;
-    dim3 grid((N + 255) / 256, beta, nbatch);
     const int ne = nq + K;
+    if (ne > HB_MAX_PRIMES) throw std::invalid_argument("modup_bconv: too many primes");
     ProfScope ps(KC_MODUP_BCONV, 8.0 * nbatch * (double)N * (nq + (double)beta * ne),
                  (double)nbatch * N * ((double)nq + (double)alpha * ((double)beta * ne - nq)), s, 1);
-    k_modup_bconv<<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, beta, tab, logN, in_stride, out_stride,
-                                       c1_stride);
+    if (tab.split && alpha <= 8) {
+        const int full = nq / alpha, rag = nq - full * alpha;
+        if (full > 0)
+            modup_split_dispatch(alpha, D, X, c1ntt, nq, K, L, alpha, 0, full, tab, logN, nbatch, in_stride,
+                                 out_stride, c1_stride, s);
+        if (rag > 0)
+            modup_split_dispatch(rag, D, X, c1ntt, nq, K, L, alpha, full, 1, tab, logN, nbatch, in_stride,
+                                 out_stride, c1_stride, s);
+    } else {
+        dim3 grid((N + 255) / 256, beta, nbatch);
+        k_modup_bconv<<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, beta, tab, logN, in_stride, out_stride,
+                                           c1_stride);
+    }
     check_launch("modup_bconv");
 }
 
@@ -989,14 +1072,67 @@ __global__ void k_moddown_bconv(u64 *__restrict__ Z, const u64 *__restrict__ Y, 
         Zb[(size_t)i * N + n] = reduce128(acc, c_pc[i]);
     }
 }
+// The same conversion with split-30 products (every main prime below 2^40:
+// table entries below 2^40, special-prime values below 2^61).  KK = number
+// of special primes; the phat and pneg rows are staged in shared memory.
+template <int KK>
+__global__ void __launch_bounds__(256)
+    k_moddown_bconv_split(u64 *__restrict__ Z, const u64 *__restrict__ Y, int nq, int L, ModDownTab tab, int logN,
+                          size_t in_stride, size_t out_stride) {
+    __shared__ u64 st[(KK + 1) * HB_MAX_PRIMES];  // phat [k][i], then pneg [i]
+    for (int i = threadIdx.x; i < KK * nq; i += blockDim.x) st[i] = tab.phat_s[i];
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) st[KK * nq + i] = tab.pneg_s[i];
+    __syncthreads();
+    const int N = 1 << logN;
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const int b = blockIdx.y;
+    const u64 *Yb = Y + b * in_stride;
+    u64 *Zb = Z + b * out_stride;
+    u64 y[KK];
+    unsigned nneg = 0;
+#pragma unroll
+    for (int k = 0; k < KK; k++) {
+        const u64 pk = c_pc[L + k].q;
+        const u64 v = mul_shoup(Yb[(size_t)k * N + n], tab.phinv[k], tab.phinvp[k], pk);
+        nneg += v > (pk >> 1);
+        y[k] = split_pack(v);
+    }
+    for (int i = 0; i < nq; i++) {
+        SplitW acc = {0, 0, 0};
+#pragma unroll
+        for (int k = 0; k < KK; k++) {
+            splitw_mac(acc, st[k * nq + i], y[k]);
+            if ((k & 3) == 3 && k + 1 < KK) splitw_normalize(acc);
+        }
+        splitw_mac_small(acc, nneg, st[KK * nq + i]);
+        Zb[(size_t)i * N + n] = splitw_reduce(acc, c_pc[i]);
+    }
+}
+
 void moddown_bconv(u64 *Z, const u64 *Y, int nq, int K, int L, const ModDownTab &tab, int logN, int nbatch,
                    size_t in_stride, size_t out_stride, cudaStream_t s) {
     if (K > 8) throw std::invalid_argument("at most 8 special primes");
+    if (nq > HB_MAX_PRIMES) throw std::invalid_argument("moddown_bconv: too many primes");
     const int N = 1 << logN;
     dim3 grid((N + 255) / 256, nbatch);
     ProfScope ps(KC_MODDOWN_BCONV, 8.0 * nbatch * (double)N * (K + nq), (double)nbatch * N * (K + (double)K * nq), s,
                  1);
-    k_moddown_bconv<<<grid, 256, 0, s>>>(Z, Y, nq, K, L, tab, logN, in_stride, out_stride);
+    if (tab.split) {
+        switch (K) {
+#define HB_MD_CASE(A)                                                                                             \
+    case A:                                                                                                        \
+        k_moddown_bconv_split<A><<<grid, 256, 0, s>>>(Z, Y, nq, L, tab, logN, in_stride, out_stride);              \
+        break;
+            HB_MD_CASE(1) HB_MD_CASE(2) HB_MD_CASE(3) HB_MD_CASE(4) HB_MD_CASE(5) HB_MD_CASE(6) HB_MD_CASE(7)
+            HB_MD_CASE(8)
+#undef HB_MD_CASE
+            default:
+                k_moddown_bconv<<<grid, 256, 0, s>>>(Z, Y, nq, K, L, tab, logN, in_stride, out_stride);
+        }
+    } else {
+        k_moddown_bconv<<<grid, 256, 0, s>>>(Z, Y, nq, K, L, tab, logN, in_stride, out_stride);
+    }
     check_launch("moddown_bconv");
 }
 

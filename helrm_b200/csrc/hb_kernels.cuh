@@ -126,8 +126,9 @@ struct ModUpTab {
     const u64 *qhinvp;
     const u64 *qhat;    // [beta][alpha][ne]        qhat_m mod t_e
     const u64 *qjneg;   // [beta][ne]               t_e - (Q_j mod t_e)
-    const u64 *qhat_s;  // qhat in split-30 packed form (targets below 2^40)
+    const u64 *qhat_s;  // qhat in split-30 packed form
     const u64 *qjneg_s; // qjneg in split-30 packed form
+    int split;          // every main prime below 2^40: split-30 products
 };
 void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
                  const ModUpTab &tab, int logN, int nbatch, size_t in_stride, size_t out_stride, size_t c1_stride,
@@ -140,6 +141,9 @@ struct ModDownTab {
     const u64 *pinv;    // [nq] P^-1 mod q_i, with Shoup
     const u64 *pinvp;
     const u64 *pneg;    // [nq] q_i - (P mod q_i)
+    const u64 *phat_s;  // phat in split-30 packed form
+    const u64 *pneg_s;  // pneg in split-30 packed form
+    int split;          // every main prime below 2^40: split-30 products
 };
 // Z[i] = sum_k (Y_k * phinv_k mod p_k) * phat_k mod q_i  (coefficient form),
 // with the same centred lift as ModUp.
