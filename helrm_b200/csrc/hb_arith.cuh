@@ -76,6 +76,24 @@ __device__ __forceinline__ u64 mul_shoup_lazy(u64 a, u64 w, u64 wp, u64 q) {
     return a * w - hi * q;
 }
 
+// Lazy product y*w mod q in [0, 2q) for q < 2^40 and y < 2^47, with the
+// Shoup quotient estimated in double precision instead of a 64x64-bit high
+// product.  wq = fl(w/q) (relative error <= 2^-53).  y < 2^52 becomes a
+// double exactly by placing it in the mantissa of 2^52 (bit pattern
+// 0x4330... | y) and subtracting 2^52; fma(y, wq, 2^52) rounds y*wq to the
+// nearest integer Q, read back from the mantissa bits.  |y*wq - y*w/q| <=
+// y 2^-53 <= 2^-6, so |Q - y*w/q| <= 0.52 and y*w + q - Q*q, computed
+// modulo 2^64, lies in [0.48q, 1.52q].  The double-precision pipe is
+// separate from the integer-multiply pipe, which the rest of the NTT keeps
+// busy.
+__device__ __forceinline__ u64 mul_fq_lazy(u64 y, u64 w, double wq, u64 q) {
+    const double two52 = 4503599627370496.0;
+    const double yd = __longlong_as_double((long long)(y | 0x4330000000000000ull)) - two52;
+    const double r = __fma_rn(yd, wq, two52);
+    const u64 Q = (u64)__double_as_longlong(r) & 0x000FFFFFFFFFFFFFull;
+    return y * w + q - Q * q;
+}
+
 struct u128 {
     u64 lo, hi;
 };

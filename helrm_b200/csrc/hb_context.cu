@@ -217,7 +217,9 @@ public:
         upload_prime_consts(pcs.data(), P);
 
         // twiddles
-        std::vector<u64> tw((size_t)4 * P * N);
+        // [4][P][N] u64 twiddles and Shoup companions, then [2][P][N] doubles
+        // fl(w / q) for primes below 2^40 (quotient estimates of the NTT)
+        std::vector<u64> tw((size_t)6 * P * N, 0);
         for (int p = 0; p < P; p++) {
             u64 q = primes[p];
             u64 psi = find_psi(q, logN), ipsi = h_invm(psi, q);
@@ -235,6 +237,14 @@ public:
                 Tp[i] = h_shoup(T[i], q);
                 Ip[i] = h_shoup(I[i], q);
             }
+            if (q < (1ull << 40)) {
+                double *Tq = reinterpret_cast<double *>(&tw[(size_t)(4 * P + p) * N]);
+                double *Iq = reinterpret_cast<double *>(&tw[(size_t)(5 * P + p) * N]);
+                for (int i = 0; i < N; i++) {
+                    Tq[i] = (double)T[i] / (double)q;  // both exact doubles: correctly rounded
+                    Iq[i] = (double)I[i] / (double)q;
+                }
+            }
         }
         d_tables = alloc(tw.size());
         cuda_check(cudaMemcpyAsync(d_tables, tw.data(), tw.size() * 8, cudaMemcpyHostToDevice, stream), "tw upload");
@@ -242,6 +252,8 @@ public:
         ntt.twp = d_tables + (size_t)P * N;
         ntt.itw = d_tables + (size_t)2 * P * N;
         ntt.itwp = d_tables + (size_t)3 * P * N;
+        ntt.twq = reinterpret_cast<const double *>(d_tables + (size_t)4 * P * N);
+        ntt.itwq = reinterpret_cast<const double *>(d_tables + (size_t)5 * P * N);
         ntt.logN = logN;
 
         std::vector<u64> pm(P);

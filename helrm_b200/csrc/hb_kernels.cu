@@ -138,6 +138,27 @@ __device__ __forceinline__ void ct_bfly(u64 &x, u64 &y, u64 w, u64 wp, u64 q) {
     y = x + two_q - t;
     x = x + t;
 }
+// Forward butterfly without the correction of x, for q below 2^40: with
+// inputs below B the outputs stay below B + 2q (Shoup's lazy product is
+// below 2q for any 64-bit input), so the 16 stages of a 2^16-point
+// transform end below 33q < 2^46 and one reduction per element follows.
+// The twiddle product uses the double-precision quotient (mul_fq_lazy),
+// valid for these inputs (below 2^46).
+__device__ __forceinline__ void ct_bfly_nc(u64 &x, u64 &y, u64 w, double wq, u64 q, u64 two_q) {
+    const u64 t = mul_fq_lazy(y, w, wq, q);
+    y = x + two_q - t;
+    x = x + t;
+}
+// Inverse butterfly for q below 2^40 with the double-precision quotient:
+// values stay in [0, 2q) as in gs_bfly.
+__device__ __forceinline__ void gs_bfly_fq(u64 &x, u64 &y, u64 w, double wq, u64 q) {
+    const u64 two_q = 2 * q;
+    u64 s = x + y;
+    if (s >= two_q) s -= two_q;
+    const u64 d = x + two_q - y;
+    x = s;
+    y = mul_fq_lazy(d, w, wq, q);
+}
 __device__ __forceinline__ void gs_bfly(u64 &x, u64 &y, u64 w, u64 wp, u64 q) {
     const u64 two_q = 2 * q;
     u64 s = x + y;
@@ -412,6 +433,58 @@ __device__ __forceinline__ void fwd_b(u64 (&x)[16], const u64 *W, const u64 *Wp,
         }
     }
 }
+// the same two forward halves with uncorrected butterflies (q < 2^40)
+__device__ __forceinline__ void fwd_a_nc(u64 (&x)[16], const u64 *W, const double *Wq, int base, u64 q) {
+    const u64 two_q = 2 * q;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 1 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int wi = g * base + (k >> (4 - s));
+            ct_bfly_nc(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q, two_q);
+        }
+    }
+}
+__device__ __forceinline__ void fwd_b_nc(u64 (&x)[16], const u64 *W, const double *Wq, int base, int c, u64 q) {
+    const u64 two_q = 2 * q;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 16 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int wi = g * base + (c << s) + (k >> (4 - s));
+            ct_bfly_nc(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q, two_q);
+        }
+    }
+}
+// inverse halves with the double-precision quotient (q < 2^40)
+__device__ __forceinline__ void inv_b_fq(u64 (&x)[16], const u64 *W, const double *Wq, int base, int c, u64 q) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 16 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int wi = g * base + (c << s) + (k >> (4 - s));
+            gs_bfly_fq(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q);
+        }
+    }
+}
+__device__ __forceinline__ void inv_a_fq(u64 (&x)[16], const u64 *W, const double *Wq, int base, u64 q) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 1 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            const int wi = g * base + (k >> (4 - s));
+            gs_bfly_fq(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q);
+        }
+    }
+}
 // inverse, layout B, groups 128, 64, 32, 16 (distances 1..8)
 __device__ __forceinline__ void inv_b(u64 (&x)[16], const u64 *W, const u64 *Wp, int base, int c, u64 q) {
 #pragma unroll
@@ -443,8 +516,9 @@ __device__ __forceinline__ void inv_a(u64 (&x)[16], const u64 *W, const u64 *Wp,
 
 // Column pass: the 16 columns c0..c0+15, element (r, col) at r*256 + c0 + col.
 template <bool INV>
-__global__ void __launch_bounds__(256) k_ntt256_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
-                                                      const u64 *__restrict__ twp, int row0) {
+__global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+                                                      const u64 *__restrict__ twp,
+                                                      const double *__restrict__ twq, int row0) {
     __shared__ u64 sm[256 * 17];
     const int row = row0 + blockIdx.y;
     if (map.skip(row)) return;
@@ -454,29 +528,49 @@ __global__ void __launch_bounds__(256) k_ntt256_cols(u64 *__restrict__ data, Row
     const int c0 = blockIdx.x << 4;
     u64 *a = data + ((size_t)row << 16) + c0 + col;
     const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
+    const double *Wq = twq + ((size_t)p << 16);
     u64 x[16];
     if (!INV) {
+        // q < 2^40: uncorrected butterflies, the column pass leaves values
+        // below 17q for the block pass; otherwise Harvey's [0, 4q) form
+        const bool nc = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(c + 16 * k) << 8];
-        fwd_a(x, W, Wp, 1, q);
+        if (nc)
+            fwd_a_nc(x, W, Wq, 1, q);
+        else
+            fwd_a(x, W, Wp, 1, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) sm[(c + 16 * k) * 17 + col] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sm[(16 * c + k) * 17 + col];
-        fwd_b(x, W, Wp, 1, c, q);
+        if (nc) {
+            fwd_b_nc(x, W, Wq, 1, c, q);
 #pragma unroll
-        for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = reduce4q(x[k], q);
+            for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = x[k];
+        } else {
+            fwd_b(x, W, Wp, 1, c, q);
+#pragma unroll
+            for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = reduce4q(x[k], q);
+        }
     } else {
+        const bool fq = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(16 * c + k) << 8];
-        inv_b(x, W, Wp, 1, c, q);
+        if (fq)
+            inv_b_fq(x, W, Wq, 1, c, q);
+        else
+            inv_b(x, W, Wp, 1, c, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) sm[(16 * c + k) * 17 + col] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sm[(c + 16 * k) * 17 + col];
-        inv_a(x, W, Wp, 1, q);
+        if (fq)
+            inv_a_fq(x, W, Wq, 1, q);
+        else
+            inv_a(x, W, Wp, 1, q);
         const u64 ni = c_pc[p].ninv, nip = c_pc[p].ninvp;
 #pragma unroll
         for (int k = 0; k < 16; k++) a[(size_t)(c + 16 * k) << 8] = mul_shoup(x[k], ni, nip, q);
@@ -485,8 +579,9 @@ __global__ void __launch_bounds__(256) k_ntt256_cols(u64 *__restrict__ data, Row
 
 // Block pass: blocks rb0..rb0+15 of 256 contiguous elements.
 template <bool INV>
-__global__ void __launch_bounds__(256) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
-                                                      const u64 *__restrict__ twp, int row0) {
+__global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+                                                      const u64 *__restrict__ twp,
+                                                      const double *__restrict__ twq, int row0) {
     __shared__ u64 sm[16 * 272];
     const int row = row0 + blockIdx.y;
     if (map.skip(row)) return;
@@ -496,21 +591,36 @@ __global__ void __launch_bounds__(256) k_ntt256_rows(u64 *__restrict__ data, Row
     const int rb = (blockIdx.x << 4) + blk;
     u64 *a = data + ((size_t)row << 16) + ((size_t)rb << 8);
     const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
+    const double *Wq = twq + ((size_t)p << 16);
     u64 *sb = sm + blk * 272;  // 256 elements of this block, 17-word rows of 16 (padding)
     u64 x[16];
     if (!INV) {
+        const bool nc = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[c + 16 * k];
-        fwd_a(x, W, Wp, 256 + rb, q);
+        if (nc)
+            fwd_a_nc(x, W, Wq, 256 + rb, q);
+        else
+            fwd_a(x, W, Wp, 256 + rb, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[k * 17 + c] = x[k];  // element c + 16k at (k, c)
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];  // element 16c + k
-        fwd_b(x, W, Wp, 256 + rb, c, q);
+        if (nc) {
+            // values below 33q: one Barrett step with floor(2^64/q)
+            fwd_b_nc(x, W, Wq, 256 + rb, c, q);
+            const u64 onep = c_pc[p].onep;
+#pragma unroll
+            for (int k = 0; k < 16; k++) x[k] = mul_shoup(x[k], 1ull, onep, q);
+        } else {
+            fwd_b(x, W, Wp, 256 + rb, c, q);
+#pragma unroll
+            for (int k = 0; k < 16; k++) x[k] = reduce4q(x[k], q);
+        }
         __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) sb[c * 17 + k] = reduce4q(x[k], q);
+        for (int k = 0; k < 16; k++) sb[c * 17 + k] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) a[c + 16 * k] = sb[k * 17 + c];
@@ -518,16 +628,23 @@ __global__ void __launch_bounds__(256) k_ntt256_rows(u64 *__restrict__ data, Row
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[k * 17 + c] = a[c + 16 * k];
         __syncthreads();
+        const bool fq = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];
-        inv_b(x, W, Wp, 256 + rb, c, q);
+        if (fq)
+            inv_b_fq(x, W, Wq, 256 + rb, c, q);
+        else
+            inv_b(x, W, Wp, 256 + rb, c, q);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[c * 17 + k] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[k * 17 + c];
-        inv_a(x, W, Wp, 256 + rb, q);
+        if (fq)
+            inv_a_fq(x, W, Wq, 256 + rb, q);
+        else
+            inv_a(x, W, Wp, 256 + rb, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) a[c + 16 * k] = x[k];  // [0, 2q): the column pass reduces
     }
@@ -538,11 +655,11 @@ static void ntt256_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bo
         const int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
         const dim3 grid(16, nr);
         if (!inv) {
-            k_ntt256_cols<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, r0);
-            k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, r0);
+            k_ntt256_cols<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twq, r0);
+            k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twq, r0);
         } else {
-            k_ntt256_rows<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, r0);
-            k_ntt256_cols<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, r0);
+            k_ntt256_rows<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwq, r0);
+            k_ntt256_cols<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwq, r0);
         }
     }
 }
