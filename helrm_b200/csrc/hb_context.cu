@@ -217,9 +217,9 @@ public:
         upload_prime_consts(pcs.data(), P);
 
         // twiddles
-        // [4][P][N] u64 twiddles and Shoup companions, then [2][P][N] doubles
-        // fl(w / q) for primes below 2^40 (quotient estimates of the NTT)
-        std::vector<u64> tw((size_t)6 * P * N, 0);
+        // [4][P][N] u64 twiddles and Shoup companions, then [2][P][N] pairs
+        // {w, fl(w/q)} for primes below 2^40 (quotient estimates of the NTT)
+        std::vector<u64> tw((size_t)8 * P * N, 0);
         for (int p = 0; p < P; p++) {
             u64 q = primes[p];
             u64 psi = find_psi(q, logN), ipsi = h_invm(psi, q);
@@ -238,11 +238,15 @@ public:
                 Ip[i] = h_shoup(I[i], q);
             }
             if (q < (1ull << 40)) {
-                double *Tq = reinterpret_cast<double *>(&tw[(size_t)(4 * P + p) * N]);
-                double *Iq = reinterpret_cast<double *>(&tw[(size_t)(5 * P + p) * N]);
+                u64 *Tx = &tw[(size_t)4 * P * N + (size_t)p * 2 * N];
+                u64 *Ix = &tw[(size_t)6 * P * N + (size_t)p * 2 * N];
                 for (int i = 0; i < N; i++) {
-                    Tq[i] = (double)T[i] / (double)q;  // both exact doubles: correctly rounded
-                    Iq[i] = (double)I[i] / (double)q;
+                    // both operands exact doubles: the quotient is correctly rounded
+                    const double tq = (double)T[i] / (double)q, iq = (double)I[i] / (double)q;
+                    Tx[2 * i] = T[i];
+                    std::memcpy(&Tx[2 * i + 1], &tq, 8);
+                    Ix[2 * i] = I[i];
+                    std::memcpy(&Ix[2 * i + 1], &iq, 8);
                 }
             }
         }
@@ -252,8 +256,8 @@ public:
         ntt.twp = d_tables + (size_t)P * N;
         ntt.itw = d_tables + (size_t)2 * P * N;
         ntt.itwp = d_tables + (size_t)3 * P * N;
-        ntt.twq = reinterpret_cast<const double *>(d_tables + (size_t)4 * P * N);
-        ntt.itwq = reinterpret_cast<const double *>(d_tables + (size_t)5 * P * N);
+        ntt.twx = reinterpret_cast<const ulonglong2 *>(d_tables + (size_t)4 * P * N);
+        ntt.itwx = reinterpret_cast<const ulonglong2 *>(d_tables + (size_t)6 * P * N);
         ntt.logN = logN;
 
         std::vector<u64> pm(P);

@@ -138,27 +138,6 @@ __device__ __forceinline__ void ct_bfly(u64 &x, u64 &y, u64 w, u64 wp, u64 q) {
     y = x + two_q - t;
     x = x + t;
 }
-// Forward butterfly without the correction of x, for q below 2^40: with
-// inputs below B the outputs stay below B + 2q (Shoup's lazy product is
-// below 2q for any 64-bit input), so the 16 stages of a 2^16-point
-// transform end below 33q < 2^46 and one reduction per element follows.
-// The twiddle product uses the double-precision quotient (mul_fq_lazy),
-// valid for these inputs (below 2^46).
-__device__ __forceinline__ void ct_bfly_nc(u64 &x, u64 &y, u64 w, double wq, u64 q, u64 two_q) {
-    const u64 t = mul_fq_lazy(y, w, wq, q);
-    y = x + two_q - t;
-    x = x + t;
-}
-// Inverse butterfly for q below 2^40 with the double-precision quotient:
-// values stay in [0, 2q) as in gs_bfly.
-__device__ __forceinline__ void gs_bfly_fq(u64 &x, u64 &y, u64 w, double wq, u64 q) {
-    const u64 two_q = 2 * q;
-    u64 s = x + y;
-    if (s >= two_q) s -= two_q;
-    const u64 d = x + two_q - y;
-    x = s;
-    y = mul_fq_lazy(d, w, wq, q);
-}
 __device__ __forceinline__ void gs_bfly(u64 &x, u64 &y, u64 w, u64 wp, u64 q) {
     const u64 two_q = 2 * q;
     u64 s = x + y;
@@ -433,58 +412,6 @@ __device__ __forceinline__ void fwd_b(u64 (&x)[16], const u64 *W, const u64 *Wp,
         }
     }
 }
-// the same two forward halves with uncorrected butterflies (q < 2^40)
-__device__ __forceinline__ void fwd_a_nc(u64 (&x)[16], const u64 *W, const double *Wq, int base, u64 q) {
-    const u64 two_q = 2 * q;
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-        const int d = 8 >> s, g = 1 << s;
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            const int wi = g * base + (k >> (4 - s));
-            ct_bfly_nc(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q, two_q);
-        }
-    }
-}
-__device__ __forceinline__ void fwd_b_nc(u64 (&x)[16], const u64 *W, const double *Wq, int base, int c, u64 q) {
-    const u64 two_q = 2 * q;
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-        const int d = 8 >> s, g = 16 << s;
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            const int wi = g * base + (c << s) + (k >> (4 - s));
-            ct_bfly_nc(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q, two_q);
-        }
-    }
-}
-// inverse halves with the double-precision quotient (q < 2^40)
-__device__ __forceinline__ void inv_b_fq(u64 (&x)[16], const u64 *W, const double *Wq, int base, int c, u64 q) {
-#pragma unroll
-    for (int s = 3; s >= 0; s--) {
-        const int d = 8 >> s, g = 16 << s;
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            const int wi = g * base + (c << s) + (k >> (4 - s));
-            gs_bfly_fq(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q);
-        }
-    }
-}
-__device__ __forceinline__ void inv_a_fq(u64 (&x)[16], const u64 *W, const double *Wq, int base, u64 q) {
-#pragma unroll
-    for (int s = 3; s >= 0; s--) {
-        const int d = 8 >> s, g = 1 << s;
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            const int wi = g * base + (k >> (4 - s));
-            gs_bfly_fq(x[k], x[k + d], __ldg(W + wi), __ldg(Wq + wi), q);
-        }
-    }
-}
 // inverse, layout B, groups 128, 64, 32, 16 (distances 1..8)
 __device__ __forceinline__ void inv_b(u64 (&x)[16], const u64 *W, const u64 *Wp, int base, int c, u64 q) {
 #pragma unroll
@@ -514,39 +441,118 @@ __device__ __forceinline__ void inv_a(u64 (&x)[16], const u64 *W, const u64 *Wp,
     }
 }
 
+// ---- primes below 2^40: twiddle pairs {w, fl(w/q)} and the double-precision
+// quotient of mul_fq_c.  Forward butterflies are left uncorrected: with
+// inputs below B, x + q +- (y*w mod q centred) stays below B + 1.52q, so the
+// 16 stages end below 26q < 2^45 and one reduction per element follows.
+// The inverse keeps Gentleman-Sande values in [0, 2q).
+template <bool G>
+__device__ __forceinline__ ulonglong2 twld(const ulonglong2 *t, int i) {
+    if (G) return __ldg(t + i);
+    return t[i];
+}
+__device__ __forceinline__ void ct_bfly_f(u64 &x, u64 &y, ulonglong2 tw, u64 q, u64 nq) {
+    const u64 P = mul_fq_c(y, tw.x, __longlong_as_double((long long)tw.y), nq);
+    const u64 xq = x + q;
+    x = xq + P;
+    y = xq - P;
+}
+__device__ __forceinline__ void gs_bfly_f(u64 &x, u64 &y, ulonglong2 tw, u64 q, u64 nq) {
+    const u64 two_q = 2 * q;
+    u64 s = x + y;
+    if (s >= two_q) s -= two_q;
+    const u64 d = x + two_q - y;
+    x = s;
+    y = mul_fq_c(d, tw.x, __longlong_as_double((long long)tw.y), nq) + q;
+}
+template <bool G>
+__device__ __forceinline__ void fwd_a_f(u64 (&x)[16], const ulonglong2 *T, int base, u64 q, u64 nq) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 1 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            ct_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (k >> (4 - s))), q, nq);
+        }
+    }
+}
+template <bool G>
+__device__ __forceinline__ void fwd_b_f(u64 (&x)[16], const ulonglong2 *T, int base, int c, u64 q, u64 nq) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 16 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            ct_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (c << s) + (k >> (4 - s))), q, nq);
+        }
+    }
+}
+template <bool G>
+__device__ __forceinline__ void inv_b_f(u64 (&x)[16], const ulonglong2 *T, int base, int c, u64 q, u64 nq) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 16 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            gs_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (c << s) + (k >> (4 - s))), q, nq);
+        }
+    }
+}
+template <bool G>
+__device__ __forceinline__ void inv_a_f(u64 (&x)[16], const ulonglong2 *T, int base, u64 q, u64 nq) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 1 << s;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            gs_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (k >> (4 - s))), q, nq);
+        }
+    }
+}
+
 // Column pass: the 16 columns c0..c0+15, element (r, col) at r*256 + c0 + col.
+// Primes below 2^40 take twiddle pairs {w, fl(w/q)} (the first 256
+// entries, the same for every block, staged in shared memory); the others
+// Shoup pairs from global memory.
 template <bool INV>
 __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
                                                       const u64 *__restrict__ twp,
-                                                      const double *__restrict__ twq, int row0) {
+                                                      const ulonglong2 *__restrict__ twx, int row0) {
     __shared__ u64 sm[256 * 17];
+    __shared__ ulonglong2 stw[256];
     const int row = row0 + blockIdx.y;
     if (map.skip(row)) return;
     const int p = map.prime(row);
     const u64 q = c_pc[p].q;
+    const bool fast = q < (1ull << 40);
+    const u64 nq = 0ull - q;
     const int col = threadIdx.x & 15, c = threadIdx.x >> 4;
     const int c0 = blockIdx.x << 4;
     u64 *a = data + ((size_t)row << 16) + c0 + col;
     const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
-    const double *Wq = twq + ((size_t)p << 16);
+    if (fast) stw[threadIdx.x] = __ldg(twx + ((size_t)p << 16) + threadIdx.x);
     u64 x[16];
     if (!INV) {
-        // q < 2^40: uncorrected butterflies, the column pass leaves values
-        // below 17q for the block pass; otherwise Harvey's [0, 4q) form
-        const bool nc = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(c + 16 * k) << 8];
-        if (nc)
-            fwd_a_nc(x, W, Wq, 1, q);
-        else
+        if (fast) {
+            __syncthreads();
+            fwd_a_f<false>(x, stw, 1, q, nq);
+        } else {
             fwd_a(x, W, Wp, 1, q);
+        }
 #pragma unroll
         for (int k = 0; k < 16; k++) sm[(c + 16 * k) * 17 + col] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sm[(16 * c + k) * 17 + col];
-        if (nc) {
-            fwd_b_nc(x, W, Wq, 1, c, q);
+        if (fast) {
+            // left uncorrected (below 14q) for the block pass
+            fwd_b_f<false>(x, stw, 1, c, q, nq);
 #pragma unroll
             for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = x[k];
         } else {
@@ -555,20 +561,21 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
             for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = reduce4q(x[k], q);
         }
     } else {
-        const bool fq = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(16 * c + k) << 8];
-        if (fq)
-            inv_b_fq(x, W, Wq, 1, c, q);
-        else
+        if (fast) {
+            __syncthreads();
+            inv_b_f<false>(x, stw, 1, c, q, nq);
+        } else {
             inv_b(x, W, Wp, 1, c, q);
+        }
 #pragma unroll
         for (int k = 0; k < 16; k++) sm[(16 * c + k) * 17 + col] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sm[(c + 16 * k) * 17 + col];
-        if (fq)
-            inv_a_fq(x, W, Wq, 1, q);
+        if (fast)
+            inv_a_f<false>(x, stw, 1, q, nq);
         else
             inv_a(x, W, Wp, 1, q);
         const u64 ni = c_pc[p].ninv, nip = c_pc[p].ninvp;
@@ -581,25 +588,26 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
 template <bool INV>
 __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
                                                       const u64 *__restrict__ twp,
-                                                      const double *__restrict__ twq, int row0) {
+                                                      const ulonglong2 *__restrict__ twx, int row0) {
     __shared__ u64 sm[16 * 272];
     const int row = row0 + blockIdx.y;
     if (map.skip(row)) return;
     const int p = map.prime(row);
     const u64 q = c_pc[p].q;
+    const bool fast = q < (1ull << 40);
+    const u64 nq = 0ull - q;
     const int c = threadIdx.x & 15, blk = threadIdx.x >> 4;
     const int rb = (blockIdx.x << 4) + blk;
     u64 *a = data + ((size_t)row << 16) + ((size_t)rb << 8);
     const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
-    const double *Wq = twq + ((size_t)p << 16);
+    const ulonglong2 *T = twx + ((size_t)p << 16);
     u64 *sb = sm + blk * 272;  // 256 elements of this block, 17-word rows of 16 (padding)
     u64 x[16];
     if (!INV) {
-        const bool nc = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[c + 16 * k];
-        if (nc)
-            fwd_a_nc(x, W, Wq, 256 + rb, q);
+        if (fast)
+            fwd_a_f<true>(x, T, 256 + rb, q, nq);
         else
             fwd_a(x, W, Wp, 256 + rb, q);
 #pragma unroll
@@ -607,9 +615,9 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];  // element 16c + k
-        if (nc) {
-            // values below 33q: one Barrett step with floor(2^64/q)
-            fwd_b_nc(x, W, Wq, 256 + rb, c, q);
+        if (fast) {
+            // values below 26q: one Barrett step with floor(2^64/q)
+            fwd_b_f<true>(x, T, 256 + rb, c, q, nq);
             const u64 onep = c_pc[p].onep;
 #pragma unroll
             for (int k = 0; k < 16; k++) x[k] = mul_shoup(x[k], 1ull, onep, q);
@@ -628,11 +636,10 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[k * 17 + c] = a[c + 16 * k];
         __syncthreads();
-        const bool fq = q < (1ull << 40);
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];
-        if (fq)
-            inv_b_fq(x, W, Wq, 256 + rb, c, q);
+        if (fast)
+            inv_b_f<true>(x, T, 256 + rb, c, q, nq);
         else
             inv_b(x, W, Wp, 256 + rb, c, q);
         __syncthreads();
@@ -641,8 +648,8 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[k * 17 + c];
-        if (fq)
-            inv_a_fq(x, W, Wq, 256 + rb, q);
+        if (fast)
+            inv_a_f<true>(x, T, 256 + rb, q, nq);
         else
             inv_a(x, W, Wp, 256 + rb, q);
 #pragma unroll
@@ -655,11 +662,11 @@ static void ntt256_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bo
         const int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
         const dim3 grid(16, nr);
         if (!inv) {
-            k_ntt256_cols<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twq, r0);
-            k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twq, r0);
+            k_ntt256_cols<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twx, r0);
+            k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twx, r0);
         } else {
-            k_ntt256_rows<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwq, r0);
-            k_ntt256_cols<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwq, r0);
+            k_ntt256_rows<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwx, r0);
+            k_ntt256_cols<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwx, r0);
         }
     }
 }
