@@ -27,10 +27,38 @@ __device__ __forceinline__ void mac_split_packed(Split3 &s, u64 a_packed, u64 b_
     split_mac(s, (unsigned)a_packed, (unsigned)(a_packed >> 32), (unsigned)b_packed, (unsigned)(b_packed >> 32));
 }
 
+// 16-byte asynchronous copy global -> shared (bypassing L1), grouped by
+// commit and waited for with wait_group.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 }  // namespace
+
+// Shared-memory words of one launch (descriptors, key tiles, R tile, two
+// gather buffers, rotation tables).
+__host__ __device__ inline size_t bsgs_smem_words(int beta) {
+    return (size_t)HB_BCH * (sizeof(BabyDesc) / 8) + (size_t)HB_BCH * beta * 2 * HB_BT + (size_t)HB_BCH * 2 * HB_BT +
+           (size_t)2 * HB_BCH * (beta + 1) * HB_BT + (size_t)HB_BCH * HB_BT / 8 + HB_BCH / 2;
+}
 
 // NBF = HB_BCH: a full chunk, the baby count is a compile-time constant and
 // the unrolled loops carry no guards; NBF = 0: the count is read at run time.
+//
+// The automorphism X -> X^g maps every aligned tile of 16 coefficients (in
+// the bit-reversed NTT order) onto another aligned tile of 16, permuted:
+// for t = n0 + i the low 4 bits of t land in the top bits of brv(t), and
+// multiplying 2 brv(t) + 1 by g leaves the low logN - 3 bits unchanged by i,
+// so the high logN - 4 bits of tau(t) are those of tau(n0).  A baby's
+// gathers for a tile are therefore one contiguous 128-byte segment per
+// digit row, fetched with asynchronous copies one batch item ahead of the
+// arithmetic (double buffer); the in-tile permutation is a table built once.
 template <int NBF>
 __global__ void __launch_bounds__(kThreads, 2)
     k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
@@ -46,15 +74,30 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool fast = pc.q < (1ull << 40);
     const int tid = threadIdx.x;
     const int nb = NBF ? NBF : ch.nbabies;
+    const int R1 = beta + 1;  // gathered rows per baby: beta digits, then c0
 
-    // shared memory: descriptors | key tiles [nb][beta][2][BT] | R [nb][2][BT]
+    // shared memory: descriptors | key tiles [nb][beta][2][BT] | R [nb][BT][2]
+    // | gathers [2][nb][beta+1][BT] | in-tile offsets [nb][BT] (bytes) |
+    // source tile bases [nb]
     BabyDesc *sdesc = reinterpret_cast<BabyDesc *>(sm);
     u64 *skey = sm + (size_t)HB_BCH * (sizeof(BabyDesc) / 8);
     u64 *sR = skey + (size_t)HB_BCH * beta * 2 * HB_BT;
+    u64 *sG = sR + (size_t)HB_BCH * 2 * HB_BT;
+    unsigned char *soff = reinterpret_cast<unsigned char *>(sG + (size_t)2 * HB_BCH * R1 * HB_BT);
+    unsigned *sblk = reinterpret_cast<unsigned *>(soff + HB_BCH * HB_BT);
+    const size_t gbuf = (size_t)nb * R1 * HB_BT;
 
     for (int i = tid; i < nb * (int)(sizeof(BabyDesc) / 8); i += kThreads)
         sm[i] = reinterpret_cast<const u64 *>(ch.babies)[i];
     __syncthreads();
+    // rotation tables: tile base of tau(n0) and in-tile offsets
+    for (int i = tid; i < nb * HB_BT; i += kThreads) {
+        const int bb = i / HB_BT, n = i % HB_BT;
+        const u64 g = sdesc[bb].galois;
+        const unsigned src = sdesc[bb].key ? aut_index((unsigned)(n0 + n), g, logN) : (unsigned)(n0 + n);
+        soff[i] = (unsigned char)(src & (HB_BT - 1));
+        if (n == 0) sblk[bb] = src & ~(unsigned)(HB_BT - 1);
+    }
     // key tiles (split form on fast limbs)
     {
         const int per = beta * 2 * HB_BT;
@@ -66,6 +109,41 @@ __global__ void __launch_bounds__(kThreads, 2)
             skey[i] = fast ? split_pack(v) : v;
         }
     }
+    __syncthreads();
+
+    // 32-bit element offsets inside one ciphertext's digits / c0 (the whole
+    // extended digit stack of one ciphertext stays far below 2^32 words)
+    const unsigned dstride = (unsigned)ne << logN;
+    const unsigned erow = (unsigned)e << logN;
+    const size_t nall = (size_t)ne << logN;
+
+    // asynchronous gathers of batch item b into buffer buf: for a rotated
+    // baby the beta digit rows and c0 at its source tile, for the identity
+    // baby c0 and c1 at the tile itself (rows 0 and 1); c-rows exist only on
+    // the q limbs
+    auto issue = [&](int b, int buf) {
+        const u64 *c0b = ct + b * ct_stride;
+        const u64 *Db = D + b * d_stride;
+        u64 *Gb = sG + buf * gbuf;
+        const int nchunk = nb * R1 * (HB_BT / 2);
+        for (int i = tid; i < nchunk; i += kThreads) {
+            const int bb = i / (R1 * (HB_BT / 2)), r = (i / (HB_BT / 2)) % R1, k = i % (HB_BT / 2);
+            const u64 *src;
+            if (sdesc[bb].key == nullptr) {
+                if (e >= nq || r >= 2) continue;
+                src = c0b + ((size_t)r * nq << logN) + erow + n0;
+            } else if (r < beta) {
+                src = Db + (size_t)r * dstride + erow + sblk[bb];
+            } else {
+                if (e >= nq) continue;
+                src = c0b + erow + sblk[bb];
+            }
+            cp_async16(Gb + ((size_t)bb * R1 + r) * HB_BT + 2 * k, src + 2 * k);
+        }
+        cp_async_commit();
+    };
+    issue(0, 0);
+
     // plaintexts of (giant slot gi, baby bb) at this thread's coefficient
     const int gi = tid / HB_BT, nl = tid % HB_BT;
     const bool gactive = gi < ch.gcount;
@@ -85,49 +163,40 @@ __global__ void __launch_bounds__(kThreads, 2)
         pq = pmod_q[e];
         pq_packed = split_pack(pq);
     }
-    __syncthreads();
 
-    // 32-bit element offsets inside one ciphertext's digits / c0 (the whole
-    // extended digit stack of one ciphertext stays far below 2^32 words)
-    const unsigned dstride = (unsigned)ne << logN;
-    const unsigned erow = (unsigned)e << logN;
-    const size_t nall = (size_t)ne << logN;
     for (int b = 0; b < nbatch; b++) {
-        const u64 *c0 = ct + b * ct_stride;
-        const u64 *c1 = c0 + ((size_t)nq << logN);
-        const u64 *Dbe = D + b * d_stride + erow;
-        // ---- phase A: baby rotations of this tile.  The gathers of an item
-        // (beta digits at the rotated index, and c0) are all issued before
-        // any of them is used, so their latencies overlap.
+        if (b + 1 < nbatch) {
+            issue(b + 1, (b + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const u64 *Gb = sG + (b & 1) * gbuf;
+        // ---- phase A: baby rotations of this tile, from the gathered rows
 #pragma unroll
         for (int it0 = 0; it0 < (NBF ? NBF * HB_BT : HB_BCH * HB_BT); it0 += kThreads) {
             const int it = it0 + tid;
             if (!NBF && it >= nb * HB_BT) break;
             const int bb = it / HB_BT, n = it % HB_BT;
-            const unsigned t = (unsigned)(n0 + n);
-            const BabyDesc &bd = sdesc[bb];
+            const u64 *g = Gb + (size_t)bb * R1 * HB_BT;
             u64 rb, ra;
-            if (bd.key == nullptr) {
-                rb = e < nq ? mul_mod(pq, c0[erow + t], pc) : 0;
-                ra = e < nq ? mul_mod(pq, c1[erow + t], pc) : 0;
+            if (sdesc[bb].key == nullptr) {
+                rb = e < nq ? mul_mod(pq, g[n], pc) : 0;
+                ra = e < nq ? mul_mod(pq, g[HB_BT + n], pc) : 0;
             } else {
-                const unsigned src = aut_index(t, bd.galois, logN);
+                const int so = soff[it];
                 const u64 *kt = skey + (size_t)bb * beta * 2 * HB_BT + n;
-                u64 dv[HB_MAX_BETA];
-#pragma unroll
-                for (int j = 0; j < HB_MAX_BETA; j++)
-                    if (j < beta) dv[j] = Dbe[(unsigned)j * dstride + src];
-                const u64 cv = e < nq ? c0[erow + src] : 0;
                 if (fast) {
                     Split3 sb = {0, 0, 0}, sa = {0, 0, 0};
 #pragma unroll
                     for (int j = 0; j < HB_MAX_BETA; j++)
                         if (j < beta) {
-                            const u64 d = split_pack(dv[j]);
+                            const u64 d = split_pack(g[j * HB_BT + so]);
                             mac_split_packed(sb, d, kt[(j * 2 + 0) * HB_BT]);
                             mac_split_packed(sa, d, kt[(j * 2 + 1) * HB_BT]);
                         }
-                    if (e < nq) mac_split_packed(sb, pq_packed, split_pack(cv));
+                    if (e < nq) mac_split_packed(sb, pq_packed, split_pack(g[beta * HB_BT + so]));
                     rb = split_reduce(sb, pc);
                     ra = split_reduce(sa, pc);
                 } else {
@@ -135,16 +204,18 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                     for (int j = 0; j < HB_MAX_BETA; j++)
                         if (j < beta) {
-                            mac128(sb, dv[j], kt[(j * 2 + 0) * HB_BT]);
-                            mac128(sa, dv[j], kt[(j * 2 + 1) * HB_BT]);
+                            const u64 d = g[j * HB_BT + so];
+                            mac128(sb, d, kt[(j * 2 + 0) * HB_BT]);
+                            mac128(sa, d, kt[(j * 2 + 1) * HB_BT]);
                         }
-                    if (e < nq) mac128(sb, pq, cv);
+                    if (e < nq) mac128(sb, pq, g[beta * HB_BT + so]);
                     rb = reduce128(sb, pc);
                     ra = reduce128(sa, pc);
                 }
             }
-            sR[(bb * 2 + 0) * HB_BT + n] = fast ? split_pack(rb) : rb;
-            sR[(bb * 2 + 1) * HB_BT + n] = fast ? split_pack(ra) : ra;
+            // R tile interleaved {b, a} per coefficient: one 16-byte read in phase B
+            reinterpret_cast<ulonglong2 *>(sR)[bb * HB_BT + n] =
+                fast ? make_ulonglong2(split_pack(rb), split_pack(ra)) : make_ulonglong2(rb, ra);
         }
         __syncthreads();
         // ---- phase B: inner[g] += pt(g, b) * R_b.  Split sums: S0 takes 16
@@ -152,14 +223,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         // instructions); one reduction per output.  128-bit sums of at most
         // 32 products below 2^122 need no intermediate reduction.
         if (gactive) {
+            const ulonglong2 *R2 = reinterpret_cast<const ulonglong2 *>(sR) + nl;
             u64 vb, va;
             if (fast) {
                 Split3 ab = {0, 0, 0}, aa = {0, 0, 0};
 #pragma unroll
                 for (int bb = 0; bb < HB_BCH; bb++) {
                     if (NBF || bb < nb) {
-                        mac_split_packed(ab, ptv[bb], sR[(bb * 2 + 0) * HB_BT + nl]);
-                        mac_split_packed(aa, ptv[bb], sR[(bb * 2 + 1) * HB_BT + nl]);
+                        const ulonglong2 r = R2[bb * HB_BT];
+                        mac_split_packed(ab, ptv[bb], r.x);
+                        mac_split_packed(aa, ptv[bb], r.y);
                         if (bb == 15) {
                             split_normalize(ab);
                             split_normalize(aa);
@@ -173,8 +246,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                 for (int bb = 0; bb < HB_BCH; bb++) {
                     if (NBF || bb < nb) {
-                        mac128(ab, ptv[bb], sR[(bb * 2 + 0) * HB_BT + nl]);
-                        mac128(aa, ptv[bb], sR[(bb * 2 + 1) * HB_BT + nl]);
+                        const ulonglong2 r = R2[bb * HB_BT];
+                        mac128(ab, ptv[bb], r.x);
+                        mac128(aa, ptv[bb], r.y);
                     }
                 }
                 vb = reduce128(ab, pc);

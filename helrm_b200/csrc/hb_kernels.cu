@@ -1416,7 +1416,7 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
                    int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride, size_t d_stride,
                    size_t inner_stride, cudaStream_t s) {
     if (ch.nbabies > HB_BCH || ch.gcount > HB_GCH) throw std::invalid_argument("bsgs chunk too large");
-    const size_t smem = HB_BCH * sizeof(BabyDesc) + (size_t)HB_BCH * beta * 2 * HB_BT * 8 + (size_t)HB_BCH * 2 * HB_BT * 8;
+    const size_t smem = bsgs_smem_words(beta) * 8;
     if (smem > 227 * 1024 || beta > HB_MAX_BETA)
         throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
     static size_t attr = 0;
