@@ -26,33 +26,12 @@ struct PrimeConst {
     u64 onep;     // floor(2^64 / q) (Shoup companion of 1)
     u64 ninv;     // N^-1 mod q
     u64 ninvp;
-    u64 c30, c30p;  // 2^30 mod q (split-product recombination)
     u64 c60, c60p;  // 2^60 mod q
+    u64 c58, c58p;  // 2^58 mod q (Karatsuba split-29 recombination)
 };
 
-// Split-30 products for residues below 2^40: a = ah*2^30 + al (al < 2^30,
-// ah < 2^10).  A sum of products is kept as S0 + S1*2^30 + S2*2^60 with
-// S0 = sum al*bl (< 2^60 per term, at most 16 terms), S1 = sum al*bh +
-// ah*bl (< 2^41 per term), S2 = sum ah*bh (< 2^20 per term); each term is
-// four 32x32 multiply-adds instead of a 64x64->128 product.
 #define HB_SPLIT_MASK 0x3FFFFFFFull
-struct Split3 {
-    u64 s0, s1;
-    unsigned s2;
-};
-__device__ __forceinline__ void split_mac(Split3 &acc, unsigned al, unsigned ah, unsigned bl, unsigned bh) {
-    // one 32x32+64 multiply-add each (mad.wide.u32)
-    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s0) : "r"(al), "r"(bl));
-    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s1) : "r"(al), "r"(bh));
-    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s1) : "r"(ah), "r"(bl));
-    acc.s2 += ah * bh;
-}
-// Moves the bits of S0 above 2^30 into S1 (same value), so S0 can take 16
-// more terms.  S1 gains < 2^34 per call.
-__device__ __forceinline__ void split_normalize(Split3 &acc) {
-    acc.s1 += acc.s0 >> 30;
-    acc.s0 &= 0x3FFFFFFFull;
-}
+// split-30 packed form (v >> 30) << 32 | (v mod 2^30), for v < 2^62
 __device__ __forceinline__ u64 split_pack(u64 v) { return ((v >> 30) << 32) | (v & HB_SPLIT_MASK); }
 
 __device__ __forceinline__ u64 add_mod(u64 a, u64 b, u64 q) {
@@ -124,15 +103,37 @@ __device__ __forceinline__ u64 reduce128(const u128 &x, const PrimeConst &pc) {
 __device__ __forceinline__ u64 mul_mod(u64 a, u64 b, const PrimeConst &pc) {
     return reduce128(__umul64hi(a, b), a * b, pc);
 }
-// (S0 + S1 2^30 + S2 2^60) mod q, for S1 < 2^62 and S2 < 2^32: the value is
-// first rewritten as lo + hi 2^60 with lo < 2^60 (carries of S0 into S1 and
-// of S1 into S2), then hi 2^60 is folded with 2^60 mod q (a lazy Shoup
-// product, < 2q) and the sum (< 2^61) reduced once with floor(2^64/q).
-__device__ __forceinline__ u64 split_reduce(const Split3 &s, const PrimeConst &pc) {
-    const u64 s1 = s.s1 + (s.s0 >> 30);
-    const u64 lo = (s.s0 & HB_SPLIT_MASK) | ((s1 & HB_SPLIT_MASK) << 30);
-    const u64 hi = (u64)s.s2 + (s1 >> 30);
-    const u64 v = lo + mul_shoup_lazy(hi, pc.c60, pc.c60p, pc.q);
+// Karatsuba split-29 sums of products, both factors below 2^40: a = ah 2^29
+// + al (al < 2^29, ah < 2^11), same for b.  A sum of up to 33 products is
+// kept as S0 = sum al*bl (< 2^58 per term), M = sum (al+ah)(bl+bh) (< 2^58.01
+// per term) and S2 = sum ah*bh (< 2^22 per term), none of which can
+// overflow its word; the middle sum S1 = M - S0 - S2 (< 2^47) is exact in
+// 64-bit arithmetic.  Two 32x32->64 multiply-adds and one 32-bit
+// multiply-add per product.  The caller passes the sum bl + bh, which it
+// usually shares between products.
+#define HB_K29_MASK 0x1FFFFFFFull
+struct Kara29 {
+    u64 s0, m;
+    unsigned s2;
+};
+__device__ __forceinline__ u64 k29_pack(u64 v) { return ((v >> 29) << 32) | (v & HB_K29_MASK); }
+__device__ __forceinline__ unsigned k29_sum(u64 packed) { return (unsigned)packed + (unsigned)(packed >> 32); }
+__device__ __forceinline__ void k29_mac(Kara29 &acc, u64 a_packed, u64 b_packed, unsigned b_sum) {
+    const unsigned al = (unsigned)a_packed, ah = (unsigned)(a_packed >> 32);
+    const unsigned bl = (unsigned)b_packed, bh = (unsigned)(b_packed >> 32);
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s0) : "r"(al), "r"(bl));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.m) : "r"(al + ah), "r"(b_sum));
+    acc.s2 += ah * bh;
+}
+// (S0 + S1 2^29 + S2 2^58) mod q: carries give lo + hi 2^58 with lo < 2^58,
+// hi 2^58 is folded with 2^58 mod q (lazy Shoup, < 2q) and the sum reduced
+// once with floor(2^64/q).
+__device__ __forceinline__ u64 k29_reduce(const Kara29 &a, const PrimeConst &pc) {
+    const u64 s1 = a.m - a.s0 - a.s2;
+    const u64 t = s1 + (a.s0 >> 29);
+    const u64 lo = (a.s0 & HB_K29_MASK) | ((t & HB_K29_MASK) << 29);
+    const u64 hi = (u64)a.s2 + (t >> 29);
+    const u64 v = lo + mul_shoup_lazy(hi, pc.c58, pc.c58p, pc.q);
     return mul_shoup(v, 1ull, pc.onep, pc.q);
 }
 
@@ -167,7 +168,9 @@ __device__ __forceinline__ void splitw_normalize(SplitW &acc) {
     acc.s1 &= HB_SPLIT_MASK;
 }
 // (S0 + S1 2^30 + S2 2^60) mod q for S0 < 2^64, S1 < 2^64 - 2^34, S2 < 2^63
-// and any q < 2^62: lo + hi 2^60 with lo < 2^60 as in split_reduce.
+// and any q < 2^62: carries of S0 into S1 and of S1 into S2 give lo + hi 2^60
+// with lo < 2^60, hi 2^60 is folded with 2^60 mod q (lazy Shoup, < 2q) and
+// the sum reduced once with floor(2^64/q).
 __device__ __forceinline__ u64 splitw_reduce(const SplitW &s, const PrimeConst &pc) {
     const u64 s1 = s.s1 + (s.s0 >> 30);
     const u64 lo = (s.s0 & HB_SPLIT_MASK) | ((s1 & HB_SPLIT_MASK) << 30);

@@ -1,4 +1,4 @@
-// hb_bsgs.cu -- the fused baby-step + diagonal-MAC kernel of the
+// hb_bsgs.cuh -- the fused baby-step + diagonal-MAC kernel of the
 // double-hoisted BSGS linear transform (the embedding PCMM's hot loop).
 //
 // For one extended limb e and a tile of HB_BT coefficients, over every
@@ -11,9 +11,10 @@
 // memory and each thread its plaintext values in registers, so keys and
 // diagonals stream from HBM once per batch while the ciphertext data
 // (digits D, c0, inner sums) streams once per ciphertext.  Residues below
-// 2^40 (the 36-bit q limbs) multiply with the split-30 form, four 32-bit
-// multiply-adds per product; the 60-bit special-prime limbs use 64x64->128
-// products.  Accumulation is lazy: one modular reduction per output.
+// 2^40 (the 36-bit q limbs) multiply in the Karatsuba split-29 form, two
+// 32x32->64 and one 32-bit multiply-add per product; the 60-bit
+// special-prime limbs use 64x64->128 products.  Accumulation is lazy: one
+// modular reduction per output.
 // Included by hb_kernels.cu (it reads the per-prime __constant__ table).
 #pragma once
 
@@ -22,10 +23,6 @@ namespace hb {
 namespace {
 
 constexpr int kThreads = HB_GCH * HB_BT;  // 256: half a warp per giant slot
-
-__device__ __forceinline__ void mac_split_packed(Split3 &s, u64 a_packed, u64 b_packed) {
-    split_mac(s, (unsigned)a_packed, (unsigned)(a_packed >> 32), (unsigned)b_packed, (unsigned)(b_packed >> 32));
-}
 
 // 16-byte asynchronous copy global -> shared (bypassing L1), grouped by
 // commit and waited for with wait_group.
@@ -98,7 +95,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         soff[i] = (unsigned char)(src & (HB_BT - 1));
         if (n == 0) sblk[bb] = src & ~(unsigned)(HB_BT - 1);
     }
-    // key tiles (split form on fast limbs)
+    // key tiles (split-29 form on fast limbs)
     {
         const int per = beta * 2 * HB_BT;
         for (int i = tid; i < nb * per; i += kThreads) {
@@ -106,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const u64 *key = sdesc[bb].key;
             u64 v = 0;
             if (key) v = key[((size_t)jp * keyP + p) * N + n0 + n];
-            skey[i] = fast ? split_pack(v) : v;
+            skey[i] = fast ? k29_pack(v) : v;
         }
     }
     __syncthreads();
@@ -156,12 +153,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             const u64 *pp = sdesc[bb].pt[gi];
             if (pp) v = pp[pt_off];
         }
-        ptv[bb] = fast ? split_pack(v) : v;
+        ptv[bb] = fast ? k29_pack(v) : v;
     }
     u64 pq_packed = 0, pq = 0;
     if (e < nq) {
         pq = pmod_q[e];
-        pq_packed = split_pack(pq);
+        pq_packed = k29_pack(pq);
     }
 
     for (int b = 0; b < nbatch; b++) {
@@ -188,17 +185,21 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const int so = soff[it];
                 const u64 *kt = skey + (size_t)bb * beta * 2 * HB_BT + n;
                 if (fast) {
-                    Split3 sb = {0, 0, 0}, sa = {0, 0, 0};
+                    Kara29 sb = {0, 0, 0}, sa = {0, 0, 0};
 #pragma unroll
                     for (int j = 0; j < HB_MAX_BETA; j++)
                         if (j < beta) {
-                            const u64 d = split_pack(g[j * HB_BT + so]);
-                            mac_split_packed(sb, d, kt[(j * 2 + 0) * HB_BT]);
-                            mac_split_packed(sa, d, kt[(j * 2 + 1) * HB_BT]);
+                            const u64 d = k29_pack(g[j * HB_BT + so]);
+                            const unsigned ds = k29_sum(d);
+                            k29_mac(sb, kt[(j * 2 + 0) * HB_BT], d, ds);
+                            k29_mac(sa, kt[(j * 2 + 1) * HB_BT], d, ds);
                         }
-                    if (e < nq) mac_split_packed(sb, pq_packed, split_pack(g[beta * HB_BT + so]));
-                    rb = split_reduce(sb, pc);
-                    ra = split_reduce(sa, pc);
+                    if (e < nq) {
+                        const u64 cv = k29_pack(g[beta * HB_BT + so]);
+                        k29_mac(sb, pq_packed, cv, k29_sum(cv));
+                    }
+                    rb = k29_reduce(sb, pc);
+                    ra = k29_reduce(sa, pc);
                 } else {
                     u128 sb = {0, 0}, sa = {0, 0};
 #pragma unroll
@@ -215,32 +216,29 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
             // R tile interleaved {b, a} per coefficient: one 16-byte read in phase B
             reinterpret_cast<ulonglong2 *>(sR)[bb * HB_BT + n] =
-                fast ? make_ulonglong2(split_pack(rb), split_pack(ra)) : make_ulonglong2(rb, ra);
+                fast ? make_ulonglong2(k29_pack(rb), k29_pack(ra)) : make_ulonglong2(rb, ra);
         }
         __syncthreads();
-        // ---- phase B: inner[g] += pt(g, b) * R_b.  Split sums: S0 takes 16
-        // terms below 2^60 before it is normalised (exact, three
-        // instructions); one reduction per output.  128-bit sums of at most
-        // 32 products below 2^122 need no intermediate reduction.
+        // ---- phase B: inner[g] += pt(g, b) * R_b.  Karatsuba split-29 sums
+        // of at most 32 products need no intermediate normalisation; one
+        // reduction per output.  128-bit sums of at most 32 products below
+        // 2^122 need no intermediate reduction either.
         if (gactive) {
             const ulonglong2 *R2 = reinterpret_cast<const ulonglong2 *>(sR) + nl;
             u64 vb, va;
             if (fast) {
-                Split3 ab = {0, 0, 0}, aa = {0, 0, 0};
+                Kara29 ab = {0, 0, 0}, aa = {0, 0, 0};
 #pragma unroll
                 for (int bb = 0; bb < HB_BCH; bb++) {
                     if (NBF || bb < nb) {
                         const ulonglong2 r = R2[bb * HB_BT];
-                        mac_split_packed(ab, ptv[bb], r.x);
-                        mac_split_packed(aa, ptv[bb], r.y);
-                        if (bb == 15) {
-                            split_normalize(ab);
-                            split_normalize(aa);
-                        }
+                        const unsigned ps = k29_sum(ptv[bb]);
+                        k29_mac(ab, r.x, ptv[bb], ps);
+                        k29_mac(aa, r.y, ptv[bb], ps);
                     }
                 }
-                vb = split_reduce(ab, pc);
-                va = split_reduce(aa, pc);
+                vb = k29_reduce(ab, pc);
+                va = k29_reduce(aa, pc);
             } else {
                 u128 ab = {0, 0}, aa = {0, 0};
 #pragma unroll

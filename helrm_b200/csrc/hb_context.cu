@@ -208,10 +208,10 @@ public:
             c.onep = (u64)(((hu128)1 << 64) / q);
             c.ninv = h_invm((u64)N, q);
             c.ninvp = h_shoup(c.ninv, q);
-            c.c30 = (1ull << 30) % q;
-            c.c30p = h_shoup(c.c30, q);
             c.c60 = (1ull << 60) % q;
             c.c60p = h_shoup(c.c60, q);
+            c.c58 = (1ull << 58) % q;
+            c.c58p = h_shoup(c.c58, q);
             pcs[p] = c;
         }
         upload_prime_consts(pcs.data(), P);
