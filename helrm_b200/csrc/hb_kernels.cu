@@ -1350,6 +1350,11 @@ void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in,
 // key switching: key multiplication with the automorphism folded into the
 // digit gather.
 // =====================================================================
+// One thread block per (ciphertext, 256 coefficients of one limb row), the
+// ciphertext index fastest: the blocks that read the same key segment run
+// back to back, so each key segment comes from DRAM once per launch and from
+// L2 for the other ciphertexts.  Limbs below 2^40 use Karatsuba split-29
+// products, the others 128-bit products.
 __global__ void __launch_bounds__(256) k_keymult(u64 *__restrict__ acc, const u64 *__restrict__ D,
                                                  const u64 *__restrict__ key, u64 g, int nq, int K, int L, int beta,
                                                  int keyP, const u64 *__restrict__ addb, int accumulate, int logN,
@@ -1357,24 +1362,39 @@ __global__ void __launch_bounds__(256) k_keymult(u64 *__restrict__ acc, const u6
     const int N = 1 << logN;
     const int ne = nq + K;
     const size_t n_all = (size_t)ne << logN;
-    const int b = blockIdx.y;
+    const int b = blockIdx.x;
+    const size_t i = (size_t)blockIdx.y * 256 + threadIdx.x;
+    if (i >= n_all) return;
     const u64 *Db = D + b * d_stride;
     u64 *Ab = acc + b * acc_stride;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_all; i += (size_t)gridDim.x * blockDim.x) {
-        const int e = (int)(i >> logN);
-        const unsigned t = (unsigned)(i & (N - 1));
-        const unsigned src = g == 1 ? t : aut_index(t, g, logN);
-        const int p = e < nq ? e : L + (e - nq);
-        const PrimeConst &pc = c_pc[p];
-        // issue every digit gather and key load before the products
-        u64 dv[HB_MAX_BETA], kbv[HB_MAX_BETA], kav[HB_MAX_BETA];
+    const int e = (int)(i >> logN);
+    const unsigned t = (unsigned)(i & (N - 1));
+    const unsigned src = g == 1 ? t : aut_index(t, g, logN);
+    const int p = e < nq ? e : L + (e - nq);
+    const PrimeConst &pc = c_pc[p];
+    // issue every digit gather and key load before the products
+    u64 dv[HB_MAX_BETA], kbv[HB_MAX_BETA], kav[HB_MAX_BETA];
+#pragma unroll
+    for (int j = 0; j < HB_MAX_BETA; j++)
+        if (j < beta) {
+            dv[j] = Db[((size_t)j * ne + e) * N + src];
+            kbv[j] = key[(((size_t)j * 2 + 0) * keyP + p) * N + t];
+            kav[j] = key[(((size_t)j * 2 + 1) * keyP + p) * N + t];
+        }
+    u64 vb, va;
+    if (pc.q < (1ull << 40)) {
+        Kara29 sb = {0, 0, 0}, sa = {0, 0, 0};
 #pragma unroll
         for (int j = 0; j < HB_MAX_BETA; j++)
             if (j < beta) {
-                dv[j] = Db[((size_t)j * ne + e) * N + src];
-                kbv[j] = key[(((size_t)j * 2 + 0) * keyP + p) * N + t];
-                kav[j] = key[(((size_t)j * 2 + 1) * keyP + p) * N + t];
+                const u64 d = k29_pack(dv[j]);
+                const unsigned ds = k29_sum(d);
+                k29_mac(sb, k29_pack(kbv[j]), d, ds);
+                k29_mac(sa, k29_pack(kav[j]), d, ds);
             }
+        vb = k29_reduce(sb, pc);
+        va = k29_reduce(sa, pc);
+    } else {
         u128 sb = {0, 0}, sa = {0, 0};
 #pragma unroll
         for (int j = 0; j < HB_MAX_BETA; j++)
@@ -1382,30 +1402,32 @@ __global__ void __launch_bounds__(256) k_keymult(u64 *__restrict__ acc, const u6
                 mac128(sb, dv[j], kbv[j]);
                 mac128(sa, dv[j], kav[j]);
             }
-        u64 vb = reduce128(sb, pc), va = reduce128(sa, pc);
-        if (addb) vb = add_mod(vb, addb[b * add_stride + ((size_t)e << logN) + src], pc.q);
-        if (accumulate) {
-            vb = add_mod(vb, Ab[i], pc.q);
-            va = add_mod(va, Ab[n_all + i], pc.q);
-        }
-        Ab[i] = vb;
-        Ab[n_all + i] = va;
+        vb = reduce128(sb, pc);
+        va = reduce128(sa, pc);
     }
+    if (addb) vb = add_mod(vb, addb[b * add_stride + ((size_t)e << logN) + src], pc.q);
+    if (accumulate) {
+        vb = add_mod(vb, Ab[i], pc.q);
+        va = add_mod(va, Ab[n_all + i], pc.q);
+    }
+    Ab[i] = vb;
+    Ab[n_all + i] = va;
 }
 void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,
              const u64 *addb, bool accumulate, int logN, int nbatch, size_t d_stride, size_t acc_stride,
              size_t add_stride, cudaStream_t s) {
     if (beta > HB_MAX_BETA) throw std::invalid_argument("keymult: more digits than HB_MAX_BETA");
     size_t n = (size_t)(nq + K) << logN;
-    unsigned g = grid1d(n, 256);
-    if (g > 4096) g = 4096;
+    const size_t chunks = (n + 255) / 256;
+    if (chunks > 65535) throw std::invalid_argument("keymult: limb stack too large for one launch");
     // digits per ciphertext + the key once per launch + accumulator traffic
     const double nd = (double)n;
     ProfScope ps(KC_KEYMULT,
                  8.0 * (nbatch * nd * (beta + 2.0 + (addb ? 1.0 : 0.0) + (accumulate ? 2.0 : 0.0)) + 2.0 * beta * nd),
                  2.0 * beta * nbatch * nd, s, 1);
-    k_keymult<<<dim3(g, nbatch), 256, 0, s>>>(acc, D, key, galois, nq, K, L, beta, keyP, addb, accumulate ? 1 : 0,
-                                              logN, d_stride, acc_stride, add_stride);
+    k_keymult<<<dim3(nbatch, (unsigned)chunks), 256, 0, s>>>(acc, D, key, galois, nq, K, L, beta, keyP, addb,
+                                                             accumulate ? 1 : 0, logN, d_stride, acc_stride,
+                                                             add_stride);
     check_launch("keymult");
 }
 
