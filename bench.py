@@ -59,30 +59,44 @@ def parse():
 
 # --------------------------------------------------------------------------- distributed plumbing
 class Dist:
-    def __init__(self):
+    """One process per GPU (torchrun env vars).  NCCL on GPU hosts; gloo when
+    no GPU is visible or HELRM_DIST_BACKEND=gloo (the CPU tests of this
+    plumbing).  The only collectives are a barrier around the timed region
+    and the max of the per-rank times: ciphertext batches are independent,
+    so the data path has no exchange."""
+
+    def __init__(self, backend: str | None = None, timeout_s: float = 120.0):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
+        self.backend = None
         if self.world > 1:
             import datetime
 
             import torch
             import torch.distributed as dist
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
+            backend = backend or os.environ.get("HELRM_DIST_BACKEND") or \
+                ("nccl" if torch.cuda.is_available() else "gloo")
+            timeout = datetime.timedelta(seconds=timeout_s)
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", self.local))
+            else:
+                dist.init_process_group(backend, timeout=timeout)
             self.pg = dist
+            self.backend = backend
 
     def barrier(self):
         if self.pg:
             self.pg.barrier()
 
     def max(self, x: float) -> float:
+        """max over ranks of a per-rank device time"""
         if not self.pg:
             return x
         import torch
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        t = torch.tensor([x], dtype=torch.float64, device="cuda" if self.backend == "nccl" else "cpu")
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
@@ -90,6 +104,12 @@ class Dist:
         if self.pg:
             self.pg.barrier()
             self.pg.destroy_process_group()
+
+
+def whole_job_rate(world: int, batch: int, steps: int, t_max_s: float) -> float:
+    """inferences/s of the whole job: every rank ran `steps` steps of `batch`
+    ciphertexts (one query each); the job took the slowest rank's time"""
+    return world * batch * steps / t_max_s
 
 
 # --------------------------------------------------------------------------- clocks
@@ -342,7 +362,7 @@ def run_b200(args, dist):
     torch.cuda.synchronize()
     dist.barrier()
     t_dev = dist.max(ms.value / 1000.0)
-    value = dist.world * args.batch * args.steps / t_dev
+    value = whole_job_rate(dist.world, args.batch, args.steps, t_dev)
     ms_step = 1000.0 * t_dev / args.steps
 
     names = []
@@ -406,7 +426,7 @@ def run_b200(args, dist):
         ms2 = ctypes.c_double(0)
         _capi.check(capi.helrm_TimerStop(ctypes.byref(ms2)))
         t_e2e = dist.max(ms2.value / 1000.0)
-        e2e = {"value": dist.world * args.batch * args.steps / t_e2e, "unit": UNIT,
+        e2e = {"value": whole_job_rate(dist.world, args.batch, args.steps, t_e2e), "unit": UNIT,
                "h2d_bytes_per_step": args.batch * words_in * 8, "d2h_bytes_per_step": args.batch * words_out * 8,
                "ms_per_step": 1000.0 * t_e2e / args.steps}
 
