@@ -28,6 +28,8 @@ struct PrimeConst {
     u64 ninvp;
     u64 c60, c60p;  // 2^60 mod q
     u64 c58, c58p;  // 2^58 mod q (Karatsuba split-29 recombination)
+    double qinv;    // fl(1/q), quotient estimates on the FP64 pipe
+    double c58d;    // 2^58 mod q as a double (exact for q < 2^53)
 };
 
 #define HB_SPLIT_MASK 0x3FFFFFFFull
@@ -125,16 +127,29 @@ __device__ __forceinline__ void k29_mac(Kara29 &acc, u64 a_packed, u64 b_packed,
     asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.m) : "r"(al + ah), "r"(b_sum));
     acc.s2 += ah * bh;
 }
-// (S0 + S1 2^29 + S2 2^58) mod q: carries give lo + hi 2^58 with lo < 2^58,
-// hi 2^58 is folded with 2^58 mod q (lazy Shoup, < 2q) and the sum reduced
-// once with floor(2^64/q).
+// a 32-bit unsigned integer as an exact double: the bit pattern 0x43300000:x
+// is 2^52 + x
+__device__ __forceinline__ double u32_to_double(unsigned x) {
+    return __hiloint2double(0x43300000, (int)x) - 4503599627370496.0;
+}
+// (S0 + S1 2^29 + S2 2^58) mod q for q < 2^40.  Carries give
+// a0 + a1 2^29 + hi 2^58 with a0, a1 < 2^29 and hi < 2^28; with c = 2^58 mod q
+// the value is congruent to W = a0 + a1 2^29 + hi c < 2^68.  W is formed
+// modulo 2^64 on the integer pipe and, approximately, as a double on the
+// FP64 pipe (error <= 2^16); Q = round(W / q) from fl(1/q) is then within
+// 0.5 + 2^-19 of W/q, so W - Q q (modulo 2^64) lies in (-0.51q, 0.51q) and one
+// conditional addition of q finishes.  Five integer multiply instructions
+// instead of two 64-bit Shoup reductions.
 __device__ __forceinline__ u64 k29_reduce(const Kara29 &a, const PrimeConst &pc) {
     const u64 s1 = a.m - a.s0 - a.s2;
     const u64 t = s1 + (a.s0 >> 29);
-    const u64 lo = (a.s0 & HB_K29_MASK) | ((t & HB_K29_MASK) << 29);
-    const u64 hi = (u64)a.s2 + (t >> 29);
-    const u64 v = lo + mul_shoup_lazy(hi, pc.c58, pc.c58p, pc.q);
-    return mul_shoup(v, 1ull, pc.onep, pc.q);
+    const unsigned a0 = (unsigned)(a.s0 & HB_K29_MASK), a1 = (unsigned)(t & HB_K29_MASK);
+    const unsigned hi = a.s2 + (unsigned)(t >> 29);
+    const u64 W = (u64)a0 + ((u64)a1 << 29) + (u64)hi * pc.c58;
+    const double wd = __fma_rn(u32_to_double(hi), pc.c58d, __fma_rn(u32_to_double(a1), 536870912.0, u32_to_double(a0)));
+    const u64 Q = (u64)__double_as_longlong(__fma_rn(wd, pc.qinv, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
+    const u64 r = W - Q * pc.q;
+    return (long long)r < 0 ? r + pc.q : r;
 }
 
 // Split-30 sums of products a*b with one factor below 2^40 and the other

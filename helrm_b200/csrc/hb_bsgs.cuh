@@ -118,13 +118,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     // baby the beta digit rows and c0 at its source tile, for the identity
     // baby c0 and c1 at the tile itself (rows 0 and 1); c-rows exist only on
     // the q limbs
+    // segment s = bb * R1 + r; s / R1 by a reciprocal multiply, exact for
+    // s < 2^16 / R1 (at most 32 * 9 segments here)
+    const unsigned r1mul = (65536u + (unsigned)R1 - 1u) / (unsigned)R1;
     auto issue = [&](int b, int buf) {
         const u64 *c0b = ct + b * ct_stride;
         const u64 *Db = D + b * d_stride;
         u64 *Gb = sG + buf * gbuf;
         const int nchunk = nb * R1 * (HB_BT / 2);
         for (int i = tid; i < nchunk; i += kThreads) {
-            const int bb = i / (R1 * (HB_BT / 2)), r = (i / (HB_BT / 2)) % R1, k = i % (HB_BT / 2);
+            const unsigned seg = (unsigned)i >> 3;  // HB_BT / 2 = 8 chunks of 16 bytes per segment
+            const int bb = (int)((seg * r1mul) >> 16), r = (int)seg - bb * R1, k = i & 7;
             const u64 *src;
             if (sdesc[bb].key == nullptr) {
                 if (e >= nq || r >= 2) continue;

@@ -212,6 +212,8 @@ public:
             c.c60p = h_shoup(c.c60, q);
             c.c58 = (1ull << 58) % q;
             c.c58p = h_shoup(c.c58, q);
+            c.qinv = 1.0 / (double)q;
+            c.c58d = (double)c.c58;
             pcs[p] = c;
         }
         upload_prime_consts(pcs.data(), P);
