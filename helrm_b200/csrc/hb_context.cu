@@ -344,8 +344,13 @@ public:
                 for (auto &x : v) x = ((x >> 30) << 32) | (x & ((1ull << 30) - 1));
                 return v;
             };
+            auto packed29 = [](std::vector<u64> v) {  // split-29 form: (v >> 29) << 32 | (v & (2^29 - 1))
+                for (auto &x : v) x = ((x >> 29) << 32) | (x & ((1ull << 29) - 1));
+                return v;
+            };
             size_t o_qhinv = put(qhinv), o_qhinvp = put(qhinvp), o_qhat = put(qhat), o_qjneg = put(qjneg),
-                   o_pneg = put(pneg), o_qhat_s = put(packed(qhat)), o_qjneg_s = put(packed(qjneg));
+                   o_pneg = put(pneg), o_qhat_s = put(packed(qhat)), o_qjneg_s = put(packed(qjneg)),
+                   o_qhat_k = put(packed29(qhat)), o_qjneg_k = put(packed29(qjneg));
             size_t o_phinv = put(phinv), o_phinvp = put(phinvp), o_phat = put(phat), o_pinv = put(pinv),
                    o_pinvp = put(pinvp), o_qlinv = put(qlinv), o_qlinvp = put(qlinvp), o_phat_s = put(packed(phat)),
                    o_pneg_s = put(packed(pneg));
@@ -362,6 +367,8 @@ public:
             T.mu.qjneg = T.blob + o_qjneg;
             T.mu.qhat_s = T.blob + o_qhat_s;
             T.mu.qjneg_s = T.blob + o_qjneg_s;
+            T.mu.qhat_k = T.blob + o_qhat_k;
+            T.mu.qjneg_k = T.blob + o_qjneg_k;
             T.mu.split = small_main ? 1 : 0;
             T.md.pneg = T.blob + o_pneg;
             T.md.phat_s = T.blob + o_phat_s;

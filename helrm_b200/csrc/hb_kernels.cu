@@ -1082,19 +1082,27 @@ __global__ void __launch_bounds__(256)
     k_modup_bconv_split(u64 *__restrict__ D, const u64 *__restrict__ X, const u64 *__restrict__ c1ntt, int nq, int K,
                         int L, int alpha, int j0, ModUpTab tab, int logN, size_t in_stride, size_t out_stride,
                         size_t c1_stride) {
-    __shared__ u64 st[(NA + 1) * HB_MAX_PRIMES];  // qhat [m][e], then qjneg [e]
+    __shared__ u64 st[(NA + 1) * HB_MAX_PRIMES];  // split-30 qhat [m][e], then qjneg [e]
+    __shared__ u64 sk[(NA + 1) * HB_MAX_PRIMES];  // the same in split-29 form
     const int N = 1 << logN;
     const int j = j0 + blockIdx.y, b = blockIdx.z;
     const int ne = nq + K;
     const int lo = j * alpha;
-    for (int i = threadIdx.x; i < NA * ne; i += blockDim.x) st[i] = tab.qhat_s[(size_t)j * alpha * ne + i];
-    for (int i = threadIdx.x; i < ne; i += blockDim.x) st[NA * ne + i] = tab.qjneg_s[(size_t)j * ne + i];
+    for (int i = threadIdx.x; i < NA * ne; i += blockDim.x) {
+        st[i] = tab.qhat_s[(size_t)j * alpha * ne + i];
+        sk[i] = tab.qhat_k[(size_t)j * alpha * ne + i];
+    }
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) {
+        st[NA * ne + i] = tab.qjneg_s[(size_t)j * ne + i];
+        sk[NA * ne + i] = tab.qjneg_k[(size_t)j * ne + i];
+    }
     __syncthreads();
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;
     const u64 *Xb = X + b * in_stride;
     u64 *Db = D + b * out_stride + (size_t)j * ne * N;
-    u64 y[NA];
+    u64 y[NA], yk[NA];
+    unsigned ys[NA];
     unsigned nneg = 0;
 #pragma unroll
     for (int m = 0; m < NA; m++) {
@@ -1103,13 +1111,24 @@ __global__ void __launch_bounds__(256)
         const u64 v = mul_shoup(Xb[(size_t)pm * N + n], tab.qhinv[j * alpha + m], tab.qhinvp[j * alpha + m], qm);
         nneg += v > (qm >> 1);
         y[m] = split_pack(v);
+        yk[m] = k29_pack(v);
+        ys[m] = k29_sum(yk[m]);
     }
-    for (int e = 0; e < ne; e++) {
+    // q-row targets (below 2^40): Karatsuba split-29 products, one reduction
+    for (int e = 0; e < nq; e++) {
         if (e >= lo && e < lo + NA) {
             Db[(size_t)e * N + n] = c1ntt[b * c1_stride + (size_t)e * N + n];
             continue;
         }
-        const int p = e < nq ? e : L + (e - nq);
+        Kara29 acc = {0, 0, 0};
+#pragma unroll
+        for (int m = 0; m < NA; m++) k29_mac(acc, sk[m * ne + e], yk[m], ys[m]);
+        k29_mac(acc, sk[NA * ne + e], (u64)nneg, nneg);
+        Db[(size_t)e * N + n] = k29_reduce(acc, c_pc[e]);
+    }
+    // special-prime targets: split-30 products (table values below 2^61)
+    for (int e = nq; e < ne; e++) {
+        const int p = L + (e - nq);
         SplitW acc = {0, 0, 0};
 #pragma unroll
         for (int m = 0; m < NA; m++) {

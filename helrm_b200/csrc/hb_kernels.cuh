@@ -129,7 +129,9 @@ struct ModUpTab {
     const u64 *qjneg;   // [beta][ne]               t_e - (Q_j mod t_e)
     const u64 *qhat_s;  // qhat in split-30 packed form
     const u64 *qjneg_s; // qjneg in split-30 packed form
-    int split;          // every main prime below 2^40: split-30 products
+    const u64 *qhat_k;  // qhat in split-29 packed form (Karatsuba products on q-row targets)
+    const u64 *qjneg_k; // qjneg in split-29 packed form
+    int split;          // every main prime below 2^40: split products
 };
 void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
                  const ModUpTab &tab, int logN, int nbatch, size_t in_stride, size_t out_stride, size_t c1_stride,
