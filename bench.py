@@ -340,6 +340,7 @@ def run_b200(args, dist):
     lib.Synchronize()
     clocks.start()
     _capi.check(capi.helrm_ProfilerRange(1))
+    # per-kernel CUDA events on the library stream, over the timed region
     _capi.check(capi.helrm_ProfileEnable(1))
     n0 = ctypes.c_uint64(0)
     _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n0)))
@@ -364,6 +365,7 @@ def run_b200(args, dist):
     t_dev = dist.max(ms.value / 1000.0)
     value = whole_job_rate(dist.world, args.batch, args.steps, t_dev)
     ms_step = 1000.0 * t_dev / args.steps
+    prof_steps = args.steps
 
     names = []
     buf = ctypes.create_string_buffer(64)
@@ -374,7 +376,7 @@ def run_b200(args, dist):
     for i, nm in enumerate(names):
         if pl[i] == 0:
             continue
-        kern[nm] = {"ms_per_step": pms[i] / args.steps, "launches_per_step": pl[i] / args.steps,
+        kern[nm] = {"ms_per_step": pms[i] / prof_steps, "launches_per_step": pl[i] / prof_steps,
                     "share": None, "GBps": pby[i] / (pms[i] * 1e6) if pms[i] else None,
                     "Gops": pwk[i] / (pms[i] * 1e6) if pms[i] else None}
     tot = sum(v["ms_per_step"] for v in kern.values()) or 1.0

@@ -624,13 +624,37 @@ public:
         return c;
     }
 
+    // ---------------------------------------------------------- batch packing
+    // [nb][2][nq][N] <- the first nq rows of each ciphertext's two polys (one
+    // launch per HB_PTR_BATCH ciphertexts)
+    void gather_cts(u64 *dst, const std::vector<const Ct *> &v, int nq) {
+        const size_t words = (size_t)nq * N;
+        for (size_t b0 = 0; b0 < v.size(); b0 += HB_PTR_BATCH) {
+            const int n = (int)std::min<size_t>(HB_PTR_BATCH, v.size() - b0);
+            PtrBatch s0{}, s1{};
+            for (int i = 0; i < n; i++) {
+                s0.p[i] = v[b0 + i]->d;
+                s1.p[i] = v[b0 + i]->d + (size_t)v[b0 + i]->nq * N;
+            }
+            gather_items(dst + b0 * 2 * words, s0, s1, 2, words, n, stream);
+        }
+    }
+    // each destination <- its `words`-word item of the contiguous src
+    void scatter_words(const std::vector<u64 *> &dsts, const u64 *src, size_t words) {
+        for (size_t b0 = 0; b0 < dsts.size(); b0 += HB_PTR_BATCH) {
+            const int n = (int)std::min<size_t>(HB_PTR_BATCH, dsts.size() - b0);
+            PtrBatchW d{};
+            for (int i = 0; i < n; i++) d.p[i] = dsts[b0 + i];
+            scatter_items(d, src + b0 * words, words, n, stream);
+        }
+    }
+
     // ---------------------------------------------------------- key switching pieces
     // ModUp of nb polys (nq rows each, NTT) -> D [nb][beta][ne][N]
     void modup(u64 *D, const u64 *a, int nq, int nb, size_t a_stride) {
         const int ne = nq + K, beta = beta_of(nq);
         u64 *X = alloc((size_t)nb * nq * N);
-        for (int b = 0; b < nb; b++) d2d(X + (size_t)b * nq * N, a + b * a_stride, (size_t)nq * N);
-        ntt_inverse(X, nb * nq, qmap(nq), ntt, stream);
+        ntt_inverse_from(X, a, a_stride, nq, nb * nq, qmap(nq), ntt, stream);
         modup_bconv(D, X, a, nq, K, L, alpha, beta, lv[nq].mu, logN, nb, (size_t)nq * N, (size_t)beta * ne * N,
                     a_stride, stream);
         RowMap m = extmap(nq);
@@ -645,9 +669,8 @@ public:
     void moddown(u64 *out, const u64 *x, int nq, int nb, size_t xs, size_t os, const u64 *addend = nullptr,
                  u64 add_g = 1, size_t as = 0) {
         u64 *Y = alloc((size_t)nb * K * N);
-        for (int b = 0; b < nb; b++) d2d(Y + (size_t)b * K * N, x + b * xs + (size_t)nq * N, (size_t)K * N);
         RowMap pm = rowmap(K, 0, L);
-        ntt_inverse(Y, nb * K, pm, ntt, stream);
+        ntt_inverse_from(Y, x + (size_t)nq * N, xs, K, nb * K, pm, ntt, stream);
         u64 *Z = alloc((size_t)nb * nq * N);
         moddown_bconv(Z, Y, nq, K, L, lv[nq].md, logN, nb, (size_t)K * N, (size_t)nq * N, stream);
         ntt_forward(Z, nb * nq, qmap(nq), ntt, stream);
@@ -708,9 +731,9 @@ public:
         if (nq < 2) HB_THROW(HB_ESTATE, "rescale: ciphertext already at level 0");
         const int l = nq - 1;
         u64 *R = alloc((size_t)nb * npoly * N);
-        for (int b = 0; b < nb; b++)
-            for (int pl = 0; pl < npoly; pl++)
-                d2d(R + ((size_t)b * npoly + pl) * N, in + b * in_stride + ((size_t)pl * nq + l) * N, N);
+        for (int pl = 0; pl < npoly; pl++)
+            copy_strided(R + (size_t)pl * N, (size_t)npoly * N, in + ((size_t)pl * nq + l) * N, in_stride, N, nb,
+                         stream);
         RowMap rm = rowmap(1, 1, L);
         rm.pbase = l;
         ntt_inverse(R, nb * npoly, rm, ntt, stream);
@@ -730,9 +753,9 @@ public:
         const int l = nq - 1;
         u64 *R = scratch;
         u64 *W = scratch + (size_t)nb * npoly * N;
-        for (int b = 0; b < nb; b++)
-            for (int pl = 0; pl < npoly; pl++)
-                d2d(R + ((size_t)b * npoly + pl) * N, in + b * in_stride + ((size_t)pl * nq + l) * N, N);
+        for (int pl = 0; pl < npoly; pl++)
+            copy_strided(R + (size_t)pl * N, (size_t)npoly * N, in + ((size_t)pl * nq + l) * N, in_stride, N, nb,
+                         stream);
         RowMap rm = rowmap(1, 1, L);
         rm.pbase = l;
         ntt_inverse(R, nb * npoly, rm, ntt, stream);
@@ -1065,16 +1088,22 @@ public:
             bsgs_baby_mac(inner, in, D, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, nb, cts_,
                           (size_t)beta * es, (size_t)nslots * 2 * es, stream);
         release(D);
-        u64 *acc = alloc((size_t)nb * 2 * es);
-        bool acc_init = false;
-        for (int s = 0; s < nslots; s++) {
-            if (t.giant_of_slot[s] == 0) {
-                for (int b = 0; b < nb; b++)
-                    d2d(acc + (size_t)b * 2 * es, inner + ((size_t)b * nslots + s) * 2 * es, 2 * es);
-                acc_init = true;
-            }
+        // the giant-0 slot needs no rotation: its inner sum is the accumulator
+        // itself (no copy); without one, a zeroed accumulator of its own
+        int s0 = -1;
+        for (int s = 0; s < nslots; s++)
+            if (t.giant_of_slot[s] == 0) s0 = s;
+        u64 *acc_own = nullptr, *acc;
+        size_t acc_stride;
+        if (s0 >= 0) {
+            acc = inner + (size_t)s0 * 2 * es;
+            acc_stride = (size_t)nslots * 2 * es;
+        } else {
+            acc_own = alloc((size_t)nb * 2 * es);
+            zero(acc_own, (size_t)nb * 2 * es);
+            acc = acc_own;
+            acc_stride = 2 * es;
         }
-        if (!acc_init) zero(acc, (size_t)nb * 2 * es);
         u64 *aq = alloc((size_t)nb * nq * N);
         u64 *D2 = alloc((size_t)nb * beta * es);
         for (int s = 0; s < nslots; s++) {
@@ -1086,14 +1115,14 @@ public:
             moddown(aq, Ia, nq, nb, (size_t)nslots * 2 * es, (size_t)nq * N);
             modup(D2, aq, nq, nb, (size_t)nq * N);
             keymult(acc, D2, key, gal, nq, K, L, beta, P, inner + (size_t)s * 2 * es, true, logN, nb,
-                    (size_t)beta * es, 2 * es, (size_t)nslots * 2 * es, stream);
+                    (size_t)beta * es, acc_stride, (size_t)nslots * 2 * es, stream);
         }
         release(aq);
         release(D2);
+        moddown(out, acc, nq, nb, acc_stride, cts_);
+        moddown(out + (size_t)nq * N, acc + es, nq, nb, acc_stride, cts_);
         release(inner);
-        moddown(out, acc, nq, nb, 2 * es, cts_);
-        moddown(out + (size_t)nq * N, acc + es, nq, nb, 2 * es, cts_);
-        release(acc);
+        if (acc_own) release(acc_own);
     }
 
     size_t lt_bytes_per_ct(const LinTrans &t, int nq) {
@@ -1124,21 +1153,21 @@ public:
             for (size_t c0 = 0; c0 < idx.size(); c0 += chunk) {
                 int nb = (int)std::min<size_t>(chunk, idx.size() - c0);
                 u64 *in = alloc((size_t)nb * cts_);
-                for (int b = 0; b < nb; b++) {
-                    const Ct &c = ct(ids[idx[c0 + b]]);
-                    d2d(in + (size_t)b * cts_, c.d, (size_t)nq * N);
-                    d2d(in + (size_t)b * cts_ + (size_t)nq * N, c.d + (size_t)c.nq * N, (size_t)nq * N);
-                }
+                std::vector<const Ct *> src(nb);
+                for (int b = 0; b < nb; b++) src[b] = &ct(ids[idx[c0 + b]]);
+                gather_cts(in, src, nq);
                 u64 *out = alloc((size_t)nb * cts_);
                 lt_eval_packed(t, in, nq, nb, out);
                 release(in);
+                std::vector<u64 *> dst(nb);
                 for (int b = 0; b < nb; b++) {
                     const Ct &c = ct(ids[idx[c0 + b]]);
                     Ct o = new_ct(nq, 2, c.scale * default_scale);
                     o.slots = c.slots;
-                    d2d(o.d, out + (size_t)b * cts_, cts_);
+                    dst[b] = o.d;
                     outs[idx[c0 + b]] = put_ct(o);
                 }
+                scatter_words(dst, out, cts_);
                 release(out);
             }
         }
@@ -1154,7 +1183,13 @@ public:
             const size_t cts_ = (size_t)2 * nq * N;
             const int nb = (int)v.size();
             u64 *buf = alloc((size_t)nb * cts_), *rot = alloc((size_t)nb * cts_);
-            for (int b = 0; b < nb; b++) d2d(buf + (size_t)b * cts_, ct(v[b]).d, cts_);
+            std::vector<const Ct *> src(nb);
+            std::vector<u64 *> dst(nb);
+            for (int b = 0; b < nb; b++) {
+                src[b] = &ct(v[b]);
+                dst[b] = ct(v[b]).d;
+            }
+            gather_cts(buf, src, nq);
             for (int i = 1; i <= rotations; i++) {
                 int k = slots >> i;
                 u64 g = galois_of(k);
@@ -1162,7 +1197,7 @@ public:
                 rotate_batch(rot, buf, nq, nb, g, key);
                 ew_add(buf, buf, rot, nb * 2 * nq, qmap(nq), logN, stream);
             }
-            for (int b = 0; b < nb; b++) d2d(ct(v[b]).d, buf + (size_t)b * cts_, cts_);
+            scatter_words(dst, buf, cts_);
             release(buf);
             release(rot);
         }
@@ -1501,9 +1536,43 @@ HB_API int helrm_Rescale(int ct) {
 HB_API int helrm_RescaleBatch(const int *cts, int n) {
     return guard([&] {
         Context &c = C();
+        if (n < 0 || (n > 0 && !cts)) HB_THROW(HB_EINVAL, "RescaleBatch: bad arguments");
+        // ciphertexts of the same level and degree are rescaled together:
+        // gathered into one batch, rescaled with batched kernels, scattered
+        // into fresh ciphertexts that replace the inputs (same ids)
+        std::map<std::pair<int, int>, std::vector<int>> groups;
         for (int i = 0; i < n; i++) {
-            int o = rescale_new(c, cts[i]);
-            c.replace_ct(cts[i], o);
+            const Ct &x = c.ct(cts[i]);
+            if (x.nq < 2) HB_THROW(HB_ESTATE, "RescaleBatch: ciphertext already at level 0.");
+            groups[{x.nq, x.npoly}].push_back(cts[i]);
+        }
+        for (auto &kv : groups) {
+            const int nq = kv.first.first, npoly = kv.first.second;
+            const auto &v = kv.second;
+            const int nb = (int)v.size();
+            if (npoly != 2) {
+                for (int id : v) c.replace_ct(id, rescale_new(c, id));
+                continue;
+            }
+            const size_t in_w = (size_t)2 * nq * c.N, out_w = (size_t)2 * (nq - 1) * c.N;
+            u64 *in = c.alloc((size_t)nb * in_w), *out = c.alloc((size_t)nb * out_w);
+            std::vector<const Ct *> src(nb);
+            for (int b = 0; b < nb; b++) src[b] = &c.ct(v[b]);
+            c.gather_cts(in, src, nq);
+            c.rescale(out, in, 2, nq, nb, in_w, out_w);
+            std::vector<u64 *> dst(nb);
+            std::vector<int> fresh(nb);
+            for (int b = 0; b < nb; b++) {
+                const Ct &x = c.ct(v[b]);
+                Ct o = c.new_ct(nq - 1, 2, x.scale / (double)c.primes[nq - 1]);
+                o.slots = x.slots;
+                dst[b] = o.d;
+                fresh[b] = c.put_ct(o);
+            }
+            c.scatter_words(dst, out, out_w);
+            c.release(in);
+            c.release(out);
+            for (int b = 0; b < nb; b++) c.replace_ct(v[b], fresh[b]);
         }
     });
 }

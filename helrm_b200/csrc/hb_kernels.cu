@@ -588,7 +588,9 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
 template <bool INV>
 __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
                                                       const u64 *__restrict__ twp,
-                                                      const ulonglong2 *__restrict__ twx, int row0) {
+                                                      const ulonglong2 *__restrict__ twx, int row0,
+                                                      const u64 *__restrict__ src = nullptr, size_t src_stride = 0,
+                                                      int src_per = 1) {
     __shared__ u64 sm[16 * 272];
     const int row = row0 + blockIdx.y;
     if (map.skip(row)) return;
@@ -633,8 +635,13 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
 #pragma unroll
         for (int k = 0; k < 16; k++) a[c + 16 * k] = sb[k * 17 + c];
     } else {
+        // out of place: the first (block) pass of the inverse reads row `row`
+        // of the source, item row / src_per at src_stride, limb row % src_per
+        const u64 *ain = src ? src + (size_t)(row / src_per) * src_stride + ((size_t)(row % src_per) << 16) +
+                                   ((size_t)rb << 8)
+                             : a;
 #pragma unroll
-        for (int k = 0; k < 16; k++) sb[k * 17 + c] = a[c + 16 * k];
+        for (int k = 0; k < 16; k++) sb[k * 17 + c] = ain[c + 16 * k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];
@@ -716,6 +723,30 @@ static void ntt_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bool 
         }
     }
     check_launch("ntt");
+}
+
+// dst[row] = INTT(src row), rows grouped `per_item` to an item of the source
+// at src_stride (destination rows contiguous): the first pass reads the
+// source, so no copy of the input is made (N = 2^16; other sizes copy first)
+void ntt_inverse_from(u64 *dst, const u64 *src, size_t src_stride, int per_item, int nrows, RowMap map,
+                      const NttTables &t, cudaStream_t s) {
+    if (nrows <= 0) return;
+    if (t.logN != 16 || map.alpha > 0) {
+        copy_strided(dst, (size_t)per_item << t.logN, src, src_stride, (size_t)per_item << t.logN,
+                     nrows / per_item, s);
+        ntt_inverse(dst, nrows, map, t, s);
+        return;
+    }
+    if (nrows % per_item) throw std::invalid_argument("ntt_inverse_from: rows not a whole number of items");
+    const double nwords = (double)nrows * 65536.0;
+    ProfScope ps(KC_NTT_INV, 16.0 * nwords, nwords / 2 * 16, s, 2 * ((nrows + 65534) / 65535));
+    for (int r0 = 0; r0 < nrows; r0 += 65535) {
+        const int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
+        const dim3 grid(16, nr);
+        k_ntt256_rows<true><<<grid, 256, 0, s>>>(dst, map, t.itw, t.itwp, t.itwx, r0, src, src_stride, per_item);
+        k_ntt256_cols<true><<<grid, 256, 0, s>>>(dst, map, t.itw, t.itwp, t.itwx, r0);
+    }
+    check_launch("ntt256_from");
 }
 
 void ntt_forward(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s) {
@@ -1482,6 +1513,63 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
         k_bsgs_mac<0><<<grid, HB_GCH * HB_BT, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN,
                                                          nbatch, ct_stride, d_stride, inner_stride);
     check_launch("bsgs_mac");
+}
+
+// ---- batched copies ----------------------------------------------------------
+__global__ void k_copy_strided(ulonglong2 *__restrict__ dst, size_t dstride2, const ulonglong2 *__restrict__ src,
+                               size_t sstride2, size_t n2) {
+    const size_t b = blockIdx.y;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n2; i += (size_t)gridDim.x * blockDim.x)
+        dst[b * dstride2 + i] = src[b * sstride2 + i];
+}
+__global__ void k_gather_items(ulonglong2 *__restrict__ dst, PtrBatch seg0, PtrBatch seg1, int nseg, size_t n2) {
+    const int b = blockIdx.y;
+    for (int j = 0; j < nseg; j++) {
+        const ulonglong2 *src = reinterpret_cast<const ulonglong2 *>(j == 0 ? seg0.p[b] : seg1.p[b]);
+        ulonglong2 *d = dst + ((size_t)b * nseg + j) * n2;
+        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n2; i += (size_t)gridDim.x * blockDim.x)
+            d[i] = src[i];
+    }
+}
+__global__ void k_scatter_items(PtrBatchW dst, const ulonglong2 *__restrict__ src, size_t n2) {
+    const int b = blockIdx.y;
+    ulonglong2 *d = reinterpret_cast<ulonglong2 *>(dst.p[b]);
+    const ulonglong2 *sb = src + (size_t)b * n2;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n2; i += (size_t)gridDim.x * blockDim.x)
+        d[i] = sb[i];
+}
+static void copy_check(size_t words, int nb) {
+    if (words % 2 || nb <= 0 || nb > 65535) throw std::invalid_argument("batched copy: bad shape");
+}
+static unsigned copy_grid(size_t n2) {
+    size_t g = (n2 + 255) / 256;
+    return (unsigned)(g > 1024 ? 1024 : g);
+}
+void copy_strided(u64 *dst, size_t dstride, const u64 *src, size_t sstride, size_t words, int nb, cudaStream_t s) {
+    copy_check(words, nb);
+    if (dstride % 2 || sstride % 2) throw std::invalid_argument("copy_strided: odd stride");
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * words * nb, 0.0, s, 1);
+    k_copy_strided<<<dim3(copy_grid(words / 2), nb), 256, 0, s>>>(
+        reinterpret_cast<ulonglong2 *>(dst), dstride / 2, reinterpret_cast<const ulonglong2 *>(src), sstride / 2,
+        words / 2);
+    check_launch("copy_strided");
+}
+void gather_items(u64 *dst, const PtrBatch &seg0, const PtrBatch &seg1, int nseg, size_t words, int nb,
+                  cudaStream_t s) {
+    copy_check(words, nb);
+    if (nb > HB_PTR_BATCH || nseg < 1 || nseg > 2) throw std::invalid_argument("gather_items: bad batch");
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * words * nb * nseg, 0.0, s, 1);
+    k_gather_items<<<dim3(copy_grid(words / 2), nb), 256, 0, s>>>(reinterpret_cast<ulonglong2 *>(dst), seg0, seg1,
+                                                                   nseg, words / 2);
+    check_launch("gather_items");
+}
+void scatter_items(const PtrBatchW &dst, const u64 *src, size_t words, int nb, cudaStream_t s) {
+    copy_check(words, nb);
+    if (nb > HB_PTR_BATCH) throw std::invalid_argument("scatter_items: bad batch");
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * words * nb, 0.0, s, 1);
+    k_scatter_items<<<dim3(copy_grid(words / 2), nb), 256, 0, s>>>(dst, reinterpret_cast<const ulonglong2 *>(src),
+                                                                    words / 2);
+    check_launch("scatter_items");
 }
 
 void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s) {

@@ -70,6 +70,10 @@ unsigned long long launch_count();     // kernels launched since load
 // ---- NTT -----------------------------------------------------------------
 void ntt_forward(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s);
 void ntt_inverse(u64 *data, int nrows, RowMap map, const NttTables &t, cudaStream_t s);
+// out-of-place inverse: dst rows (contiguous) from source items of per_item
+// rows at src_stride
+void ntt_inverse_from(u64 *dst, const u64 *src, size_t src_stride, int per_item, int nrows, RowMap map,
+                      const NttTables &t, cudaStream_t s);
 
 // ---- elementwise ---------------------------------------------------------
 // out = a op b on nrows rows (rows map to primes with `map`)
@@ -203,5 +207,22 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
 
 // copy rows with optional automorphism (used to place P*c parts etc.)
 void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s);
+
+// ---- batched copies (one launch per batch; words, strides and pointers are
+// whole limbs, so 16-byte aligned) ------------------------------------------------
+// dst[b * dstride + i] = src[b * sstride + i] for i < words, b < nb
+void copy_strided(u64 *dst, size_t dstride, const u64 *src, size_t sstride, size_t words, int nb, cudaStream_t s);
+#define HB_PTR_BATCH 128
+struct PtrBatch {
+    const u64 *p[HB_PTR_BATCH];
+};
+struct PtrBatchW {
+    u64 *p[HB_PTR_BATCH];
+};
+// dst[b][j * words + i] = seg_j.p[b][i] for the nseg (1 or 2) segments of item b
+void gather_items(u64 *dst, const PtrBatch &seg0, const PtrBatch &seg1, int nseg, size_t words, int nb,
+                  cudaStream_t s);
+// dst.p[b][i] = src[b * words + i]
+void scatter_items(const PtrBatchW &dst, const u64 *src, size_t words, int nb, cudaStream_t s);
 
 }  // namespace hb
