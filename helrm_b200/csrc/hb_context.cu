@@ -62,6 +62,7 @@ struct Ct {
     int npoly = 2;
     double scale = 1.0;
     int slots = 0;
+    bool xfer = false;  // an asynchronous download may still read d: free behind it
 };
 struct Pt {
     u64 *d = nullptr;
@@ -136,14 +137,58 @@ public:
         peak = std::max(peak, live);
         return (u64 *)p;
     }
-    void release(void *p) {
+    void release(void *p, cudaStream_t on = nullptr) {
         if (!p) return;
         auto it = alloc_sizes.find(p);
         if (it != alloc_sizes.end()) {
             live -= it->second;
             alloc_sizes.erase(it);
         }
-        cudaFreeAsync(p, stream);
+        cudaFreeAsync(p, on ? on : stream);
+    }
+    u64 *alloc_on(size_t words, cudaStream_t s) {
+        void *p = nullptr;
+        if (words == 0) words = 1;
+        cuda_check(cudaMallocAsync(&p, words * sizeof(u64), s), "cudaMallocAsync");
+        alloc_sizes[p] = words * sizeof(u64);
+        live += words * sizeof(u64);
+        peak = std::max(peak, live);
+        return (u64 *)p;
+    }
+
+    // ---------------------------------------------------------- transfer streams
+    // Host <-> device copies of whole ciphertexts run on two more streams, one
+    // per direction (PCIe is full duplex), so that they overlap each other and
+    // the arithmetic on `stream`; events order the streams.
+    cudaStream_t up = nullptr, dn = nullptr;
+    cudaEvent_t ev_up = nullptr, ev_dn = nullptr, ev_comp = nullptr;
+    void ensure_xfer() {
+        if (up) return;
+        cuda_check(cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking), "upload stream");
+        cuda_check(cudaStreamCreateWithFlags(&dn, cudaStreamNonBlocking), "download stream");
+        cuda_check(cudaEventCreateWithFlags(&ev_up, cudaEventDisableTiming), "event");
+        cuda_check(cudaEventCreateWithFlags(&ev_dn, cudaEventDisableTiming), "event");
+        cuda_check(cudaEventCreateWithFlags(&ev_comp, cudaEventDisableTiming), "event");
+    }
+    // `on` waits for everything issued on `after` so far
+    void wait_for(cudaStream_t on, cudaStream_t after, cudaEvent_t ev) {
+        cuda_check(cudaEventRecord(ev, after), "event");
+        cuda_check(cudaStreamWaitEvent(on, ev, 0), "wait");
+    }
+    void sync_xfer() {
+        if (up) cuda_check(cudaStreamSynchronize(up), "upload sync");
+        if (dn) cuda_check(cudaStreamSynchronize(dn), "download sync");
+    }
+    // free a ciphertext's memory; behind both the arithmetic and the download
+    // stream when a download may be in flight
+    void release_ct(Ct &c) {
+        if (c.xfer && dn) {
+            wait_for(dn, stream, ev_comp);
+            release(c.d, dn);
+        } else {
+            release(c.d);
+        }
+        c.d = nullptr;
     }
     void zero(u64 *p, size_t words) { cuda_check(cudaMemsetAsync(p, 0, words * 8, stream), "memset"); }
     void d2d(u64 *dst, const u64 *src, size_t words) {
@@ -387,6 +432,10 @@ public:
     ~Context() {
         if (stream) {
             cudaStreamSynchronize(stream);
+            if (up) {
+                cudaStreamSynchronize(up);
+                cudaStreamSynchronize(dn);
+            }
             for (auto &kv : cts) release(kv.second.d);
             for (auto &kv : pts) release(kv.second.d);
             for (auto &kv : lts) free_lt(*kv.second);
@@ -396,7 +445,18 @@ public:
             for (auto &t : lv) release(t.blob);
             release(d_pmod);
             release(d_tables);
+            if (up) {
+                cudaStreamSynchronize(up);
+                cudaStreamSynchronize(dn);
+            }
             cudaStreamSynchronize(stream);
+            if (up) {
+                cudaEventDestroy(ev_up);
+                cudaEventDestroy(ev_dn);
+                cudaEventDestroy(ev_comp);
+                cudaStreamDestroy(up);
+                cudaStreamDestroy(dn);
+            }
             cudaStreamDestroy(stream);
         }
     }
@@ -430,7 +490,7 @@ public:
     void del_ct(int id) {
         auto it = cts.find(id);
         if (it == cts.end()) return;
-        release(it->second.d);
+        release_ct(it->second);
         cts.erase(it);
     }
     void del_pt(int id) {
@@ -449,7 +509,7 @@ public:
     void replace_ct(int id, int from) {
         Ct &dst = ct(id);
         Ct src = ct(from);
-        release(dst.d);
+        release_ct(dst);
         dst = src;
         cts.erase(from);
     }
@@ -1842,6 +1902,51 @@ HB_API int helrm_NewCiphertextFromData(const uint64_t *data, int level, int npol
         *out = c.put_ct(o);
     });
 }
+HB_API int helrm_UploadCiphertextsAsync(const uint64_t *const *host, int n, int level, int npoly, double scale,
+                                        int *out_ids) {
+    return guard([&] {
+        Context &c = C();
+        if (!host || !out_ids || n <= 0 || level < 0 || level >= c.L || npoly < 2 || npoly > 3)
+            HB_THROW(HB_EINVAL, "UploadCiphertextsAsync: bad arguments");
+        for (int i = 0; i < n; i++)
+            if (!host[i]) HB_THROW(HB_EINVAL, "UploadCiphertextsAsync: null host buffer");
+        c.ensure_xfer();
+        const size_t words = (size_t)npoly * (level + 1) * c.N;
+        for (int i = 0; i < n; i++) {
+            Ct o;
+            o.nq = level + 1;
+            o.npoly = npoly;
+            o.scale = scale;
+            o.slots = c.slots;
+            o.d = c.alloc_on(words, c.up);
+            cuda_check(cudaMemcpyAsync(o.d, host[i], words * 8, cudaMemcpyHostToDevice, c.up), "h2d");
+            out_ids[i] = c.put_ct(o);
+        }
+        c.wait_for(c.stream, c.up, c.ev_up);
+    });
+}
+HB_API int helrm_DownloadCiphertextsAsync(const int *ids, int n, uint64_t *const *host, size_t words_each) {
+    return guard([&] {
+        Context &c = C();
+        if (!ids || !host || n <= 0) HB_THROW(HB_EINVAL, "DownloadCiphertextsAsync: bad arguments");
+        for (int i = 0; i < n; i++) {
+            const Ct &x = c.ct(ids[i]);
+            if (!host[i] || words_each < (size_t)x.npoly * x.nq * c.N)
+                HB_THROW(HB_EINVAL, "DownloadCiphertextsAsync: buffer too small");
+        }
+        c.ensure_xfer();
+        c.wait_for(c.dn, c.stream, c.ev_comp);
+        for (int i = 0; i < n; i++) {
+            Ct &x = c.ct(ids[i]);
+            cuda_check(cudaMemcpyAsync(host[i], x.d, (size_t)x.npoly * x.nq * c.N * 8, cudaMemcpyDeviceToHost, c.dn),
+                       "d2h");
+            x.xfer = true;
+        }
+    });
+}
+HB_API int helrm_TransferSync(void) {
+    return guard([&] { C().sync_xfer(); });
+}
 HB_API int helrm_GetPlaintextData(int pt, uint64_t *out, size_t words) {
     return guard([&] {
         Context &c = C();
@@ -2066,6 +2171,10 @@ HB_API int helrm_TimerStop(double *ms) {
         Context &c = C();
         OUT(ms);
         if (!g_t0) HB_THROW(HB_ESTATE, "TimerStop without TimerStart");
+        if (c.up) {  // the region ends after the transfers issued in it, too
+            c.wait_for(c.stream, c.up, c.ev_up);
+            c.wait_for(c.stream, c.dn, c.ev_dn);
+        }
         cuda_check(cudaEventRecord(g_t1, c.stream), "event record");
         cuda_check(cudaEventSynchronize(g_t1), "event sync");
         float f = 0.f;

@@ -18,8 +18,9 @@
  *   - plain pointers and sizes only; arrays are caller-allocated;
  *   - single-threaded and stateful like the reference (one scheme per
  *     process, orion/backend/lattigo/scheme.go:32); all GPU work is
- *     enqueued on the library's own stream and synchronised only where a
- *     result crosses to the host.
+ *     enqueued on the library's own stream (the asynchronous batch
+ *     transfers on two more, ordered with events) and synchronised only
+ *     where a result crosses to the host.
  * Levels follow Orion: a ciphertext at level l has l+1 residue limbs, a
  * fresh one sits at len(LogQ)-1 (orion/backend/python/parameters.py:258).
  * Rotation by k is a left shift, rot(ct,k)[i] = ct[i+k], shifts reduced to
@@ -187,6 +188,24 @@ int helrm_GetKeyData(uint64_t galois, uint64_t *out, size_t words);
 int helrm_GetSecretKeyData(uint64_t *out, size_t words);
 /* extended-basis plaintext of diagonal `k` of a transform */
 int helrm_GetLinearTransformPlaintext(int lt, int k, uint64_t *out, size_t words);
+
+/* ---- asynchronous batch transfers (no reference counterpart: the reference
+ * uploads with Encrypt on the device and reads results through Decrypt/Decode,
+ * examples/criteo/bench_sweep.py:225-243).  Copies run on two more streams,
+ * one per direction, and overlap the arithmetic; the library orders them with
+ * events.  Host buffers should be pinned (page-locked) for the copies to be
+ * asynchronous, and must stay valid and unmodified until helrm_TransferSync
+ * returns. ------------------------------------------------------------------- */
+/* n ciphertexts [npoly][level+1][N] from host[i]; ids written to out_ids.
+ * Work issued later on the ciphertexts waits for the copies on the device. */
+int helrm_UploadCiphertextsAsync(const uint64_t *const *host, int n, int level, int npoly, double scale,
+                                 int *out_ids);
+/* copy n ciphertexts to host[i] (each at least words_each words) after all
+ * work issued so far; deleting them afterwards is safe (the memory is freed
+ * behind the copy). */
+int helrm_DownloadCiphertextsAsync(const int *ids, int n, uint64_t *const *host, size_t words_each);
+/* wait for every asynchronous transfer */
+int helrm_TransferSync(void);
 
 /* ---- kernel-level entry points on device pointers (microbenchmarks) --------- */
 /* Forward / inverse NTT in place on nrows limbs laid out as blocks of
