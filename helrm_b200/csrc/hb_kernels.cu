@@ -441,21 +441,13 @@ __device__ __forceinline__ void inv_a(u64 (&x)[16], const u64 *W, const u64 *Wp,
     }
 }
 
-// ---- primes below 2^40: twiddle pairs {w, fl(w/q)} and the double-precision
-// quotient of mul_fq_c.  Forward butterflies are left uncorrected: with
-// inputs below B, x + q +- (y*w mod q centred) stays below B + 1.52q, so the
-// 16 stages end below 26q < 2^45 and one reduction per element follows.
-// The inverse keeps Gentleman-Sande values in [0, 2q).
+// ---- primes below 2^40, inverse: twiddle pairs {w, fl(w/q)} and the
+// double-precision quotient of mul_fq_c.  Gentleman-Sande values stay in
+// [0, 2q).
 template <bool G>
 __device__ __forceinline__ ulonglong2 twld(const ulonglong2 *t, int i) {
     if (G) return __ldg(t + i);
     return t[i];
-}
-__device__ __forceinline__ void ct_bfly_f(u64 &x, u64 &y, ulonglong2 tw, u64 q, u64 nq) {
-    const u64 P = mul_fq_c(y, tw.x, __longlong_as_double((long long)tw.y), nq);
-    const u64 xq = x + q;
-    x = xq + P;
-    y = xq - P;
 }
 __device__ __forceinline__ void gs_bfly_f(u64 &x, u64 &y, ulonglong2 tw, u64 q, u64 nq) {
     const u64 two_q = 2 * q;
@@ -465,29 +457,64 @@ __device__ __forceinline__ void gs_bfly_f(u64 &x, u64 &y, ulonglong2 tw, u64 q, 
     x = s;
     y = mul_fq_c(d, tw.x, __longlong_as_double((long long)tw.y), nq) + q;
 }
+// Forward butterflies in double precision (primes below 2^40).  Values are
+// exact integers held as doubles, centred (possibly negative).  With
+// Q = round(y fl(w/q)) (magic-number rounding), ph + pl = Q q exactly
+// (TwoProduct: ph = fl(Q q), pl = fma(Q, q, -ph)), and fma(y, w, -ph) is the
+// exact integer y w - ph (below 2^41 in magnitude), so
+// t = y w - Q q = fma(y, w, -ph) - pl exactly, |t| <= 0.502 q for |y| < 2^44.
+// x' = x + t, y' = x - t: magnitudes grow by 0.502 q per stage, below 9.1 q
+// after 16 stages.  Eight FP64 instructions, no integer multiply: the FP64
+// pipe is as fast as the integer-multiply pipe and otherwise idle.
+__device__ __forceinline__ double u64_to_d(u64 v) {
+    return __dsub_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), 4503599627370496.0);
+}
+__device__ __forceinline__ void ct_bfly_d(double &x, double &y, const double2 tw, double q) {
+    const double magic = 6755399441055744.0;  // 1.5 * 2^52
+    const double Qd = __dsub_rn(__fma_rn(y, tw.y, magic), magic);
+    const double ph = __dmul_rn(Qd, q);
+    const double pl = __fma_rn(Qd, q, -ph);
+    const double t = __dsub_rn(__fma_rn(y, tw.x, -ph), pl);
+    const double xn = __dadd_rn(x, t);
+    y = __dsub_rn(x, t);
+    x = xn;
+}
 template <bool G>
-__device__ __forceinline__ void fwd_a_f(u64 (&x)[16], const ulonglong2 *T, int base, u64 q, u64 nq) {
+__device__ __forceinline__ double2 twld_d(const double2 *t, int i) {
+    if (G) return __ldg(t + i);
+    return t[i];
+}
+template <bool G>
+__device__ __forceinline__ void fwd_a_d(double (&x)[16], const double2 *T, int base, double q) {
 #pragma unroll
     for (int s = 0; s < 4; s++) {
         const int d = 8 >> s, g = 1 << s;
 #pragma unroll
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
-            ct_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (k >> (4 - s))), q, nq);
+            ct_bfly_d(x[k], x[k + d], twld_d<G>(T, g * base + (k >> (4 - s))), q);
         }
     }
 }
 template <bool G>
-__device__ __forceinline__ void fwd_b_f(u64 (&x)[16], const ulonglong2 *T, int base, int c, u64 q, u64 nq) {
+__device__ __forceinline__ void fwd_b_d(double (&x)[16], const double2 *T, int base, int c, double q) {
 #pragma unroll
     for (int s = 0; s < 4; s++) {
         const int d = 8 >> s, g = 16 << s;
 #pragma unroll
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
-            ct_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (c << s) + (k >> (4 - s))), q, nq);
+            ct_bfly_d(x[k], x[k + d], twld_d<G>(T, g * base + (c << s) + (k >> (4 - s))), q);
         }
     }
+}
+// centred double v (|v| < 2^51) -> v mod q in [0, q) as u64
+__device__ __forceinline__ u64 d_mod_to_u64(double v, double q, double qinv) {
+    const double magic = 6755399441055744.0;
+    const double Qd = __dsub_rn(__fma_rn(v, qinv, magic), magic);
+    double r = __fma_rn(-Qd, q, v);  // exact: |r| <= 0.5 q + tiny
+    if (r < 0.0) r = __dadd_rn(r, q);
+    return (u64)__double_as_longlong(__dadd_rn(r, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
 }
 template <bool G>
 __device__ __forceinline__ void inv_b_f(u64 (&x)[16], const ulonglong2 *T, int base, int c, u64 q, u64 nq) {
@@ -536,30 +563,37 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
     const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
     if (fast) stw[threadIdx.x] = __ldg(twx + ((size_t)p << 16) + threadIdx.x);
     u64 x[16];
-    if (!INV) {
+    if (!INV && fast) {
+        // double-precision butterflies; the block pass receives the centred
+        // values as doubles (|v| < 5 q) and reduces at its end
+        const double qd = (double)q;
+        const double2 *stwd = reinterpret_cast<const double2 *>(stw);
+        double xd[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) xd[k] = u64_to_d(a[(size_t)(c + 16 * k) << 8]);
+        __syncthreads();
+        fwd_a_d<false>(xd, stwd, 1, qd);
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[(c + 16 * k) * 17 + col] = (u64)__double_as_longlong(xd[k]);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sm[(16 * c + k) * 17 + col]);
+        fwd_b_d<false>(xd, stwd, 1, c, qd);
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = (u64)__double_as_longlong(xd[k]);
+    } else if (!INV) {
+        // primes of 40 bits and more: Harvey's lazy butterflies in [0, 4q)
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(c + 16 * k) << 8];
-        if (fast) {
-            __syncthreads();
-            fwd_a_f<false>(x, stw, 1, q, nq);
-        } else {
-            fwd_a(x, W, Wp, 1, q);
-        }
+        fwd_a(x, W, Wp, 1, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) sm[(c + 16 * k) * 17 + col] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sm[(16 * c + k) * 17 + col];
-        if (fast) {
-            // left uncorrected (below 14q) for the block pass
-            fwd_b_f<false>(x, stw, 1, c, q, nq);
+        fwd_b(x, W, Wp, 1, c, q);
 #pragma unroll
-            for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = x[k];
-        } else {
-            fwd_b(x, W, Wp, 1, c, q);
-#pragma unroll
-            for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = reduce4q(x[k], q);
-        }
+        for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = reduce4q(x[k], q);
     } else {
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(16 * c + k) << 8];
@@ -605,29 +639,39 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
     const ulonglong2 *T = twx + ((size_t)p << 16);
     u64 *sb = sm + blk * 272;  // 256 elements of this block, 17-word rows of 16 (padding)
     u64 x[16];
-    if (!INV) {
+    if (!INV && fast) {
+        // doubles from the column pass; reduced and converted at the end
+        const double qd = (double)q, qinv = c_pc[p].qinv;
+        const double2 *Td = reinterpret_cast<const double2 *>(T);
+        double xd[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)a[c + 16 * k]);
+        fwd_a_d<true>(xd, Td, 256 + rb, qd);
+#pragma unroll
+        for (int k = 0; k < 16; k++) sb[k * 17 + c] = (u64)__double_as_longlong(xd[k]);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sb[c * 17 + k]);
+        fwd_b_d<true>(xd, Td, 256 + rb, c, qd);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) sb[c * 17 + k] = d_mod_to_u64(xd[k], qd, qinv);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[c + 16 * k] = sb[k * 17 + c];
+    } else if (!INV) {
+        // primes of 40 bits and more: Harvey's lazy butterflies in [0, 4q)
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[c + 16 * k];
-        if (fast)
-            fwd_a_f<true>(x, T, 256 + rb, q, nq);
-        else
-            fwd_a(x, W, Wp, 256 + rb, q);
+        fwd_a(x, W, Wp, 256 + rb, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[k * 17 + c] = x[k];  // element c + 16k at (k, c)
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];  // element 16c + k
-        if (fast) {
-            // values below 26q: one Barrett step with floor(2^64/q)
-            fwd_b_f<true>(x, T, 256 + rb, c, q, nq);
-            const u64 onep = c_pc[p].onep;
+        fwd_b(x, W, Wp, 256 + rb, c, q);
 #pragma unroll
-            for (int k = 0; k < 16; k++) x[k] = mul_shoup(x[k], 1ull, onep, q);
-        } else {
-            fwd_b(x, W, Wp, 256 + rb, c, q);
-#pragma unroll
-            for (int k = 0; k < 16; k++) x[k] = reduce4q(x[k], q);
-        }
+        for (int k = 0; k < 16; k++) x[k] = reduce4q(x[k], q);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[c * 17 + k] = x[k];
