@@ -57,31 +57,6 @@ __device__ __forceinline__ u64 mul_shoup_lazy(u64 a, u64 w, u64 wp, u64 q) {
     return a * w - hi * q;
 }
 
-// y*w mod q for q < 2^40 and y < 2^47 with the Shoup quotient estimated in
-// double precision instead of a 64x64-bit high product.  wq = fl(w/q)
-// (relative error <= 2^-53).  y < 2^52 becomes a double exactly by placing
-// it in the mantissa of 2^52 (bit pattern 0x4330... | y) and subtracting
-// 2^52; fma(y, wq, 2^52) rounds y*wq to the nearest integer Q, read back
-// from the mantissa bits.  |y*wq - y*w/q| <= y 2^-53 <= 2^-6, so
-// |Q - y*w/q| <= 0.52 and the result y*w - Q*q is a signed value in
-// [-0.52q, 0.52q] (two's complement modulo 2^64).  It is formed as
-// y*w + Q*nq modulo 2^64 (nq = 2^64 - q): two 32x32->64 multiply-adds for
-// the low words and four 32-bit cross products added into the high word.
-// The double-precision pipe is separate from the integer-multiply pipe,
-// which the rest of the arithmetic keeps busy.
-__device__ __forceinline__ u64 mul_fq_c(u64 y, u64 w, double wq, u64 nq) {
-    const double two52 = 4503599627370496.0;
-    const double yd = __longlong_as_double((long long)(y | 0x4330000000000000ull)) - two52;
-    const u64 Q = (u64)__double_as_longlong(__fma_rn(yd, wq, two52)) & 0x000FFFFFFFFFFFFFull;
-    const unsigned yl = (unsigned)y, yh = (unsigned)(y >> 32), wl = (unsigned)w, wh = (unsigned)(w >> 32);
-    const unsigned Ql = (unsigned)Q, Qh = (unsigned)(Q >> 32), nl = (unsigned)nq, nh = (unsigned)(nq >> 32);
-    u64 lo;
-    asm("mul.wide.u32 %0, %1, %2;" : "=l"(lo) : "r"(yl), "r"(wl));
-    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(lo) : "r"(Ql), "r"(nl));
-    const unsigned hi = yl * wh + yh * wl + Ql * nh + Qh * nl;
-    return lo + ((u64)hi << 32);
-}
-
 struct u128 {
     u64 lo, hi;
 };

@@ -290,11 +290,12 @@ public:
                 for (int i = 0; i < N; i++) {
                     // both operands exact doubles: the quotient is correctly rounded
                     const double tq = (double)T[i] / (double)q, iq = (double)I[i] / (double)q;
-                    // forward pairs as doubles {w, fl(w/q)} (double-precision butterflies)
+                    // pairs of doubles {w, fl(w/q)} (double-precision butterflies)
                     const double td = (double)T[i];
                     std::memcpy(&Tx[2 * i], &td, 8);
                     std::memcpy(&Tx[2 * i + 1], &tq, 8);
-                    Ix[2 * i] = I[i];
+                    const double id = (double)I[i];
+                    std::memcpy(&Ix[2 * i], &id, 8);
                     std::memcpy(&Ix[2 * i + 1], &iq, 8);
                 }
             }

@@ -441,22 +441,6 @@ __device__ __forceinline__ void inv_a(u64 (&x)[16], const u64 *W, const u64 *Wp,
     }
 }
 
-// ---- primes below 2^40, inverse: twiddle pairs {w, fl(w/q)} and the
-// double-precision quotient of mul_fq_c.  Gentleman-Sande values stay in
-// [0, 2q).
-template <bool G>
-__device__ __forceinline__ ulonglong2 twld(const ulonglong2 *t, int i) {
-    if (G) return __ldg(t + i);
-    return t[i];
-}
-__device__ __forceinline__ void gs_bfly_f(u64 &x, u64 &y, ulonglong2 tw, u64 q, u64 nq) {
-    const u64 two_q = 2 * q;
-    u64 s = x + y;
-    if (s >= two_q) s -= two_q;
-    const u64 d = x + two_q - y;
-    x = s;
-    y = mul_fq_c(d, tw.x, __longlong_as_double((long long)tw.y), nq) + q;
-}
 // Forward butterflies in double precision (primes below 2^40).  Values are
 // exact integers held as doubles, centred (possibly negative).  With
 // Q = round(y fl(w/q)) (magic-number rounding), ph + pl = Q q exactly
@@ -516,28 +500,57 @@ __device__ __forceinline__ u64 d_mod_to_u64(double v, double q, double qinv) {
     if (r < 0.0) r = __dadd_rn(r, q);
     return (u64)__double_as_longlong(__dadd_rn(r, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
 }
+// Inverse (Gentleman-Sande) butterflies in double precision: x' = x + y,
+// y' = (x - y) w mod q (centred, as in ct_bfly_d).  Sums grow: from values
+// below B a 4-stage group ends below 16 B, so every group ends by re-centring
+// its 16 values to |v| <= 0.5 q; the first group starts from [0, q) and stays
+// below 16 q < 2^44, the bound of the exact product.
+__device__ __forceinline__ double mulmod_d(double y, const double2 tw, double q) {
+    const double magic = 6755399441055744.0;  // 1.5 * 2^52
+    const double Qd = __dsub_rn(__fma_rn(y, tw.y, magic), magic);
+    const double ph = __dmul_rn(Qd, q);
+    const double pl = __fma_rn(Qd, q, -ph);
+    return __dsub_rn(__fma_rn(y, tw.x, -ph), pl);
+}
+__device__ __forceinline__ double center_d(double v, double q, double qinv) {
+    const double magic = 6755399441055744.0;
+    const double Qd = __dsub_rn(__fma_rn(v, qinv, magic), magic);
+    return __fma_rn(-Qd, q, v);  // exact
+}
+__device__ __forceinline__ void gs_bfly_d(double &x, double &y, const double2 tw, double q) {
+    const double sm = __dadd_rn(x, y);
+    const double df = __dsub_rn(x, y);
+    x = sm;
+    y = mulmod_d(df, tw, q);
+}
 template <bool G>
-__device__ __forceinline__ void inv_b_f(u64 (&x)[16], const ulonglong2 *T, int base, int c, u64 q, u64 nq) {
+__device__ __forceinline__ void inv_b_d(double (&x)[16], const double2 *T, int base, int c, double q, double qinv) {
 #pragma unroll
     for (int s = 3; s >= 0; s--) {
         const int d = 8 >> s, g = 16 << s;
 #pragma unroll
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
-            gs_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (c << s) + (k >> (4 - s))), q, nq);
+            gs_bfly_d(x[k], x[k + d], twld_d<G>(T, g * base + (c << s) + (k >> (4 - s))), q);
         }
     }
+#pragma unroll
+    for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
 }
-template <bool G>
-__device__ __forceinline__ void inv_a_f(u64 (&x)[16], const ulonglong2 *T, int base, u64 q, u64 nq) {
+template <bool G, bool CENTER>
+__device__ __forceinline__ void inv_a_d(double (&x)[16], const double2 *T, int base, double q, double qinv) {
 #pragma unroll
     for (int s = 3; s >= 0; s--) {
         const int d = 8 >> s, g = 1 << s;
 #pragma unroll
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
-            gs_bfly_f(x[k], x[k + d], twld<G>(T, g * base + (k >> (4 - s))), q, nq);
+            gs_bfly_d(x[k], x[k + d], twld_d<G>(T, g * base + (k >> (4 - s))), q);
         }
+    }
+    if (CENTER) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
     }
 }
 
@@ -556,7 +569,6 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
     const int p = map.prime(row);
     const u64 q = c_pc[p].q;
     const bool fast = q < (1ull << 40);
-    const u64 nq = 0ull - q;
     const int col = threadIdx.x & 15, c = threadIdx.x >> 4;
     const int c0 = blockIdx.x << 4;
     u64 *a = data + ((size_t)row << 16) + c0 + col;
@@ -594,24 +606,42 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
         fwd_b(x, W, Wp, 1, c, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) a[(size_t)(16 * c + k) << 8] = reduce4q(x[k], q);
+    } else if (fast) {
+        // second pass of the double-precision inverse: doubles from the block
+        // pass (|v| <= 0.5 q), the last 8 stages, then the factor N^-1
+        const double qd = (double)q, qinv = c_pc[p].qinv;
+        const double2 *stwd = reinterpret_cast<const double2 *>(stw);
+        double xd[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)a[(size_t)(16 * c + k) << 8]);
+        __syncthreads();
+        inv_b_d<false>(xd, stwd, 1, c, qd, qinv);
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[(16 * c + k) * 17 + col] = (u64)__double_as_longlong(xd[k]);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sm[(c + 16 * k) * 17 + col]);
+        inv_a_d<false, false>(xd, stwd, 1, qd, qinv);
+        const double nid = (double)c_pc[p].ninv;
+        const double2 ni = make_double2(nid, __ddiv_rn(nid, qd));
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            double r = mulmod_d(xd[k], ni, qd);  // |r| <= 0.502 q
+            if (r < 0.0) r = __dadd_rn(r, qd);
+            a[(size_t)(c + 16 * k) << 8] =
+                (u64)__double_as_longlong(__dadd_rn(r, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
+        }
     } else {
+        // primes of 40 bits and more: Gentleman-Sande values in [0, 2q)
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(16 * c + k) << 8];
-        if (fast) {
-            __syncthreads();
-            inv_b_f<false>(x, stw, 1, c, q, nq);
-        } else {
-            inv_b(x, W, Wp, 1, c, q);
-        }
+        inv_b(x, W, Wp, 1, c, q);
 #pragma unroll
         for (int k = 0; k < 16; k++) sm[(16 * c + k) * 17 + col] = x[k];
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sm[(c + 16 * k) * 17 + col];
-        if (fast)
-            inv_a_f<false>(x, stw, 1, q, nq);
-        else
-            inv_a(x, W, Wp, 1, q);
+        inv_a(x, W, Wp, 1, q);
         const u64 ni = c_pc[p].ninv, nip = c_pc[p].ninvp;
 #pragma unroll
         for (int k = 0; k < 16; k++) a[(size_t)(c + 16 * k) << 8] = mul_shoup(x[k], ni, nip, q);
@@ -631,7 +661,6 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
     const int p = map.prime(row);
     const u64 q = c_pc[p].q;
     const bool fast = q < (1ull << 40);
-    const u64 nq = 0ull - q;
     const int c = threadIdx.x & 15, blk = threadIdx.x >> 4;
     const int rb = (blockIdx.x << 4) + blk;
     u64 *a = data + ((size_t)row << 16) + ((size_t)rb << 8);
@@ -687,24 +716,38 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[k * 17 + c] = ain[c + 16 * k];
         __syncthreads();
+        if (fast) {
+            // first pass of the double-precision inverse; the column pass
+            // receives centred doubles (|v| <= 0.5 q)
+            const double qd = (double)q, qinv = c_pc[p].qinv;
+            const double2 *Td = reinterpret_cast<const double2 *>(T);
+            double xd[16];
 #pragma unroll
-        for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];
-        if (fast)
-            inv_b_f<true>(x, T, 256 + rb, c, q, nq);
-        else
+            for (int k = 0; k < 16; k++) xd[k] = u64_to_d(sb[c * 17 + k]);
+            inv_b_d<true>(xd, Td, 256 + rb, c, qd, qinv);
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 16; k++) sb[c * 17 + k] = (u64)__double_as_longlong(xd[k]);
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sb[k * 17 + c]);
+            inv_a_d<true, true>(xd, Td, 256 + rb, qd, qinv);
+#pragma unroll
+            for (int k = 0; k < 16; k++) a[c + 16 * k] = (u64)__double_as_longlong(xd[k]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; k++) x[k] = sb[c * 17 + k];
             inv_b(x, W, Wp, 256 + rb, c, q);
-        __syncthreads();
+            __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) sb[c * 17 + k] = x[k];
-        __syncthreads();
+            for (int k = 0; k < 16; k++) sb[c * 17 + k] = x[k];
+            __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) x[k] = sb[k * 17 + c];
-        if (fast)
-            inv_a_f<true>(x, T, 256 + rb, q, nq);
-        else
+            for (int k = 0; k < 16; k++) x[k] = sb[k * 17 + c];
             inv_a(x, W, Wp, 256 + rb, q);
 #pragma unroll
-        for (int k = 0; k < 16; k++) a[c + 16 * k] = x[k];  // [0, 2q): the column pass reduces
+            for (int k = 0; k < 16; k++) a[c + 16 * k] = x[k];  // [0, 2q): the column pass reduces
+        }
     }
 }
 

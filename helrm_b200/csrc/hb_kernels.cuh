@@ -45,8 +45,7 @@ inline RowMap rowmap(int per, int nq, int L) {
 struct NttTables {
     const u64 *tw, *twp;    // [P][N] psi^brv(i) and Shoup companions
     const u64 *itw, *itwp;  // [P][N] psi^-brv(i)
-    // [P][N] pairs for primes below 2^40 (else 0): forward {w, fl(w/q)} as
-    // doubles; inverse {w, bits of fl(w/q)}
+    // [P][N] pairs of doubles {w, fl(w/q)} for primes below 2^40 (else 0)
     const ulonglong2 *twx, *itwx;
     int logN;
 };
