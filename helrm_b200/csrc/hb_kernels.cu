@@ -468,6 +468,56 @@ __device__ __forceinline__ double2 twld_d(const double2 *t, int i) {
     if (G) return __ldg(t + i);
     return t[i];
 }
+// NP consecutive twiddle pairs from global memory, two pairs per 256-bit
+// load (the start is 32-byte aligned for NP >= 2: an even pair index)
+template <int NP>
+__device__ __forceinline__ void ld_pairs(double2 (&tw)[8], const double2 *src) {
+    if (NP == 1) {
+        tw[0] = __ldg(src);
+    } else {
+#pragma unroll
+        for (int v = 0; v < NP / 2; v++)
+            asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
+                : "=d"(tw[2 * v].x), "=d"(tw[2 * v].y), "=d"(tw[2 * v + 1].x), "=d"(tw[2 * v + 1].y)
+                : "l"(src + 2 * v));
+    }
+}
+// the two forward halves with twiddles from global memory (block pass):
+// stage s needs 2^s consecutive pairs per thread, loaded at the stage start
+__device__ __forceinline__ void fwd_a_dg(double (&x)[16], const double2 *T, int base, double q) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 1 << s;
+        double2 tw[8];
+        if (s == 0) ld_pairs<1>(tw, T + base);
+        if (s == 1) ld_pairs<2>(tw, T + 2 * base);
+        if (s == 2) ld_pairs<4>(tw, T + 4 * base);
+        if (s == 3) ld_pairs<8>(tw, T + 8 * base);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            ct_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
+        }
+        (void)g;
+    }
+}
+__device__ __forceinline__ void fwd_b_dg(double (&x)[16], const double2 *T, int base, int c, double q) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 16 << s;
+        double2 tw[8];
+        const double2 *src = T + g * base + (c << s);
+        if (s == 0) ld_pairs<1>(tw, src);
+        if (s == 1) ld_pairs<2>(tw, src);
+        if (s == 2) ld_pairs<4>(tw, src);
+        if (s == 3) ld_pairs<8>(tw, src);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            ct_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
+        }
+    }
+}
 template <bool G>
 __device__ __forceinline__ void fwd_a_d(double (&x)[16], const double2 *T, int base, double q) {
 #pragma unroll
@@ -532,6 +582,44 @@ __device__ __forceinline__ void inv_b_d(double (&x)[16], const double2 *T, int b
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
             gs_bfly_d(x[k], x[k + d], twld_d<G>(T, g * base + (c << s) + (k >> (4 - s))), q);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
+}
+// inverse halves with twiddles from global memory (block pass), wide loads
+__device__ __forceinline__ void inv_b_dg(double (&x)[16], const double2 *T, int base, int c, double q, double qinv) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 16 << s;
+        double2 tw[8];
+        const double2 *src = T + g * base + (c << s);
+        if (s == 0) ld_pairs<1>(tw, src);
+        if (s == 1) ld_pairs<2>(tw, src);
+        if (s == 2) ld_pairs<4>(tw, src);
+        if (s == 3) ld_pairs<8>(tw, src);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            gs_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
+}
+__device__ __forceinline__ void inv_a_dg(double (&x)[16], const double2 *T, int base, double q, double qinv) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s;
+        double2 tw[8];
+        if (s == 0) ld_pairs<1>(tw, T + base);
+        if (s == 1) ld_pairs<2>(tw, T + 2 * base);
+        if (s == 2) ld_pairs<4>(tw, T + 4 * base);
+        if (s == 3) ld_pairs<8>(tw, T + 8 * base);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            gs_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
         }
     }
 #pragma unroll
@@ -675,13 +763,13 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
         double xd[16];
 #pragma unroll
         for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)a[c + 16 * k]);
-        fwd_a_d<true>(xd, Td, 256 + rb, qd);
+        fwd_a_dg(xd, Td, 256 + rb, qd);
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[k * 17 + c] = (u64)__double_as_longlong(xd[k]);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sb[c * 17 + k]);
-        fwd_b_d<true>(xd, Td, 256 + rb, c, qd);
+        fwd_b_dg(xd, Td, 256 + rb, c, qd);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[c * 17 + k] = d_mod_to_u64(xd[k], qd, qinv);
@@ -724,14 +812,14 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
             double xd[16];
 #pragma unroll
             for (int k = 0; k < 16; k++) xd[k] = u64_to_d(sb[c * 17 + k]);
-            inv_b_d<true>(xd, Td, 256 + rb, c, qd, qinv);
+            inv_b_dg(xd, Td, 256 + rb, c, qd, qinv);
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 16; k++) sb[c * 17 + k] = (u64)__double_as_longlong(xd[k]);
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sb[k * 17 + c]);
-            inv_a_d<true, true>(xd, Td, 256 + rb, qd, qinv);
+            inv_a_dg(xd, Td, 256 + rb, qd, qinv);
 #pragma unroll
             for (int k = 0; k < 16; k++) a[c + 16 * k] = (u64)__double_as_longlong(xd[k]);
         } else {
@@ -1492,7 +1580,7 @@ void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in,
 // back to back, so each key segment comes from DRAM once per launch and from
 // L2 for the other ciphertexts.  Limbs below 2^40 use Karatsuba split-29
 // products, the others 128-bit products.
-__global__ void __launch_bounds__(256) k_keymult(u64 *__restrict__ acc, const u64 *__restrict__ D,
+__global__ void __launch_bounds__(256, 4) k_keymult(u64 *__restrict__ acc, const u64 *__restrict__ D,
                                                  const u64 *__restrict__ key, u64 g, int nq, int K, int L, int beta,
                                                  int keyP, const u64 *__restrict__ addb, int accumulate, int logN,
                                                  size_t d_stride, size_t acc_stride, size_t add_stride) {
