@@ -80,6 +80,30 @@ __device__ __forceinline__ u64 reduce128(const u128 &x, const PrimeConst &pc) {
 __device__ __forceinline__ u64 mul_mod(u64 a, u64 b, const PrimeConst &pc) {
     return reduce128(__umul64hi(a, b), a * b, pc);
 }
+// ---- exact modular arithmetic on the FP64 pipe (moduli below 2^40) -----------
+// Integers below 2^53 are exact doubles.  u64_to_d converts v < 2^52 by
+// placing it in the mantissa of 2^52.  mulmod_d(y, {w, fl(w/q)}, q) returns
+// y w - Q q with Q = round(y fl(w/q)) (magic-number rounding), computed
+// exactly: ph + pl = Q q (TwoProduct: ph = fl(Q q), pl = fma(Q, q, -ph)) and
+// fma(y, w, -ph) is the exact integer y w - ph, below 2^41 in magnitude; the
+// result is centred, |t| <= 0.502 q, for |y| < 2^44 and w < q < 2^40.
+// center_d(v) = v - round(v / q) q, |result| <= 0.5 q (+ rounding slack).
+__device__ __forceinline__ double u64_to_d(u64 v) {
+    return __dsub_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), 4503599627370496.0);
+}
+__device__ __forceinline__ double mulmod_d(double y, const double2 tw, double q) {
+    const double magic = 6755399441055744.0;  // 1.5 * 2^52
+    const double Qd = __dsub_rn(__fma_rn(y, tw.y, magic), magic);
+    const double ph = __dmul_rn(Qd, q);
+    const double pl = __fma_rn(Qd, q, -ph);
+    return __dsub_rn(__fma_rn(y, tw.x, -ph), pl);
+}
+__device__ __forceinline__ double center_d(double v, double q, double qinv) {
+    const double magic = 6755399441055744.0;
+    const double Qd = __dsub_rn(__fma_rn(v, qinv, magic), magic);
+    return __fma_rn(-Qd, q, v);  // exact
+}
+
 // Karatsuba split-29 sums of products, both factors below 2^40: a = ah 2^29
 // + al (al < 2^29, ah < 2^11), same for b.  A sum of up to 33 products is
 // kept as S0 = sum al*bl (< 2^58 per term), M = sum (al+ah)(bl+bh) (< 2^58.01

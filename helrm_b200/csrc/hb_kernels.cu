@@ -450,9 +450,6 @@ __device__ __forceinline__ void inv_a(u64 (&x)[16], const u64 *W, const u64 *Wp,
 // x' = x + t, y' = x - t: magnitudes grow by 0.502 q per stage, below 9.1 q
 // after 16 stages.  Eight FP64 instructions, no integer multiply: the FP64
 // pipe is as fast as the integer-multiply pipe and otherwise idle.
-__device__ __forceinline__ double u64_to_d(u64 v) {
-    return __dsub_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), 4503599627370496.0);
-}
 __device__ __forceinline__ void ct_bfly_d(double &x, double &y, const double2 tw, double q) {
     const double magic = 6755399441055744.0;  // 1.5 * 2^52
     const double Qd = __dsub_rn(__fma_rn(y, tw.y, magic), magic);
@@ -555,18 +552,6 @@ __device__ __forceinline__ u64 d_mod_to_u64(double v, double q, double qinv) {
 // below B a 4-stage group ends below 16 B, so every group ends by re-centring
 // its 16 values to |v| <= 0.5 q; the first group starts from [0, q) and stays
 // below 16 q < 2^44, the bound of the exact product.
-__device__ __forceinline__ double mulmod_d(double y, const double2 tw, double q) {
-    const double magic = 6755399441055744.0;  // 1.5 * 2^52
-    const double Qd = __dsub_rn(__fma_rn(y, tw.y, magic), magic);
-    const double ph = __dmul_rn(Qd, q);
-    const double pl = __fma_rn(Qd, q, -ph);
-    return __dsub_rn(__fma_rn(y, tw.x, -ph), pl);
-}
-__device__ __forceinline__ double center_d(double v, double q, double qinv) {
-    const double magic = 6755399441055744.0;
-    const double Qd = __dsub_rn(__fma_rn(v, qinv, magic), magic);
-    return __fma_rn(-Qd, q, v);  // exact
-}
 __device__ __forceinline__ void gs_bfly_d(double &x, double &y, const double2 tw, double q) {
     const double sm = __dadd_rn(x, y);
     const double df = __dsub_rn(x, y);
