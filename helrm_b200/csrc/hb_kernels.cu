@@ -1565,10 +1565,18 @@ void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in,
 // back to back, so each key segment comes from DRAM once per launch and from
 // L2 for the other ciphertexts.  Limbs below 2^40 use Karatsuba split-29
 // products, the others 128-bit products.
-__global__ void __launch_bounds__(256, 4) k_keymult(u64 *__restrict__ acc, const u64 *__restrict__ D,
-                                                 const u64 *__restrict__ key, u64 g, int nq, int K, int L, int beta,
+#ifndef HB_KEYMULT_BLOCKS
+#define HB_KEYMULT_BLOCKS 6  // resident blocks per SM (occupancy hides the gathers' latency)
+#endif
+// BETA > 0: the digit count as a compile-time constant (registers for
+// exactly BETA digits); BETA = 0: read at run time (up to HB_MAX_BETA)
+template <int BETA>
+__global__ void __launch_bounds__(256, HB_KEYMULT_BLOCKS) k_keymult(u64 *__restrict__ acc, const u64 *__restrict__ D,
+                                                 const u64 *__restrict__ key, u64 g, int nq, int K, int L, int beta_rt,
                                                  int keyP, const u64 *__restrict__ addb, int accumulate, int logN,
                                                  size_t d_stride, size_t acc_stride, size_t add_stride) {
+    constexpr int MB = BETA ? BETA : HB_MAX_BETA;
+    const int beta = BETA ? BETA : beta_rt;
     const int N = 1 << logN;
     const int ne = nq + K;
     const size_t n_all = (size_t)ne << logN;
@@ -1583,9 +1591,9 @@ __global__ void __launch_bounds__(256, 4) k_keymult(u64 *__restrict__ acc, const
     const int p = e < nq ? e : L + (e - nq);
     const PrimeConst &pc = c_pc[p];
     // issue every digit gather and key load before the products
-    u64 dv[HB_MAX_BETA], kbv[HB_MAX_BETA], kav[HB_MAX_BETA];
+    u64 dv[MB], kbv[MB], kav[MB];
 #pragma unroll
-    for (int j = 0; j < HB_MAX_BETA; j++)
+    for (int j = 0; j < MB; j++)
         if (j < beta) {
             dv[j] = Db[((size_t)j * ne + e) * N + src];
             kbv[j] = key[(((size_t)j * 2 + 0) * keyP + p) * N + t];
@@ -1595,7 +1603,7 @@ __global__ void __launch_bounds__(256, 4) k_keymult(u64 *__restrict__ acc, const
     if (pc.q < (1ull << 40)) {
         Kara29 sb = {0, 0, 0}, sa = {0, 0, 0};
 #pragma unroll
-        for (int j = 0; j < HB_MAX_BETA; j++)
+        for (int j = 0; j < MB; j++)
             if (j < beta) {
                 const u64 d = k29_pack(dv[j]);
                 const unsigned ds = k29_sum(d);
@@ -1607,7 +1615,7 @@ __global__ void __launch_bounds__(256, 4) k_keymult(u64 *__restrict__ acc, const
     } else {
         u128 sb = {0, 0}, sa = {0, 0};
 #pragma unroll
-        for (int j = 0; j < HB_MAX_BETA; j++)
+        for (int j = 0; j < MB; j++)
             if (j < beta) {
                 mac128(sb, dv[j], kbv[j]);
                 mac128(sa, dv[j], kav[j]);
@@ -1635,9 +1643,16 @@ void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, 
     ProfScope ps(KC_KEYMULT,
                  8.0 * (nbatch * nd * (beta + 2.0 + (addb ? 1.0 : 0.0) + (accumulate ? 2.0 : 0.0)) + 2.0 * beta * nd),
                  2.0 * beta * nbatch * nd, s, 1);
-    k_keymult<<<dim3(nbatch, (unsigned)chunks), 256, 0, s>>>(acc, D, key, galois, nq, K, L, beta, keyP, addb,
-                                                             accumulate ? 1 : 0, logN, d_stride, acc_stride,
-                                                             add_stride);
+    const dim3 grid(nbatch, (unsigned)chunks);
+#define HB_KM_ARGS acc, D, key, galois, nq, K, L, beta, keyP, addb, accumulate ? 1 : 0, logN, d_stride, acc_stride, add_stride
+    switch (beta) {
+        case 1: k_keymult<1><<<grid, 256, 0, s>>>(HB_KM_ARGS); break;
+        case 2: k_keymult<2><<<grid, 256, 0, s>>>(HB_KM_ARGS); break;
+        case 3: k_keymult<3><<<grid, 256, 0, s>>>(HB_KM_ARGS); break;
+        case 4: k_keymult<4><<<grid, 256, 0, s>>>(HB_KM_ARGS); break;
+        default: k_keymult<0><<<grid, 256, 0, s>>>(HB_KM_ARGS); break;
+    }
+#undef HB_KM_ARGS
     check_launch("keymult");
 }
 
