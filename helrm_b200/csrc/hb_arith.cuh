@@ -30,6 +30,8 @@ struct PrimeConst {
     u64 c58, c58p;  // 2^58 mod q (Karatsuba split-29 recombination)
     double qinv;    // fl(1/q), quotient estimates on the FP64 pipe
     double c58d;    // 2^58 mod q as a double (exact for q < 2^53)
+    u64 c90;        // 2^90 mod q
+    double c60d, c90d;  // 2^60 and 2^90 mod q as doubles (rounded above 2^53)
 };
 
 #define HB_SPLIT_MASK 0x3FFFFFFFull
@@ -182,15 +184,24 @@ __device__ __forceinline__ void splitw_normalize(SplitW &acc) {
     acc.s1 &= HB_SPLIT_MASK;
 }
 // (S0 + S1 2^30 + S2 2^60) mod q for S0 < 2^64, S1 < 2^64 - 2^34, S2 < 2^63
-// and any q < 2^62: carries of S0 into S1 and of S1 into S2 give lo + hi 2^60
-// with lo < 2^60, hi 2^60 is folded with 2^60 mod q (lazy Shoup, < 2q) and
-// the sum reduced once with floor(2^64/q).
+// and 2^26 <= q < 2^62.  Carries give lo + hi 2^60 with lo = a0 + a1 2^30
+// (a0, a1 < 2^30); hi = hl + hh 2^30, so the value is congruent to
+// W = lo + hl (2^60 mod q) + hh (2^90 mod q) < 2^60 + 2^31 q.  W is formed
+// modulo 2^64 on the integer pipe and, approximately (error below
+// 2^8 + q 2^-22), as a double; Q = round(W / q) from fl(1/q) is within
+// 0.5 + 2^-16 of W/q, so W - Q q (modulo 2^64) is centred below 0.51 q and one
+// conditional addition of q finishes.
 __device__ __forceinline__ u64 splitw_reduce(const SplitW &s, const PrimeConst &pc) {
     const u64 s1 = s.s1 + (s.s0 >> 30);
-    const u64 lo = (s.s0 & HB_SPLIT_MASK) | ((s1 & HB_SPLIT_MASK) << 30);
+    const unsigned a0 = (unsigned)(s.s0 & HB_SPLIT_MASK), a1 = (unsigned)(s1 & HB_SPLIT_MASK);
     const u64 hi = s.s2 + (s1 >> 30);
-    const u64 v = lo + mul_shoup_lazy(hi, pc.c60, pc.c60p, pc.q);
-    return mul_shoup(v, 1ull, pc.onep, pc.q);
+    const unsigned hl = (unsigned)(hi & HB_SPLIT_MASK), hh = (unsigned)(hi >> 30);
+    const u64 W = (u64)a0 + ((u64)a1 << 30) + (u64)hl * pc.c60 + (u64)hh * pc.c90;
+    const double lod = __fma_rn(u32_to_double(a1), 1073741824.0, u32_to_double(a0));
+    const double wd = __fma_rn(u32_to_double(hh), pc.c90d, __fma_rn(u32_to_double(hl), pc.c60d, lod));
+    const u64 Q = (u64)__double_as_longlong(__fma_rn(wd, pc.qinv, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
+    const u64 r = W - Q * pc.q;
+    return (long long)r < 0 ? r + pc.q : r;
 }
 
 // bit reversal of the low `bits` bits

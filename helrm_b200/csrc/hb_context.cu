@@ -259,6 +259,9 @@ public:
             c.c58p = h_shoup(c.c58, q);
             c.qinv = 1.0 / (double)q;
             c.c58d = (double)c.c58;
+            c.c90 = h_mulm((1ull << 60) % q, (1ull << 30) % q, q);
+            c.c60d = (double)c.c60;
+            c.c90d = (double)c.c90;
             pcs[p] = c;
         }
         upload_prime_consts(pcs.data(), P);
