@@ -1288,46 +1288,72 @@ __global__ void __launch_bounds__(256)
         sk[NA * ne + i] = tab.qjneg_k[(size_t)j * ne + i];
     }
     __syncthreads();
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= N) return;
+    // two coefficients per thread, 256 apart: every table value, prime
+    // constant and loop step serves two outputs; stores stay coalesced
+    const int n0 = blockIdx.x * (2 * blockDim.x) + threadIdx.x;
+    if (n0 >= N) return;  // N is a multiple of 512, so n0 + 256 < N as well
     const u64 *Xb = X + b * in_stride;
     u64 *Db = D + b * out_stride + (size_t)j * ne * N;
-    u64 y[NA], yk[NA];
-    unsigned ys[NA];
-    unsigned nneg = 0;
+    u64 y[2][NA], yk[2][NA];
+    unsigned ys[2][NA];
+    unsigned nneg[2] = {0, 0};
 #pragma unroll
     for (int m = 0; m < NA; m++) {
         const int pm = lo + m;
         const u64 qm = c_pc[pm].q;
-        const u64 v = mul_shoup(Xb[(size_t)pm * N + n], tab.qhinv[j * alpha + m], tab.qhinvp[j * alpha + m], qm);
-        nneg += v > (qm >> 1);
-        y[m] = split_pack(v);
-        yk[m] = k29_pack(v);
-        ys[m] = k29_sum(yk[m]);
+        const u64 w = tab.qhinv[j * alpha + m], wp = tab.qhinvp[j * alpha + m];
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const u64 v = mul_shoup(Xb[(size_t)pm * N + n0 + 256 * c], w, wp, qm);
+            nneg[c] += v > (qm >> 1);
+            y[c][m] = split_pack(v);
+            yk[c][m] = k29_pack(v);
+            ys[c][m] = k29_sum(yk[c][m]);
+        }
     }
     // q-row targets (below 2^40): Karatsuba split-29 products, one reduction
     for (int e = 0; e < nq; e++) {
+        u64 *de = Db + (size_t)e * N + n0;
         if (e >= lo && e < lo + NA) {
-            Db[(size_t)e * N + n] = c1ntt[b * c1_stride + (size_t)e * N + n];
+            const u64 *ce = c1ntt + b * c1_stride + (size_t)e * N + n0;
+            de[0] = ce[0];
+            de[256] = ce[256];
             continue;
         }
-        Kara29 acc = {0, 0, 0};
+        Kara29 acc0 = {0, 0, 0}, acc1 = {0, 0, 0};
 #pragma unroll
-        for (int m = 0; m < NA; m++) k29_mac(acc, sk[m * ne + e], yk[m], ys[m]);
-        k29_mac(acc, sk[NA * ne + e], (u64)nneg, nneg);
-        Db[(size_t)e * N + n] = k29_reduce(acc, c_pc[e]);
+        for (int m = 0; m < NA; m++) {
+            const u64 tv = sk[m * ne + e];
+            k29_mac(acc0, tv, yk[0][m], ys[0][m]);
+            k29_mac(acc1, tv, yk[1][m], ys[1][m]);
+        }
+        const u64 tn = sk[NA * ne + e];
+        k29_mac(acc0, tn, (u64)nneg[0], nneg[0]);
+        k29_mac(acc1, tn, (u64)nneg[1], nneg[1]);
+        const PrimeConst &pc = c_pc[e];
+        de[0] = k29_reduce(acc0, pc);
+        de[256] = k29_reduce(acc1, pc);
     }
     // special-prime targets: split-30 products (table values below 2^61)
     for (int e = nq; e < ne; e++) {
-        const int p = L + (e - nq);
-        SplitW acc = {0, 0, 0};
+        const PrimeConst &pc = c_pc[L + (e - nq)];
+        SplitW acc0 = {0, 0, 0}, acc1 = {0, 0, 0};
 #pragma unroll
         for (int m = 0; m < NA; m++) {
-            splitw_mac(acc, y[m], st[m * ne + e]);
-            if ((m & 3) == 3 && m + 1 < NA) splitw_normalize(acc);
+            const u64 tv = st[m * ne + e];
+            splitw_mac(acc0, y[0][m], tv);
+            splitw_mac(acc1, y[1][m], tv);
+            if ((m & 3) == 3 && m + 1 < NA) {
+                splitw_normalize(acc0);
+                splitw_normalize(acc1);
+            }
         }
-        splitw_mac_small(acc, nneg, st[NA * ne + e]);
-        Db[(size_t)e * N + n] = splitw_reduce(acc, c_pc[p]);
+        const u64 tn = st[NA * ne + e];
+        splitw_mac_small(acc0, nneg[0], tn);
+        splitw_mac_small(acc1, nneg[1], tn);
+        u64 *de = Db + (size_t)e * N + n0;
+        de[0] = splitw_reduce(acc0, pc);
+        de[256] = splitw_reduce(acc1, pc);
     }
 }
 
@@ -1335,7 +1361,7 @@ template <int NA>
 static void modup_split_launch(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int j0,
                                int ndig, const ModUpTab &tab, int logN, int nbatch, size_t in_stride,
                                size_t out_stride, size_t c1_stride, cudaStream_t s) {
-    dim3 grid(((1 << logN) + 255) / 256, ndig, nbatch);
+    dim3 grid(((1 << logN) + 511) / 512, ndig, nbatch);  // two coefficients per thread
     k_modup_bconv_split<NA><<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, j0, tab, logN, in_stride, out_stride,
                                                   c1_stride);
 }
@@ -1364,7 +1390,7 @@ void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, i
     if (ne > HB_MAX_PRIMES) throw std::invalid_argument("modup_bconv: too many primes");
     ProfScope ps(KC_MODUP_BCONV, 8.0 * nbatch * (double)N * (nq + (double)beta * ne),
                  (double)nbatch * N * ((double)nq + (double)alpha * ((double)beta * ne - nq)), s, 1);
-    if (tab.split && alpha <= 8) {
+    if (tab.split && alpha <= 8 && N >= 512) {
         const int full = nq / alpha, rag = nq - full * alpha;
         if (full > 0)
             modup_split_dispatch(alpha, D, X, c1ntt, nq, K, L, alpha, 0, full, tab, logN, nbatch, in_stride,
@@ -1590,14 +1616,19 @@ __global__ void __launch_bounds__(256, HB_KEYMULT_BLOCKS) k_keymult(u64 *__restr
     const unsigned src = g == 1 ? t : aut_index(t, g, logN);
     const int p = e < nq ? e : L + (e - nq);
     const PrimeConst &pc = c_pc[p];
-    // issue every digit gather and key load before the products
+    // issue every digit gather and key load before the products; base
+    // pointers and strides once, one add per digit
+    const u64 *dp = Db + ((size_t)e << logN) + src;
+    const size_t dstep = n_all;
+    const u64 *kp = key + ((size_t)p << logN) + t;
+    const size_t kstep = (size_t)keyP << logN;
     u64 dv[MB], kbv[MB], kav[MB];
 #pragma unroll
     for (int j = 0; j < MB; j++)
         if (j < beta) {
-            dv[j] = Db[((size_t)j * ne + e) * N + src];
-            kbv[j] = key[(((size_t)j * 2 + 0) * keyP + p) * N + t];
-            kav[j] = key[(((size_t)j * 2 + 1) * keyP + p) * N + t];
+            dv[j] = dp[j * dstep];
+            kbv[j] = kp[(2 * j) * kstep];
+            kav[j] = kp[(2 * j + 1) * kstep];
         }
     u64 vb, va;
     if (pc.q < (1ull << 40)) {
