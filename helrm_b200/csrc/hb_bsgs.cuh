@@ -47,6 +47,8 @@ __host__ __device__ inline size_t bsgs_smem_words(int beta) {
 
 // NBF = HB_BCH: a full chunk, the baby count is a compile-time constant and
 // the unrolled loops carry no guards; NBF = 0: the count is read at run time.
+// BETA > 0 fixes the digit count at compile time (row strides and the
+// segment division fold to constants); BETA = 0 reads beta_rt.
 //
 // The automorphism X -> X^g maps every aligned tile of 16 coefficients (in
 // the bit-reversed NTT order) onto another aligned tile of 16, permuted:
@@ -56,10 +58,10 @@ __host__ __device__ inline size_t bsgs_smem_words(int beta) {
 // gathers for a tile are therefore one contiguous 128-byte segment per
 // digit row, fetched with asynchronous copies one batch item ahead of the
 // arithmetic (double buffer); the in-tile permutation is a table built once.
-template <int NBF>
+template <int NBF, int BETA>
 __global__ void __launch_bounds__(kThreads, 2)
     k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
-               int K, int L, int beta, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch,
+               int K, int L, int beta_rt, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch,
                size_t ct_stride, size_t d_stride, size_t inner_stride) {
     extern __shared__ u64 sm[];
     const int N = 1 << logN;
@@ -71,6 +73,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool fast = pc.q < (1ull << 40);
     const int tid = threadIdx.x;
     const int nb = NBF ? NBF : ch.nbabies;
+    const int beta = BETA ? BETA : beta_rt;
     const int R1 = beta + 1;  // gathered rows per baby: beta digits, then c0
 
     // shared memory: descriptors | key tiles [nb][beta][2][BT] | R [nb][BT][2]
