@@ -49,6 +49,11 @@ __host__ __device__ inline size_t bsgs_smem_words(int beta) {
 // the unrolled loops carry no guards; NBF = 0: the count is read at run time.
 // BETA > 0 fixes the digit count at compile time (row strides and the
 // segment division fold to constants); BETA = 0 reads beta_rt.
+// ROWS selects the limb rows of the launch: 0 every row (q rows, then the
+// special rows; the product form chosen per row at run time), 1 the q rows
+// only, every one below 2^40 (split-29 products), 2 the special rows only,
+// every one at or above 2^40 (128-bit products).  Row e of the extended
+// basis is blockIdx.y + e0.
 //
 // The automorphism X -> X^g maps every aligned tile of 16 coefficients (in
 // the bit-reversed NTT order) onto another aligned tile of 16, permuted:
@@ -58,19 +63,20 @@ __host__ __device__ inline size_t bsgs_smem_words(int beta) {
 // gathers for a tile are therefore one contiguous 128-byte segment per
 // digit row, fetched with asynchronous copies one batch item ahead of the
 // arithmetic (double buffer); the in-tile permutation is a table built once.
-template <int NBF, int BETA>
+template <int NBF, int BETA, int ROWS>
 __global__ void __launch_bounds__(kThreads, 2)
     k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
-               int K, int L, int beta_rt, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch,
+               int K, int L, int beta_rt, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch, int e0,
                size_t ct_stride, size_t d_stride, size_t inner_stride) {
     extern __shared__ u64 sm[];
     const int N = 1 << logN;
-    const int e = blockIdx.y;
+    const int e = blockIdx.y + e0;
+    const bool qrow = ROWS == 1 ? true : ROWS == 2 ? false : e < nq;
     const int n0 = blockIdx.x * HB_BT;
     const int ne = nq + K;
-    const int p = e < nq ? e : L + (e - nq);
+    const int p = qrow ? e : L + (e - nq);
     const PrimeConst pc = c_pc[p];
-    const bool fast = pc.q < (1ull << 40);
+    const bool fast = ROWS == 1 ? true : ROWS == 2 ? false : pc.q < (1ull << 40);
     const int tid = threadIdx.x;
     const int nb = NBF ? NBF : ch.nbabies;
     const int beta = BETA ? BETA : beta_rt;
@@ -134,12 +140,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int bb = (int)((seg * r1mul) >> 16), r = (int)seg - bb * R1, k = i & 7;
             const u64 *src;
             if (sdesc[bb].key == nullptr) {
-                if (e >= nq || r >= 2) continue;
+                if (!qrow || r >= 2) continue;
                 src = c0b + ((size_t)r * nq << logN) + erow + n0;
             } else if (r < beta) {
                 src = Db + (size_t)r * dstride + erow + sblk[bb];
             } else {
-                if (e >= nq) continue;
+                if (!qrow) continue;
                 src = c0b + erow + sblk[bb];
             }
             cp_async16(Gb + ((size_t)bb * R1 + r) * HB_BT + 2 * k, src + 2 * k);
@@ -151,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // plaintexts of (giant slot gi, baby bb) at this thread's coefficient
     const int gi = tid / HB_BT, nl = tid % HB_BT;
     const bool gactive = gi < ch.gcount;
-    const size_t pt_off = ((size_t)(e < nq ? e : pt_nq + (e - nq)) << logN) + n0 + nl;
+    const size_t pt_off = ((size_t)(qrow ? e : pt_nq + (e - nq)) << logN) + n0 + nl;
     u64 ptv[HB_BCH];
 #pragma unroll
     for (int bb = 0; bb < HB_BCH; bb++) {
@@ -163,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         ptv[bb] = fast ? k29_pack(v) : v;
     }
     u64 pq_packed = 0, pq = 0;
-    if (e < nq) {
+    if (qrow) {
         pq = pmod_q[e];
         pq_packed = k29_pack(pq);
     }
@@ -186,8 +192,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             const u64 *g = Gb + (size_t)bb * R1 * HB_BT;
             u64 rb, ra;
             if (sdesc[bb].key == nullptr) {
-                rb = e < nq ? mul_mod(pq, g[n], pc) : 0;
-                ra = e < nq ? mul_mod(pq, g[HB_BT + n], pc) : 0;
+                rb = qrow ? mul_mod(pq, g[n], pc) : 0;
+                ra = qrow ? mul_mod(pq, g[HB_BT + n], pc) : 0;
             } else {
                 const int so = soff[it];
                 const u64 *kt = skey + (size_t)bb * beta * 2 * HB_BT + n;
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                             k29_mac(sb, kt[(j * 2 + 0) * HB_BT], d, ds);
                             k29_mac(sa, kt[(j * 2 + 1) * HB_BT], d, ds);
                         }
-                    if (e < nq) {
+                    if (qrow) {
                         const u64 cv = k29_pack(g[beta * HB_BT + so]);
                         k29_mac(sb, pq_packed, cv, k29_sum(cv));
                     }
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                             mac128(sb, d, kt[(j * 2 + 0) * HB_BT]);
                             mac128(sa, d, kt[(j * 2 + 1) * HB_BT]);
                         }
-                    if (e < nq) mac128(sb, pq, g[beta * HB_BT + so]);
+                    if (qrow) mac128(sb, pq, g[beta * HB_BT + so]);
                     rb = reduce128(sb, pc);
                     ra = reduce128(sa, pc);
                 }
@@ -234,15 +240,23 @@ __global__ void __launch_bounds__(kThreads, 2)
             const ulonglong2 *R2 = reinterpret_cast<const ulonglong2 *>(sR) + nl;
             u64 vb, va;
             if (fast) {
-                Kara29 ab = {0, 0, 0}, aa = {0, 0, 0};
+                // the q-row kernel alternates two sets of sums over the
+                // babies (half-length dependency chains; the merged sums
+                // are the same sums of at most 32 products)
+                constexpr bool kTwo = ROWS == 1;
+                Kara29 ab = {0, 0, 0}, aa = {0, 0, 0}, ab1 = {0, 0, 0}, aa1 = {0, 0, 0};
 #pragma unroll
                 for (int bb = 0; bb < HB_BCH; bb++) {
                     if (NBF || bb < nb) {
                         const ulonglong2 r = R2[bb * HB_BT];
                         const unsigned ps = k29_sum(ptv[bb]);
-                        k29_mac(ab, r.x, ptv[bb], ps);
-                        k29_mac(aa, r.y, ptv[bb], ps);
+                        k29_mac((kTwo && (bb & 1)) ? ab1 : ab, r.x, ptv[bb], ps);
+                        k29_mac((kTwo && (bb & 1)) ? aa1 : aa, r.y, ptv[bb], ps);
                     }
+                }
+                if (kTwo) {
+                    ab.s0 += ab1.s0, ab.m += ab1.m, ab.s2 += ab1.s2;
+                    aa.s0 += aa1.s0, aa.m += aa1.m, aa.s2 += aa1.s2;
                 }
                 vb = k29_reduce(ab, pc);
                 va = k29_reduce(aa, pc);

@@ -27,9 +27,25 @@ static void check_launch(const char *what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// host copy of the moduli in the constant table (launchers pick kernel
+// specialisations by prime size)
+static u64 g_host_q[HB_MAX_PRIMES];
+static int g_host_nq = 0;
+
 void upload_prime_consts(const PrimeConst *pc, int n) {
     cudaError_t e = cudaMemcpyToSymbol(c_pc, pc, sizeof(PrimeConst) * n);
     if (e != cudaSuccess) throw std::runtime_error(std::string("prime constants: ") + cudaGetErrorString(e));
+    for (int i = 0; i < n; i++) g_host_q[i] = pc[i].q;
+    g_host_nq = n;
+}
+
+// every prime p0 .. p0 + n - 1 of the table below 2^40 (below = true) or
+// every one at or above it (below = false)
+static bool primes_sized(int p0, int n, bool below) {
+    if (p0 < 0 || p0 + n > g_host_nq) return false;
+    for (int i = p0; i < p0 + n; i++)
+        if ((g_host_q[i] < (1ull << 40)) != below) return false;
+    return true;
 }
 
 // =====================================================================
@@ -479,8 +495,22 @@ __device__ __forceinline__ void ld_pairs(double2 (&tw)[8], const double2 *src) {
                 : "l"(src + 2 * v));
     }
 }
+// NP pairs, two per 256-bit load, the loads STRIDE pairs apart: the block
+// pass's last two forward stages (first two inverse ones) store the pairs
+// of a stage segment thread-interleaved, so that every warp load reads
+// contiguous lines
+template <int NP, int STRIDE>
+__device__ __forceinline__ void ld_pairs_s(double2 (&tw)[8], const double2 *src) {
+#pragma unroll
+    for (int v = 0; v < NP / 2; v++)
+        asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
+            : "=d"(tw[2 * v].x), "=d"(tw[2 * v].y), "=d"(tw[2 * v + 1].x), "=d"(tw[2 * v + 1].y)
+            : "l"(src + STRIDE * v));
+}
 // the two forward halves with twiddles from global memory (block pass):
-// stage s needs 2^s consecutive pairs per thread, loaded at the stage start
+// stage s needs 2^s pairs per thread, loaded at the stage start.  In the
+// segment of stage s >= 2 (16 threads x 2^s pairs) thread c's pair i sits
+// at 32 (i / 2) + 2 c + (i % 2), the layout written by the table setup.
 __device__ __forceinline__ void fwd_a_dg(double (&x)[16], const double2 *T, int base, double q) {
 #pragma unroll
     for (int s = 0; s < 4; s++) {
@@ -503,11 +533,11 @@ __device__ __forceinline__ void fwd_b_dg(double (&x)[16], const double2 *T, int 
     for (int s = 0; s < 4; s++) {
         const int d = 8 >> s, g = 16 << s;
         double2 tw[8];
-        const double2 *src = T + g * base + (c << s);
-        if (s == 0) ld_pairs<1>(tw, src);
-        if (s == 1) ld_pairs<2>(tw, src);
-        if (s == 2) ld_pairs<4>(tw, src);
-        if (s == 3) ld_pairs<8>(tw, src);
+        const double2 *seg = T + g * base;
+        if (s == 0) ld_pairs<1>(tw, seg + c);
+        if (s == 1) ld_pairs<2>(tw, seg + 2 * c);
+        if (s == 2) ld_pairs_s<4, 32>(tw, seg + 2 * c);
+        if (s == 3) ld_pairs_s<8, 32>(tw, seg + 2 * c);
 #pragma unroll
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
@@ -578,11 +608,11 @@ __device__ __forceinline__ void inv_b_dg(double (&x)[16], const double2 *T, int 
     for (int s = 3; s >= 0; s--) {
         const int d = 8 >> s, g = 16 << s;
         double2 tw[8];
-        const double2 *src = T + g * base + (c << s);
-        if (s == 0) ld_pairs<1>(tw, src);
-        if (s == 1) ld_pairs<2>(tw, src);
-        if (s == 2) ld_pairs<4>(tw, src);
-        if (s == 3) ld_pairs<8>(tw, src);
+        const double2 *seg = T + g * base;  // thread-interleaved for s >= 2
+        if (s == 0) ld_pairs<1>(tw, seg + c);
+        if (s == 1) ld_pairs<2>(tw, seg + 2 * c);
+        if (s == 2) ld_pairs_s<4, 32>(tw, seg + 2 * c);
+        if (s == 3) ld_pairs_s<8, 32>(tw, seg + 2 * c);
 #pragma unroll
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
@@ -1699,35 +1729,42 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
         throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
     static size_t attr = 0;
     if (smem > attr) {
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<0, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<0, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<0, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<0, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = smem;
     }
     const size_t n = (size_t)(nq + K) << logN;
     // per ciphertext: c0/c1 rows, the digits, the inner sums written; per
     // launch: every baby key and plaintext of the chunk once
     const double nd = (double)n, nqw = (double)nq * (1 << logN);
+    const bool split = beta == 4 && primes_sized(0, nq, true) && primes_sized(L, K, false);
     ProfScope ps(KC_BSGS_MAC,
                  8.0 * (nbatch * (2.0 * nqw + beta * nd + 2.0 * ch.gcount * nd * (ch.accumulate ? 2 : 1)) +
                         2.0 * beta * ch.nkeys * nd + ch.npts * nd),
-                 (double)nbatch * nd * (2.0 * beta * ch.nkeys + 2.0 * ch.npts), s, 1);
-    dim3 grid((1u << logN) / HB_BT, nq + K);
-    // specialised for full chunks and for four digits (the dnum-4 key of the
-    // benchmark parameter sets at the top level); anything else runs the
-    // generic form
-#define HB_BSGS_LAUNCH(NBF_, BETA_)                                                                        \
-    k_bsgs_mac<NBF_, BETA_><<<grid, HB_GCH * HB_BT, smem, s>>>(inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, \
-                                                               pmod_q, logN, nbatch, ct_stride, d_stride,  \
-                                                               inner_stride)
+                 (double)nbatch * nd * (2.0 * beta * ch.nkeys + 2.0 * ch.npts), s, split && K ? 2 : 1);
+    // specialised for full chunks, four digits (the dnum-4 key of the
+    // benchmark parameter sets at the top level) and q rows below 2^40 with
+    // special rows above it: one launch per kind of row, each with a single
+    // product form.  Anything else runs the generic form over every row.
+#define HB_BSGS_LAUNCH(NBF_, BETA_, ROWS_, E0_, NROWS_)                                                         \
+    k_bsgs_mac<NBF_, BETA_, ROWS_><<<dim3((1u << logN) / HB_BT, NROWS_), HB_GCH * HB_BT, smem, s>>>(           \
+        inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN, nbatch, E0_, ct_stride, d_stride, inner_stride)
     const bool full = ch.nbabies == HB_BCH;
-    if (beta == 4) {
-        if (full) HB_BSGS_LAUNCH(HB_BCH, 4);
-        else HB_BSGS_LAUNCH(0, 4);
+    if (split) {
+        if (full) {
+            HB_BSGS_LAUNCH(HB_BCH, 4, 1, 0, nq);
+            if (K) HB_BSGS_LAUNCH(HB_BCH, 4, 2, nq, K);
+        } else {
+            HB_BSGS_LAUNCH(0, 4, 1, 0, nq);
+            if (K) HB_BSGS_LAUNCH(0, 4, 2, nq, K);
+        }
     } else {
-        if (full) HB_BSGS_LAUNCH(HB_BCH, 0);
-        else HB_BSGS_LAUNCH(0, 0);
+        if (full) HB_BSGS_LAUNCH(HB_BCH, 0, 0, 0, nq + K);
+        else HB_BSGS_LAUNCH(0, 0, 0, 0, nq + K);
     }
 #undef HB_BSGS_LAUNCH
     check_launch("bsgs_mac");
