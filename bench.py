@@ -133,12 +133,20 @@ class ClockSampler:
             if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else None
 
     def start(self):
+        """Start sampling and wait for the first sample: nvidia-smi's start-up
+        (NVML initialisation) stalls the GPU's work submission for tens of
+        milliseconds and must not fall inside the timed region."""
+        self.first = ""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.sel, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return
+        import select
+        if select.select([self.proc.stdout], [], [], 10.0)[0]:
+            self.first = self.proc.stdout.readline()
 
     def stop(self) -> dict:
         if not self.proc:
@@ -146,10 +154,11 @@ class ClockSampler:
         time.sleep(0.25)
         self.proc.terminate()
         out, _ = self.proc.communicate(timeout=10)
+        # the first sample precedes the timed region: kept in the file only
         rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
         if self.path:
             with open(self.path, "w") as f:
-                f.write(out)
+                f.write(self.first + out)
         sm = [float(r[0]) for r in rows if len(r) >= 8 and r[0].replace(".", "").isdigit()]
         mx = [float(r[1]) for r in rows if len(r) >= 8 and r[1].replace(".", "").isdigit()]
         pw = [float(r[2]) for r in rows if len(r) >= 8 and r[2].replace(".", "").isdigit()]
