@@ -49,11 +49,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-threads", type=int, default=0, help="oracle threads (0 = all host cores)")
     ap.add_argument("--small", action="store_true",
-                    help="profiling case: same 512-diagonal PCMM on 6 q limbs + 2 special primes (dnum 3), "
-                         "so an ncu capture keeps a few GB on the device")
+                    help="profiling case: same 512-diagonal PCMM on 8 q limbs + 2 special primes (dnum 4, "
+                         "so four digits as in the headline), so an ncu capture keeps a few GB on the device")
     args = ap.parse_args()
     if args.small:
-        args.level = min(args.level, 5)
+        args.level = min(args.level, 7)
     return args
 
 
@@ -282,8 +282,8 @@ def cfg_dict(args, batch):
          "queries_per_ciphertext": 1, "parallelism": f"dp{args.gpus} (query batch)",
          "l2": "inputs larger than L2 (1.5 GiB ciphertexts, 7 GiB diagonals, 5.7 GiB keys per step)"}
     if getattr(args, "small", False):
-        d.update({"workload": "profiling case (NOT the headline): cfg2 PCMM on 6 q limbs + 2 special primes",
-                  "q_limbs": 6, "special_primes": 2, "dnum": 3})
+        d.update({"workload": "profiling case (NOT the headline): cfg2 PCMM on 8 q limbs + 2 special primes",
+                  "q_limbs": 8, "special_primes": 2, "dnum": 4})
     return d
 
 
@@ -298,7 +298,7 @@ def run_b200(args, dist):
     dev = dist.local
     torch.cuda.set_device(dev)
     if args.small:
-        cfg, dnum = CKKSConfig(logn=16, logq=[36] * 6, logp=[60] * 2, logscale=36, h=192), 3
+        cfg, dnum = CKKSConfig(logn=16, logq=[36] * 8, logp=[60] * 2, logscale=36, h=192), 4
     else:
         cfg, dnum = CFG2, CFG2_DNUM
     lib = B200Library(dnum=dnum, seed=1000 + dist.rank, device=dev)

@@ -42,7 +42,8 @@ __device__ __forceinline__ void cp_async_wait() {
 // gather buffers, rotation tables).
 __host__ __device__ inline size_t bsgs_smem_words(int beta) {
     return (size_t)HB_BCH * (sizeof(BabyDesc) / 8) + (size_t)HB_BCH * beta * 2 * HB_BT + (size_t)HB_BCH * 2 * HB_BT +
-           (size_t)2 * HB_BCH * (beta + 1) * HB_BT + (size_t)HB_BCH * HB_BT / 8 + HB_BCH / 2;
+           (size_t)2 * HB_BCH * (beta + 1) * HB_BT + (size_t)HB_BCH * HB_BT / 8 + HB_BCH / 2 +
+           (size_t)HB_BCH * (beta + 1) * (HB_BT / 2);  // gather descriptors (fixed-shape kernels)
 }
 
 // NBF = HB_BCH: a full chunk, the baby count is a compile-time constant and
@@ -91,6 +92,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     u64 *sG = sR + (size_t)HB_BCH * 2 * HB_BT;
     unsigned char *soff = reinterpret_cast<unsigned char *>(sG + (size_t)2 * HB_BCH * R1 * HB_BT);
     unsigned *sblk = reinterpret_cast<unsigned *>(soff + HB_BCH * HB_BT);
+    u64 *sgd = reinterpret_cast<u64 *>(sblk + HB_BCH);  // gather descriptors [NCH][kThreads]
     const size_t gbuf = (size_t)nb * R1 * HB_BT;
 
     for (int i = tid; i < nb * (int)(sizeof(BabyDesc) / 8); i += kThreads)
@@ -130,9 +132,55 @@ __global__ void __launch_bounds__(kThreads, 2)
     // segment s = bb * R1 + r; s / R1 by a reciprocal multiply, exact for
     // s < 2^16 / R1 (at most 32 * 9 segments here)
     const unsigned r1mul = (65536u + (unsigned)R1 - 1u) / (unsigned)R1;
+    // Fixed-shape kernels (full chunk, compile-time digit count): every
+    // thread issues exactly NCH 16-byte copies per batch item, whose source
+    // offsets (inside one item's digits or ciphertext) and destinations do
+    // not depend on the item.  They are packed once per block into
+    // sgd[j][tid]: source word offset (bits 0-31), destination byte offset in
+    // the gather buffer (32-47), source is the ciphertext (48), copy wanted (49).
+    constexpr bool kFixed = NBF != 0 && BETA != 0;
+    constexpr int NCH = kFixed ? NBF * (BETA + 1) * (HB_BT / 2) / kThreads : 0;
+    static_assert(!kFixed || NBF * (BETA + 1) * (HB_BT / 2) % kThreads == 0, "gather chunks per thread");
+    if (kFixed) {
+#pragma unroll
+        for (int j = 0; j < NCH; j++) {
+            const int i = tid + j * kThreads;
+            const unsigned seg = (unsigned)i >> 3;
+            const int bb = (int)((seg * r1mul) >> 16), r = (int)seg - bb * R1, k = i & 7;
+            u64 srcw, use_c = 1, want = 1;
+            if (sdesc[bb].key == nullptr) {
+                want = qrow && r < 2;
+                srcw = ((u64)r * nq << logN) + erow + n0 + 2 * k;
+            } else if (r < beta) {
+                use_c = 0;
+                srcw = (u64)r * dstride + erow + sblk[bb] + 2 * k;
+            } else {
+                want = qrow;
+                srcw = (u64)erow + sblk[bb] + 2 * k;
+            }
+            const u64 dstb = (((u64)bb * R1 + r) * HB_BT + 2 * k) * 8;
+            sgd[j * kThreads + tid] = srcw | (dstb << 32) | (use_c << 48) | (want << 49);
+        }
+        // each thread reads only its own descriptors: no barrier needed
+    }
+    const unsigned sG_sa = (unsigned)__cvta_generic_to_shared(sG);
     auto issue = [&](int b, int buf) {
         const u64 *c0b = ct + b * ct_stride;
         const u64 *Db = D + b * d_stride;
+        if (kFixed) {
+            const unsigned gb = sG_sa + (unsigned)(buf * gbuf * 8);
+#pragma unroll
+            for (int j = 0; j < NCH; j++) {
+                const u64 d = sgd[j * kThreads + tid];
+                const u64 *src = ((d >> 48) & 1 ? c0b : Db) + (unsigned)d;
+                if ((d >> 49) & 1) {
+                    const unsigned sa = gb + ((unsigned)(d >> 32) & 0xFFFFu);
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(src) : "memory");
+                }
+            }
+            cp_async_commit();
+            return;
+        }
         u64 *Gb = sG + buf * gbuf;
         const int nchunk = nb * R1 * (HB_BT / 2);
         for (int i = tid; i < nchunk; i += kThreads) {
