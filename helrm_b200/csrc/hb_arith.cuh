@@ -128,6 +128,13 @@ __device__ __forceinline__ void k29_mac(Kara29 &acc, u64 a_packed, u64 b_packed,
     asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.m) : "r"(al + ah), "r"(b_sum));
     acc.s2 += ah * bh;
 }
+// the same product from unpacked halves and both digit sums
+__device__ __forceinline__ void k29_mac_s(Kara29 &acc, unsigned al, unsigned ah, unsigned a_sum, unsigned bl,
+                                          unsigned bh, unsigned b_sum) {
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.s0) : "r"(al), "r"(bl));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc.m) : "r"(a_sum), "r"(b_sum));
+    acc.s2 += ah * bh;
+}
 // a 32-bit unsigned integer as an exact double: the bit pattern 0x43300000:x
 // is 2^52 + x
 __device__ __forceinline__ double u32_to_double(unsigned x) {

@@ -41,7 +41,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // Shared-memory words of one launch (descriptors, key tiles, R tile, two
 // gather buffers, rotation tables).
 __host__ __device__ inline size_t bsgs_smem_words(int beta) {
-    return (size_t)HB_BCH * (sizeof(BabyDesc) / 8) + (size_t)HB_BCH * beta * 2 * HB_BT + (size_t)HB_BCH * 2 * HB_BT +
+    return (size_t)HB_BCH * (sizeof(BabyDesc) / 8) + (size_t)HB_BCH * beta * 2 * HB_BT + (size_t)HB_BCH * 3 * HB_BT +
            (size_t)2 * HB_BCH * (beta + 1) * HB_BT + (size_t)HB_BCH * HB_BT / 8 + HB_BCH / 2 +
            (size_t)HB_BCH * (beta + 1) * (HB_BT / 2);  // gather descriptors (fixed-shape kernels)
 }
@@ -82,6 +82,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int nb = NBF ? NBF : ch.nbabies;
     const int beta = BETA ? BETA : beta_rt;
     const int R1 = beta + 1;  // gathered rows per baby: beta digits, then c0
+    // fixed-shape kernels (full chunk, compile-time digit count): precomputed
+    // gather descriptors, and the identity baby handled as a rotated one
+    // whose key tile holds P mod q at (row 0, b) and (row 1, a)
+    constexpr bool kFixed = NBF != 0 && BETA != 0;
+    const u64 pq_e = qrow ? pmod_q[e] : 0;
 
     // shared memory: descriptors | key tiles [nb][beta][2][BT] | R [nb][BT][2]
     // | gathers [2][nb][beta+1][BT] | in-tile offsets [nb][BT] (bytes) |
@@ -89,7 +94,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     BabyDesc *sdesc = reinterpret_cast<BabyDesc *>(sm);
     u64 *skey = sm + (size_t)HB_BCH * (sizeof(BabyDesc) / 8);
     u64 *sR = skey + (size_t)HB_BCH * beta * 2 * HB_BT;
-    u64 *sG = sR + (size_t)HB_BCH * 2 * HB_BT;
+    uint2 *sRs = reinterpret_cast<uint2 *>(sR + (size_t)HB_BCH * 2 * HB_BT);  // split-29 digit sums of R
+    u64 *sG = sR + (size_t)HB_BCH * 3 * HB_BT;
     unsigned char *soff = reinterpret_cast<unsigned char *>(sG + (size_t)2 * HB_BCH * R1 * HB_BT);
     unsigned *sblk = reinterpret_cast<unsigned *>(soff + HB_BCH * HB_BT);
     u64 *sgd = reinterpret_cast<u64 *>(sblk + HB_BCH);  // gather descriptors [NCH][kThreads]
@@ -114,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const u64 *key = sdesc[bb].key;
             u64 v = 0;
             if (key) v = key[((size_t)jp * keyP + p) * N + n0 + n];
+            else if (kFixed && (jp == 0 || jp == 3)) v = pq_e;
             skey[i] = fast ? k29_pack(v) : v;
         }
     }
@@ -132,13 +139,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // segment s = bb * R1 + r; s / R1 by a reciprocal multiply, exact for
     // s < 2^16 / R1 (at most 32 * 9 segments here)
     const unsigned r1mul = (65536u + (unsigned)R1 - 1u) / (unsigned)R1;
-    // Fixed-shape kernels (full chunk, compile-time digit count): every
-    // thread issues exactly NCH 16-byte copies per batch item, whose source
-    // offsets (inside one item's digits or ciphertext) and destinations do
-    // not depend on the item.  They are packed once per block into
-    // sgd[j][tid]: source word offset (bits 0-31), destination byte offset in
-    // the gather buffer (32-47), source is the ciphertext (48), copy wanted (49).
-    constexpr bool kFixed = NBF != 0 && BETA != 0;
+    // Fixed-shape kernels: every thread issues exactly NCH 16-byte copies
+    // per batch item, whose source offsets (inside one item's digits or
+    // ciphertext) and destinations do not depend on the item.  They are
+    // packed once per block into sgd[j][tid]: source word offset (bits
+    // 0-31), destination byte offset in the gather buffer (32-47), source is
+    // the ciphertext (48), copy wanted (49).  A copy not wanted zero-fills
+    // its 16 bytes (the identity baby's unused rows, c-rows on special rows).
     constexpr int NCH = kFixed ? NBF * (BETA + 1) * (HB_BT / 2) / kThreads : 0;
     static_assert(!kFixed || NBF * (BETA + 1) * (HB_BT / 2) % kThreads == 0, "gather chunks per thread");
     if (kFixed) {
@@ -150,13 +157,13 @@ __global__ void __launch_bounds__(kThreads, 2)
             u64 srcw, use_c = 1, want = 1;
             if (sdesc[bb].key == nullptr) {
                 want = qrow && r < 2;
-                srcw = ((u64)r * nq << logN) + erow + n0 + 2 * k;
+                srcw = want ? ((u64)r * nq << logN) + erow + n0 + 2 * k : 0;
             } else if (r < beta) {
                 use_c = 0;
                 srcw = (u64)r * dstride + erow + sblk[bb] + 2 * k;
             } else {
                 want = qrow;
-                srcw = (u64)erow + sblk[bb] + 2 * k;
+                srcw = want ? (u64)erow + sblk[bb] + 2 * k : 0;
             }
             const u64 dstb = (((u64)bb * R1 + r) * HB_BT + 2 * k) * 8;
             sgd[j * kThreads + tid] = srcw | (dstb << 32) | (use_c << 48) | (want << 49);
@@ -173,10 +180,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int j = 0; j < NCH; j++) {
                 const u64 d = sgd[j * kThreads + tid];
                 const u64 *src = ((d >> 48) & 1 ? c0b : Db) + (unsigned)d;
-                if ((d >> 49) & 1) {
-                    const unsigned sa = gb + ((unsigned)(d >> 32) & 0xFFFFu);
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(src) : "memory");
-                }
+                const unsigned sa = gb + ((unsigned)(d >> 32) & 0xFFFFu);
+                const unsigned nbytes = (unsigned)((d >> 45) & 16);  // bit 49 -> 16 or 0 bytes read
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(src), "r"(nbytes)
+                             : "memory");
             }
             cp_async_commit();
             return;
@@ -239,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int bb = it / HB_BT, n = it % HB_BT;
             const u64 *g = Gb + (size_t)bb * R1 * HB_BT;
             u64 rb, ra;
-            if (sdesc[bb].key == nullptr) {
+            if (!kFixed && sdesc[bb].key == nullptr) {
                 rb = qrow ? mul_mod(pq, g[n], pc) : 0;
                 ra = qrow ? mul_mod(pq, g[HB_BT + n], pc) : 0;
             } else {
@@ -275,9 +282,15 @@ __global__ void __launch_bounds__(kThreads, 2)
                     ra = reduce128(sa, pc);
                 }
             }
-            // R tile interleaved {b, a} per coefficient: one 16-byte read in phase B
-            reinterpret_cast<ulonglong2 *>(sR)[bb * HB_BT + n] =
-                fast ? make_ulonglong2(k29_pack(rb), k29_pack(ra)) : make_ulonglong2(rb, ra);
+            // R tile interleaved {b, a} per coefficient: one 16-byte read in
+            // phase B; on fast limbs also the digit sums lo + hi of both
+            if (fast) {
+                const u64 pb = k29_pack(rb), pa = k29_pack(ra);
+                reinterpret_cast<ulonglong2 *>(sR)[bb * HB_BT + n] = make_ulonglong2(pb, pa);
+                sRs[bb * HB_BT + n] = make_uint2(k29_sum(pb), k29_sum(pa));
+            } else {
+                reinterpret_cast<ulonglong2 *>(sR)[bb * HB_BT + n] = make_ulonglong2(rb, ra);
+            }
         }
         __syncthreads();
         // ---- phase B: inner[g] += pt(g, b) * R_b.  Karatsuba split-29 sums
@@ -286,6 +299,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // 2^122 need no intermediate reduction either.
         if (gactive) {
             const ulonglong2 *R2 = reinterpret_cast<const ulonglong2 *>(sR) + nl;
+            const uint4 *R4 = reinterpret_cast<const uint4 *>(sR) + nl;
+            const uint2 *RS = sRs + nl;
             u64 vb, va;
             if (fast) {
                 // the q-row kernel alternates two sets of sums over the
@@ -296,10 +311,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                 for (int bb = 0; bb < HB_BCH; bb++) {
                     if (NBF || bb < nb) {
-                        const ulonglong2 r = R2[bb * HB_BT];
-                        const unsigned ps = k29_sum(ptv[bb]);
-                        k29_mac((kTwo && (bb & 1)) ? ab1 : ab, r.x, ptv[bb], ps);
-                        k29_mac((kTwo && (bb & 1)) ? aa1 : aa, r.y, ptv[bb], ps);
+                        const uint4 r = R4[bb * HB_BT];
+                        const uint2 rs = RS[bb * HB_BT];
+                        const unsigned pl = (unsigned)ptv[bb], ph = (unsigned)(ptv[bb] >> 32), ps = pl + ph;
+                        k29_mac_s((kTwo && (bb & 1)) ? ab1 : ab, r.x, r.y, rs.x, pl, ph, ps);
+                        k29_mac_s((kTwo && (bb & 1)) ? aa1 : aa, r.z, r.w, rs.y, pl, ph, ps);
                     }
                 }
                 if (kTwo) {
