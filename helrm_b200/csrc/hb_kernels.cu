@@ -1692,6 +1692,91 @@ __global__ void __launch_bounds__(256, HB_KEYMULT_BLOCKS) k_keymult(u64 *__restr
     Ab[i] = vb;
     Ab[n_all + i] = va;
 }
+// The batch-looping form (four digits): one thread per coefficient of one
+// limb row, looping over the ciphertexts of the batch.  The key words of
+// the coefficient (split-29 halves and their sums on limbs below 2^40) and
+// the automorphism index stay in registers across the batch, so per
+// ciphertext a thread only gathers its digits and the addend and updates
+// the accumulator.
+#ifndef HB_KEYMULT_LOOP_BLOCKS
+#define HB_KEYMULT_LOOP_BLOCKS 4
+#endif
+template <int BETA>
+__global__ void __launch_bounds__(256, HB_KEYMULT_LOOP_BLOCKS)
+    k_keymult_loop(u64 *__restrict__ acc, const u64 *__restrict__ D, const u64 *__restrict__ key, u64 g, int nq,
+                   int K, int L, int keyP, const u64 *__restrict__ addb, int accumulate, int logN, int nbatch,
+                   size_t d_stride, size_t acc_stride, size_t add_stride) {
+    const int ne = nq + K;
+    const size_t n_all = (size_t)ne << logN;
+    const int e = blockIdx.y;
+    const unsigned t = blockIdx.x * 256u + threadIdx.x;
+    const unsigned src = g == 1 ? t : aut_index(t, g, logN);
+    const int p = e < nq ? e : L + (e - nq);
+    const PrimeConst pc = c_pc[p];
+    const u64 *kp = key + ((size_t)p << logN) + t;
+    const size_t kstep = (size_t)keyP << logN;
+    const size_t drow = ((size_t)e << logN) + src, irow = ((size_t)e << logN) + t;
+    if (pc.q < (1ull << 40)) {
+        unsigned kbl[BETA], kbh[BETA], kbs[BETA], kal[BETA], kah[BETA], kas[BETA];
+#pragma unroll
+        for (int j = 0; j < BETA; j++) {
+            const u64 kb = k29_pack(kp[(2 * j) * kstep]), ka = k29_pack(kp[(2 * j + 1) * kstep]);
+            kbl[j] = (unsigned)kb, kbh[j] = (unsigned)(kb >> 32), kbs[j] = kbl[j] + kbh[j];
+            kal[j] = (unsigned)ka, kah[j] = (unsigned)(ka >> 32), kas[j] = kal[j] + kah[j];
+        }
+#pragma unroll 2
+        for (int b = 0; b < nbatch; b++) {
+            const u64 *dp = D + b * d_stride + drow;
+            u64 dv[BETA];
+#pragma unroll
+            for (int j = 0; j < BETA; j++) dv[j] = dp[j * n_all];
+            Kara29 sb = {0, 0, 0}, sa = {0, 0, 0};
+#pragma unroll
+            for (int j = 0; j < BETA; j++) {
+                const u64 d = k29_pack(dv[j]);
+                const unsigned dl = (unsigned)d, dh = (unsigned)(d >> 32), ds = dl + dh;
+                k29_mac_s(sb, kbl[j], kbh[j], kbs[j], dl, dh, ds);
+                k29_mac_s(sa, kal[j], kah[j], kas[j], dl, dh, ds);
+            }
+            u64 vb = k29_reduce(sb, pc), va = k29_reduce(sa, pc);
+            if (addb) vb = add_mod(vb, addb[b * add_stride + drow], pc.q);
+            u64 *A = acc + b * acc_stride + irow;
+            if (accumulate) {
+                vb = add_mod(vb, A[0], pc.q);
+                va = add_mod(va, A[n_all], pc.q);
+            }
+            A[0] = vb;
+            A[n_all] = va;
+        }
+    } else {
+        u64 kb[BETA], ka[BETA];
+#pragma unroll
+        for (int j = 0; j < BETA; j++) {
+            kb[j] = kp[(2 * j) * kstep];
+            ka[j] = kp[(2 * j + 1) * kstep];
+        }
+        for (int b = 0; b < nbatch; b++) {
+            const u64 *dp = D + b * d_stride + drow;
+            u128 sb = {0, 0}, sa = {0, 0};
+#pragma unroll
+            for (int j = 0; j < BETA; j++) {
+                const u64 d = dp[j * n_all];
+                mac128(sb, d, kb[j]);
+                mac128(sa, d, ka[j]);
+            }
+            u64 vb = reduce128(sb, pc), va = reduce128(sa, pc);
+            if (addb) vb = add_mod(vb, addb[b * add_stride + drow], pc.q);
+            u64 *A = acc + b * acc_stride + irow;
+            if (accumulate) {
+                vb = add_mod(vb, A[0], pc.q);
+                va = add_mod(va, A[n_all], pc.q);
+            }
+            A[0] = vb;
+            A[n_all] = va;
+        }
+    }
+}
+
 void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,
              const u64 *addb, bool accumulate, int logN, int nbatch, size_t d_stride, size_t acc_stride,
              size_t add_stride, cudaStream_t s) {
@@ -1704,6 +1789,13 @@ void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, 
     ProfScope ps(KC_KEYMULT,
                  8.0 * (nbatch * nd * (beta + 2.0 + (addb ? 1.0 : 0.0) + (accumulate ? 2.0 : 0.0)) + 2.0 * beta * nd),
                  2.0 * beta * nbatch * nd, s, 1);
+    if (beta == 4 && logN >= 8 && nq + K <= 65535) {
+        k_keymult_loop<4><<<dim3(1u << (logN - 8), nq + K), 256, 0, s>>>(
+            acc, D, key, galois, nq, K, L, keyP, addb, accumulate ? 1 : 0, logN, nbatch, d_stride, acc_stride,
+            add_stride);
+        check_launch("keymult_loop");
+        return;
+    }
     const dim3 grid(nbatch, (unsigned)chunks);
 #define HB_KM_ARGS acc, D, key, galois, nq, K, L, beta, keyP, addb, accumulate ? 1 : 0, logN, d_stride, acc_stride, add_stride
     switch (beta) {
