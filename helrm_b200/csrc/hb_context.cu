@@ -415,13 +415,34 @@ public:
                 for (auto &x : v) x = ((x >> 30) << 32) | (x & ((1ull << 30) - 1));
                 return v;
             };
-            auto packed29 = [](std::vector<u64> v) {  // split-29 form: (v >> 29) << 32 | (v & (2^29 - 1))
-                for (auto &x : v) x = ((x >> 29) << 32) | (x & ((1ull << 29) - 1));
-                return v;
+            // q-row targets (primes below 2^40) as exact doubles: qhat as
+            // pairs {t, fl(t / q_e)} (quotient estimates of the FP64 modular
+            // products), qjneg as t; special-prime targets left zero
+            auto pairs_d = [&](const std::vector<u64> &v) {
+                std::vector<u64> o(2 * v.size(), 0);
+                for (size_t i = 0; i < v.size(); i++) {
+                    const int e = (int)(i % ne);
+                    if (e >= nq || primes[e] >= (1ull << 40)) continue;
+                    const double t = (double)v[i], r = t / (double)primes[e];
+                    std::memcpy(&o[2 * i], &t, 8);
+                    std::memcpy(&o[2 * i + 1], &r, 8);
+                }
+                return o;
+            };
+            auto singles_d = [&](const std::vector<u64> &v) {
+                std::vector<u64> o(v.size(), 0);
+                for (size_t i = 0; i < v.size(); i++) {
+                    const int e = (int)(i % ne);
+                    if (e >= nq || primes[e] >= (1ull << 40)) continue;
+                    const double t = (double)v[i];
+                    std::memcpy(&o[i], &t, 8);
+                }
+                return o;
             };
             size_t o_qhinv = put(qhinv), o_qhinvp = put(qhinvp), o_qhat = put(qhat), o_qjneg = put(qjneg),
-                   o_pneg = put(pneg), o_qhat_s = put(packed(qhat)), o_qjneg_s = put(packed(qjneg)),
-                   o_qhat_k = put(packed29(qhat)), o_qjneg_k = put(packed29(qjneg));
+                   o_pneg = put(pneg), o_qhat_s = put(packed(qhat)), o_qjneg_s = put(packed(qjneg));
+            if (blob.size() & 1) blob.push_back(0);  // 16-byte alignment of the pairs
+            size_t o_qhat_d = put(pairs_d(qhat)), o_qjneg_d = put(singles_d(qjneg));
             size_t o_phinv = put(phinv), o_phinvp = put(phinvp), o_phat = put(phat), o_pinv = put(pinv),
                    o_pinvp = put(pinvp), o_qlinv = put(qlinv), o_qlinvp = put(qlinvp), o_phat_s = put(packed(phat)),
                    o_pneg_s = put(packed(pneg));
@@ -438,8 +459,8 @@ public:
             T.mu.qjneg = T.blob + o_qjneg;
             T.mu.qhat_s = T.blob + o_qhat_s;
             T.mu.qjneg_s = T.blob + o_qjneg_s;
-            T.mu.qhat_k = T.blob + o_qhat_k;
-            T.mu.qjneg_k = T.blob + o_qjneg_k;
+            T.mu.qhat_d = reinterpret_cast<const double2 *>(T.blob + o_qhat_d);
+            T.mu.qjneg_d = reinterpret_cast<const double *>(T.blob + o_qjneg_d);
             T.mu.split = small_main ? 1 : 0;
             T.md.pneg = T.blob + o_pneg;
             T.md.phat_s = T.blob + o_phat_s;

@@ -1294,28 +1294,32 @@ __global__ void k_modup_bconv(u64 *__restrict__ D, const u64 *__restrict__ X, co
     }
 }
 
-// The same conversion with split-30 products (every main prime below 2^40;
-// the digit values y_m are then below 2^40 and every table entry below
-// 2^61).  NA = digits size, a compile-time constant; blockIdx.y + j0 is the
-// digit.  The digit's qhat and qjneg rows are staged in shared memory.
+// The same conversion for main primes below 2^40 (the digit values y_m are
+// then below 2^40).  q-row targets on the FP64 pipe: exact centred products
+// y_m * qhat_m mod q_e (|t| <= 0.502 q each) and the lift term
+// nneg * (-Q_j mod q_e) < 8 q, summed exactly as doubles (|S| < 13 q), one
+// reduction per output.  Special-prime targets in split-30 products (table
+// values below 2^61).  NA = digit size, a compile-time constant;
+// blockIdx.y + j0 is the digit.  The digit's tables are staged in shared
+// memory.
 template <int NA>
 __global__ void __launch_bounds__(256)
     k_modup_bconv_split(u64 *__restrict__ D, const u64 *__restrict__ X, const u64 *__restrict__ c1ntt, int nq, int K,
                         int L, int alpha, int j0, ModUpTab tab, int logN, size_t in_stride, size_t out_stride,
                         size_t c1_stride) {
-    __shared__ u64 st[(NA + 1) * HB_MAX_PRIMES];  // split-30 qhat [m][e], then qjneg [e]
-    __shared__ u64 sk[(NA + 1) * HB_MAX_PRIMES];  // the same in split-29 form
+    __shared__ u64 st[(NA + 1) * HB_MAX_PRIMES];      // split-30 qhat [m][e], then qjneg [e]
+    __shared__ double2 sd[(NA + 1) * HB_MAX_PRIMES];  // q-row targets: {t, fl(t / q_e)} [m][e], then {qjneg, 0}
     const int N = 1 << logN;
     const int j = j0 + blockIdx.y, b = blockIdx.z;
     const int ne = nq + K;
     const int lo = j * alpha;
     for (int i = threadIdx.x; i < NA * ne; i += blockDim.x) {
         st[i] = tab.qhat_s[(size_t)j * alpha * ne + i];
-        sk[i] = tab.qhat_k[(size_t)j * alpha * ne + i];
+        sd[i] = tab.qhat_d[(size_t)j * alpha * ne + i];
     }
     for (int i = threadIdx.x; i < ne; i += blockDim.x) {
         st[NA * ne + i] = tab.qjneg_s[(size_t)j * ne + i];
-        sk[NA * ne + i] = tab.qjneg_k[(size_t)j * ne + i];
+        sd[NA * ne + i] = make_double2(tab.qjneg_d[(size_t)j * ne + i], 0.0);
     }
     __syncthreads();
     // two coefficients per thread, 256 apart: every table value, prime
@@ -1324,8 +1328,8 @@ __global__ void __launch_bounds__(256)
     if (n0 >= N) return;  // N is a multiple of 512, so n0 + 256 < N as well
     const u64 *Xb = X + b * in_stride;
     u64 *Db = D + b * out_stride + (size_t)j * ne * N;
-    u64 y[2][NA], yk[2][NA];
-    unsigned ys[2][NA];
+    u64 y[2][NA];
+    double yd[2][NA];
     unsigned nneg[2] = {0, 0};
 #pragma unroll
     for (int m = 0; m < NA; m++) {
@@ -1337,11 +1341,11 @@ __global__ void __launch_bounds__(256)
             const u64 v = mul_shoup(Xb[(size_t)pm * N + n0 + 256 * c], w, wp, qm);
             nneg[c] += v > (qm >> 1);
             y[c][m] = split_pack(v);
-            yk[c][m] = k29_pack(v);
-            ys[c][m] = k29_sum(yk[c][m]);
+            yd[c][m] = u64_to_d(v);
         }
     }
-    // q-row targets (below 2^40): Karatsuba split-29 products, one reduction
+    const double nn0 = u32_to_double(nneg[0]), nn1 = u32_to_double(nneg[1]);
+    // q-row targets; the digit's own rows are copies of its input
     for (int e = 0; e < nq; e++) {
         u64 *de = Db + (size_t)e * N + n0;
         if (e >= lo && e < lo + NA) {
@@ -1350,19 +1354,18 @@ __global__ void __launch_bounds__(256)
             de[256] = ce[256];
             continue;
         }
-        Kara29 acc0 = {0, 0, 0}, acc1 = {0, 0, 0};
+        const PrimeConst &pc = c_pc[e];
+        const double qd = u64_to_d(pc.q);
+        const double tn = sd[NA * ne + e].x;
+        double s0 = __dmul_rn(nn0, tn), s1 = __dmul_rn(nn1, tn);
 #pragma unroll
         for (int m = 0; m < NA; m++) {
-            const u64 tv = sk[m * ne + e];
-            k29_mac(acc0, tv, yk[0][m], ys[0][m]);
-            k29_mac(acc1, tv, yk[1][m], ys[1][m]);
+            const double2 tw = sd[m * ne + e];
+            s0 = __dadd_rn(s0, mulmod_d(yd[0][m], tw, qd));
+            s1 = __dadd_rn(s1, mulmod_d(yd[1][m], tw, qd));
         }
-        const u64 tn = sk[NA * ne + e];
-        k29_mac(acc0, tn, (u64)nneg[0], nneg[0]);
-        k29_mac(acc1, tn, (u64)nneg[1], nneg[1]);
-        const PrimeConst &pc = c_pc[e];
-        de[0] = k29_reduce(acc0, pc);
-        de[256] = k29_reduce(acc1, pc);
+        de[0] = d_mod_to_u64(s0, qd, pc.qinv);
+        de[256] = d_mod_to_u64(s1, qd, pc.qinv);
     }
     // special-prime targets: split-30 products (table values below 2^61)
     for (int e = nq; e < ne; e++) {

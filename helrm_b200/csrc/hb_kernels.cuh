@@ -134,8 +134,8 @@ struct ModUpTab {
     const u64 *qjneg;   // [beta][ne]               t_e - (Q_j mod t_e)
     const u64 *qhat_s;  // qhat in split-30 packed form
     const u64 *qjneg_s; // qjneg in split-30 packed form
-    const u64 *qhat_k;  // qhat in split-29 packed form (Karatsuba products on q-row targets)
-    const u64 *qjneg_k; // qjneg in split-29 packed form
+    const double2 *qhat_d;  // q-row targets: qhat as {t, fl(t / q_e)} (FP64 modular products)
+    const double *qjneg_d;  // q-row targets: qjneg as a double
     int split;          // every main prime below 2^40: split products
 };
 void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
