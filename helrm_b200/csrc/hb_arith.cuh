@@ -100,6 +100,14 @@ __device__ __forceinline__ double mulmod_d(double y, const double2 tw, double q)
     const double pl = __fma_rn(Qd, q, -ph);
     return __dsub_rn(__fma_rn(y, tw.x, -ph), pl);
 }
+// centred double v (|v| < 2^51) -> v mod q in [0, q) as u64
+__device__ __forceinline__ u64 d_mod_to_u64(double v, double q, double qinv) {
+    const double magic = 6755399441055744.0;
+    const double Qd = __dsub_rn(__fma_rn(v, qinv, magic), magic);
+    double r = __fma_rn(-Qd, q, v);  // exact: |r| <= 0.5 q + tiny
+    if (r < 0.0) r = __dadd_rn(r, q);
+    return (u64)__double_as_longlong(__dadd_rn(r, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
+}
 __device__ __forceinline__ double center_d(double v, double q, double qinv) {
     const double magic = 6755399441055744.0;
     const double Qd = __dsub_rn(__fma_rn(v, qinv, magic), magic);

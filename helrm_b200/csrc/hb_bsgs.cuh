@@ -121,7 +121,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             u64 v = 0;
             if (key) v = key[((size_t)jp * keyP + p) * N + n0 + n];
             else if (kFixed && (jp == 0 || jp == 3)) v = pq_e;
-            skey[i] = fast ? k29_pack(v) : v;
+            // limbs below 2^40: the key words as exact doubles (phase A on
+            // the FP64 pipe); others as they are (128-bit products)
+            skey[i] = fast ? (u64)__double_as_longlong(u64_to_d(v)) : v;
         }
     }
     __syncthreads();
@@ -223,11 +225,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         ptv[bb] = fast ? k29_pack(v) : v;
     }
-    u64 pq_packed = 0, pq = 0;
-    if (qrow) {
-        pq = pmod_q[e];
-        pq_packed = k29_pack(pq);
-    }
+    const u64 pq = pq_e;
+    // phase A on limbs below 2^40: exact centred FP64 products key * digit
+    // with the digit's quotient estimate fl(d fl(1/q)) (within 2^-15 of
+    // key * d / q, so each |t| <= 0.502 q), nine of them summed exactly
+    const double qd = u64_to_d(pc.q);
+    const double2 pqw = make_double2(u64_to_d(pq), __dmul_rn(u64_to_d(pq), pc.qinv));
 
     for (int b = 0; b < nbatch; b++) {
         if (b + 1 < nbatch) {
@@ -253,21 +256,19 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const int so = soff[it];
                 const u64 *kt = skey + (size_t)bb * beta * 2 * HB_BT + n;
                 if (fast) {
-                    Kara29 sb = {0, 0, 0}, sa = {0, 0, 0};
+                    const double *kd = reinterpret_cast<const double *>(kt);
+                    double sb = 0.0, sa = 0.0;
 #pragma unroll
                     for (int j = 0; j < HB_MAX_BETA; j++)
                         if (j < beta) {
-                            const u64 d = k29_pack(g[j * HB_BT + so]);
-                            const unsigned ds = k29_sum(d);
-                            k29_mac(sb, kt[(j * 2 + 0) * HB_BT], d, ds);
-                            k29_mac(sa, kt[(j * 2 + 1) * HB_BT], d, ds);
+                            const double dv = u64_to_d(g[j * HB_BT + so]);
+                            const double2 w = make_double2(dv, __dmul_rn(dv, pc.qinv));
+                            sb = __dadd_rn(sb, mulmod_d(kd[(j * 2 + 0) * HB_BT], w, qd));
+                            sa = __dadd_rn(sa, mulmod_d(kd[(j * 2 + 1) * HB_BT], w, qd));
                         }
-                    if (qrow) {
-                        const u64 cv = k29_pack(g[beta * HB_BT + so]);
-                        k29_mac(sb, pq_packed, cv, k29_sum(cv));
-                    }
-                    rb = k29_reduce(sb, pc);
-                    ra = k29_reduce(sa, pc);
+                    if (qrow) sb = __dadd_rn(sb, mulmod_d(u64_to_d(g[beta * HB_BT + so]), pqw, qd));
+                    rb = d_mod_to_u64(sb, qd, pc.qinv);
+                    ra = d_mod_to_u64(sa, qd, pc.qinv);
                 } else {
                     u128 sb = {0, 0}, sa = {0, 0};
 #pragma unroll

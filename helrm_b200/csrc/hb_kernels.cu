@@ -569,14 +569,6 @@ __device__ __forceinline__ void fwd_b_d(double (&x)[16], const double2 *T, int b
         }
     }
 }
-// centred double v (|v| < 2^51) -> v mod q in [0, q) as u64
-__device__ __forceinline__ u64 d_mod_to_u64(double v, double q, double qinv) {
-    const double magic = 6755399441055744.0;
-    const double Qd = __dsub_rn(__fma_rn(v, qinv, magic), magic);
-    double r = __fma_rn(-Qd, q, v);  // exact: |r| <= 0.5 q + tiny
-    if (r < 0.0) r = __dadd_rn(r, q);
-    return (u64)__double_as_longlong(__dadd_rn(r, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
-}
 // Inverse (Gentleman-Sande) butterflies in double precision: x' = x + y,
 // y' = (x - y) w mod q (centred, as in ct_bfly_d).  Sums grow: from values
 // below B a 4-stage group ends below 16 B, so every group ends by re-centring
