@@ -269,7 +269,7 @@ public:
         // twiddles
         // [4][P][N] u64 twiddles and Shoup companions, then [2][P][N] pairs
         // {w, fl(w/q)} for primes below 2^40 (quotient estimates of the NTT)
-        std::vector<u64> tw((size_t)8 * P * N, 0);
+        std::vector<u64> tw((size_t)10 * P * N, 0);
         for (int p = 0; p < P; p++) {
             u64 q = primes[p];
             u64 psi = find_psi(q, logN), ipsi = h_invm(psi, q);
@@ -302,6 +302,20 @@ public:
                     std::memcpy(&Ix[2 * i + 1], &iq, 8);
                 }
                 if (logN == 16) {
+                    // single doubles w for the block pass; in the segment of
+                    // the 2^15-group stage (16 threads x 8 values) value i of
+                    // thread c is stored at 64 (i / 4) + 4 c + (i % 4)
+                    double *Ts = reinterpret_cast<double *>(&tw[(size_t)(8 * P + p) * N]);
+                    double *Is = reinterpret_cast<double *>(&tw[(size_t)(9 * P + p) * N]);
+                    for (int i = 0; i < N; i++) {
+                        size_t dst = (size_t)i;
+                        if (i >= 32768) {
+                            const int b0 = i & ~127, r = i & 127, c = r >> 3, k = r & 7;
+                            dst = (size_t)b0 + 64 * (k >> 2) + 4 * c + (k & 3);
+                        }
+                        Ts[dst] = (double)T[i];
+                        Is[dst] = (double)I[i];
+                    }
                     // the 256-point block pass reads the stages of 2^14 and
                     // 2^15 groups in segments of 16 threads x 2^s pairs
                     // (s = 2, 3); pair i of thread c is stored at
@@ -331,6 +345,8 @@ public:
         ntt.itwp = d_tables + (size_t)3 * P * N;
         ntt.twx = reinterpret_cast<const ulonglong2 *>(d_tables + (size_t)4 * P * N);
         ntt.itwx = reinterpret_cast<const ulonglong2 *>(d_tables + (size_t)6 * P * N);
+        ntt.tws = reinterpret_cast<const double *>(d_tables + (size_t)8 * P * N);
+        ntt.itws = reinterpret_cast<const double *>(d_tables + (size_t)9 * P * N);
         ntt.logN = logN;
 
         std::vector<u64> pm(P);

@@ -632,6 +632,99 @@ __device__ __forceinline__ void inv_a_dg(double (&x)[16], const double2 *T, int 
 #pragma unroll
     for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
 }
+// Block-pass twiddles as single doubles w; the pair {w, fl(w fl(1/q))} is
+// formed in registers (the quotient estimate within 2^-12 of y w / q for
+// |y| < 2^40, so a butterfly's |t| stays at most 0.5002 q).  NP values per
+// thread: 1, 2 (one 128-bit load) or 4 (one 256-bit load) contiguous; 8 as
+// two 256-bit loads STRIDE values apart.
+template <int NP, int STRIDE>
+__device__ __forceinline__ void ld_tw1(double2 (&tw)[8], const double *src, double qinv) {
+    double w[8];
+    if (NP == 1) {
+        w[0] = __ldg(src);
+    } else if (NP == 2) {
+        const double2 v = __ldg(reinterpret_cast<const double2 *>(src));
+        w[0] = v.x, w[1] = v.y;
+    } else {
+#pragma unroll
+        for (int v = 0; v < NP / 4; v++)
+            asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
+                : "=d"(w[4 * v]), "=d"(w[4 * v + 1]), "=d"(w[4 * v + 2]), "=d"(w[4 * v + 3])
+                : "l"(src + STRIDE * v));
+    }
+#pragma unroll
+    for (int i = 0; i < NP; i++) tw[i] = make_double2(w[i], __dmul_rn(w[i], qinv));
+}
+__device__ __forceinline__ void fwd_a_ds(double (&x)[16], const double *T, int base, double q, double qinv) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s;
+        double2 tw[8];
+        if (s == 0) ld_tw1<1, 0>(tw, T + base, qinv);
+        if (s == 1) ld_tw1<2, 0>(tw, T + 2 * base, qinv);
+        if (s == 2) ld_tw1<4, 0>(tw, T + 4 * base, qinv);
+        if (s == 3) ld_tw1<8, 4>(tw, T + 8 * base, qinv);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            ct_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
+        }
+    }
+}
+__device__ __forceinline__ void fwd_b_ds(double (&x)[16], const double *T, int base, int c, double q, double qinv) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int d = 8 >> s, g = 16 << s;
+        double2 tw[8];
+        const double *seg = T + g * base;
+        if (s == 0) ld_tw1<1, 0>(tw, seg + c, qinv);
+        if (s == 1) ld_tw1<2, 0>(tw, seg + 2 * c, qinv);
+        if (s == 2) ld_tw1<4, 0>(tw, seg + 4 * c, qinv);
+        if (s == 3) ld_tw1<8, 64>(tw, seg + 4 * c, qinv);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            ct_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
+        }
+    }
+}
+__device__ __forceinline__ void inv_b_ds(double (&x)[16], const double *T, int base, int c, double q, double qinv) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s, g = 16 << s;
+        double2 tw[8];
+        const double *seg = T + g * base;
+        if (s == 0) ld_tw1<1, 0>(tw, seg + c, qinv);
+        if (s == 1) ld_tw1<2, 0>(tw, seg + 2 * c, qinv);
+        if (s == 2) ld_tw1<4, 0>(tw, seg + 4 * c, qinv);
+        if (s == 3) ld_tw1<8, 64>(tw, seg + 4 * c, qinv);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            gs_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
+}
+__device__ __forceinline__ void inv_a_ds(double (&x)[16], const double *T, int base, double q, double qinv) {
+#pragma unroll
+    for (int s = 3; s >= 0; s--) {
+        const int d = 8 >> s;
+        double2 tw[8];
+        if (s == 0) ld_tw1<1, 0>(tw, T + base, qinv);
+        if (s == 1) ld_tw1<2, 0>(tw, T + 2 * base, qinv);
+        if (s == 2) ld_tw1<4, 0>(tw, T + 4 * base, qinv);
+        if (s == 3) ld_tw1<8, 4>(tw, T + 8 * base, qinv);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (k & d) continue;
+            gs_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
+}
 template <bool G, bool CENTER>
 __device__ __forceinline__ void inv_a_d(double (&x)[16], const double2 *T, int base, double q, double qinv) {
 #pragma unroll
@@ -747,7 +840,8 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
 template <bool INV>
 __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
                                                       const u64 *__restrict__ twp,
-                                                      const ulonglong2 *__restrict__ twx, int row0,
+                                                      const ulonglong2 *__restrict__ twx,
+                                                      const double *__restrict__ tws, int row0,
                                                       const u64 *__restrict__ src = nullptr, size_t src_stride = 0,
                                                       int src_per = 1) {
     __shared__ u64 sm[16 * 272];
@@ -760,23 +854,22 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
     const int rb = (blockIdx.x << 4) + blk;
     u64 *a = data + ((size_t)row << 16) + ((size_t)rb << 8);
     const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
-    const ulonglong2 *T = twx + ((size_t)p << 16);
     u64 *sb = sm + blk * 272;  // 256 elements of this block, 17-word rows of 16 (padding)
     u64 x[16];
     if (!INV && fast) {
         // doubles from the column pass; reduced and converted at the end
         const double qd = (double)q, qinv = c_pc[p].qinv;
-        const double2 *Td = reinterpret_cast<const double2 *>(T);
         double xd[16];
 #pragma unroll
         for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)a[c + 16 * k]);
-        fwd_a_dg(xd, Td, 256 + rb, qd);
+        const double *Ts = tws + ((size_t)p << 16);
+        fwd_a_ds(xd, Ts, 256 + rb, qd, qinv);
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[k * 17 + c] = (u64)__double_as_longlong(xd[k]);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sb[c * 17 + k]);
-        fwd_b_dg(xd, Td, 256 + rb, c, qd);
+        fwd_b_ds(xd, Ts, 256 + rb, c, qd, qinv);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) sb[c * 17 + k] = d_mod_to_u64(xd[k], qd, qinv);
@@ -815,18 +908,18 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, 
             // first pass of the double-precision inverse; the column pass
             // receives centred doubles (|v| <= 0.5 q)
             const double qd = (double)q, qinv = c_pc[p].qinv;
-            const double2 *Td = reinterpret_cast<const double2 *>(T);
             double xd[16];
 #pragma unroll
             for (int k = 0; k < 16; k++) xd[k] = u64_to_d(sb[c * 17 + k]);
-            inv_b_dg(xd, Td, 256 + rb, c, qd, qinv);
+            const double *Ts = tws + ((size_t)p << 16);
+            inv_b_ds(xd, Ts, 256 + rb, c, qd, qinv);
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 16; k++) sb[c * 17 + k] = (u64)__double_as_longlong(xd[k]);
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 16; k++) xd[k] = __longlong_as_double((long long)sb[k * 17 + c]);
-            inv_a_dg(xd, Td, 256 + rb, qd, qinv);
+            inv_a_ds(xd, Ts, 256 + rb, qd, qinv);
 #pragma unroll
             for (int k = 0; k < 16; k++) a[c + 16 * k] = (u64)__double_as_longlong(xd[k]);
         } else {
@@ -852,9 +945,9 @@ static void ntt256_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bo
         const dim3 grid(16, nr);
         if (!inv) {
             k_ntt256_cols<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twx, r0);
-            k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twx, r0);
+            k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twx, t.tws, r0);
         } else {
-            k_ntt256_rows<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwx, r0);
+            k_ntt256_rows<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwx, t.itws, r0);
             k_ntt256_cols<true><<<grid, 256, 0, s>>>(data, map, t.itw, t.itwp, t.itwx, r0);
         }
     }
@@ -925,7 +1018,8 @@ void ntt_inverse_from(u64 *dst, const u64 *src, size_t src_stride, int per_item,
     for (int r0 = 0; r0 < nrows; r0 += 65535) {
         const int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
         const dim3 grid(16, nr);
-        k_ntt256_rows<true><<<grid, 256, 0, s>>>(dst, map, t.itw, t.itwp, t.itwx, r0, src, src_stride, per_item);
+        k_ntt256_rows<true><<<grid, 256, 0, s>>>(dst, map, t.itw, t.itwp, t.itwx, t.itws, r0, src, src_stride,
+                                                 per_item);
         k_ntt256_cols<true><<<grid, 256, 0, s>>>(dst, map, t.itw, t.itwp, t.itwx, r0);
     }
     check_launch("ntt256_from");

@@ -47,6 +47,9 @@ struct NttTables {
     const u64 *itw, *itwp;  // [P][N] psi^-brv(i)
     // [P][N] pairs of doubles {w, fl(w/q)} for primes below 2^40 (else 0)
     const ulonglong2 *twx, *itwx;
+    // [P][N] w as a double for primes below 2^40 (block pass of the 2^16
+    // NTT; its fl(w/q) is formed in the kernel)
+    const double *tws, *itws;
     int logN;
 };
 
