@@ -316,24 +316,6 @@ public:
                         Ts[dst] = (double)T[i];
                         Is[dst] = (double)I[i];
                     }
-                    // the 256-point block pass reads the stages of 2^14 and
-                    // 2^15 groups in segments of 16 threads x 2^s pairs
-                    // (s = 2, 3); pair i of thread c is stored at
-                    // 32 (i / 2) + 2 c + (i % 2) of its segment
-                    std::vector<u64> seg((size_t)2 * 16 * 8);
-                    for (u64 *X : {Tx, Ix})
-                        for (int st = 2; st <= 3; st++) {
-                            const int per = 1 << st, len = 16 * per;
-                            for (int b0 = (16 << st) * 256; b0 < (16 << st) * 512; b0 += len) {
-                                std::memcpy(seg.data(), X + (size_t)2 * b0, (size_t)len * 16);
-                                for (int c = 0; c < 16; c++)
-                                    for (int i = 0; i < per; i++) {
-                                        const size_t dst = (size_t)b0 + 32 * (i >> 1) + 2 * c + (i & 1);
-                                        X[2 * dst] = seg[(size_t)2 * (c * per + i)];
-                                        X[2 * dst + 1] = seg[(size_t)2 * (c * per + i) + 1];
-                                    }
-                            }
-                        }
                 }
             }
         }

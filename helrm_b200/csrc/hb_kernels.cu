@@ -481,70 +481,6 @@ __device__ __forceinline__ double2 twld_d(const double2 *t, int i) {
     if (G) return __ldg(t + i);
     return t[i];
 }
-// NP consecutive twiddle pairs from global memory, two pairs per 256-bit
-// load (the start is 32-byte aligned for NP >= 2: an even pair index)
-template <int NP>
-__device__ __forceinline__ void ld_pairs(double2 (&tw)[8], const double2 *src) {
-    if (NP == 1) {
-        tw[0] = __ldg(src);
-    } else {
-#pragma unroll
-        for (int v = 0; v < NP / 2; v++)
-            asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
-                : "=d"(tw[2 * v].x), "=d"(tw[2 * v].y), "=d"(tw[2 * v + 1].x), "=d"(tw[2 * v + 1].y)
-                : "l"(src + 2 * v));
-    }
-}
-// NP pairs, two per 256-bit load, the loads STRIDE pairs apart: the block
-// pass's last two forward stages (first two inverse ones) store the pairs
-// of a stage segment thread-interleaved, so that every warp load reads
-// contiguous lines
-template <int NP, int STRIDE>
-__device__ __forceinline__ void ld_pairs_s(double2 (&tw)[8], const double2 *src) {
-#pragma unroll
-    for (int v = 0; v < NP / 2; v++)
-        asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
-            : "=d"(tw[2 * v].x), "=d"(tw[2 * v].y), "=d"(tw[2 * v + 1].x), "=d"(tw[2 * v + 1].y)
-            : "l"(src + STRIDE * v));
-}
-// the two forward halves with twiddles from global memory (block pass):
-// stage s needs 2^s pairs per thread, loaded at the stage start.  In the
-// segment of stage s >= 2 (16 threads x 2^s pairs) thread c's pair i sits
-// at 32 (i / 2) + 2 c + (i % 2), the layout written by the table setup.
-__device__ __forceinline__ void fwd_a_dg(double (&x)[16], const double2 *T, int base, double q) {
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-        const int d = 8 >> s, g = 1 << s;
-        double2 tw[8];
-        if (s == 0) ld_pairs<1>(tw, T + base);
-        if (s == 1) ld_pairs<2>(tw, T + 2 * base);
-        if (s == 2) ld_pairs<4>(tw, T + 4 * base);
-        if (s == 3) ld_pairs<8>(tw, T + 8 * base);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            ct_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
-        }
-        (void)g;
-    }
-}
-__device__ __forceinline__ void fwd_b_dg(double (&x)[16], const double2 *T, int base, int c, double q) {
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-        const int d = 8 >> s, g = 16 << s;
-        double2 tw[8];
-        const double2 *seg = T + g * base;
-        if (s == 0) ld_pairs<1>(tw, seg + c);
-        if (s == 1) ld_pairs<2>(tw, seg + 2 * c);
-        if (s == 2) ld_pairs_s<4, 32>(tw, seg + 2 * c);
-        if (s == 3) ld_pairs_s<8, 32>(tw, seg + 2 * c);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            ct_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
-        }
-    }
-}
 template <bool G>
 __device__ __forceinline__ void fwd_a_d(double (&x)[16], const double2 *T, int base, double q) {
 #pragma unroll
@@ -589,44 +525,6 @@ __device__ __forceinline__ void inv_b_d(double (&x)[16], const double2 *T, int b
         for (int k = 0; k < 16; k++) {
             if (k & d) continue;
             gs_bfly_d(x[k], x[k + d], twld_d<G>(T, g * base + (c << s) + (k >> (4 - s))), q);
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
-}
-// inverse halves with twiddles from global memory (block pass), wide loads
-__device__ __forceinline__ void inv_b_dg(double (&x)[16], const double2 *T, int base, int c, double q, double qinv) {
-#pragma unroll
-    for (int s = 3; s >= 0; s--) {
-        const int d = 8 >> s, g = 16 << s;
-        double2 tw[8];
-        const double2 *seg = T + g * base;  // thread-interleaved for s >= 2
-        if (s == 0) ld_pairs<1>(tw, seg + c);
-        if (s == 1) ld_pairs<2>(tw, seg + 2 * c);
-        if (s == 2) ld_pairs_s<4, 32>(tw, seg + 2 * c);
-        if (s == 3) ld_pairs_s<8, 32>(tw, seg + 2 * c);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            gs_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < 16; k++) x[k] = center_d(x[k], q, qinv);
-}
-__device__ __forceinline__ void inv_a_dg(double (&x)[16], const double2 *T, int base, double q, double qinv) {
-#pragma unroll
-    for (int s = 3; s >= 0; s--) {
-        const int d = 8 >> s;
-        double2 tw[8];
-        if (s == 0) ld_pairs<1>(tw, T + base);
-        if (s == 1) ld_pairs<2>(tw, T + 2 * base);
-        if (s == 2) ld_pairs<4>(tw, T + 4 * base);
-        if (s == 3) ld_pairs<8>(tw, T + 8 * base);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (k & d) continue;
-            gs_bfly_d(x[k], x[k + d], tw[k >> (4 - s)], q);
         }
     }
 #pragma unroll
