@@ -770,23 +770,26 @@ public:
     }
 
     // ModDown of nb extended polys x (ne rows, item stride xs) -> out (nq rows, stride os),
-    // optionally + addend[tau_g] (stride as)
+    // optionally + addend[tau_g] (stride as) and + add2 (unrotated, stride a2s)
     void moddown(u64 *out, const u64 *x, int nq, int nb, size_t xs, size_t os, const u64 *addend = nullptr,
-                 u64 add_g = 1, size_t as = 0) {
+                 u64 add_g = 1, size_t as = 0, const u64 *add2 = nullptr, size_t a2s = 0) {
         u64 *Y = alloc((size_t)nb * K * N);
         RowMap pm = rowmap(K, 0, L);
         ntt_inverse_from(Y, x + (size_t)nq * N, xs, K, nb * K, pm, ntt, stream);
         u64 *Z = alloc((size_t)nb * nq * N);
         moddown_bconv(Z, Y, nq, K, L, lv[nq].md, logN, nb, (size_t)K * N, (size_t)nq * N, stream);
         ntt_forward(Z, nb * nq, qmap(nq), ntt, stream);
-        moddown_combine(out, x, Z, nq, lv[nq].md, addend, add_g, logN, nb, xs, (size_t)nq * N, os, as, stream);
+        moddown_combine(out, x, Z, nq, lv[nq].md, addend, add_g, logN, nb, xs, (size_t)nq * N, os, as, stream, add2,
+                        a2s);
         release(Y);
         release(Z);
     }
 
     // rotations of nb ciphertexts (contiguous [nb][2][nq][N] at `in`) by
-    // Galois g into `out` (same layout): one ModUp per ciphertext.
-    void rotate_batch(u64 *out, const u64 *in, int nq, int nb, u64 g, const u64 *key) {
+    // Galois g into `out` (same layout): one ModUp per ciphertext.  With
+    // `fold`, out = in + rot(in) (the hybrid fold's step, added in the
+    // ModDown combine; out must not alias in).
+    void rotate_batch(u64 *out, const u64 *in, int nq, int nb, u64 g, const u64 *key, bool fold = false) {
         const int ne = nq + K, beta = beta_of(nq);
         const size_t cts_ = (size_t)2 * nq * N;
         u64 *D = alloc((size_t)nb * beta * ne * N);
@@ -795,8 +798,9 @@ public:
         keymult(acc, D, key, g, nq, K, L, beta, P, nullptr, false, logN, nb, (size_t)beta * ne * N,
                 (size_t)2 * ne * N, 0, stream);
         release(D);
-        moddown(out, acc, nq, nb, (size_t)2 * ne * N, cts_, in, g, cts_);
-        moddown(out + (size_t)nq * N, acc + (size_t)ne * N, nq, nb, (size_t)2 * ne * N, cts_);
+        moddown(out, acc, nq, nb, (size_t)2 * ne * N, cts_, in, g, cts_, fold ? in : nullptr, cts_);
+        moddown(out + (size_t)nq * N, acc + (size_t)ne * N, nq, nb, (size_t)2 * ne * N, cts_, nullptr, 1, 0,
+                fold ? in + (size_t)nq * N : nullptr, cts_);
         release(acc);
     }
 
@@ -1299,8 +1303,8 @@ public:
                 int k = slots >> i;
                 u64 g = galois_of(k);
                 u64 *key = rotation_key(g);
-                rotate_batch(rot, buf, nq, nb, g, key);
-                ew_add(buf, buf, rot, nb * 2 * nq, qmap(nq), logN, stream);
+                rotate_batch(rot, buf, nq, nb, g, key, true);  // rot = buf + rot(buf)
+                std::swap(buf, rot);
             }
             scatter_words(dst, buf, cts_);
             release(buf);

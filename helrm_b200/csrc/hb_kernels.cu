@@ -1515,7 +1515,7 @@ void moddown_bconv(u64 *Z, const u64 *Y, int nq, int K, int L, const ModDownTab 
 
 __global__ void k_moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, ModDownTab tab, const u64 *addend,
                                   u64 g, int logN, size_t x_stride, size_t z_stride, size_t out_stride,
-                                  size_t add_stride) {
+                                  size_t add_stride, const u64 *add2, size_t add2_stride) {
     const int N = 1 << logN;
     const size_t n = (size_t)nq << logN;
     const int b = blockIdx.y;
@@ -1528,19 +1528,21 @@ __global__ void k_moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, 
             const unsigned src = g == 1 ? t : aut_index(t, g, logN);
             v = add_mod(v, addend[b * add_stride + ((size_t)row << logN) + src], q);
         }
+        if (add2) v = add_mod(v, add2[b * add2_stride + i], q);
         out[b * out_stride + i] = v;
     }
 }
 void moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, const ModDownTab &tab, const u64 *addend,
                      u64 add_galois, int logN, int nbatch, size_t x_stride, size_t z_stride, size_t out_stride,
-                     size_t add_stride, cudaStream_t s) {
+                     size_t add_stride, cudaStream_t s, const u64 *add2, size_t add2_stride) {
     size_t n = (size_t)nq << logN;
     unsigned g = grid1d(n, 256);
     if (g > 4096) g = 4096;
     dim3 grid(g, nbatch);
-    ProfScope ps(KC_MODDOWN_COMBINE, 8.0 * nbatch * (double)n * (addend ? 4 : 3), (double)nbatch * n, s, 1);
+    ProfScope ps(KC_MODDOWN_COMBINE, 8.0 * nbatch * (double)n * (3 + (addend ? 1 : 0) + (add2 ? 1 : 0)),
+                 (double)nbatch * n, s, 1);
     k_moddown_combine<<<grid, 256, 0, s>>>(out, x, Z, nq, tab, addend, add_galois, logN, x_stride, z_stride,
-                                           out_stride, add_stride);
+                                           out_stride, add_stride, add2, add2_stride);
     check_launch("moddown_combine");
 }
 

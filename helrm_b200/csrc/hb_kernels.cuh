@@ -161,9 +161,11 @@ struct ModDownTab {
 void moddown_bconv(u64 *Z, const u64 *Y, int nq, int K, int L, const ModDownTab &tab, int logN, int nbatch,
                    size_t in_stride, size_t out_stride, cudaStream_t s);
 // out[i] = (x[i] - Z[i]) * pinv_i (+ addend[i][tau_g(n)] if addend)
+// (+ add2[i] if add2: an unrotated addend, the hybrid fold's c + rot(c))
 void moddown_combine(u64 *out, const u64 *x, const u64 *Z, int nq, const ModDownTab &tab, const u64 *addend,
                      u64 add_galois, int logN, int nbatch, size_t x_stride, size_t z_stride,
-                     size_t out_stride, size_t add_stride, cudaStream_t s);
+                     size_t out_stride, size_t add_stride, cudaStream_t s, const u64 *add2 = nullptr,
+                     size_t add2_stride = 0);
 
 // ---- rescale ---------------------------------------------------------------
 // prep: W[pl][i] = (h mod q_i) - ((R[pl] + h) mod q_l mod q_i), R = INTT of last limb (coef)
