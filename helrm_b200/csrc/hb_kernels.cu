@@ -640,12 +640,19 @@ __device__ __forceinline__ void inv_a_d(double (&x)[16], const double2 *T, int b
     }
 }
 
+// resident blocks per SM of the two 2^16 NTT passes
+#ifndef HB_NTT_COLS_BLOCKS
+#define HB_NTT_COLS_BLOCKS 4
+#endif
+#ifndef HB_NTT_ROWS_BLOCKS
+#define HB_NTT_ROWS_BLOCKS 3
+#endif
 // Column pass: the 16 columns c0..c0+15, element (r, col) at r*256 + c0 + col.
 // Primes below 2^40 take twiddle pairs {w, fl(w/q)} (the first 256
 // entries, the same for every block, staged in shared memory); the others
 // Shoup pairs from global memory.
 template <bool INV>
-__global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+__global__ void __launch_bounds__(256, HB_NTT_COLS_BLOCKS) k_ntt256_cols(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
                                                       const u64 *__restrict__ twp,
                                                       const ulonglong2 *__restrict__ twx, int row0) {
     __shared__ u64 sm[256 * 17];
@@ -736,7 +743,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt256_cols(u64 *__restrict__ data, 
 
 // Block pass: blocks rb0..rb0+15 of 256 contiguous elements.
 template <bool INV>
-__global__ void __launch_bounds__(256, 3) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
+__global__ void __launch_bounds__(256, HB_NTT_ROWS_BLOCKS) k_ntt256_rows(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw,
                                                       const u64 *__restrict__ twp,
                                                       const ulonglong2 *__restrict__ twx,
                                                       const double *__restrict__ tws, int row0,
