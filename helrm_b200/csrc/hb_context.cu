@@ -1215,19 +1215,36 @@ public:
         }
         u64 *aq = alloc((size_t)nb * nq * N);
         u64 *D2 = alloc((size_t)nb * beta * es);
-        for (int s = 0; s < nslots; s++) {
-            const int g = t.giant_of_slot[s];
-            if (g == 0) continue;
-            const u64 gal = galois_of(g * t.bs);
-            const u64 *key = rot_keys.at(gal);
-            const u64 *Ia = inner + (size_t)s * 2 * es + es;
-            moddown(aq, Ia, nq, nb, (size_t)nslots * 2 * es, (size_t)nq * N);
+        std::vector<int> gslots;
+        for (int s = 0; s < nslots; s++)
+            if (t.giant_of_slot[s] != 0) gslots.push_back(s);
+        // four digits: giant steps in pairs, one key multiplication per pair
+        const bool pairs = beta == 4 && logN >= 8 && gslots.size() >= 2;
+        u64 *D2b = pairs ? alloc((size_t)nb * beta * es) : nullptr;
+        const size_t is = (size_t)nslots * 2 * es;
+        for (size_t i = 0; i < gslots.size();) {
+            const int s1 = gslots[i];
+            const u64 gal1 = galois_of(t.giant_of_slot[s1] * t.bs);
+            moddown(aq, inner + (size_t)s1 * 2 * es + es, nq, nb, is, (size_t)nq * N);
             modup(D2, aq, nq, nb, (size_t)nq * N);
-            keymult(acc, D2, key, gal, nq, K, L, beta, P, inner + (size_t)s * 2 * es, true, logN, nb,
-                    (size_t)beta * es, acc_stride, (size_t)nslots * 2 * es, stream);
+            if (pairs && i + 1 < gslots.size()) {
+                const int s2 = gslots[i + 1];
+                const u64 gal2 = galois_of(t.giant_of_slot[s2] * t.bs);
+                moddown(aq, inner + (size_t)s2 * 2 * es + es, nq, nb, is, (size_t)nq * N);
+                modup(D2b, aq, nq, nb, (size_t)nq * N);
+                keymult2(acc, D2, rot_keys.at(gal1), gal1, inner + (size_t)s1 * 2 * es, D2b, rot_keys.at(gal2), gal2,
+                         inner + (size_t)s2 * 2 * es, nq, K, L, beta, P, true, logN, nb, (size_t)beta * es,
+                         acc_stride, is, stream);
+                i += 2;
+            } else {
+                keymult(acc, D2, rot_keys.at(gal1), gal1, nq, K, L, beta, P, inner + (size_t)s1 * 2 * es, true, logN,
+                        nb, (size_t)beta * es, acc_stride, is, stream);
+                i += 1;
+            }
         }
         release(aq);
         release(D2);
+        if (D2b) release(D2b);
         moddown(out, acc, nq, nb, acc_stride, cts_);
         moddown(out + (size_t)nq * N, acc + es, nq, nb, acc_stride, cts_);
         release(inner);

@@ -1773,6 +1773,120 @@ __global__ void __launch_bounds__(256, HB_KEYMULT_LOOP_BLOCKS)
     }
 }
 
+// Two giant steps in one pass (four digits each): acc += KS(D1, key1) +
+// sigma_1(addb1) + KS(D2, key2) + sigma_2(addb2).  The accumulator is read
+// and written once for both, and the eight products of each output share
+// one reduction (split-29 sums hold up to 33 terms, 128-bit sums of eight
+// 120-bit products stay below 2^124).
+#ifndef HB_KEYMULT2_BLOCKS
+#define HB_KEYMULT2_BLOCKS 3
+#endif
+__global__ void __launch_bounds__(256, HB_KEYMULT2_BLOCKS)
+    k_keymult_loop2(u64 *__restrict__ acc, const u64 *__restrict__ D1, const u64 *__restrict__ key1, u64 g1,
+                    const u64 *__restrict__ addb1, const u64 *__restrict__ D2, const u64 *__restrict__ key2, u64 g2,
+                    const u64 *__restrict__ addb2, int nq, int K, int L, int keyP, int accumulate, int logN,
+                    int nbatch, size_t d_stride, size_t acc_stride, size_t add_stride) {
+    constexpr int B = 4;
+    const int ne = nq + K;
+    const size_t n_all = (size_t)ne << logN;
+    const int e = blockIdx.y;
+    const unsigned t = blockIdx.x * 256u + threadIdx.x;
+    const unsigned src1 = g1 == 1 ? t : aut_index(t, g1, logN), src2 = g2 == 1 ? t : aut_index(t, g2, logN);
+    const int p = e < nq ? e : L + (e - nq);
+    const PrimeConst pc = c_pc[p];
+    const size_t kofs = ((size_t)p << logN) + t, kstep = (size_t)keyP << logN;
+    const size_t erow = (size_t)e << logN, drow1 = erow + src1, drow2 = erow + src2, irow = erow + t;
+    if (pc.q < (1ull << 40)) {
+        unsigned kl[2][2][B], kh[2][2][B], ks[2][2][B];  // [giant][b/a][digit]
+#pragma unroll
+        for (int gi = 0; gi < 2; gi++) {
+            const u64 *kp = (gi ? key2 : key1) + kofs;
+#pragma unroll
+            for (int j = 0; j < B; j++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const u64 k = k29_pack(kp[(2 * j + c) * kstep]);
+                    kl[gi][c][j] = (unsigned)k, kh[gi][c][j] = (unsigned)(k >> 32);
+                    ks[gi][c][j] = kl[gi][c][j] + kh[gi][c][j];
+                }
+        }
+        for (int b = 0; b < nbatch; b++) {
+            Kara29 sb = {0, 0, 0}, sa = {0, 0, 0};
+#pragma unroll
+            for (int gi = 0; gi < 2; gi++) {
+                const u64 *dp = (gi ? D2 : D1) + b * d_stride + (gi ? drow2 : drow1);
+                u64 dv[B];
+#pragma unroll
+                for (int j = 0; j < B; j++) dv[j] = dp[j * n_all];
+#pragma unroll
+                for (int j = 0; j < B; j++) {
+                    const u64 d = k29_pack(dv[j]);
+                    const unsigned dl = (unsigned)d, dh = (unsigned)(d >> 32), ds = dl + dh;
+                    k29_mac_s(sb, kl[gi][0][j], kh[gi][0][j], ks[gi][0][j], dl, dh, ds);
+                    k29_mac_s(sa, kl[gi][1][j], kh[gi][1][j], ks[gi][1][j], dl, dh, ds);
+                }
+            }
+            u64 vb = k29_reduce(sb, pc), va = k29_reduce(sa, pc);
+            vb = add_mod(vb, addb1[b * add_stride + drow1], pc.q);
+            vb = add_mod(vb, addb2[b * add_stride + drow2], pc.q);
+            u64 *A = acc + b * acc_stride + irow;
+            if (accumulate) {
+                vb = add_mod(vb, A[0], pc.q);
+                va = add_mod(va, A[n_all], pc.q);
+            }
+            A[0] = vb;
+            A[n_all] = va;
+        }
+    } else {
+        u64 kv[2][2][B];
+#pragma unroll
+        for (int gi = 0; gi < 2; gi++) {
+            const u64 *kp = (gi ? key2 : key1) + kofs;
+#pragma unroll
+            for (int j = 0; j < B; j++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) kv[gi][c][j] = kp[(2 * j + c) * kstep];
+        }
+        for (int b = 0; b < nbatch; b++) {
+            u128 sb = {0, 0}, sa = {0, 0};
+#pragma unroll
+            for (int gi = 0; gi < 2; gi++) {
+                const u64 *dp = (gi ? D2 : D1) + b * d_stride + (gi ? drow2 : drow1);
+#pragma unroll
+                for (int j = 0; j < B; j++) {
+                    const u64 d = dp[j * n_all];
+                    mac128(sb, d, kv[gi][0][j]);
+                    mac128(sa, d, kv[gi][1][j]);
+                }
+            }
+            u64 vb = reduce128(sb, pc), va = reduce128(sa, pc);
+            vb = add_mod(vb, addb1[b * add_stride + drow1], pc.q);
+            vb = add_mod(vb, addb2[b * add_stride + drow2], pc.q);
+            u64 *A = acc + b * acc_stride + irow;
+            if (accumulate) {
+                vb = add_mod(vb, A[0], pc.q);
+                va = add_mod(va, A[n_all], pc.q);
+            }
+            A[0] = vb;
+            A[n_all] = va;
+        }
+    }
+}
+
+void keymult2(u64 *acc, const u64 *D1, const u64 *key1, u64 g1, const u64 *addb1, const u64 *D2, const u64 *key2,
+              u64 g2, const u64 *addb2, int nq, int K, int L, int beta, int keyP, bool accumulate, int logN,
+              int nbatch, size_t d_stride, size_t acc_stride, size_t add_stride, cudaStream_t s) {
+    if (beta != 4 || logN < 8 || nq + K > 65535)
+        throw std::invalid_argument("keymult2: four digits, N >= 256 and at most 65535 limb rows");
+    const double nd = (double)((size_t)(nq + K) << logN);
+    ProfScope ps(KC_KEYMULT, 8.0 * (nbatch * nd * (2.0 * beta + 2.0 + 2.0 * (accumulate ? 2.0 : 1.0)) + 4.0 * beta * nd),
+                 4.0 * beta * nbatch * nd, s, 1);
+    k_keymult_loop2<<<dim3(1u << (logN - 8), nq + K), 256, 0, s>>>(acc, D1, key1, g1, addb1, D2, key2, g2, addb2, nq,
+                                                                  K, L, keyP, accumulate ? 1 : 0, logN, nbatch,
+                                                                  d_stride, acc_stride, add_stride);
+    check_launch("keymult2");
+}
+
 void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,
              const u64 *addb, bool accumulate, int logN, int nbatch, size_t d_stride, size_t acc_stride,
              size_t add_stride, cudaStream_t s) {
