@@ -1214,47 +1214,58 @@ public:
             acc_stride = 2 * es;
         }
         u64 *aq = alloc((size_t)nb * nq * N);
-        u64 *D2 = alloc((size_t)nb * beta * es);
         std::vector<int> gslots;
         for (int s = 0; s < nslots; s++)
             if (t.giant_of_slot[s] != 0) gslots.push_back(s);
-        // four digits: giant steps in pairs, one key multiplication per pair
-        const bool pairs = beta == 4 && logN >= 8 && gslots.size() >= 2;
-        u64 *D2b = pairs ? alloc((size_t)nb * beta * es) : nullptr;
+        // four digits: the giant steps in groups of up to lt_group(), one key
+        // multiplication per group (the accumulator read and written once)
+        const int G = (beta == 4 && logN >= 8) ? std::max(1, std::min(lt_group(), (int)gslots.size())) : 1;
+        std::vector<u64 *> D2(G);
+        for (auto &d : D2) d = alloc((size_t)nb * beta * es);
         const size_t is = (size_t)nslots * 2 * es;
         for (size_t i = 0; i < gslots.size();) {
-            const int s1 = gslots[i];
-            const u64 gal1 = galois_of(t.giant_of_slot[s1] * t.bs);
-            moddown(aq, inner + (size_t)s1 * 2 * es + es, nq, nb, is, (size_t)nq * N);
-            modup(D2, aq, nq, nb, (size_t)nq * N);
-            if (pairs && i + 1 < gslots.size()) {
-                const int s2 = gslots[i + 1];
-                const u64 gal2 = galois_of(t.giant_of_slot[s2] * t.bs);
-                moddown(aq, inner + (size_t)s2 * 2 * es + es, nq, nb, is, (size_t)nq * N);
-                modup(D2b, aq, nq, nb, (size_t)nq * N);
-                keymult2(acc, D2, rot_keys.at(gal1), gal1, inner + (size_t)s1 * 2 * es, D2b, rot_keys.at(gal2), gal2,
-                         inner + (size_t)s2 * 2 * es, nq, K, L, beta, P, true, logN, nb, (size_t)beta * es,
-                         acc_stride, is, stream);
-                i += 2;
-            } else {
-                keymult(acc, D2, rot_keys.at(gal1), gal1, nq, K, L, beta, P, inner + (size_t)s1 * 2 * es, true, logN,
-                        nb, (size_t)beta * es, acc_stride, is, stream);
-                i += 1;
+            const int n = (int)std::min<size_t>(G, gslots.size() - i);
+            const u64 *Dp[HB_MAX_GIANTS], *kp[HB_MAX_GIANTS], *ap[HB_MAX_GIANTS];
+            u64 gp[HB_MAX_GIANTS];
+            for (int k = 0; k < n; k++) {
+                const int sl = gslots[i + k];
+                gp[k] = galois_of(t.giant_of_slot[sl] * t.bs);
+                kp[k] = rot_keys.at(gp[k]);
+                ap[k] = inner + (size_t)sl * 2 * es;
+                Dp[k] = D2[k];
+                moddown(aq, inner + (size_t)sl * 2 * es + es, nq, nb, is, (size_t)nq * N);
+                modup(D2[k], aq, nq, nb, (size_t)nq * N);
             }
+            if (n >= 2)
+                keymult_group(acc, n, Dp, kp, gp, ap, nq, K, L, beta, P, true, logN, nb, (size_t)beta * es, acc_stride,
+                              is, stream);
+            else
+                keymult(acc, D2[0], kp[0], gp[0], nq, K, L, beta, P, ap[0], true, logN, nb, (size_t)beta * es,
+                        acc_stride, is, stream);
+            i += n;
         }
         release(aq);
-        release(D2);
-        if (D2b) release(D2b);
+        for (auto *d : D2) release(d);
         moddown(out, acc, nq, nb, acc_stride, cts_);
         moddown(out + (size_t)nq * N, acc + es, nq, nb, acc_stride, cts_);
         release(inner);
         if (acc_own) release(acc_own);
     }
 
+    // giant steps per key multiplication in the LT (four digits)
+    static int lt_group() {
+#ifndef HB_LT_GIANT_GROUP
+#define HB_LT_GIANT_GROUP 3
+#endif
+        return HB_LT_GIANT_GROUP;
+    }
     size_t lt_bytes_per_ct(const LinTrans &t, int nq) {
         const int ne = nq + K, beta = beta_of(nq);
         const size_t es = (size_t)ne * N * 8;
-        return (size_t)t.groups.size() * 2 * es + 3 * beta * es + 2 * es + (size_t)6 * nq * N * 8;
+        // inner sums, the digits of the baby steps or of one giant group
+        // (and ModUp's temporaries), the accumulator, ModDown's temporaries
+        return (size_t)t.groups.size() * 2 * es + (size_t)(lt_group() + 2) * beta * es + 2 * es +
+               (size_t)6 * nq * N * 8;
     }
 
     void eval_lt_batch(int ltid, const std::vector<int> &ids, std::vector<int> &outs) {
@@ -1273,7 +1284,7 @@ public:
             const int nq = kv.first;
             const auto &idx = kv.second;
             size_t per = lt_bytes_per_ct(t, nq);
-            size_t budget = std::min<size_t>(free_b / 2, (size_t)48 << 30);
+            size_t budget = std::min<size_t>(free_b / 2, (size_t)64 << 30);
             int chunk = (int)std::max<size_t>(1, std::min<size_t>(idx.size(), budget / std::max<size_t>(per, 1)));
             const size_t cts_ = (size_t)2 * nq * N;
             for (size_t c0 = 0; c0 < idx.size(); c0 += chunk) {

@@ -1773,48 +1773,49 @@ __global__ void __launch_bounds__(256, HB_KEYMULT_LOOP_BLOCKS)
     }
 }
 
-// Two giant steps in one pass (four digits each): acc += KS(D1, key1) +
-// sigma_1(addb1) + KS(D2, key2) + sigma_2(addb2).  The accumulator is read
-// and written once for both, and the eight products of each output share
-// one reduction (split-29 sums hold up to 33 terms, 128-bit sums of eight
-// 120-bit products stay below 2^124).
-#ifndef HB_KEYMULT2_BLOCKS
-#define HB_KEYMULT2_BLOCKS 3
-#endif
-__global__ void __launch_bounds__(256, HB_KEYMULT2_BLOCKS)
-    k_keymult_loop2(u64 *__restrict__ acc, const u64 *__restrict__ D1, const u64 *__restrict__ key1, u64 g1,
-                    const u64 *__restrict__ addb1, const u64 *__restrict__ D2, const u64 *__restrict__ key2, u64 g2,
-                    const u64 *__restrict__ addb2, int nq, int K, int L, int keyP, int accumulate, int logN,
+// G giant steps in one pass (four digits each): acc += sum_i KS(D_i, key_i)
+// + sigma_i(addb_i).  The accumulator is read and written once for all G,
+// and the 8G products of each output share one reduction (split-29 sums
+// hold up to 33 terms; 128-bit sums of 8G 120-bit products stay below
+// 2^125 for G <= 4).  The key words of every giant stay in registers.
+struct GiantSet {
+    const u64 *D[HB_MAX_GIANTS], *key[HB_MAX_GIANTS], *addb[HB_MAX_GIANTS];
+    u64 g[HB_MAX_GIANTS];
+};
+template <int G>
+__global__ void __launch_bounds__(256, G <= 2 ? 3 : 2)
+    k_keymult_group(u64 *__restrict__ acc, GiantSet gs, int nq, int K, int L, int keyP, int accumulate, int logN,
                     int nbatch, size_t d_stride, size_t acc_stride, size_t add_stride) {
     constexpr int B = 4;
     const int ne = nq + K;
     const size_t n_all = (size_t)ne << logN;
     const int e = blockIdx.y;
     const unsigned t = blockIdx.x * 256u + threadIdx.x;
-    const unsigned src1 = g1 == 1 ? t : aut_index(t, g1, logN), src2 = g2 == 1 ? t : aut_index(t, g2, logN);
     const int p = e < nq ? e : L + (e - nq);
     const PrimeConst pc = c_pc[p];
     const size_t kofs = ((size_t)p << logN) + t, kstep = (size_t)keyP << logN;
-    const size_t erow = (size_t)e << logN, drow1 = erow + src1, drow2 = erow + src2, irow = erow + t;
-    if (pc.q < (1ull << 40)) {
-        unsigned kl[2][2][B], kh[2][2][B], ks[2][2][B];  // [giant][b/a][digit]
+    const size_t erow = (size_t)e << logN, irow = erow + t;
+    size_t drow[G];
 #pragma unroll
-        for (int gi = 0; gi < 2; gi++) {
-            const u64 *kp = (gi ? key2 : key1) + kofs;
+    for (int gi = 0; gi < G; gi++) drow[gi] = erow + (gs.g[gi] == 1 ? t : aut_index(t, gs.g[gi], logN));
+    if (pc.q < (1ull << 40)) {
+        unsigned kl[G][2][B], kh[G][2][B], ks[G][2][B];  // [giant][b/a][digit]
+#pragma unroll
+        for (int gi = 0; gi < G; gi++)
 #pragma unroll
             for (int j = 0; j < B; j++)
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
-                    const u64 k = k29_pack(kp[(2 * j + c) * kstep]);
+                    const u64 k = k29_pack(gs.key[gi][kofs + (2 * j + c) * kstep]);
                     kl[gi][c][j] = (unsigned)k, kh[gi][c][j] = (unsigned)(k >> 32);
                     ks[gi][c][j] = kl[gi][c][j] + kh[gi][c][j];
                 }
-        }
         for (int b = 0; b < nbatch; b++) {
             Kara29 sb = {0, 0, 0}, sa = {0, 0, 0};
+            u64 vb = 0;
 #pragma unroll
-            for (int gi = 0; gi < 2; gi++) {
-                const u64 *dp = (gi ? D2 : D1) + b * d_stride + (gi ? drow2 : drow1);
+            for (int gi = 0; gi < G; gi++) {
+                const u64 *dp = gs.D[gi] + b * d_stride + drow[gi];
                 u64 dv[B];
 #pragma unroll
                 for (int j = 0; j < B; j++) dv[j] = dp[j * n_all];
@@ -1825,10 +1826,10 @@ __global__ void __launch_bounds__(256, HB_KEYMULT2_BLOCKS)
                     k29_mac_s(sb, kl[gi][0][j], kh[gi][0][j], ks[gi][0][j], dl, dh, ds);
                     k29_mac_s(sa, kl[gi][1][j], kh[gi][1][j], ks[gi][1][j], dl, dh, ds);
                 }
+                vb = add_mod(vb, gs.addb[gi][b * add_stride + drow[gi]], pc.q);
             }
-            u64 vb = k29_reduce(sb, pc), va = k29_reduce(sa, pc);
-            vb = add_mod(vb, addb1[b * add_stride + drow1], pc.q);
-            vb = add_mod(vb, addb2[b * add_stride + drow2], pc.q);
+            vb = add_mod(vb, k29_reduce(sb, pc), pc.q);
+            u64 va = k29_reduce(sa, pc);
             u64 *A = acc + b * acc_stride + irow;
             if (accumulate) {
                 vb = add_mod(vb, A[0], pc.q);
@@ -1838,30 +1839,23 @@ __global__ void __launch_bounds__(256, HB_KEYMULT2_BLOCKS)
             A[n_all] = va;
         }
     } else {
-        u64 kv[2][2][B];
-#pragma unroll
-        for (int gi = 0; gi < 2; gi++) {
-            const u64 *kp = (gi ? key2 : key1) + kofs;
-#pragma unroll
-            for (int j = 0; j < B; j++)
-#pragma unroll
-                for (int c = 0; c < 2; c++) kv[gi][c][j] = kp[(2 * j + c) * kstep];
-        }
         for (int b = 0; b < nbatch; b++) {
             u128 sb = {0, 0}, sa = {0, 0};
+            u64 vb = 0;
 #pragma unroll
-            for (int gi = 0; gi < 2; gi++) {
-                const u64 *dp = (gi ? D2 : D1) + b * d_stride + (gi ? drow2 : drow1);
+            for (int gi = 0; gi < G; gi++) {
+                const u64 *dp = gs.D[gi] + b * d_stride + drow[gi];
+                const u64 *kp = gs.key[gi] + kofs;
 #pragma unroll
                 for (int j = 0; j < B; j++) {
                     const u64 d = dp[j * n_all];
-                    mac128(sb, d, kv[gi][0][j]);
-                    mac128(sa, d, kv[gi][1][j]);
+                    mac128(sb, d, kp[(2 * j) * kstep]);
+                    mac128(sa, d, kp[(2 * j + 1) * kstep]);
                 }
+                vb = add_mod(vb, gs.addb[gi][b * add_stride + drow[gi]], pc.q);
             }
-            u64 vb = reduce128(sb, pc), va = reduce128(sa, pc);
-            vb = add_mod(vb, addb1[b * add_stride + drow1], pc.q);
-            vb = add_mod(vb, addb2[b * add_stride + drow2], pc.q);
+            vb = add_mod(vb, reduce128(sb, pc), pc.q);
+            u64 va = reduce128(sa, pc);
             u64 *A = acc + b * acc_stride + irow;
             if (accumulate) {
                 vb = add_mod(vb, A[0], pc.q);
@@ -1873,18 +1867,30 @@ __global__ void __launch_bounds__(256, HB_KEYMULT2_BLOCKS)
     }
 }
 
-void keymult2(u64 *acc, const u64 *D1, const u64 *key1, u64 g1, const u64 *addb1, const u64 *D2, const u64 *key2,
-              u64 g2, const u64 *addb2, int nq, int K, int L, int beta, int keyP, bool accumulate, int logN,
-              int nbatch, size_t d_stride, size_t acc_stride, size_t add_stride, cudaStream_t s) {
-    if (beta != 4 || logN < 8 || nq + K > 65535)
-        throw std::invalid_argument("keymult2: four digits, N >= 256 and at most 65535 limb rows");
+void keymult_group(u64 *acc, int ngiants, const u64 *const *D, const u64 *const *keys, const u64 *galois,
+                   const u64 *const *addb, int nq, int K, int L, int beta, int keyP, bool accumulate, int logN,
+                   int nbatch, size_t d_stride, size_t acc_stride, size_t add_stride, cudaStream_t s) {
+    if (beta != 4 || logN < 8 || nq + K > 65535 || ngiants < 2 || ngiants > HB_MAX_GIANTS)
+        throw std::invalid_argument("keymult_group: four digits, 2..HB_MAX_GIANTS giants, N >= 256");
+    GiantSet gs{};
+    for (int i = 0; i < ngiants; i++) {
+        gs.D[i] = D[i];
+        gs.key[i] = keys[i];
+        gs.addb[i] = addb[i];
+        gs.g[i] = galois[i];
+    }
     const double nd = (double)((size_t)(nq + K) << logN);
-    ProfScope ps(KC_KEYMULT, 8.0 * (nbatch * nd * (2.0 * beta + 2.0 + 2.0 * (accumulate ? 2.0 : 1.0)) + 4.0 * beta * nd),
-                 4.0 * beta * nbatch * nd, s, 1);
-    k_keymult_loop2<<<dim3(1u << (logN - 8), nq + K), 256, 0, s>>>(acc, D1, key1, g1, addb1, D2, key2, g2, addb2, nq,
-                                                                  K, L, keyP, accumulate ? 1 : 0, logN, nbatch,
-                                                                  d_stride, acc_stride, add_stride);
-    check_launch("keymult2");
+    ProfScope ps(KC_KEYMULT,
+                 8.0 * (nbatch * nd * (ngiants * (beta + 1.0) + (accumulate ? 4.0 : 2.0)) + 2.0 * ngiants * beta * nd),
+                 2.0 * ngiants * beta * nbatch * nd, s, 1);
+    const dim3 grid(1u << (logN - 8), nq + K);
+    const int acc_i = accumulate ? 1 : 0;
+    switch (ngiants) {
+        case 2: k_keymult_group<2><<<grid, 256, 0, s>>>(acc, gs, nq, K, L, keyP, acc_i, logN, nbatch, d_stride, acc_stride, add_stride); break;
+        case 3: k_keymult_group<3><<<grid, 256, 0, s>>>(acc, gs, nq, K, L, keyP, acc_i, logN, nbatch, d_stride, acc_stride, add_stride); break;
+        default: k_keymult_group<4><<<grid, 256, 0, s>>>(acc, gs, nq, K, L, keyP, acc_i, logN, nbatch, d_stride, acc_stride, add_stride); break;
+    }
+    check_launch("keymult_group");
 }
 
 void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,

@@ -184,10 +184,12 @@ void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in,
 void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, int L, int beta, int keyP,
              const u64 *addb, bool accumulate, int logN, int nbatch, size_t d_stride, size_t acc_stride,
              size_t add_stride, cudaStream_t s);
-// two giant steps of four digits each in one pass (both addends required)
-void keymult2(u64 *acc, const u64 *D1, const u64 *key1, u64 g1, const u64 *addb1, const u64 *D2, const u64 *key2,
-              u64 g2, const u64 *addb2, int nq, int K, int L, int beta, int keyP, bool accumulate, int logN,
-              int nbatch, size_t d_stride, size_t acc_stride, size_t add_stride, cudaStream_t s);
+// 2..HB_MAX_GIANTS giant steps of four digits each in one pass (every
+// giant with its digits, key, Galois element and unrotated addend)
+#define HB_MAX_GIANTS 4
+void keymult_group(u64 *acc, int ngiants, const u64 *const *D, const u64 *const *keys, const u64 *galois,
+                   const u64 *const *addb, int nq, int K, int L, int beta, int keyP, bool accumulate, int logN,
+                   int nbatch, size_t d_stride, size_t acc_stride, size_t add_stride, cudaStream_t s);
 
 // ---- fused double-hoisted baby steps + plaintext MAC --------------------------
 #define HB_MAX_BETA 8  // key-switching digits handled by the fused kernels
