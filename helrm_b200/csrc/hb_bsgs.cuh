@@ -10,11 +10,13 @@
 // The thread block keeps the evaluation-key tiles of its babies in shared
 // memory and each thread its plaintext values in registers, so keys and
 // diagonals stream from HBM once per batch while the ciphertext data
-// (digits D, c0, inner sums) streams once per ciphertext.  Residues below
-// 2^40 (the 36-bit q limbs) multiply in the Karatsuba split-29 form, two
-// 32x32->64 and one 32-bit multiply-add per product; the 60-bit
-// special-prime limbs use 64x64->128 products.  Accumulation is lazy: one
-// modular reduction per output.
+// (digits D, c0, inner sums) streams once per ciphertext.  On residues
+// below 2^40 (the 36-bit q limbs) phase A runs on the FP64 pipe (exact
+// centred products key * digit, summed exactly) and phase B on the integer
+// pipe in the Karatsuba split-29 form (two 32x32->64 and one 32-bit
+// multiply-add per product), so the two phases use different pipes; the
+// 60-bit special-prime limbs use 64x64->128 products.  Accumulation is
+// lazy: one modular reduction per output.
 // Included by hb_kernels.cu (it reads the per-prime __constant__ table).
 #pragma once
 

@@ -1616,7 +1616,9 @@ void rescale_combine(u64 *out, const u64 *c, const u64 *W, int npoly, int nq_in,
 // ciphertext index fastest: the blocks that read the same key segment run
 // back to back, so each key segment comes from DRAM once per launch and from
 // L2 for the other ciphertexts.  Limbs below 2^40 use Karatsuba split-29
-// products, the others 128-bit products.
+// products, the others 128-bit products.  This form serves digit counts
+// other than four; four digits run the batch-looping forms below
+// (k_keymult_loop for one giant step, k_keymult_group for several).
 #ifndef HB_KEYMULT_BLOCKS
 #define HB_KEYMULT_BLOCKS 6  // resident blocks per SM (occupancy hides the gathers' latency)
 #endif
