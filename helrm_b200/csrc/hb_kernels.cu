@@ -1467,30 +1467,43 @@ __global__ void __launch_bounds__(256)
     for (int i = threadIdx.x; i < KK * nq; i += blockDim.x) st[i] = tab.phat_s[i];
     for (int i = threadIdx.x; i < nq; i += blockDim.x) st[KK * nq + i] = tab.pneg_s[i];
     __syncthreads();
+    // two coefficients per thread, 256 apart (N is a multiple of 512): every
+    // table value and loop step serves two outputs; stores stay coalesced
     const int N = 1 << logN;
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= N) return;
+    const int n0 = blockIdx.x * 512 + threadIdx.x;
     const int b = blockIdx.y;
     const u64 *Yb = Y + b * in_stride;
     u64 *Zb = Z + b * out_stride;
-    u64 y[KK];
-    unsigned nneg = 0;
+    u64 y[2][KK];
+    unsigned nneg[2] = {0, 0};
 #pragma unroll
     for (int k = 0; k < KK; k++) {
         const u64 pk = c_pc[L + k].q;
-        const u64 v = mul_shoup(Yb[(size_t)k * N + n], tab.phinv[k], tab.phinvp[k], pk);
-        nneg += v > (pk >> 1);
-        y[k] = split_pack(v);
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const u64 v = mul_shoup(Yb[(size_t)k * N + n0 + 256 * c], tab.phinv[k], tab.phinvp[k], pk);
+            nneg[c] += v > (pk >> 1);
+            y[c][k] = split_pack(v);
+        }
     }
     for (int i = 0; i < nq; i++) {
-        SplitW acc = {0, 0, 0};
+        SplitW a0 = {0, 0, 0}, a1 = {0, 0, 0};
 #pragma unroll
         for (int k = 0; k < KK; k++) {
-            splitw_mac(acc, st[k * nq + i], y[k]);
-            if ((k & 3) == 3 && k + 1 < KK) splitw_normalize(acc);
+            const u64 tv = st[k * nq + i];
+            splitw_mac(a0, tv, y[0][k]);
+            splitw_mac(a1, tv, y[1][k]);
+            if ((k & 3) == 3 && k + 1 < KK) {
+                splitw_normalize(a0);
+                splitw_normalize(a1);
+            }
         }
-        splitw_mac_small(acc, nneg, st[KK * nq + i]);
-        Zb[(size_t)i * N + n] = splitw_reduce(acc, c_pc[i]);
+        const u64 tn = st[KK * nq + i];
+        splitw_mac_small(a0, nneg[0], tn);
+        splitw_mac_small(a1, nneg[1], tn);
+        const PrimeConst &pc = c_pc[i];
+        Zb[(size_t)i * N + n0] = splitw_reduce(a0, pc);
+        Zb[(size_t)i * N + n0 + 256] = splitw_reduce(a1, pc);
     }
 }
 
@@ -1500,13 +1513,14 @@ void moddown_bconv(u64 *Z, const u64 *Y, int nq, int K, int L, const ModDownTab 
     if (nq > HB_MAX_PRIMES) throw std::invalid_argument("moddown_bconv: too many primes");
     const int N = 1 << logN;
     dim3 grid((N + 255) / 256, nbatch);
+    const dim3 grid2(N / 512, nbatch);  // the split kernel: two coefficients per thread
     ProfScope ps(KC_MODDOWN_BCONV, 8.0 * nbatch * (double)N * (K + nq), (double)nbatch * N * (K + (double)K * nq), s,
                  1);
-    if (tab.split) {
+    if (tab.split && N >= 512) {
         switch (K) {
 #define HB_MD_CASE(A)                                                                                             \
     case A:                                                                                                        \
-        k_moddown_bconv_split<A><<<grid, 256, 0, s>>>(Z, Y, nq, L, tab, logN, in_stride, out_stride);              \
+        k_moddown_bconv_split<A><<<grid2, 256, 0, s>>>(Z, Y, nq, L, tab, logN, in_stride, out_stride);             \
         break;
             HB_MD_CASE(1) HB_MD_CASE(2) HB_MD_CASE(3) HB_MD_CASE(4) HB_MD_CASE(5) HB_MD_CASE(6) HB_MD_CASE(7)
             HB_MD_CASE(8)
