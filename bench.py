@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--level", type=int, default=23, help="PCMM input level (23 = all 24 limbs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cfg3", action="store_true", help="skip the config-3 primitive microbenchmark")
     ap.add_argument("--cpu-threads", type=int, default=0, help="oracle threads (0 = all host cores)")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: same 512-diagonal PCMM on 8 q limbs + 2 special primes (dnum 4, "
@@ -129,8 +130,6 @@ class ClockSampler:
         except Exception:
             sel = str(device_index)
         self.sel = sel
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_r{device_index}.csv") \
-            if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else None
 
     def start(self):
         """Start sampling and wait for the first sample: nvidia-smi's start-up
@@ -154,11 +153,8 @@ class ClockSampler:
         time.sleep(0.25)
         self.proc.terminate()
         out, _ = self.proc.communicate(timeout=10)
-        # the first sample precedes the timed region: kept in the file only
+        # the first sample (read in start()) precedes the timed region
         rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
-        if self.path:
-            with open(self.path, "w") as f:
-                f.write(self.first + out)
         sm = [float(r[0]) for r in rows if len(r) >= 8 and r[0].replace(".", "").isdigit()]
         mx = [float(r[1]) for r in rows if len(r) >= 8 and r[1].replace(".", "").isdigit()]
         pw = [float(r[2]) for r in rows if len(r) >= 8 and r[2].replace(".", "").isdigit()]
@@ -202,46 +198,49 @@ def ncu_traffic(kernel: str):
 
 
 # --------------------------------------------------------------------------- CPU baseline (oracle)
-def cpu_pcmm_seconds(ks, diags, rot, x, level, threads, reps=1):
-    """The same PCMM for one ciphertext on the CPU restatement (oracle/),
-    with `threads` host threads.  Returns (seconds per ciphertext, setup s)."""
+def oracle_for_cfg2():
     from oracle import oracle as om
-    from helrm_b200 import workload as W
     from helrm_b200.params import CFG2, CFG2_DNUM
-    from concurrent.futures import ThreadPoolExecutor
-    t0 = time.time()
     main, aux = om.scheme_primes(CFG2.logq, CFG2.logp, CFG2.logn)
-    o = om.Oracle(CFG2.logn, main, aux, CFG2_DNUM)
+    return om, om.Oracle(CFG2.logn, main, aux, CFG2_DNUM)
+
+
+def cpu_operands_own(o, om, ks, diags, rot, x, level, threads, seed=4242):
+    """Keys, extended-basis diagonals and one ciphertext for the oracle,
+    made on the CPU from its own seed (the reference arm has no GPU)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from helrm_b200 import workload as W
+    from helrm_b200.params import CFG2
     plan = W.bsgs_plan(ks, 2.0, o.N // 2)
     nq = level + 1
     scale = float(1 << CFG2.logscale)
-    # untimed setup: one task per diagonal / key, each single-threaded inside
-    # the oracle (ctypes releases the GIL, so the pool runs them in parallel)
+    # one task per diagonal / key, each single-threaded inside the oracle
+    # (ctypes releases the GIL, so the pool runs them in parallel)
     om.set_threads(1)
-    sk = o.secret_ntt(o.sample_secret(4242, CFG2.h))
+    sk = o.secret_ntt(o.sample_secret(seed, CFG2.h))
     gal = sorted({o.galois(dd) for dd in plan["rotation_keys"]} |
                  {o.galois((o.N // 2) >> i) for i in range(1, rot + 1)})
     with ThreadPoolExecutor(max_workers=threads) as ex:
         pts = list(ex.map(lambda k: o.encode(W.preroll(diags[k], k // plan["stride"], plan["stride"]), nq, scale,
                                              ext=True), ks))
-        keys = dict(zip(gal, ex.map(lambda g: o.rotation_key(sk, 4242, g), gal)))
-    om.set_threads(threads)
+        keys = dict(zip(gal, ex.map(lambda g: o.rotation_key(sk, seed, g), gal)))
     v = np.zeros(o.N // 2)
     v[:len(x)] = x
     ct = o.encrypt(sk, o.encode(v, nq, scale), 7)
-    setup = time.time() - t0
-    times = []
+    return ct, pts, plan["stride"], keys
+
+
+def cpu_pcmm_times(o, om, ct, ks, pts, stride, keys, rot, threads, reps=1):
+    """The same PCMM step (LT + rescale + fold) for one ciphertext on the
+    oracle with `threads` host threads: (per-rep seconds, last output)."""
+    om.set_threads(threads)
+    times, out = [], None
     for _ in range(reps):
         t1 = time.time()
-        out = o.rescale(o.bsgs_lt(ct, ks, pts, plan["stride"], keys))
-        for i in range(1, rot + 1):
-            g = o.galois((o.N // 2) >> i)
-            r = o.rotate(out, keys[g], g)
-            qs = np.array(o.primes[:out.shape[1]], dtype=np.uint64)[None, :, None]
-            s = out + r  # residues < 2^60, no uint64 overflow
-            out = np.where(s >= qs, s - qs, s)
+        out = o.pcmm(ct, ks, pts, stride, keys, rot)
         times.append(time.time() - t1)
-    return min(times), setup, times
+    om.set_threads(1)
+    return times, out
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -254,9 +253,11 @@ def run_reference(args, dist):
         return
     threads = args.cpu_threads or os.cpu_count() or 1
     M, ks, diags, rot, xs = build_workload(1, seed=100)
-    # one oracle setup (keys, diagonals; untimed), then warmup + timed steps
-    _, setup, times_all = cpu_pcmm_seconds(ks, diags, rot, xs[0], args.level, threads,
-                                           reps=args.warmup + args.steps)
+    om, o = oracle_for_cfg2()
+    t0 = time.time()
+    ct, pts, stride, keys = cpu_operands_own(o, om, ks, diags, rot, xs[0], args.level, threads)
+    setup = time.time() - t0
+    times_all, _ = cpu_pcmm_times(o, om, ct, ks, pts, stride, keys, rot, threads, reps=args.warmup + args.steps)
     times = times_all[args.warmup:]
     ms = 1000.0 * sum(times) / len(times)
     value = 1000.0 / ms
@@ -288,13 +289,38 @@ def cfg_dict(args, batch):
 
 
 # --------------------------------------------------------------------------- B200 arm
+REL_TOL = 2.0 ** -15   # north_star: decrypted embedding slots within 2^-15 relative
+
+
+def read_profile(capi, _capi, steps):
+    """per-kernel-class statistics of the library's CUDA-event profiler"""
+    K = 16
+    pms, pby, pwk = (ctypes.c_double * K)(), (ctypes.c_double * K)(), (ctypes.c_double * K)()
+    pl = (ctypes.c_uint64 * K)()
+    ncls = ctypes.c_int(0)
+    _capi.check(capi.helrm_ProfileRead(pms, pby, pwk, pl, K, ctypes.byref(ncls)))
+    buf = ctypes.create_string_buffer(64)
+    raw = {}
+    for i in range(ncls.value):
+        capi.helrm_KernelClassName(i, buf, 64)
+        if pl[i]:
+            raw[buf.value.decode()] = (pms[i], pby[i], pwk[i], pl[i])
+    kern = {}
+    for nm, (ms_, by, wk, n) in raw.items():
+        kern[nm] = {"ms_per_step": ms_ / steps, "launches_per_step": n / steps, "share": None,
+                    "GBps": by / (ms_ * 1e6) if ms_ else None, "Gops": wk / (ms_ * 1e6) if ms_ else None}
+    tot = sum(v["ms_per_step"] for v in kern.values()) or 1.0
+    for v in kern.values():
+        v["share"] = v["ms_per_step"] / tot
+    return kern, raw
+
+
 def run_b200(args, dist):
     import torch
 
-    from helrm_b200 import B200Library, _capi
+    from helrm_b200 import B200Library, CKKSConfig, _capi
     from helrm_b200.params import CFG2, CFG2_DNUM
 
-    from helrm_b200 import CKKSConfig
     dev = dist.local
     torch.cuda.set_device(dev)
     if args.small:
@@ -314,94 +340,114 @@ def run_b200(args, dist):
     for i in range(1, rot + 1):
         lib.AddRotationKey(slots >> i)
     scale = float(1 << CFG2.logscale)
-    cts = []
-    for x in xs:
-        v = np.zeros(slots)
-        v[:len(x)] = x
-        pt = lib.Encode(list(v), args.level, scale)
-        cts.append(lib.Encrypt(pt))
-        lib.DeletePlaintext(pt)
+
+    def encrypt_batch(level):
+        out = []
+        for x in xs:
+            v = np.zeros(slots)
+            v[:len(x)] = x
+            pt = lib.Encode(list(v), level, scale)
+            out.append(lib.Encrypt(pt))
+            lib.DeletePlaintext(pt)
+        return out
+
+    cts = encrypt_batch(args.level)
     capi = _capi.load()
 
-    def step(ids):
-        outs = lib.EvaluateLinearTransformBatch(lt, ids)
+    def step(ids, t=lt):
+        outs = lib.EvaluateLinearTransformBatch(t, ids)
         lib.RescaleBatch(outs)
         lib.HybridFoldBatch(outs, rot)
         return outs
 
-    # correctness spot check outside the timed region: first ciphertext
+    # correctness spot check outside the timed region: first ciphertext,
+    # decrypted embedding slots against the cleartext product (relative
+    # to the largest magnitude), residues kept for the CPU leg's comparison
     o = step(cts[:1])[0]
+    gpu_out0 = lib.GetCiphertextData(o)
     got = np.array(lib.Decode(lib.Decrypt(o)))[:416]
     ref = M.astype(np.float64) @ xs[0]
     max_err = float(np.abs(got - ref).max())
+    rel_err = max_err / float(np.abs(ref).max())
+    correct = bool(rel_err <= REL_TOL)
     lib.DeleteCiphertext(o)
 
+    def timed_steps(nsteps, ids, t=lt, profile=False):
+        """nsteps steps on the library stream between CUDA events; returns
+        (device ms, launches of this library in the region)"""
+        lib.Synchronize()
+        torch.cuda.synchronize()
+        if profile:
+            _capi.check(capi.helrm_ProfileEnable(1))
+        n0 = ctypes.c_uint64(0)
+        _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n0)))
+        _capi.check(capi.helrm_TimerStart())
+        for _ in range(nsteps):
+            for oo in step(ids, t):
+                lib.DeleteCiphertext(oo)
+        ms = ctypes.c_double(0)
+        _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+        n1 = ctypes.c_uint64(0)
+        _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n1)))
+        return ms.value, int(n1.value - n0.value)
+
     for _ in range(args.warmup):
-        for o in step(cts):
-            lib.DeleteCiphertext(o)
+        for oo in step(cts):
+            lib.DeleteCiphertext(oo)
     lib.Synchronize()
     torch.cuda.synchronize()
 
-    # ---- device-resident timed region
+    # ---- device-resident timed region (per-kernel profiling off)
     clocks = ClockSampler(dev)
     dist.barrier()
     torch.cuda.synchronize()
     lib.Synchronize()
     clocks.start()
-    _capi.check(capi.helrm_ProfilerRange(1))
-    # per-kernel CUDA events on the library stream, over the timed region
-    _capi.check(capi.helrm_ProfileEnable(1))
-    n0 = ctypes.c_uint64(0)
-    _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n0)))
-    _capi.check(capi.helrm_TimerStart())
-    for _ in range(args.steps):
-        for o in step(cts):
-            lib.DeleteCiphertext(o)
-    ms = ctypes.c_double(0)
-    _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
-    n1 = ctypes.c_uint64(0)
-    _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n1)))
-    K = 16
-    pms, pby, pwk = (ctypes.c_double * K)(), (ctypes.c_double * K)(), (ctypes.c_double * K)()
-    pl = (ctypes.c_uint64 * K)()
-    ncls = ctypes.c_int(0)
-    _capi.check(capi.helrm_ProfileRead(pms, pby, pwk, pl, K, ctypes.byref(ncls)))
-    _capi.check(capi.helrm_ProfileEnable(0))
-    _capi.check(capi.helrm_ProfilerRange(0))
+    ms_dev, launches = timed_steps(args.steps, cts)
     clk = clocks.stop()
     torch.cuda.synchronize()
     dist.barrier()
-    t_dev = dist.max(ms.value / 1000.0)
+    t_dev = dist.max(ms_dev / 1000.0)
     value = whole_job_rate(dist.world, args.batch, args.steps, t_dev)
     ms_step = 1000.0 * t_dev / args.steps
-    prof_steps = args.steps
 
-    names = []
-    buf = ctypes.create_string_buffer(64)
-    for i in range(ncls.value):
-        capi.helrm_KernelClassName(i, buf, 64)
-        names.append(buf.value.decode())
-    kern = {}
-    for i, nm in enumerate(names):
-        if pl[i] == 0:
-            continue
-        kern[nm] = {"ms_per_step": pms[i] / prof_steps, "launches_per_step": pl[i] / prof_steps,
-                    "share": None, "GBps": pby[i] / (pms[i] * 1e6) if pms[i] else None,
-                    "Gops": pwk[i] / (pms[i] * 1e6) if pms[i] else None}
-    tot = sum(v["ms_per_step"] for v in kern.values()) or 1.0
-    for v in kern.values():
-        v["share"] = v["ms_per_step"] / tot
+    # ---- a second pass over the same steps with per-kernel CUDA events on
+    # the library stream: the kernel breakdown and the roofline's kernel
+    # duration (the events add a little time, so this pass is not the headline)
+    prof_steps = max(1, min(args.steps, 5))
+    _capi.check(capi.helrm_ProfilerRange(1))
+    ms_prof, _ = timed_steps(prof_steps, cts, profile=True)
+    kern, raw = read_profile(capi, _capi, prof_steps)
+    _capi.check(capi.helrm_ProfileEnable(0))
+    _capi.check(capi.helrm_ProfilerRange(0))
     dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
-    di = names.index(dom)
+    dms, dby, _, dl = raw[dom]
     hbm, src = peaks()
-    achieved = pby[di] / (pms[di] * 1e6)
+    achieved = dby / (dms * 1e6)
     roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured"
-                else "fallback 6.65 TB/s", "bytes_per_launch": pby[di] / pl[di],
-                "avg_launch_ms": pms[di] / pl[di],
-                "traffic": ncu_traffic(dom)}
-    ksi = names.index("keymult")
-    keyswitch_gbps = pby[ksi] / (pms[ksi] * 1e6) if pl[ksi] else None
+                else "fallback 6.65 TB/s", "bytes_per_launch": dby / dl, "avg_launch_ms": dms / dl,
+                "traffic": ncu_traffic(dom), "profiled_steps": prof_steps,
+                "profiled_ms_per_step": ms_prof / prof_steps}
+    keymult = kern.get("keymult", {}).get("GBps")
+
+    # ---- secondary line (NOT the headline): the same PCMM with the selector
+    # at level 4, where the reference's HE-LRM compiler places the embedding
+    # input (examples/criteo/table2.py:212, examples/criteo/network.py:209-211)
+    low = None
+    if not args.small and args.level > 4 and dist.world == 1:
+        lt4 = lib.GenerateLinearTransform(ks, data, 4, 2.0, "none")
+        cts4 = encrypt_batch(4)
+        for _ in range(args.warmup):
+            for oo in step(cts4, lt4):
+                lib.DeleteCiphertext(oo)
+        ms4, _ = timed_steps(args.steps, cts4, lt4)
+        low = {"note": "not the headline: selector at level 4 (5 q limbs), the reference's placement",
+               "pcmm_level": 4, "ms_per_step": ms4 / args.steps,
+               "value": args.batch * args.steps / (ms4 / 1000.0), "unit": UNIT}
+        for c in cts4:
+            lib.DeleteCiphertext(c)
+        lib.DeleteLinearTransform(lt4)
 
     # ---- end to end through the C ABI with host buffers
     e2e = None
@@ -412,7 +458,6 @@ def run_b200(args, dist):
         hout = torch.empty((args.batch, words_out), dtype=torch.int64, pin_memory=True)
         for i, c in enumerate(cts):
             hin[i].copy_(torch.from_numpy(lib.GetCiphertextData(c).reshape(-1).view(np.int64)))
-        u64p = ctypes.POINTER(ctypes.c_uint64)
 
         # pinned host buffers; uploads and read-backs go through the library's
         # transfer streams, so step i+1's upload and step i's read-back overlap
@@ -442,24 +487,66 @@ def run_b200(args, dist):
         _capi.check(capi.helrm_TransferSync())
         ms2 = ctypes.c_double(0)
         _capi.check(capi.helrm_TimerStop(ctypes.byref(ms2)))
-        # the read-back holds the last step's results
-        if not hout[args.batch - 1].any():
-            raise RuntimeError("e2e read-back is empty")
+        # the read-back holds the last step's results: the first one must be
+        # the spot-checked ciphertext's output, residue for residue
+        back0 = hout[0].numpy().view(np.uint64).reshape(gpu_out0.shape)
+        e2e_match = bool(np.array_equal(back0, gpu_out0))
         t_e2e = dist.max(ms2.value / 1000.0)
         e2e = {"value": whole_job_rate(dist.world, args.batch, args.steps, t_e2e), "unit": UNIT,
                "h2d_bytes_per_step": args.batch * words_in * 8, "d2h_bytes_per_step": args.batch * words_out * 8,
-               "ms_per_step": 1000.0 * t_e2e / args.steps}
+               "ms_per_step": 1000.0 * t_e2e / args.steps, "readback_matches_device_output": e2e_match}
+        correct = correct and e2e_match
 
+    # ---- CPU baseline: the oracle on the same ciphertext, diagonals and
+    # switching keys as the GPU run (fetched from the library), at all host
+    # cores and at one thread; its output residues must equal the GPU's
     cpu = None
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+    residues_match = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and not args.small:
         threads = args.cpu_threads or os.cpu_count() or 1
         try:
-            s, setup, _ = cpu_pcmm_seconds(ks, diags, rot, xs[0], args.level, threads)
-            cpu = {"value": 1.0 / s, "unit": UNIT, "cores": threads, "kind": "port",
+            from helrm_b200 import workload as W
+            om, o = oracle_for_cfg2()
+            t0 = time.time()
+            plan = W.bsgs_plan(ks, 2.0, slots)
+            gal = sorted({o.galois(d) for d in plan["rotation_keys"]} |
+                         {o.galois(slots >> i) for i in range(1, rot + 1)})
+            keys = {g: lib.GetKeyData(g) for g in gal}
+            pts = [lib.GetLinearTransformPlaintext(lt, k) for k in ks]
+            ct0 = lib.GetCiphertextData(cts[0])
+            setup = time.time() - t0
+            tall, out_all = cpu_pcmm_times(o, om, ct0, ks, pts, plan["stride"], keys, rot, threads)
+            residues_match = bool(np.array_equal(out_all, gpu_out0))
+            t1, out_1 = cpu_pcmm_times(o, om, ct0, ks, pts, plan["stride"], keys, rot, 1)
+            residues_match = residues_match and bool(np.array_equal(out_1, gpu_out0))
+            cpu = {"value": 1.0 / tall[0], "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"1 ciphertext of the same PCMM (LT + rescale + {rot} fold rotations) on the oracle "
-                             f"port, {threads} threads, {s:.2f} s (setup {setup:.1f} s untimed)"}
+                             f"port with the GPU run's ciphertext, diagonals and keys: {tall[0]:.2f} s on "
+                             f"{threads} threads, {t1[0]:.2f} s on 1 thread (operand fetch {setup:.1f} s untimed)",
+                   "nproc": os.cpu_count(), "single_thread": {"value": 1.0 / t1[0], "unit": UNIT, "cores": 1,
+                                                              "seconds": t1[0]},
+                   "residues_match": residues_match,
+                   "lattigo": go_probe()}
+            del keys, pts
+            correct = correct and residues_match
         except Exception as ex:  # the baseline must not sink the GPU line
             cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "port", "sample": f"failed: {ex}"}
+
+    lib.DeleteScheme()
+
+    # ---- config 3 (primitive microbenchmark), its own scheme; the
+    # key-switch figure is the whole hoisted key switch (ModUp + KeyMult +
+    # ModDown, NTTs included) over 32 rotations at batch 16
+    cfg3 = None
+    keyswitch = None
+    if dist.world == 1 and not args.small and not args.no_cfg3:
+        from helrm_b200 import microbench
+        cfg3 = microbench.run(batches=(1, 16, 128), reps=3, device=dev)
+        for r in cfg3:
+            if r["op"] == "hoisted_keyswitch_R32" and r["batch"] == 16:
+                keyswitch = {"GBps": r["GBps"], "frac_hbm": r["frac_hbm"], "batch": 16, "rotations": 32,
+                             "ms": r["ms"], "what": "whole hoisted key switch (ModUp + KeyMult + ModDown, NTTs "
+                                                    "included), SURVEY 8(d) algorithmic bytes"}
 
     if dist.rank == 0:
         line = {
@@ -467,13 +554,32 @@ def run_b200(args, dist):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u64", "data": "synthetic (seeded Criteo-shaped queries; dataset absent)",
             "config": cfg_dict(args, args.batch),
-            "pcmm_ms_per_batch": ms_step, "keyswitch_GBps": keyswitch_gbps,
+            "pcmm_ms_per_batch": ms_step, "keyswitch_GBps": keyswitch["GBps"] if keyswitch else None,
+            "keyswitch": keyswitch, "keymult_GBps": keymult,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": int(n1.value - n0.value), "clocks": clk, "kernels": kern,
-            "max_abs_err_embedding": max_err,
+            "gpu_launches": launches, "clocks": clk, "kernels": kern,
+            "max_abs_err_embedding": max_err, "rel_err_embedding": rel_err, "rel_tol": REL_TOL,
+            "residues_match": residues_match, "correct": correct, "level4_secondary": low, "cfg3": cfg3,
         }
         print(json.dumps(line), flush=True)
-    lib.DeleteScheme()
+    if not correct:
+        raise SystemExit("bench: results out of tolerance or residues differ from the oracle")
+
+
+def go_probe() -> str:
+    """Whether the reference's Lattigo CPU path could be built on this host:
+    a Go toolchain and the lattigo/v6 module in the module cache."""
+    import shutil
+    go = shutil.which("go")
+    if not go:
+        return "unavailable on this box: no go toolchain on PATH"
+    try:
+        ver = subprocess.run([go, "version"], capture_output=True, text=True, timeout=20).stdout.strip()
+        modc = subprocess.run([go, "env", "GOMODCACHE"], capture_output=True, text=True, timeout=20).stdout.strip()
+    except Exception as ex:
+        return f"go present, probe failed: {ex}"
+    have = os.path.isdir(os.path.join(modc, "github.com", "baahl-nyu")) if modc else False
+    return f"{ver}; lattigo module cache {'present' if have else 'absent'}"
 
 
 class _Solo:

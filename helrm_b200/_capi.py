@@ -113,6 +113,7 @@ SIGNATURES = {
     "helrm_ProfileRead": [P(c_double), P(c_double), P(c_double), P(c_u64), c_int, P(c_int)],
     "helrm_KernelClassName": [c_int, ctypes.c_char_p, c_int],
     "helrm_GetLaunchCount": [P(c_u64)],
+    "helrm_GetAllocCount": [P(c_u64)],
     "helrm_ProfilerRange": [c_int],
 }
 

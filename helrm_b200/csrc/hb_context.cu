@@ -105,6 +105,30 @@ struct LinTrans {
     std::vector<int> giant_of_slot;   // slot -> g
 };
 
+// ---- fixed scratch of the no-allocation rescale -----------------------------
+// Some callers must not allocate device memory at all: a host runtime that
+// reserves the whole HBM budget up front through its own allocator (an
+// allocation behind its back can fail or push its pool out of memory), and
+// serving loops where the first request of a new batch size would otherwise
+// grow the stream-ordered pool with a blocking cudaMalloc in the middle of a
+// latency-critical step.  For them helrm_kernel_rescale_noalloc takes its
+// temporaries from this fixed array, part of the library's device image.
+// Every word the call reads from it is written earlier in the same call, so
+// nothing in it has to start at zero and it is never cleared.
+static __device__ __align__(256) u64 g_rescale_scratch[HELRM_RESCALE_SCRATCH_WORDS];
+
+// The array's device address on the current device.  In host code the
+// symbol is only a host-side stand-in, so kernels get this address instead.
+// Called with the scheme's device current when the scheme is created (the
+// lookup loads the library's device image on that device), so the address
+// always belongs to the live context.
+static u64 *lookup_rescale_scratch() {
+    void *p = nullptr;
+    cuda_check(cudaGetSymbolAddress(&p, g_rescale_scratch), "cudaGetSymbolAddress(rescale scratch)");
+    if (!p) HB_THROW(HB_ECUDA, "cudaGetSymbolAddress(rescale scratch) returned null");
+    return (u64 *)p;
+}
+
 class Context {
 public:
     int device = 0;
@@ -132,6 +156,10 @@ public:
     // memory accounting
     std::unordered_map<void *, size_t> alloc_sizes;
     size_t live = 0, peak = 0, key_bytes = 0;
+    u64 n_allocs = 0;  // device-pool allocations made through alloc()/alloc_on()
+    // device address of the fixed rescale scratch array on this scheme's
+    // device, looked up once when the scheme is created
+    u64 *d_rescale_scratch = nullptr;
 
     size_t limb_bytes() const { return (size_t)N * sizeof(u64); }
     size_t key_words() const { return (size_t)dnum * 2 * P * N; }
@@ -141,6 +169,7 @@ public:
         void *p = nullptr;
         if (words == 0) words = 1;
         cuda_check(cudaMallocAsync(&p, words * sizeof(u64), stream), "cudaMallocAsync");
+        n_allocs++;
         alloc_sizes[p] = words * sizeof(u64);
         live += words * sizeof(u64);
         peak = std::max(peak, live);
@@ -159,6 +188,7 @@ public:
         void *p = nullptr;
         if (words == 0) words = 1;
         cuda_check(cudaMallocAsync(&p, words * sizeof(u64), s), "cudaMallocAsync");
+        n_allocs++;
         alloc_sizes[p] = words * sizeof(u64);
         live += words * sizeof(u64);
         peak = std::max(peak, live);
@@ -246,6 +276,7 @@ public:
                                     " key-switching digits; pass a smaller dnum or more special primes");
 
         cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+        d_rescale_scratch = lookup_rescale_scratch();
         cudaMemPool_t pool;
         cuda_check(cudaDeviceGetDefaultMemPool(&pool, dev), "mempool");
         u64 thr = ~0ull;
@@ -2131,40 +2162,7 @@ HB_API int helrm_kernel_rescale(const uint64_t *in, uint64_t *out, int nq, int n
 }
 
 // ---- rescale without device allocation ---------------------------------------
-// Some callers must not allocate device memory at all: a host runtime that
-// reserves the whole HBM budget up front through its own allocator (an
-// allocation behind its back can fail or push its pool out of memory), and
-// serving loops where the first request of a new batch size would otherwise
-// grow the stream-ordered pool with a blocking cudaMalloc in the middle of a
-// latency-critical step.  For them the rescale temporaries come from this
-// fixed array, part of the library's device image.  Every word the call
-// reads from it is written earlier in the same call, so nothing in it has to
-// start at zero and it is never cleared.
-static __device__ __align__(256) u64 g_rescale_scratch[HELRM_RESCALE_SCRATCH_WORDS];
-
-#define HB_SCRATCH_DEVICES 64
-static std::mutex g_rescale_scratch_mu;
-static u64 *g_rescale_scratch_ptr[HB_SCRATCH_DEVICES] = {};
-
-// The array's address on `device`, looked up once per device with that
-// device current (the lookup loads the library's device image there).
-static u64 *rescale_scratch_on(int device) {
-    if (device < 0 || device >= HB_SCRATCH_DEVICES) HB_THROW(HB_EINVAL, "rescale scratch: device out of range");
-    std::lock_guard<std::mutex> lk(g_rescale_scratch_mu);
-    if (!g_rescale_scratch_ptr[device]) {
-        int cur = -1;
-        cuda_check(cudaGetDevice(&cur), "cudaGetDevice");
-        if (cur != device) cuda_check(cudaSetDevice(device), "cudaSetDevice");
-        void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_rescale_scratch);
-        if (cur != device) cudaSetDevice(cur);
-        cuda_check(e, "cudaGetSymbolAddress(rescale scratch)");
-        if (!p) HB_THROW(HB_ECUDA, "cudaGetSymbolAddress(rescale scratch) returned null");
-        g_rescale_scratch_ptr[device] = (u64 *)p;
-    }
-    return g_rescale_scratch_ptr[device];
-}
-
+// (the scratch array itself and its address lookup sit above class Context)
 HB_API int helrm_kernel_rescale_noalloc(const uint64_t *in, uint64_t *out, int nq, int nbatch, void *stream) {
     return guard([&] {
         Context &c = C();
@@ -2175,7 +2173,7 @@ HB_API int helrm_kernel_rescale_noalloc(const uint64_t *in, uint64_t *out, int n
             HB_THROW(HB_EINVAL, "kernel_rescale_noalloc: needs " + std::to_string(need) +
                                     " scratch words (nbatch*2*nq*N), above the static limit of " +
                                     std::to_string((size_t)HELRM_RESCALE_SCRATCH_WORDS));
-        u64 *scratch = rescale_scratch_on(c.device);
+        u64 *scratch = c.d_rescale_scratch;
         cudaStream_t old = c.stream;
         if (stream) c.stream = (cudaStream_t)stream;
         try {
@@ -2299,5 +2297,11 @@ HB_API int helrm_GetLaunchCount(uint64_t *n) {
     return guard([&] {
         OUT(n);
         *n = launch_count();
+    });
+}
+HB_API int helrm_GetAllocCount(uint64_t *n) {
+    return guard([&] {
+        OUT(n);
+        *n = C().n_allocs;
     });
 }

@@ -34,128 +34,145 @@ def _peak():
         return 6650.0, "fallback"
 
 
-def main():
+def run(batches=(1, 16, 128), reps=5, ops="ntt,intt,aut,mac,rescale,ks", rotations=32, device=0,
+        emit=None) -> list[dict]:
+    """Run the config-3 primitives and return one dict per (primitive,
+    batch); `emit` (if given) is called on each as it is measured.  Creates
+    and deletes its own scheme (the library holds one per process)."""
     import torch
 
     from helrm_b200 import B200Library, _capi
     from helrm_b200.params import CFG2, CFG2_DNUM
 
+    ops = set(ops.split(",")) if isinstance(ops, str) else set(ops)
+    results: list[dict] = []
+    lib = B200Library(dnum=CFG2_DNUM, seed=5, device=device)
+    lib.setup_bindings(CFG2)
+    try:
+        lib.GenerateSecretKey()
+        info = lib.scheme_info()
+        N, L, K, alpha = info["N"], info["L"], info["K"], info["alpha"]
+        nq = L
+        primes = lib.GetModuliChain()
+        beta = (nq + alpha - 1) // alpha
+        R = rotations
+        if "ks" in ops:
+            for k in range(1, R + 1):
+                lib.AddRotationKey(k)
+        capi = _capi.load()
+        limb = N * 8
+        peak, src = _peak()
+        # an explicit stream: a NULL handle would select the library's own
+        # stream, outside the events recorded here
+        stream = torch.cuda.Stream()
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        gen = torch.Generator(device="cuda").manual_seed(1)
+
+        def residues(nct):
+            t = torch.empty((nct, 2, nq, N), dtype=torch.int64, device="cuda")
+            for i, q in enumerate(primes):
+                t[:, :, i].random_(0, q, generator=gen)
+            return t
+
+        def timed(fn):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps):
+                fn()
+            b.record(stream)
+            b.synchronize()
+            return a.elapsed_time(b) / reps
+
+        def report(op, B, ms, nbytes, extra=None):
+            gbs = nbytes / (ms * 1e6)
+            line = {"op": op, "batch": B, "ms": ms, "GBps": gbs, "frac_hbm": gbs / peak,
+                    "peak": f"{peak} GB/s ({src})"}
+            line.update(extra or {})
+            results.append(line)
+            if emit:
+                emit(line)
+
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        with torch.cuda.stream(stream):
+            for B in batches:
+                x = residues(B)
+                rows = B * 2 * nq
+                if "ntt" in ops:
+                    ms = timed(lambda: _capi.check(capi.helrm_kernel_ntt(ptr(x), rows, nq, nq, 0, sp)))
+                    report("ntt_forward", B, ms, 2 * 2 * nq * limb * B,
+                           {"Gbutterflies_s": rows * (N // 2) * 16 / (ms * 1e6)})
+                if "intt" in ops:
+                    ms = timed(lambda: _capi.check(capi.helrm_kernel_ntt(ptr(x), rows, nq, nq, 1, sp)))
+                    report("ntt_inverse", B, ms, 2 * 2 * nq * limb * B,
+                           {"Gbutterflies_s": rows * (N // 2) * 16 / (ms * 1e6)})
+                if "aut" in ops:
+                    y = torch.empty_like(x)
+                    g = pow(5, 7, 2 * N)
+                    ms = timed(lambda: _capi.check(capi.helrm_kernel_automorphism(ptr(x), ptr(y), rows, g, sp)))
+                    report("automorphism", B, ms, 2 * 2 * nq * limb * B)
+                    del y
+                if "rescale" in ops:
+                    y = torch.empty((B, 2, nq - 1, N), dtype=torch.int64, device="cuda")
+                    ms = timed(lambda: _capi.check(capi.helrm_kernel_rescale(ptr(x), ptr(y), nq, B, sp)))
+                    report("rescale", B, ms, (2 * nq + 2 * (nq - 1)) * limb * B)
+                    del y
+                if "mac" in ops:
+                    g = 32
+                    cts = residues(g)
+                    pts = torch.empty((g, nq, N), dtype=torch.int64, device="cuda")
+                    for i, q in enumerate(primes):
+                        pts[:, i].random_(0, q, generator=gen)
+                    out = torch.empty((2, nq, N), dtype=torch.int64, device="cuda")
+                    cp = (ctypes.c_void_p * g)(*[c.data_ptr() for c in cts])
+                    pp = (ctypes.c_void_p * g)(*[p.data_ptr() for p in pts])
+
+                    def mac_batch():
+                        for _ in range(B):
+                            _capi.check(capi.helrm_kernel_mac(cp, pp, g, nq, ptr(out), sp))
+                    ms = timed(mac_batch)
+                    report("mac_32_pairs", B, ms, (g * 3 * nq + 2 * nq) * limb * B)
+                    del cts, pts, out
+                if "ks" in ops:
+                    # outputs [R][B][2][nq][N]; bound the device memory at ~12 GB
+                    sub = max(1, min(B, int(12e9 // (R * 2 * nq * limb))))
+                    outs = torch.empty((R, sub, 2, nq, N), dtype=torch.int64, device="cuda")
+                    ks = (ctypes.c_int * R)(*range(1, R + 1))
+
+                    def ks_batch():
+                        for s0 in range(0, B, sub):
+                            nb = min(sub, B - s0)
+                            xs = x[s0:s0 + nb]
+                            _capi.check(capi.helrm_kernel_rotate_hoisted(ptr(xs), nq, nb, ks, R, ptr(outs), sp))
+                    ms = timed(ks_batch)
+                    ne = nq + K
+                    # SURVEY-style algorithmic bytes of ModUp + KeyMult + ModDown,
+                    # their NTTs included (each operand read or written once)
+                    modup = nq * limb + beta * ne * limb
+                    per_rot = beta * ne * limb + 2 * ne * limb + (2 * ne + 2 * nq) * limb + nq * limb
+                    evk = 2 * beta * ne * limb * R * ((B + sub - 1) // sub)
+                    report("hoisted_keyswitch_R32", B, ms, B * (modup + R * per_rot) + evk,
+                           {"rotations": R, "launch_batch": sub})
+                    del outs
+                del x
+                torch.cuda.empty_cache()
+        stream.synchronize()
+    finally:
+        lib.DeleteScheme()
+    return results
+
+
+def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batches", default="1,16,128")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--ops", default="ntt,intt,aut,mac,rescale,ks")
     ap.add_argument("--rotations", type=int, default=32)
     args = ap.parse_args()
-    ops = set(args.ops.split(","))
-
-    lib = B200Library(dnum=CFG2_DNUM, seed=5, device=0)
-    lib.setup_bindings(CFG2)
-    lib.GenerateSecretKey()
-    info = lib.scheme_info()
-    N, L, K, alpha = info["N"], info["L"], info["K"], info["alpha"]
-    nq = L
-    primes = lib.GetModuliChain()
-    beta = (nq + alpha - 1) // alpha
-    R = args.rotations
-    if "ks" in ops:
-        for k in range(1, R + 1):
-            lib.AddRotationKey(k)
-    capi = _capi.load()
-    limb = N * 8
-    peak, src = _peak()
-    # an explicit stream: a NULL handle would select the library's own
-    # stream, outside the events recorded here
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    sp = ctypes.c_void_p(stream.cuda_stream)
-    gen = torch.Generator(device="cuda").manual_seed(1)
-
-    def residues(nct):
-        t = torch.empty((nct, 2, nq, N), dtype=torch.int64, device="cuda")
-        for i, q in enumerate(primes):
-            t[:, :, i].random_(0, q, generator=gen)
-        return t
-
-    def timed(fn):
-        for _ in range(2):
-            fn()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(args.reps):
-            fn()
-        b.record(stream)
-        b.synchronize()
-        return a.elapsed_time(b) / args.reps
-
-    def report(op, B, ms, nbytes, extra=None):
-        gbs = nbytes / (ms * 1e6)
-        line = {"op": op, "batch": B, "ms": ms, "GBps": gbs, "frac_hbm": gbs / peak,
-                "peak": f"{peak} GB/s ({src})"}
-        line.update(extra or {})
-        print(json.dumps(line), flush=True)
-
-    ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-    for B in [int(b) for b in args.batches.split(",")]:
-        x = residues(B)
-        rows = B * 2 * nq
-        if "ntt" in ops:
-            ms = timed(lambda: _capi.check(capi.helrm_kernel_ntt(ptr(x), rows, nq, nq, 0, sp)))
-            report("ntt_forward", B, ms, 2 * 2 * nq * limb * B,
-                   {"Gbutterflies_s": rows * (N // 2) * 16 / (ms * 1e6)})
-        if "intt" in ops:
-            ms = timed(lambda: _capi.check(capi.helrm_kernel_ntt(ptr(x), rows, nq, nq, 1, sp)))
-            report("ntt_inverse", B, ms, 2 * 2 * nq * limb * B,
-                   {"Gbutterflies_s": rows * (N // 2) * 16 / (ms * 1e6)})
-        if "aut" in ops:
-            y = torch.empty_like(x)
-            g = pow(5, 7, 2 * N)
-            ms = timed(lambda: _capi.check(capi.helrm_kernel_automorphism(ptr(x), ptr(y), rows, g, sp)))
-            report("automorphism", B, ms, 2 * 2 * nq * limb * B)
-            del y
-        if "rescale" in ops:
-            y = torch.empty((B, 2, nq - 1, N), dtype=torch.int64, device="cuda")
-            ms = timed(lambda: _capi.check(capi.helrm_kernel_rescale(ptr(x), ptr(y), nq, B, sp)))
-            report("rescale", B, ms, (2 * nq + 2 * (nq - 1)) * limb * B)
-            del y
-        if "mac" in ops:
-            g = 32
-            cts = residues(g)
-            pts = torch.empty((g, nq, N), dtype=torch.int64, device="cuda")
-            for i, q in enumerate(primes):
-                pts[:, i].random_(0, q, generator=gen)
-            out = torch.empty((2, nq, N), dtype=torch.int64, device="cuda")
-            cp = (ctypes.c_void_p * g)(*[c.data_ptr() for c in cts])
-            pp = (ctypes.c_void_p * g)(*[p.data_ptr() for p in pts])
-
-            def mac_batch():
-                for _ in range(B):
-                    _capi.check(capi.helrm_kernel_mac(cp, pp, g, nq, ptr(out), sp))
-            ms = timed(mac_batch)
-            report("mac_32_pairs", B, ms, (g * 3 * nq + 2 * nq) * limb * B)
-            del cts, pts, out
-        if "ks" in ops:
-            # outputs [R][B][2][nq][N]; bound the device memory at ~12 GB
-            sub = max(1, min(B, int(12e9 // (R * 2 * nq * limb))))
-            outs = torch.empty((R, sub, 2, nq, N), dtype=torch.int64, device="cuda")
-            ks = (ctypes.c_int * R)(*range(1, R + 1))
-
-            def ks_batch():
-                for s0 in range(0, B, sub):
-                    nb = min(sub, B - s0)
-                    xs = x[s0:s0 + nb]
-                    _capi.check(capi.helrm_kernel_rotate_hoisted(ptr(xs), nq, nb, ks, R, ptr(outs), sp))
-            ms = timed(ks_batch)
-            ne = nq + K
-            modup = nq * limb + beta * ne * limb
-            per_rot = beta * ne * limb + 2 * ne * limb + (2 * ne + 2 * nq) * limb + nq * limb
-            evk = 2 * beta * ne * limb * R * ((B + sub - 1) // sub)
-            report("hoisted_keyswitch_R32", B, ms, B * (modup + R * per_rot) + evk,
-                   {"rotations": R, "launch_batch": sub})
-            del outs
-        del x
-        torch.cuda.empty_cache()
-    lib.DeleteScheme()
+    run([int(b) for b in args.batches.split(",")], args.reps, args.ops, args.rotations,
+        emit=lambda line: print(json.dumps(line), flush=True))
 
 
 if __name__ == "__main__":

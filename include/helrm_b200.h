@@ -229,10 +229,11 @@ int helrm_kernel_rotate_hoisted(const uint64_t *d_in, int nq, int nbatch, const 
  * term, nbatch*2*nq*N words in all) come from one fixed array compiled into
  * the library, HELRM_RESCALE_SCRATCH_WORDS words (32 MiB) per device: one
  * ciphertext of N = 2^16 at 24 limbs fits.  Larger requests fail with
- * HB_EINVAL before any work is issued.  The first call on a device looks up
- * that array's address; make it before any stream capture.  All calls on a
- * device share the array: calls whose GPU work overlaps (unordered streams,
- * several host threads) race and corrupt each other's output. */
+ * HB_EINVAL before any work is issued.  helrm_NewScheme looks up that
+ * array's device address once, with the scheme's device current, so the
+ * call itself does no set-up.  All calls on a device share the array: calls
+ * whose GPU work overlaps (unordered streams, several host threads) race and
+ * corrupt each other's output. */
 #define HELRM_RESCALE_SCRATCH_WORDS (4u << 20)
 int helrm_kernel_rescale_noalloc(const uint64_t *d_in, uint64_t *d_out, int nq, int nbatch, void *stream);
 /* synchronise the library stream */
@@ -254,6 +255,8 @@ int helrm_KernelClassName(int cls, char *out, int cap);
 int helrm_ProfilerRange(int on);
 /* number of kernels this library has launched since it was loaded */
 int helrm_GetLaunchCount(uint64_t *n);
+/* number of device-pool allocations the current scheme has made */
+int helrm_GetAllocCount(uint64_t *n);
 
 #ifdef __cplusplus
 }

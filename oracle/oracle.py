@@ -348,6 +348,24 @@ class Oracle:
             raise KeyError("missing rotation key for the BSGS linear transform")
         return out
 
+    def fold_add(self, a, b):
+        """(a + b) mod q_i, limb by limb (residues below 2^61: no overflow)."""
+        qs = np.array(self.primes[:a.shape[1]], dtype=np.uint64)[None, :, None]
+        s = a + b
+        return np.where(s >= qs, s - qs, s)
+
+    def pcmm(self, ct, diag_ks, pts, bs, keys, fold_rotations):
+        """The embedding layer's encrypted step as the reference runs it
+        (orion/nn/linear.py:99-140): the BSGS linear transform, the rescale
+        (orion/backend/python/lt_evaluator.py:262-273), then the hybrid
+        output fold out += rot(out, slots / 2^i) for i = 1..fold_rotations
+        (linear.py:115-117).  keys must hold the fold rotations' keys too."""
+        out = self.rescale(self.bsgs_lt(ct, diag_ks, pts, bs, keys))
+        for i in range(1, fold_rotations + 1):
+            g = self.galois((self.N // 2) >> i)
+            out = self.fold_add(out, self.rotate(out, keys[g], g))
+        return out
+
 
 def set_threads(n: int) -> None:
     """Worker threads for the oracle's limb-parallel loops (default 1)."""

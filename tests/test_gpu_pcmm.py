@@ -3,9 +3,12 @@
 cfg1: single 1024 x 16 table, base-32 digits,
 LogN 13 -- bit-exact against the oracle and within tolerance of the
 cleartext lookup.  cfg2: the 26-table block-diagonal
-416 x 4224 matrix at LogN 16, 24 limbs + 4 special primes, dnum 4 --
-decrypted embedding slots against the cleartext matrix product, and the
-cfg3 primitives (NTT, hoisted key switch) bit-exact at that size.
+416 x 4224 matrix at LogN 16, 24 limbs + 4 special primes, dnum 4, the
+whole step (LT, rescale, fold) on a batch of two -- every residue against
+the oracle, and the decrypted embedding slots against the cleartext matrix
+product.  cfg3 primitives at that size, bit-exact: NTT/INTT on
+a batch of 16 ciphertexts, the hoisted key switch for 32 rotations, MAC
+and rescale.
 
 Tolerance on embedding slots: the error of every
 output slot is at most 2^-15 relative to the largest embedding magnitude.
@@ -136,12 +139,22 @@ def test_cfg3_rescale_and_mac_bit_exact(cfg2):
     assert np.array_equal(cfg2.ct_data(r), cfg2.o.rescale(want))
 
 
-def test_cfg2_pcmm_embedding_slots(cfg2):
+@pytest.fixture(scope="module")
+def cfg2_pcmm(cfg2):
+    """The headline step at its own shape on a batch of two ciphertexts:
+    the 512-diagonal block-diagonal LT (bs 32, 16 giant groups), the
+    rescale and the six hybrid-fold rotations, through the batch entry
+    points the bench times."""
     V = W.cfg2_vocab()
     M = W.block_diag_matrix(V, 64, 16, 0.05, seed=0)
     q = W.zipf_queries(V, 2)
     xs = [W.selector(qq, V) for qq in q]
     lt, ks, diags, rot, cts, outs = _pcmm(cfg2, M, xs, cfg2.info["max_level"])
+    return M, xs, lt, ks, rot, cts, outs
+
+
+def test_cfg2_pcmm_embedding_slots(cfg2, cfg2_pcmm):
+    M, xs, lt, ks, rot, cts, outs = cfg2_pcmm
     info = cfg2.lib.GetLinearTransformInfo(lt)
     assert info["bs"] == 32 and info["n_diags"] == 512 and info["n_giant"] == 16
     for x, o in zip(xs, outs):
@@ -150,3 +163,73 @@ def test_cfg2_pcmm_embedding_slots(cfg2):
         err = np.abs(got - ref).max()
         assert err <= REL_TOL * np.abs(ref).max(), err
         assert cfg2.lib.GetCiphertextLevel(o) == 22
+
+
+def test_cfg2_pcmm_residues_bit_exact(cfg2, cfg2_pcmm):
+    """Every residue of the headline step (LogN 16, 24 q + 4 special primes,
+    dnum 4, 512 diagonals, batch of two) equals the oracle's LT -> rescale ->
+    fold on the same ciphertexts, plaintext diagonals and switching keys:
+    the fixed-shape fused kernels (four digits, full 32-baby chunks, giant
+    steps three per key multiplication, the fold's add inside ModDown) at
+    the size the bench times."""
+    import os
+    M, xs, lt, ks, rot, cts, outs = cfg2_pcmm
+    o = cfg2.o
+    cfg2.om.set_threads(os.cpu_count() or 1)
+    try:
+        plan = W.bsgs_plan(ks, 2.0, cfg2.slots)
+        gal = {o.galois(d) for d in plan["rotation_keys"]} | {o.galois(cfg2.slots >> i) for i in range(1, rot + 1)}
+        keys = {g: cfg2.key(g) for g in sorted(gal)}
+        pts = [cfg2.lib.GetLinearTransformPlaintext(lt, k) for k in ks]
+        for c, out in zip(cts, outs):
+            want = o.pcmm(cfg2.ct_data(c), ks, pts, plan["stride"], keys, rot)
+            got = cfg2.ct_data(out)
+            assert got.shape == want.shape == (2, 23, cfg2.N)
+            assert np.array_equal(got, want)
+    finally:
+        cfg2.om.set_threads(1)
+
+
+def test_cfg3_hoisted_keyswitch_r32_bit_exact(cfg2):
+    """The config-3 hoisted key switch at its own size: 32 rotations of one
+    ciphertext sharing one ModUp, every output residue against the oracle."""
+    import os
+    ct = cfg2.encrypt(np.sin(np.arange(cfg2.slots) / 77.0))
+    ks = list(range(1, 33))
+    outs = cfg2.lib.RotateBatchNew(ct, ks)
+    data = cfg2.ct_data(ct)
+    gs = [cfg2.o.galois(k) for k in ks]
+    cfg2.om.set_threads(os.cpu_count() or 1)
+    try:
+        want = cfg2.o.rotate_hoisted(data, [cfg2.key(g) for g in gs], gs)
+    finally:
+        cfg2.om.set_threads(1)
+    for i, o in enumerate(outs):
+        assert np.array_equal(cfg2.ct_data(o), want[i]), ks[i]
+
+
+def test_cfg3_ntt_batch16_bit_exact(cfg2):
+    """Forward and inverse NTT on a config-3 batch of 16 ciphertexts
+    (768 limbs of 2^16 residues, the microbenchmark's layout) against the
+    oracle's NTT of every limb."""
+    import torch
+    from helrm_b200 import _capi
+    lib = _capi.load()
+    B, nq, N = 16, 24, cfg2.N
+    primes = cfg2.o.primes
+    rng = np.random.default_rng(16)
+    host = np.empty((B, 2, nq, N), dtype=np.uint64)
+    for i in range(nq):
+        host[:, :, i] = rng.integers(0, primes[i], (B, 2, N), dtype=np.uint64)
+    dev = torch.from_numpy(host.view(np.int64).copy()).cuda()
+    rows = B * 2 * nq
+    _capi.check(lib.helrm_kernel_ntt(ctypes.c_void_p(dev.data_ptr()), rows, nq, nq, 0, None))
+    _capi.check(lib.helrm_Synchronize())
+    fwd = dev.cpu().numpy().view(np.uint64).reshape(B, 2, nq, N)
+    for b in range(B):
+        for pl in range(2):
+            for i in range(nq):
+                assert np.array_equal(fwd[b, pl, i], cfg2.o.ntt(i, host[b, pl, i])), (b, pl, i)
+    _capi.check(lib.helrm_kernel_ntt(ctypes.c_void_p(dev.data_ptr()), rows, nq, nq, 1, None))
+    _capi.check(lib.helrm_Synchronize())
+    assert np.array_equal(dev.cpu().numpy().view(np.uint64).reshape(B, 2, nq, N), host)

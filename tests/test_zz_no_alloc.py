@@ -3,7 +3,8 @@ live in a fixed array inside the library instead of the device pool.
 
 Its output must equal helrm_kernel_rescale's on the same input (integer
 residues: the tolerance is zero), on two calls issued back to back, and the
-call must leave the library's allocation high-water mark where it was.
+calls must make no device-pool allocation: the library's allocation count
+(helrm_GetAllocCount, every cudaMallocAsync the scheme makes) stays put.
 Requests above the fixed array's size must be refused before any work.
 This file is named to be collected last, so it also runs after every other
 GPU test in the same process; it needs nothing from them.
@@ -47,6 +48,12 @@ def _peak_mb(capi):
     return peak.value
 
 
+def _allocs(capi):
+    n = ctypes.c_uint64(0)
+    _capi.check(capi.helrm_GetAllocCount(ctypes.byref(n)))
+    return n.value
+
+
 def test_noalloc_rescale_matches_allocating_entry_point(scheme):
     import torch
     capi = _capi.load()
@@ -59,15 +66,17 @@ def test_noalloc_rescale_matches_allocating_entry_point(scheme):
     want = [torch.full_like(g, -2) for g in got]
     torch.cuda.synchronize()
 
-    peak0 = _peak_mb(capi)
+    n0 = _allocs(capi)
     for (nq, nb), x, g in zip(cases, xs, got):  # two calls in a row, no sync between
         _capi.check(capi.helrm_kernel_rescale_noalloc(_ptr(x), _ptr(g), nq, nb, None))
     _capi.check(capi.helrm_Synchronize())
-    assert _peak_mb(capi) == peak0, "the no-allocation entry point drew on the device pool"
+    assert _allocs(capi) == n0, "the no-allocation entry point drew on the device pool"
 
     for (nq, nb), x, w in zip(cases, xs, want):
         _capi.check(capi.helrm_kernel_rescale(_ptr(x), _ptr(w), nq, nb, None))
     _capi.check(capi.helrm_Synchronize())
+    # the counter does see the allocating entry point's temporaries
+    assert _allocs(capi) > n0
     for g, w in zip(got, want):
         assert torch.equal(g.cpu(), w.cpu())  # tolerance 0: exact residues
 
