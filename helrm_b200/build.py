@@ -16,7 +16,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libhelrm_b200.so")
 SOURCES = ["hb_kernels.cu", "hb_context.cu", "hb_host.cpp"]
-HEADERS = ["hb_arith.cuh", "hb_kernels.cuh", "hb_bsgs.cuh", "hb_host.hpp"]
+HEADERS = ["hb_arith.cuh", "hb_kernels.cuh", "hb_bsgs.cuh", "hb_bsgs_tc.cuh", "hb_host.hpp"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

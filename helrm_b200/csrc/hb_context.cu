@@ -140,6 +140,9 @@ public:
     NttTables ntt{};
     u64 *d_tables = nullptr;
     u64 *d_pmod = nullptr;     // P mod q_p, [P]
+    u64 *d_cls8 = nullptr;     // [L][9] 2^(8s) mod q_i (tensor-core MAC epilogue)
+    int *d_tc_err = nullptr;   // error bits of the tensor-core MAC's bounded waits
+    bool use_tc = false;       // tensor-core baby-step MAC where supported (HELRM_B200_MAC=tc)
     std::vector<LevelTabs> lv; // index nq (1..L)
     std::vector<PrimeConst> pcs;
     // keys
@@ -233,7 +236,21 @@ public:
     void d2d(u64 *dst, const u64 *src, size_t words) {
         cuda_check(cudaMemcpyAsync(dst, src, words * 8, cudaMemcpyDeviceToDevice, stream), "d2d");
     }
-    void sync() { cuda_check(cudaStreamSynchronize(stream), "sync"); }
+    void sync() {
+        cuda_check(cudaStreamSynchronize(stream), "sync");
+        check_tc_error();
+    }
+    // a tensor-core MAC pipeline wait that ran out leaves its bits in d_tc_err
+    void check_tc_error() {
+        if (!d_tc_err) return;
+        int v = 0;
+        cuda_check(cudaMemcpy(&v, d_tc_err, sizeof(int), cudaMemcpyDeviceToHost), "tc error word");
+        if (v) {
+            cudaMemset(d_tc_err, 0, sizeof(int));
+            HB_THROW(HB_ECUDA, "tensor-core MAC: a pipeline wait timed out (bits " + std::to_string(v) +
+                                   "); its output is invalid");
+        }
+    }
 
     RowMap qmap(int nq) const { return rowmap(nq, nq, L); }
     RowMap extmap(int nq) const { return rowmap(nq + K, nq, L); }
@@ -379,6 +396,16 @@ public:
         }
         d_pmod = alloc(P);
         cuda_check(cudaMemcpyAsync(d_pmod, pm.data(), P * 8, cudaMemcpyHostToDevice, stream), "pmod");
+        {
+            std::vector<u64> cls((size_t)L * 9, 0);
+            bsgs_mma_class_consts(cls.data(), primes.data(), L);
+            d_cls8 = alloc((size_t)L * 9);
+            cuda_check(cudaMemcpyAsync(d_cls8, cls.data(), cls.size() * 8, cudaMemcpyHostToDevice, stream), "cls8");
+            d_tc_err = (int *)alloc(1);
+            cuda_check(cudaMemsetAsync(d_tc_err, 0, 8, stream), "tc error word");
+            const char *m = std::getenv("HELRM_B200_MAC");
+            use_tc = m && std::string(m) == "tc";
+        }
 
         build_level_tables();
         sync();
@@ -1212,6 +1239,14 @@ public:
                     ch.nkeys += bd.key != nullptr;
                     for (int gi = 0; gi < HB_GCH; gi++) ch.npts += bd.pt[gi] != nullptr;
                 }
+                ch.ptp = nullptr;
+                if (use_tc && bsgs_mma_supported(nq, beta_of(nq))) {
+                    // the chunk's plaintexts as byte planes for the tensor-core MAC
+                    u64 *planes = alloc((bsgs_mma_planes_bytes(nq, logN) + 7) / 8);
+                    t.plan_dev.push_back((BabyDesc *)planes);
+                    ch.ptp = (const uint8_t *)planes;
+                    bsgs_mma_planes((uint8_t *)planes, ch, nq, logN, stream);
+                }
                 t.plan_chunks.push_back(ch);
                 sync();
             }
@@ -1233,9 +1268,18 @@ public:
         u64 *D = alloc((size_t)nb * beta * es);
         modup(D, in + (size_t)nq * N, nq, nb, cts_);
         u64 *inner = alloc((size_t)nb * nslots * 2 * es);
-        for (auto &ch : t.plan_chunks)
-            bsgs_baby_mac(inner, in, D, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, nb, cts_,
-                          (size_t)beta * es, (size_t)nslots * 2 * es, stream);
+        for (auto &ch : t.plan_chunks) {
+            if (ch.ptp) {
+                // q rows on the tensor cores, special rows on the CUDA cores
+                bsgs_baby_mma(inner, in, D, ch, d_cls8, nq, K, L, beta, P, d_pmod, logN, nb, cts_, (size_t)beta * es,
+                              (size_t)nslots * 2 * es, d_tc_err, stream);
+                bsgs_baby_mac_special(inner, in, D, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, nb, cts_,
+                                      (size_t)beta * es, (size_t)nslots * 2 * es, stream);
+            } else {
+                bsgs_baby_mac(inner, in, D, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, nb, cts_,
+                              (size_t)beta * es, (size_t)nslots * 2 * es, stream);
+            }
+        }
         release(D);
         // the giant-0 slot needs no rotation: its inner sum is the accumulator
         // itself (no copy); without one, a zeroed accumulator of its own

@@ -19,6 +19,7 @@ __constant__ PrimeConst c_pc[HB_MAX_PRIMES];
 }  // namespace hb
 
 #include "hb_bsgs.cuh"
+#include "hb_bsgs_tc.cuh"
 
 namespace hb {
 
@@ -100,7 +101,7 @@ struct ProfScope {
 
 static const char *kClassNames[KC_COUNT] = {
     "ntt_forward", "ntt_inverse", "modup_bconv", "moddown_bconv", "moddown_combine", "keymult",
-    "bsgs_baby_mac", "rescale", "elementwise", "automorphism", "sampling"};
+    "bsgs_baby_mac", "rescale", "elementwise", "automorphism", "sampling", "bsgs_mac_mma"};
 
 const char *kclass_name(int c) { return (c >= 0 && c < KC_COUNT) ? kClassNames[c] : ""; }
 unsigned long long launch_count() { return g_launches; }
@@ -1992,6 +1993,120 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
     }
 #undef HB_BSGS_LAUNCH
     check_launch("bsgs_mac");
+}
+
+// ---- the tensor-core MAC (hb_bsgs_tc.cuh) ------------------------------------
+bool bsgs_mma_supported(int nq, int beta) {
+    if (beta < 1 || beta > 4 || nq < 1 || nq > g_host_nq) return false;
+    for (int i = 0; i < nq; i++)
+        if (g_host_q[i] >= (1ull << 37)) return false;
+    return true;
+}
+size_t bsgs_mma_planes_bytes(int nq, int logN) { return (size_t)nq * ((size_t)1 << logN) / kTcCoef * kTcPtTile; }
+
+void bsgs_mma_planes(uint8_t *ptp, const BsgsChunk &ch, int nq, int logN, cudaStream_t s) {
+    if (ch.nbabies > 32 || ch.gcount > HB_GCH) throw std::invalid_argument("bsgs_mma: chunk too large");
+    ProfScope ps(KC_ELEMENTWISE, (double)nq * (1 << logN) * (8.0 * ch.npts / ch.gcount + kTcPlanes * 512.0 / kTcCoef),
+                 0.0, s, 1);
+    const int N = 1 << logN;
+    k_pt_planes<<<dim3((N + 127) / 128, nq), 128, 0, s>>>(ptp, ch.babies, ch.nbabies, ch.gcount, logN);
+    check_launch("pt_planes");
+}
+
+void bsgs_mma_class_consts(u64 *out, const u64 *primes, int nq) {
+    for (int e = 0; e < nq; e++) {
+        const unsigned __int128 q = primes[e];
+        unsigned __int128 v = 1;
+        for (int c = 0; c < kTcClasses; c++) {
+            out[(size_t)e * kTcClasses + c] = (u64)(v % q);
+            v = (v % q) << 8;
+        }
+    }
+}
+
+void bsgs_baby_mma(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, const u64 *cls, int nq, int K,
+                   int L, int beta, int keyP, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride,
+                   size_t d_stride, size_t inner_stride, int *err, cudaStream_t s) {
+    (void)L;
+    if (!ch.ptp || ch.nbabies > 32 || ch.gcount > HB_GCH || !bsgs_mma_supported(nq, beta))
+        throw std::invalid_argument("bsgs_mma: unsupported chunk or primes");
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_bsgs_mma<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        cudaFuncSetAttribute(k_bsgs_mma<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        cudaFuncSetAttribute(k_bsgs_mma<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        cudaFuncSetAttribute(k_bsgs_mma<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        attr = true;
+    }
+    static int nsm = 0;
+    if (!nsm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        if (nsm <= 0) nsm = 148;
+    }
+    const long tiles = (long)nq * ((1 << logN) / kTcCoef);
+    const int grid = (int)std::min<long>(nsm, tiles);
+    const double nqw = (double)nq * (1 << logN);
+    // a pass waits on nothing outside itself; 2 s bounds every pipeline wait
+    const unsigned long long limit_ns = 2000000000ull;
+    for (int ct0 = 0; ct0 < nbatch; ct0 += kTcCts) {
+        const int nb = std::min(kTcCts, nbatch - ct0);
+        // per pass: the chunk's keys (q rows) and plaintext planes once; per
+        // ciphertext: the q rows of c0/c1 and of the digits, the inner sums written
+        ProfScope ps(KC_BSGS_MMA,
+                     nb * 8.0 * (2.0 * nqw + beta * nqw + 2.0 * ch.gcount * nqw * (ch.accumulate ? 2 : 1)) +
+                         8.0 * 2.0 * beta * ch.nkeys * nqw + (double)bsgs_mma_planes_bytes(nq, logN),
+                     (double)nb * nqw * (2.0 * beta * ch.nkeys + 2.0 * ch.npts), s, 1);
+#define HB_MMA_LAUNCH(B_)                                                                                       \
+    k_bsgs_mma<B_><<<grid, kTcThreads, kTcSmem, s>>>(inner, ct, D, ch, ch.ptp, cls, nq, K, keyP, pmod_q, logN,   \
+                                                     nbatch, ct0, ct_stride, d_stride, inner_stride, err, limit_ns)
+        switch (beta) {
+            case 1: HB_MMA_LAUNCH(1); break;
+            case 2: HB_MMA_LAUNCH(2); break;
+            case 3: HB_MMA_LAUNCH(3); break;
+            default: HB_MMA_LAUNCH(4); break;
+        }
+#undef HB_MMA_LAUNCH
+        check_launch("bsgs_mma");
+    }
+}
+
+void bsgs_baby_mac_special(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, int nq, int K, int L,
+                           int beta, int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch,
+                           size_t ct_stride, size_t d_stride, size_t inner_stride, cudaStream_t s) {
+    if (K == 0) return;
+    if (ch.nbabies > HB_BCH || ch.gcount > HB_GCH) throw std::invalid_argument("bsgs chunk too large");
+    const size_t smem = bsgs_smem_words(beta) * 8;
+    if (smem > 227 * 1024 || beta > HB_MAX_BETA)
+        throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<0, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<0, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+    }
+    const double kd = (double)K * (1 << logN);
+    ProfScope ps(KC_BSGS_MAC,
+                 8.0 * (nbatch * (beta * kd + 2.0 * ch.gcount * kd * (ch.accumulate ? 2 : 1)) +
+                        2.0 * beta * ch.nkeys * kd + ch.npts * kd),
+                 (double)nbatch * kd * (2.0 * beta * ch.nkeys + 2.0 * ch.npts), s, 1);
+    const bool split = beta == 4 && primes_sized(L, K, false);
+    const int e0 = nq;
+    if (split && ch.nbabies == HB_BCH)
+        k_bsgs_mac<HB_BCH, 4, 2><<<dim3((1u << logN) / HB_BT, K), HB_GCH * HB_BT, smem, s>>>(
+            inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN, nbatch, e0, ct_stride, d_stride,
+            inner_stride);
+    else if (split)
+        k_bsgs_mac<0, 4, 2><<<dim3((1u << logN) / HB_BT, K), HB_GCH * HB_BT, smem, s>>>(
+            inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN, nbatch, e0, ct_stride, d_stride,
+            inner_stride);
+    else
+        k_bsgs_mac<0, 0, 0><<<dim3((1u << logN) / HB_BT, K), HB_GCH * HB_BT, smem, s>>>(
+            inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN, nbatch, e0, ct_stride, d_stride,
+            inner_stride);
+    check_launch("bsgs_mac_special");
 }
 
 // ---- batched copies ----------------------------------------------------------

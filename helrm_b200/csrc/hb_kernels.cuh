@@ -58,7 +58,7 @@ void upload_prime_consts(const PrimeConst *pc, int n);
 // ---- launch accounting ------------------------------------------------------
 enum KernelClass {
     KC_NTT_FWD, KC_NTT_INV, KC_MODUP_BCONV, KC_MODDOWN_BCONV, KC_MODDOWN_COMBINE, KC_KEYMULT,
-    KC_BSGS_MAC, KC_RESCALE, KC_ELEMENTWISE, KC_AUTOMORPHISM, KC_SAMPLE, KC_COUNT
+    KC_BSGS_MAC, KC_RESCALE, KC_ELEMENTWISE, KC_AUTOMORPHISM, KC_SAMPLE, KC_BSGS_MMA, KC_COUNT
 };
 struct ProfStats {
     double ms[KC_COUNT] = {};
@@ -209,6 +209,7 @@ struct BsgsChunk {
     int nkeys;               // babies with a key (b != 0), for accounting
     int npts;                // plaintexts referenced by the chunk, for accounting
     int accumulate;          // add into inner (later baby chunks of the same giant slots)
+    const uint8_t *ptp;      // plaintext byte planes of the q rows (tensor-core MAC), or null
 };
 // inner[g][pl][e][n] for g in [gbase, gbase+gcount): sum over babies of
 // pt(g, b) * R_b, R_b = baby rotation of the input kept in the PQ basis:
@@ -216,6 +217,27 @@ struct BsgsChunk {
 void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, int nq, int K, int L,
                    int beta, int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride,
                    size_t d_stride, size_t inner_stride, cudaStream_t s);
+
+// ---- the same MAC on the tensor cores (q rows; hb_bsgs_tc.cuh) ----------------
+// Usable when every q row prime is below 2^37, the chunk has at most 32
+// babies and 16 giant slots, and beta is 1..4.
+bool bsgs_mma_supported(int nq, int beta);
+// bytes of the plaintext byte planes of one chunk (q rows nq)
+size_t bsgs_mma_planes_bytes(int nq, int logN);
+// ch.ptp <- the chunk's plaintexts as byte planes (one launch)
+void bsgs_mma_planes(uint8_t *ptp, const BsgsChunk &ch, int nq, int logN, cudaStream_t s);
+// [nq][9] table 2^(8s) mod q_e for the epilogue (host values)
+void bsgs_mma_class_consts(u64 *out, const u64 *primes, int nq);
+// inner[g][pl][e][n] for the q rows e < nq, over nbatch ciphertexts in
+// passes of 32; the special rows are left to bsgs_baby_mac_special.
+// err: device word receiving HB_TC_ERR_* bits if a pipeline wait ran out.
+void bsgs_baby_mma(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, const u64 *cls, int nq, int K,
+                   int L, int beta, int keyP, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride,
+                   size_t d_stride, size_t inner_stride, int *err, cudaStream_t s);
+// the CUDA-core MAC on the special-prime rows only
+void bsgs_baby_mac_special(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, int nq, int K, int L,
+                           int beta, int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch,
+                           size_t ct_stride, size_t d_stride, size_t inner_stride, cudaStream_t s);
 
 // copy rows with optional automorphism (used to place P*c parts etc.)
 void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s);
