@@ -43,6 +43,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--mode", default="dp", choices=["dp", "tables"],
+                    help="dp: each rank its own batch (weak scaling); tables: the 26 tables split across the "
+                         "ranks, one batch, partial ciphertexts summed by one NCCL reduce (strong scaling)")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--level", type=int, default=23, help="PCMM input level (23 = all 24 limbs)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -566,6 +569,105 @@ def run_b200(args, dist):
         raise SystemExit("bench: results out of tolerance or residues differ from the oracle")
 
 
+def run_b200_tables(args, dist):
+    """Table-sharded embedding layer (helrm_b200/sharding.py): every rank
+    holds the same keys and the same encrypted batch and evaluates only its
+    contiguous group of tables (block height 64 at 8 ranks); the partial
+    packed ciphertexts are summed as 64-bit residues by one NCCL reduce to
+    rank 0, which imports the sum with every limb reduced modulo its prime.
+    One step = one batch through the whole layer; the job's rate is the
+    batch over the slowest rank's device time (strong scaling)."""
+    import torch
+
+    from helrm_b200 import B200Library, sharding as S
+    from helrm_b200.params import CFG2, CFG2_DNUM
+
+    dev = dist.local
+    torch.cuda.set_device(dev)
+    lib = B200Library(dnum=CFG2_DNUM, seed=1000, device=dev)  # one key set, shared by every rank
+    lib.setup_bindings(CFG2)
+    lib.GenerateSecretKey()
+    M, ks, diags, rot, xs = build_workload(args.batch, seed=100)
+    tables = S.table_shards(26, dist.world)[dist.rank]
+    se = S.ShardedEmbedding(lib, M, tables, args.level)
+    info = lib.scheme_info()
+    slots, N = info["slots"], info["N"]
+    scale = float(1 << CFG2.logscale)
+    cts = []
+    for x in xs:
+        v = np.zeros(slots)
+        v[:len(x)] = x
+        pt = lib.Encode(list(v), args.level, scale)
+        cts.append(lib.Encrypt(pt))
+        lib.DeletePlaintext(pt)
+    nq_out = args.level - 1
+    words = 2 * nq_out * N
+    part = torch.zeros((args.batch, words), dtype=torch.int64, device="cuda")
+    tdist = dist.pg
+
+    def step(keep=False):
+        outs = se.evaluate(cts)
+        out_scale = lib.GetCiphertextScale(outs[0])
+        lib.CiphertextsToDevice(outs, part.data_ptr(), words)
+        for o in outs:
+            lib.DeleteCiphertext(o)
+        S.exchange_sum(part, tdist, dst=0)
+        merged = None
+        if dist.rank == 0:
+            torch.cuda.current_stream().synchronize()
+            merged = lib.NewCiphertextsFromDeviceSum(part.data_ptr(), args.batch, args.level - 2, 2, out_scale)
+            if not keep:
+                for m in merged:
+                    lib.DeleteCiphertext(m)
+        lib.Synchronize()
+        return merged
+
+    merged = step(keep=True)
+    correct, rel_err = True, None
+    if dist.rank == 0:
+        got = np.array(lib.Decode(lib.Decrypt(merged[0])))[:416]
+        ref = M.astype(np.float64) @ xs[0]
+        rel_err = float(np.abs(got - ref).max() / np.abs(ref).max())
+        correct = rel_err <= REL_TOL
+        for m in merged:
+            lib.DeleteCiphertext(m)
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    torch.cuda.synchronize()
+    lib.Synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    clk = clocks.stop()
+    dist.barrier()
+    t = dist.max(e0.elapsed_time(e1) / 1000.0)
+    value = args.batch * args.steps / t
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * t / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u64",
+            "data": "synthetic (seeded Criteo-shaped queries; dataset absent)",
+            "config": dict(cfg_dict(args, args.batch), parallelism=f"tables{dist.world} (26 tables over "
+                           f"{dist.world} ranks, one NCCL reduce of the packed partial ciphertexts)",
+                           shard_tables=[len(r) for r in S.table_shards(26, dist.world)],
+                           shard_block_height=se.bh, shard_diagonals=len(se.ks), shard_fold_rotations=se.rot),
+            "mode": "tables", "rel_err_embedding": rel_err, "correct": correct, "clocks": clk,
+            "exchange_bytes_per_rank": args.batch * words * 8, "e2e": None,
+        }
+        print(json.dumps(line), flush=True)
+    se.close()
+    lib.DeleteScheme()
+    if not correct:
+        raise SystemExit("bench: sharded embedding out of tolerance")
+
+
 def go_probe() -> str:
     """Whether the reference's Lattigo CPU path could be built on this host:
     a Go toolchain and the lattigo/v6 module in the module cache."""
@@ -596,7 +698,10 @@ def main():
         return
     dist = Dist()
     try:
-        run_b200(args, dist)
+        if args.mode == "tables":
+            run_b200_tables(args, dist)
+        else:
+            run_b200(args, dist)
     finally:
         dist.close()
 

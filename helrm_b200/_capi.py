@@ -100,6 +100,8 @@ SIGNATURES = {
     "helrm_UploadCiphertextsAsync": [P(c_void), c_int, c_int, c_int, c_double, P(c_int)],
     "helrm_DownloadCiphertextsAsync": [P(c_int), c_int, P(c_void), c_size],
     "helrm_TransferSync": [],
+    "helrm_CiphertextsToDevice": [P(c_int), c_int, c_void, c_size],
+    "helrm_NewCiphertextsFromDeviceSum": [c_void, c_int, c_int, c_int, c_double, P(c_int)],
     "helrm_kernel_ntt": [c_void, c_int, c_int, c_int, c_int, c_void],
     "helrm_kernel_automorphism": [c_void, c_void, c_int, c_u64, c_void],
     "helrm_kernel_rescale": [c_void, c_void, c_int, c_int, c_void],

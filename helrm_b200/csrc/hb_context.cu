@@ -2100,6 +2100,37 @@ HB_API int helrm_DownloadCiphertextsAsync(const int *ids, int n, uint64_t *const
         }
     });
 }
+HB_API int helrm_CiphertextsToDevice(const int *ids, int n, uint64_t *d_out, size_t words_each) {
+    return guard([&] {
+        Context &c = C();
+        if (!ids || !d_out || n <= 0) HB_THROW(HB_EINVAL, "CiphertextsToDevice: bad arguments");
+        for (int i = 0; i < n; i++) {
+            const Ct &x = c.ct(ids[i]);
+            const size_t words = (size_t)x.npoly * x.nq * c.N;
+            if (words > words_each) HB_THROW(HB_EINVAL, "CiphertextsToDevice: item smaller than the ciphertext");
+            cuda_check(cudaMemcpyAsync(d_out + (size_t)i * words_each, x.d, words * 8, cudaMemcpyDeviceToDevice,
+                                       c.stream),
+                       "CiphertextsToDevice");
+        }
+        c.sync();  // the caller's stream (a collective) reads the buffer next
+    });
+}
+HB_API int helrm_NewCiphertextsFromDeviceSum(const uint64_t *d_in, int n, int level, int npoly, double scale,
+                                             int *out_ids) {
+    return guard([&] {
+        Context &c = C();
+        if (!d_in || !out_ids || n <= 0 || level < 0 || level >= c.L || npoly < 1 || npoly > 3)
+            HB_THROW(HB_EINVAL, "NewCiphertextsFromDeviceSum: bad arguments");
+        const int nq = level + 1;
+        const size_t words = (size_t)npoly * nq * c.N;
+        for (int i = 0; i < n; i++) {
+            Ct o = c.new_ct(nq, npoly, scale);
+            o.slots = c.slots;
+            ew_reduce_rows(o.d, (const u64 *)d_in + (size_t)i * words, npoly * nq, c.qmap(nq), c.logN, c.stream);
+            out_ids[i] = c.put_ct(o);
+        }
+    });
+}
 HB_API int helrm_TransferSync(void) {
     return guard([&] { C().sync_xfer(); });
 }

@@ -999,6 +999,23 @@ void ew_neg(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cudaStream_
     check_launch("neg");
 }
 
+// out[r] = a[r] mod q(r) for any 64-bit a (Shoup multiplication by 1):
+// the import of summed residues from several ranks
+__global__ void k_reduce_rows(u64 *out, const u64 *a, size_t n, RowMap map, int logN) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const PrimeConst &pc = c_pc[map.prime((int)(i >> logN))];
+        out[i] = mul_shoup(a[i], 1, pc.onep, pc.q);
+    }
+}
+void ew_reduce_rows(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cudaStream_t s) {
+    size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * n, 0, s, 1);
+    k_reduce_rows<<<g, 256, 0, s>>>(out, a, n, map, logN);
+    check_launch("reduce_rows");
+}
+
 // out[pl][i] = a[pl][i] * b[i]
 __global__ void k_mul_bcast(u64 *out, const u64 *a, const u64 *b, size_t n, int nq, int logN) {
     const size_t per = (size_t)nq << logN;

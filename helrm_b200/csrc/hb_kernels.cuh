@@ -84,6 +84,8 @@ void ntt_inverse_from(u64 *dst, const u64 *src, size_t src_stride, int per_item,
 void ew_add(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap map, int logN, cudaStream_t s);
 void ew_sub(u64 *out, const u64 *a, const u64 *b, int nrows, RowMap map, int logN, cudaStream_t s);
 void ew_neg(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cudaStream_t s);
+// out = a mod q(row) for any 64-bit a (sums of residues from several ranks)
+void ew_reduce_rows(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cudaStream_t s);
 // out[pl][i] = a[pl][i] * b[i]   (b broadcast over npoly blocks of nq rows)
 void ew_mul_bcast(u64 *out, const u64 *a, const u64 *b, int npoly, int nq, int b_rows_stride_nq,
                   int logN, cudaStream_t s);

@@ -207,6 +207,20 @@ int helrm_DownloadCiphertextsAsync(const int *ids, int n, uint64_t *const *host,
 /* wait for every asynchronous transfer */
 int helrm_TransferSync(void);
 
+/* ---- device-buffer exchange of ciphertexts between ranks (no reference
+ * counterpart: the reference runs on one GPU; this is the table-sharded
+ * layer's exchange step).  The buffers are device memory of the scheme's
+ * GPU, e.g. the tensor a collective reduces. ------------------------------ */
+/* copy n ciphertexts' residues [npoly][level+1][N] into d_out, item i at
+ * i * words_each; returns after the copies have finished */
+int helrm_CiphertextsToDevice(const int *ids, int n, uint64_t *d_out, size_t words_each);
+/* n new ciphertexts [npoly][level+1][N] from d_in holding per-limb 64-bit
+ * sums of residues (several ranks' partial ciphertexts added as integers);
+ * every word is reduced modulo its limb's prime on import.  d_in must be
+ * complete before the call (the library orders only its own stream). */
+int helrm_NewCiphertextsFromDeviceSum(const uint64_t *d_in, int n, int level, int npoly, double scale,
+                                      int *out_ids);
+
 /* ---- kernel-level entry points on device pointers (microbenchmarks) --------- */
 /* Forward / inverse NTT in place on nrows limbs laid out as blocks of
  * `per` rows (nq main-prime rows then special-prime rows). */
