@@ -94,7 +94,7 @@ class ShardedEmbedding:
     B200Library scheme: the shard's transform, its rotation keys and the
     mask plaintext, and evaluate() for a batch of selector ciphertexts."""
 
-    def __init__(self, lib, M: np.ndarray, tables: range, level: int, ratio: float = 2.0):
+    def __init__(self, lib, M: np.ndarray, tables: range, level: int, ratio: float | None = None):
         self.lib = lib
         info = lib.scheme_info()
         self.slots = info["slots"]
@@ -106,7 +106,11 @@ class ShardedEmbedding:
         self.diags = diags
         data = np.concatenate([diags[k].astype(np.float64) for k in self.ks])
         self.level = level
-        self.lt = lib.GenerateLinearTransform(self.ks, data, level, ratio, "none")
+        # baby-step stride 32 (ratio 1024 / diagonals, at least the
+        # reference's 2): every shard size runs the full-chunk MAC and as
+        # few giant-step key switches as the unsharded transform's 16 groups allow
+        self.ratio = float(ratio) if ratio else max(2.0, 1024.0 / len(self.ks))
+        self.lt = lib.GenerateLinearTransform(self.ks, data, level, self.ratio, "none")
         for k in lib.GetLinearTransformRotationKeys(self.lt):
             lib.GenerateLinearTransformRotationKey(k)
         for i in range(1, self.rot + 1):

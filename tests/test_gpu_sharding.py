@@ -92,7 +92,7 @@ def test_shard_partial_bit_exact_vs_oracle(pair):
     se = S.ShardedEmbedding(pair.lib, M, tb, level)
     out = se.evaluate(cts)[0]
     o = pair.o
-    plan = W.bsgs_plan(se.ks, 2.0, pair.slots)
+    plan = W.bsgs_plan(se.ks, se.ratio, pair.slots)
     gal = {o.galois(d) for d in plan["rotation_keys"]} | {o.galois(pair.slots >> i) for i in range(1, se.rot + 1)}
     keys = {g: pair.key(g) for g in gal}
     pts = [pair.lib.GetLinearTransformPlaintext(se.lt, k) for k in se.ks]
