@@ -36,6 +36,11 @@
 #define HB_LT_GIANT_GROUP 3
 #endif
 static_assert(HB_LT_GIANT_GROUP >= 1 && HB_LT_GIANT_GROUP <= HB_MAX_GIANTS, "giant group size");
+// Ciphertexts per launch of the CUDA-core baby-step MAC (HELRM_B200_MAC_CHUNK
+// overrides).
+#ifndef HB_MAC_CT_CHUNK
+#define HB_MAC_CT_CHUNK 64
+#endif
 
 namespace hb {
 
@@ -1276,8 +1281,17 @@ public:
                 bsgs_baby_mac_special(inner, in, D, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, nb, cts_,
                                       (size_t)beta * es, (size_t)nslots * 2 * es, stream);
             } else {
-                bsgs_baby_mac(inner, in, D, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, nb, cts_,
-                              (size_t)beta * es, (size_t)nslots * 2 * es, stream);
+                // ciphertexts in chunks: one limb's rotated-digit gather set for
+                // the chunk (chunk x (beta + 1) rows) stays L2-resident across the
+                // waves of blocks, at the price of the chunk's keys and
+                // plaintexts streaming once per chunk
+                const int cc = mac_ct_chunk();
+                for (int c0 = 0; c0 < nb; c0 += cc) {
+                    const int n = std::min(cc, nb - c0);
+                    bsgs_baby_mac(inner + (size_t)c0 * nslots * 2 * es, in + (size_t)c0 * cts_,
+                                  D + (size_t)c0 * beta * es, ch, nq, K, L, beta, P, t.level + 1, d_pmod, logN, n,
+                                  cts_, (size_t)beta * es, (size_t)nslots * 2 * es, stream);
+                }
             }
         }
         release(D);
@@ -1338,6 +1352,15 @@ public:
 
     // giant steps per key multiplication in the LT (four digits)
     static int lt_group() { return HB_LT_GIANT_GROUP; }
+    // ciphertexts per launch of the CUDA-core baby-step MAC
+    static int mac_ct_chunk() {
+        static int v = [] {
+            const char *e = std::getenv("HELRM_B200_MAC_CHUNK");
+            const int x = e && *e ? std::atoi(e) : HB_MAC_CT_CHUNK;
+            return x > 0 ? x : HB_MAC_CT_CHUNK;
+        }();
+        return v;
+    }
     size_t lt_bytes_per_ct(const LinTrans &t, int nq) {
         const int ne = nq + K, beta = beta_of(nq);
         const size_t es = (size_t)ne * N * 8;
