@@ -545,6 +545,7 @@ def run_b200(args, dist):
     if dist.world == 1 and not args.small and not args.no_cfg3:
         from helrm_b200 import microbench
         cfg3 = microbench.run(batches=(1, 16, 128), reps=3, device=dev)
+        cfg3.append(microbench.run_table_matmul(device=dev))
         for r in cfg3:
             if r["op"] == "hoisted_keyswitch_R32" and r["batch"] == 16:
                 keyswitch = {"GBps": r["GBps"], "frac_hbm": r["frac_hbm"], "batch": 16, "rotations": 32,

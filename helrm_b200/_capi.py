@@ -100,6 +100,14 @@ SIGNATURES = {
     "helrm_UploadCiphertextsAsync": [P(c_void), c_int, c_int, c_int, c_double, P(c_int)],
     "helrm_DownloadCiphertextsAsync": [P(c_int), c_int, P(c_void), c_size],
     "helrm_TransferSync": [],
+    "helrm_EncodeConstantNew": [c_double, c_int, c_double, P(c_int)],
+    "helrm_DeleteConstant": [c_int],
+    "helrm_MulConstantAccumNew": [P(c_int), P(c_int), c_int, P(c_int)],
+    "helrm_PackConstantTableNew": [P(c_int), c_int, c_int, P(c_int)],
+    "helrm_PackPlaintextTableNew": [P(c_int), c_int, c_int, P(c_int)],
+    "helrm_DeleteTable": [c_int],
+    "helrm_GetTableShape": [c_int, P(c_int), P(c_int), P(c_int)],
+    "helrm_MulTableMatMulNew": [P(c_int), c_int, c_int, P(c_int)],
     "helrm_CiphertextsToDevice": [P(c_int), c_int, c_void, c_size],
     "helrm_NewCiphertextsFromDeviceSum": [c_void, c_int, c_int, c_int, c_double, P(c_int)],
     "helrm_kernel_ntt": [c_void, c_int, c_int, c_int, c_int, c_void],

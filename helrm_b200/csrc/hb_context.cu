@@ -159,6 +159,21 @@ public:
     std::unordered_map<int, Ct> cts;
     std::unordered_map<int, Pt> pts;
     std::unordered_map<int, std::unique_ptr<LinTrans>> lts;
+    // broadcast constants (one word per prime) and the IVE lookup's tables
+    struct Konst {
+        int level = 0;
+        double scale = 1.0;
+        std::vector<u64> words;  // [level + 1]
+    };
+    struct Table {
+        int rows = 0, cols = 0, level = 0;
+        double scale = 1.0;
+        bool pt = false;
+        double *tab = nullptr;        // constants [nq][rows][cols] (device)
+        std::vector<int> pt_ids;      // plaintext table, row-major (kept by id)
+    };
+    std::unordered_map<int, Konst> konsts;
+    std::unordered_map<int, Table> tables;
     int next_id = 1;
     u64 enc_counter = 0;
     // memory accounting
@@ -560,7 +575,10 @@ public:
             release(d_rlk);
             release(d_sk);
             for (auto &t : lv) release(t.blob);
+            for (auto &kv : tables) release(kv.second.tab);
             release(d_pmod);
+            release(d_cls8);
+            release(d_tc_err);
             release(d_tables);
             if (up) {
                 cudaStreamSynchronize(up);
@@ -1114,6 +1132,135 @@ public:
         }
         for (auto *p : tmps) release(p);
         return put_ct(o);
+    }
+
+    // ---------------------------------------------------------- broadcast constants and tables
+    int encode_constant(double v, int level, double sc) {
+        if (level < 0 || level >= L) HB_THROW(HB_EINVAL, "EncodeConstantNew: level out of range");
+        const long double x = (long double)v * (long double)sc;
+        if (!(std::fabs((double)x) < 9.2e18)) HB_THROW(HB_EINVAL, "EncodeConstantNew: scalar * scale beyond 2^63");
+        const long long r = std::llroundl(x);
+        Konst k;
+        k.level = level;
+        k.scale = sc;
+        for (int i = 0; i <= level; i++) {
+            const long long m = (long long)(r % (long long)primes[i]);
+            k.words.push_back((u64)(m < 0 ? m + (long long)primes[i] : m));
+        }
+        const int id = next_id++;
+        konsts[id] = std::move(k);
+        return id;
+    }
+    const Konst &konst(int id) {
+        auto it = konsts.find(id);
+        if (it == konsts.end()) HB_THROW(HB_ENOENT, "constant " + std::to_string(id) + " not found");
+        return it->second;
+    }
+    Table &table(int id) {
+        auto it = tables.find(id);
+        if (it == tables.end()) HB_THROW(HB_ENOENT, "table " + std::to_string(id) + " not found");
+        return it->second;
+    }
+    int pack_constant_table(const int *ids, int n, int rows) {
+        if (rows <= 0 || n <= 0 || n % rows) HB_THROW(HB_EINVAL, "PackConstantTableNew: ids must be a non-empty rows x cols table");
+        Table t;
+        t.rows = rows;
+        t.cols = n / rows;
+        const Konst &k0 = konst(ids[0]);
+        t.level = k0.level;
+        t.scale = k0.scale;
+        const int nq = t.level + 1;
+        std::vector<double> h((size_t)nq * n);
+        for (int i = 0; i < n; i++) {
+            const Konst &k = konst(ids[i]);
+            if (k.level != t.level) HB_THROW(HB_EINVAL, "PackConstantTableNew: all constants must share one level");
+            if (std::fabs(k.scale - t.scale) > 1e-9 * t.scale)
+                HB_THROW(HB_EINVAL, "PackConstantTableNew: all constants must share one scale");
+            for (int e = 0; e < nq; e++) h[(size_t)e * n + i] = (double)k.words[e];
+        }
+        t.tab = (double *)alloc(h.size());
+        cuda_check(cudaMemcpyAsync(t.tab, h.data(), h.size() * 8, cudaMemcpyHostToDevice, stream), "table");
+        sync();
+        const int id = next_id++;
+        tables[id] = std::move(t);
+        return id;
+    }
+    int pack_plaintext_table(const int *ids, int n, int rows) {
+        if (rows <= 0 || n <= 0 || n % rows) HB_THROW(HB_EINVAL, "PackPlaintextTableNew: ids must be a non-empty rows x cols table");
+        Table t;
+        t.rows = rows;
+        t.cols = n / rows;
+        t.pt = true;
+        const Pt &p0 = pt(ids[0]);
+        t.level = p0.nq - 1;
+        t.scale = p0.scale;
+        for (int i = 0; i < n; i++) {
+            const Pt &p = pt(ids[i]);
+            if (p.nq != p0.nq) HB_THROW(HB_EINVAL, "PackPlaintextTableNew: all plaintexts must share one level");
+            if (std::fabs(p.scale - t.scale) > 1e-9 * t.scale)
+                HB_THROW(HB_EINVAL, "PackPlaintextTableNew: all plaintexts must share one scale");
+            t.pt_ids.push_back(ids[i]);
+        }
+        const int id = next_id++;
+        tables[id] = std::move(t);
+        return id;
+    }
+    void delete_table(int id) {
+        Table &t = table(id);
+        if (t.tab) release(t.tab);
+        tables.erase(id);
+    }
+    // rows new ciphertexts: sum_k T[r][k] * ct_k at the table's level
+    std::vector<int> table_matmul_ids(const int *cts, int n, Table &t) {
+        if (n != t.cols)
+            HB_THROW(HB_EINVAL, "table product: expected " + std::to_string(t.cols) + " ciphertexts, got " +
+                                    std::to_string(n));
+        const int nq = t.level + 1;
+        double cscale = 0.0;
+        std::vector<const u64 *> xp((size_t)2 * n);
+        for (int k = 0; k < n; k++) {
+            const Ct &c = ct(cts[k]);
+            if (c.npoly != 2) HB_THROW(HB_ESTATE, "table product: operand is degree-2; relinearize first");
+            if (c.nq < nq)
+                HB_THROW(HB_ESTATE, "table product: ciphertext at level " + std::to_string(c.nq - 1) +
+                                        " is below the table's level " + std::to_string(t.level));
+            if (k == 0) cscale = c.scale;
+            else if (std::fabs(c.scale - cscale) > 1e-9 * cscale)
+                HB_THROW(HB_ESTATE, "table product: inconsistent ciphertext scales");
+            xp[2 * k] = c.d;
+            xp[2 * k + 1] = c.d + (size_t)c.nq * N;
+        }
+        std::vector<int> outs;
+        std::vector<u64 *> op;
+        for (int r = 0; r < t.rows; r++) {
+            Ct o = new_ct(nq, 2, cscale * t.scale);
+            o.slots = ct(cts[0]).slots;
+            op.push_back(o.d);
+            outs.push_back(put_ct(o));
+        }
+        std::vector<const u64 *> pp;
+        if (t.pt)
+            for (int id : t.pt_ids) pp.push_back(pt(id).d);
+        // pointer arrays in device memory, freed behind the launch
+        u64 *dx = alloc(xp.size()), *dout = alloc(op.size()), *dpt = pp.empty() ? nullptr : alloc(pp.size());
+        cuda_check(cudaMemcpyAsync(dx, xp.data(), xp.size() * 8, cudaMemcpyHostToDevice, stream), "matmul ptrs");
+        cuda_check(cudaMemcpyAsync(dout, op.data(), op.size() * 8, cudaMemcpyHostToDevice, stream), "matmul ptrs");
+        if (dpt) cuda_check(cudaMemcpyAsync(dpt, pp.data(), pp.size() * 8, cudaMemcpyHostToDevice, stream), "matmul ptrs");
+        MatMulArgs a{};
+        a.out = (u64 *const *)dout;
+        a.x = (const u64 *const *)dx;
+        a.tab = t.tab;
+        a.pts = (const u64 *const *)dpt;
+        a.rows = t.rows;
+        a.cols = t.cols;
+        a.nq = nq;
+        a.logN = logN;
+        table_matmul(a, t.pt, stream);
+        release(dx);
+        release(dout);
+        if (dpt) release(dpt);
+        sync();  // the host pointer arrays above go out of scope
+        return outs;
     }
 
     // ---------------------------------------------------------- linear transforms
@@ -1966,6 +2113,68 @@ HB_API int helrm_HybridFoldBatch(const int *cts, int n, int rotations) {
     });
 }
 
+HB_API int helrm_EncodeConstantNew(double scalar, int level, double scale, int *out) {
+    return guard([&] {
+        OUT(out);
+        *out = C().encode_constant(scalar, level, scale);
+    });
+}
+HB_API int helrm_DeleteConstant(int id) {
+    return guard([&] {
+        Context &c = C();
+        c.konst(id);
+        c.konsts.erase(id);
+    });
+}
+HB_API int helrm_MulConstantAccumNew(const int *cts, const int *consts, int n, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        if (!cts || !consts || n <= 0) HB_THROW(HB_EINVAL, "MulConstantAccumNew: bad arguments");
+        const int t = c.pack_constant_table(consts, n, 1);
+        try {
+            *out = c.table_matmul_ids(cts, n, c.table(t))[0];
+        } catch (...) {
+            c.delete_table(t);
+            throw;
+        }
+        c.delete_table(t);
+    });
+}
+HB_API int helrm_PackConstantTableNew(const int *consts, int n, int rows, int *out) {
+    return guard([&] {
+        OUT(out);
+        if (!consts) HB_THROW(HB_EINVAL, "PackConstantTableNew: null ids");
+        *out = C().pack_constant_table(consts, n, rows);
+    });
+}
+HB_API int helrm_PackPlaintextTableNew(const int *pts, int n, int rows, int *out) {
+    return guard([&] {
+        OUT(out);
+        if (!pts) HB_THROW(HB_EINVAL, "PackPlaintextTableNew: null ids");
+        *out = C().pack_plaintext_table(pts, n, rows);
+    });
+}
+HB_API int helrm_DeleteTable(int table) {
+    return guard([&] { C().delete_table(table); });
+}
+HB_API int helrm_GetTableShape(int table, int *rows, int *cols, int *level) {
+    return guard([&] {
+        Context::Table &t = C().table(table);
+        if (rows) *rows = t.rows;
+        if (cols) *cols = t.cols;
+        if (level) *level = t.level;
+    });
+}
+HB_API int helrm_MulTableMatMulNew(const int *cts, int n, int table, int *outs) {
+    return guard([&] {
+        Context &c = C();
+        OUT(outs);
+        if (!cts) HB_THROW(HB_EINVAL, "MulTableMatMulNew: null ids");
+        std::vector<int> o = c.table_matmul_ids(cts, n, c.table(table));
+        for (size_t i = 0; i < o.size(); i++) outs[i] = o[i];
+    });
+}
 HB_API int helrm_DeleteCiphertext(int ct) {
     return guard([&] {
         if (g_ctx) g_ctx->del_ct(ct);

@@ -2012,6 +2012,99 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
     check_launch("bsgs_mac");
 }
 
+// ---- one-pass plaintext x ciphertext matrix products (the IVE lookup) ------------
+// out_r = sum_k T[r][k] * ct_k for a rows x cols table T of broadcast
+// constants (one word per prime) or of plaintext polynomials, every input
+// ciphertext read once for all rows of the launch (the reference's
+// ConstMatMulKernel / PlaintextMatMulKernel, cheddar_pybind.cu:1044-1569).
+// One thread per coefficient position of one (poly, limb) row; RB rows
+// accumulated as exact centred FP64 remainders (each below 0.502 q < 2^35.1
+// for q < 2^40, so up to 2^17 terms sum exactly) and reduced once.
+constexpr int kMmKT = 64;  // table columns staged per shared-memory tile
+
+template <int RB, bool PT>
+__global__ void __launch_bounds__(256) k_table_matmul(MatMulArgs a) {
+    __shared__ double2 s_c[RB * kMmKT];          // constants as {c, fl(c/q)}
+    __shared__ const u64 *s_p[RB * kMmKT];       // or plaintext limb pointers
+    __shared__ const u64 *s_x[kMmKT];            // input ciphertext rows
+    const int N = 1 << a.logN;
+    const int rowid = blockIdx.y;                // poly * nq + limb
+    const int pl = rowid / a.nq, e = rowid - pl * a.nq;
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const PrimeConst pc = c_pc[e];
+    const double qd = u64_to_d(pc.q);
+    double acc[RB];
+#pragma unroll
+    for (int r = 0; r < RB; r++) acc[r] = 0.0;
+    const int rows = min(RB, a.rows - a.r0);
+    for (int k0 = 0; k0 < a.cols; k0 += kMmKT) {
+        const int kt = min(kMmKT, a.cols - k0);
+        __syncthreads();
+        for (int t = threadIdx.x; t < RB * kt; t += blockDim.x) {
+            const int r = t / kt, kk = t - r * kt;
+            if (PT) {
+                s_p[r * kMmKT + kk] = r < rows ? a.pts[(size_t)(a.r0 + r) * a.cols + k0 + kk] + ((size_t)e << a.logN)
+                                               : nullptr;
+            } else {
+                const double c = r < rows ? a.tab[((size_t)e * a.rows + a.r0 + r) * a.cols + k0 + kk] : 0.0;
+                s_c[r * kMmKT + kk] = make_double2(c, __dmul_rn(c, pc.qinv));
+            }
+        }
+        for (int t = threadIdx.x; t < kt; t += blockDim.x)
+            s_x[t] = a.x[(size_t)(k0 + t) * 2 + pl] + ((size_t)e << a.logN);
+        __syncthreads();
+        if (n < N) {
+            for (int kk = 0; kk < kt; kk++) {
+                const double y = u64_to_d(__ldcs(s_x[kk] + n));
+#pragma unroll
+                for (int r = 0; r < RB; r++) {
+                    if (PT) {
+                        if (r < rows) {
+                            const double w = u64_to_d(__ldg(s_p[r * kMmKT + kk] + n));
+                            acc[r] = __dadd_rn(acc[r], mulmod_d(y, make_double2(w, __dmul_rn(w, pc.qinv)), qd));
+                        }
+                    } else {
+                        acc[r] = __dadd_rn(acc[r], mulmod_d(y, s_c[r * kMmKT + kk], qd));
+                    }
+                }
+            }
+        }
+    }
+    if (n < N) {
+#pragma unroll
+        for (int r = 0; r < RB; r++)
+            if (r < rows) a.out[a.r0 + r][((size_t)rowid << a.logN) + n] = d_mod_to_u64(acc[r], qd, pc.qinv);
+    }
+}
+
+void table_matmul(const MatMulArgs &args, bool pt, cudaStream_t s) {
+    if (args.cols <= 0 || args.rows <= 0 || args.cols > (1 << 16))
+        throw std::invalid_argument("table_matmul: bad table shape");
+    for (int i = 0; i < args.nq; i++)
+        if (g_host_q[i] >= (1ull << 40)) throw std::invalid_argument("table_matmul: primes of 40 bits and more");
+    const int N = 1 << args.logN;
+    const double words = (double)args.nq * N;
+    for (int r0 = 0; r0 < args.rows; r0 += 16) {
+        MatMulArgs a = args;
+        a.r0 = r0;
+        const int rb = std::min(16, args.rows - r0);
+        // per pass: every input ciphertext once, the rows written once, and
+        // the plaintexts (a plaintext table) once
+        ProfScope ps(KC_ELEMENTWISE,
+                     8.0 * words * (2.0 * args.cols + 2.0 * rb + (pt ? (double)rb * args.cols : 0.0)),
+                     2.0 * words * rb * args.cols, s, 1);
+        const dim3 grid((N + 255) / 256, 2 * args.nq);
+#define HB_MM(RB_)                                                                 \
+    (pt ? (void)k_table_matmul<RB_, true><<<grid, 256, 0, s>>>(a)                   \
+        : (void)k_table_matmul<RB_, false><<<grid, 256, 0, s>>>(a))
+        if (rb == 1) HB_MM(1);
+        else if (rb <= 4) HB_MM(4);
+        else HB_MM(16);
+#undef HB_MM
+        check_launch("table_matmul");
+    }
+}
+
 // ---- the tensor-core MAC (hb_bsgs_tc.cuh) ------------------------------------
 bool bsgs_mma_supported(int nq, int beta) {
     if (beta < 1 || beta > 4 || nq < 1 || nq > g_host_nq) return false;

@@ -220,6 +220,18 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
                    int beta, int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride,
                    size_t d_stride, size_t inner_stride, cudaStream_t s);
 
+// ---- one-pass table x ciphertext-vector products (IVE lookup) -----------------
+struct MatMulArgs {
+    u64 *const *out;          // device array: rows output ciphertexts [2][nq][N]
+    const u64 *const *x;      // device array: 2 * cols pointers (poly 0, poly 1 of each input)
+    const double *tab;        // constants [nq][rows][cols] (exact doubles), or null
+    const u64 *const *pts;    // plaintext table [rows][cols] of q-row pointers, or null
+    int rows, cols, nq, logN;
+    int r0;                   // first row of the launch (set by the launcher)
+};
+// out_r = sum_k T[r][k] * x_k over the q rows of every limb; primes below 2^40
+void table_matmul(const MatMulArgs &args, bool pt, cudaStream_t s);
+
 // ---- the same MAC on the tensor cores (q rows; hb_bsgs_tc.cuh) ----------------
 // Usable when every q row prime is below 2^37, the chunk has at most 32
 // babies and 16 giant slots, and beta is 1..4.

@@ -164,15 +164,72 @@ def run(batches=(1, 16, 128), reps=5, ops="ntt,intt,aut,mac,rescale,ks", rotatio
     return results
 
 
+def run_table_matmul(rows=16, cols=64, level=23, reps=3, device=0) -> dict:
+    """The IVE lookup's one-pass table product at LogN 16 (config 2/3
+    primes): a rows x cols table of broadcast constants against cols
+    ciphertexts, MulConstantMatMulNew (each input read once) against rows
+    calls of MulConstantAccumNew (the inputs re-read per row), CUDA events
+    on the library stream.  Algorithmic bytes: the inputs once and the
+    outputs once."""
+    import ctypes
+
+    from helrm_b200 import B200Library, _capi
+    from helrm_b200.params import CFG2, CFG2_DNUM
+
+    lib = B200Library(dnum=CFG2_DNUM, seed=9, device=device)
+    lib.setup_bindings(CFG2)
+    try:
+        lib.GenerateSecretKey()
+        info = lib.scheme_info()
+        slots, N = info["slots"], info["N"]
+        rng = np.random.default_rng(0)
+        cts = []
+        for _ in range(cols):
+            pt = lib.Encode(list(rng.uniform(-1, 1, slots)), level, float(1 << CFG2.logscale))
+            cts.append(lib.Encrypt(pt))
+            lib.DeletePlaintext(pt)
+        kids = [lib.EncodeConstantNew(float(v), level, 2.0 ** 20) for v in rng.uniform(-1, 1, rows * cols)]
+        tab = lib.PackConstantTableNew(kids, rows)
+        capi = _capi.load()
+
+        def timed(fn):
+            for _ in range(2):
+                for o in fn():
+                    lib.DeleteCiphertext(o)
+            lib.Synchronize()
+            _capi.check(capi.helrm_TimerStart())
+            for _ in range(reps):
+                for o in fn():
+                    lib.DeleteCiphertext(o)
+            ms = ctypes.c_double(0)
+            _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+            return ms.value / reps
+
+        one = timed(lambda: lib.MulConstantMatMulNew(cts, tab))
+        per_row = timed(lambda: [lib.MulConstantAccumNew(cts, kids[r * cols:(r + 1) * cols]) for r in range(rows)])
+        limb = N * 8
+        nbytes = (cols + rows) * 2 * (level + 1) * limb
+        peak, src = _peak()
+        lib.DeleteConstantTable(tab)
+        return {"op": "ive_table_matmul", "rows": rows, "cols": cols, "level": level, "ms_one_pass": one,
+                "ms_row_at_a_time": per_row, "GBps_one_pass": nbytes / (one * 1e6),
+                "frac_hbm": nbytes / (one * 1e6) / peak, "peak": f"{peak} GB/s ({src})"}
+    finally:
+        lib.DeleteScheme()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batches", default="1,16,128")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--ops", default="ntt,intt,aut,mac,rescale,ks")
     ap.add_argument("--rotations", type=int, default=32)
+    ap.add_argument("--table", action="store_true", help="also the IVE lookup's one-pass table product")
     args = ap.parse_args()
     run([int(b) for b in args.batches.split(",")], args.reps, args.ops, args.rotations,
         emit=lambda line: print(json.dumps(line), flush=True))
+    if args.table:
+        print(json.dumps(run_table_matmul()), flush=True)
 
 
 if __name__ == "__main__":

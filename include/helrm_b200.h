@@ -158,6 +158,29 @@ int helrm_HybridFoldBatch(const int *cts, int n, int rotations);
 /* Rescale n ciphertexts in place. */
 int helrm_RescaleBatch(const int *cts, int n);
 
+/* ---- broadcast constants and the one-pass table products of the IVE lookup
+ * (cheddar bindings.py:621-706; cheddar_pybind.cu:1044-1569).  A constant is
+ * round(scalar * scale) mod q_i, one word per prime; a table is rows x cols
+ * constants or plaintexts, row-major.  The products read every input
+ * ciphertext once for all rows; outputs carry scale ct * table and are not
+ * rescaled.  Ciphertexts above the table's level are read at its level;
+ * primes below 2^40. */
+/* EncodeConstantNew -- bindings.py:621-630 */
+int helrm_EncodeConstantNew(double scalar, int level, double scale, int *out);
+int helrm_DeleteConstant(int id);
+/* MulConstantAccumNew -- sum_i c_i * ct_i, bindings.py:635-643 */
+int helrm_MulConstantAccumNew(const int *cts, const int *consts, int n, int *out);
+/* PackConstantTableNew / PackPlaintextTableNew -- bindings.py:645-686
+ * (a plaintext table refers to its plaintexts by id: keep them alive) */
+int helrm_PackConstantTableNew(const int *consts, int n, int rows, int *out_table);
+int helrm_PackPlaintextTableNew(const int *pts, int n, int rows, int *out_table);
+/* DeleteConstantTable / DeletePlaintextTable -- bindings.py:656-687 */
+int helrm_DeleteTable(int table);
+int helrm_GetTableShape(int table, int *rows, int *cols, int *level);
+/* MulConstantMatMulNew / MulPlaintextMatMulNew -- bindings.py:659-697:
+ * n = cols input ciphertexts, rows ids written to outs */
+int helrm_MulTableMatMulNew(const int *cts, int n, int table, int *outs);
+
 /* ---- metadata (tensors.go:35-104; cheddar bindings.py:1278-1320) ------------- */
 int helrm_DeleteCiphertext(int ct);
 int helrm_DeletePlaintext(int pt);
