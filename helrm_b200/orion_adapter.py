@@ -10,10 +10,15 @@ orion (the reference checkout on PYTHONPATH) before calling it.
 from __future__ import annotations
 
 _installed = False
+_factory = None
 
 
-def install() -> None:
-    global _installed
+def install(factory=None) -> None:
+    """Register ``backend: b200``.  ``factory`` builds the backend object
+    (default: ``B200Library()``); a test may pass a stand-in with the same
+    methods."""
+    global _installed, _factory
+    _factory = factory
     if _installed:
         return
     import orion.core.orion as orion_mod
@@ -37,8 +42,11 @@ def install() -> None:
 
     def setup_backend(self, params):
         if params.get_backend() == "b200":
-            from .library import B200Library
-            lib = B200Library()
+            if _factory is not None:
+                lib = _factory()
+            else:
+                from .library import B200Library
+                lib = B200Library()
             lib.setup_bindings(params)
             return lib
         return orig_setup(self, params)

@@ -82,3 +82,17 @@ def test_product_path_has_no_oracle_dependency():
             if f.endswith((".py", ".cu", ".cuh", ".cpp", ".hpp")):
                 txt = open(os.path.join(dirpath, f), errors="ignore").read()
                 assert "ckks_oracle" not in txt and "from oracle" not in txt and "import oracle" not in txt, f
+
+
+def test_orion_trace_methods_exist_on_backend():
+    """Every backend method the reference's Orion called in the recorded
+    flows (tests/golden/orion_trace.json) exists on B200Library."""
+    import json
+    import os
+    from helrm_b200 import B200Library
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "orion_trace.json")
+    with open(path) as f:
+        trace = json.load(f)
+    methods = {c["m"] for t in trace.values() for c in t["calls"]}
+    assert {"GenerateLinearTransform", "EvaluateLinearTransform", "RescaleNew", "AddPlaintext"} <= methods
+    assert [m for m in methods if not hasattr(B200Library, m)] == []
