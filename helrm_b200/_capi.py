@@ -108,6 +108,9 @@ SIGNATURES = {
     "helrm_DeleteTable": [c_int],
     "helrm_GetTableShape": [c_int, P(c_int), P(c_int), P(c_int)],
     "helrm_MulTableMatMulNew": [P(c_int), c_int, c_int, P(c_int)],
+    "helrm_EvaluatePolynomial": [c_int, P(c_double), c_int, c_int, c_double, P(c_int)],
+    "helrm_EvaluatePolynomialBatch": [P(c_int), c_int, P(c_double), c_int, c_int, c_double, P(c_int)],
+    "helrm_PolynomialPlanInfo": [c_int, c_double, P(c_double), c_int, c_int, c_double, P(c_int)],
     "helrm_CiphertextsToDevice": [P(c_int), c_int, c_void, c_size],
     "helrm_NewCiphertextsFromDeviceSum": [c_void, c_int, c_int, c_int, c_double, P(c_int)],
     "helrm_kernel_ntt": [c_void, c_int, c_int, c_int, c_int, c_void],

@@ -110,6 +110,260 @@ struct LinTrans {
     std::vector<int> giant_of_slot;   // slot -> g
 };
 
+// ---- polynomial evaluation plans --------------------------------------------
+// EvaluatePolynomial (orion/backend/python/poly_evaluator.py:25-35, bound by
+// orion/backend/cheddar/bindings.py:1102-1116 to the native EvalPoly of
+// cheddar_pybind.cu:2207-2262) evaluates sum_j c_j T_j(x) (Chebyshev basis)
+// or sum_j c_j x^j with ceil(log2(d+1)) levels, the depth orion/nn/
+// activation.py:22-28,101-110 places the layers with, and returns exactly the
+// requested output scale.  The evaluation is the baby-step giant-step
+// recursion (Paterson-Stockmeyer in the Chebyshev basis, as published by
+// Bossuat, Mouchet, Troncoso-Pastoriza and Hubaux, Eurocrypt 2021):
+//   p = q * T_{2^k} + r,  2^k <= deg p < 2^(k+1),
+// with q evaluated one level higher at scale S q_{L+1} / s(T_{2^k}), the
+// product and the remainder's leaf sum  sum_i round(r_i S q_{L+1} / s_i) T_i
+// + round(r_0 S q_{L+1})  added before one rescale, so every node lands on
+// its target scale exactly.  A node is a leaf when all its powers are in the
+// basis (T_1..T_bs and the powers of two) at a level above its target.  In
+// the basis, T_{a+b} = 2 T_a T_b - T_{a-b} is formed before its rescale as
+// 2 T_a T_b - K T_{a-b}, K = round(s_a s_b / s_{a-b}) (an integer multiple:
+// no level, a relative scale error below 2^-36), and T_{2a} = 2 T_a^2 - 1.
+// The host builds the whole evaluation as a plan of four device operations
+// (product with relinearization, linear combination, rescale, add), picks
+// the baby-step count bs in {2, 4, .., 32} with the fewest products, and
+// replays the plan over a batch of ciphertexts.
+enum { PO_MUL, PO_LIN, PO_RESCALE, PO_ADD };
+struct PolyOp {
+    int kind = 0;
+    int out = 0, a = -1, b = -1;  // value ids
+    int t0 = 0, nt = 0;           // PO_LIN: operand value ids terms[t0 .. t0 + nt)
+    size_t coef = 0;              // PO_LIN: offset of the [nt][nq] residues in consts
+    long k0 = -1;                 // PO_LIN: offset of the [nq] constant's residues, or -1
+};
+struct PolyPlan {
+    int bs = 0, depth = 0, products = 0, rescales = 0;
+    double target = 0;
+    std::vector<PolyOp> ops;
+    std::vector<int> terms;
+    std::vector<int> vnq;        // rows per polynomial of each value (value 0 = the input)
+    std::vector<double> vscale;
+    std::vector<int> last_use;   // index of the last op reading each value
+    std::vector<u64> consts;     // host residues
+    u64 *d_consts = nullptr;
+    int out = 0;
+};
+
+static int poly_ceil_log2(long v) {
+    int k = 0;
+    while ((1L << k) < v) k++;
+    return k;
+}
+static long poly_floor_pow2(long v) {
+    long p = 1;
+    while (p * 2 <= v) p *= 2;
+    return p;
+}
+static int poly_degree(const std::vector<double> &c) {
+    int d = (int)c.size() - 1;
+    while (d > 0 && c[d] == 0.0) d--;
+    return d < 0 ? 0 : d;
+}
+
+class PolyPlanner {
+public:
+    PolyPlanner(const std::vector<u64> &primes, bool cheb, int nq0, double s1, int bs)
+        : primes_(primes), cheb_(cheb), nq0_(nq0), bs_(bs) {
+        p.bs = bs;
+        value(nq0, s1);
+        tv_[1] = 0;
+    }
+    // plan the evaluation of c to `levels` levels below the input at scale S
+    PolyPlan build(const std::vector<double> &c, int levels, double S) {
+        const int L = nq0_ - 1 - levels;
+        if (L < 0) HB_THROW(HB_ESTATE, "EvaluatePolynomial: not enough levels for the polynomial's degree.");
+        p.depth = levels;
+        p.target = S;
+        p.out = eval(c, L, S);
+        p.last_use.assign(p.vnq.size(), -1);
+        for (size_t i = 0; i < p.ops.size(); i++) {
+            const PolyOp &o = p.ops[i];
+            if (o.a >= 0) p.last_use[o.a] = (int)i;
+            if (o.b >= 0) p.last_use[o.b] = (int)i;
+            for (int t = 0; t < o.nt; t++) p.last_use[p.terms[o.t0 + t]] = (int)i;
+        }
+        return std::move(p);
+    }
+
+private:
+    typedef std::vector<std::pair<int, double>> Terms;
+    const std::vector<u64> &primes_;
+    bool cheb_;
+    int nq0_, bs_;
+    PolyPlan p;
+    std::map<long, int> tv_;  // power index -> value id
+
+    int value(int nq, double scale) {
+        p.vnq.push_back(nq);
+        p.vscale.push_back(scale);
+        return (int)p.vnq.size() - 1;
+    }
+    double q(int nq) const { return (double)primes_[nq - 1]; }
+    // round half away from zero, then one residue per prime of the first nq
+    void residues(double v, int nq) {
+        const double r = std::round(v);
+        if (!(std::fabs(r) < 1.0e38)) HB_THROW(HB_EINVAL, "EvaluatePolynomial: a coefficient times its scale overflows");
+        const hi128 x = (hi128)r;
+        for (int i = 0; i < nq; i++) {
+            const u64 m = (u64)((hu128)(x < 0 ? -x : x) % primes_[i]);
+            p.consts.push_back(x < 0 && m ? primes_[i] - m : m);
+        }
+    }
+    int mul(int a, int b) {
+        const int nq = std::min(p.vnq[a], p.vnq[b]);
+        const int v = value(nq, p.vscale[a] * p.vscale[b]);
+        PolyOp o;
+        o.kind = PO_MUL, o.out = v, o.a = a, o.b = b;
+        p.ops.push_back(o);
+        p.products++;
+        return v;
+    }
+    int lin(int nq, double scale, const Terms &t, bool has_k0, double k0) {
+        if ((int)t.size() > HB_LC_MAX) HB_THROW(HB_ESTATE, "EvaluatePolynomial: leaf wider than the combination kernel");
+        const int v = value(nq, scale);
+        PolyOp o;
+        o.kind = PO_LIN, o.out = v, o.t0 = (int)p.terms.size(), o.nt = (int)t.size(), o.coef = p.consts.size();
+        for (auto &x : t) {
+            if (p.vnq[x.first] < nq) HB_THROW(HB_ESTATE, "EvaluatePolynomial: operand below the node's level");
+            p.terms.push_back(x.first);
+            residues(x.second, nq);
+        }
+        if (has_k0) {
+            o.k0 = (long)p.consts.size();
+            residues(k0, nq);
+        }
+        p.ops.push_back(o);
+        return v;
+    }
+    int rescale(int a, double scale) {
+        if (p.vnq[a] < 2) HB_THROW(HB_ESTATE, "EvaluatePolynomial: rescale below level 0");
+        const int v = value(p.vnq[a] - 1, scale);
+        PolyOp o;
+        o.kind = PO_RESCALE, o.out = v, o.a = a;
+        p.ops.push_back(o);
+        p.rescales++;
+        return v;
+    }
+    int add(int a, int b) {
+        if (p.vnq[a] != p.vnq[b]) HB_THROW(HB_ESTATE, "EvaluatePolynomial: adding nodes of different levels");
+        const int v = value(p.vnq[a], p.vscale[a]);
+        PolyOp o;
+        o.kind = PO_ADD, o.out = v, o.a = a, o.b = b;
+        p.ops.push_back(o);
+        return v;
+    }
+    bool pow2(long i) const { return (i & (i - 1)) == 0; }
+    int nq_of_power(long i) const { return nq0_ - poly_ceil_log2(i); }
+    // T_i (or x^i), its rows nq0 - ceil(log2 i)
+    int power(long i) {
+        auto it = tv_.find(i);
+        if (it != tv_.end()) return it->second;
+        int v;
+        if (!cheb_) {
+            const long a = pow2(i) ? i / 2 : poly_floor_pow2(i), b = i - a;
+            const int va = power(a), vb = power(b);
+            const int P = mul(va, vb);
+            v = rescale(P, p.vscale[P] / q(p.vnq[P]));
+        } else if (pow2(i)) {
+            const int va = power(i / 2);
+            const int P = mul(va, va);
+            const double sp = p.vscale[P];
+            const int Lv = lin(p.vnq[P], sp, Terms{{P, 2.0}}, true, -sp);
+            v = rescale(Lv, sp / q(p.vnq[P]));
+        } else {
+            const long a = poly_floor_pow2(i), b = i - a, c = a - b;
+            const int va = power(a), vb = power(b), vc = power(c);
+            const int P = mul(va, vb);
+            const double sp = p.vscale[P];
+            const double K = std::round(sp / p.vscale[vc]);
+            const int Lv = lin(p.vnq[P], sp, Terms{{P, 2.0}, {vc, -K}}, false, 0.0);
+            v = rescale(Lv, sp / q(p.vnq[P]));
+        }
+        tv_[i] = v;
+        return v;
+    }
+    bool leafable(const std::vector<double> &c, int L) const {
+        for (size_t i = 1; i < c.size(); i++) {
+            if (c[i] == 0.0) continue;
+            if (!((long)i <= bs_ || pow2((long)i)) || nq_of_power((long)i) < L + 2) return false;
+        }
+        return true;
+    }
+    double leaf_terms(const std::vector<double> &c, double Sp, Terms &t) {
+        for (size_t i = 1; i < c.size(); i++) {
+            if (c[i] == 0.0) continue;
+            const int v = power((long)i);
+            t.push_back({v, (c[i] * Sp) / p.vscale[v]});
+        }
+        return c[0] * Sp;
+    }
+    // a ciphertext of c at level L (L + 1 rows) and scale exactly S
+    int eval(const std::vector<double> &c0, int L, double S) {
+        const int d = poly_degree(c0);
+        const std::vector<double> c(c0.begin(), c0.begin() + d + 1);
+        const double Sp = S * q(L + 2);
+        if (leafable(c, L)) {
+            Terms t;
+            const double k0 = leaf_terms(c, Sp, t);
+            if (t.empty()) t.push_back({power(1), 0.0});
+            return rescale(lin(L + 2, Sp, t, true, k0), S);
+        }
+        const long n2 = poly_floor_pow2(d);
+        std::vector<double> qv((size_t)(d - n2 + 1)), rv(c.begin(), c.begin() + n2);
+        if (cheb_) {
+            qv[0] = c[n2];
+            for (long i = 1; i <= d - n2; i++) {
+                qv[i] = 2.0 * c[n2 + i];
+                rv[n2 - i] -= c[n2 + i];
+            }
+        } else {
+            for (long i = 0; i <= d - n2; i++) qv[i] = c[n2 + i];
+        }
+        const int G = power(n2);
+        if (p.vnq[G] < L + 2) HB_THROW(HB_ESTATE, "EvaluatePolynomial: giant step below the node's level");
+        Terms t;
+        const bool qconst = poly_degree(qv) == 0;
+        if (qconst)
+            t.push_back({G, (qv[0] * Sp) / p.vscale[G]});
+        else
+            t.push_back({mul(eval(qv, L + 1, Sp / p.vscale[G]), G), 1.0});
+        if (leafable(rv, L)) {
+            const double k0 = leaf_terms(rv, Sp, t);
+            return rescale(lin(L + 2, Sp, t, true, k0), S);
+        }
+        const int R = eval(rv, L, S);
+        const int v = qconst ? lin(L + 2, Sp, t, false, 0.0) : t[0].first;
+        return add(rescale(v, S), R);
+    }
+};
+
+// the plan with the fewest products (then rescales) over bs = 2 .. 32
+static PolyPlan plan_polynomial(const std::vector<u64> &primes, bool cheb, int nq0, double s1,
+                                const std::vector<double> &c, double S) {
+    if (c.size() < 3) HB_THROW(HB_EINVAL, "EvaluatePolynomial: the native evaluation needs degree >= 2");
+    const int levels = poly_ceil_log2((long)c.size());
+    PolyPlan best;
+    bool have = false;
+    for (int bs = 2; bs <= 32 && bs <= (1 << levels); bs *= 2) {
+        PolyPlan cand = PolyPlanner(primes, cheb, nq0, s1, bs).build(c, levels, S);
+        if (!have || cand.products < best.products ||
+            (cand.products == best.products && cand.rescales < best.rescales)) {
+            best = std::move(cand);
+            have = true;
+        }
+    }
+    return best;
+}
+
 // ---- fixed scratch of the no-allocation rescale -----------------------------
 // Some callers must not allocate device memory at all: a host runtime that
 // reserves the whole HBM budget up front through its own allocator (an
@@ -174,6 +428,9 @@ public:
     };
     std::unordered_map<int, Konst> konsts;
     std::unordered_map<int, Table> tables;
+    // polynomial evaluation plans by basis, input rows and scale, output
+    // scale and coefficients (device residues uploaded once per plan)
+    std::map<std::string, PolyPlan> poly_plans;
     int next_id = 1;
     u64 enc_counter = 0;
     // memory accounting
@@ -576,6 +833,7 @@ public:
             release(d_sk);
             for (auto &t : lv) release(t.blob);
             for (auto &kv : tables) release(kv.second.tab);
+            for (auto &kv : poly_plans) release(kv.second.d_consts);
             release(d_pmod);
             release(d_cls8);
             release(d_tc_err);
@@ -913,15 +1171,21 @@ public:
         release(D);
     }
 
-    void relinearize(u64 *out, const u64 *in3, int nq) {
+    void relinearize(u64 *out, const u64 *in3, int nq) { relinearize_batch(out, in3, nq, 1); }
+
+    // nb degree-2 ciphertexts [nb][3][nq][N] -> [nb][2][nq][N]
+    void relinearize_batch(u64 *out, const u64 *in3, int nq, int nb) {
         const int ne = nq + K, beta = beta_of(nq);
-        u64 *D = alloc((size_t)beta * ne * N);
-        modup(D, in3 + (size_t)2 * nq * N, nq, 1, 0);
-        u64 *acc = alloc((size_t)2 * ne * N);
-        keymult(acc, D, d_rlk, 1, nq, K, L, beta, P, nullptr, false, logN, 1, 0, 0, 0, stream);
+        const size_t s3 = (size_t)3 * nq * N, s2 = (size_t)2 * nq * N;
+        u64 *D = alloc((size_t)nb * beta * ne * N);
+        modup(D, in3 + (size_t)2 * nq * N, nq, nb, s3);
+        u64 *acc = alloc((size_t)nb * 2 * ne * N);
+        keymult(acc, D, d_rlk, 1, nq, K, L, beta, P, nullptr, false, logN, nb, (size_t)beta * ne * N,
+                (size_t)2 * ne * N, 0, stream);
         release(D);
-        moddown(out, acc, nq, 1, 0, 0, in3, 1, 0);
-        moddown(out + (size_t)nq * N, acc + (size_t)ne * N, nq, 1, 0, 0, in3 + (size_t)nq * N, 1, 0);
+        moddown(out, acc, nq, nb, (size_t)2 * ne * N, s2, in3, 1, s3);
+        moddown(out + (size_t)nq * N, acc + (size_t)ne * N, nq, nb, (size_t)2 * ne * N, s2, in3 + (size_t)nq * N, 1,
+                s3);
         release(acc);
     }
 
@@ -1859,6 +2123,164 @@ static int mul_relin(Context &c, int a, int b) {
     return c.put_ct(o);
 }
 NEW_AND_INPLACE2(MulRelinCiphertext, mul_relin(c, a, b))
+
+// ---- polynomial evaluation ----------------------------------------------------
+static PolyPlan &poly_plan(Context &c, bool cheb, int nq0, double s1, const std::vector<double> &co, double S) {
+    std::string key;
+    auto put = [&](const void *p, size_t n) { key.append((const char *)p, n); };
+    const int b = cheb ? 1 : 0;
+    put(&b, sizeof b);
+    put(&nq0, sizeof nq0);
+    put(&s1, sizeof s1);
+    put(&S, sizeof S);
+    put(co.data(), co.size() * sizeof(double));
+    auto it = c.poly_plans.find(key);
+    if (it != c.poly_plans.end()) return it->second;
+    if (c.poly_plans.size() >= 64) {
+        for (auto &kv : c.poly_plans) c.release(kv.second.d_consts);
+        c.poly_plans.clear();
+    }
+    PolyPlan pl = plan_polynomial(c.primes, cheb, nq0, s1, co, S);
+    pl.d_consts = c.alloc(pl.consts.size());
+    cuda_check(cudaMemcpyAsync(pl.d_consts, pl.consts.data(), pl.consts.size() * 8, cudaMemcpyHostToDevice, c.stream),
+               "polynomial constants");
+    c.sync();
+    return c.poly_plans.emplace(key, std::move(pl)).first->second;
+}
+
+// replay a plan over nb ciphertexts of the plan's input rows and scale
+static std::vector<int> poly_run(Context &c, const PolyPlan &pl, const std::vector<int> &ids) {
+    const int nb = (int)ids.size();
+    const size_t N = c.N;
+    const size_t nv = pl.vnq.size();
+    std::vector<u64 *> vd(nv, nullptr);
+    std::vector<char> own(nv, 1);
+    auto stride = [&](int v) { return (size_t)2 * pl.vnq[v] * N; };
+    if (nb == 1) {
+        vd[0] = c.ct(ids[0]).d;
+        own[0] = 0;
+    } else {
+        std::vector<const Ct *> v;
+        for (int id : ids) v.push_back(&c.ct(id));
+        vd[0] = c.alloc((size_t)nb * stride(0));
+        c.gather_cts(vd[0], v, pl.vnq[0]);
+    }
+    for (size_t i = 0; i < pl.ops.size(); i++) {
+        const PolyOp &o = pl.ops[i];
+        const int nq = pl.vnq[o.out];
+        vd[o.out] = c.alloc((size_t)nb * stride(o.out));
+        if (o.kind == PO_MUL) {
+            u64 *t3 = c.alloc((size_t)nb * 3 * nq * N);
+            ew_tensor_batch(t3, vd[o.a], vd[o.b], nq, pl.vnq[o.a], pl.vnq[o.b], nb, stride(o.a), stride(o.b), c.logN,
+                            c.stream);
+            c.relinearize_batch(vd[o.out], t3, nq, nb);
+            c.release(t3);
+        } else if (o.kind == PO_LIN) {
+            LinCombArgs a{};
+            a.n = o.nt;
+            for (int t = 0; t < o.nt; t++) {
+                const int v = pl.terms[o.t0 + t];
+                a.x[t] = vd[v];
+                a.xs[t] = stride(v);
+                a.nq[t] = pl.vnq[v];
+            }
+            a.coef = pl.d_consts + o.coef;
+            a.k0 = o.k0 >= 0 ? pl.d_consts + o.k0 : nullptr;
+            ew_lincomb(vd[o.out], a, nq, nb, stride(o.out), c.logN, c.stream);
+        } else if (o.kind == PO_RESCALE) {
+            c.rescale(vd[o.out], vd[o.a], 2, pl.vnq[o.a], nb, stride(o.a), stride(o.out));
+        } else {
+            ew_add(vd[o.out], vd[o.a], vd[o.b], nb * 2 * nq, c.qmap(nq), c.logN, c.stream);
+        }
+        auto drop = [&](int v) {
+            if (v >= 0 && v != pl.out && own[v] && vd[v] && pl.last_use[v] == (int)i) {
+                c.release(vd[v]);
+                vd[v] = nullptr;
+            }
+        };
+        drop(o.a);
+        drop(o.b);
+        for (int t = 0; t < o.nt; t++) drop(pl.terms[o.t0 + t]);
+    }
+    std::vector<int> outs;
+    const int onq = pl.vnq[pl.out];
+    if (nb == 1) {
+        Ct o;
+        o.d = vd[pl.out];
+        o.nq = onq;
+        o.npoly = 2;
+        o.scale = pl.target;
+        o.slots = c.ct(ids[0]).slots;
+        outs.push_back(c.put_ct(o));
+    } else {
+        std::vector<u64 *> dsts;
+        for (int id : ids) {
+            Ct o = c.new_ct(onq, 2, pl.target);
+            o.slots = c.ct(id).slots;
+            dsts.push_back(o.d);
+            outs.push_back(c.put_ct(o));
+        }
+        c.scatter_words(dsts, vd[pl.out], stride(pl.out));
+        c.release(vd[pl.out]);
+    }
+    return outs;
+}
+
+// ciphertexts grouped by (rows, scale), one plan replay per group
+static void eval_polynomial(Context &c, const int *ids, int nb, const double *coeffs, int n, int cheb, double S,
+                            int *outs) {
+    if (nb <= 0 || !ids || !outs) HB_THROW(HB_EINVAL, "EvaluatePolynomial: empty input");
+    if (n < 3 || !coeffs) HB_THROW(HB_EINVAL, "EvaluatePolynomial: the native evaluation needs degree >= 2");
+    if (!(S > 0)) HB_THROW(HB_EINVAL, "EvaluatePolynomial: output scale must be positive");
+    const std::vector<double> co(coeffs, coeffs + n);
+    for (double v : co)
+        if (!std::isfinite(v)) HB_THROW(HB_EINVAL, "EvaluatePolynomial: non-finite coefficient");
+    if (!c.d_rlk) c.gen_relin();
+    std::map<std::pair<int, double>, std::vector<int>> groups;
+    for (int i = 0; i < nb; i++) {
+        const Ct &x = c.ct(ids[i]);
+        if (x.npoly != 2)
+            HB_THROW(HB_ESTATE, "EvaluatePolynomial: relinearize before evaluating a polynomial.");
+        groups[{x.nq, x.scale}].push_back(i);
+    }
+    for (auto &kv : groups) {
+        const PolyPlan &pl = poly_plan(c, cheb != 0, kv.first.first, kv.first.second, co, S);
+        std::vector<int> g;
+        for (int i : kv.second) g.push_back(ids[i]);
+        const std::vector<int> r = poly_run(c, pl, g);
+        for (size_t j = 0; j < r.size(); j++) outs[kv.second[j]] = r[j];
+    }
+}
+
+HB_API int helrm_EvaluatePolynomial(int ct, const double *coeffs, int n, int chebyshev, double scale, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        eval_polynomial(c, &ct, 1, coeffs, n, chebyshev, scale, out);
+    });
+}
+
+HB_API int helrm_EvaluatePolynomialBatch(const int *cts, int nb, const double *coeffs, int n, int chebyshev,
+                                         double scale, int *outs) {
+    return guard([&] {
+        Context &c = C();
+        eval_polynomial(c, cts, nb, coeffs, n, chebyshev, scale, outs);
+    });
+}
+
+HB_API int helrm_PolynomialPlanInfo(int nq, double in_scale, const double *coeffs, int n, int chebyshev, double scale,
+                                    int *info) {
+    return guard([&] {
+        Context &c = C();
+        if (!info || !coeffs || nq < 1 || nq > c.L) HB_THROW(HB_EINVAL, "PolynomialPlanInfo: bad arguments");
+        const PolyPlan pl =
+            plan_polynomial(c.primes, chebyshev != 0, nq, in_scale, std::vector<double>(coeffs, coeffs + n), scale);
+        info[0] = pl.depth;
+        info[1] = pl.products;
+        info[2] = pl.rescales;
+        info[3] = pl.bs;
+    });
+}
 
 HB_API int helrm_Negate(int ct) {
     return guard([&] {

@@ -1148,6 +1148,72 @@ void ew_mac(u64 *out, const MacArgs &args, int npoly, int nq, int logN, cudaStre
 }
 
 // =====================================================================
+// polynomial evaluation: batched degree-1 tensor and the fused linear
+// combination every power-basis step and every leaf of the evaluation
+// tree reduces to
+// =====================================================================
+__global__ void k_tensor_batch(u64 *out, const u64 *a, const u64 *b, int nq, int anq, int bnq, size_t as,
+                               size_t bs, int logN) {
+    const size_t n = (size_t)nq << logN;
+    const size_t item = blockIdx.y;
+    const u64 *A = a + item * as, *B = b + item * bs;
+    const size_t a1 = (size_t)anq << logN, b1 = (size_t)bnq << logN;
+    u64 *O = out + item * 3 * n;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const PrimeConst &pc = c_pc[i >> logN];
+        const u64 a0 = A[i], x1 = A[a1 + i], b0 = B[i], y1 = B[b1 + i];
+        O[i] = mul_mod(a0, b0, pc);
+        u128 acc = {0, 0};
+        mac128(acc, a0, y1);
+        mac128(acc, x1, b0);
+        O[n + i] = reduce128(acc, pc);
+        O[2 * n + i] = mul_mod(x1, y1, pc);
+    }
+}
+void ew_tensor_batch(u64 *out, const u64 *a, const u64 *b, int nq, int anq, int bnq, int nb, size_t as, size_t bs,
+                     int logN, cudaStream_t s) {
+    const size_t n = (size_t)nq << logN;
+    unsigned g = grid1d(n, 256);
+    const unsigned cap = (148u * 64u + nb - 1) / nb;
+    if (g > cap) g = cap < 1 ? 1 : cap;
+    ProfScope ps(KC_ELEMENTWISE, 56.0 * n * nb, 4.0 * n * nb, s, 1);
+    k_tensor_batch<<<dim3(g, nb), 256, 0, s>>>(out, a, b, nq, anq, bnq, as, bs, logN);
+    check_launch("tensor_batch");
+}
+
+__global__ void k_lincomb(u64 *out, LinCombArgs a, int nq, size_t out_stride, int logN) {
+    const size_t per = (size_t)nq << logN;
+    const int item = blockIdx.y >> 1, pl = blockIdx.y & 1;
+    u64 *O = out + (size_t)item * out_stride + (size_t)pl * per;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < per; i += (size_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i >> logN);
+        const PrimeConst &pc = c_pc[row];
+        u128 acc = {0, 0};
+        u64 partial = 0;
+        for (int t = 0; t < a.n; t++) {
+            const u64 x = a.x[t][(size_t)item * a.xs[t] + ((size_t)pl * a.nq[t] << logN) + i];
+            mac128(acc, x, a.coef[(size_t)t * nq + row]);
+            if ((t & 15) == 15) {
+                partial = add_mod(partial, reduce128(acc, pc), pc.q);
+                acc.lo = acc.hi = 0;
+            }
+        }
+        u64 v = add_mod(partial, reduce128(acc, pc), pc.q);
+        if (pl == 0 && a.k0) v = add_mod(v, a.k0[row], pc.q);
+        O[i] = v;
+    }
+}
+void ew_lincomb(u64 *out, const LinCombArgs &a, int nq, int nb, size_t out_stride, int logN, cudaStream_t s) {
+    const size_t per = (size_t)nq << logN;
+    unsigned g = grid1d(per, 256);
+    const unsigned cap = (148u * 32u + nb - 1) / nb;
+    if (g > cap) g = cap < 1 ? 1 : cap;
+    ProfScope ps(KC_ELEMENTWISE, 8.0 * per * 2 * nb * (a.n + 1), (double)per * 2 * nb * a.n, s, 1);
+    k_lincomb<<<dim3(g, 2 * nb), 256, 0, s>>>(out, a, nq, out_stride, logN);
+    check_launch("lincomb");
+}
+
+// =====================================================================
 // counter-based sampler (SplitMix64 finaliser, Steele-Lea-Flood 2014)
 // rand64(seed, domain, idx) = mix(mix(seed ^ mix(domain)) ^ idx); uniform
 // residues by Lemire's multiply-shift with rejection (retry counters in

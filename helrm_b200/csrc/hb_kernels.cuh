@@ -109,6 +109,24 @@ struct MacArgs {
 // out[pl][i] = sum_t ct_t[pl][i] * pt_t[i]
 void ew_mac(u64 *out, const MacArgs &args, int npoly, int nq, int logN, cudaStream_t s);
 
+// ---- polynomial evaluation -------------------------------------------------------
+// nb degree-1 products out[b] = a[b] (x) b[b] ([nb][3][nq][N]); operand items
+// sit at strides as / bs and hold anq / bnq rows per polynomial (>= nq)
+void ew_tensor_batch(u64 *out, const u64 *a, const u64 *b, int nq, int anq, int bnq, int nb, size_t as, size_t bs,
+                     int logN, cudaStream_t s);
+#define HB_LC_MAX 48
+struct LinCombArgs {
+    const u64 *x[HB_LC_MAX];  // operand t: nb ciphertexts, item stride xs[t]
+    size_t xs[HB_LC_MAX];
+    int nq[HB_LC_MAX];        // rows per polynomial of operand t (>= the output's)
+    int n;
+    const u64 *coef;          // [n][nq] residues below q_i
+    const u64 *k0;            // [nq] residues added to polynomial 0, or null
+};
+// out[b][pl][i] = sum_t coef[t][i] * x_t[b][pl][i] (+ k0[i] for pl = 0), the
+// output's nq rows of each operand, nb degree-1 ciphertexts at out_stride
+void ew_lincomb(u64 *out, const LinCombArgs &a, int nq, int nb, size_t out_stride, int logN, cudaStream_t s);
+
 // ---- sampling (counter-based; see hb_kernels.cu) ---------------------------
 void sample_uniform(u64 *out, int nrows, const int *row_prime_host_unused, RowMap map, u64 seed, u64 domain,
                     u64 idx_base, u64 idx_row_stride, int logN, cudaStream_t s);

@@ -38,6 +38,37 @@ def _out_int():
     return ctypes.c_int(0)
 
 
+def _cheb_basis(x: np.ndarray, degree: int) -> np.ndarray:
+    """[len(x), degree + 1] matrix of T_0(x) .. T_degree(x), by T_{j+1} = 2 x T_j - T_{j-1}."""
+    t = np.empty((len(x), degree + 1))
+    t[:, 0] = 1.0
+    if degree >= 1:
+        t[:, 1] = x
+    for j in range(2, degree + 1):
+        t[:, j] = 2.0 * x * t[:, j - 1] - t[:, j - 2]
+    return t
+
+
+def _composite_sign_coeffs(degrees, gap):
+    lo, hi = -1.0, 1.0
+    flat: list[float] = []
+    for i, d in enumerate(degrees):
+        last = i == len(degrees) - 1
+        npts = max(8 * d, 500)
+        x = np.concatenate([np.linspace(lo, -gap, npts), np.linspace(gap, hi, npts)])
+        target = np.where(x > 0, 1.0, 0.0) if last else np.sign(x)
+        c = np.linalg.lstsq(_cheb_basis(x, d), target, rcond=None)[0]
+        flat.extend(c[:d + 1].tolist())
+        if last:
+            break
+        grid = np.concatenate([np.linspace(lo, -gap, 2000), np.linspace(gap, hi, 2000)])
+        vals = _cheb_basis(grid, d) @ c
+        lo, hi = float(vals.min()), float(vals.max())
+        edge = _cheb_basis(np.array([gap, -gap]), d) @ c
+        gap = max(float(min(abs(edge[0]), abs(edge[1]))), 1e-12)
+    return flat
+
+
 class B200Library:
     """Orion backend over libhelrm_b200.so.
 
@@ -518,10 +549,38 @@ class B200Library:
         return pid
 
     def EvaluatePolynomial(self, ct_id, poly_id, scale=None) -> int:
-        """Horner's rule over MulRelin + Rescale (ascending coefficients)."""
+        """f(ct) for a polynomial from GenerateMonomial / GenerateChebyshev,
+        at scale ``scale`` (the default scale when None), as the reference
+        backends do (cheddar bindings.py:1102-1116): degree >= 2 runs the
+        native log-depth evaluation (ceil(log2(d+1)) levels, the depth
+        orion/nn/activation.py plans with), below that Horner's rule."""
         coeffs, kind = self._polys[poly_id]
+        if len(coeffs) - 1 >= 2:
+            return self._eval_native([ct_id], coeffs, kind, scale)[0]
         if kind == "chebyshev":
+            # degree <= 1: T0 = 1, T1 = x, the conversion is exact
             coeffs = np.polynomial.chebyshev.cheb2poly(coeffs).tolist()
+        return self._eval_horner(ct_id, coeffs)
+
+    def EvaluatePolynomialBatch(self, ct_ids: Sequence[int], poly_id, scale=None) -> list[int]:
+        """EvaluatePolynomial over all ciphertexts of a CipherTensor
+        (poly_evaluator.py:29-31 calls it once per id) in batched kernels."""
+        coeffs, kind = self._polys[poly_id]
+        if len(coeffs) - 1 >= 2:
+            return self._eval_native(list(ct_ids), coeffs, kind, scale)
+        return [self.EvaluatePolynomial(c, poly_id, scale) for c in ct_ids]
+
+    def _eval_native(self, ct_ids, coeffs, kind, scale):
+        ca, cp = _int_array(ct_ids)
+        co, pp = _f64_array(coeffs)
+        s = float(self._default_scale if scale is None else scale)
+        outs = np.zeros(len(ca), dtype=np.int32)
+        call("helrm_EvaluatePolynomialBatch", cp, len(ca), pp, len(co), 1 if kind == "chebyshev" else 0, s,
+             outs.ctypes.data_as(P(c_int)))
+        return [int(v) for v in outs]
+
+    def _eval_horner(self, ct_id, coeffs):
+        """Horner's rule over MulRelin + Rescale (ascending coefficients)."""
         n = len(coeffs) - 1
         if n < 0:
             raise ValueError("EvaluatePolynomial: empty coefficient list.")
@@ -536,8 +595,37 @@ class B200Library:
             acc = self.AddScalar(acc, coeffs[i])
         return acc
 
-    def GenerateMinimaxSignCoeffs(self, degrees, prec, logalpha, logerr, debug):
-        self._not_implemented("GenerateMinimaxSignCoeffs")
+    def GetPolyDepth(self, poly_id) -> int:
+        """Levels EvaluatePolynomial consumes (poly_evaluator.py:58-59):
+        ceil(log2(d+1)) natively, one for the Horner path's degree 0 or 1."""
+        coeffs, _ = self._polys[poly_id]
+        d = len(coeffs) - 1
+        return max(1, math.ceil(math.log2(d + 1))) if d >= 2 else 1
+
+    def PolynomialPlanInfo(self, poly_id, level: int, in_scale: float, scale=None) -> dict:
+        """The native evaluation plan for an input at ``level`` and
+        ``in_scale``: levels consumed, ciphertext products, rescales and
+        the baby-step count."""
+        coeffs, kind = self._polys[poly_id]
+        co, pp = _f64_array(coeffs)
+        info = (c_int * 4)()
+        s = float(self._default_scale if scale is None else scale)
+        call("helrm_PolynomialPlanInfo", int(level) + 1, float(in_scale), pp, len(co),
+             1 if kind == "chebyshev" else 0, s, info)
+        return {"depth": info[0], "products": info[1], "rescales": info[2], "bs": info[3]}
+
+    def GenerateMinimaxSignCoeffs(self, degrees, prec, logalpha, logerr, debug) -> list[float]:
+        """Coefficients of a composite sign approximation, the stages'
+        Chebyshev coefficients concatenated (the host computation of the
+        reference's Cheddar backend, bindings.py:1164-1230).  Stage i is the
+        least-squares fit, in the standard Chebyshev basis, of sign(x) --
+        the last stage of the step x > 0 -> 1, else 0 (ReLU = x * step(x))
+        -- on max(8 d, 500) evenly spaced points on each of [lo, -gap] and
+        [gap, hi].  The first stage covers [-1, 1] with gap 2^-logalpha; each
+        later one the previous stage's output range over 2000-point grids of
+        its intervals, with gap the smaller magnitude of its output at
+        +-gap.  prec, logerr and debug do not change the fit."""
+        return _composite_sign_coeffs([int(d) for d in degrees], 2.0 ** (-float(logalpha)))
 
     # ------------------------------------------------------------ bootstrap (out of this backend's scope)
     def NewBootstrapper(self, logPs, slots: int) -> None:

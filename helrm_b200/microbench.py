@@ -19,6 +19,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
 
 import numpy as np
@@ -218,6 +219,86 @@ def run_table_matmul(rows=16, cols=64, level=23, reps=3, device=0) -> dict:
         lib.DeleteScheme()
 
 
+def run_relu(batches=(1, 8), reps=3, degrees=(15, 15, 27), level=23, device=0) -> list[dict]:
+    """Orion's ReLU (orion/nn/activation.py:246-300) at LogN 16 (config 2/3
+    primes): the composite step polynomial, stage by stage through
+    EvaluatePolynomialBatch (the last stage at scale q[level] so the
+    product's rescale is exact), then x * step(x) and its rescale, on
+    batches of ciphertexts at `level`.  CUDA events on the library stream;
+    reports milliseconds per ciphertext and per ciphertext product."""
+    from helrm_b200 import B200Library, _capi
+    from helrm_b200.params import CFG2, CFG2_DNUM
+
+    lib = B200Library(dnum=CFG2_DNUM, seed=13, device=device)
+    lib.setup_bindings(CFG2)
+    out = []
+    try:
+        lib.GenerateSecretKey()
+        lib.GenerateRelinearizationKey()
+        info = lib.scheme_info()
+        slots = info["slots"]
+        scale = float(1 << CFG2.logscale)
+        chain = lib.GetModuliChain()
+        flat = lib.GenerateMinimaxSignCoeffs(list(degrees), 128, 6, 12, 0)
+        stages, o = [], 0
+        for d in degrees:
+            stages.append(lib.GenerateChebyshev(flat[o:o + d + 1]))
+            o += d + 1
+        products = sum(lib.PolynomialPlanInfo(p, level, scale)["products"] for p in stages) + 1
+        capi = _capi.load()
+        rng = np.random.default_rng(1)
+        for nb in batches:
+            xs = [rng.uniform(-1, 1, slots) for _ in range(nb)]
+            cts = []
+            for x in xs:
+                pt = lib.Encode(list(x), level, scale)
+                cts.append(lib.Encrypt(pt))
+                lib.DeletePlaintext(pt)
+
+            def relu():
+                cur = list(cts)
+                for i, p in enumerate(stages):
+                    lvl = lib.GetCiphertextLevel(cur[0]) - lib.GetPolyDepth(p)
+                    target = float(chain[lvl]) if i == len(stages) - 1 else scale
+                    nxt = lib.EvaluatePolynomialBatch(cur, p, target)
+                    if cur is not cts and cur[0] not in cts:
+                        for c in cur:
+                            lib.DeleteCiphertext(c)
+                    cur = nxt
+                res = []
+                for x, s in zip(cts, cur):
+                    res.append(lib.Rescale(lib.MulRelinCiphertextNew(x, s)))
+                    lib.DeleteCiphertext(s)
+                return res
+
+            for r in relu():  # warm-up (plans, pools)
+                lib.DeleteCiphertext(r)
+            lib.Synchronize()
+            _capi.check(capi.helrm_TimerStart())
+            last = None
+            for _ in range(reps):
+                if last:
+                    for r in last:
+                        lib.DeleteCiphertext(r)
+                last = relu()
+            ms = ctypes.c_double(0)
+            _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+            got = np.array(lib.Decode(lib.Decrypt(last[0])))
+            err = float(np.abs(got - np.maximum(xs[0], 0))[np.abs(xs[0]) > 2.0 ** -5].max())
+            for r in last:
+                lib.DeleteCiphertext(r)
+            for c in cts:
+                lib.DeleteCiphertext(c)
+            per = ms.value / reps / nb
+            out.append({"op": "relu_composite", "degrees": list(degrees), "batch": nb, "level_in": level,
+                        "level_out": level - sum(math.ceil(math.log2(d + 1)) for d in degrees) - 1,
+                        "ms_per_ct": per, "products_per_ct": products, "ms_per_product": per / products,
+                        "max_err_outside_gap": err})
+    finally:
+        lib.DeleteScheme()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batches", default="1,16,128")
@@ -225,11 +306,15 @@ def main():
     ap.add_argument("--ops", default="ntt,intt,aut,mac,rescale,ks")
     ap.add_argument("--rotations", type=int, default=32)
     ap.add_argument("--table", action="store_true", help="also the IVE lookup's one-pass table product")
+    ap.add_argument("--relu", action="store_true", help="also Orion's composite ReLU through EvaluatePolynomial")
     args = ap.parse_args()
     run([int(b) for b in args.batches.split(",")], args.reps, args.ops, args.rotations,
         emit=lambda line: print(json.dumps(line), flush=True))
     if args.table:
         print(json.dumps(run_table_matmul()), flush=True)
+    if args.relu:
+        for line in run_relu():
+            print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -181,6 +181,23 @@ int helrm_GetTableShape(int table, int *rows, int *cols, int *level);
  * n = cols input ciphertexts, rows ids written to outs */
 int helrm_MulTableMatMulNew(const int *cts, int n, int table, int *outs);
 
+/* ---- polynomial evaluation (poly_evaluator.py:25-35; cheddar bindings.py:
+ * 1102-1116 -> EvaluatePolynomialNative, cheddar_pybind.cu:2207-2262) --------
+ * coeffs[0..n) ascending, n >= 3 (degree >= 2; the Python layer keeps Horner
+ * below that, bindings.py:1104-1116), chebyshev != 0: sum c_j T_j(x), else
+ * sum c_j x^j.  The output sits ceil(log2(n)) levels below the input
+ * (orion/nn/activation.py:22-28,101-110) at exactly `scale`; the input must be
+ * relinearized and hold that many levels. */
+int helrm_EvaluatePolynomial(int ct, const double *coeffs, int n, int chebyshev, double scale, int *out);
+/* the same polynomial over nb ciphertexts (the ids of a CipherTensor,
+ * poly_evaluator.py:29-31) in batched kernels; nb ids written to outs */
+int helrm_EvaluatePolynomialBatch(const int *cts, int nb, const double *coeffs, int n, int chebyshev,
+                                  double scale, int *outs);
+/* the evaluation plan for an input of nq rows at in_scale: info[0] levels
+ * consumed, info[1] ciphertext products, info[2] rescales, info[3] baby steps */
+int helrm_PolynomialPlanInfo(int nq, double in_scale, const double *coeffs, int n, int chebyshev, double scale,
+                             int *info);
+
 /* ---- metadata (tensors.go:35-104; cheddar bindings.py:1278-1320) ------------- */
 int helrm_DeleteCiphertext(int ct);
 int helrm_DeletePlaintext(int pt);
