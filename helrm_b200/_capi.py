@@ -43,7 +43,7 @@ SIGNATURES = {
     "helrm_SubCiphertext": [c_int, c_int],
     "helrm_MulRelinCiphertextNew": [c_int, c_int, P(c_int)],
     "helrm_MulRelinCiphertext": [c_int, c_int],
-    "helrm_Negate": [c_int],
+    "helrm_Negate": [c_int, P(c_int)],
     "helrm_AddPlaintextNew": [c_int, c_int, P(c_int)],
     "helrm_AddPlaintext": [c_int, c_int],
     "helrm_SubPlaintextNew": [c_int, c_int, P(c_int)],
@@ -108,6 +108,10 @@ SIGNATURES = {
     "helrm_DeleteTable": [c_int],
     "helrm_GetTableShape": [c_int, P(c_int), P(c_int), P(c_int)],
     "helrm_MulTableMatMulNew": [P(c_int), c_int, c_int, P(c_int)],
+    "helrm_EncodeBatch": [P(c_double), c_int, c_int, c_int, c_double, P(c_int)],
+    "helrm_MulImaginaryUnitNew": [c_int, P(c_int)],
+    "helrm_MulImaginaryUnit": [c_int],
+    "helrm_UnpackLanes": [P(c_int), c_int, c_int, P(c_int)],
     "helrm_EvaluatePolynomial": [c_int, P(c_double), c_int, c_int, c_double, P(c_int)],
     "helrm_EvaluatePolynomialBatch": [P(c_int), c_int, P(c_double), c_int, c_int, c_double, P(c_int)],
     "helrm_PolynomialPlanInfo": [c_int, c_double, P(c_double), c_int, c_int, c_double, P(c_int)],

@@ -400,6 +400,9 @@ public:
     u64 *d_tables = nullptr;
     u64 *d_pmod = nullptr;     // P mod q_p, [P]
     u64 *d_cls8 = nullptr;     // [L][9] 2^(8s) mod q_i (tensor-core MAC epilogue)
+    u64 *d_iunit = nullptr;    // [P][4] w, w', q - w, (q - w)': X^(N/2) in the NTT order (w = psi^(N/2))
+    int *d_enc_perm = nullptr;     // device encoding: slot -> transform position
+    double2 *d_enc_tw = nullptr;   // device encoding: exp(-2 pi i k / (N/2))
     int *d_tc_err = nullptr;   // error bits of the tensor-core MAC's bounded waits
     bool use_tc = false;       // tensor-core baby-step MAC where supported (HELRM_B200_MAC=tc)
     std::vector<LevelTabs> lv; // index nq (1..L)
@@ -674,6 +677,20 @@ public:
         d_pmod = alloc(P);
         cuda_check(cudaMemcpyAsync(d_pmod, pm.data(), P * 8, cudaMemcpyHostToDevice, stream), "pmod");
         {
+            // slot-wise multiplication by i is multiplication by X^(N/2); NTT
+            // position t evaluates at psi^(2 brv(t) + 1), so the multiplier is
+            // w = psi^(N/2) (w^2 = -1) for t < N/2 and -w above
+            std::vector<u64> iu((size_t)4 * P);
+            for (int p = 0; p < P; p++) {
+                const u64 q = primes[p], w = h_powm(find_psi(q, logN), (u64)N / 2, q);
+                iu[4 * p] = w, iu[4 * p + 1] = h_shoup(w, q);
+                iu[4 * p + 2] = q - w, iu[4 * p + 3] = h_shoup(q - w, q);
+            }
+            d_iunit = alloc((size_t)4 * P);
+            cuda_check(cudaMemcpyAsync(d_iunit, iu.data(), iu.size() * 8, cudaMemcpyHostToDevice, stream), "iunit");
+            sync();
+        }
+        {
             std::vector<u64> cls((size_t)L * 9, 0);
             bsgs_mma_class_consts(cls.data(), primes.data(), L);
             d_cls8 = alloc((size_t)L * 9);
@@ -837,6 +854,9 @@ public:
             release(d_pmod);
             release(d_cls8);
             release(d_tc_err);
+            release(d_iunit);
+            release(d_enc_perm);
+            release(d_enc_tw);
             release(d_tables);
             if (up) {
                 cudaStreamSynchronize(up);
@@ -1001,44 +1021,62 @@ public:
 
     // ---------------------------------------------------------- encode
     // integer coefficients -> NTT residues on `rows` rows (q rows then aux)
-    void upload_coeffs(const std::vector<hi128> &co, int nq, bool ext, u64 *dst) {
+    // ---------------------------------------------------------- encoding on the device
+    EncTables enc_tables_dev() {
+        if (!d_enc_perm) {
+            const size_t n = (size_t)N / 2;
+            d_enc_perm = (int *)alloc((n + 1) / 2);
+            d_enc_tw = (double2 *)alloc(n / 2 > 0 ? n : 2);  // n/2 entries of 16 bytes
+            enc_tables(d_enc_perm, d_enc_tw, logN, stream);
+        }
+        return EncTables{d_enc_perm, d_enc_tw, logN};
+    }
+    // count vectors of nvals slot values (interleaved re, im when cplx) ->
+    // plaintexts at dsts[v] ([nq (+K)][N], NTT order), scale `scale`
+    void encode_device(const double *vals, int nvals, bool cplx, int count, int nq, bool ext, double scale,
+                       u64 *const *dsts) {
+        if (count <= 0) return;
+        if (nvals < 0 || nvals > slots) HB_THROW(HB_EINVAL, "encode: more values than slots");
+        const size_t per = (size_t)nvals * (cplx ? 2 : 1);
+        // |coefficient| <= scale * max |slot| (the inverse transform averages)
+        double mx = 0.0;
+        for (size_t i = 0; i < per * count; i++) mx = std::max(mx, std::fabs(vals[i]));
+        if (cplx) mx *= 2.0;
+        if (!std::isfinite(mx) || !(mx * scale < 4.0e18))
+            HB_THROW(HB_EINVAL, "encode: value * scale beyond 2^62 (or not finite)");
+        const EncTables et = enc_tables_dev();
         const int rows = nq + (ext ? K : 0);
-        std::vector<u64> host((size_t)rows * N);
-        auto work = [&](int r0, int r1) {
-            for (int r = r0; r < r1; r++) {
-                const int p = r < nq ? r : L + (r - nq);
-                const u64 q = primes[p];
-                u64 *row = &host[(size_t)r * N];
-                for (int n = 0; n < N; n++) {
-                    hi128 x = co[n];
-                    if (x >= 0)
-                        row[n] = x < ((hi128)1 << 63) ? (u64)x % q : (u64)((hu128)x % q);
-                    else {
-                        u64 m = (-x) < ((hi128)1 << 63) ? (u64)(-x) % q : (u64)((hu128)(-x) % q);
-                        row[n] = m ? q - m : 0;
-                    }
-                }
-            }
-        };
-        work(0, rows);
-        cuda_check(cudaMemcpyAsync(dst, host.data(), host.size() * 8, cudaMemcpyHostToDevice, stream), "encode upload");
-        ntt_forward(dst, rows, rowmap(rows, nq, L), ntt, stream);
-        sync();  // host buffer lifetime
+        const RowMap rm = rowmap(rows, nq, L);
+        const int chunk = std::min(count, HB_PTR_BATCH);
+        u64 *dv = alloc(std::max<size_t>(1, per * chunk));
+        double2 *z = (double2 *)alloc((size_t)chunk * N);  // chunk x N/2 complex points
+        for (int c0 = 0; c0 < count; c0 += chunk) {
+            const int cnt = std::min(chunk, count - c0);
+            if (per)
+                cuda_check(cudaMemcpyAsync(dv, vals + per * c0, per * cnt * 8, cudaMemcpyHostToDevice, stream),
+                           "encode values");
+            enc_scatter(z, (const double *)dv, nvals, cplx ? 1 : 0, cnt, et, stream);
+            enc_ifft(z, cnt, et, stream);
+            PtrBatchW d{};
+            for (int i = 0; i < cnt; i++) d.p[i] = dsts[c0 + i];
+            enc_round(d, z, rows, rm, scale, cnt, et, stream);
+            for (int i = 0; i < cnt; i++) ntt_forward(dsts[c0 + i], rows, rm, ntt, stream);
+        }
+        release(dv);
+        release(z);
     }
 
     int encode(const double *inter, int n, int level, double scale, bool ext) {
         if (level < 0 || level >= L) HB_THROW(HB_EINVAL, "encode: level out of range");
         if (n > slots) HB_THROW(HB_EINVAL, "encode: more values than slots");
         if (!(scale > 0)) scale = default_scale;
-        std::vector<hi128> co;
-        encode_coeffs(logN, inter, n, (long double)scale, co);
         Pt p;
         p.nq = level + 1;
         p.ext = ext;
         p.scale = scale;
         p.slots = slots;
         p.d = alloc((size_t)(p.nq + (ext ? K : 0)) * N);
-        upload_coeffs(co, p.nq, ext, p.d);
+        encode_device(inter, n, true, 1, p.nq, ext, scale, &p.d);
         return put_pt(p);
     }
 
@@ -1551,37 +1589,35 @@ public:
             if (!seen.insert(k).second) HB_THROW(HB_EINVAL, "GenerateLinearTransform: duplicate diagonal index");
             t->ks.push_back(k);
         }
-        // encode every diagonal once (pre-rolled by g*bs), host FFTs in parallel
-        std::vector<std::vector<hi128>> coeffs(n);
-        int nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
-        auto worker = [&](int tid) {
-            std::vector<double> inter((size_t)2 * width);
-            for (int i = tid; i < n; i += nthreads) {
-                const int k = idxs[i], g = t->use_bsgs ? k / bs : 0, shift = g * bs;
+        // encode every diagonal once (pre-rolled by g*bs), on the device in
+        // batches of up to HB_PTR_BATCH diagonals
+        std::vector<double> rolled;
+        std::vector<u64 *> dsts;
+        for (int i0 = 0; i0 < n; i0 += HB_PTR_BATCH) {
+            const int cnt = std::min(HB_PTR_BATCH, n - i0);
+            rolled.assign((size_t)cnt * width, 0.0);
+            dsts.clear();
+            for (int j = 0; j < cnt; j++) {
+                const int i = i0 + j, k = idxs[i], g = t->use_bsgs ? k / bs : 0, shift = g * bs;
                 const double *vals = data + (size_t)i * width;
+                double *dst = &rolled[(size_t)j * width];
                 for (int s = 0; s < width; s++) {
                     // numpy roll to the right by shift over the diagonal's own width
-                    int src = ((s - shift) % width + width) % width;
-                    inter[2 * s] = vals[src];
-                    inter[2 * s + 1] = 0.0;
+                    const int src = ((s - shift) % width + width) % width;
+                    dst[s] = vals[src];
                 }
-                encode_coeffs(logN, inter.data(), width, (long double)default_scale, coeffs[i]);
+                Pt p;
+                p.nq = level + 1;
+                p.ext = true;
+                p.scale = default_scale;
+                p.slots = slots;
+                p.d = alloc((size_t)(p.nq + K) * N);
+                t->pts[k] = p;
+                dsts.push_back(p.d);
+                const int b = t->use_bsgs ? k % bs : k;
+                t->groups[g].push_back({b, k});
             }
-        };
-        std::vector<std::thread> th;
-        for (int tid = 0; tid < nthreads; tid++) th.emplace_back(worker, tid);
-        for (auto &x : th) x.join();
-        for (int i = 0; i < n; i++) {
-            Pt p;
-            p.nq = level + 1;
-            p.ext = true;
-            p.scale = default_scale;
-            p.slots = slots;
-            p.d = alloc((size_t)(p.nq + K) * N);
-            upload_coeffs(coeffs[i], p.nq, true, p.d);
-            t->pts[idxs[i]] = p;
-            int k = idxs[i], g = t->use_bsgs ? k / bs : 0, b = t->use_bsgs ? k % bs : k;
-            t->groups[g].push_back({b, k});
+            encode_device(rolled.data(), width, false, cnt, level + 1, true, default_scale, dsts.data());
         }
         int id = next_id++;
         lts[id] = std::move(t);
@@ -2282,11 +2318,17 @@ HB_API int helrm_PolynomialPlanInfo(int nq, double in_scale, const double *coeff
     });
 }
 
-HB_API int helrm_Negate(int ct) {
+// a fresh ciphertext -ct, the input untouched, as every reference backend
+// returns it (lattigo evaluator.go:68-78, cheddar_pybind.cu:1798-1803)
+HB_API int helrm_Negate(int ct, int *out) {
     return guard([&] {
         Context &c = C();
-        Ct &x = c.ct(ct);
-        ew_neg(x.d, x.d, x.npoly * x.nq, c.qmap(x.nq), c.logN, c.stream);
+        OUT(out);
+        const Ct &x = c.ct(ct);
+        Ct o = c.new_ct(x.nq, x.npoly, x.scale);
+        o.slots = x.slots;
+        ew_neg(o.d, x.d, x.npoly * x.nq, c.qmap(x.nq), c.logN, c.stream);
+        *out = c.put_ct(o);
     });
 }
 
@@ -2433,6 +2475,111 @@ static int conj_new(Context &c, int id) {
     c.rotate_batch(o.d, x.d, x.nq, 1, g, key);
     return c.put_ct(o);
 }
+// slot-wise multiplication by sqrt(-1): key-free, no level
+// (cheddar_pybind.cu:1825-1837, bindings.py:607-612)
+static int mul_iunit_new(Context &c, int id) {
+    const Ct &x = c.ct(id);
+    Ct o = c.new_ct(x.nq, x.npoly, x.scale);
+    o.slots = x.slots;
+    ew_mul_iunit(o.d, x.d, x.npoly * x.nq, x.nq, c.d_iunit, c.logN, c.stream);
+    return c.put_ct(o);
+}
+HB_API int helrm_MulImaginaryUnitNew(int ct, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        *out = mul_iunit_new(c, ct);
+    });
+}
+HB_API int helrm_MulImaginaryUnit(int ct) {
+    return guard([&] {
+        Context &c = C();
+        int o = mul_iunit_new(c, ct);
+        c.replace_ct(ct, o);
+    });
+}
+
+// the server side of complex-lane packing (orion/core/lane_packing.py:84-115):
+// packed p = (x + i y) / 2 -> x = p + conj(p), y = -i (p - conj(p)); one
+// batched conjugation key switch for all packed ciphertexts, both lanes in
+// one pass.  outs[2m], outs[2m+1] are the lanes of packed[m]; the first
+// num_real are kept (an odd count drops the last zero-padded partner).
+static void unpack_lanes(Context &c, const int *ids, int n, int num_real, int *outs) {
+    if (n <= 0 || !ids || !outs || num_real < 0 || num_real > 2 * n)
+        HB_THROW(HB_EINVAL, "UnpackLanes: bad arguments");
+    const Ct &x0 = c.ct(ids[0]);
+    const int nq = x0.nq;
+    for (int i = 0; i < n; i++) {
+        const Ct &x = c.ct(ids[i]);
+        if (x.npoly != 2) HB_THROW(HB_ESTATE, "UnpackLanes: input is degree-2; relinearize first.");
+        if (x.nq != nq) HB_THROW(HB_ESTATE, "UnpackLanes: packed ciphertexts must share one level");
+    }
+    const u64 g = 2ull * c.N - 1;
+    u64 *key = c.rotation_key(g);
+    const size_t words = (size_t)2 * nq * c.N;
+    const int chunk = std::min(n, 64);
+    u64 *buf = c.alloc((size_t)chunk * words), *cj = c.alloc((size_t)chunk * words);
+    for (int c0 = 0; c0 < n; c0 += chunk) {
+        const int cnt = std::min(chunk, n - c0);
+        std::vector<const Ct *> v;
+        for (int i = 0; i < cnt; i++) v.push_back(&c.ct(ids[c0 + i]));
+        c.gather_cts(buf, v, nq);
+        c.rotate_batch(cj, buf, nq, cnt, g, key);
+        PtrBatchW ev{}, od{};
+        std::vector<Ct> made;
+        for (int i = 0; i < cnt; i++) {
+            const Ct &x = c.ct(ids[c0 + i]);
+            for (int lane = 0; lane < 2; lane++) {
+                Ct o = c.new_ct(nq, 2, x.scale);
+                o.slots = x.slots;
+                (lane ? od : ev).p[i] = o.d;
+                made.push_back(o);
+            }
+        }
+        lane_split(ev, od, buf, cj, nq, cnt, c.d_iunit, c.logN, c.stream);
+        for (int i = 0; i < cnt; i++)
+            for (int lane = 0; lane < 2; lane++) {
+                const int r = 2 * (c0 + i) + lane;
+                Ct &o = made[(size_t)2 * i + lane];
+                if (r < num_real)
+                    outs[r] = c.put_ct(o);
+                else
+                    c.release(o.d);
+            }
+    }
+    c.release(buf);
+    c.release(cj);
+}
+HB_API int helrm_UnpackLanes(const int *packed, int n, int num_real, int *outs) {
+    return guard([&] {
+        Context &c = C();
+        unpack_lanes(c, packed, n, num_real, outs);
+    });
+}
+
+HB_API int helrm_EncodeBatch(const double *values, int count, int n, int level, double scale, int *outs) {
+    return guard([&] {
+        Context &c = C();
+        if (count <= 0 || !outs || n < 0 || (n > 0 && !values)) HB_THROW(HB_EINVAL, "EncodeBatch: bad arguments");
+        if (level < 0 || level >= c.L) HB_THROW(HB_EINVAL, "encode: level out of range");
+        if (!(scale > 0)) scale = c.default_scale;
+        std::vector<u64 *> d;
+        std::vector<Pt> made;
+        for (int i = 0; i < count; i++) {
+            Pt p;
+            p.nq = level + 1;
+            p.ext = false;
+            p.scale = scale;
+            p.slots = c.slots;
+            p.d = c.alloc((size_t)p.nq * c.N);
+            d.push_back(p.d);
+            made.push_back(p);
+        }
+        c.encode_device(values, n, false, count, level + 1, false, scale, d.data());
+        for (int i = 0; i < count; i++) outs[i] = c.put_pt(made[i]);
+    });
+}
+
 HB_API int helrm_ConjugateNew(int ct, int *out) {
     return guard([&] {
         Context &c = C();

@@ -132,31 +132,6 @@ void fft_ld(std::vector<cld> &a, int logn, bool inverse) {
 
 }  // namespace
 
-void encode_coeffs(int logn, const double *vals, int nvals, long double scale,
-                   std::vector<hi128> &coeffs) {
-    const int N = 1 << logn, S = N / 2;
-    const u64 twoN = 2ull * N;
-    const long double PI = 3.141592653589793238462643383279502884L;
-    std::vector<cld> v(N, cld{0.0L, 0.0L});
-    u64 e = 1;
-    for (int j = 0; j < S; j++) {
-        long double re = j < nvals ? vals[2 * j] : 0.0L;
-        long double im = j < nvals ? vals[2 * j + 1] : 0.0L;
-        v[(e - 1) / 2] = {re, im};
-        v[(twoN - e - 1) / 2] = {re, -im};
-        e = (e * 5) % twoN;
-    }
-    fft_ld(v, logn, true);
-    coeffs.resize(N);
-    for (int n = 0; n < N; n++) {
-        long double ang = -PI * n / N;
-        long double re = (v[n].re * cosl(ang) - v[n].im * sinl(ang)) / N * scale;
-        long double r = re >= 0 ? floorl(re + 0.5L) : -floorl(-re + 0.5L);
-        if (!(fabsl(r) < 1.6e38L)) throw std::overflow_error("encode: coefficient exceeds 127 bits");
-        coeffs[n] = (hi128)r;
-    }
-}
-
 void decode_coeffs(int logn, const std::vector<long double> &coeffs, long double scale,
                    double *vals_out) {
     const int N = 1 << logn, S = N / 2;

@@ -30,15 +30,10 @@ std::vector<u64> gen_primes(const std::vector<int> &bits, int logn, std::vector<
 // psi = x^((q-1)/2N) for the smallest x >= 2 giving a primitive 2N-th root.
 u64 find_psi(u64 q, int logn);
 
-// Canonical embedding.  Slot j is the evaluation at zeta^(5^j mod 2N),
-// zeta = exp(i pi / N); slots = N/2.  `vals` holds nvals interleaved
-// (re, im) pairs, zero padded to N/2.  Output: integer coefficients of
-// round(scale * m(X)) (rounded half away from zero).
-void encode_coeffs(int logn, const double *vals, int nvals, long double scale,
-                   std::vector<hi128> &coeffs);
-
-// Inverse of encode_coeffs on centred integer coefficients (long double),
-// writing nslots interleaved (re, im) pairs divided by `scale`.
+// Canonical embedding, decoding side (encoding runs on the device).  Slot
+// j is the evaluation at zeta^(5^j mod 2N), zeta = exp(i pi / N); slots =
+// N/2.  From centred integer coefficients (long double), writes the N/2
+// interleaved (re, im) slot values divided by `scale`.
 void decode_coeffs(int logn, const std::vector<long double> &coeffs, long double scale,
                    double *vals_out);
 

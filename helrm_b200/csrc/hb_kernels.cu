@@ -2342,6 +2342,215 @@ void scatter_items(const PtrBatchW &dst, const u64 *src, size_t words, int nb, c
     check_launch("scatter_items");
 }
 
+// =====================================================================
+// device CKKS encoding (the upload side of the path)
+// With n = N/2 slots and zeta = exp(i pi / N), slot j is m(zeta^(5^j mod 2N)).
+// Writing m(X) = sum_{k<n} (m_k + X^n m_{k+n}) X^k and using zeta^(g n) = i for
+// g = 1 mod 4, the slots are the length-n DFT of w_k zeta^k (w_k = m_k + i
+// m_{k+n}) at position r = (5^j mod 2N - 1) / 4.  Encoding inverts that:
+// place slot j at r_j, take the unnormalised inverse DFT y, then
+// w_k = zeta^-k y_k / n and m_k = round(scale Re w_k), m_{k+n} = round(scale
+// Im w_k).  The DFT is radix-2 decimation in time in FP64: the input is
+// scattered straight into bit-reversed order, the first log2(min(n, 2048))
+// stages run on contiguous 2048-point blocks in shared memory, the remaining
+// ones on strided columns of 2048 points, also in shared memory.
+// =====================================================================
+namespace {
+constexpr int kEncBlock = 2048;  // complex points per block (32 KB of shared memory)
+
+__device__ __forceinline__ double2 cmul(double2 a, double2 b) {
+    return make_double2(__fma_rn(a.x, b.x, -a.y * b.y), __fma_rn(a.x, b.y, a.y * b.x));
+}
+}  // namespace
+
+__global__ void k_enc_tables(int *perm, double2 *tw, int logN) {
+    const unsigned n = 1u << (logN - 1);
+    const u64 m2 = 2ull << logN;
+    for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+        u64 g = 1, b = 5, e = j;
+        while (e) {
+            if (e & 1) g = g * b % m2;
+            b = b * b % m2;
+            e >>= 1;
+        }
+        const unsigned r = (unsigned)((g - 1) >> 2);
+        perm[j] = (int)(__brev(r) >> (33 - logN));
+        if (j < n / 2) {
+            double sn, cs;
+            sincospi(2.0 * (double)j / (double)n, &sn, &cs);
+            tw[j] = make_double2(cs, -sn);  // exp(-2 pi i j / n)
+        }
+    }
+}
+void enc_tables(int *perm, double2 *tw, int logN, cudaStream_t s) {
+    const unsigned n = 1u << (logN - 1);
+    k_enc_tables<<<grid1d(n, 256), 256, 0, s>>>(perm, tw, logN);
+    check_launch("enc_tables");
+}
+
+__global__ void k_enc_scatter(double2 *z, const double *vals, int nvals, int cplx, const int *perm, int h) {
+    const unsigned n = 1u << h;
+    const size_t v = blockIdx.y;
+    for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+        double2 x = make_double2(0.0, 0.0);
+        if ((int)j < nvals) {
+            const double *src = vals + v * (size_t)nvals * (cplx ? 2 : 1);
+            x = cplx ? make_double2(src[2 * j], src[2 * j + 1]) : make_double2(src[j], 0.0);
+        }
+        z[v * n + perm[j]] = x;
+    }
+}
+void enc_scatter(double2 *z, const double *vals, int nvals, int cplx, int count, const EncTables &t, cudaStream_t s) {
+    const unsigned n = 1u << (t.logN - 1);
+    ProfScope ps(KC_ELEMENTWISE, (double)count * n * (cplx ? 32.0 : 24.0), 0.0, s, 1);
+    k_enc_scatter<<<dim3(grid1d(n, 256), count), 256, 0, s>>>(z, vals, nvals, cplx, t.perm, t.logN - 1);
+    check_launch("enc_scatter");
+}
+
+// stages 0 .. cs-1 on contiguous blocks of 2^cs points
+__global__ void __launch_bounds__(kEncBlock / 2) k_enc_fft_rows(double2 *z, const double2 *tw, int h, int cs) {
+    __shared__ double2 a[kEncBlock];
+    const unsigned n = 1u << h, C = 1u << cs;
+    double2 *blk = z + (size_t)blockIdx.y * n + (size_t)blockIdx.x * C;
+    for (unsigned i = threadIdx.x; i < C; i += blockDim.x) a[i] = blk[i];
+    __syncthreads();
+    for (int st = 0; st < cs; st++) {
+        const unsigned half = 1u << st;
+        for (unsigned p = threadIdx.x; p < C / 2; p += blockDim.x) {
+            const unsigned k = p & (half - 1), i0 = ((p >> st) << (st + 1)) + k, i1 = i0 + half;
+            const double2 w = tw[(size_t)k * (n >> (st + 1))];
+            const double2 u = a[i0], t = cmul(w, a[i1]);
+            a[i0] = make_double2(u.x + t.x, u.y + t.y);
+            a[i1] = make_double2(u.x - t.x, u.y - t.y);
+        }
+        __syncthreads();
+    }
+    for (unsigned i = threadIdx.x; i < C; i += blockDim.x) blk[i] = a[i];
+}
+
+// stages cs .. h-1 on blocks of bc consecutive columns x 2^(h-cs) rows
+__global__ void __launch_bounds__(kEncBlock / 2) k_enc_fft_cols(double2 *z, const double2 *tw, int h, int cs) {
+    __shared__ double2 a[kEncBlock];
+    const unsigned n = 1u << h, C = 1u << cs, R = n >> cs, bc = kEncBlock / R;
+    const unsigned b0 = blockIdx.x * bc;
+    double2 *vec = z + (size_t)blockIdx.y * n;
+    for (unsigned i = threadIdx.x; i < kEncBlock; i += blockDim.x) {
+        const unsigned j = i / bc, c = i % bc;
+        a[i] = vec[(size_t)j * C + b0 + c];
+    }
+    __syncthreads();
+    for (int st = cs; st < h; st++) {
+        const int sp = st - cs;
+        const unsigned half = 1u << sp;
+        for (unsigned p = threadIdx.x; p < kEncBlock / 2; p += blockDim.x) {
+            const unsigned c = p % bc, jp = p / bc;
+            const unsigned kk = jp & (half - 1), j0 = ((jp >> sp) << (sp + 1)) + kk, j1 = j0 + half;
+            const unsigned k = b0 + c + kk * C;  // index inside the span of 2^(st+1)
+            const double2 w = tw[(size_t)k * (n >> (st + 1))];
+            const double2 u = a[j0 * bc + c], t = cmul(w, a[j1 * bc + c]);
+            a[j0 * bc + c] = make_double2(u.x + t.x, u.y + t.y);
+            a[j1 * bc + c] = make_double2(u.x - t.x, u.y - t.y);
+        }
+        __syncthreads();
+    }
+    for (unsigned i = threadIdx.x; i < kEncBlock; i += blockDim.x) {
+        const unsigned j = i / bc, c = i % bc;
+        vec[(size_t)j * C + b0 + c] = a[i];
+    }
+}
+
+void enc_ifft(double2 *z, int count, const EncTables &t, cudaStream_t s) {
+    const int h = t.logN - 1;
+    const unsigned n = 1u << h;
+    const int cs = h < 11 ? h : 11;
+    const unsigned C = 1u << cs;
+    ProfScope ps(KC_ELEMENTWISE, (double)count * n * 32.0 * (h > cs ? 2 : 1), 0.0, s, h > cs ? 2 : 1);
+    k_enc_fft_rows<<<dim3(n / C, count), C / 2 > 1 ? C / 2 : 1, 0, s>>>(z, t.tw, h, cs);
+    check_launch("enc_fft_rows");
+    if (h > cs) {
+        const unsigned R = n >> cs;
+        if (R > (unsigned)kEncBlock) throw std::invalid_argument("enc_ifft: ring too large");
+        k_enc_fft_cols<<<dim3(C / (kEncBlock / R), count), kEncBlock / 2, 0, s>>>(z, t.tw, h, cs);
+        check_launch("enc_fft_cols");
+    }
+}
+
+__global__ void k_enc_round(PtrBatchW dst, const double2 *z, int rows, RowMap map, double scale, int logN) {
+    const unsigned N = 1u << logN, n = N >> 1;
+    const size_t v = blockIdx.y;
+    u64 *out = dst.p[v];
+    const double inv_n = 1.0 / (double)n;
+    for (unsigned k = blockIdx.x * blockDim.x + threadIdx.x; k < n; k += gridDim.x * blockDim.x) {
+        const double2 y = z[v * n + k];
+        double sn, cs;
+        sincospi((double)k / (double)N, &sn, &cs);  // zeta^-k = cs - i sn
+        const double re = (y.x * cs + y.y * sn) * inv_n * scale;
+        const double im = (y.y * cs - y.x * sn) * inv_n * scale;
+        const long long a = __double2ll_rn(re), b = __double2ll_rn(im);
+        const u64 ua = (u64)(a < 0 ? -a : a), ub = (u64)(b < 0 ? -b : b);
+        for (int r = 0; r < rows; r++) {
+            const PrimeConst &pc = c_pc[map.prime(r)];
+            const u64 ma = mul_shoup(ua, 1ull, pc.onep, pc.q), mb = mul_shoup(ub, 1ull, pc.onep, pc.q);
+            out[(size_t)r * N + k] = (a < 0 && ma) ? pc.q - ma : ma;
+            out[(size_t)r * N + k + n] = (b < 0 && mb) ? pc.q - mb : mb;
+        }
+    }
+}
+void enc_round(const PtrBatchW &dst, const double2 *z, int rows, RowMap map, double scale, int count,
+               const EncTables &t, cudaStream_t s) {
+    if (count > HB_PTR_BATCH) throw std::invalid_argument("enc_round: bad batch");
+    const unsigned n = 1u << (t.logN - 1);
+    ProfScope ps(KC_ELEMENTWISE, (double)count * n * (16.0 + 16.0 * rows), 0.0, s, 1);
+    k_enc_round<<<dim3(grid1d(n, 256), count), 256, 0, s>>>(dst, z, rows, map, scale, t.logN);
+    check_launch("enc_round");
+}
+
+// slot-wise multiplication by i (X^(N/2)) and the conjugation lane split
+__global__ void k_mul_iunit(u64 *out, const u64 *in, int nrows, int nq, const u64 *iu, int logN) {
+    const size_t n = (size_t)nrows << logN;
+    const unsigned half = 1u << (logN - 1), mask = (1u << logN) - 1;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i >> logN) % nq;
+        const int sel = ((unsigned)i & mask) >= half ? 2 : 0;
+        out[i] = mul_shoup(in[i], iu[4 * p + sel], iu[4 * p + sel + 1], c_pc[p].q);
+    }
+}
+void ew_mul_iunit(u64 *out, const u64 *in, int nrows, int nq, const u64 *iu, int logN, cudaStream_t s) {
+    const size_t n = (size_t)nrows << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 16.0 * n, (double)n, s, 1);
+    k_mul_iunit<<<g, 256, 0, s>>>(out, in, nrows, nq, iu, logN);
+    check_launch("mul_iunit");
+}
+
+__global__ void k_lane_split(PtrBatchW ev, PtrBatchW od, const u64 *pk, const u64 *cj, int nq, const u64 *iu,
+                             int logN) {
+    const size_t n = (size_t)(2 * nq) << logN;
+    const size_t base = blockIdx.y * n;
+    u64 *E = ev.p[blockIdx.y], *O = od.p[blockIdx.y];
+    const unsigned half = 1u << (logN - 1), mask = (1u << logN) - 1;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i >> logN) % nq;
+        const u64 q = c_pc[p].q;
+        const u64 a = pk[base + i], b = cj[base + i];
+        const int sel = ((unsigned)i & mask) >= half ? 2 : 0;
+        E[i] = add_mod(a, b, q);
+        O[i] = mul_shoup(sub_mod(b, a, q), iu[4 * p + sel], iu[4 * p + sel + 1], q);
+    }
+}
+void lane_split(const PtrBatchW &ev, const PtrBatchW &od, const u64 *pk, const u64 *cj, int nq, int nb, const u64 *iu,
+                int logN, cudaStream_t s) {
+    if (nb > HB_PTR_BATCH) throw std::invalid_argument("lane_split: bad batch");
+    const size_t n = (size_t)(2 * nq) << logN;
+    unsigned g = grid1d(n, 256);
+    const unsigned cap = (148u * 32u + nb - 1) / nb;
+    if (g > cap) g = cap < 1 ? 1 : cap;
+    ProfScope ps(KC_ELEMENTWISE, 32.0 * n * nb, (double)n * nb, s, 1);
+    k_lane_split<<<dim3(g, nb), 256, 0, s>>>(ev, od, pk, cj, nq, iu, logN);
+    check_launch("lane_split");
+}
+
 void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s) {
     cudaError_t e = cudaMemcpyAsync(dst, src, nwords * sizeof(u64), cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) throw std::runtime_error(std::string("copy: ") + cudaGetErrorString(e));

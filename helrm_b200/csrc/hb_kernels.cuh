@@ -291,4 +291,30 @@ void gather_items(u64 *dst, const PtrBatch &seg0, const PtrBatch &seg1, int nseg
 // dst.p[b][i] = src[b * words + i]
 void scatter_items(const PtrBatchW &dst, const u64 *src, size_t words, int nb, cudaStream_t s);
 
+// ---- device CKKS encoding ------------------------------------------------------
+// perm[j]: bit-reversed position of slot j in the length-N/2 transform;
+// tw[k] = exp(-2 pi i k / (N/2)), k < N/4
+struct EncTables {
+    const int *perm;
+    const double2 *tw;
+    int logN;
+};
+void enc_tables(int *perm, double2 *tw, int logN, cudaStream_t s);
+// z[v] <- the nvals slot values of vector v (interleaved re, im when cplx, else
+// real), zero in the other slots, in the transform's input order
+void enc_scatter(double2 *z, const double *vals, int nvals, int cplx, int count, const EncTables &t, cudaStream_t s);
+// in-place unnormalised inverse DFT of every vector
+void enc_ifft(double2 *z, int count, const EncTables &t, cudaStream_t s);
+// coefficients of vector v as residues on `rows` rows of `map` into dst.p[v]
+// (coefficient order; |scale * value| below 2^62)
+void enc_round(const PtrBatchW &dst, const double2 *z, int rows, RowMap map, double scale, int count,
+               const EncTables &t, cudaStream_t s);
+// out = i * in slot-wise (multiplication by X^(N/2)): nrows rows, prime of
+// row r is r % nq, iu = [P][4] {w, w', q - w, (q - w)'} (w = psi^(N/2))
+void ew_mul_iunit(u64 *out, const u64 *in, int nrows, int nq, const u64 *iu, int logN, cudaStream_t s);
+// lane split of nb packed ciphertexts p and their conjugates c (both
+// contiguous [nb][2][nq][N]): ev.p[b] = p + c, od.p[b] = i (c - p)
+void lane_split(const PtrBatchW &ev, const PtrBatchW &od, const u64 *pk, const u64 *cj, int nq, int nb, const u64 *iu,
+                int logN, cudaStream_t s);
+
 }  // namespace hb

@@ -200,6 +200,17 @@ class B200Library:
         call("helrm_Encode", ptr, len(arr), int(level), float(scale), ctypes.byref(out))
         return out.value
 
+    def EncodeBatch(self, values, level: int, scale) -> list[int]:
+        """One plaintext per row of ``values`` (count x n reals), encoded on
+        the device in one pass."""
+        arr = np.ascontiguousarray(np.asarray(values, dtype=np.float64))
+        if arr.ndim != 2:
+            raise ValueError("EncodeBatch: values must be a 2-D array (count x n)")
+        outs = np.zeros(arr.shape[0], dtype=np.int32)
+        call("helrm_EncodeBatch", arr.ctypes.data_as(P(c_double)), arr.shape[0], arr.shape[1], int(level),
+             float(scale), outs.ctypes.data_as(P(c_int)))
+        return [int(v) for v in outs]
+
     def EncodeComplex(self, interleaved, level: int, scale) -> int:
         arr, ptr = _f64_array(list(interleaved))
         if len(arr) % 2:
@@ -270,8 +281,11 @@ class B200Library:
         return int(a)
 
     def Negate(self, ct_id):
-        call("helrm_Negate", int(ct_id))
-        return int(ct_id)
+        """A new ciphertext holding -ct (the input is left as it is), like
+        every reference backend's Negate."""
+        out = _out_int()
+        call("helrm_Negate", int(ct_id), ctypes.byref(out))
+        return out.value
 
     def MulPlaintextNew(self, ct_id, pt_id):
         return self._new2("helrm_MulPlaintextNew", ct_id, pt_id)
@@ -377,6 +391,25 @@ class B200Library:
     def Conjugate(self, ct_id):
         call("helrm_Conjugate", int(ct_id))
         return int(ct_id)
+
+    def MulImaginaryUnitNew(self, ct_id):
+        """Slot-wise multiply by sqrt(-1): key-free, no level consumed."""
+        out = _out_int()
+        call("helrm_MulImaginaryUnitNew", int(ct_id), ctypes.byref(out))
+        return out.value
+
+    def MulImaginaryUnit(self, ct_id):
+        call("helrm_MulImaginaryUnit", int(ct_id))
+        return int(ct_id)
+
+    def UnpackLanes(self, packed_ids: Sequence[int], num_real: int) -> list[int]:
+        """Server side of complex-lane packing (orion/core/lane_packing.py:
+        84-115): packed[m] = (x_2m + i x_2m+1) / 2 -> [x_0, x_1, ...], the
+        first num_real of them, one batched conjugation for all inputs."""
+        pa, pp = _int_array(packed_ids)
+        outs = np.zeros(max(1, int(num_real)), dtype=np.int32)
+        call("helrm_UnpackLanes", pp, len(pa), int(num_real), outs.ctypes.data_as(P(c_int)))
+        return [int(v) for v in outs[:int(num_real)]]
 
     # ------------------------------------------------------------ lifecycle
     def DeleteCiphertext(self, ct_id):

@@ -106,7 +106,8 @@ int helrm_SubCiphertextNew(int a, int b, int *out);
 int helrm_SubCiphertext(int a, int b);
 int helrm_MulRelinCiphertextNew(int a, int b, int *out);
 int helrm_MulRelinCiphertext(int a, int b);
-int helrm_Negate(int ct);
+/* Negate -- a new ciphertext -ct (evaluator.go:68-78, cheddar_pybind.cu:1798-1803) */
+int helrm_Negate(int ct, int *out);
 int helrm_AddPlaintextNew(int ct, int pt, int *out);
 int helrm_AddPlaintext(int ct, int pt);
 int helrm_SubPlaintextNew(int ct, int pt, int *out);
@@ -180,6 +181,21 @@ int helrm_GetTableShape(int table, int *rows, int *cols, int *level);
 /* MulConstantMatMulNew / MulPlaintextMatMulNew -- bindings.py:659-697:
  * n = cols input ciphertexts, rows ids written to outs */
 int helrm_MulTableMatMulNew(const int *cts, int n, int table, int *outs);
+
+/* ---- upload path (cheddar_pybind.cu:538-560 Encode, 1825-1837
+ * MulImaginaryUnit; orion/core/lane_packing.py:84-115) -------------------------
+ * Encoding runs on the device: the slot values cross to HBM as doubles and
+ * the special FFT, rounding, residues and NTT happen there.
+ * EncodeBatch: count real vectors of n values each ([count][n], row-major),
+ * one plaintext per vector, ids written to outs. */
+int helrm_EncodeBatch(const double *values, int count, int n, int level, double scale, int *outs);
+/* slot-wise multiplication by sqrt(-1): key-free, no level consumed */
+int helrm_MulImaginaryUnitNew(int ct, int *out);
+int helrm_MulImaginaryUnit(int ct);
+/* complex-lane unpacking of n packed uploads p = (x + i y) / 2: outs[2m] = x,
+ * outs[2m+1] = y of packed[m] (x = p + conj p, y = -i (p - conj p)), the
+ * first num_real of them (0 <= num_real <= 2n) written to outs */
+int helrm_UnpackLanes(const int *packed, int n, int num_real, int *outs);
 
 /* ---- polynomial evaluation (poly_evaluator.py:25-35; cheddar bindings.py:
  * 1102-1116 -> EvaluatePolynomialNative, cheddar_pybind.cu:2207-2262) --------

@@ -159,8 +159,9 @@ def test_add_sub_negate_bit_exact(pair):
     d = pair.ct_data(pair.lib.SubCiphertextNew(a, b)).astype(object)
     assert ((s - (da.astype(object) + db.astype(object))) % q == 0).all()
     assert ((d - (da.astype(object) - db.astype(object))) % q == 0).all()
-    pair.lib.Negate(a)
-    assert ((pair.ct_data(a).astype(object) + da.astype(object)) % q == 0).all()
+    neg = pair.lib.Negate(a)
+    assert neg != a and np.array_equal(pair.ct_data(a), da)  # a fresh ciphertext, input untouched
+    assert ((pair.ct_data(neg).astype(object) + da.astype(object)) % q == 0).all()
 
 
 LT_CASES = [

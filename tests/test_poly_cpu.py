@@ -155,3 +155,17 @@ def test_relu_composite(poly_mod, deep):
     relu = o.rescale(o.relinearize(o.tensor(xs, cur), rlk))
     got = o.decode(o.decrypt(sk, relu), 2.0 ** 36)
     assert np.abs(got - np.maximum(x, 0)).max() < 1e-3
+
+
+def test_pack_lanes_layout():
+    """orion/core/lane_packing.py:60-81: chunk 2m in the real lane and chunk
+    2m+1 in the imaginary lane of packed m, scaled by 0.5, zero padded."""
+    from helrm_b200 import lanes
+    slots = 8
+    v = np.arange(1, 3 * slots - 2, dtype=np.float64)
+    packed, n = lanes.pack_lanes(v, slots)
+    assert n == 3 and lanes.plan_packing(v.size, slots) == (3, 2)
+    flat = np.concatenate([v, np.zeros(4 * slots - v.size)])
+    ch = flat.reshape(4, slots)
+    assert np.array_equal(packed.reshape(2, slots), 0.5 * (ch[0::2] + 1j * ch[1::2]))
+    assert lanes.is_profitable(2 * slots, slots) and not lanes.is_profitable(slots, slots)
