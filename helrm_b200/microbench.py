@@ -299,6 +299,70 @@ def run_relu(batches=(1, 8), reps=3, degrees=(15, 15, 27), level=23, device=0) -
     return out
 
 
+def run_upload(count=64, level=4, reps=3, device=0) -> dict:
+    """The selector upload at LogN 16 (config 2/3 primes), server side of
+    examples/criteo/bench_sweep.py:355-420: `count` real vectors, device
+    encoding one at a time (Encode) and batched (EncodeBatch), and the lane
+    split of count/2 packed ciphertexts (UnpackLanes) against the
+    reference's op-by-op sequence (conjugate, add, sub, i, negate).  CUDA
+    events on the library stream; host-to-device copies of the slot values
+    are inside the encode times."""
+    from helrm_b200 import B200Library, _capi, lanes
+    from helrm_b200.params import CFG2, CFG2_DNUM
+
+    lib = B200Library(dnum=CFG2_DNUM, seed=21, device=device)
+    lib.setup_bindings(CFG2)
+    try:
+        lib.GenerateSecretKey()
+        slots = lib.scheme_info()["slots"]
+        scale = float(1 << CFG2.logscale)
+        capi = _capi.load()
+        rng = np.random.default_rng(0)
+        vals = rng.uniform(-1, 1, (count, slots))
+
+        def timed(fn):
+            # outputs are freed (stream-ordered) after every repetition, so
+            # the memory pool stays at its warmed-up size
+            for _ in range(2):
+                for i, d in fn():
+                    d(i)
+            lib.Synchronize()
+            _capi.check(capi.helrm_TimerStart())
+            for _ in range(reps):
+                for i, d in fn():
+                    d(i)
+            ms = ctypes.c_double(0)
+            _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+            return ms.value / reps
+
+        dp, dc = lib.DeletePlaintext, lib.DeleteCiphertext
+        single = timed(lambda: [(lib.Encode(list(v), level, scale), dp) for v in vals])
+        batch = timed(lambda: [(i, dp) for i in lib.EncodeBatch(vals, level, scale)])
+        packed_vec, num_real = lanes.pack_lanes(vals.ravel(), slots)
+        pts = lanes.encode_packed(lib, packed_vec, slots, level, scale)
+        packed = [lib.Encrypt(p) for p in pts]
+        fused = timed(lambda: [(i, dc) for i in lib.UnpackLanes(packed, num_real)])
+
+        def op_by_op():
+            out = []
+            for pid in packed:
+                conj = lib.ConjugateNew(pid)
+                even = lib.AddCiphertextNew(pid, conj)
+                diff = lib.SubCiphertextNew(pid, conj)
+                lib.MulImaginaryUnit(diff)
+                odd = lib.Negate(diff)
+                dc(conj)
+                dc(diff)
+                out.extend([(even, dc), (odd, dc)])
+            return out
+        ops = timed(op_by_op)
+        return {"op": "selector_upload", "vectors": count, "level": level, "ms_encode_each": single / count,
+                "ms_encode_batch_per_vector": batch / count, "ms_unpack_fused": fused,
+                "ms_unpack_op_by_op": ops, "packed_cts": len(packed)}
+    finally:
+        lib.DeleteScheme()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batches", default="1,16,128")
@@ -307,6 +371,7 @@ def main():
     ap.add_argument("--rotations", type=int, default=32)
     ap.add_argument("--table", action="store_true", help="also the IVE lookup's one-pass table product")
     ap.add_argument("--relu", action="store_true", help="also Orion's composite ReLU through EvaluatePolynomial")
+    ap.add_argument("--upload", action="store_true", help="also the selector upload (device encode, lane split)")
     args = ap.parse_args()
     run([int(b) for b in args.batches.split(",")], args.reps, args.ops, args.rotations,
         emit=lambda line: print(json.dumps(line), flush=True))
@@ -315,6 +380,8 @@ def main():
     if args.relu:
         for line in run_relu():
             print(json.dumps(line), flush=True)
+    if args.upload:
+        print(json.dumps(run_upload()), flush=True)
 
 
 if __name__ == "__main__":
