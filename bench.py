@@ -21,6 +21,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -48,6 +49,8 @@ def parse():
                          "ranks, one batch, partial ciphertexts summed by one NCCL reduce (strong scaling)")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--level", type=int, default=23, help="PCMM input level (23 = all 24 limbs)")
+    ap.add_argument("--bsgs-ratio", type=float, default=8.0,
+                    help="the embedding layer's bsgs_ratio (orion/nn/linear.py:149; bs = ceil(sqrt(512 * ratio)))")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cfg3", action="store_true", help="skip the config-3 primitive microbenchmark")
@@ -208,13 +211,13 @@ def oracle_for_cfg2():
     return om, om.Oracle(CFG2.logn, main, aux, CFG2_DNUM)
 
 
-def cpu_operands_own(o, om, ks, diags, rot, x, level, threads, seed=4242):
+def cpu_operands_own(o, om, ks, diags, rot, x, level, threads, ratio, seed=4242):
     """Keys, extended-basis diagonals and one ciphertext for the oracle,
     made on the CPU from its own seed (the reference arm has no GPU)."""
     from concurrent.futures import ThreadPoolExecutor
     from helrm_b200 import workload as W
     from helrm_b200.params import CFG2
-    plan = W.bsgs_plan(ks, 2.0, o.N // 2)
+    plan = W.bsgs_plan(ks, ratio, o.N // 2)
     nq = level + 1
     scale = float(1 << CFG2.logscale)
     # one task per diagonal / key, each single-threaded inside the oracle
@@ -258,7 +261,7 @@ def run_reference(args, dist):
     M, ks, diags, rot, xs = build_workload(1, seed=100)
     om, o = oracle_for_cfg2()
     t0 = time.time()
-    ct, pts, stride, keys = cpu_operands_own(o, om, ks, diags, rot, xs[0], args.level, threads)
+    ct, pts, stride, keys = cpu_operands_own(o, om, ks, diags, rot, xs[0], args.level, threads, args.bsgs_ratio)
     setup = time.time() - t0
     times_all, _ = cpu_pcmm_times(o, om, ct, ks, pts, stride, keys, rot, threads, reps=args.warmup + args.steps)
     times = times_all[args.warmup:]
@@ -278,11 +281,17 @@ def run_reference(args, dist):
     print(json.dumps(line), flush=True)
 
 
+def bs_of(ratio):
+    """baby steps of the 512-diagonal transform (cheddar bindings.py:160-175 rule)"""
+    return max(1, math.ceil(math.sqrt(512 * ratio)))
+
+
 def cfg_dict(args, batch):
     d = {"workload": "cfg2: 26-table block-diagonal embedding PCMM (BASELINE configs[1])",
          "logN": 16, "slots": 32768, "q_limbs": 24, "q_bits": 36, "special_primes": 4, "p_bits": 60,
          "dnum": 4, "pcmm_level": args.level, "matrix": "416x4224 block-diagonal", "diagonals": 512,
-         "bs": 32, "giant_groups": 16, "fold_rotations": 6, "batch_ciphertexts": batch,
+         "bsgs_ratio": args.bsgs_ratio, "bs": bs_of(args.bsgs_ratio), "giant_groups": -(-512 // bs_of(args.bsgs_ratio)),
+         "fold_rotations": 6, "batch_ciphertexts": batch,
          "queries_per_ciphertext": 1, "parallelism": f"dp{args.gpus} (query batch)",
          "l2": "inputs larger than L2 (1.5 GiB ciphertexts, 7 GiB diagonals, 5.7 GiB keys per step)"}
     if getattr(args, "small", False):
@@ -337,7 +346,7 @@ def run_b200(args, dist):
     info = lib.scheme_info()
     slots, N = info["slots"], info["N"]
     data = np.concatenate([diags[k].astype(np.float64) for k in ks])
-    lt = lib.GenerateLinearTransform(ks, data, args.level, 2.0, "none")
+    lt = lib.GenerateLinearTransform(ks, data, args.level, args.bsgs_ratio, "none")
     for k in lib.GetLinearTransformRotationKeys(lt):
         lib.GenerateLinearTransformRotationKey(k)
     for i in range(1, rot + 1):
@@ -439,14 +448,18 @@ def run_b200(args, dist):
     # input (examples/criteo/table2.py:212, examples/criteo/network.py:209-211)
     low = None
     if not args.small and args.level > 4 and dist.world == 1:
+        # at 5 limbs the giant steps are cheap: the reference's default ratio
+        # 2 (bs 32) is the faster split there
         lt4 = lib.GenerateLinearTransform(ks, data, 4, 2.0, "none")
+        for k in lib.GetLinearTransformRotationKeys(lt4):
+            lib.GenerateLinearTransformRotationKey(k)
         cts4 = encrypt_batch(4)
         for _ in range(args.warmup):
             for oo in step(cts4, lt4):
                 lib.DeleteCiphertext(oo)
         ms4, _ = timed_steps(args.steps, cts4, lt4)
         low = {"note": "not the headline: selector at level 4 (5 q limbs), the reference's placement",
-               "pcmm_level": 4, "ms_per_step": ms4 / args.steps,
+               "pcmm_level": 4, "bsgs_ratio": 2.0, "bs": bs_of(2.0), "ms_per_step": ms4 / args.steps,
                "value": args.batch * args.steps / (ms4 / 1000.0), "unit": UNIT}
         for c in cts4:
             lib.DeleteCiphertext(c)
@@ -511,7 +524,7 @@ def run_b200(args, dist):
             from helrm_b200 import workload as W
             om, o = oracle_for_cfg2()
             t0 = time.time()
-            plan = W.bsgs_plan(ks, 2.0, slots)
+            plan = W.bsgs_plan(ks, args.bsgs_ratio, slots)
             gal = sorted({o.galois(d) for d in plan["rotation_keys"]} |
                          {o.galois(slots >> i) for i in range(1, rot + 1)})
             keys = {g: lib.GetKeyData(g) for g in gal}
@@ -658,7 +671,8 @@ def run_b200_tables(args, dist):
             "config": dict(cfg_dict(args, args.batch), parallelism=f"tables{dist.world} (26 tables over "
                            f"{dist.world} ranks, one NCCL reduce of the packed partial ciphertexts)",
                            shard_tables=[len(r) for r in S.table_shards(26, dist.world)],
-                           shard_block_height=se.bh, shard_diagonals=len(se.ks), shard_fold_rotations=se.rot),
+                           shard_block_height=se.bh, shard_diagonals=len(se.ks), shard_fold_rotations=se.rot,
+                           shard_bsgs_ratio=se.ratio),
             "mode": "tables", "rel_err_embedding": rel_err, "correct": correct, "clocks": clk,
             "exchange_bytes_per_rank": args.batch * words * 8, "e2e": None,
         }

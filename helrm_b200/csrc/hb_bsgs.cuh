@@ -40,10 +40,13 @@ __device__ __forceinline__ void cp_async_wait() {
 
 }  // namespace
 
-// Shared-memory words of one launch (descriptors, key tiles, R tile, two
-// gather buffers, rotation tables).
-__host__ __device__ inline size_t bsgs_smem_words(int beta) {
-    return (size_t)HB_BCH * (sizeof(BabyDesc) / 8) + (size_t)HB_BCH * beta * 2 * HB_BT + (size_t)HB_BCH * 3 * HB_BT +
+// Shared-memory words of one launch (descriptors, key tiles, R tiles of
+// `pair` batch items, two gather buffers, rotation tables).  The
+// fixed-shape kernels read the descriptors only while setting up, so they
+// keep them in the first R tile's space.
+__host__ __device__ inline size_t bsgs_smem_words(int beta, int pair = 1, bool fixed = false) {
+    return (fixed ? 0 : (size_t)HB_BCH * (sizeof(BabyDesc) / 8)) + (size_t)HB_BCH * beta * 2 * HB_BT +
+           (size_t)pair * HB_BCH * 3 * HB_BT +
            (size_t)2 * HB_BCH * (beta + 1) * HB_BT + (size_t)HB_BCH * HB_BT / 8 + HB_BCH / 2 +
            (size_t)HB_BCH * (beta + 1) * (HB_BT / 2);  // gather descriptors (fixed-shape kernels)
 }
@@ -58,6 +61,13 @@ __host__ __device__ inline size_t bsgs_smem_words(int beta) {
 // every one at or above 2^40 (128-bit products).  Row e of the extended
 // basis is blockIdx.y + e0.
 //
+// PAIR = 2 (fixed-shape kernels, chunks of at most HB_GCH / 2 giant slots):
+// two batch items per iteration.  Both gather buffers hold the pair, phase A
+// builds both R tiles, and in phase B the upper half of the block's giant
+// groups works on the second item, so every thread stays busy when a chunk
+// has half the giant slots (bs = 2 x 32 for 512 diagonals).  The next
+// pair's gathers are issued after phase A and overlap phase B.
+//
 // The automorphism X -> X^g maps every aligned tile of 16 coefficients (in
 // the bit-reversed NTT order) onto another aligned tile of 16, permuted:
 // for t = n0 + i the low 4 bits of t land in the top bits of brv(t), and
@@ -66,7 +76,7 @@ __host__ __device__ inline size_t bsgs_smem_words(int beta) {
 // gathers for a tile are therefore one contiguous 128-byte segment per
 // digit row, fetched with asynchronous copies one batch item ahead of the
 // arithmetic (double buffer); the in-tile permutation is a table built once.
-template <int NBF, int BETA, int ROWS>
+template <int NBF, int BETA, int ROWS, int PAIR = 1>
 __global__ void __launch_bounds__(kThreads, 2)
     k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
                int K, int L, int beta_rt, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch, int e0,
@@ -88,16 +98,20 @@ __global__ void __launch_bounds__(kThreads, 2)
     // gather descriptors, and the identity baby handled as a rotated one
     // whose key tile holds P mod q at (row 0, b) and (row 1, a)
     constexpr bool kFixed = NBF != 0 && BETA != 0;
+    static_assert(PAIR == 1 || (PAIR == 2 && kFixed), "paired items need the fixed-shape kernel");
     const u64 pq_e = qrow ? pmod_q[e] : 0;
 
     // shared memory: descriptors | key tiles [nb][beta][2][BT] | R [nb][BT][2]
     // | gathers [2][nb][beta+1][BT] | in-tile offsets [nb][BT] (bytes) |
     // source tile bases [nb]
+    constexpr size_t kRW = (size_t)HB_BCH * 3 * HB_BT;  // R tile + digit sums of one item
+    static_assert(!kFixed || HB_BCH * (sizeof(BabyDesc) / 8) <= kRW, "descriptors fit in an R tile");
+    // fixed shape: [R tiles | keys | ...] with the descriptors in the first R
+    // tile until the loop starts; otherwise [descriptors | keys | R tiles | ...]
     BabyDesc *sdesc = reinterpret_cast<BabyDesc *>(sm);
-    u64 *skey = sm + (size_t)HB_BCH * (sizeof(BabyDesc) / 8);
-    u64 *sR = skey + (size_t)HB_BCH * beta * 2 * HB_BT;
-    uint2 *sRs = reinterpret_cast<uint2 *>(sR + (size_t)HB_BCH * 2 * HB_BT);  // split-29 digit sums of R
-    u64 *sG = sR + (size_t)HB_BCH * 3 * HB_BT;
+    u64 *sR = kFixed ? sm : sm + (size_t)HB_BCH * (sizeof(BabyDesc) / 8) + (size_t)HB_BCH * beta * 2 * HB_BT;
+    u64 *skey = kFixed ? sm + PAIR * kRW : sm + (size_t)HB_BCH * (sizeof(BabyDesc) / 8);
+    u64 *sG = kFixed ? skey + (size_t)HB_BCH * beta * 2 * HB_BT : sR + PAIR * kRW;
     unsigned char *soff = reinterpret_cast<unsigned char *>(sG + (size_t)2 * HB_BCH * R1 * HB_BT);
     unsigned *sblk = reinterpret_cast<unsigned *>(soff + HB_BCH * HB_BT);
     u64 *sgd = reinterpret_cast<u64 *>(sblk + HB_BCH);  // gather descriptors [NCH][kThreads]
@@ -214,7 +228,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     issue(0, 0);
 
     // plaintexts of (giant slot gi, baby bb) at this thread's coefficient
-    const int gi = tid / HB_BT, nl = tid % HB_BT;
+    const int gi = (tid / HB_BT) % (HB_GCH / PAIR), nl = tid % HB_BT;
+    const int sub_t = (tid / HB_BT) / (HB_GCH / PAIR);  // item of the pair this thread accumulates
     const bool gactive = gi < ch.gcount;
     const size_t pt_off = ((size_t)(qrow ? e : pt_nq + (e - nq)) << logN) + n0 + nl;
     u64 ptv[HB_BCH];
@@ -234,20 +249,30 @@ __global__ void __launch_bounds__(kThreads, 2)
     const double qd = u64_to_d(pc.q);
     const double2 pqw = make_double2(u64_to_d(pq), __dmul_rn(u64_to_d(pq), pc.qinv));
 
-    for (int b = 0; b < nbatch; b++) {
-        if (b + 1 < nbatch) {
+    if (PAIR == 2 && nbatch > 1) issue(1, 1);
+    for (int b = 0; b < nbatch; b += PAIR) {
+        const bool two = PAIR == 2 && b + 1 < nbatch;
+        if (PAIR == 2) {
+            cp_async_wait<0>();
+        } else if (b + 1 < nbatch) {
             issue(b + 1, (b + 1) & 1);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncthreads();
-        const u64 *Gb = sG + (b & 1) * gbuf;
         // ---- phase A: baby rotations of this tile, from the gathered rows
+        constexpr int kItems = NBF ? NBF * HB_BT : HB_BCH * HB_BT;
 #pragma unroll
-        for (int it0 = 0; it0 < (NBF ? NBF * HB_BT : HB_BCH * HB_BT); it0 += kThreads) {
-            const int it = it0 + tid;
+        for (int it0 = 0; it0 < PAIR * kItems; it0 += kThreads) {
+            const int itp = it0 + tid;
+            const int sub = PAIR == 2 ? itp / kItems : 0;
+            const int it = PAIR == 2 ? itp - sub * kItems : itp;
             if (!NBF && it >= nb * HB_BT) break;
+            if (PAIR == 2 && sub == 1 && !two) break;
+            const u64 *Gb = sG + (PAIR == 2 ? sub : (b & 1)) * gbuf;
+            u64 *sRi = sR + sub * kRW;
+            uint2 *sRsi = reinterpret_cast<uint2 *>(sRi + (size_t)HB_BCH * 2 * HB_BT);
             const int bb = it / HB_BT, n = it % HB_BT;
             const u64 *g = Gb + (size_t)bb * R1 * HB_BT;
             u64 rb, ra;
@@ -289,21 +314,28 @@ __global__ void __launch_bounds__(kThreads, 2)
             // phase B; on fast limbs also the digit sums lo + hi of both
             if (fast) {
                 const u64 pb = k29_pack(rb), pa = k29_pack(ra);
-                reinterpret_cast<ulonglong2 *>(sR)[bb * HB_BT + n] = make_ulonglong2(pb, pa);
-                sRs[bb * HB_BT + n] = make_uint2(k29_sum(pb), k29_sum(pa));
+                reinterpret_cast<ulonglong2 *>(sRi)[bb * HB_BT + n] = make_ulonglong2(pb, pa);
+                sRsi[bb * HB_BT + n] = make_uint2(k29_sum(pb), k29_sum(pa));
             } else {
-                reinterpret_cast<ulonglong2 *>(sR)[bb * HB_BT + n] = make_ulonglong2(rb, ra);
+                reinterpret_cast<ulonglong2 *>(sRi)[bb * HB_BT + n] = make_ulonglong2(rb, ra);
             }
         }
         __syncthreads();
+        if (PAIR == 2) {
+            // phase A is done with both gather buffers: the next pair's
+            // copies overlap phase B
+            if (b + 2 < nbatch) issue(b + 2, 0);
+            if (b + 3 < nbatch) issue(b + 3, 1);
+        }
         // ---- phase B: inner[g] += pt(g, b) * R_b.  Karatsuba split-29 sums
         // of at most 32 products need no intermediate normalisation; one
         // reduction per output.  128-bit sums of at most 32 products below
         // 2^122 need no intermediate reduction either.
-        if (gactive) {
-            const ulonglong2 *R2 = reinterpret_cast<const ulonglong2 *>(sR) + nl;
-            const uint4 *R4 = reinterpret_cast<const uint4 *>(sR) + nl;
-            const uint2 *RS = sRs + nl;
+        if (gactive && (PAIR == 1 || sub_t == 0 || two)) {
+            const u64 *sRt = sR + sub_t * kRW;
+            const ulonglong2 *R2 = reinterpret_cast<const ulonglong2 *>(sRt) + nl;
+            const uint4 *R4 = reinterpret_cast<const uint4 *>(sRt) + nl;
+            const uint2 *RS = reinterpret_cast<const uint2 *>(sRt + (size_t)HB_BCH * 2 * HB_BT) + nl;
             u64 vb, va;
             if (fast) {
                 // the q-row kernel alternates two sets of sums over the
@@ -340,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 vb = reduce128(ab, pc);
                 va = reduce128(aa, pc);
             }
-            u64 *o = inner + b * inner_stride + (size_t)(ch.gbase + gi) * 2 * nall + erow + n0 + nl;
+            u64 *o = inner + (b + sub_t) * inner_stride + (size_t)(ch.gbase + gi) * 2 * nall + erow + n0 + nl;
             if (ch.accumulate) {
                 vb = add_mod(vb, o[0], pc.q);
                 va = add_mod(va, o[nall], pc.q);

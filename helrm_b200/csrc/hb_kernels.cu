@@ -2032,7 +2032,11 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
                    int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride, size_t d_stride,
                    size_t inner_stride, cudaStream_t s) {
     if (ch.nbabies > HB_BCH || ch.gcount > HB_GCH) throw std::invalid_argument("bsgs chunk too large");
-    const size_t smem = bsgs_smem_words(beta) * 8;
+    const bool split = beta == 4 && primes_sized(0, nq, true) && primes_sized(L, K, false);
+    const bool full = ch.nbabies == HB_BCH;
+    // chunks of at most half the giant slots: two batch items per iteration
+    const bool pair = split && full && ch.gcount <= HB_GCH / 2 && nbatch > 1;
+    const size_t smem = bsgs_smem_words(beta, pair ? 2 : 1, split && full) * 8;
     if (smem > 227 * 1024 || beta > HB_MAX_BETA)
         throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
     static size_t attr = 0;
@@ -2043,13 +2047,14 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
         cudaFuncSetAttribute(k_bsgs_mac<0, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaFuncSetAttribute(k_bsgs_mac<0, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = smem;
     }
     const size_t n = (size_t)(nq + K) << logN;
     // per ciphertext: c0/c1 rows, the digits, the inner sums written; per
     // launch: every baby key and plaintext of the chunk once
     const double nd = (double)n, nqw = (double)nq * (1 << logN);
-    const bool split = beta == 4 && primes_sized(0, nq, true) && primes_sized(L, K, false);
     ProfScope ps(KC_BSGS_MAC,
                  8.0 * (nbatch * (2.0 * nqw + beta * nd + 2.0 * ch.gcount * nd * (ch.accumulate ? 2 : 1)) +
                         2.0 * beta * ch.nkeys * nd + ch.npts * nd),
@@ -2058,21 +2063,23 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
     // benchmark parameter sets at the top level) and q rows below 2^40 with
     // special rows above it: one launch per kind of row, each with a single
     // product form.  Anything else runs the generic form over every row.
-#define HB_BSGS_LAUNCH(NBF_, BETA_, ROWS_, E0_, NROWS_)                                                         \
-    k_bsgs_mac<NBF_, BETA_, ROWS_><<<dim3((1u << logN) / HB_BT, NROWS_), HB_GCH * HB_BT, smem, s>>>(           \
+#define HB_BSGS_LAUNCH(NBF_, BETA_, ROWS_, PAIR_, E0_, NROWS_)                                                  \
+    k_bsgs_mac<NBF_, BETA_, ROWS_, PAIR_><<<dim3((1u << logN) / HB_BT, NROWS_), HB_GCH * HB_BT, smem, s>>>(    \
         inner, ct, D, ch, nq, K, L, beta, keyP, pt_nq, pmod_q, logN, nbatch, E0_, ct_stride, d_stride, inner_stride)
-    const bool full = ch.nbabies == HB_BCH;
     if (split) {
-        if (full) {
-            HB_BSGS_LAUNCH(HB_BCH, 4, 1, 0, nq);
-            if (K) HB_BSGS_LAUNCH(HB_BCH, 4, 2, nq, K);
+        if (pair) {
+            HB_BSGS_LAUNCH(HB_BCH, 4, 1, 2, 0, nq);
+            if (K) HB_BSGS_LAUNCH(HB_BCH, 4, 2, 2, nq, K);
+        } else if (full) {
+            HB_BSGS_LAUNCH(HB_BCH, 4, 1, 1, 0, nq);
+            if (K) HB_BSGS_LAUNCH(HB_BCH, 4, 2, 1, nq, K);
         } else {
-            HB_BSGS_LAUNCH(0, 4, 1, 0, nq);
-            if (K) HB_BSGS_LAUNCH(0, 4, 2, nq, K);
+            HB_BSGS_LAUNCH(0, 4, 1, 1, 0, nq);
+            if (K) HB_BSGS_LAUNCH(0, 4, 2, 1, nq, K);
         }
     } else {
-        if (full) HB_BSGS_LAUNCH(HB_BCH, 0, 0, 0, nq + K);
-        else HB_BSGS_LAUNCH(0, 0, 0, 0, nq + K);
+        if (full) HB_BSGS_LAUNCH(HB_BCH, 0, 0, 1, 0, nq + K);
+        else HB_BSGS_LAUNCH(0, 0, 0, 1, 0, nq + K);
     }
 #undef HB_BSGS_LAUNCH
     check_launch("bsgs_mac");

@@ -70,3 +70,31 @@ def test_fixed_shape_fold_bit_exact(pair4):
             r = pair4.o.rotate(x, pair4.key(g), g)
             x = ((x.astype(object) + r.astype(object)) % q).astype(np.uint64)
         assert np.array_equal(pair4.ct_data(c), x)
+
+
+@pytest.mark.parametrize("nb", [2, 4, 5])
+def test_paired_items_bit_exact(pair4, nb):
+    """Chunks of at most 8 giant slots run two batch items per iteration:
+    512 diagonals at bs = 64 (ratio 8) give two full baby chunks over the
+    same 8 giant slots (the second accumulating), at even and odd batches."""
+    rng = np.random.default_rng(50 + nb)
+    slots = pair4.slots
+    ks = list(range(512))
+    diags = {k: rng.uniform(-0.5, 0.5, slots) for k in ks}
+    data = np.concatenate([diags[k] for k in ks])
+    lt = pair4.lib.GenerateLinearTransform(ks, data, LEVEL, 8.0, "none")
+    plan = W.bsgs_plan(ks, 8.0, slots)
+    assert plan["bs"] == 64 and pair4.lib.GetLinearTransformInfo(lt)["bs"] == 64
+    for kk in pair4.lib.GetLinearTransformRotationKeys(lt):
+        pair4.lib.GenerateLinearTransformRotationKey(kk)
+    xs = [rng.uniform(-1, 1, slots) for _ in range(nb)]
+    cts = [pair4.encrypt(x) for x in xs]
+    outs = pair4.lib.EvaluateLinearTransformBatch(lt, cts)
+    pts = [pair4.lib.GetLinearTransformPlaintext(lt, k) for k in ks]
+    keys = {pair4.o.galois(d): pair4.key(pair4.o.galois(d)) for d in plan["rotation_keys"]}
+    for c, o in zip(cts, outs):
+        want = pair4.o.bsgs_lt(pair4.ct_data(c), ks, pts, plan["stride"], keys)
+        assert np.array_equal(pair4.ct_data(o), want)
+    got = pair4.decrypt(pair4.lib.RescaleNew(outs[-1]))
+    assert np.abs(got - W.cleartext_lt(xs[-1], diags, slots)).max() < 1e-3
+    pair4.lib.DeleteLinearTransform(lt)

@@ -233,3 +233,32 @@ def test_cfg3_ntt_batch16_bit_exact(cfg2):
     _capi.check(lib.helrm_kernel_ntt(ctypes.c_void_p(dev.data_ptr()), rows, nq, nq, 1, None))
     _capi.check(lib.helrm_Synchronize())
     assert np.array_equal(dev.cpu().numpy().view(np.uint64).reshape(B, 2, nq, N), host)
+
+
+def test_cfg2_pcmm_bench_ratio_bit_exact(cfg2):
+    """The headline step as the bench runs it (bsgs_ratio 8: bs 64, two full
+    baby chunks over 8 giant slots, the paired-item MAC kernel), batch of
+    two, every residue against the oracle at the same split."""
+    import os
+    V = W.cfg2_vocab()
+    M = W.block_diag_matrix(V, 64, 16, 0.05, seed=0)
+    xs = [W.selector(qq, V) for qq in W.zipf_queries(V, 2, seed=5)]
+    lt, ks, diags, rot, cts, outs = _pcmm(cfg2, M, xs, cfg2.info["max_level"], ratio=8.0)
+    info = cfg2.lib.GetLinearTransformInfo(lt)
+    assert info["bs"] == 64 and info["n_giant"] == 8
+    o = cfg2.o
+    cfg2.om.set_threads(os.cpu_count() or 1)
+    try:
+        plan = W.bsgs_plan(ks, 8.0, cfg2.slots)
+        gal = {o.galois(d) for d in plan["rotation_keys"]} | {o.galois(cfg2.slots >> i) for i in range(1, rot + 1)}
+        keys = {g: cfg2.key(g) for g in sorted(gal)}
+        pts = [cfg2.lib.GetLinearTransformPlaintext(lt, k) for k in ks]
+        for x, c, out in zip(xs, cts, outs):
+            want = o.pcmm(cfg2.ct_data(c), ks, pts, plan["stride"], keys, rot)
+            assert np.array_equal(cfg2.ct_data(out), want)
+            got = cfg2.decrypt(out)[:416]
+            ref = M.astype(np.float64) @ x
+            assert np.abs(got - ref).max() <= REL_TOL * np.abs(ref).max()
+    finally:
+        cfg2.om.set_threads(1)
+    cfg2.lib.DeleteLinearTransform(lt)
