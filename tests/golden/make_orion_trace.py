@@ -35,6 +35,14 @@ CONFIG = {
                     "RingType": "Standard"},
     "orion": {"backend": "b200", "io_mode": "none", "debug": False, "embedding_method": "hybrid", "margin": 2},
 }
+# the ReLU network: 20 primes, enough levels for Linear -> ReLU (15 levels:
+# prescale, the [15, 15, 27] sign stages, x * step(x)) -> Linear without
+# bootstrapping
+CONFIG_DEEP = {
+    "ckks_params": {"LogN": 13, "LogQ": [40] + [36] * 19, "LogP": [60] * 4, "LogScale": 36, "H": 192,
+                    "RingType": "Standard"},
+    "orion": dict(CONFIG["orion"]),
+}
 
 
 class Recorder:
@@ -48,7 +56,7 @@ class Recorder:
         self.calls = []
         self.arrays = {}
         self.next_id = 1
-        self.cts, self.pts, self.lts = {}, {}, {}
+        self.cts, self.pts, self.lts, self.polys = {}, {}, {}, {}
 
     # -- logging helpers -------------------------------------------------
     def _arr(self, values):
@@ -146,6 +154,80 @@ class Recorder:
     def AddRotationKey(self, k):
         self._log("AddRotationKey", [int(k)], None)
 
+    # -- scalars and ciphertext products (the B200Library's scale rules) ---
+    def _scalar(self, name, ct, v, inplace, square):
+        meta = dict(self.cts[ct])
+        if square:
+            meta["scale"] = meta["scale"] * meta["scale"]
+        if inplace:
+            self.cts[ct] = meta
+            return self._log(name, [{"ct": ct}, v], {"ct": ct})["ct"]
+        i = self._ct_new(meta)
+        return self._log(name, [{"ct": ct}, v], {"ct": i})["ct"]
+
+    def MulScalarIntNew(self, ct, v):
+        return self._scalar("MulScalarIntNew", ct, int(v), False, False)
+
+    def MulScalarInt(self, ct, v):
+        return self._scalar("MulScalarInt", ct, int(v), True, False)
+
+    def MulScalarFloatNew(self, ct, v):
+        return self._scalar("MulScalarFloatNew", ct, float(v), False, True)
+
+    def MulScalarFloat(self, ct, v):
+        return self._scalar("MulScalarFloat", ct, float(v), True, True)
+
+    def AddScalarNew(self, ct, v):
+        return self._scalar("AddScalarNew", ct, float(v), False, False)
+
+    def AddScalar(self, ct, v):
+        return self._scalar("AddScalar", ct, float(v), True, False)
+
+    def _relin(self, name, a, b, inplace):
+        ma, mb = self.cts[a], self.cts[b]
+        meta = {"level": min(ma["level"], mb["level"]), "scale": ma["scale"] * mb["scale"],
+                "slots": max(ma["slots"], mb["slots"])}
+        if inplace:
+            self.cts[a] = meta
+            return self._log(name, [{"ct": a}, {"ct": b}], {"ct": a})["ct"]
+        i = self._ct_new(meta)
+        return self._log(name, [{"ct": a}, {"ct": b}], {"ct": i})["ct"]
+
+    def MulRelinCiphertextNew(self, a, b):
+        return self._relin("MulRelinCiphertextNew", a, b, False)
+
+    def MulRelinCiphertext(self, a, b):
+        return self._relin("MulRelinCiphertext", a, b, True)
+
+    # -- polynomials -------------------------------------------------------
+    def GenerateMinimaxSignCoeffs(self, degrees, prec, logalpha, logerr, debug):
+        sys.path.insert(0, ROOT)
+        from helrm_b200.library import _composite_sign_coeffs
+        out = _composite_sign_coeffs([int(d) for d in degrees], 2.0 ** (-float(logalpha)))
+        return self._log("GenerateMinimaxSignCoeffs", [[int(d) for d in degrees], int(prec), int(logalpha),
+                                                       int(logerr), int(debug)], out)
+
+    def _poly(self, name, coeffs):
+        c = [float(x) for x in coeffs]
+        i = self._new(self.polys, {"n": len(c)})
+        return self._log(name, [self._arr(c)], {"poly": i})["poly"]
+
+    def GenerateChebyshev(self, coeffs):
+        return self._poly("GenerateChebyshev", coeffs)
+
+    def GenerateMonomial(self, coeffs):
+        return self._poly("GenerateMonomial", coeffs)
+
+    def EvaluatePolynomial(self, ct, poly, scale=None):
+        n = self.polys[poly]["n"]
+        depth = math.ceil(math.log2(n)) if n >= 3 else 1
+        meta = dict(self.cts[ct])
+        meta["level"] -= depth
+        meta["scale"] = float(scale) if scale is not None else self._default_scale
+        i = self._ct_new(meta)
+        return self._log("EvaluatePolynomial", [{"ct": ct}, {"poly": poly},
+                                                None if scale is None else float(scale)], {"ct": i})["ct"]
+
     def _binary(self, name, a, b, inplace, kind_b="ct"):
         ma = self.cts[a]
         mb = self.cts[b] if kind_b == "ct" else self.pts[b]
@@ -205,6 +287,13 @@ class Recorder:
         return self._log("EvaluateLinearTransform", [{"lt": lt}, {"ct": ct}], {"ct": i})["ct"]
 
     def DeleteLinearTransform(self, lt):
+        # layers of a network recorded earlier in this process are garbage
+        # collected while the next one runs, and their __del__
+        # (orion/nn/linear.py:41-46) deletes their transforms through the
+        # current backend: ids this recorder never handed out are not part
+        # of the recorded flow
+        if lt not in self.lts:
+            return
         self.lts.pop(lt, None)
         self._log("DeleteLinearTransform", [{"lt": lt}], None)
 
@@ -265,7 +354,7 @@ def _import_reference(ref_root):
     return orion
 
 
-def record(net_kind: str, ref_root: str):
+def record(net_kind: str, ref_root: str, config=None):
     import torch
 
     orion = _import_reference(ref_root)
@@ -275,8 +364,9 @@ def record(net_kind: str, ref_root: str):
     from helrm_b200 import orion_adapter
     from oracle import oracle as om
 
-    main, _aux = om.scheme_primes(CONFIG["ckks_params"]["LogQ"], CONFIG["ckks_params"]["LogP"],
-                                  CONFIG["ckks_params"]["LogN"])
+    config = config or CONFIG
+    main, _aux = om.scheme_primes(config["ckks_params"]["LogQ"], config["ckks_params"]["LogP"],
+                                  config["ckks_params"]["LogN"])
     holder = {}
 
     def factory():
@@ -295,6 +385,24 @@ def record(net_kind: str, ref_root: str):
                 return self.fc(x)
         net = Net()
         inp = torch.randn(1, 32)
+    elif net_kind == "mlp_relu":
+        class Net(on.Module):
+            def __init__(self):
+                super().__init__()
+                self.fc1 = on.Linear(16, 8)
+                self.act = on.ReLU()
+                self.fc2 = on.Linear(8, 4)
+
+            def forward(self, x):
+                return self.fc2(self.act(self.fc1(x)))
+        net = Net()
+        # an input whose hidden pre-activations stay clear of the sign's gap
+        # (|h| >= 0.05 max|h|), where the composite step is within 1e-4
+        for seed in range(100):
+            inp = torch.randn(1, 16, generator=torch.Generator().manual_seed(seed))
+            h = net.fc1(inp).detach().abs()
+            if float(h.min()) >= 0.05 * float(h.max()):
+                break
     else:
         class Net(on.Module):
             def __init__(self):
@@ -306,7 +414,7 @@ def record(net_kind: str, ref_root: str):
         net = Net()
         inp = torch.zeros(1, 64)
         inp[0, 37] = 1.0  # one-hot selector, the HE-LRM lookup's input
-    scheme = orion.init_scheme(CONFIG)
+    scheme = orion.init_scheme(config)
     rec = holder["rec"]
     net.eval()
     out_clear = net(inp).detach().numpy().ravel()
@@ -329,8 +437,8 @@ def main():
     if not ref or not os.path.isdir(ref):
         raise SystemExit("usage: make_orion_trace.py <reference checkout>")
     traces, arrays = {}, {}
-    for kind in ("linear", "embedding"):
-        rec, out_clear, decodes, level = record(kind, ref)
+    for kind in ("linear", "embedding", "mlp_relu"):
+        rec, out_clear, decodes, level = record(kind, ref, CONFIG_DEEP if kind == "mlp_relu" else CONFIG)
         traces[kind] = {"params": rec.params, "calls": rec.calls, "output_decode_calls": decodes,
                         "input_level": int(level), "cleartext_output": [float(v) for v in out_clear]}
         for k, v in rec.arrays.items():

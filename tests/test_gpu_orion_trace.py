@@ -3,7 +3,11 @@
 tests/golden/make_orion_trace.py ran the reference's own flow (init_scheme,
 fit, compile, encode, encrypt, the encrypted forward of an ``on.Linear``
 and of an ``on.Embedding`` layer, decrypt, decode; orion/core/orion.py,
-orion/nn/linear.py:99-140, orion/backend/python/lt_evaluator.py:224-275)
+orion/nn/linear.py:99-140, orion/backend/python/lt_evaluator.py:224-275),
+and of a Linear -> ReLU -> Linear network whose ReLU is Orion's composite
+minimax sign [15, 15, 27] (orion/nn/activation.py:201-300: the sign
+coefficients from GenerateMinimaxSignCoeffs, three EvaluatePolynomial
+stages at the levels Orion's compiler placed, x * step(x))
 with ``backend: b200`` registered through helrm_b200.orion_adapter and
 recorded every backend call, in order, with its arguments.  The reference
 cannot travel to the GPU box, so the calls are replayed here on the real
@@ -60,6 +64,8 @@ def _replay(kind):
                 handles[(k, v)] = res
             elif c["m"] == "GetLinearTransformRotationKeys":
                 assert sorted(res) == sorted(r)  # the same key set the recording planned
+            elif c["m"] == "GenerateMinimaxSignCoeffs":
+                assert np.allclose(res, r, rtol=0, atol=1e-12)
             if c["m"] == "Decode":
                 decoded[i] = np.asarray(res)
         out = decoded[t["output_decode_calls"][0]]
@@ -68,7 +74,7 @@ def _replay(kind):
         lib.DeleteScheme()
 
 
-@pytest.mark.parametrize("kind", ["linear", "embedding"])
+@pytest.mark.parametrize("kind", ["linear", "embedding", "mlp_relu"])
 def test_orion_flow_replayed_on_b200(kind):
     out, clear = _replay(kind)
     n = len(clear)
