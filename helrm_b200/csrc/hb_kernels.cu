@@ -6,7 +6,9 @@
 // than once per thread block (NTT twiddle tiles, the per-chunk baby-step
 // descriptors) is staged in shared memory; everything else streams with
 // 16-byte vector accesses.
+#include <cooperative_groups.h>
 #include <cstdio>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -845,10 +847,234 @@ __global__ void __launch_bounds__(256, HB_NTT_ROWS_BLOCKS) k_ntt256_rows(u64 *__
     }
 }
 
+// One-pass 2^16 NTT: a cluster of 8 CTAs holds one limb in shared memory.
+// CTA k runs the column pass on columns [32k, 32k+32) (two groups of 16,
+// exactly the two-pass kernel's arithmetic), leaves the column-transformed
+// values in its shared memory, and after a cluster barrier the row pass on
+// rows [32k, 32k+32) reads its 256 columns from the 8 CTAs' shared memory
+// (distributed shared memory, all within this GPU).  The inverse runs the
+// row pass first.  The limb crosses HBM once each way instead of twice, and
+// every butterfly is the two-pass kernels' own, so the results are
+// identical.  Shared memory: one region reused by the column transposes,
+// the exchange tile and the row transposes (barriers between the uses).
+constexpr int kNttCl = 8;                     // CTAs per limb
+constexpr int kNttClWords = 2 * 256 * 17;     // 8704 words: max of the three uses
+constexpr int kNttXS = 33;                    // forward exchange tile row stride ([256][32])
+constexpr int kNttXSi = 257;                  // inverse exchange tile row stride ([32][256])
+
+template <bool INV>
+__global__ void __cluster_dims__(kNttCl, 1, 1) __launch_bounds__(512, 2)
+    k_ntt_cl(u64 *__restrict__ data, RowMap map, const u64 *__restrict__ tw, const u64 *__restrict__ twp,
+             const ulonglong2 *__restrict__ twx, const double *__restrict__ tws, int row0,
+             const u64 *__restrict__ src, size_t src_stride, int src_per) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ u64 shm[];
+    __shared__ ulonglong2 stw[256];
+    const int row = row0 + blockIdx.y;
+    if (map.skip(row)) return;  // uniform over the cluster (same row)
+    const int k = (int)cluster.block_rank();
+    const int t = threadIdx.x;
+    const int p = map.prime(row);
+    const u64 q = c_pc[p].q;
+    const bool fast = q < (1ull << 40);
+    const double qd = (double)q, qinv = c_pc[p].qinv;
+    const u64 *W = tw + ((size_t)p << 16), *Wp = twp + ((size_t)p << 16);
+    const double *Ts = tws + ((size_t)p << 16);
+    const double2 *stwd = reinterpret_cast<const double2 *>(stw);
+    u64 *limb = data + ((size_t)row << 16);
+    if (fast && t < 256) stw[t] = __ldg(twx + ((size_t)p << 16) + t);
+    // column-pass roles: group g of 16 columns, column col, row phase c
+    const int g = t >> 8, tt = t & 255, col = tt & 15, c = tt >> 4;
+    const int gc = 32 * k + 16 * g + col;
+    u64 *T = shm + g * 256 * 17;
+    // row-pass roles: local row blk, phase cr
+    const int blk = t >> 4, cr = t & 15;
+    const int rb = 32 * k + blk;
+    u64 *sb = shm + blk * 272;
+    double xd[16];
+    u64 x[16];
+    if (!INV) {
+        // ---- column pass (rows c + 16j of column gc)
+        if (fast) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = u64_to_d(limb[((size_t)(c + 16 * j) << 8) + gc]);
+            __syncthreads();  // stw
+            fwd_a_d<false>(xd, stwd, 1, qd);
+#pragma unroll
+            for (int j = 0; j < 16; j++) T[(c + 16 * j) * 17 + col] = (u64)__double_as_longlong(xd[j]);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = __longlong_as_double((long long)T[(16 * c + j) * 17 + col]);
+            fwd_b_d<false>(xd, stwd, 1, c, qd);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) shm[(16 * c + j) * kNttXS + 16 * g + col] = (u64)__double_as_longlong(xd[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = limb[((size_t)(c + 16 * j) << 8) + gc];
+            fwd_a(x, W, Wp, 1, q);
+#pragma unroll
+            for (int j = 0; j < 16; j++) T[(c + 16 * j) * 17 + col] = x[j];
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = T[(16 * c + j) * 17 + col];
+            fwd_b(x, W, Wp, 1, c, q);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) shm[(16 * c + j) * kNttXS + 16 * g + col] = reduce4q(x[j], q);
+        }
+        cluster.sync();
+        // ---- row pass: row rb, columns cr + 16j from CTA j / 2
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const u64 *px = cluster.map_shared_rank(shm, j >> 1);
+            x[j] = px[rb * kNttXS + cr + 16 * (j & 1)];
+        }
+        cluster.sync();  // every remote read done: the region is free again
+        if (fast) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = __longlong_as_double((long long)x[j]);
+            fwd_a_ds(xd, Ts, 256 + rb, qd, qinv);
+#pragma unroll
+            for (int j = 0; j < 16; j++) sb[j * 17 + cr] = (u64)__double_as_longlong(xd[j]);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = __longlong_as_double((long long)sb[cr * 17 + j]);
+            fwd_b_ds(xd, Ts, 256 + rb, cr, qd, qinv);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) sb[cr * 17 + j] = d_mod_to_u64(xd[j], qd, qinv);
+        } else {
+            fwd_a(x, W, Wp, 256 + rb, q);
+#pragma unroll
+            for (int j = 0; j < 16; j++) sb[j * 17 + cr] = x[j];
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = sb[cr * 17 + j];
+            fwd_b(x, W, Wp, 256 + rb, cr, q);
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = reduce4q(x[j], q);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) sb[cr * 17 + j] = x[j];
+        }
+        __syncthreads();
+        u64 *a = limb + ((size_t)rb << 8);
+#pragma unroll
+        for (int j = 0; j < 16; j++) a[cr + 16 * j] = sb[j * 17 + cr];
+    } else {
+        // ---- row pass first (row rb, from src when given)
+        const u64 *ain = src ? src + (size_t)(row / src_per) * src_stride + ((size_t)(row % src_per) << 16) +
+                                   ((size_t)rb << 8)
+                             : limb + ((size_t)rb << 8);
+#pragma unroll
+        for (int j = 0; j < 16; j++) sb[j * 17 + cr] = ain[cr + 16 * j];
+        __syncthreads();
+        u64 *X = shm + blk * kNttXSi;  // local row blk of the exchange tile [32][256]
+        if (fast) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = u64_to_d(sb[cr * 17 + j]);
+            inv_b_ds(xd, Ts, 256 + rb, cr, qd, qinv);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) sb[cr * 17 + j] = (u64)__double_as_longlong(xd[j]);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = __longlong_as_double((long long)sb[j * 17 + cr]);
+            inv_a_ds(xd, Ts, 256 + rb, qd, qinv);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) X[cr + 16 * j] = (u64)__double_as_longlong(xd[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = sb[cr * 17 + j];
+            inv_b(x, W, Wp, 256 + rb, cr, q);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) sb[cr * 17 + j] = x[j];
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = sb[j * 17 + cr];
+            inv_a(x, W, Wp, 256 + rb, q);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) X[cr + 16 * j] = x[j];
+        }
+        cluster.sync();
+        // ---- column pass: column gc, rows 16c + j, all in CTA c / 2
+        {
+            const u64 *px = cluster.map_shared_rank(shm, c >> 1);
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = px[(16 * (c & 1) + j) * kNttXSi + gc];
+        }
+        cluster.sync();
+        if (fast) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = __longlong_as_double((long long)x[j]);
+            inv_b_d<false>(xd, stwd, 1, c, qd, qinv);
+#pragma unroll
+            for (int j = 0; j < 16; j++) T[(16 * c + j) * 17 + col] = (u64)__double_as_longlong(xd[j]);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) xd[j] = __longlong_as_double((long long)T[(c + 16 * j) * 17 + col]);
+            inv_a_d<false, false>(xd, stwd, 1, qd, qinv);
+            const double nid = (double)c_pc[p].ninv;
+            const double2 ni = make_double2(nid, __ddiv_rn(nid, qd));
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                double r = mulmod_d(xd[j], ni, qd);  // |r| <= 0.502 q
+                if (r < 0.0) r = __dadd_rn(r, qd);
+                limb[((size_t)(c + 16 * j) << 8) + gc] =
+                    (u64)__double_as_longlong(__dadd_rn(r, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
+            }
+        } else {
+            inv_b(x, W, Wp, 1, c, q);
+#pragma unroll
+            for (int j = 0; j < 16; j++) T[(16 * c + j) * 17 + col] = x[j];
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 16; j++) x[j] = T[(c + 16 * j) * 17 + col];
+            inv_a(x, W, Wp, 1, q);
+            const u64 ni = c_pc[p].ninv, nip = c_pc[p].ninvp;
+#pragma unroll
+            for (int j = 0; j < 16; j++) limb[((size_t)(c + 16 * j) << 8) + gc] = mul_shoup(x[j], ni, nip, q);
+        }
+    }
+}
+
+// opt-in (HELRM_B200_NTT=cluster): bit-exact, but measured slower than the
+// two-pass kernels (B = 128 ciphertexts of 24 limbs: forward 3.61 ms
+// against 2.34 ms, inverse 3.92 against 2.54): two 512-thread CTAs per SM
+// and two cluster barriers per limb leave too little independent work to
+// hide the load and exchange latency
+static bool ntt_cluster_on() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = std::getenv("HELRM_B200_NTT");
+        on = (e && std::string(e) == "cluster") ? 1 : 0;
+        if (on) {
+            cudaFuncSetAttribute(k_ntt_cl<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kNttClWords * 8);
+            cudaFuncSetAttribute(k_ntt_cl<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kNttClWords * 8);
+        }
+    }
+    return on == 1;
+}
+
 static void ntt256_impl(u64 *data, int nrows, RowMap map, const NttTables &t, bool inv, cudaStream_t s) {
     for (int r0 = 0; r0 < nrows; r0 += 65535) {
         const int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
         const dim3 grid(16, nr);
+        if (ntt_cluster_on()) {
+            const dim3 gcl(kNttCl, nr);
+            if (!inv)
+                k_ntt_cl<false><<<gcl, 512, kNttClWords * 8, s>>>(data, map, t.tw, t.twp, t.twx, t.tws, r0, nullptr,
+                                                                  0, 1);
+            else
+                k_ntt_cl<true><<<gcl, 512, kNttClWords * 8, s>>>(data, map, t.itw, t.itwp, t.itwx, t.itws, r0,
+                                                                 nullptr, 0, 1);
+            continue;
+        }
         if (!inv) {
             k_ntt256_cols<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twx, r0);
             k_ntt256_rows<false><<<grid, 256, 0, s>>>(data, map, t.tw, t.twp, t.twx, t.tws, r0);
@@ -924,6 +1150,11 @@ void ntt_inverse_from(u64 *dst, const u64 *src, size_t src_stride, int per_item,
     for (int r0 = 0; r0 < nrows; r0 += 65535) {
         const int nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
         const dim3 grid(16, nr);
+        if (ntt_cluster_on()) {
+            k_ntt_cl<true><<<dim3(kNttCl, nr), 512, kNttClWords * 8, s>>>(dst, map, t.itw, t.itwp, t.itwx, t.itws, r0,
+                                                                         src, src_stride, per_item);
+            continue;
+        }
         k_ntt256_rows<true><<<grid, 256, 0, s>>>(dst, map, t.itw, t.itwp, t.itwx, t.itws, r0, src, src_stride,
                                                  per_item);
         k_ntt256_cols<true><<<grid, 256, 0, s>>>(dst, map, t.itw, t.itwp, t.itwx, r0);
