@@ -108,6 +108,9 @@ SIGNATURES = {
     "helrm_DeleteTable": [c_int],
     "helrm_GetTableShape": [c_int, P(c_int), P(c_int), P(c_int)],
     "helrm_MulTableMatMulNew": [P(c_int), c_int, c_int, P(c_int)],
+    "helrm_ModRaiseNew": [c_int, P(c_int)],
+    "helrm_GenerateLinearTransformEx": [P(c_int), c_int, P(c_double), c_int, c_int, c_double, c_int, c_double,
+                                        P(c_int)],
     "helrm_EncodeBatch": [P(c_double), c_int, c_int, c_int, c_double, P(c_int)],
     "helrm_MulImaginaryUnitNew": [c_int, P(c_int)],
     "helrm_MulImaginaryUnit": [c_int],

@@ -1,0 +1,215 @@
+"""CKKS bootstrapping for sparse slot counts on the B200 backend.
+
+The reference exposes ``NewBootstrapper(logPs, slots)`` / ``Bootstrap(ct,
+slots)`` (orion/backend/cheddar/bindings.py:1326-1342, reaching Cheddar's
+BootContext, cheddar_pybind.cu:2049-2187, which is not in the checkout).
+Orion places the calls (orion/core/auto_bootstrap.py:227-331) and hands the
+backend ciphertexts whose slot values it has already scaled into [-1, 1]
+(orion/nn/operations.py:38-115).  This module is the circuit, built on the
+library's native operators, after the published method (Cheon, Han, Kim,
+Kim, Song, "Bootstrapping for approximate homomorphic encryption",
+EUROCRYPT 2018; sparse packing and the cosine / double-angle EvalMod of
+Chen, Chillotti, Song, EUROCRYPT 2019):
+
+  ModRaise   the level-0 ciphertext, lifted to every prime, decrypts to
+             t = m + q0 I (I small: the overflow of c0 + c1 s over q0);
+  SubSum     log2(N / 2n) rotations by n 2^i add the conjugates of the
+             sparse subring: R t_sub with R = N / 2n, so read at scale
+             R q0 the n slots hold E(t_sub) / q0;
+  CtS        one dense n x n transform M^-1 / 2B, M the subring's encoding
+             matrix (slot j = sum_k w_k zeta^(k g_j), w_k = t_k + i t_{k+n},
+             g_j = 5^j mod 4n): slots (t_k + i t_{k+n}) / (2 B q0);
+  EvalMod    for the real and the imaginary part (one conjugation, the
+             imaginary unit): u = (x - 1/4) / B in [-1, 1], a Chebyshev
+             approximation of cos(2 pi B u / 2^r), r double angles
+             c <- 2 c^2 - 1 giving sin(2 pi x), then arcsin(s) / 1 on the
+             odd Taylor terms (s + s^3/6 + 3 s^5/40) so that the result is
+             2 pi (m / q0) up to (2 pi m / q0)^7 terms;
+  StC        one dense transform M / 2 pi back to the coefficient packing,
+             landing at the top level of the usable chain at the default
+             scale.
+
+Levels: CtS 1, cosine 6 (degree 63), double angles 3, arcsine 3, StC 1 --
+BOOT_LEVELS primes are reserved above the usable chain, the top one of
+60 bits (the CtS plaintexts need the precision), the others of
+min(logscale + 15, 60) bits as the reference's Cheddar setup does
+(bindings.py:279-294).  The input must satisfy q0 >= 2^4 scale (the
+message ratio) and slots n <= 4096 (the dense transforms hold n diagonals).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+COS_DEGREE = 63      # depth 6
+DOUBLE_ANGLES = 3
+ASIN_COEFFS = [0.0, 1.0, 0.0, 1.0 / 6.0, 0.0, 3.0 / 40.0]  # arcsin Taylor to s^5 (depth 3)
+BOOT_LEVELS = 1 + 6 + DOUBLE_ANGLES + 3 + 1
+MAX_SLOTS = 4096
+
+
+def boot_prime_bits(logscale: int) -> list[int]:
+    """Bit sizes of the reserved primes, lowest first (the top one is the
+    CtS level)."""
+    return [min(int(logscale) + 15, 60)] * (BOOT_LEVELS - 1) + [60]
+
+
+def encoding_matrix(n: int) -> np.ndarray:
+    """M[j, k] = zeta^(k g_j), zeta = exp(i pi / 2n), g_j = 5^j mod 4n: the
+    slots of a subring polynomial from its packed coefficients
+    w_k = t_k + i t_{k+n}."""
+    g = np.ones(n, dtype=np.int64)
+    for j in range(1, n):
+        g[j] = g[j - 1] * 5 % (4 * n)
+    k = np.arange(n)
+    return np.exp(1j * np.pi * np.outer(g, k) / (2 * n))
+
+
+def diagonals(A: np.ndarray, slots: int) -> np.ndarray:
+    """Orion's diagonal convention out[i] = sum_l d_l[i] in[(i + l) mod n]
+    for an n x n matrix acting on n-periodic slots, each diagonal repeated
+    over all slots: [n][slots] complex."""
+    n = A.shape[0]
+    i = np.arange(n)
+    d = np.stack([A[i, (i + l) % n] for l in range(n)])
+    return np.tile(d, (1, slots // n))
+
+
+def cos_coeffs(B: float, r: int, degree: int) -> list[float]:
+    """Chebyshev coefficients of cos(2 pi B u / 2^r) on [-1, 1]."""
+    from numpy.polynomial import chebyshev as C
+    x = np.cos(np.pi * (np.arange(4 * degree) + 0.5) / (4 * degree))
+    return C.chebfit(x, np.cos(2.0 * math.pi * B / 2 ** r * x), degree).tolist()
+
+
+def overflow_bound(h: int) -> int:
+    """|I| bound of ModRaise's overflow: a sum of h terms uniform in
+    [-1/2, 1/2] (variance h/12), taken at 7 standard deviations."""
+    return int(math.ceil(7.0 * math.sqrt(max(h, 1) / 12.0)))
+
+
+class BootContext:
+    """The transforms, the polynomials and the scales for one slot count."""
+
+    def __init__(self, lib, slots: int):
+        S = lib._slots
+        n = int(slots)
+        if n < 1 or n & (n - 1) or n > S:
+            raise ValueError(f"Bootstrap: slots must be a power of two up to {S}")
+        if n > MAX_SLOTS:
+            raise ValueError(f"Bootstrap: at most {MAX_SLOTS} slots (dense transforms)")
+        self.n, self.R = n, S // n
+        q = lib.GetAllModuliChain()
+        self.q = [float(x) for x in q]
+        self.q0 = self.q[0]
+        self.top = len(q) - 1
+        self.usable_top = lib._max_level
+        if self.top - BOOT_LEVELS != self.usable_top:
+            raise RuntimeError("Bootstrap: the scheme was created without the reserved bootstrapping primes")
+        self.B = overflow_bound(lib._h) + 1
+        M = encoding_matrix(n)
+        Minv = np.linalg.inv(M)
+        # CtS at the top level: the SubSum output read at scale R q0, the
+        # plaintext scale chosen so that the output scale is q[top - 1]
+        self.s_u = self.q[self.top - 1]
+        s_cts = self.s_u * self.q[self.top] / (self.R * self.q0)
+        self.cts = self._transform(lib, Minv / (2 * self.B), self.top, s_cts)
+        self.poly_cos = lib.GenerateChebyshev(cos_coeffs(self.B, DOUBLE_ANGLES, COS_DEGREE))
+        self.poly_asin = lib.GenerateMonomial(list(ASIN_COEFFS))  # ascending, as the backend takes them
+        # scales through EvalMod (deterministic: targets at the primes)
+        lvl = self.top - 1 - 6
+        self.s_cos = self.q[lvl]
+        s = self.s_cos
+        for _ in range(DOUBLE_ANGLES):
+            s = s * s / self.q[lvl]
+            lvl -= 1
+        self.s_dbl = s
+        self.lvl_asin_in = lvl
+        self.s_asin = self.q[lvl - 3]
+        self.lvl_stc = lvl - 3
+        assert self.lvl_stc == self.usable_top + 1
+        # StC: slots 2 pi (m / q0) packed -> E(m) / q0, pt scale chosen so
+        # that an input at the default scale comes out at the default scale
+        d = float(lib._default_scale)
+        self.s_stc = d * self.q0 * self.q[self.lvl_stc] / (d * self.s_asin)
+        self.stc = self._transform(lib, M / (2 * math.pi), self.lvl_stc, self.s_stc)
+        # keys: the SubSum rotations, both transforms', the conjugation
+        self.subsum_steps = []
+        step = n
+        while step < S:
+            self.subsum_steps.append(step)
+            step *= 2
+        for k in self.subsum_steps:
+            lib.AddRotationKey(k)
+        for lt in (self.cts, self.stc):
+            for k in lib.GetLinearTransformRotationKeys(lt):
+                lib.GenerateLinearTransformRotationKey(k)
+
+    @staticmethod
+    def _transform(lib, A, level, scale):
+        S = lib._slots
+        d = diagonals(A, S)
+        inter = np.stack([d.real, d.imag], axis=-1).reshape(A.shape[0], 2 * S)
+        return lib.GenerateLinearTransformEx(list(range(A.shape[0])), inter, S, level, 2.0, True, scale)
+
+
+def bootstrap(lib, ctx: BootContext, ct: int) -> int:
+    """The circuit on one ciphertext; returns a new ciphertext at the top
+    of the usable chain holding the same slot values."""
+    scale_in = lib.GetCiphertextScale(ct)
+    if ctx.q0 < 16.0 * scale_in:
+        raise RuntimeError("Bootstrap: the message ratio q0 / scale must be at least 2^4 "
+                           f"(q0 = 2^{math.log2(ctx.q0):.1f}, scale = 2^{math.log2(scale_in):.1f})")
+    owned = []
+
+    def new(x):
+        owned.append(x)
+        return x
+
+    x = lib.AlignToLevelNew(ct, 0) if lib.GetCiphertextLevel(ct) > 0 else ct
+    if x != ct:
+        owned.append(x)
+    t = new(lib.ModRaiseNew(x))
+    for k in ctx.subsum_steps:
+        r = lib.RotateNew(t, k)
+        lib.AddCiphertext(t, r)
+        lib.DeleteCiphertext(r)
+    lib.SetCiphertextScale(t, ctx.R * ctx.q0)
+    w = new(lib.RescaleNew(new(lib.EvaluateLinearTransform(ctx.cts, t))))
+    # u_re = w + conj(w) - 1/4B, u_im = i (conj(w) - w) - 1/4B
+    cj = new(lib.ConjugateNew(w))
+    u_re = lib.AddCiphertextNew(w, cj)
+    u_im = lib.SubCiphertextNew(cj, w)
+    lib.MulImaginaryUnit(u_im)
+    for u in (u_re, u_im):
+        lib.SetCiphertextScale(u, ctx.s_u)
+        lib.AddScalar(u, -1.0 / (4.0 * ctx.B))
+    ys = lib.EvaluatePolynomialBatch([u_re, u_im], ctx.poly_cos, ctx.s_cos)
+    lib.DeleteCiphertext(u_re)
+    lib.DeleteCiphertext(u_im)
+    out = []
+    for y in ys:
+        for _ in range(DOUBLE_ANGLES):
+            sq = lib.MulRelinCiphertextNew(y, y)
+            lib.DeleteCiphertext(y)
+            lib.Rescale(sq)
+            lib.AddCiphertext(sq, sq)
+            lib.AddScalar(sq, -1.0)
+            y = sq
+        out.append(y)
+    zs = lib.EvaluatePolynomialBatch(out, ctx.poly_asin, ctx.s_asin)
+    for y in out:
+        lib.DeleteCiphertext(y)
+    lib.MulImaginaryUnit(zs[1])
+    lib.AddCiphertext(zs[0], zs[1])
+    lib.DeleteCiphertext(zs[1])
+    res = lib.EvaluateLinearTransform(ctx.stc, zs[0])
+    lib.DeleteCiphertext(zs[0])
+    lib.Rescale(res)
+    # the values: E(m) / q0 at scale s_asin s_stc / q_stc, i.e. the input's
+    # slots at s_asin s_stc scale_in / (q_stc q0)
+    lib.SetCiphertextScale(res, ctx.s_asin * ctx.s_stc * scale_in / (ctx.q[ctx.lvl_stc] * ctx.q0))
+    for o in owned:
+        lib.DeleteCiphertext(o)
+    return res

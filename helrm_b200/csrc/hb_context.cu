@@ -97,6 +97,7 @@ struct LevelTabs {
 
 struct LinTrans {
     int level = 0;
+    double scale = 0.0;                           // plaintext scale of the diagonals
     int bs = 1;
     bool use_bsgs = false;
     std::vector<int> ks;
@@ -1266,6 +1267,27 @@ public:
                         (size_t)npoly * l * N, out_stride, stream);
     }
 
+    // ---------------------------------------------------------- bootstrapping: ModRaise
+    // a level-0 ciphertext (one limb, NTT) -> every main prime: each
+    // coefficient of c0, c1 is lifted centred from q_0 and reduced modulo
+    // q_i, so the result decrypts to m + q_0 I with I small (the integer
+    // overflow of c0 + c1 s over q_0)
+    int mod_raise(int id) {
+        const Ct &x = ct(id);
+        if (x.npoly != 2) HB_THROW(HB_ESTATE, "ModRaise: relinearize first");
+        if (x.nq != 1) HB_THROW(HB_ESTATE, "ModRaise: the input must be at level 0");
+        Ct o = new_ct(L, 2, x.scale);
+        o.slots = x.slots;
+        u64 *co = alloc((size_t)2 * N);
+        d2d(co, x.d, (size_t)2 * N);
+        RowMap r0 = rowmap(1, 1, L);
+        ntt_inverse(co, 2, r0, ntt, stream);
+        mod_raise_rows(o.d, co, L, logN, stream);
+        ntt_forward(o.d, 2 * L, qmap(L), ntt, stream);
+        release(co);
+        return put_ct(o);
+    }
+
     // ---------------------------------------------------------- level / scale alignment
     Ct drop_to(const Ct &c, int nq) {
         Ct o = new_ct(nq, c.npoly, c.scale);
@@ -1566,12 +1588,15 @@ public:
     }
 
     // ---------------------------------------------------------- linear transforms
-    int generate_lt(const int *idxs, int n, const double *data, int width, int level, double ratio) {
+    int generate_lt(const int *idxs, int n, const double *data, int width, int level, double ratio,
+                    bool cplx = false, double pscale = 0.0) {
+        if (!(pscale > 0)) pscale = default_scale;
         if (n <= 0) HB_THROW(HB_EINVAL, "GenerateLinearTransform: no diagonals");
         if (width <= 0 || width > slots) HB_THROW(HB_EINVAL, "GenerateLinearTransform: bad diagonal width");
         if (level < 0 || level >= L) HB_THROW(HB_EINVAL, "GenerateLinearTransform: level out of range");
         auto t = std::make_unique<LinTrans>();
         t->level = level;
+        t->scale = pscale;
         t->use_bsgs = ratio > 0 && n > 1;
         int bs;
         const char *env = std::getenv("HELRM_B200_BS");
@@ -1595,21 +1620,22 @@ public:
         std::vector<u64 *> dsts;
         for (int i0 = 0; i0 < n; i0 += HB_PTR_BATCH) {
             const int cnt = std::min(HB_PTR_BATCH, n - i0);
-            rolled.assign((size_t)cnt * width, 0.0);
+            const int per = cplx ? 2 : 1;
+            rolled.assign((size_t)cnt * width * per, 0.0);
             dsts.clear();
             for (int j = 0; j < cnt; j++) {
                 const int i = i0 + j, k = idxs[i], g = t->use_bsgs ? k / bs : 0, shift = g * bs;
-                const double *vals = data + (size_t)i * width;
-                double *dst = &rolled[(size_t)j * width];
+                const double *vals = data + (size_t)i * width * per;
+                double *dst = &rolled[(size_t)j * width * per];
                 for (int s = 0; s < width; s++) {
                     // numpy roll to the right by shift over the diagonal's own width
                     const int src = ((s - shift) % width + width) % width;
-                    dst[s] = vals[src];
+                    for (int e = 0; e < per; e++) dst[per * s + e] = vals[per * src + e];
                 }
                 Pt p;
                 p.nq = level + 1;
                 p.ext = true;
-                p.scale = default_scale;
+                p.scale = pscale;
                 p.slots = slots;
                 p.d = alloc((size_t)(p.nq + K) * N);
                 t->pts[k] = p;
@@ -1617,7 +1643,7 @@ public:
                 const int b = t->use_bsgs ? k % bs : k;
                 t->groups[g].push_back({b, k});
             }
-            encode_device(rolled.data(), width, false, cnt, level + 1, true, default_scale, dsts.data());
+            encode_device(rolled.data(), width, cplx, cnt, level + 1, true, pscale, dsts.data());
         }
         int id = next_id++;
         lts[id] = std::move(t);
@@ -1848,7 +1874,7 @@ public:
                 std::vector<u64 *> dst(nb);
                 for (int b = 0; b < nb; b++) {
                     const Ct &c = ct(ids[idx[c0 + b]]);
-                    Ct o = new_ct(nq, 2, c.scale * default_scale);
+                    Ct o = new_ct(nq, 2, c.scale * t.scale);
                     o.slots = c.slots;
                     dst[b] = o.d;
                     outs[idx[c0 + b]] = put_ct(o);
@@ -2580,6 +2606,14 @@ HB_API int helrm_EncodeBatch(const double *values, int count, int n, int level, 
     });
 }
 
+HB_API int helrm_ModRaiseNew(int ct, int *out) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out);
+        *out = c.mod_raise(ct);
+    });
+}
+
 HB_API int helrm_ConjugateNew(int ct, int *out) {
     return guard([&] {
         Context &c = C();
@@ -2630,6 +2664,17 @@ HB_API int helrm_GenerateLinearTransform(const int *diag_idxs, int n, const doub
         OUT(out_lt);
         if (!diag_idxs || !data) HB_THROW(HB_EINVAL, "GenerateLinearTransform: null input");
         *out_lt = c.generate_lt(diag_idxs, n, data, width, level, bsgs_ratio);
+    });
+}
+// complex diagonals (interleaved re, im when cplx != 0) encoded at an
+// explicit plaintext scale (<= 0: the default scale)
+HB_API int helrm_GenerateLinearTransformEx(const int *diag_idxs, int n, const double *data, int width, int level,
+                                           double bsgs_ratio, int cplx, double scale, int *out_lt) {
+    return guard([&] {
+        Context &c = C();
+        OUT(out_lt);
+        if (!diag_idxs || !data) HB_THROW(HB_EINVAL, "GenerateLinearTransform: null input");
+        *out_lt = c.generate_lt(diag_idxs, n, data, width, level, bsgs_ratio, cplx != 0, scale);
     });
 }
 HB_API int helrm_EvaluateLinearTransformBatch(int lt, const int *cts, int n, int *outs) {

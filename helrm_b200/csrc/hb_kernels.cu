@@ -2789,6 +2789,33 @@ void lane_split(const PtrBatchW &ev, const PtrBatchW &od, const u64 *pk, const u
     check_launch("lane_split");
 }
 
+// bootstrapping's ModRaise: out[pl][i][n] = centred(co[pl][n] mod q_0) mod q_i
+__global__ void k_mod_raise(u64 *out, const u64 *co, int nq, int logN) {
+    const size_t per = (size_t)nq << logN, n = 2 * per;
+    const u64 q0 = c_pc[0].q;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
+        const int pl = (int)(idx / per);
+        const size_t rem = idx - (size_t)pl * per;
+        const int i = (int)(rem >> logN);
+        const u64 v = co[((size_t)pl << logN) + (rem & ((1u << logN) - 1))];
+        const PrimeConst &pc = c_pc[i];
+        if (v <= q0 / 2) {
+            out[idx] = mul_shoup(v, 1ull, pc.onep, pc.q);
+        } else {
+            const u64 m = mul_shoup(q0 - v, 1ull, pc.onep, pc.q);
+            out[idx] = m ? pc.q - m : 0;
+        }
+    }
+}
+void mod_raise_rows(u64 *out, const u64 *co, int nq, int logN, cudaStream_t s) {
+    const size_t n = ((size_t)2 * nq) << logN;
+    unsigned g = grid1d(n, 256);
+    if (g > 148u * 64u) g = 148u * 64u;
+    ProfScope ps(KC_ELEMENTWISE, 8.0 * n + 16.0 * (1 << logN), (double)n, s, 1);
+    k_mod_raise<<<g, 256, 0, s>>>(out, co, nq, logN);
+    check_launch("mod_raise");
+}
+
 void copy_rows(u64 *dst, const u64 *src, size_t nwords, cudaStream_t s) {
     cudaError_t e = cudaMemcpyAsync(dst, src, nwords * sizeof(u64), cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) throw std::runtime_error(std::string("copy: ") + cudaGetErrorString(e));

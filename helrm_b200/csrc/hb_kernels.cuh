@@ -309,6 +309,9 @@ void enc_ifft(double2 *z, int count, const EncTables &t, cudaStream_t s);
 // (coefficient order; |scale * value| below 2^62)
 void enc_round(const PtrBatchW &dst, const double2 *z, int rows, RowMap map, double scale, int count,
                const EncTables &t, cudaStream_t s);
+// bootstrapping's ModRaise: the coefficient-form rows co[2][N] (modulo q_0),
+// lifted centred, as residues of the first nq main primes into out[2][nq][N]
+void mod_raise_rows(u64 *out, const u64 *co, int nq, int logN, cudaStream_t s);
 // out = i * in slot-wise (multiplication by X^(N/2)): nrows rows, prime of
 // row r is r % nq, iu = [P][4] {w, w', q - w, (q - w)'} (w = psi^(N/2))
 void ew_mul_iunit(u64 *out, const u64 *in, int nrows, int nq, const u64 *iu, int logN, cudaStream_t s);

@@ -91,6 +91,8 @@ class B200Library:
         self._slots = None
         self._max_level = None
         self._default_scale = None
+        self._h = 0
+        self._boot = {}        # slots -> bootstrap.BootContext
 
     # ------------------------------------------------------------ setup
     def setup_bindings(self, orion_params) -> None:
@@ -119,12 +121,22 @@ class B200Library:
         dnum = self._dnum if self._dnum is not None else int(os.environ.get("HELRM_B200_DNUM", "0"))
         seed = self._seed if self._seed is not None else int(os.environ.get("HELRM_B200_SEED", "0"))
         device = self._device if self._device is not None else int(os.environ.get("HELRM_B200_DEVICE", "0"))
-        qa, qp = _int_array(logq)
+        # bootstrapping reserves primes above the usable chain, as the
+        # reference's Cheddar setup does when Orion's boot parameters are set
+        # (orion/backend/cheddar/bindings.py:262-294); GetModuliChain keeps
+        # returning the usable primes only
+        boot = getattr(orion_params, "get_boot_num_cts_levels", lambda: None)() is not None or \
+            bool(getattr(orion_params, "boot", False))
+        from . import bootstrap as _bt
+        logq_all = logq + (_bt.boot_prime_bits(logscale) if boot else [])
+        qa, qp = _int_array(logq_all)
         pa, pp = _int_array(logp)
-        call("helrm_NewScheme", logn, qp, len(logq), pp, len(logp), logscale, h, dnum, seed, device)
+        call("helrm_NewScheme", logn, qp, len(logq_all), pp, len(logp), logscale, h, dnum, seed, device)
         self._slots = 1 << (logn - 1)
         self._max_level = len(logq) - 1
         self._default_scale = 1 << logscale
+        self._h = h
+        self._boot = {}
 
     def DeleteScheme(self) -> None:
         call("helrm_DeleteScheme")
@@ -392,6 +404,13 @@ class B200Library:
         call("helrm_Conjugate", int(ct_id))
         return int(ct_id)
 
+    def ModRaiseNew(self, ct_id):
+        """A level-0 ciphertext lifted (centred) to every main prime: it
+        decrypts to m + q_0 I (bootstrapping's first step)."""
+        out = _out_int()
+        call("helrm_ModRaiseNew", int(ct_id), ctypes.byref(out))
+        return out.value
+
     def MulImaginaryUnitNew(self, ct_id):
         """Slot-wise multiply by sqrt(-1): key-free, no level consumed."""
         out = _out_int()
@@ -432,6 +451,20 @@ class B200Library:
         out = _out_int()
         call("helrm_GenerateLinearTransform", ip, n, data.ctypes.data_as(P(c_double)), width, int(level), ratio,
              ctypes.byref(out))
+        return out.value
+
+    def GenerateLinearTransformEx(self, diag_idxs, diags_data, width: int, level: int, bsgs_ratio,
+                                  cplx: bool, scale: float) -> int:
+        """A transform with complex diagonals (interleaved re, im pairs,
+        `width` pairs each when cplx) at an explicit plaintext scale."""
+        ia, ip = _int_array(diag_idxs)
+        data = np.ascontiguousarray(np.asarray(diags_data, dtype=np.float64).ravel())
+        per = 2 if cplx else 1
+        if data.size != len(ia) * int(width) * per:
+            raise ValueError("GenerateLinearTransformEx: data size does not match the diagonals")
+        out = _out_int()
+        call("helrm_GenerateLinearTransformEx", ip, len(ia), data.ctypes.data_as(P(c_double)), int(width), int(level),
+             float(bsgs_ratio), 1 if cplx else 0, float(scale), ctypes.byref(out))
         return out.value
 
     def GetLinearTransformRotationKeys(self, lt_id) -> list[int]:
@@ -662,13 +695,31 @@ class B200Library:
 
     # ------------------------------------------------------------ bootstrap (out of this backend's scope)
     def NewBootstrapper(self, logPs, slots: int) -> None:
-        self._not_implemented("NewBootstrapper")
+        """Prepare the bootstrapping circuit for `slots` (its transforms,
+        polynomials and keys; helrm_b200/bootstrap.py).  logPs is accepted
+        for the interface, as the reference's Cheddar backend does
+        (bindings.py:1326-1339).  Idempotent per slot count."""
+        from . import bootstrap as _bt
+        n = int(slots)
+        if n not in self._boot:
+            self._boot[n] = _bt.BootContext(self, n)
 
-    def Bootstrap(self, ct_id, slots):
-        self._not_implemented("Bootstrap")
+    def Bootstrap(self, ct_id, slots) -> int:
+        """A fresh ciphertext at the top of the usable chain holding the
+        slot values of ct_id (|values| <= 1 as Orion's Bootstrap layer
+        scales them, orion/nn/operations.py:38-115)."""
+        from . import bootstrap as _bt
+        n = int(slots)
+        if n not in self._boot:
+            self.NewBootstrapper(None, n)
+        return _bt.bootstrap(self, self._boot[n], int(ct_id))
 
     def DeleteBootstrappers(self):
-        """No-op."""
+        """Release the bootstrapping transforms (keys stay cached)."""
+        for ctx in self._boot.values():
+            self.DeleteLinearTransform(ctx.cts)
+            self.DeleteLinearTransform(ctx.stc)
+        self._boot = {}
 
     # ------------------------------------------------------------ metadata
     def _get(self, name, obj_id, ctype=c_int):
@@ -677,6 +728,12 @@ class B200Library:
         return v.value
 
     def GetModuliChain(self) -> list[int]:
+        """The usable primes q_0..q_max_level (the bootstrapping primes
+        reserved above them are left out, as the reference does)."""
+        return self.GetAllModuliChain()[:self._max_level + 1]
+
+    def GetAllModuliChain(self) -> list[int]:
+        """Every main prime, the reserved bootstrapping primes included."""
         n = _out_int()
         buf = np.zeros(64, dtype=np.uint64)
         call("helrm_GetModuliChain", buf.ctypes.data_as(P(c_u64)), 64, ctypes.byref(n))

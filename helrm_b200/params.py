@@ -14,6 +14,7 @@ class CKKSConfig:
     logscale: int = 40
     h: int = 192
     ringtype: str = "standard"
+    boot: bool = False   # reserve the bootstrapping primes above the chain
 
     @classmethod
     def from_dict(cls, cfg: dict) -> "CKKSConfig":

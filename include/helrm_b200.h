@@ -197,6 +197,19 @@ int helrm_MulImaginaryUnit(int ct);
  * first num_real of them (0 <= num_real <= 2n) written to outs */
 int helrm_UnpackLanes(const int *packed, int n, int num_real, int *outs);
 
+/* ---- bootstrapping pieces (NewBootstrapper / Bootstrap, cheddar bindings.py:
+ * 1326-1342 -> cheddar_pybind.cu:2049-2187; the circuit runs in the Python
+ * layer over these and the operators above) ----------------------------------
+ * ModRaise: a level-0 ciphertext lifted (centred) to every main prime; it
+ * decrypts to m + q_0 I with I the small overflow polynomial. */
+int helrm_ModRaiseNew(int ct, int *out);
+/* GenerateLinearTransform with complex diagonals (cplx != 0: interleaved re,
+ * im pairs, width pairs per diagonal) encoded at plaintext scale `scale`
+ * (<= 0: the default scale); the transform's output scale is the input's
+ * times `scale` */
+int helrm_GenerateLinearTransformEx(const int *diag_idxs, int n, const double *data, int width, int level,
+                                    double bsgs_ratio, int cplx, double scale, int *out_lt);
+
 /* ---- polynomial evaluation (poly_evaluator.py:25-35; cheddar bindings.py:
  * 1102-1116 -> EvaluatePolynomialNative, cheddar_pybind.cu:2207-2262) --------
  * coeffs[0..n) ascending, n >= 3 (degree >= 2; the Python layer keeps Horner

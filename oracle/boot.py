@@ -1,0 +1,110 @@
+"""CPU restatement of the bootstrapping circuit of helrm_b200/bootstrap.py.
+
+TEST INFRASTRUCTURE ONLY: the checker for the GPU path's Bootstrap; the
+product package never imports it.
+
+The reference's bootstrapping is Cheddar's BootContext (reached through
+orion/backend/cheddar/bindings.py:1326-1342, cheddar_pybind.cu:2049-2187),
+third-party code absent from the checkout.  This file restates, on the
+oracle's exact operators, the published circuit the B200 library runs
+(ModRaise, SubSum, a dense CoeffsToSlots, the cosine / double-angle /
+arcsine EvalMod, a dense SlotsToCoeffs; see the library module for the
+derivation), in the same order with the same constants, so that given the
+same keys and transform plaintexts the GPU output must match residue for
+residue.  `bootstrap` takes the library's plaintexts and keys as inputs;
+`prepare` builds them on the CPU for a standalone run.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import poly
+
+
+def _qs(o, nq):
+    return np.array(o.primes[:nq], dtype=object)[None, :, None]
+
+
+def add(o, a, b):
+    nq = min(a.shape[1], b.shape[1])
+    return ((a[:, :nq].astype(object) + b[:, :nq].astype(object)) % _qs(o, nq)).astype(np.uint64)
+
+
+def sub(o, a, b):
+    nq = min(a.shape[1], b.shape[1])
+    return ((a[:, :nq].astype(object) - b[:, :nq].astype(object)) % _qs(o, nq)).astype(np.uint64)
+
+
+def add_scalar(o, ct, v, scale):
+    """c0 + round(v * scale) with the library's rounding: the product in
+    80-bit long double, then half away from zero"""
+    x = np.longdouble(v) * np.longdouble(scale)
+    r = np.floor(x + np.longdouble(0.5)) if x >= 0 else -np.floor(-x + np.longdouble(0.5))
+    num, den = r.as_integer_ratio()
+    k = num // den
+    out = ct.astype(object).copy()
+    for i in range(ct.shape[1]):
+        out[0, i] = (out[0, i] + k) % o.primes[i]
+    return out.astype(np.uint64)
+
+
+def iunit_rows(o, nq):
+    rows = []
+    for i in range(nq):
+        m = np.zeros(o.N, dtype=np.uint64)
+        m[o.N // 2] = 1
+        rows.append(o.ntt(i, m))
+    return np.array(rows, dtype=object)
+
+
+def mul_i(o, ct):
+    nq = ct.shape[1]
+    return ((ct.astype(object) * iunit_rows(o, nq)[None]) % _qs(o, nq)).astype(np.uint64)
+
+
+def mod_raise(o, ct, nq_all):
+    q0 = o.primes[0]
+    out = np.zeros((2, nq_all, o.N), dtype=np.uint64)
+    for pl in range(2):
+        coef = o.intt(0, ct[pl, 0]).astype(object)
+        cen = [int(v) - q0 if int(v) > q0 // 2 else int(v) for v in coef]
+        for i in range(nq_all):
+            out[pl, i] = o.ntt(i, np.array([v % o.primes[i] for v in cen], dtype=np.uint64))
+    return out
+
+
+def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts):
+    """ctx: the scales and constants of helrm_b200.bootstrap.BootContext
+    (dict with n, R, B, q0, s_u, s_cos, s_asin, subsum_steps, cts_bs, stc_bs,
+    cos_coeffs, asin_coeffs, top); keys: {galois: switching key};
+    cts_pts / stc_pts: the transforms' extended-basis plaintexts, diagonal k
+    at index k.  Returns (ciphertext, output scale)."""
+    n, S = ctx["n"], o.N // 2
+    nq_all = ctx["top"] + 1
+    x = ct[:, :1]
+    t = mod_raise(o, x, nq_all)
+    for k in ctx["subsum_steps"]:
+        g = o.galois(k)
+        t = add(o, t, o.rotate(t, keys[g], g))
+    ks = list(range(n))
+    w = o.rescale(o.bsgs_lt(t, ks, cts_pts, ctx["cts_bs"], keys))
+    gc = 2 * o.N - 1
+    cj = o.rotate(w, keys[gc], gc)
+    u_re = add_scalar(o, add(o, w, cj), -1.0 / (4.0 * ctx["B"]), ctx["s_u"])
+    u_im = add_scalar(o, mul_i(o, sub(o, cj, w)), -1.0 / (4.0 * ctx["B"]), ctx["s_u"])
+    ys = []
+    for u in (u_re, u_im):
+        y, _ = poly.evaluate(o, rlk, u, ctx["s_u"], ctx["cos_coeffs"], ctx["s_cos"], chebyshev=True)
+        s = ctx["s_cos"]
+        for _ in range(ctx["double_angles"]):
+            sq = o.rescale(o.relinearize(o.tensor(y, y), rlk))
+            s = s * s / float(o.primes[y.shape[1] - 1])
+            y = add_scalar(o, add(o, sq, sq), -1.0, s)
+        z, _ = poly.evaluate(o, rlk, y, s, ctx["asin_coeffs"], ctx["s_asin"], chebyshev=False)
+        ys.append(z)
+    y = add(o, ys[0], mul_i(o, ys[1]))
+    out = o.rescale(o.bsgs_lt(y, ks, stc_pts, ctx["stc_bs"], keys))
+    q_stc = float(o.primes[y.shape[1] - 1])
+    return out, ctx["s_asin"] * ctx["s_stc"] * scale_in / (q_stc * ctx["q0"])

@@ -20,7 +20,7 @@ class Pair:
         self.lib.GenerateSecretKey()
         self.lib.GenerateRelinearizationKey()
         self.info = self.lib.scheme_info()
-        self.o = oracle_mod.Oracle(cfg.logn, self.lib.GetModuliChain(), self.lib.GetAuxModuliChain(), dnum)
+        self.o = oracle_mod.Oracle(cfg.logn, self.lib.GetAllModuliChain(), self.lib.GetAuxModuliChain(), dnum)
         assert self.o.alpha == self.info["alpha"] and self.o.dnum == self.info["dnum"]
         self.om = oracle_mod
         self.enc_count = 0
