@@ -30,9 +30,8 @@ Chen, Chillotti, Song, EUROCRYPT 2019):
              scale.
 
 Levels: CtS 1, cosine 6 (degree 63), double angles 3, arcsine 3, StC 1 --
-BOOT_LEVELS primes are reserved above the usable chain, the top one of
-60 bits (the CtS plaintexts need the precision), the others of
-min(logscale + 15, 60) bits as the reference's Cheddar setup does
+BOOT_LEVELS primes of 60 bits are reserved above the usable chain, as the
+reference's Cheddar setup reserves its boot primes there
 (bindings.py:279-294).  The input must satisfy q0 >= 2^4 scale (the
 message ratio) and slots n <= 4096 (the dense transforms hold n diagonals).
 """
@@ -51,8 +50,12 @@ MAX_SLOTS = 4096
 
 def boot_prime_bits(logscale: int) -> list[int]:
     """Bit sizes of the reserved primes, lowest first (the top one is the
-    CtS level)."""
-    return [min(int(logscale) + 15, 60)] * (BOOT_LEVELS - 1) + [60]
+    CtS level).  All of 60 bits: EvalMod's scales sit at these primes, and
+    its rescale noise (about sqrt(N h) per product) is amplified by the
+    degree-63 Chebyshev basis (up to 63^2) and the double angles (4^3); at
+    LogN 16 and h = 192, 51-bit primes (logscale + 15, the reference's
+    Cheddar sizing) left 2e-4 in the slots, 60-bit primes 2^9 less."""
+    return [60] * BOOT_LEVELS
 
 
 def encoding_matrix(n: int) -> np.ndarray:

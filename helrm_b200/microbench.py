@@ -363,6 +363,57 @@ def run_upload(count=64, level=4, reps=3, device=0) -> dict:
         lib.DeleteScheme()
 
 
+def run_boot(slot_counts=(512,), reps=3, device=0) -> list[dict]:
+    """Bootstrapping at LogN 16: the cfg2 chain with a 50-bit q0 (message
+    ratio 2^14) under 24 usable levels, the 14 reserved 60-bit primes above it,
+    six 60-bit special primes (dnum 7); sparse slot counts as Orion's
+    bootstrap layers use for the MLP widths.  CUDA events on the library
+    stream around Bootstrap calls on a level-0 ciphertext; the precision
+    is the largest slot error after decryption."""
+    from helrm_b200 import B200Library, CKKSConfig, _capi
+
+    cfg = CKKSConfig(logn=16, logq=[50] + [36] * 23, logp=[60] * 6, logscale=36, h=192, boot=True)
+    lib = B200Library(seed=31, device=device)
+    lib.setup_bindings(cfg)
+    out = []
+    try:
+        lib.GenerateSecretKey()
+        lib.GenerateRelinearizationKey()
+        S = lib.scheme_info()["slots"]
+        capi = _capi.load()
+        rng = np.random.default_rng(2)
+        for n in slot_counts:
+            import time
+            t0 = time.time()
+            lib.NewBootstrapper(None, n)
+            lib.Synchronize()
+            setup_s = time.time() - t0
+            z = rng.uniform(-1, 1, n)
+            pt = lib.Encode(list(np.tile(z, S // n)), 0, float(1 << 36))
+            ct = lib.Encrypt(pt)
+            lib.DeletePlaintext(pt)
+            lib.DeleteCiphertext(lib.Bootstrap(ct, n))  # warm-up (plans, pools)
+            lib.Synchronize()
+            _capi.check(capi.helrm_TimerStart())
+            res = None
+            for _ in range(reps):
+                if res is not None:
+                    lib.DeleteCiphertext(res)
+                res = lib.Bootstrap(ct, n)
+            ms = ctypes.c_double(0)
+            _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+            got = np.array(lib.Decode(lib.Decrypt(res)))
+            err = float(np.abs(got - np.tile(z, S // n)).max())
+            out.append({"op": "bootstrap", "logN": 16, "slots": n, "ms": ms.value / reps,
+                        "level_out": lib.GetCiphertextLevel(res), "max_err": err,
+                        "setup_s": setup_s, "chain": "50 + 23 x 36 usable, 14 x 60 reserved, 6 x 60 special"})
+            lib.DeleteCiphertext(res)
+            lib.DeleteCiphertext(ct)
+    finally:
+        lib.DeleteScheme()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batches", default="1,16,128")
@@ -372,6 +423,7 @@ def main():
     ap.add_argument("--table", action="store_true", help="also the IVE lookup's one-pass table product")
     ap.add_argument("--relu", action="store_true", help="also Orion's composite ReLU through EvaluatePolynomial")
     ap.add_argument("--upload", action="store_true", help="also the selector upload (device encode, lane split)")
+    ap.add_argument("--boot", action="store_true", help="also bootstrapping at LogN 16 (256 and 512 slots)")
     args = ap.parse_args()
     run([int(b) for b in args.batches.split(",")], args.reps, args.ops, args.rotations,
         emit=lambda line: print(json.dumps(line), flush=True))
@@ -382,6 +434,9 @@ def main():
             print(json.dumps(line), flush=True)
     if args.upload:
         print(json.dumps(run_upload()), flush=True)
+    if args.boot:
+        for line in run_boot(slot_counts=(256, 512)):
+            print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
