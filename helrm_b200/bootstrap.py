@@ -11,6 +11,13 @@ Kim, Song, "Bootstrapping for approximate homomorphic encryption",
 EUROCRYPT 2018; sparse packing and the cosine / double-angle EvalMod of
 Chen, Chillotti, Song, EUROCRYPT 2019):
 
+  Replicate  a ciphertext tagged wider than n slots carries its values in
+             slots [0, n) and zeros elsewhere (Orion's Bootstrap layer zeroes
+             the rest with its prescale multiply, orion/nn/operations.py:
+             98-104): log2(N / 2n) rotations by n 2^i at level 0 (no level)
+             tile it into the sparse subring; one tagged with n slots
+             (SetCiphertextSlots, the reference's sparse ciphertexts) is
+             periodic already;
   ModRaise   the level-0 ciphertext, lifted to every prime, decrypts to
              t = m + q0 I (I small: the overflow of c0 + c1 s over q0);
   SubSum     log2(N / 2n) rotations by n 2^i add the conjugates of the
@@ -170,9 +177,12 @@ def bootstrap(lib, ctx: BootContext, ct: int) -> int:
         owned.append(x)
         return x
 
-    x = lib.AlignToLevelNew(ct, 0) if lib.GetCiphertextLevel(ct) > 0 else ct
-    if x != ct:
-        owned.append(x)
+    x = new(lib.AlignToLevelNew(ct, 0))
+    if lib.GetCiphertextSlots(ct) > ctx.n:
+        for k in ctx.subsum_steps:
+            r = lib.RotateNew(x, k)
+            lib.AddCiphertext(x, r)
+            lib.DeleteCiphertext(r)
     t = new(lib.ModRaiseNew(x))
     for k in ctx.subsum_steps:
         r = lib.RotateNew(t, k)
@@ -213,6 +223,7 @@ def bootstrap(lib, ctx: BootContext, ct: int) -> int:
     # the values: E(m) / q0 at scale s_asin s_stc / q_stc, i.e. the input's
     # slots at s_asin s_stc scale_in / (q_stc q0)
     lib.SetCiphertextScale(res, ctx.s_asin * ctx.s_stc * scale_in / (ctx.q[ctx.lvl_stc] * ctx.q0))
+    lib.SetCiphertextSlots(res, lib.GetCiphertextSlots(ct))
     for o in owned:
         lib.DeleteCiphertext(o)
     return res

@@ -2259,6 +2259,25 @@ void keymult(u64 *acc, const u64 *D, const u64 *key, u64 galois, int nq, int K, 
 // =====================================================================
 // fused baby steps + diagonal MAC (double hoisting): see hb_bsgs.cuh
 // =====================================================================
+// Every instantiation of the fused MAC may take up to the per-block limit
+// of dynamic shared memory: set once for all of them (a launch allocates
+// only what it asks for).  Two launchers with their own high-water marks
+// would lower each other's settings.
+static void bsgs_mac_attributes() {
+    static bool done = false;
+    if (done) return;
+    const int lim = 227 * 1024;
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<0, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<0, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<0, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    done = true;
+}
+
 void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch, int nq, int K, int L, int beta,
                    int keyP, int pt_nq, const u64 *pmod_q, int logN, int nbatch, size_t ct_stride, size_t d_stride,
                    size_t inner_stride, cudaStream_t s) {
@@ -2270,18 +2289,7 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
     const size_t smem = bsgs_smem_words(beta, pair ? 2 : 1, split && full) * 8;
     if (smem > 227 * 1024 || beta > HB_MAX_BETA)
         throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
-    static size_t attr = 0;
-    if (smem > attr) {
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<0, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<0, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<0, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
+    bsgs_mac_attributes();
     const size_t n = (size_t)(nq + K) << logN;
     // per ciphertext: c0/c1 rows, the digits, the inner sums written; per
     // launch: every baby key and plaintext of the chunk once
@@ -2494,13 +2502,7 @@ void bsgs_baby_mac_special(u64 *inner, const u64 *ct, const u64 *D, const BsgsCh
     const size_t smem = bsgs_smem_words(beta) * 8;
     if (smem > 227 * 1024 || beta > HB_MAX_BETA)
         throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
-    static size_t attr = 0;
-    if (smem > attr) {
-        cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<0, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_bsgs_mac<0, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
+    bsgs_mac_attributes();
     const double kd = (double)K * (1 << logN);
     ProfScope ps(KC_BSGS_MAC,
                  8.0 * (nbatch * (beta * kd + 2.0 * ch.gcount * kd * (ch.accumulate ? 2 : 1)) +

@@ -11,8 +11,8 @@ oracle's exact operators, the published circuit the B200 library runs
 arcsine EvalMod, a dense SlotsToCoeffs; see the library module for the
 derivation), in the same order with the same constants, so that given the
 same keys and transform plaintexts the GPU output must match residue for
-residue.  `bootstrap` takes the library's plaintexts and keys as inputs;
-`prepare` builds them on the CPU for a standalone run.
+residue.  `bootstrap` takes the transform plaintexts and keys as inputs
+(the library's, or ones the CPU test builds with the oracle's encoder).
 """
 from __future__ import annotations
 
@@ -75,15 +75,21 @@ def mod_raise(o, ct, nq_all):
     return out
 
 
-def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts):
+def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts, replicate=False):
     """ctx: the scales and constants of helrm_b200.bootstrap.BootContext
     (dict with n, R, B, q0, s_u, s_cos, s_asin, subsum_steps, cts_bs, stc_bs,
     cos_coeffs, asin_coeffs, top); keys: {galois: switching key};
     cts_pts / stc_pts: the transforms' extended-basis plaintexts, diagonal k
-    at index k.  Returns (ciphertext, output scale)."""
+    at index k.  replicate: the input holds its values in slots [0, n) and
+    zeros elsewhere and is first tiled over the subring by rotations at
+    level 0.  Returns (ciphertext, output scale)."""
     n, S = ctx["n"], o.N // 2
     nq_all = ctx["top"] + 1
-    x = ct[:, :1]
+    x = np.ascontiguousarray(ct[:, :1])
+    if replicate:
+        for k in ctx["subsum_steps"]:
+            g = o.galois(k)
+            x = add(o, x, o.rotate(x, keys[g], g))
     t = mod_raise(o, x, nq_all)
     for k in ctx["subsum_steps"]:
         g = o.galois(k)

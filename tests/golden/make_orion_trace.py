@@ -43,6 +43,15 @@ CONFIG_DEEP = {
                     "RingType": "Standard"},
     "orion": dict(CONFIG["orion"]),
 }
+# the network that needs bootstrapping: two ReLUs (15 levels each) over a
+# usable chain of 17 levels, so Orion's placement inserts a bootstrap; the
+# boot parameters make the backend reserve its bootstrapping primes
+CONFIG_BOOT = {
+    "ckks_params": {"LogN": 13, "LogQ": [50] + [36] * 17, "LogP": [60] * 6, "LogScale": 36, "H": 192,
+                    "RingType": "Standard"},
+    "boot_params": {"LogP": [60] * 6, "num_cts_levels": 1, "num_stc_levels": 1, "log_message_ratio": 14},
+    "orion": dict(CONFIG["orion"]),
+}
 
 
 class Recorder:
@@ -91,11 +100,12 @@ class Recorder:
         self._default_scale = float(1 << int(params.get_logscale()))
         self.params = {"logn": int(params.get_logn()), "logq": [int(x) for x in params.get_logq()],
                        "logp": [int(x) for x in params.get_logp()], "logscale": int(params.get_logscale()),
-                       "h": int(params.get_hamming_weight())}
+                       "h": int(params.get_hamming_weight()),
+                       "boot": params.get_boot_num_cts_levels() is not None}
 
     def __getattr__(self, name):
         # the setup and key calls Orion makes with nothing to return
-        if name.startswith("New") or name in ("GenerateSecretKey", "GeneratePublicKey",
+        if (name.startswith("New") and name != "NewBootstrapper") or name in ("GenerateSecretKey", "GeneratePublicKey",
                                               "GenerateRelinearizationKey", "GenerateEvaluationKeys",
                                               "DeleteBootstrappers"):
             def noop(*a):
@@ -182,6 +192,23 @@ class Recorder:
 
     def AddScalar(self, ct, v):
         return self._scalar("AddScalar", ct, float(v), True, False)
+
+    def SubScalarNew(self, ct, v):
+        return self._scalar("SubScalarNew", ct, float(v), False, False)
+
+    def SubScalar(self, ct, v):
+        return self._scalar("SubScalar", ct, float(v), True, False)
+
+    # -- bootstrapping (the output at the top of the usable chain, the
+    # input's scale; helrm_b200/bootstrap.py) ------------------------------
+    def NewBootstrapper(self, logp, slots):
+        self._log("NewBootstrapper", [None, int(slots)], None)
+
+    def Bootstrap(self, ct, slots):
+        meta = dict(self.cts[ct])
+        meta["level"] = self._max_level
+        i = self._ct_new(meta)
+        return self._log("Bootstrap", [{"ct": ct}, int(slots)], {"ct": i})["ct"]
 
     def _relin(self, name, a, b, inplace):
         ma, mb = self.cts[a], self.cts[b]
@@ -385,6 +412,26 @@ def record(net_kind: str, ref_root: str, config=None):
                 return self.fc(x)
         net = Net()
         inp = torch.randn(1, 32)
+    elif net_kind == "mlp_boot":
+        class Net(on.Module):
+            def __init__(self):
+                super().__init__()
+                self.fc1 = on.Linear(16, 8)
+                self.act1 = on.ReLU()
+                self.fc2 = on.Linear(8, 8)
+                self.act2 = on.ReLU()
+                self.fc3 = on.Linear(8, 4)
+
+            def forward(self, x):
+                return self.fc3(self.act2(self.fc2(self.act1(self.fc1(x)))))
+        net = Net()
+        for seed in range(200):
+            inp = torch.randn(1, 16, generator=torch.Generator().manual_seed(seed))
+            h1 = net.fc1(inp).detach()
+            h2 = net.fc2(torch.relu(h1)).detach()
+            if (float(h1.abs().min()) >= 0.05 * float(h1.abs().max()) and
+                    float(h2.abs().min()) >= 0.05 * float(h2.abs().max())):
+                break
     elif net_kind == "mlp_relu":
         class Net(on.Module):
             def __init__(self):
@@ -437,8 +484,9 @@ def main():
     if not ref or not os.path.isdir(ref):
         raise SystemExit("usage: make_orion_trace.py <reference checkout>")
     traces, arrays = {}, {}
-    for kind in ("linear", "embedding", "mlp_relu"):
-        rec, out_clear, decodes, level = record(kind, ref, CONFIG_DEEP if kind == "mlp_relu" else CONFIG)
+    configs = {"mlp_relu": CONFIG_DEEP, "mlp_boot": CONFIG_BOOT}
+    for kind in ("linear", "embedding", "mlp_relu", "mlp_boot"):
+        rec, out_clear, decodes, level = record(kind, ref, configs.get(kind, CONFIG))
         traces[kind] = {"params": rec.params, "calls": rec.calls, "output_decode_calls": decodes,
                         "input_level": int(level), "cleartext_output": [float(v) for v in out_clear]}
         for k, v in rec.arrays.items():

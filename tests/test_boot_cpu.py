@@ -50,7 +50,8 @@ def _transform_pts(o, A, level, scale, bs):
     return [o.encode(W.preroll(d[k], k // bs, bs), level + 1, scale, ext=True) for k in range(A.shape[0])]
 
 
-def test_oracle_bootstrap_precision(scheme):
+@pytest.mark.parametrize("padded", [False, True])
+def test_oracle_bootstrap_precision(scheme, padded):
     from oracle import boot as OB
     o, sk, logscale = scheme
     n, S = 8, o.N // 2
@@ -89,8 +90,13 @@ def test_oracle_bootstrap_precision(scheme):
     rng = np.random.default_rng(4)
     z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.7
     scale = float(1 << logscale)
-    ct = o.encrypt(sk, o.encode(np.tile(z, R), 1, scale), 11)
-    out, s_out = OB.bootstrap(o, ct, scale, ctx, keys, rlk, cts_pts, stc_pts)
+    if padded:  # values in slots [0, n), zeros after them (tiled first)
+        v = np.zeros(S, complex)
+        v[:n] = z
+    else:       # the sparse (periodic) form
+        v = np.tile(z, R)
+    ct = o.encrypt(sk, o.encode(v, 1, scale), 11)
+    out, s_out = OB.bootstrap(o, ct, scale, ctx, keys, rlk, cts_pts, stc_pts, replicate=padded)
     assert out.shape[1] == usable_top + 1
     assert s_out == pytest.approx(scale, rel=1e-9)
     got = o.decode(o.decrypt(sk, out), s_out, complex_out=True)

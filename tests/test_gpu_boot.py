@@ -34,12 +34,22 @@ def pair(oracle_mod):
     p.close()
 
 
-def _encrypt_sparse(pair, z, n, level):
-    vals = np.tile(np.asarray(z, complex), pair.slots // n)
+def _encrypt_sparse(pair, z, n, level, padded=False):
+    """n slot values repeated over every slot and tagged as a sparse
+    ciphertext of n slots (the reference's sparse ciphertexts), or, with
+    padded, in slots [0, n) and zero elsewhere at the full width (what
+    Orion's Bootstrap layer hands a non-Cheddar backend)"""
+    if padded:
+        vals = np.zeros(pair.slots, complex)
+        vals[:n] = z
+    else:
+        vals = np.tile(np.asarray(z, complex), pair.slots // n)
     inter = np.stack([vals.real, vals.imag], axis=-1).ravel()
     pt = pair.lib.EncodeComplex(inter, level, pair.scale)
     ct = pair.lib.Encrypt(pt)
     pair.lib.DeletePlaintext(pt)
+    if not padded:
+        pair.lib.SetCiphertextSlots(ct, n)
     return ct
 
 
@@ -64,26 +74,32 @@ def test_bootstrap_restores_values(pair, n):
     assert np.abs(got - np.tile(z, pair.slots // n)).max() < 1e-5
 
 
-def test_bootstrap_real_values_from_a_higher_level(pair):
-    """Orion's real activations, handed over above level 0 (dropped first)."""
+def test_bootstrap_zero_padded_input_from_a_higher_level(pair):
+    """Orion's real activations as its Bootstrap layer hands them to a
+    non-Cheddar backend: the first n slots, zeros after them, at the full
+    width and above level 0 (dropped first); the values come back in the
+    first n slots (repeated over the rest)."""
     n = 32
     x = np.linspace(-1, 1, n)
-    ct = _encrypt_sparse(pair, x, n, 2)
+    ct = _encrypt_sparse(pair, x, n, 2, padded=True)
     out = pair.lib.Bootstrap(ct, n)
     got = _decrypt_c(pair, out)
     assert np.abs(got.real - np.tile(x, pair.slots // n)).max() < 1e-5
     assert np.abs(got.imag).max() < 1e-5
-    # and a second pass: bootstrapping the output again
-    again = pair.lib.Bootstrap(pair.lib.AlignToLevelNew(out, 0), n)
+    # and a second pass on the (periodic) output, tagged sparse
+    low = pair.lib.AlignToLevelNew(out, 0)
+    pair.lib.SetCiphertextSlots(low, n)
+    again = pair.lib.Bootstrap(low, n)
     assert np.abs(_decrypt_c(pair, again).real - np.tile(x, pair.slots // n)).max() < 2e-5
 
 
-def test_bootstrap_residues_match_oracle(pair):
+@pytest.mark.parametrize("padded", [False, True])
+def test_bootstrap_residues_match_oracle(pair, padded):
     from oracle import boot as OB
     n = 16
     rng = np.random.default_rng(3)
     z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.7
-    ct = _encrypt_sparse(pair, z, n, 0)
+    ct = _encrypt_sparse(pair, z, n, 0, padded=padded)
     pair.lib.NewBootstrapper(None, n)
     ctx = pair.lib._boot[n]
     out = pair.lib.Bootstrap(ct, n)
@@ -99,7 +115,8 @@ def test_bootstrap_residues_match_oracle(pair):
          "cos_coeffs": BT.cos_coeffs(ctx.B, BT.DOUBLE_ANGLES, BT.COS_DEGREE), "asin_coeffs": BT.ASIN_COEFFS}
     cts_pts = [lib.GetLinearTransformPlaintext(ctx.cts, k) for k in range(n)]
     stc_pts = [lib.GetLinearTransformPlaintext(ctx.stc, k) for k in range(n)]
-    want, s_out = OB.bootstrap(o, pair.ct_data(ct), pair.scale, c, keys, pair.key(0), cts_pts, stc_pts)
+    want, s_out = OB.bootstrap(o, pair.ct_data(ct), pair.scale, c, keys, pair.key(0), cts_pts, stc_pts,
+                               replicate=padded)
     assert np.array_equal(pair.ct_data(out), want)
     assert lib.GetCiphertextScale(out) == pytest.approx(s_out, rel=1e-12)
 

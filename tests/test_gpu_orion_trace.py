@@ -7,7 +7,10 @@ orion/nn/linear.py:99-140, orion/backend/python/lt_evaluator.py:224-275),
 and of a Linear -> ReLU -> Linear network whose ReLU is Orion's composite
 minimax sign [15, 15, 27] (orion/nn/activation.py:201-300: the sign
 coefficients from GenerateMinimaxSignCoeffs, three EvaluatePolynomial
-stages at the levels Orion's compiler placed, x * step(x))
+stages at the levels Orion's compiler placed, x * step(x)), and of a
+network with two ReLUs over a chain too short for both, where Orion's own
+bootstrap placement (orion/core/auto_bootstrap.py) inserted two
+NewBootstrapper / Bootstrap calls (orion/nn/operations.py:38-115)
 with ``backend: b200`` registered through helrm_b200.orion_adapter and
 recorded every backend call, in order, with its arguments.  The reference
 cannot travel to the GPU box, so the calls are replayed here on the real
@@ -43,7 +46,7 @@ def _replay(kind):
     p = t["params"]
     lib = B200Library(seed=17, device=0)
     lib.setup_bindings(CKKSConfig(logn=p["logn"], logq=p["logq"], logp=p["logp"], logscale=p["logscale"],
-                                  h=p["h"]))
+                                  h=p["h"], boot=bool(p.get("boot", False))))
     handles = {}
     decoded = {}
     try:
@@ -74,7 +77,7 @@ def _replay(kind):
         lib.DeleteScheme()
 
 
-@pytest.mark.parametrize("kind", ["linear", "embedding", "mlp_relu"])
+@pytest.mark.parametrize("kind", ["linear", "embedding", "mlp_relu", "mlp_boot"])
 def test_orion_flow_replayed_on_b200(kind):
     out, clear = _replay(kind)
     n = len(clear)
