@@ -44,9 +44,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--mode", default="dp", choices=["dp", "tables"],
+    ap.add_argument("--mode", default="dp", choices=["dp", "tables", "helrm"],
                     help="dp: each rank its own batch (weak scaling); tables: the 26 tables split across the "
-                         "ranks, one batch, partial ciphertexts summed by one NCCL reduce (strong scaling)")
+                         "ranks, one batch, partial ciphertexts summed by one NCCL reduce (strong scaling); "
+                         "helrm: BASELINE config 4, the whole bootstrapped HE-LRM forward, each rank its own batch")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--level", type=int, default=23, help="PCMM input level (23 = all 24 limbs)")
     ap.add_argument("--bsgs-ratio", type=float, default=8.0,
@@ -683,6 +684,154 @@ def run_b200_tables(args, dist):
         raise SystemExit("bench: sharded embedding out of tolerance")
 
 
+LOGIT_TOL = 1e-3   # north_star: decrypted logits within 1e-3
+
+
+def run_b200_helrm(args, dist):
+    """the end-to-end HE-LRM forward (bottom MLP, the
+    26-table embedding, top MLP, Orion's composite ReLUs and five
+    bootstraps per query) over a batch of ciphertexts, one query each.
+    A step is the forward of the batch with its inputs resident; e2e adds
+    the encoding and encryption of the host inputs and the decryption and
+    decoding of the logits to host memory."""
+    import torch
+
+    from helrm_b200 import B200Library, _capi
+    from helrm_b200 import helrm as H
+    from helrm_b200 import workload as W
+    from helrm_b200.params import CFG4, CFG4_DNUM
+
+    dev = dist.local
+    torch.cuda.set_device(dev)
+    lib = B200Library(dnum=CFG4_DNUM, seed=2000 + dist.rank, device=dev)
+    lib.setup_bindings(CFG4)
+    lib.GenerateSecretKey()
+    lib.GenerateRelinearizationKey()
+    t0 = time.time()
+    net = H.HELRM(lib, seed=0, emb_ratio=args.bsgs_ratio)
+    setup_s = time.time() - t0
+    dense = H.dense_inputs(args.batch, 100 + dist.rank)
+    sel = net.selectors(W.zipf_queries(net.vocab, args.batch, seed=200 + dist.rank))
+    d_cts, s_cts = net.encrypt(dense, sel)
+    capi = _capi.load()
+
+    def run(nsteps):
+        for _ in range(nsteps):
+            for o in net.forward(d_cts, s_cts):
+                lib.DeleteCiphertext(o)
+
+    # correctness on the first warm-up step
+    outs = net.forward(d_cts, s_cts)
+    got = net.decrypt(outs)
+    for o in outs:
+        lib.DeleteCiphertext(o)
+    want = net.cleartext(dense, sel)
+    exact = net.cleartext(dense, sel, poly=False)
+    err_poly = float(np.abs(got - want).max())
+    err_exact = float(np.abs(got - exact).max())
+    approx_exact = float(np.abs(want - exact).max())
+    correct = err_poly <= LOGIT_TOL
+    run(max(0, args.warmup - 1))
+    lib.Synchronize()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(dev)
+    dist.barrier()
+    torch.cuda.synchronize()
+    lib.Synchronize()
+    clocks.start()
+    n0 = ctypes.c_uint64(0)
+    _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n0)))
+    _capi.check(capi.helrm_TimerStart())
+    run(args.steps)
+    ms = ctypes.c_double(0)
+    _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+    n1 = ctypes.c_uint64(0)
+    _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n1)))
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t_dev = dist.max(ms.value / 1000.0)
+    value = whole_job_rate(dist.world, args.batch, args.steps, t_dev)
+
+    # one more step with the per-kernel profiler: breakdown and roofline
+    _capi.check(capi.helrm_ProfilerRange(1))
+    _capi.check(capi.helrm_ProfileEnable(1))
+    lib.Synchronize()
+    _capi.check(capi.helrm_TimerStart())
+    run(1)
+    ms_prof = ctypes.c_double(0)
+    _capi.check(capi.helrm_TimerStop(ctypes.byref(ms_prof)))
+    kern, raw = read_profile(capi, _capi, 1)
+    _capi.check(capi.helrm_ProfileEnable(0))
+    _capi.check(capi.helrm_ProfilerRange(0))
+    dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
+    dms, dby, _, dl = raw[dom]
+    hbm, src = peaks()
+    achieved = dby / (dms * 1e6)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured"
+                else "fallback 6.65 TB/s", "bytes_per_launch": dby / dl, "avg_launch_ms": dms / dl,
+                "traffic": None, "profiled_ms_per_step": ms_prof.value}
+
+    # end to end: host inputs -> encode + encrypt -> forward -> decrypt +
+    # decode -> host logits, every step inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        def e2e_step():
+            dc, sc = net.encrypt(dense, sel)
+            outs = net.forward(dc, sc)
+            net.decrypt(outs)
+            for x in dc + sc + outs:
+                lib.DeleteCiphertext(x)
+
+        e2e_step()
+        dist.barrier()
+        lib.Synchronize()
+        _capi.check(capi.helrm_TimerStart())
+        for _ in range(args.steps):
+            e2e_step()
+        ms2 = ctypes.c_double(0)
+        _capi.check(capi.helrm_TimerStop(ctypes.byref(ms2)))
+        t_e2e = dist.max(ms2.value / 1000.0)
+        N = lib.scheme_info()["N"]
+        e2e = {"value": whole_job_rate(dist.world, args.batch, args.steps, t_e2e), "unit": UNIT,
+               "h2d_bytes_per_step": int(dense.size * 8 + sel.size * 8),
+               "d2h_bytes_per_step": int(args.batch * min(4, net.level_out + 1) * N * 8),
+               "ms_per_step": 1000.0 * t_e2e / args.steps,
+               "what": "EncodeBatch of the host features and selectors, Encrypt, the forward, Decrypt, Decode "
+                       "(the decoder reads back the plaintext's first limbs and decodes on the host)"}
+    info = net.info()
+    mem = {"peak_device_mb": lib.GetPeakDeviceMemoryMB(), "key_mb": lib.GetKeyMemoryMB()}
+    net.close()
+    lib.DeleteScheme()
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * t_dev / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64",
+            "data": "synthetic (seeded Criteo-shaped dense features and Zipf queries; random-init weights)",
+            "config": {"workload": "cfg4: end-to-end HE-LRM forward (BASELINE configs[3])", "logN": 16,
+                       "q_limbs_usable": 24, "q_bits": "50 + 23 x 36", "boot_primes": "14 x 60",
+                       "special_primes": "6 x 60", "dnum": CFG4_DNUM, "h": 192, "batch_ciphertexts": args.batch,
+                       "queries_per_ciphertext": 1, "bottom": list(H.BOTTOM), "top": [432] + list(H.TOP_HIDDEN) + [1],
+                       "relu": list(H.SIGN_DEGREES), "embedding_bsgs_ratio": args.bsgs_ratio,
+                       "parallelism": f"dp{args.gpus} (query batch)", "plan": info,
+                       "l2": "inputs larger than L2 (tens of GB of diagonals and keys per step)"},
+            "roofline": roofline,
+            "cpu_baseline": {"value": None, "unit": UNIT, "cores": 0, "kind": "port",
+                             "sample": "not run: one bootstrapped LogN-16 forward on the oracle port takes hours; "
+                                       "the config-2 line carries the CPU baseline of the embedding product"},
+            "e2e": e2e, "gpu_launches": int(n1.value - n0.value), "clocks": clk, "kernels": kern,
+            "max_abs_err_logits_vs_polynomial_cleartext": err_poly, "max_abs_err_logits_vs_relu_cleartext": err_exact,
+            "composite_relu_approximation_error": approx_exact, "logit_tol": LOGIT_TOL, "correct": correct,
+            "setup_s": setup_s, "memory": mem,
+        }
+        print(json.dumps(line), flush=True)
+    if not correct:
+        raise SystemExit("bench: logits out of tolerance")
+
+
 def go_probe() -> str:
     """Whether the reference's Lattigo CPU path could be built on this host:
     a Go toolchain and the lattigo/v6 module in the module cache."""
@@ -715,6 +864,8 @@ def main():
     try:
         if args.mode == "tables":
             run_b200_tables(args, dist)
+        elif args.mode == "helrm":
+            run_b200_helrm(args, dist)
         else:
             run_b200(args, dist)
     finally:

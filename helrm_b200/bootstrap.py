@@ -165,44 +165,58 @@ class BootContext:
 
 
 def bootstrap(lib, ctx: BootContext, ct: int) -> int:
-    """The circuit on one ciphertext; returns a new ciphertext at the top
-    of the usable chain holding the same slot values."""
-    scale_in = lib.GetCiphertextScale(ct)
-    if ctx.q0 < 16.0 * scale_in:
-        raise RuntimeError("Bootstrap: the message ratio q0 / scale must be at least 2^4 "
-                           f"(q0 = 2^{math.log2(ctx.q0):.1f}, scale = 2^{math.log2(scale_in):.1f})")
-    owned = []
+    """The circuit on one ciphertext (bootstrap_batch of one)."""
+    return bootstrap_batch(lib, ctx, [ct])[0]
 
-    def new(x):
-        owned.append(x)
-        return x
 
-    x = new(lib.AlignToLevelNew(ct, 0))
-    if lib.GetCiphertextSlots(ct) > ctx.n:
-        for k in ctx.subsum_steps:
-            r = lib.RotateNew(x, k)
-            lib.AddCiphertext(x, r)
-            lib.DeleteCiphertext(r)
-    t = new(lib.ModRaiseNew(x))
-    for k in ctx.subsum_steps:
-        r = lib.RotateNew(t, k)
-        lib.AddCiphertext(t, r)
-        lib.DeleteCiphertext(r)
-    lib.SetCiphertextScale(t, ctx.R * ctx.q0)
-    w = new(lib.RescaleNew(new(lib.EvaluateLinearTransform(ctx.cts, t))))
+def bootstrap_batch(lib, ctx: BootContext, cts) -> list[int]:
+    """The circuit on a batch of ciphertexts of the same slot count: the
+    rotations, transforms, rescales and polynomials run through the
+    library's batched entry points.  Returns new ciphertexts at the top of
+    the usable chain holding the same slot values."""
+    cts = [int(c) for c in cts]
+    if not cts:
+        return []
+    scales = [lib.GetCiphertextScale(c) for c in cts]
+    for s_in in scales:
+        if ctx.q0 < 16.0 * s_in:
+            raise RuntimeError("Bootstrap: the message ratio q0 / scale must be at least 2^4 "
+                               f"(q0 = 2^{math.log2(ctx.q0):.1f}, scale = 2^{math.log2(s_in):.1f})")
+    reps = len(ctx.subsum_steps)
+    # level 0; a full-width input is tiled into the subring by the same
+    # rotations (slots/2, slots/4, ..., n: the hybrid fold's)
+    xs = [lib.AlignToLevelNew(c, 0) for c in cts]
+    wide = [x for x, c in zip(xs, cts) if lib.GetCiphertextSlots(c) > ctx.n]
+    if wide and reps:
+        lib.HybridFoldBatch(wide, reps)
+    ts = [lib.ModRaiseNew(x) for x in xs]
+    for x in xs:
+        lib.DeleteCiphertext(x)
+    if reps:
+        lib.HybridFoldBatch(ts, reps)   # SubSum
+    for t in ts:
+        lib.SetCiphertextScale(t, ctx.R * ctx.q0)
+    ws = lib.EvaluateLinearTransformBatch(ctx.cts, ts)
+    for t in ts:
+        lib.DeleteCiphertext(t)
+    lib.RescaleBatch(ws)
     # u_re = w + conj(w) - 1/4B, u_im = i (conj(w) - w) - 1/4B
-    cj = new(lib.ConjugateNew(w))
-    u_re = lib.AddCiphertextNew(w, cj)
-    u_im = lib.SubCiphertextNew(cj, w)
-    lib.MulImaginaryUnit(u_im)
-    for u in (u_re, u_im):
-        lib.SetCiphertextScale(u, ctx.s_u)
-        lib.AddScalar(u, -1.0 / (4.0 * ctx.B))
-    ys = lib.EvaluatePolynomialBatch([u_re, u_im], ctx.poly_cos, ctx.s_cos)
-    lib.DeleteCiphertext(u_re)
-    lib.DeleteCiphertext(u_im)
-    out = []
-    for y in ys:
+    us = []
+    for w in ws:
+        cj = lib.ConjugateNew(w)
+        u_re = lib.AddCiphertextNew(w, cj)
+        u_im = lib.SubCiphertextNew(cj, w)
+        lib.MulImaginaryUnit(u_im)
+        lib.DeleteCiphertext(cj)
+        lib.DeleteCiphertext(w)
+        for u in (u_re, u_im):
+            lib.SetCiphertextScale(u, ctx.s_u)
+            lib.AddScalar(u, -1.0 / (4.0 * ctx.B))
+        us += [u_re, u_im]
+    ys = lib.EvaluatePolynomialBatch(us, ctx.poly_cos, ctx.s_cos)
+    for u in us:
+        lib.DeleteCiphertext(u)
+    for i, y in enumerate(ys):
         for _ in range(DOUBLE_ANGLES):
             sq = lib.MulRelinCiphertextNew(y, y)
             lib.DeleteCiphertext(y)
@@ -210,20 +224,23 @@ def bootstrap(lib, ctx: BootContext, ct: int) -> int:
             lib.AddCiphertext(sq, sq)
             lib.AddScalar(sq, -1.0)
             y = sq
-        out.append(y)
-    zs = lib.EvaluatePolynomialBatch(out, ctx.poly_asin, ctx.s_asin)
-    for y in out:
+        ys[i] = y
+    zs = lib.EvaluatePolynomialBatch(ys, ctx.poly_asin, ctx.s_asin)
+    for y in ys:
         lib.DeleteCiphertext(y)
-    lib.MulImaginaryUnit(zs[1])
-    lib.AddCiphertext(zs[0], zs[1])
-    lib.DeleteCiphertext(zs[1])
-    res = lib.EvaluateLinearTransform(ctx.stc, zs[0])
-    lib.DeleteCiphertext(zs[0])
-    lib.Rescale(res)
+    pre = []
+    for re, im in zip(zs[0::2], zs[1::2]):
+        lib.MulImaginaryUnit(im)
+        lib.AddCiphertext(re, im)
+        lib.DeleteCiphertext(im)
+        pre.append(re)
+    outs = lib.EvaluateLinearTransformBatch(ctx.stc, pre)
+    for y in pre:
+        lib.DeleteCiphertext(y)
+    lib.RescaleBatch(outs)
     # the values: E(m) / q0 at scale s_asin s_stc / q_stc, i.e. the input's
     # slots at s_asin s_stc scale_in / (q_stc q0)
-    lib.SetCiphertextScale(res, ctx.s_asin * ctx.s_stc * scale_in / (ctx.q[ctx.lvl_stc] * ctx.q0))
-    lib.SetCiphertextSlots(res, lib.GetCiphertextSlots(ct))
-    for o in owned:
-        lib.DeleteCiphertext(o)
-    return res
+    for o, c, s_in in zip(outs, cts, scales):
+        lib.SetCiphertextScale(o, ctx.s_asin * ctx.s_stc * s_in / (ctx.q[ctx.lvl_stc] * ctx.q0))
+        lib.SetCiphertextSlots(o, lib.GetCiphertextSlots(c))
+    return outs

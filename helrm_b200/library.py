@@ -714,6 +714,15 @@ class B200Library:
             self.NewBootstrapper(None, n)
         return _bt.bootstrap(self, self._boot[n], int(ct_id))
 
+    def BootstrapBatch(self, ct_ids: Sequence[int], slots) -> list[int]:
+        """Bootstrap over a batch of ciphertexts of one slot count; each
+        output equals Bootstrap of that input residue for residue."""
+        from . import bootstrap as _bt
+        n = int(slots)
+        if n not in self._boot:
+            self.NewBootstrapper(None, n)
+        return _bt.bootstrap_batch(self, self._boot[n], [int(c) for c in ct_ids])
+
     def DeleteBootstrappers(self):
         """Release the bootstrapping transforms (keys stay cached)."""
         for ctx in self._boot.values():

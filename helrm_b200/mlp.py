@@ -33,10 +33,12 @@ class LinearLayer:
     """One encrypted Linear layer (weight out x in, bias out) on a
     B200Library scheme, evaluated on a batch of ciphertexts that each hold
     one input vector in slots 0..in-1 (any period-replicated copies beyond
-    are ignored: the diagonals read only the first copy)."""
+    are ignored: the diagonals read only the first copy).  narrow retags
+    the folded output to its period; exact encodes the diagonals at the
+    level's prime instead of the default scale."""
 
     def __init__(self, lib, weight: np.ndarray, bias, level: int, last: bool = False, ratio: float = 2.0,
-                 narrow: bool = True):
+                 narrow: bool = True, exact: bool = False):
         self.lib = lib
         info = lib.scheme_info()
         self.slots = info["slots"]
@@ -44,13 +46,18 @@ class LinearLayer:
         H, Wd = self.weight.shape
         if max(H, Wd) > self.slots:
             raise ValueError("layer wider than the ciphertext's slots")
+        self.has_bias = bias is not None  # Orion's Linear(bias=False) adds nothing
         self.bias = np.zeros(H) if bias is None else np.asarray(bias, dtype=np.float64)
         self.level, self.last = level, last
         d, self.rot = W.diagonalize(self.weight, self.slots, "hybrid", last=last)
         self.diags = d[(0, 0)]
         self.ks = sorted(self.diags)
         data = np.concatenate([self.diags[k].astype(np.float64) for k in self.ks])
-        self.lt = lib.GenerateLinearTransform(self.ks, data, level, ratio, "none")
+        if exact:  # diagonals at q_level: the rescaled output keeps the input's scale exactly
+            q = float(lib.GetModuliChain()[level])
+            self.lt = lib.GenerateLinearTransformEx(self.ks, data, self.slots, level, ratio, False, q)
+        else:
+            self.lt = lib.GenerateLinearTransform(self.ks, data, level, ratio, "none")
         for k in lib.GetLinearTransformRotationKeys(self.lt):
             lib.GenerateLinearTransformRotationKey(k)
         for i in range(1, self.rot + 1):
@@ -78,7 +85,8 @@ class LinearLayer:
         for o in outs:
             if self.folded_slots and self.folded_slots < lib.GetCiphertextSlots(o):
                 lib.SetCiphertextSlots(o, self.folded_slots)
-            lib.AddPlaintext(o, self._bias_for(lib.GetCiphertextScale(o)))
+            if self.has_bias:
+                lib.AddPlaintext(o, self._bias_for(lib.GetCiphertextScale(o)))
         return outs
 
     def cleartext(self, x) -> np.ndarray:

@@ -85,15 +85,15 @@ def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts, replicate=False
     level 0.  Returns (ciphertext, output scale)."""
     n, S = ctx["n"], o.N // 2
     nq_all = ctx["top"] + 1
+    def fold(c):  # c += rot(c, k) for k = slots/2, slots/4, ..., n (the hybrid fold's order)
+        for k in reversed(ctx["subsum_steps"]):
+            g = o.galois(k)
+            c = add(o, c, o.rotate(c, keys[g], g))
+        return c
     x = np.ascontiguousarray(ct[:, :1])
     if replicate:
-        for k in ctx["subsum_steps"]:
-            g = o.galois(k)
-            x = add(o, x, o.rotate(x, keys[g], g))
-    t = mod_raise(o, x, nq_all)
-    for k in ctx["subsum_steps"]:
-        g = o.galois(k)
-        t = add(o, t, o.rotate(t, keys[g], g))
+        x = fold(x)
+    t = fold(mod_raise(o, x, nq_all))
     ks = list(range(n))
     w = o.rescale(o.bsgs_lt(t, ks, cts_pts, ctx["cts_bs"], keys))
     gc = 2 * o.N - 1
