@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cfg3", action="store_true", help="skip the config-3 primitive microbenchmark")
+    ap.add_argument("--no-cfg4", action="store_true",
+                    help="skip the compact config-4 forward (one warm-up, one timed step) of the default line")
     ap.add_argument("--cpu-threads", type=int, default=0, help="oracle threads (0 = all host cores)")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: same 512-diagonal PCMM on 8 q limbs + 2 special primes (dnum 4, "
@@ -566,6 +568,20 @@ def run_b200(args, dist):
                              "ms": r["ms"], "what": "whole hoisted key switch (ModUp + KeyMult + ModDown, NTTs "
                                                     "included), SURVEY 8(d) algorithmic bytes"}
 
+    # ---- config 4 (the whole HE-LRM forward), compact: the correctness
+    # step, one warm-up, one timed step (bench.py --mode helrm for the full
+    # line with W >= 3, the kernel breakdown and e2e)
+    cfg4 = None
+    if dist.world == 1 and not args.small and not args.no_cfg4:
+        try:
+            cfg4 = helrm_measure(dist, args.batch, 1, 2, profile=False, e2e=False)
+            cfg4["config"] = helrm_config(args)
+            cfg4["note"] = ("config 4 end to end: HE-LRM inferences/s (the headline value above is the config-2 "
+                            "embedding PCMM, one query per ciphertext)")
+            correct = correct and cfg4["correct"]
+        except Exception as ex:  # the PCMM line must not be lost with it
+            cfg4 = {"value": None, "error": f"{type(ex).__name__}: {ex}"}
+
     if dist.rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
@@ -578,6 +594,7 @@ def run_b200(args, dist):
             "gpu_launches": launches, "clocks": clk, "kernels": kern,
             "max_abs_err_embedding": max_err, "rel_err_embedding": rel_err, "rel_tol": REL_TOL,
             "residues_match": residues_match, "correct": correct, "level4_secondary": low, "cfg3": cfg3,
+            "cfg4_helrm_forward": cfg4,
         }
         print(json.dumps(line), flush=True)
     if not correct:
@@ -663,6 +680,20 @@ def run_b200_tables(args, dist):
     dist.barrier()
     t = dist.max(e0.elapsed_time(e1) / 1000.0)
     value = args.batch * args.steps / t
+    # ---- config 4 (the whole HE-LRM forward), compact: the correctness
+    # step, one warm-up, one timed step (bench.py --mode helrm for the full
+    # line with W >= 3, the kernel breakdown and e2e)
+    cfg4 = None
+    if dist.world == 1 and not args.small and not args.no_cfg4:
+        try:
+            cfg4 = helrm_measure(dist, args.batch, 1, 2, profile=False, e2e=False)
+            cfg4["config"] = helrm_config(args)
+            cfg4["note"] = ("config 4 end to end: HE-LRM inferences/s (the headline value above is the config-2 "
+                            "embedding PCMM, one query per ciphertext)")
+            correct = correct and cfg4["correct"]
+        except Exception as ex:  # the PCMM line must not be lost with it
+            cfg4 = {"value": None, "error": f"{type(ex).__name__}: {ex}"}
+
     if dist.rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
@@ -687,13 +718,15 @@ def run_b200_tables(args, dist):
 LOGIT_TOL = 1e-3   # north_star: decrypted logits within 1e-3
 
 
-def run_b200_helrm(args, dist):
+def helrm_measure(dist, batch: int, steps: int, warmup: int, profile: bool = True, e2e: bool = True) -> dict:
     """the end-to-end HE-LRM forward (bottom MLP, the
     26-table embedding, top MLP, Orion's composite ReLUs and five
     bootstraps per query) over a batch of ciphertexts, one query each.
-    A step is the forward of the batch with its inputs resident; e2e adds
-    the encoding and encryption of the host inputs and the decryption and
-    decoding of the logits to host memory."""
+    A step is the forward of the batch with its inputs resident (the first
+    warm-up step is checked against the cleartext forward); e2e adds the
+    encoding and encryption of the host inputs and the decryption and
+    decoding of the logits to host memory.  Returns the measurements (the
+    rank's own; times are maxima over ranks)."""
     import torch
 
     from helrm_b200 import B200Library, _capi
@@ -708,10 +741,10 @@ def run_b200_helrm(args, dist):
     lib.GenerateSecretKey()
     lib.GenerateRelinearizationKey()
     t0 = time.time()
-    net = H.HELRM(lib, seed=0, emb_ratio=args.bsgs_ratio)
+    net = H.HELRM(lib, seed=0)
     setup_s = time.time() - t0
-    dense = H.dense_inputs(args.batch, 100 + dist.rank)
-    sel = net.selectors(W.zipf_queries(net.vocab, args.batch, seed=200 + dist.rank))
+    dense = H.dense_inputs(batch, 100 + dist.rank)
+    sel = net.selectors(W.zipf_queries(net.vocab, batch, seed=200 + dist.rank))
     d_cts, s_cts = net.encrypt(dense, sel)
     capi = _capi.load()
 
@@ -720,7 +753,6 @@ def run_b200_helrm(args, dist):
             for o in net.forward(d_cts, s_cts):
                 lib.DeleteCiphertext(o)
 
-    # correctness on the first warm-up step
     outs = net.forward(d_cts, s_cts)
     got = net.decrypt(outs)
     for o in outs:
@@ -728,10 +760,7 @@ def run_b200_helrm(args, dist):
     want = net.cleartext(dense, sel)
     exact = net.cleartext(dense, sel, poly=False)
     err_poly = float(np.abs(got - want).max())
-    err_exact = float(np.abs(got - exact).max())
-    approx_exact = float(np.abs(want - exact).max())
-    correct = err_poly <= LOGIT_TOL
-    run(max(0, args.warmup - 1))
+    run(max(0, warmup - 1))
     lib.Synchronize()
     torch.cuda.synchronize()
 
@@ -743,7 +772,7 @@ def run_b200_helrm(args, dist):
     n0 = ctypes.c_uint64(0)
     _capi.check(capi.helrm_GetLaunchCount(ctypes.byref(n0)))
     _capi.check(capi.helrm_TimerStart())
-    run(args.steps)
+    run(steps)
     ms = ctypes.c_double(0)
     _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
     n1 = ctypes.c_uint64(0)
@@ -752,32 +781,37 @@ def run_b200_helrm(args, dist):
     torch.cuda.synchronize()
     dist.barrier()
     t_dev = dist.max(ms.value / 1000.0)
-    value = whole_job_rate(dist.world, args.batch, args.steps, t_dev)
+    res = {"value": whole_job_rate(dist.world, batch, steps, t_dev), "unit": UNIT,
+           "ms_per_step": 1000.0 * t_dev / steps, "steps": steps, "warmup": warmup, "batch_ciphertexts": batch,
+           "gpu_launches": int(n1.value - n0.value), "clocks": clk,
+           "max_abs_err_logits_vs_polynomial_cleartext": err_poly,
+           "max_abs_err_logits_vs_relu_cleartext": float(np.abs(got - exact).max()),
+           "composite_relu_approximation_error": float(np.abs(want - exact).max()),
+           "logit_tol": LOGIT_TOL, "correct": err_poly <= LOGIT_TOL, "setup_s": setup_s, "plan": net.info()}
 
-    # one more step with the per-kernel profiler: breakdown and roofline
-    _capi.check(capi.helrm_ProfilerRange(1))
-    _capi.check(capi.helrm_ProfileEnable(1))
-    lib.Synchronize()
-    _capi.check(capi.helrm_TimerStart())
-    run(1)
-    ms_prof = ctypes.c_double(0)
-    _capi.check(capi.helrm_TimerStop(ctypes.byref(ms_prof)))
-    kern, raw = read_profile(capi, _capi, 1)
-    _capi.check(capi.helrm_ProfileEnable(0))
-    _capi.check(capi.helrm_ProfilerRange(0))
-    dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
-    dms, dby, _, dl = raw[dom]
-    hbm, src = peaks()
-    achieved = dby / (dms * 1e6)
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured"
-                else "fallback 6.65 TB/s", "bytes_per_launch": dby / dl, "avg_launch_ms": dms / dl,
-                "traffic": None, "profiled_ms_per_step": ms_prof.value}
+    if profile:  # one more step with the per-kernel profiler: breakdown and roofline
+        _capi.check(capi.helrm_ProfilerRange(1))
+        _capi.check(capi.helrm_ProfileEnable(1))
+        lib.Synchronize()
+        _capi.check(capi.helrm_TimerStart())
+        run(1)
+        ms_prof = ctypes.c_double(0)
+        _capi.check(capi.helrm_TimerStop(ctypes.byref(ms_prof)))
+        kern, raw = read_profile(capi, _capi, 1)
+        _capi.check(capi.helrm_ProfileEnable(0))
+        _capi.check(capi.helrm_ProfilerRange(0))
+        dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
+        dms, dby, _, dl = raw[dom]
+        hbm, src = peaks()
+        achieved = dby / (dms * 1e6)
+        res["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                           "frac": achieved / hbm,
+                           "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured"
+                           else "fallback 6.65 TB/s", "bytes_per_launch": dby / dl, "avg_launch_ms": dms / dl,
+                           "traffic": None, "profiled_ms_per_step": ms_prof.value}
+        res["kernels"] = kern
 
-    # end to end: host inputs -> encode + encrypt -> forward -> decrypt +
-    # decode -> host logits, every step inside the timed region
-    e2e = None
-    if not args.no_e2e:
+    if e2e:  # host inputs -> encode + encrypt -> forward -> decrypt + decode -> host logits
         def e2e_step():
             dc, sc = net.encrypt(dense, sel)
             outs = net.forward(dc, sc)
@@ -789,46 +823,56 @@ def run_b200_helrm(args, dist):
         dist.barrier()
         lib.Synchronize()
         _capi.check(capi.helrm_TimerStart())
-        for _ in range(args.steps):
+        for _ in range(steps):
             e2e_step()
         ms2 = ctypes.c_double(0)
         _capi.check(capi.helrm_TimerStop(ctypes.byref(ms2)))
         t_e2e = dist.max(ms2.value / 1000.0)
         N = lib.scheme_info()["N"]
-        e2e = {"value": whole_job_rate(dist.world, args.batch, args.steps, t_e2e), "unit": UNIT,
-               "h2d_bytes_per_step": int(dense.size * 8 + sel.size * 8),
-               "d2h_bytes_per_step": int(args.batch * min(4, net.level_out + 1) * N * 8),
-               "ms_per_step": 1000.0 * t_e2e / args.steps,
-               "what": "EncodeBatch of the host features and selectors, Encrypt, the forward, Decrypt, Decode "
-                       "(the decoder reads back the plaintext's first limbs and decodes on the host)"}
-    info = net.info()
-    mem = {"peak_device_mb": lib.GetPeakDeviceMemoryMB(), "key_mb": lib.GetKeyMemoryMB()}
+        res["e2e"] = {"value": whole_job_rate(dist.world, batch, steps, t_e2e), "unit": UNIT,
+                      "h2d_bytes_per_step": int(dense.size * 8 + sel.size * 8),
+                      "d2h_bytes_per_step": int(batch * min(4, net.level_out + 1) * N * 8),
+                      "ms_per_step": 1000.0 * t_e2e / steps,
+                      "what": "EncodeBatch of the host features and selectors, Encrypt, the forward, Decrypt, "
+                              "Decode (the decoder reads back the plaintext's first limbs and decodes on the host)"}
+    res["memory"] = {"peak_device_mb": lib.GetPeakDeviceMemoryMB(), "key_mb": lib.GetKeyMemoryMB()}
     net.close()
     lib.DeleteScheme()
+    return res
+
+
+def helrm_config(args) -> dict:
+    from helrm_b200 import helrm as H
+    from helrm_b200.params import CFG4_DNUM
+    return {"workload": "cfg4: end-to-end HE-LRM forward (BASELINE configs[3])", "logN": 16,
+            "q_limbs_usable": 24, "q_bits": "50 + 23 x 36", "boot_primes": "14 x 60", "special_primes": "6 x 60",
+            "dnum": CFG4_DNUM, "h": 192, "batch_ciphertexts": args.batch, "queries_per_ciphertext": 1,
+            "bottom": list(H.BOTTOM), "top": [432] + list(H.TOP_HIDDEN) + [1], "relu": list(H.SIGN_DEGREES),
+            "bsgs": "32 baby steps per transform (64 above 512 diagonals)",
+            "parallelism": f"dp{args.gpus} (query batch)",
+            "l2": "inputs larger than L2 (tens of GB of diagonals and keys per step)"}
+
+
+def run_b200_helrm(args, dist):
+    """bench.py --mode helrm: the config-4 line."""
+    r = helrm_measure(dist, args.batch, args.steps, args.warmup, profile=True, e2e=not args.no_e2e)
     if dist.rank == 0:
+        cfg = helrm_config(args)
+        cfg["plan"] = r.pop("plan")
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * t_dev / args.steps, "higher_is_better": True,
+            "metric": METRIC, "value": r.pop("value"), "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r.pop("ms_per_step"), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u64",
             "data": "synthetic (seeded Criteo-shaped dense features and Zipf queries; random-init weights)",
-            "config": {"workload": "cfg4: end-to-end HE-LRM forward (BASELINE configs[3])", "logN": 16,
-                       "q_limbs_usable": 24, "q_bits": "50 + 23 x 36", "boot_primes": "14 x 60",
-                       "special_primes": "6 x 60", "dnum": CFG4_DNUM, "h": 192, "batch_ciphertexts": args.batch,
-                       "queries_per_ciphertext": 1, "bottom": list(H.BOTTOM), "top": [432] + list(H.TOP_HIDDEN) + [1],
-                       "relu": list(H.SIGN_DEGREES), "embedding_bsgs_ratio": args.bsgs_ratio,
-                       "parallelism": f"dp{args.gpus} (query batch)", "plan": info,
-                       "l2": "inputs larger than L2 (tens of GB of diagonals and keys per step)"},
-            "roofline": roofline,
+            "config": cfg, "roofline": r.pop("roofline"),
             "cpu_baseline": {"value": None, "unit": UNIT, "cores": 0, "kind": "port",
                              "sample": "not run: one bootstrapped LogN-16 forward on the oracle port takes hours; "
                                        "the config-2 line carries the CPU baseline of the embedding product"},
-            "e2e": e2e, "gpu_launches": int(n1.value - n0.value), "clocks": clk, "kernels": kern,
-            "max_abs_err_logits_vs_polynomial_cleartext": err_poly, "max_abs_err_logits_vs_relu_cleartext": err_exact,
-            "composite_relu_approximation_error": approx_exact, "logit_tol": LOGIT_TOL, "correct": correct,
-            "setup_s": setup_s, "memory": mem,
+            "e2e": r.pop("e2e", None), "gpu_launches": r.pop("gpu_launches"), "clocks": r.pop("clocks"),
         }
+        line.update(r)
         print(json.dumps(line), flush=True)
-    if not correct:
+    if not r["correct"]:
         raise SystemExit("bench: logits out of tolerance")
 
 

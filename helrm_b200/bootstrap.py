@@ -23,24 +23,26 @@ Chen, Chillotti, Song, EUROCRYPT 2019):
   SubSum     log2(N / 2n) rotations by n 2^i add the conjugates of the
              sparse subring: R t_sub with R = N / 2n, so read at scale
              R q0 the n slots hold E(t_sub) / q0;
-  CtS        one dense n x n transform M^-1 / 2B, M the subring's encoding
-             matrix (slot j = sum_k w_k zeta^(k g_j), w_k = t_k + i t_{k+n},
-             g_j = 5^j mod 4n): slots (t_k + i t_{k+n}) / (2 B q0);
-  EvalMod    for the real and the imaginary part (one conjugation, the
-             imaginary unit): u = (x - 1/4) / B in [-1, 1], a Chebyshev
-             approximation of cos(2 pi B u / 2^r), r double angles
+  CtS        one dense 2n x n transform [M^-1; -i M^-1] / 2B, M the
+             subring's encoding matrix (slot j = sum_k w_k zeta^(k g_j),
+             w_k = t_k + i t_{k+n}, g_j = 5^j mod 4n), onto 2n slots; with
+             its conjugate added (one conjugation) the 2n slots hold the
+             real coefficients t_k / (B q0), k < 2n (sparse packing of the
+             real and imaginary parts side by side: 2n <= N / 2);
+  EvalMod    on that one ciphertext: u = (x - 1/4) / B in [-1, 1], a
+             Chebyshev approximation of cos(2 pi B u / 2^r), r double angles
              c <- 2 c^2 - 1 giving sin(2 pi x), then arcsin(s) / 1 on the
              odd Taylor terms (s + s^3/6 + 3 s^5/40) so that the result is
              2 pi (m / q0) up to (2 pi m / q0)^7 terms;
-  StC        one dense transform M / 2 pi back to the coefficient packing,
-             landing at the top level of the usable chain at the default
-             scale.
+  StC        one dense n x 2n transform [M, i M] / 2 pi from the 2n real
+             slots back to the n-slot packing, landing at the top level of
+             the usable chain at the default scale.
 
 Levels: CtS 1, cosine 6 (degree 63), double angles 3, arcsine 3, StC 1 --
 BOOT_LEVELS primes of 60 bits are reserved above the usable chain, as the
 reference's Cheddar setup reserves its boot primes there
 (bindings.py:279-294).  The input must satisfy q0 >= 2^4 scale (the
-message ratio) and slots n <= 4096 (the dense transforms hold n diagonals).
+message ratio) and slots n <= 4096 (CtS holds n diagonals, StC 2n).
 """
 from __future__ import annotations
 
@@ -77,13 +79,15 @@ def encoding_matrix(n: int) -> np.ndarray:
 
 
 def diagonals(A: np.ndarray, slots: int) -> np.ndarray:
-    """Orion's diagonal convention out[i] = sum_l d_l[i] in[(i + l) mod n]
-    for an n x n matrix acting on n-periodic slots, each diagonal repeated
-    over all slots: [n][slots] complex."""
-    n = A.shape[0]
-    i = np.arange(n)
-    d = np.stack([A[i, (i + l) % n] for l in range(n)])
-    return np.tile(d, (1, slots // n))
+    """Orion's diagonal convention out[i] = sum_l d_l[i] in[(i + l) mod S]
+    for an r x c matrix (r, c powers of two) acting on c-periodic slots and
+    giving r-periodic ones: d_l[i] = A[i mod r, (i + l) mod c] for
+    l < c, period max(r, c), repeated over all slots: [c][slots] complex."""
+    r, c = A.shape
+    p = max(r, c)
+    i = np.arange(p)
+    d = np.stack([A[i % r, (i + l) % c] for l in range(c)])
+    return np.tile(d, (1, slots // p))
 
 
 def cos_coeffs(B: float, r: int, degree: int) -> list[float]:
@@ -107,8 +111,8 @@ class BootContext:
         n = int(slots)
         if n < 1 or n & (n - 1) or n > S:
             raise ValueError(f"Bootstrap: slots must be a power of two up to {S}")
-        if n > MAX_SLOTS:
-            raise ValueError(f"Bootstrap: at most {MAX_SLOTS} slots (dense transforms)")
+        if n > MAX_SLOTS or 2 * n > S:
+            raise ValueError(f"Bootstrap: at most {min(MAX_SLOTS, S // 2)} slots (dense transforms over 2n slots)")
         self.n, self.R = n, S // n
         q = lib.GetAllModuliChain()
         self.q = [float(x) for x in q]
@@ -124,7 +128,7 @@ class BootContext:
         # plaintext scale chosen so that the output scale is q[top - 1]
         self.s_u = self.q[self.top - 1]
         s_cts = self.s_u * self.q[self.top] / (self.R * self.q0)
-        self.cts = self._transform(lib, Minv / (2 * self.B), self.top, s_cts)
+        self.cts = self._transform(lib, np.vstack([Minv, -1j * Minv]) / (2 * self.B), self.top, s_cts)
         self.poly_cos = lib.GenerateChebyshev(cos_coeffs(self.B, DOUBLE_ANGLES, COS_DEGREE))
         self.poly_asin = lib.GenerateMonomial(list(ASIN_COEFFS))  # ascending, as the backend takes them
         # scales through EvalMod (deterministic: targets at the primes)
@@ -143,7 +147,7 @@ class BootContext:
         # that an input at the default scale comes out at the default scale
         d = float(lib._default_scale)
         self.s_stc = d * self.q0 * self.q[self.lvl_stc] / (d * self.s_asin)
-        self.stc = self._transform(lib, M / (2 * math.pi), self.lvl_stc, self.s_stc)
+        self.stc = self._transform(lib, np.hstack([M, 1j * M]) / (2 * math.pi), self.lvl_stc, self.s_stc)
         # keys: the SubSum rotations, both transforms', the conjugation
         self.subsum_steps = []
         step = n
@@ -157,11 +161,20 @@ class BootContext:
                 lib.GenerateLinearTransformRotationKey(k)
 
     @staticmethod
+    def transform_ratio(ndiag: int) -> float:
+        """BSGS ratio giving 32 baby steps (64 above 512 diagonals): the
+        fused MAC's full-chunk shapes, the fastest splits measured on the
+        LogN-16 transforms (bs 23 or 46 ran up to 1.8x slower)."""
+        bs = 64 if ndiag > 512 else 32
+        return bs * bs / float(ndiag)
+
+    @staticmethod
     def _transform(lib, A, level, scale):
         S = lib._slots
         d = diagonals(A, S)
-        inter = np.stack([d.real, d.imag], axis=-1).reshape(A.shape[0], 2 * S)
-        return lib.GenerateLinearTransformEx(list(range(A.shape[0])), inter, S, level, 2.0, True, scale)
+        inter = np.stack([d.real, d.imag], axis=-1).reshape(A.shape[1], 2 * S)
+        return lib.GenerateLinearTransformEx(list(range(A.shape[1])), inter, S, level,
+                                             BootContext.transform_ratio(A.shape[1]), True, scale)
 
 
 def bootstrap(lib, ctx: BootContext, ct: int) -> int:
@@ -200,19 +213,15 @@ def bootstrap_batch(lib, ctx: BootContext, cts) -> list[int]:
     for t in ts:
         lib.DeleteCiphertext(t)
     lib.RescaleBatch(ws)
-    # u_re = w + conj(w) - 1/4B, u_im = i (conj(w) - w) - 1/4B
+    # u = w + conj(w) - 1/4B: the 2n real coefficients side by side
     us = []
     for w in ws:
         cj = lib.ConjugateNew(w)
-        u_re = lib.AddCiphertextNew(w, cj)
-        u_im = lib.SubCiphertextNew(cj, w)
-        lib.MulImaginaryUnit(u_im)
+        lib.AddCiphertext(w, cj)
         lib.DeleteCiphertext(cj)
-        lib.DeleteCiphertext(w)
-        for u in (u_re, u_im):
-            lib.SetCiphertextScale(u, ctx.s_u)
-            lib.AddScalar(u, -1.0 / (4.0 * ctx.B))
-        us += [u_re, u_im]
+        lib.SetCiphertextScale(w, ctx.s_u)
+        lib.AddScalar(w, -1.0 / (4.0 * ctx.B))
+        us.append(w)
     ys = lib.EvaluatePolynomialBatch(us, ctx.poly_cos, ctx.s_cos)
     for u in us:
         lib.DeleteCiphertext(u)
@@ -228,15 +237,9 @@ def bootstrap_batch(lib, ctx: BootContext, cts) -> list[int]:
     zs = lib.EvaluatePolynomialBatch(ys, ctx.poly_asin, ctx.s_asin)
     for y in ys:
         lib.DeleteCiphertext(y)
-    pre = []
-    for re, im in zip(zs[0::2], zs[1::2]):
-        lib.MulImaginaryUnit(im)
-        lib.AddCiphertext(re, im)
-        lib.DeleteCiphertext(im)
-        pre.append(re)
-    outs = lib.EvaluateLinearTransformBatch(ctx.stc, pre)
-    for y in pre:
-        lib.DeleteCiphertext(y)
+    outs = lib.EvaluateLinearTransformBatch(ctx.stc, zs)
+    for z in zs:
+        lib.DeleteCiphertext(z)
     lib.RescaleBatch(outs)
     # the values: E(m) / q0 at scale s_asin s_stc / q_stc, i.e. the input's
     # slots at s_asin s_stc scale_in / (q_stc q0)

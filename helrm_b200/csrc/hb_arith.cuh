@@ -219,6 +219,27 @@ __device__ __forceinline__ u64 splitw_reduce(const SplitW &s, const PrimeConst &
     return (long long)r < 0 ? r + pc.q : r;
 }
 
+// The same reduction for sums of products of two factors below 2^60 (basis
+// conversion over primes of up to 60 bits): S0 < 2^64, S1 < 2^64 - 2^34,
+// S2 < 2^64 - 2^35, 2^26 <= q < 2^62.  With hi = S2 + (S1 >> 30) < 2^64 split
+// as hl + hh 2^30 (hh < 2^34), W = lo + hl (2^60 mod q) + hh (2^90 mod q) is
+// congruent to the sum and below 2^60 + 2^35 q; its double image is within
+// q 2^-17 of it, so Q = round(W / q) is within 0.5 + 2^-16 of W / q and
+// W - Q q (modulo 2^64) lies in (-0.51 q, 0.51 q).
+__device__ __forceinline__ u64 splitw_reduce_wide(const SplitW &s, const PrimeConst &pc) {
+    const u64 s1 = s.s1 + (s.s0 >> 30);
+    const unsigned a0 = (unsigned)(s.s0 & HB_SPLIT_MASK), a1 = (unsigned)(s1 & HB_SPLIT_MASK);
+    const u64 hi = s.s2 + (s1 >> 30);
+    const unsigned hl = (unsigned)(hi & HB_SPLIT_MASK);
+    const u64 hh = hi >> 30;
+    const u64 W = (u64)a0 + ((u64)a1 << 30) + (u64)hl * pc.c60 + hh * pc.c90;
+    const double lod = __fma_rn(u32_to_double(a1), 1073741824.0, u32_to_double(a0));
+    const double wd = __fma_rn(__ull2double_rn(hh), pc.c90d, __fma_rn(u32_to_double(hl), pc.c60d, lod));
+    const u64 Q = (u64)__double_as_longlong(__fma_rn(wd, pc.qinv, 4503599627370496.0)) & 0x000FFFFFFFFFFFFFull;
+    const u64 r = W - Q * pc.q;
+    return (long long)r < 0 ? r + pc.q : r;
+}
+
 // bit reversal of the low `bits` bits
 __device__ __forceinline__ unsigned brev_bits(unsigned x, int bits) {
     return __brev(x) >> (32 - bits);

@@ -806,8 +806,13 @@ public:
             size_t o_phinv = put(phinv), o_phinvp = put(phinvp), o_phat = put(phat), o_pinv = put(pinv),
                    o_pinvp = put(pinvp), o_qlinv = put(qlinv), o_qlinvp = put(qlinvp), o_phat_s = put(packed(phat)),
                    o_pneg_s = put(packed(pneg));
-            bool small_main = true;  // split-30 basis conversion needs main primes below 2^40
+            // split-30 basis conversion: every prime below 2^60, or main
+            // primes below 2^40 with special primes below 2^61
+            bool below60 = true, small_main = true, special61 = true;
+            for (int i = 0; i < P; i++) below60 = below60 && primes[i] < (1ull << 60);
             for (int i = 0; i < L; i++) small_main = small_main && primes[i] < (1ull << 40);
+            for (int i = L; i < P; i++) special61 = special61 && primes[i] < (1ull << 61);
+            const bool split_ok = below60 || (small_main && special61);
             LevelTabs &T = lv[nq];
             T.blob = alloc(blob.size());
             cuda_check(cudaMemcpyAsync(T.blob, blob.data(), blob.size() * 8, cudaMemcpyHostToDevice, stream),
@@ -821,11 +826,11 @@ public:
             T.mu.qjneg_s = T.blob + o_qjneg_s;
             T.mu.qhat_d = reinterpret_cast<const double2 *>(T.blob + o_qhat_d);
             T.mu.qjneg_d = reinterpret_cast<const double *>(T.blob + o_qjneg_d);
-            T.mu.split = small_main ? 1 : 0;
+            T.mu.split = split_ok ? 1 : 0;
             T.md.pneg = T.blob + o_pneg;
             T.md.phat_s = T.blob + o_phat_s;
             T.md.pneg_s = T.blob + o_pneg_s;
-            T.md.split = small_main ? 1 : 0;
+            T.md.split = split_ok ? 1 : 0;
             T.md.phinv = T.blob + o_phinv;
             T.md.phinvp = T.blob + o_phinvp;
             T.md.phat = T.blob + o_phat;

@@ -1600,14 +1600,15 @@ __global__ void k_modup_bconv(u64 *__restrict__ D, const u64 *__restrict__ X, co
     }
 }
 
-// The same conversion for main primes below 2^40 (the digit values y_m are
-// then below 2^40).  q-row targets on the FP64 pipe: exact centred products
-// y_m * qhat_m mod q_e (|t| <= 0.502 q each) and the lift term
-// nneg * (-Q_j mod q_e) < 8 q, summed exactly as doubles (|S| < 13 q), one
-// reduction per output.  Special-prime targets in split-30 products (table
-// values below 2^61).  NA = digit size, a compile-time constant;
-// blockIdx.y + j0 is the digit.  The digit's tables are staged in shared
-// memory.
+// The same conversion for primes below 2^60.  q-row targets below 2^40 of a
+// digit whose primes are all below 2^40 (digit values y_m below 2^40) on
+// the FP64 pipe: exact centred products y_m * qhat_m mod q_e (|t| <= 0.502 q
+// each) and the lift term nneg * (-Q_j mod q_e) < 8 q, summed exactly as
+// doubles (|S| < 13 q), one reduction per output.  Every other target
+// (special primes, wider main primes, or any target of a digit holding a
+// wider prime) in split-30 products of two factors below 2^60.  NA = digit
+// size, a compile-time constant; blockIdx.y + j0 is the digit.  The digit's
+// tables are staged in shared memory.
 template <int NA>
 __global__ void __launch_bounds__(256)
     k_modup_bconv_split(u64 *__restrict__ D, const u64 *__restrict__ X, const u64 *__restrict__ c1ntt, int nq, int K,
@@ -1651,6 +1652,9 @@ __global__ void __launch_bounds__(256)
         }
     }
     const double nn0 = u32_to_double(nneg[0]), nn1 = u32_to_double(nneg[1]);
+    bool dsmall = true;  // every prime of the digit below 2^40 (block-uniform)
+#pragma unroll
+    for (int m = 0; m < NA; m++) dsmall = dsmall && c_pc[lo + m].q < (1ull << 40);
     // q-row targets; the digit's own rows are copies of its input
     for (int e = 0; e < nq; e++) {
         u64 *de = Db + (size_t)e * N + n0;
@@ -1661,6 +1665,25 @@ __global__ void __launch_bounds__(256)
             continue;
         }
         const PrimeConst &pc = c_pc[e];
+        if (!dsmall || pc.q >= (1ull << 40)) {
+            SplitW acc0 = {0, 0, 0}, acc1 = {0, 0, 0};
+#pragma unroll
+            for (int m = 0; m < NA; m++) {
+                const u64 tv = st[m * ne + e];
+                splitw_mac(acc0, y[0][m], tv);
+                splitw_mac(acc1, y[1][m], tv);
+                if ((m & 3) == 3 && m + 1 < NA) {
+                    splitw_normalize(acc0);
+                    splitw_normalize(acc1);
+                }
+            }
+            const u64 tn = st[NA * ne + e];
+            splitw_mac_small(acc0, nneg[0], tn);
+            splitw_mac_small(acc1, nneg[1], tn);
+            de[0] = splitw_reduce_wide(acc0, pc);
+            de[256] = splitw_reduce_wide(acc1, pc);
+            continue;
+        }
         const double qd = u64_to_d(pc.q);
         const double tn = sd[NA * ne + e].x;
         double s0 = __dmul_rn(nn0, tn), s1 = __dmul_rn(nn1, tn);
@@ -1673,7 +1696,7 @@ __global__ void __launch_bounds__(256)
         de[0] = d_mod_to_u64(s0, qd, pc.qinv);
         de[256] = d_mod_to_u64(s1, qd, pc.qinv);
     }
-    // special-prime targets: split-30 products (table values below 2^61)
+    // special-prime targets: split-30 products
     for (int e = nq; e < ne; e++) {
         const PrimeConst &pc = c_pc[L + (e - nq)];
         SplitW acc0 = {0, 0, 0}, acc1 = {0, 0, 0};
@@ -1691,8 +1714,8 @@ __global__ void __launch_bounds__(256)
         splitw_mac_small(acc0, nneg[0], tn);
         splitw_mac_small(acc1, nneg[1], tn);
         u64 *de = Db + (size_t)e * N + n0;
-        de[0] = splitw_reduce(acc0, pc);
-        de[256] = splitw_reduce(acc1, pc);
+        de[0] = splitw_reduce_wide(acc0, pc);
+        de[256] = splitw_reduce_wide(acc1, pc);
     }
 }
 
@@ -1771,9 +1794,9 @@ __global__ void k_moddown_bconv(u64 *__restrict__ Z, const u64 *__restrict__ Y, 
         Zb[(size_t)i * N + n] = reduce128(acc, c_pc[i]);
     }
 }
-// The same conversion with split-30 products (every main prime below 2^40:
-// table entries below 2^40, special-prime values below 2^61).  KK = number
-// of special primes; the phat and pneg rows are staged in shared memory.
+// The same conversion with split-30 products (every prime below 2^60: table
+// entries and special-prime values below 2^60).  KK = number of special
+// primes; the phat and pneg rows are staged in shared memory.
 template <int KK>
 __global__ void __launch_bounds__(256)
     k_moddown_bconv_split(u64 *__restrict__ Z, const u64 *__restrict__ Y, int nq, int L, ModDownTab tab, int logN,
@@ -1817,8 +1840,8 @@ __global__ void __launch_bounds__(256)
         splitw_mac_small(a0, nneg[0], tn);
         splitw_mac_small(a1, nneg[1], tn);
         const PrimeConst &pc = c_pc[i];
-        Zb[(size_t)i * N + n0] = splitw_reduce(a0, pc);
-        Zb[(size_t)i * N + n0 + 256] = splitw_reduce(a1, pc);
+        Zb[(size_t)i * N + n0] = splitw_reduce_wide(a0, pc);
+        Zb[(size_t)i * N + n0 + 256] = splitw_reduce_wide(a1, pc);
     }
 }
 

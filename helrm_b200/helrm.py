@@ -117,12 +117,14 @@ class HELRM:
 
     vocab: the tables' vocabulary sizes (default: config 2's 26);
     base: the digit base of the compressed one-hot selectors;
-    ratio / emb_ratio: BSGS ratios of the MLP layers / the embedding;
+    ratio / emb_ratio: BSGS ratios of the MLP layers / the embedding (None:
+    32 baby steps, 64 above 512 diagonals);
     boot_chunk: ciphertexts per bootstrap batch (bounds the working set);
     build=False stops after the fit and the level plan."""
 
     def __init__(self, lib, *, vocab=None, base: int = 64, bottom=BOTTOM, top_hidden=TOP_HIDDEN, seed: int = 0,
-                 fit_queries: int = 256, ratio: float = 2.0, emb_ratio: float = 8.0, boot_chunk: int = 16,
+                 fit_queries: int = 256, ratio: float | None = None, emb_ratio: float | None = None,
+                 boot_chunk: int = 16,
                  build: bool = True):
         self.lib = lib
         info = lib.scheme_info()

@@ -35,9 +35,10 @@ class LinearLayer:
     one input vector in slots 0..in-1 (any period-replicated copies beyond
     are ignored: the diagonals read only the first copy).  narrow retags
     the folded output to its period; exact encodes the diagonals at the
-    level's prime instead of the default scale."""
+    level's prime instead of the default scale; ratio None picks the BSGS
+    split with 32 baby steps (64 above 512 diagonals)."""
 
-    def __init__(self, lib, weight: np.ndarray, bias, level: int, last: bool = False, ratio: float = 2.0,
+    def __init__(self, lib, weight: np.ndarray, bias, level: int, last: bool = False, ratio: float | None = 2.0,
                  narrow: bool = True, exact: bool = False):
         self.lib = lib
         info = lib.scheme_info()
@@ -53,6 +54,9 @@ class LinearLayer:
         self.diags = d[(0, 0)]
         self.ks = sorted(self.diags)
         data = np.concatenate([self.diags[k].astype(np.float64) for k in self.ks])
+        if ratio is None:  # 32 baby steps (64 above 512 diagonals): the fused MAC's full chunks
+            bs = 64 if len(self.ks) > 512 else 32
+            ratio = bs * bs / float(len(self.ks))
         if exact:  # diagonals at q_level: the rescaled output keeps the input's scale exactly
             q = float(lib.GetModuliChain()[level])
             self.lt = lib.GenerateLinearTransformEx(self.ks, data, self.slots, level, ratio, False, q)

@@ -32,11 +32,6 @@ def add(o, a, b):
     return ((a[:, :nq].astype(object) + b[:, :nq].astype(object)) % _qs(o, nq)).astype(np.uint64)
 
 
-def sub(o, a, b):
-    nq = min(a.shape[1], b.shape[1])
-    return ((a[:, :nq].astype(object) - b[:, :nq].astype(object)) % _qs(o, nq)).astype(np.uint64)
-
-
 def add_scalar(o, ct, v, scale):
     """c0 + round(v * scale) with the library's rounding: the product in
     80-bit long double, then half away from zero"""
@@ -48,20 +43,6 @@ def add_scalar(o, ct, v, scale):
     for i in range(ct.shape[1]):
         out[0, i] = (out[0, i] + k) % o.primes[i]
     return out.astype(np.uint64)
-
-
-def iunit_rows(o, nq):
-    rows = []
-    for i in range(nq):
-        m = np.zeros(o.N, dtype=np.uint64)
-        m[o.N // 2] = 1
-        rows.append(o.ntt(i, m))
-    return np.array(rows, dtype=object)
-
-
-def mul_i(o, ct):
-    nq = ct.shape[1]
-    return ((ct.astype(object) * iunit_rows(o, nq)[None]) % _qs(o, nq)).astype(np.uint64)
 
 
 def mod_raise(o, ct, nq_all):
@@ -80,7 +61,7 @@ def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts, replicate=False
     (dict with n, R, B, q0, s_u, s_cos, s_asin, subsum_steps, cts_bs, stc_bs,
     cos_coeffs, asin_coeffs, top); keys: {galois: switching key};
     cts_pts / stc_pts: the transforms' extended-basis plaintexts, diagonal k
-    at index k.  replicate: the input holds its values in slots [0, n) and
+    at index k (n of CtS, 2n of StC).  replicate: the input holds its values in slots [0, n) and
     zeros elsewhere and is first tiled over the subring by rotations at
     level 0.  Returns (ciphertext, output scale)."""
     n, S = ctx["n"], o.N // 2
@@ -94,23 +75,19 @@ def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts, replicate=False
     if replicate:
         x = fold(x)
     t = fold(mod_raise(o, x, nq_all))
-    ks = list(range(n))
-    w = o.rescale(o.bsgs_lt(t, ks, cts_pts, ctx["cts_bs"], keys))
+    # CtS onto 2n slots (n diagonals), plus its conjugate: the real coefficients
+    w = o.rescale(o.bsgs_lt(t, list(range(n)), cts_pts, ctx["cts_bs"], keys))
     gc = 2 * o.N - 1
     cj = o.rotate(w, keys[gc], gc)
-    u_re = add_scalar(o, add(o, w, cj), -1.0 / (4.0 * ctx["B"]), ctx["s_u"])
-    u_im = add_scalar(o, mul_i(o, sub(o, cj, w)), -1.0 / (4.0 * ctx["B"]), ctx["s_u"])
-    ys = []
-    for u in (u_re, u_im):
-        y, _ = poly.evaluate(o, rlk, u, ctx["s_u"], ctx["cos_coeffs"], ctx["s_cos"], chebyshev=True)
-        s = ctx["s_cos"]
-        for _ in range(ctx["double_angles"]):
-            sq = o.rescale(o.relinearize(o.tensor(y, y), rlk))
-            s = s * s / float(o.primes[y.shape[1] - 1])
-            y = add_scalar(o, add(o, sq, sq), -1.0, s)
-        z, _ = poly.evaluate(o, rlk, y, s, ctx["asin_coeffs"], ctx["s_asin"], chebyshev=False)
-        ys.append(z)
-    y = add(o, ys[0], mul_i(o, ys[1]))
-    out = o.rescale(o.bsgs_lt(y, ks, stc_pts, ctx["stc_bs"], keys))
+    u = add_scalar(o, add(o, w, cj), -1.0 / (4.0 * ctx["B"]), ctx["s_u"])
+    y, _ = poly.evaluate(o, rlk, u, ctx["s_u"], ctx["cos_coeffs"], ctx["s_cos"], chebyshev=True)
+    s = ctx["s_cos"]
+    for _ in range(ctx["double_angles"]):
+        sq = o.rescale(o.relinearize(o.tensor(y, y), rlk))
+        s = s * s / float(o.primes[y.shape[1] - 1])
+        y = add_scalar(o, add(o, sq, sq), -1.0, s)
+    y, _ = poly.evaluate(o, rlk, y, s, ctx["asin_coeffs"], ctx["s_asin"], chebyshev=False)
+    # StC from the 2n real slots (2n diagonals)
+    out = o.rescale(o.bsgs_lt(y, list(range(2 * n)), stc_pts, ctx["stc_bs"], keys))
     q_stc = float(o.primes[y.shape[1] - 1])
     return out, ctx["s_asin"] * ctx["s_stc"] * scale_in / (q_stc * ctx["q0"])

@@ -47,7 +47,7 @@ def test_overflow_bound():
 def _transform_pts(o, A, level, scale, bs):
     S = o.N // 2
     d = BT.diagonals(A, S)
-    return [o.encode(W.preroll(d[k], k // bs, bs), level + 1, scale, ext=True) for k in range(A.shape[0])]
+    return [o.encode(W.preroll(d[k], k // bs, bs), level + 1, scale, ext=True) for k in range(A.shape[1])]
 
 
 @pytest.mark.parametrize("padded", [False, True])
@@ -61,9 +61,12 @@ def test_oracle_bootstrap_precision(scheme, padded):
     B = BT.overflow_bound(64) + 1
     s_u = q[top - 1]
     s_cts = s_u * q[top] / (R * q[0])
-    bs = W.bsgs_plan(list(range(n)), 2.0, S)["stride"]
+    r1, r2 = BT.BootContext.transform_ratio(n), BT.BootContext.transform_ratio(2 * n)
+    bs = W.bsgs_plan(list(range(n)), r1, S)["stride"]
+    bs2 = W.bsgs_plan(list(range(2 * n)), r2, S)["stride"]
     M = BT.encoding_matrix(n)
-    cts_pts = _transform_pts(o, np.linalg.inv(M) / (2 * B), top, s_cts, bs)
+    Minv = np.linalg.inv(M)
+    cts_pts = _transform_pts(o, np.vstack([Minv, -1j * Minv]) / (2 * B), top, s_cts, bs)
     lvl = top - 7
     s_cos = q[lvl]
     s = s_cos
@@ -74,18 +77,20 @@ def test_oracle_bootstrap_precision(scheme, padded):
     lvl_stc = lvl - 3
     assert lvl_stc == usable_top + 1
     s_stc = q[0] * q[lvl_stc] / s_asin
-    stc_pts = _transform_pts(o, M / (2 * math.pi), lvl_stc, s_stc, bs)
-    plan = W.bsgs_plan(list(range(n)), 2.0, S)
+    stc_pts = _transform_pts(o, np.hstack([M, 1j * M]) / (2 * math.pi), lvl_stc, s_stc, bs2)
+    plan = W.bsgs_plan(list(range(n)), r1, S)
+    plan2 = W.bsgs_plan(list(range(2 * n)), r2, S)
     steps = []
     step = n
     while step < S:
         steps.append(step)
         step *= 2
-    gal = {o.galois(k) for k in steps} | {o.galois(d) for d in plan["rotation_keys"]} | {2 * o.N - 1}
+    gal = ({o.galois(k) for k in steps} | {o.galois(d) for d in plan["rotation_keys"] + plan2["rotation_keys"]}
+           | {2 * o.N - 1})
     keys = {g: o.rotation_key(sk, 5, g) for g in gal}
     rlk = o.relin_key(sk, 5)
     ctx = {"n": n, "R": R, "B": B, "q0": q[0], "s_u": s_u, "s_cos": s_cos, "s_asin": s_asin, "s_stc": s_stc,
-           "subsum_steps": steps, "cts_bs": bs, "stc_bs": bs, "top": top, "double_angles": BT.DOUBLE_ANGLES,
+           "subsum_steps": steps, "cts_bs": bs, "stc_bs": bs2, "top": top, "double_angles": BT.DOUBLE_ANGLES,
            "cos_coeffs": BT.cos_coeffs(B, BT.DOUBLE_ANGLES, BT.COS_DEGREE), "asin_coeffs": BT.ASIN_COEFFS}
     rng = np.random.default_rng(4)
     z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.7

@@ -114,7 +114,7 @@ def test_bootstrap_residues_match_oracle(pair, padded):
          "cts_bs": info_c["bs"], "stc_bs": info_s["bs"], "top": ctx.top, "double_angles": BT.DOUBLE_ANGLES,
          "cos_coeffs": BT.cos_coeffs(ctx.B, BT.DOUBLE_ANGLES, BT.COS_DEGREE), "asin_coeffs": BT.ASIN_COEFFS}
     cts_pts = [lib.GetLinearTransformPlaintext(ctx.cts, k) for k in range(n)]
-    stc_pts = [lib.GetLinearTransformPlaintext(ctx.stc, k) for k in range(n)]
+    stc_pts = [lib.GetLinearTransformPlaintext(ctx.stc, k) for k in range(2 * n)]
     want, s_out = OB.bootstrap(o, pair.ct_data(ct), pair.scale, c, keys, pair.key(0), cts_pts, stc_pts,
                                replicate=padded)
     assert np.array_equal(pair.ct_data(out), want)
