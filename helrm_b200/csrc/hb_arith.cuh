@@ -198,8 +198,8 @@ __device__ __forceinline__ void splitw_normalize(SplitW &acc) {
     acc.s2 += acc.s1 >> 30;
     acc.s1 &= HB_SPLIT_MASK;
 }
-// (S0 + S1 2^30 + S2 2^60) mod q for S0 < 2^64, S1 < 2^64 - 2^34, S2 < 2^63
-// and 2^26 <= q < 2^62.  Carries give lo + hi 2^60 with lo = a0 + a1 2^30
+// (S0 + S1 2^30 + S2 2^60) mod q for S0 < 2^64, S1 < 2^64 - 2^34,
+// S2 < 2^61 - 2^34 (so that hh below fits 31 bits) and 2^26 <= q < 2^62.  Carries give lo + hi 2^60 with lo = a0 + a1 2^30
 // (a0, a1 < 2^30); hi = hl + hh 2^30, so the value is congruent to
 // W = lo + hl (2^60 mod q) + hh (2^90 mod q) < 2^60 + 2^31 q.  W is formed
 // modulo 2^64 on the integer pipe and, approximately (error below

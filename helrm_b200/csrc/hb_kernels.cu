@@ -1680,8 +1680,8 @@ __global__ void __launch_bounds__(256)
             const u64 tn = st[NA * ne + e];
             splitw_mac_small(acc0, nneg[0], tn);
             splitw_mac_small(acc1, nneg[1], tn);
-            de[0] = splitw_reduce_wide(acc0, pc);
-            de[256] = splitw_reduce_wide(acc1, pc);
+            de[0] = dsmall ? splitw_reduce(acc0, pc) : splitw_reduce_wide(acc0, pc);
+            de[256] = dsmall ? splitw_reduce(acc1, pc) : splitw_reduce_wide(acc1, pc);
             continue;
         }
         const double qd = u64_to_d(pc.q);
@@ -1714,8 +1714,8 @@ __global__ void __launch_bounds__(256)
         splitw_mac_small(acc0, nneg[0], tn);
         splitw_mac_small(acc1, nneg[1], tn);
         u64 *de = Db + (size_t)e * N + n0;
-        de[0] = splitw_reduce_wide(acc0, pc);
-        de[256] = splitw_reduce_wide(acc1, pc);
+        de[0] = dsmall ? splitw_reduce(acc0, pc) : splitw_reduce_wide(acc0, pc);
+        de[256] = dsmall ? splitw_reduce(acc1, pc) : splitw_reduce_wide(acc1, pc);
     }
 }
 
@@ -1840,8 +1840,11 @@ __global__ void __launch_bounds__(256)
         splitw_mac_small(a0, nneg[0], tn);
         splitw_mac_small(a1, nneg[1], tn);
         const PrimeConst &pc = c_pc[i];
-        Zb[(size_t)i * N + n0] = splitw_reduce_wide(a0, pc);
-        Zb[(size_t)i * N + n0 + 256] = splitw_reduce_wide(a1, pc);
+        // table entries below 2^40 keep every partial sum in the narrow
+        // reduction's range
+        const bool narrow = pc.q < (1ull << 40);
+        Zb[(size_t)i * N + n0] = narrow ? splitw_reduce(a0, pc) : splitw_reduce_wide(a0, pc);
+        Zb[(size_t)i * N + n0 + 256] = narrow ? splitw_reduce(a1, pc) : splitw_reduce_wide(a1, pc);
     }
 }
 
