@@ -76,8 +76,12 @@ __host__ __device__ inline size_t bsgs_smem_words(int beta, int pair = 1, bool f
 // gathers for a tile are therefore one contiguous 128-byte segment per
 // digit row, fetched with asynchronous copies one batch item ahead of the
 // arithmetic (double buffer); the in-tile permutation is a table built once.
+// Two blocks per SM for the split-row kernels of four digits and the
+// generic one; the fixed-shape kernels over mixed rows (and of five to
+// seven digits) hold one block per SM and take the registers their threads
+// need (at two blocks they spill).
 template <int NBF, int BETA, int ROWS, int PAIR = 1>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, ((BETA >= 5 || (ROWS == 0 && BETA != 0)) ? 1 : 2))
     k_bsgs_mac(u64 *__restrict__ inner, const u64 *__restrict__ ct, const u64 *__restrict__ D, BsgsChunk ch, int nq,
                int K, int L, int beta_rt, int keyP, int pt_nq, const u64 *__restrict__ pmod_q, int logN, int nbatch, int e0,
                size_t ct_stride, size_t d_stride, size_t inner_stride) {

@@ -826,7 +826,7 @@ public:
             T.mu.qjneg_s = T.blob + o_qjneg_s;
             T.mu.qhat_d = reinterpret_cast<const double2 *>(T.blob + o_qhat_d);
             T.mu.qjneg_d = reinterpret_cast<const double *>(T.blob + o_qjneg_d);
-            T.mu.split = split_ok ? 1 : 0;
+            T.mu.split = small_main && special61 ? 1 : split_ok ? 2 : 0;  // 2: some main prime of 2^40 or more
             T.md.pneg = T.blob + o_pneg;
             T.md.phat_s = T.blob + o_phat_s;
             T.md.pneg_s = T.blob + o_pneg_s;

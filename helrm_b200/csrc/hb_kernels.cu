@@ -1608,8 +1608,10 @@ __global__ void k_modup_bconv(u64 *__restrict__ D, const u64 *__restrict__ X, co
 // (special primes, wider main primes, or any target of a digit holding a
 // wider prime) in split-30 products of two factors below 2^60.  NA = digit
 // size, a compile-time constant; blockIdx.y + j0 is the digit.  The digit's
-// tables are staged in shared memory.
-template <int NA>
+// tables are staged in shared memory.  WIDE = false: every main prime below
+// 2^40 (the digits small, every q-row target on the FP64 pipe; the branch
+// for the other targets compiled out).
+template <int NA, bool WIDE>
 __global__ void __launch_bounds__(256)
     k_modup_bconv_split(u64 *__restrict__ D, const u64 *__restrict__ X, const u64 *__restrict__ c1ntt, int nq, int K,
                         int L, int alpha, int j0, ModUpTab tab, int logN, size_t in_stride, size_t out_stride,
@@ -1653,8 +1655,10 @@ __global__ void __launch_bounds__(256)
     }
     const double nn0 = u32_to_double(nneg[0]), nn1 = u32_to_double(nneg[1]);
     bool dsmall = true;  // every prime of the digit below 2^40 (block-uniform)
+    if (WIDE) {
 #pragma unroll
-    for (int m = 0; m < NA; m++) dsmall = dsmall && c_pc[lo + m].q < (1ull << 40);
+        for (int m = 0; m < NA; m++) dsmall = dsmall && c_pc[lo + m].q < (1ull << 40);
+    }
     // q-row targets; the digit's own rows are copies of its input
     for (int e = 0; e < nq; e++) {
         u64 *de = Db + (size_t)e * N + n0;
@@ -1665,7 +1669,7 @@ __global__ void __launch_bounds__(256)
             continue;
         }
         const PrimeConst &pc = c_pc[e];
-        if (!dsmall || pc.q >= (1ull << 40)) {
+        if (WIDE && (!dsmall || pc.q >= (1ull << 40))) {
             SplitW acc0 = {0, 0, 0}, acc1 = {0, 0, 0};
 #pragma unroll
             for (int m = 0; m < NA; m++) {
@@ -1724,7 +1728,12 @@ static void modup_split_launch(u64 *D, const u64 *X, const u64 *c1ntt, int nq, i
                                int ndig, const ModUpTab &tab, int logN, int nbatch, size_t in_stride,
                                size_t out_stride, size_t c1_stride, cudaStream_t s) {
     dim3 grid(((1 << logN) + 511) / 512, ndig, nbatch);  // two coefficients per thread
-    k_modup_bconv_split<NA><<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, j0, tab, logN, in_stride, out_stride,
+    if (tab.split == 2) {
+        k_modup_bconv_split<NA, true><<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, j0, tab, logN, in_stride,
+                                                           out_stride, c1_stride);
+        return;
+    }
+    k_modup_bconv_split<NA, false><<<grid, 256, 0, s>>>(D, X, c1ntt, nq, K, L, alpha, j0, tab, logN, in_stride, out_stride,
                                                   c1_stride);
 }
 static void modup_split_dispatch(int na, u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha,
@@ -2301,6 +2310,12 @@ static void bsgs_mac_attributes() {
     cudaFuncSetAttribute(k_bsgs_mac<0, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 3, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 5, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 6, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(k_bsgs_mac<HB_BCH, 7, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     done = true;
 }
 
@@ -2312,7 +2327,11 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
     const bool full = ch.nbabies == HB_BCH;
     // chunks of at most half the giant slots: two batch items per iteration
     const bool pair = split && full && ch.gcount <= HB_GCH / 2 && nbatch > 1;
-    const size_t smem = bsgs_smem_words(beta, pair ? 2 : 1, split && full) * 8;
+    // full chunks of 2 to 7 digits over mixed rows (primes on both sides of
+    // 2^40, e.g. a 50-bit q0 or 60-bit bootstrapping primes): the fixed-shape
+    // kernel with the product form chosen per row
+    const bool fixed_mixed = !split && full && beta >= 2 && beta <= 7;
+    const size_t smem = bsgs_smem_words(beta, pair ? 2 : 1, (split && full) || fixed_mixed) * 8;
     if (smem > 227 * 1024 || beta > HB_MAX_BETA)
         throw std::invalid_argument("bsgs: too many digits for the shared-memory key tile");
     bsgs_mac_attributes();
@@ -2342,6 +2361,13 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
             HB_BSGS_LAUNCH(0, 4, 1, 1, 0, nq);
             if (K) HB_BSGS_LAUNCH(0, 4, 2, 1, nq, K);
         }
+    } else if (fixed_mixed) {
+        if (beta == 2) HB_BSGS_LAUNCH(HB_BCH, 2, 0, 1, 0, nq + K);
+        else if (beta == 3) HB_BSGS_LAUNCH(HB_BCH, 3, 0, 1, 0, nq + K);
+        else if (beta == 4) HB_BSGS_LAUNCH(HB_BCH, 4, 0, 1, 0, nq + K);
+        else if (beta == 5) HB_BSGS_LAUNCH(HB_BCH, 5, 0, 1, 0, nq + K);
+        else if (beta == 6) HB_BSGS_LAUNCH(HB_BCH, 6, 0, 1, 0, nq + K);
+        else HB_BSGS_LAUNCH(HB_BCH, 7, 0, 1, 0, nq + K);
     } else {
         if (full) HB_BSGS_LAUNCH(HB_BCH, 0, 0, 1, 0, nq + K);
         else HB_BSGS_LAUNCH(0, 0, 0, 1, 0, nq + K);

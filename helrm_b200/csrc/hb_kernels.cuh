@@ -159,7 +159,7 @@ struct ModUpTab {
     const u64 *qjneg_s; // qjneg in split-30 packed form
     const double2 *qhat_d;  // q-row targets: qhat as {t, fl(t / q_e)} (FP64 modular products)
     const double *qjneg_d;  // q-row targets: qjneg as a double
-    int split;          // every main prime below 2^40: split products
+    int split;          // split products: 1 every main prime below 2^40, 2 every prime below 2^60
 };
 void modup_bconv(u64 *D, const u64 *X, const u64 *c1ntt, int nq, int K, int L, int alpha, int beta,
                  const ModUpTab &tab, int logN, int nbatch, size_t in_stride, size_t out_stride, size_t c1_stride,
@@ -174,7 +174,7 @@ struct ModDownTab {
     const u64 *pneg;    // [nq] q_i - (P mod q_i)
     const u64 *phat_s;  // phat in split-30 packed form
     const u64 *pneg_s;  // pneg in split-30 packed form
-    int split;          // every main prime below 2^40: split-30 products
+    int split;          // split-30 products (nonzero: every prime in the split's range)
 };
 // Z[i] = sum_k (Y_k * phinv_k mod p_k) * phat_k mod q_i  (coefficient form),
 // with the same centred lift as ModUp.
