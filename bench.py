@@ -845,7 +845,7 @@ def helrm_config(args) -> dict:
     from helrm_b200 import helrm as H
     from helrm_b200.params import CFG4_DNUM
     return {"workload": "cfg4: end-to-end HE-LRM forward (BASELINE configs[3])", "logN": 16,
-            "q_limbs_usable": 24, "q_bits": "50 + 23 x 36", "boot_primes": "14 x 60", "special_primes": "6 x 60",
+            "q_limbs_usable": 24, "q_bits": "50 + 23 x 36", "boot_primes": "11 x 60", "special_primes": "6 x 60",
             "dnum": CFG4_DNUM, "h": 192, "batch_ciphertexts": args.batch, "queries_per_ciphertext": 1,
             "bottom": list(H.BOTTOM), "top": [432] + list(H.TOP_HIDDEN) + [1], "relu": list(H.SIGN_DEGREES),
             "bsgs": "32 baby steps per transform (64 above 512 diagonals)",

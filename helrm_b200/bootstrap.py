@@ -31,15 +31,18 @@ Chen, Chillotti, Song, EUROCRYPT 2019):
              real and imaginary parts side by side: 2n <= N / 2);
   EvalMod    on that one ciphertext: u = (x - 1/4) / B in [-1, 1], a
              Chebyshev approximation of cos(2 pi B u / 2^r), r double angles
-             c <- 2 c^2 - 1 giving sin(2 pi x), then arcsin(s) / 1 on the
-             odd Taylor terms (s + s^3/6 + 3 s^5/40) so that the result is
-             2 pi (m / q0) up to (2 pi m / q0)^7 terms;
+             c <- 2 c^2 - 1 giving sin(2 pi x), then, for message ratios
+             q0 / scale below 2^10, arcsin(s) on the odd Taylor terms
+             (s + s^3/6 + 3 s^5/40) so that the result is 2 pi (m / q0) up
+             to (2 pi m / q0)^7 terms; at 2^10 and above sin(x) = x within a
+             relative x^2 / 6 <= 6e-6 and the arcsine is left out;
   StC        one dense n x 2n transform [M, i M] / 2 pi from the 2n real
              slots back to the n-slot packing, landing at the top level of
              the usable chain at the default scale.
 
-Levels: CtS 1, cosine 6 (degree 63), double angles 3, arcsine 3, StC 1 --
-BOOT_LEVELS primes of 60 bits are reserved above the usable chain, as the
+Levels: CtS 1, cosine 6 (degree 63), double angles 3, arcsine 3 (when
+used), StC 1 -- boot_levels() primes of 60 bits are reserved above the
+usable chain, as the
 reference's Cheddar setup reserves its boot primes there
 (bindings.py:279-294).  The input must satisfy q0 >= 2^4 scale (the
 message ratio) and slots n <= 4096 (CtS holds n diagonals, StC 2n).
@@ -53,18 +56,49 @@ import numpy as np
 COS_DEGREE = 63      # depth 6
 DOUBLE_ANGLES = 3
 ASIN_COEFFS = [0.0, 1.0, 0.0, 1.0 / 6.0, 0.0, 3.0 / 40.0]  # arcsin Taylor to s^5 (depth 3)
-BOOT_LEVELS = 1 + 6 + DOUBLE_ANGLES + 3 + 1
+ASIN_DEPTH = 3
+ASIN_MAX_RATIO_BITS = 10  # message ratios q0 / scale below 2^10 take the arcsine
 MAX_SLOTS = 4096
 
 
-def boot_prime_bits(logscale: int) -> list[int]:
+def uses_arcsin(logq0: float, logscale: float) -> bool:
+    return logq0 - logscale < ASIN_MAX_RATIO_BITS
+
+
+def boot_levels(logq0: float, logscale: float) -> int:
+    """Reserved primes: CtS, the cosine, the double angles, the arcsine when
+    the message ratio needs it, StC."""
+    return 1 + 6 + DOUBLE_ANGLES + (ASIN_DEPTH if uses_arcsin(logq0, logscale) else 0) + 1
+
+
+def boot_prime_bits(logscale: int, logq0: int) -> list[int]:
     """Bit sizes of the reserved primes, lowest first (the top one is the
     CtS level).  All of 60 bits: EvalMod's scales sit at these primes, and
     its rescale noise (about sqrt(N h) per product) is amplified by the
     degree-63 Chebyshev basis (up to 63^2) and the double angles (4^3); at
     LogN 16 and h = 192, 51-bit primes (logscale + 15, the reference's
     Cheddar sizing) left 2e-4 in the slots, 60-bit primes 2^9 less."""
-    return [60] * BOOT_LEVELS
+    return [60] * boot_levels(logq0, logscale)
+
+
+def level_plan(q, top: int, asin: bool) -> dict:
+    """Scales and levels of the circuit on the prime chain q (floats) whose
+    top index is `top`: the CtS output scale s_u = q[top - 1], the cosine's
+    output at q[l] for l = top - 7, each double angle squaring and dropping
+    one prime, the arcsine (when used) landing at q[l - 3]; s_evalmod is the
+    scale entering StC and lvl_stc its level."""
+    lvl = top - 1 - 6
+    out = {"s_u": q[top - 1], "s_cos": q[lvl]}
+    s = out["s_cos"]
+    for _ in range(DOUBLE_ANGLES):
+        s = s * s / q[lvl]
+        lvl -= 1
+    out["s_dbl"] = s
+    if asin:
+        out["s_evalmod"], out["lvl_stc"] = q[lvl - ASIN_DEPTH], lvl - ASIN_DEPTH
+    else:
+        out["s_evalmod"], out["lvl_stc"] = s, lvl
+    return out
 
 
 def encoding_matrix(n: int) -> np.ndarray:
@@ -119,7 +153,10 @@ class BootContext:
         self.q0 = self.q[0]
         self.top = len(q) - 1
         self.usable_top = lib._max_level
-        if self.top - BOOT_LEVELS != self.usable_top:
+        # the bit sizes the scheme was set up with (boot_prime_bits)
+        logscale, logq0 = int(lib._default_scale).bit_length() - 1, int(q[0]).bit_length()
+        self.asin = uses_arcsin(logq0, logscale)
+        if self.top - boot_levels(logq0, logscale) != self.usable_top:
             raise RuntimeError("Bootstrap: the scheme was created without the reserved bootstrapping primes")
         self.B = overflow_bound(lib._h) + 1
         M = encoding_matrix(n)
@@ -130,23 +167,17 @@ class BootContext:
         s_cts = self.s_u * self.q[self.top] / (self.R * self.q0)
         self.cts = self._transform(lib, np.vstack([Minv, -1j * Minv]) / (2 * self.B), self.top, s_cts)
         self.poly_cos = lib.GenerateChebyshev(cos_coeffs(self.B, DOUBLE_ANGLES, COS_DEGREE))
-        self.poly_asin = lib.GenerateMonomial(list(ASIN_COEFFS))  # ascending, as the backend takes them
+        # ascending, as the backend takes them
+        self.poly_asin = lib.GenerateMonomial(list(ASIN_COEFFS)) if self.asin else None
         # scales through EvalMod (deterministic: targets at the primes)
-        lvl = self.top - 1 - 6
-        self.s_cos = self.q[lvl]
-        s = self.s_cos
-        for _ in range(DOUBLE_ANGLES):
-            s = s * s / self.q[lvl]
-            lvl -= 1
-        self.s_dbl = s
-        self.lvl_asin_in = lvl
-        self.s_asin = self.q[lvl - 3]
-        self.lvl_stc = lvl - 3
-        assert self.lvl_stc == self.usable_top + 1
+        plan = level_plan(self.q, self.top, self.asin)
+        self.s_cos, self.s_dbl = plan["s_cos"], plan["s_dbl"]
+        self.s_evalmod, self.lvl_stc = plan["s_evalmod"], plan["lvl_stc"]
+        assert self.lvl_stc == self.usable_top + 1 and plan["s_u"] == self.s_u
         # StC: slots 2 pi (m / q0) packed -> E(m) / q0, pt scale chosen so
         # that an input at the default scale comes out at the default scale
         d = float(lib._default_scale)
-        self.s_stc = d * self.q0 * self.q[self.lvl_stc] / (d * self.s_asin)
+        self.s_stc = d * self.q0 * self.q[self.lvl_stc] / (d * self.s_evalmod)
         self.stc = self._transform(lib, np.hstack([M, 1j * M]) / (2 * math.pi), self.lvl_stc, self.s_stc)
         # keys: the SubSum rotations, both transforms', the conjugation
         self.subsum_steps = []
@@ -234,16 +265,19 @@ def bootstrap_batch(lib, ctx: BootContext, cts) -> list[int]:
             lib.AddScalar(sq, -1.0)
             y = sq
         ys[i] = y
-    zs = lib.EvaluatePolynomialBatch(ys, ctx.poly_asin, ctx.s_asin)
-    for y in ys:
-        lib.DeleteCiphertext(y)
+    if ctx.asin:
+        zs = lib.EvaluatePolynomialBatch(ys, ctx.poly_asin, ctx.s_evalmod)
+        for y in ys:
+            lib.DeleteCiphertext(y)
+    else:
+        zs = ys
     outs = lib.EvaluateLinearTransformBatch(ctx.stc, zs)
     for z in zs:
         lib.DeleteCiphertext(z)
     lib.RescaleBatch(outs)
-    # the values: E(m) / q0 at scale s_asin s_stc / q_stc, i.e. the input's
-    # slots at s_asin s_stc scale_in / (q_stc q0)
+    # the values: E(m) / q0 at scale s_evalmod s_stc / q_stc, i.e. the
+    # input's slots at s_evalmod s_stc scale_in / (q_stc q0)
     for o, c, s_in in zip(outs, cts, scales):
-        lib.SetCiphertextScale(o, ctx.s_asin * ctx.s_stc * s_in / (ctx.q[ctx.lvl_stc] * ctx.q0))
+        lib.SetCiphertextScale(o, ctx.s_evalmod * ctx.s_stc * s_in / (ctx.q[ctx.lvl_stc] * ctx.q0))
         lib.SetCiphertextSlots(o, lib.GetCiphertextSlots(c))
     return outs

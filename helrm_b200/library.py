@@ -128,7 +128,7 @@ class B200Library:
         boot = getattr(orion_params, "get_boot_num_cts_levels", lambda: None)() is not None or \
             bool(getattr(orion_params, "boot", False))
         from . import bootstrap as _bt
-        logq_all = logq + (_bt.boot_prime_bits(logscale) if boot else [])
+        logq_all = logq + (_bt.boot_prime_bits(logscale, logq[0]) if boot else [])
         qa, qp = _int_array(logq_all)
         pa, pp = _int_array(logp)
         call("helrm_NewScheme", logn, qp, len(logq_all), pp, len(logp), logscale, h, dnum, seed, device)

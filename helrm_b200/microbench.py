@@ -365,8 +365,8 @@ def run_upload(count=64, level=4, reps=3, device=0) -> dict:
 
 def run_boot(slot_counts=(512,), reps=3, device=0) -> list[dict]:
     """Bootstrapping at LogN 16: the cfg2 chain with a 50-bit q0 (message
-    ratio 2^14) under 24 usable levels, the 14 reserved 60-bit primes above it,
-    six 60-bit special primes (dnum 7); sparse slot counts as Orion's
+    ratio 2^14) under 24 usable levels, the 11 reserved 60-bit primes above it,
+    six 60-bit special primes (dnum 6); sparse slot counts as Orion's
     bootstrap layers use for the MLP widths.  CUDA events on the library
     stream around Bootstrap calls on a level-0 ciphertext; the precision
     is the largest slot error after decryption."""
@@ -406,7 +406,7 @@ def run_boot(slot_counts=(512,), reps=3, device=0) -> list[dict]:
             err = float(np.abs(got - np.tile(z, S // n)).max())
             out.append({"op": "bootstrap", "logN": 16, "slots": n, "ms": ms.value / reps,
                         "level_out": lib.GetCiphertextLevel(res), "max_err": err,
-                        "setup_s": setup_s, "chain": "50 + 23 x 36 usable, 14 x 60 reserved, 6 x 60 special"})
+                        "setup_s": setup_s, "chain": "50 + 23 x 36 usable, 11 x 60 reserved, 6 x 60 special"})
             lib.DeleteCiphertext(res)
             lib.DeleteCiphertext(ct)
     finally:

@@ -62,8 +62,9 @@ CFG1 = CKKSConfig(logn=13, logq=[40] * 5, logp=[60], logscale=40, h=192)
 CFG2 = CKKSConfig(logn=16, logq=[36] * 24, logp=[60] * 4, logscale=36, h=192)
 CFG2_DNUM = 4
 # config 4 (the bootstrapped HE-LRM forward): config 2's 36-bit chain under
-# a 50-bit q0 (message ratio 2^14 for bootstrapping), the 14 reserved 60-bit
-# bootstrapping primes above it, six 60-bit special primes; dnum 7 keeps
-# every digit (at most six primes of up to 60 bits) below the special modulus
+# a 50-bit q0 (message ratio 2^14 for bootstrapping: EvalMod without the
+# arcsine, 11 reserved 60-bit primes above the chain), six 60-bit special
+# primes; dnum 6 keeps every digit (at most six primes of up to 60 bits) at
+# the special modulus' size
 CFG4 = CKKSConfig(logn=16, logq=[50] + [36] * 23, logp=[60] * 6, logscale=36, h=192, boot=True)
-CFG4_DNUM = 7
+CFG4_DNUM = 6

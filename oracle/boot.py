@@ -58,8 +58,8 @@ def mod_raise(o, ct, nq_all):
 
 def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts, replicate=False):
     """ctx: the scales and constants of helrm_b200.bootstrap.BootContext
-    (dict with n, R, B, q0, s_u, s_cos, s_asin, subsum_steps, cts_bs, stc_bs,
-    cos_coeffs, asin_coeffs, top); keys: {galois: switching key};
+    (dict with n, R, B, q0, s_u, s_cos, s_evalmod, subsum_steps, cts_bs,
+    stc_bs, cos_coeffs, asin_coeffs (None: no arcsine), top); keys: {galois: switching key};
     cts_pts / stc_pts: the transforms' extended-basis plaintexts, diagonal k
     at index k (n of CtS, 2n of StC).  replicate: the input holds its values in slots [0, n) and
     zeros elsewhere and is first tiled over the subring by rotations at
@@ -86,8 +86,9 @@ def bootstrap(o, ct, scale_in, ctx, keys, rlk, cts_pts, stc_pts, replicate=False
         sq = o.rescale(o.relinearize(o.tensor(y, y), rlk))
         s = s * s / float(o.primes[y.shape[1] - 1])
         y = add_scalar(o, add(o, sq, sq), -1.0, s)
-    y, _ = poly.evaluate(o, rlk, y, s, ctx["asin_coeffs"], ctx["s_asin"], chebyshev=False)
+    if ctx["asin_coeffs"] is not None:
+        y, _ = poly.evaluate(o, rlk, y, s, ctx["asin_coeffs"], ctx["s_evalmod"], chebyshev=False)
     # StC from the 2n real slots (2n diagonals)
     out = o.rescale(o.bsgs_lt(y, list(range(2 * n)), stc_pts, ctx["stc_bs"], keys))
     q_stc = float(o.primes[y.shape[1] - 1])
-    return out, ctx["s_asin"] * ctx["s_stc"] * scale_in / (q_stc * ctx["q0"])
+    return out, ctx["s_evalmod"] * ctx["s_stc"] * scale_in / (q_stc * ctx["q0"])

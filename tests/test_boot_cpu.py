@@ -15,14 +15,23 @@ from helrm_b200 import bootstrap as BT
 from helrm_b200 import workload as W
 
 
-@pytest.fixture(scope="module")
-def scheme(oracle_mod):
+def _scheme(oracle_mod, logq0):
     logn, logscale = 10, 36
-    logq = [50, 36, 36] + BT.boot_prime_bits(logscale)
+    logq = [logq0, 36, 36] + BT.boot_prime_bits(logscale, logq0)
     main, aux = oracle_mod.scheme_primes(logq, [60] * 4, logn)
     o = oracle_mod.Oracle(logn, main, aux, dnum=5)
     sk = o.secret_ntt(o.sample_secret(9, 64))
     return o, sk, logscale
+
+
+@pytest.fixture(scope="module")
+def scheme(oracle_mod):
+    return _scheme(oracle_mod, 50)
+
+
+@pytest.fixture(scope="module")
+def scheme_asin(oracle_mod):
+    return _scheme(oracle_mod, 44)  # message ratio 2^8: the arcsine is taken
 
 
 def test_encoding_matrix_is_the_canonical_embedding(scheme):
@@ -50,14 +59,20 @@ def _transform_pts(o, A, level, scale, bs):
     return [o.encode(W.preroll(d[k], k // bs, bs), level + 1, scale, ext=True) for k in range(A.shape[1])]
 
 
-@pytest.mark.parametrize("padded", [False, True])
-def test_oracle_bootstrap_precision(scheme, padded):
+def test_arcsine_only_below_ratio_2_10():
+    assert BT.boot_levels(50, 36) == 11 and BT.boot_levels(44, 36) == 14 and BT.boot_levels(46, 36) == 11
+    assert BT.boot_prime_bits(36, 45) == [60] * 14
+
+
+@pytest.mark.parametrize("padded,asin", [(False, False), (True, False), (False, True)])
+def test_oracle_bootstrap_precision(request, padded, asin):
     from oracle import boot as OB
-    o, sk, logscale = scheme
+    o, sk, logscale = request.getfixturevalue("scheme_asin" if asin else "scheme")
     n, S = 8, o.N // 2
     R = S // n
     q = [float(p) for p in o.primes[:o.L]]
-    top, usable_top = o.L - 1, o.L - 1 - BT.BOOT_LEVELS
+    assert BT.uses_arcsin(int(o.primes[0]).bit_length(), logscale) == asin
+    top, usable_top = o.L - 1, o.L - 1 - BT.boot_levels(int(o.primes[0]).bit_length(), logscale)
     B = BT.overflow_bound(64) + 1
     s_u = q[top - 1]
     s_cts = s_u * q[top] / (R * q[0])
@@ -67,16 +82,18 @@ def test_oracle_bootstrap_precision(scheme, padded):
     M = BT.encoding_matrix(n)
     Minv = np.linalg.inv(M)
     cts_pts = _transform_pts(o, np.vstack([Minv, -1j * Minv]) / (2 * B), top, s_cts, bs)
+    # the circuit's scales, restated (helrm_b200.bootstrap.level_plan)
     lvl = top - 7
     s_cos = q[lvl]
     s = s_cos
     for _ in range(BT.DOUBLE_ANGLES):
         s = s * s / q[lvl]
         lvl -= 1
-    s_asin = q[lvl - 3]
-    lvl_stc = lvl - 3
+    s_evalmod, lvl_stc = (q[lvl - 3], lvl - 3) if asin else (s, lvl)
     assert lvl_stc == usable_top + 1
-    s_stc = q[0] * q[lvl_stc] / s_asin
+    assert BT.level_plan(q, top, asin) == {"s_u": s_u, "s_cos": s_cos, "s_dbl": s, "s_evalmod": s_evalmod,
+                                           "lvl_stc": lvl_stc}
+    s_stc = q[0] * q[lvl_stc] / s_evalmod
     stc_pts = _transform_pts(o, np.hstack([M, 1j * M]) / (2 * math.pi), lvl_stc, s_stc, bs2)
     plan = W.bsgs_plan(list(range(n)), r1, S)
     plan2 = W.bsgs_plan(list(range(2 * n)), r2, S)
@@ -89,9 +106,10 @@ def test_oracle_bootstrap_precision(scheme, padded):
            | {2 * o.N - 1})
     keys = {g: o.rotation_key(sk, 5, g) for g in gal}
     rlk = o.relin_key(sk, 5)
-    ctx = {"n": n, "R": R, "B": B, "q0": q[0], "s_u": s_u, "s_cos": s_cos, "s_asin": s_asin, "s_stc": s_stc,
+    ctx = {"n": n, "R": R, "B": B, "q0": q[0], "s_u": s_u, "s_cos": s_cos, "s_evalmod": s_evalmod, "s_stc": s_stc,
            "subsum_steps": steps, "cts_bs": bs, "stc_bs": bs2, "top": top, "double_angles": BT.DOUBLE_ANGLES,
-           "cos_coeffs": BT.cos_coeffs(B, BT.DOUBLE_ANGLES, BT.COS_DEGREE), "asin_coeffs": BT.ASIN_COEFFS}
+           "cos_coeffs": BT.cos_coeffs(B, BT.DOUBLE_ANGLES, BT.COS_DEGREE),
+           "asin_coeffs": BT.ASIN_COEFFS if asin else None}
     rng = np.random.default_rng(4)
     z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.7
     scale = float(1 << logscale)

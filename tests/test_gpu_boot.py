@@ -20,16 +20,26 @@ from helrm_b200 import bootstrap as BT
 
 pytestmark = pytest.mark.gpu
 
-# q0 of 50 bits over the 36-bit scale: message ratio 2^14
+# q0 of 50 bits over the 36-bit scale: message ratio 2^14 (no arcsine)
 CFG = CKKSConfig(logn=12, logq=[50, 36, 36, 36], logp=[60] * 4, logscale=36, h=64, boot=True)
+# q0 of 44 bits: message ratio 2^8, EvalMod ends with the arcsine
+CFG_ASIN = CKKSConfig(logn=12, logq=[44, 36, 36, 36], logp=[60] * 4, logscale=36, h=64, boot=True)
 TOP = 3
 
 
 @pytest.fixture(scope="module")
 def pair(oracle_mod):
     p = Pair(CFG, dnum=5, seed=20261205, oracle_mod=oracle_mod)
-    assert len(p.lib.GetAllModuliChain()) == 4 + BT.BOOT_LEVELS
+    assert len(p.lib.GetAllModuliChain()) == 4 + BT.boot_levels(50, 36) == 4 + 11
     assert len(p.lib.GetModuliChain()) == 4
+    yield p
+    p.close()
+
+
+@pytest.fixture(scope="module")
+def pair_asin(oracle_mod):
+    p = Pair(CFG_ASIN, dnum=5, seed=20261208, oracle_mod=oracle_mod)
+    assert len(p.lib.GetAllModuliChain()) == 4 + BT.boot_levels(44, 36) == 4 + 14
     yield p
     p.close()
 
@@ -74,6 +84,21 @@ def test_bootstrap_restores_values(pair, n):
     assert np.abs(got - np.tile(z, pair.slots // n)).max() < 1e-5
 
 
+def test_bootstrap_with_arcsine_restores_values(pair_asin):
+    """message ratio 2^8: sin(2 pi m / q0) is no longer m's linear image
+    within the precision, the arcsine step corrects it"""
+    n = 32
+    rng = np.random.default_rng(7)
+    z = rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)
+    z /= np.abs(z).max()
+    ct = _encrypt_sparse(pair_asin, z, n, 0)
+    out = pair_asin.lib.Bootstrap(ct, n)
+    assert pair_asin.lib._boot[n].asin
+    assert pair_asin.lib.GetCiphertextLevel(out) == TOP
+    got = _decrypt_c(pair_asin, out)
+    assert np.abs(got - np.tile(z, pair_asin.slots // n)).max() < 1e-5
+
+
 def test_bootstrap_zero_padded_input_from_a_higher_level(pair):
     """Orion's real activations as its Bootstrap layer hands them to a
     non-Cheddar backend: the first n slots, zeros after them, at the full
@@ -93,15 +118,17 @@ def test_bootstrap_zero_padded_input_from_a_higher_level(pair):
     assert np.abs(_decrypt_c(pair, again).real - np.tile(x, pair.slots // n)).max() < 2e-5
 
 
-@pytest.mark.parametrize("padded", [False, True])
-def test_bootstrap_residues_match_oracle(pair, padded):
+@pytest.mark.parametrize("padded,asin", [(False, False), (True, False), (False, True)])
+def test_bootstrap_residues_match_oracle(request, padded, asin):
     from oracle import boot as OB
+    pair = request.getfixturevalue("pair_asin" if asin else "pair")
     n = 16
     rng = np.random.default_rng(3)
     z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.7
     ct = _encrypt_sparse(pair, z, n, 0, padded=padded)
     pair.lib.NewBootstrapper(None, n)
     ctx = pair.lib._boot[n]
+    assert ctx.asin == asin
     out = pair.lib.Bootstrap(ct, n)
     lib, o = pair.lib, pair.o
     info_c, info_s = lib.GetLinearTransformInfo(ctx.cts), lib.GetLinearTransformInfo(ctx.stc)
@@ -110,9 +137,10 @@ def test_bootstrap_residues_match_oracle(pair, padded):
         gal |= {o.galois(k) for k in lib.GetLinearTransformRotationKeys(lt)}
     keys = {g: pair.key(g) for g in sorted(gal)}
     c = {"n": n, "R": ctx.R, "B": ctx.B, "q0": ctx.q0, "s_u": ctx.s_u, "s_cos": ctx.s_cos,
-         "s_asin": ctx.s_asin, "s_stc": ctx.s_stc, "subsum_steps": ctx.subsum_steps,
+         "s_evalmod": ctx.s_evalmod, "s_stc": ctx.s_stc, "subsum_steps": ctx.subsum_steps,
          "cts_bs": info_c["bs"], "stc_bs": info_s["bs"], "top": ctx.top, "double_angles": BT.DOUBLE_ANGLES,
-         "cos_coeffs": BT.cos_coeffs(ctx.B, BT.DOUBLE_ANGLES, BT.COS_DEGREE), "asin_coeffs": BT.ASIN_COEFFS}
+         "cos_coeffs": BT.cos_coeffs(ctx.B, BT.DOUBLE_ANGLES, BT.COS_DEGREE),
+         "asin_coeffs": BT.ASIN_COEFFS if ctx.asin else None}
     cts_pts = [lib.GetLinearTransformPlaintext(ctx.cts, k) for k in range(n)]
     stc_pts = [lib.GetLinearTransformPlaintext(ctx.stc, k) for k in range(2 * n)]
     want, s_out = OB.bootstrap(o, pair.ct_data(ct), pair.scale, c, keys, pair.key(0), cts_pts, stc_pts,
