@@ -22,8 +22,6 @@ pytestmark = pytest.mark.gpu
 
 # q0 of 50 bits over the 36-bit scale: message ratio 2^14 (no arcsine)
 CFG = CKKSConfig(logn=12, logq=[50, 36, 36, 36], logp=[60] * 4, logscale=36, h=64, boot=True)
-# q0 of 44 bits: message ratio 2^8, EvalMod ends with the arcsine
-CFG_ASIN = CKKSConfig(logn=12, logq=[44, 36, 36, 36], logp=[60] * 4, logscale=36, h=64, boot=True)
 TOP = 3
 
 
@@ -35,13 +33,6 @@ def pair(oracle_mod):
     yield p
     p.close()
 
-
-@pytest.fixture(scope="module")
-def pair_asin(oracle_mod):
-    p = Pair(CFG_ASIN, dnum=5, seed=20261208, oracle_mod=oracle_mod)
-    assert len(p.lib.GetAllModuliChain()) == 4 + BT.boot_levels(44, 36) == 4 + 14
-    yield p
-    p.close()
 
 
 def _encrypt_sparse(pair, z, n, level, padded=False):
@@ -84,21 +75,6 @@ def test_bootstrap_restores_values(pair, n):
     assert np.abs(got - np.tile(z, pair.slots // n)).max() < 1e-5
 
 
-def test_bootstrap_with_arcsine_restores_values(pair_asin):
-    """message ratio 2^8: sin(2 pi m / q0) is no longer m's linear image
-    within the precision, the arcsine step corrects it"""
-    n = 32
-    rng = np.random.default_rng(7)
-    z = rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)
-    z /= np.abs(z).max()
-    ct = _encrypt_sparse(pair_asin, z, n, 0)
-    out = pair_asin.lib.Bootstrap(ct, n)
-    assert pair_asin.lib._boot[n].asin
-    assert pair_asin.lib.GetCiphertextLevel(out) == TOP
-    got = _decrypt_c(pair_asin, out)
-    assert np.abs(got - np.tile(z, pair_asin.slots // n)).max() < 1e-5
-
-
 def test_bootstrap_zero_padded_input_from_a_higher_level(pair):
     """Orion's real activations as its Bootstrap layer hands them to a
     non-Cheddar backend: the first n slots, zeros after them, at the full
@@ -118,10 +94,11 @@ def test_bootstrap_zero_padded_input_from_a_higher_level(pair):
     assert np.abs(_decrypt_c(pair, again).real - np.tile(x, pair.slots // n)).max() < 2e-5
 
 
-@pytest.mark.parametrize("padded,asin", [(False, False), (True, False), (False, True)])
-def test_bootstrap_residues_match_oracle(request, padded, asin):
+def check_residues_match_oracle(pair, padded, asin):
+    """The bootstrap's output residues against oracle/boot.py on the
+    library's own keys and transform plaintexts (also used by the arcsine
+    module)."""
     from oracle import boot as OB
-    pair = request.getfixturevalue("pair_asin" if asin else "pair")
     n = 16
     rng = np.random.default_rng(3)
     z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.7
@@ -147,6 +124,11 @@ def test_bootstrap_residues_match_oracle(request, padded, asin):
                                replicate=padded)
     assert np.array_equal(pair.ct_data(out), want)
     assert lib.GetCiphertextScale(out) == pytest.approx(s_out, rel=1e-12)
+
+
+@pytest.mark.parametrize("padded", [False, True])
+def test_bootstrap_residues_match_oracle(pair, padded):
+    check_residues_match_oracle(pair, padded, asin=False)
 
 
 def test_message_ratio_is_checked(pair):
