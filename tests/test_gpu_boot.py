@@ -131,6 +131,27 @@ def test_bootstrap_residues_match_oracle(pair, padded):
     check_residues_match_oracle(pair, padded, asin=False)
 
 
+def test_bootstrap_keeps_a_drifted_scale(pair):
+    """The reference snaps a drifted input scale to the default one before
+    Cheddar's fixed-scale Boot and multiplies by 1/r afterwards
+    (cheddar_pybind.cu:2156-2185, one level).  This circuit reads the input
+    at whatever scale it carries: the output keeps that scale exactly, at
+    full precision, with no level spent."""
+    n = 16
+    rng = np.random.default_rng(11)
+    z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.7
+    drifted = pair.scale * 1.0123
+    vals = np.tile(z, pair.slots // n)
+    pt = pair.lib.EncodeComplex(np.stack([vals.real, vals.imag], axis=-1).ravel(), 0, drifted)
+    ct = pair.lib.Encrypt(pt)
+    pair.lib.DeletePlaintext(pt)
+    pair.lib.SetCiphertextSlots(ct, n)
+    out = pair.lib.Bootstrap(ct, n)
+    assert pair.lib.GetCiphertextScale(out) == pytest.approx(drifted, rel=1e-12)
+    assert pair.lib.GetCiphertextLevel(out) == TOP
+    assert np.abs(_decrypt_c(pair, out) - vals).max() < 1e-5
+
+
 def test_message_ratio_is_checked(pair):
     n = 16
     pt = pair.lib.Encode(list(np.zeros(pair.slots)), 0, 2.0 ** 48)
