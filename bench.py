@@ -828,13 +828,13 @@ def helrm_measure(dist, batch: int, steps: int, warmup: int, profile: bool = Tru
         ms2 = ctypes.c_double(0)
         _capi.check(capi.helrm_TimerStop(ctypes.byref(ms2)))
         t_e2e = dist.max(ms2.value / 1000.0)
-        N = lib.scheme_info()["N"]
+        slots = lib.scheme_info()["slots"]
         res["e2e"] = {"value": whole_job_rate(dist.world, batch, steps, t_e2e), "unit": UNIT,
                       "h2d_bytes_per_step": int(dense.size * 8 + sel.size * 8),
-                      "d2h_bytes_per_step": int(batch * min(4, net.level_out + 1) * N * 8),
+                      "d2h_bytes_per_step": int(batch * 2 * slots * 8),
                       "ms_per_step": 1000.0 * t_e2e / steps,
                       "what": "EncodeBatch of the host features and selectors, Encrypt, the forward, Decrypt, "
-                              "Decode (the decoder reads back the plaintext's first limbs and decodes on the host)"}
+                              "Decode (decoded on the device; the slot values, re and im, are read back)"}
     res["memory"] = {"peak_device_mb": lib.GetPeakDeviceMemoryMB(), "key_mb": lib.GetKeyMemoryMB()}
     net.close()
     lib.DeleteScheme()

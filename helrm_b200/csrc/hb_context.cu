@@ -1087,24 +1087,31 @@ public:
     }
 
     // decode (NTT) plaintext rows -> interleaved values
+    // the slots of plaintext rows d (nq limbs, NTT form) at `scale`, as
+    // interleaved (re, im) pairs, decoded on the device: the inverse NTT of
+    // the first min(nq, 4) limbs, the centred Garner CRT, the special FFT;
+    // only the slot values cross to the host
     void decode_rows(const u64 *d, int nq, double scale, std::vector<double> &out) {
-        const int nc = std::min(nq, 4);
+        const int nc = std::min(nq, HB_DEC_MAX);
         u64 *tmp = alloc((size_t)nc * N);
         d2d(tmp, d, (size_t)nc * N);
         ntt_inverse(tmp, nc, qmap(nc), ntt, stream);
-        std::vector<u64> host((size_t)nc * N);
-        cuda_check(cudaMemcpyAsync(host.data(), tmp, host.size() * 8, cudaMemcpyDeviceToHost, stream), "decode");
-        release(tmp);
-        sync();
-        CrtPlan plan(primes.data(), nc);
-        std::vector<long double> co(N);
-        std::vector<u64> res(nc);
-        for (int n = 0; n < N; n++) {
-            for (int i = 0; i < nc; i++) res[i] = host[(size_t)i * N + n];
-            co[n] = crt_centered(res.data(), plan);
+        const CrtPlan plan(primes.data(), nc);
+        DecCrt dc{};
+        dc.n = nc;
+        for (int i = 0; i < nc; i++) {
+            dc.minv[i] = plan.minv[i];
+            for (int k = 0; k < nc; k++) dc.mmod[i * HB_DEC_MAX + k] = plan.mmod[(size_t)i * nc + k];
         }
+        u64 *coef = alloc(N), *z = alloc(N), *dv = alloc((size_t)2 * slots);
+        decode_slots((double *)dv, tmp, dc, scale, 1, (double *)coef, (double2 *)z, enc_tables_dev(), stream);
         out.resize((size_t)2 * slots);
-        decode_coeffs(logN, co, (long double)scale, out.data());
+        cuda_check(cudaMemcpyAsync(out.data(), dv, out.size() * 8, cudaMemcpyDeviceToHost, stream), "decode");
+        sync();
+        release(tmp);
+        release(coef);
+        release(z);
+        release(dv);
     }
 
     // ---------------------------------------------------------- encrypt

@@ -97,69 +97,9 @@ u64 find_psi(u64 q, int logn) {
     }
 }
 
-namespace {
-
-struct cld {
-    long double re, im;
-};
-
-// In-place radix-2 DFT: forward computes sum_n a[n] w^{+rn}, inverse the
-// w^{-rn} sum (no normalisation), w = exp(2 pi i / n).
-void fft_ld(std::vector<cld> &a, int logn, bool inverse) {
-    const int n = 1 << logn;
-    for (int i = 0; i < n; i++) {
-        int j = (int)h_brv((unsigned)i, logn);
-        if (j > i) std::swap(a[i], a[j]);
-    }
-    const long double PI = 3.141592653589793238462643383279502884L;
-    std::vector<cld> w(n / 2);
-    for (int k = 0; k < n / 2; k++) {
-        long double ang = 2.0L * PI * k / n * (inverse ? -1.0L : 1.0L);
-        w[k] = {cosl(ang), sinl(ang)};
-    }
-    for (int len = 2; len <= n; len <<= 1) {
-        const int half = len >> 1, step = n / len;
-        for (int s = 0; s < n; s += len)
-            for (int k = 0; k < half; k++) {
-                const cld wk = w[k * step];
-                const cld u = a[s + k], v = a[s + k + half];
-                const cld tv = {v.re * wk.re - v.im * wk.im, v.re * wk.im + v.im * wk.re};
-                a[s + k] = {u.re + tv.re, u.im + tv.im};
-                a[s + k + half] = {u.re - tv.re, u.im - tv.im};
-            }
-    }
-}
-
-}  // namespace
-
-void decode_coeffs(int logn, const std::vector<long double> &coeffs, long double scale,
-                   double *vals_out) {
-    const int N = 1 << logn, S = N / 2;
-    const u64 twoN = 2ull * N;
-    const long double PI = 3.141592653589793238462643383279502884L;
-    std::vector<cld> w(N);
-    for (int n = 0; n < N; n++) {
-        long double ang = PI * n / N;
-        w[n] = {coeffs[n] * cosl(ang), coeffs[n] * sinl(ang)};
-    }
-    fft_ld(w, logn, false);
-    u64 e = 1;
-    for (int j = 0; j < S; j++) {
-        vals_out[2 * j] = (double)(w[(e - 1) / 2].re / scale);
-        vals_out[2 * j + 1] = (double)(w[(e - 1) / 2].im / scale);
-        e = (e * 5) % twoN;
-    }
-}
-
 CrtPlan::CrtPlan(const u64 *p, int count) : n(count), primes(p, p + count) {
     minv.resize(n);
     mmod.assign((size_t)n * n, 0);
-    mld.resize(n);
-    long double M = 1.0L;
-    for (int k = 0; k < n; k++) {
-        mld[k] = M;
-        M *= (long double)primes[k];
-    }
     for (int i = 0; i < n; i++) {
         const u64 q = primes[i];
         u64 m = 1 % q;
@@ -169,34 +109,6 @@ CrtPlan::CrtPlan(const u64 *p, int count) : n(count), primes(p, p + count) {
         }
         minv[i] = h_invm(mmod[(size_t)i * n + i], q);
     }
-}
-
-long double crt_centered(const u64 *res, const CrtPlan &P) {
-    const int n = P.n;
-    u64 d[64], r[64];
-    bool neg = false;
-    for (int pass = 0; pass < 2; pass++) {
-        for (int i = 0; i < n; i++) r[i] = pass ? (res[i] ? P.primes[i] - res[i] : 0) : res[i];
-        for (int i = 0; i < n; i++) {
-            const u64 q = P.primes[i];
-            u64 acc = 0;
-            for (int k = 0; k < i; k++) acc = h_addm(acc, h_mulm(d[k] % q, P.mmod[(size_t)i * n + k], q), q);
-            d[i] = h_mulm(h_subm(r[i] % q, acc, q), P.minv[i], q);
-        }
-        if (pass == 1) break;
-        // V > (Q-1)/2 iff its mixed-radix digits exceed (q_k-1)/2 read from the top
-        bool gt = false;
-        for (int i = n - 1; i >= 0; i--) {
-            u64 h = (P.primes[i] - 1) / 2;
-            if (d[i] > h) { gt = true; break; }
-            if (d[i] < h) { gt = false; break; }
-        }
-        if (!gt) break;
-        neg = true;
-    }
-    long double v = 0.0L;
-    for (int i = 0; i < n; i++) v += (long double)d[i] * P.mld[i];
-    return neg ? -v : v;
 }
 
 }  // namespace hb

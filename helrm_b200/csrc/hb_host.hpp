@@ -30,22 +30,14 @@ std::vector<u64> gen_primes(const std::vector<int> &bits, int logn, std::vector<
 // psi = x^((q-1)/2N) for the smallest x >= 2 giving a primitive 2N-th root.
 u64 find_psi(u64 q, int logn);
 
-// Canonical embedding, decoding side (encoding runs on the device).  Slot
-// j is the evaluation at zeta^(5^j mod 2N), zeta = exp(i pi / N); slots =
-// N/2.  From centred integer coefficients (long double), writes the N/2
-// interleaved (re, im) slot values divided by `scale`.
-void decode_coeffs(int logn, const std::vector<long double> &coeffs, long double scale,
-                   double *vals_out);
-
-// Centred CRT (Garner's mixed-radix algorithm) over primes[0..n).
+// Garner's mixed-radix constants over primes[0..n) (the device decoder's
+// centred CRT; encoding and decoding both run on the device).
 struct CrtPlan {
     int n = 0;
     std::vector<u64> primes;
     std::vector<u64> minv;        // (prod_{k<i} q_k)^-1 mod q_i
     std::vector<u64> mmod;        // [i*n + k] = prod_{j<k} q_j mod q_i
-    std::vector<long double> mld; // prod_{j<k} q_j as long double
     explicit CrtPlan(const u64 *p, int count);
 };
-long double crt_centered(const u64 *res, const CrtPlan &plan);
 
 }  // namespace hb

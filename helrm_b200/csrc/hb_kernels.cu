@@ -2797,6 +2797,83 @@ void enc_round(const PtrBatchW &dst, const double2 *z, int rows, RowMap map, dou
     check_launch("enc_round");
 }
 
+// ---- decoding on the device: the inverse of the encoding above ---------------
+// Coefficients from the first nc limbs (after the inverse NTT) by Garner's
+// mixed radix, centred as the host CRT did (digits compared with
+// (q_k - 1) / 2 from the top; a value above (Q - 1) / 2 is recomputed from
+// the negated residues), evaluated in FP64 by Horner from the top digit and
+// divided by the scale.  Then y_k = (m_k + i m_{k+n}) zeta^k and the slots
+// are the length-n DFT with exp(+2 pi i r k / n) at r_j: the encoding's FFT
+// (exp(-2 pi i ...), bit-reversed input) on conj(y), conjugated back.
+__global__ void k_dec_crt(double *out, const u64 *limbs, DecCrt c, double inv_scale, int logN) {
+    const unsigned N = 1u << logN;
+    for (unsigned t = blockIdx.x * blockDim.x + threadIdx.x; t < N; t += gridDim.x * blockDim.x) {
+        u64 r[HB_DEC_MAX], d[HB_DEC_MAX];
+        for (int i = 0; i < c.n; i++) r[i] = limbs[((size_t)i << logN) + t];
+        bool neg = false;
+        for (int pass = 0; pass < 2; pass++) {
+            if (pass) {
+                for (int i = 0; i < c.n; i++) r[i] = r[i] ? c_pc[i].q - r[i] : 0;
+            }
+            for (int i = 0; i < c.n; i++) {
+                const PrimeConst &pc = c_pc[i];
+                u64 acc = 0;
+                for (int k = 0; k < i; k++) acc = add_mod(acc, mul_mod(d[k], c.mmod[i * HB_DEC_MAX + k], pc), pc.q);
+                d[i] = mul_mod(sub_mod(r[i], acc, pc.q), c.minv[i], pc);
+            }
+            if (pass) break;
+            bool gt = false;
+            for (int i = c.n - 1; i >= 0; i--) {
+                const u64 h = (c_pc[i].q - 1) / 2;
+                if (d[i] != h) {
+                    gt = d[i] > h;
+                    break;
+                }
+            }
+            if (!gt) break;
+            neg = true;
+        }
+        double v = 0.0;
+        for (int i = c.n - 1; i >= 0; i--) v = __fma_rn(v, (double)c_pc[i].q, (double)d[i]);
+        out[t] = (neg ? -v : v) * inv_scale;
+    }
+}
+__global__ void k_dec_twist(double2 *z, const double *m, int logN) {
+    const unsigned N = 1u << logN, n = N >> 1;
+    const int h = logN - 1;
+    for (unsigned k = blockIdx.x * blockDim.x + threadIdx.x; k < n; k += gridDim.x * blockDim.x) {
+        double sn, cs;
+        sincospi((double)k / (double)N, &sn, &cs);  // zeta^k = cs + i sn
+        const double a = m[k], b = m[k + n];
+        z[__brev(k) >> (32 - h)] = make_double2(a * cs - b * sn, -(a * sn + b * cs));  // conj(y_k)
+    }
+}
+__global__ void k_dec_gather(double *out, const double2 *z, const int *perm, int cplx, int h) {
+    const unsigned n = 1u << h;
+    for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+        const double2 v = z[__brev((unsigned)perm[j]) >> (32 - h)];  // r_j
+        if (cplx) {
+            out[2 * j] = v.x;
+            out[2 * j + 1] = -v.y;
+        } else {
+            out[j] = v.x;
+        }
+    }
+}
+void decode_slots(double *out, const u64 *limbs, const DecCrt &c, double scale, int cplx, double *coef, double2 *z,
+                  const EncTables &t, cudaStream_t s) {
+    if (c.n < 1 || c.n > HB_DEC_MAX) throw std::invalid_argument("decode: 1 to 4 limbs");
+    const unsigned N = 1u << t.logN, n = N >> 1;
+    ProfScope ps(KC_ELEMENTWISE, (double)N * (8.0 * c.n + 8.0) + (double)n * 48.0, 0.0, s, 3);
+    k_dec_crt<<<grid1d(N, 256), 256, 0, s>>>(coef, limbs, c, 1.0 / scale, t.logN);
+    check_launch("dec_crt");
+    k_dec_twist<<<grid1d(n, 256), 256, 0, s>>>(z, coef, t.logN);
+    check_launch("dec_twist");
+    enc_ifft(z, 1, t, s);
+    k_dec_gather<<<grid1d(n, 256), 256, 0, s>>>(out, z, t.perm, cplx, t.logN - 1);
+    check_launch("dec_gather");
+}
+
 // slot-wise multiplication by i (X^(N/2)) and the conjugation lane split
 __global__ void k_mul_iunit(u64 *out, const u64 *in, int nrows, int nq, const u64 *iu, int logN) {
     const size_t n = (size_t)nrows << logN;

@@ -300,6 +300,18 @@ struct EncTables {
     int logN;
 };
 void enc_tables(int *perm, double2 *tw, int logN, cudaStream_t s);
+// decoding: Garner constants of the first n limbs (mmod[i][k] = q_0 .. q_{k-1}
+// mod q_i, minv[i] its inverse at k = i); out <- the slots (interleaved re, im
+// when cplx) of the plaintext whose first n limbs (coefficient form, after the
+// inverse NTT) are at limbs; coef (N doubles) and z (N/2 complex) are scratch
+#define HB_DEC_MAX 4
+struct DecCrt {
+    int n;
+    u64 mmod[HB_DEC_MAX * HB_DEC_MAX];
+    u64 minv[HB_DEC_MAX];
+};
+void decode_slots(double *out, const u64 *limbs, const DecCrt &c, double scale, int cplx, double *coef, double2 *z,
+                  const EncTables &t, cudaStream_t s);
 // z[v] <- the nvals slot values of vector v (interleaved re, im when cplx, else
 // real), zero in the other slots, in the transform's input order
 void enc_scatter(double2 *z, const double *vals, int nvals, int cplx, int count, const EncTables &t, cudaStream_t s);

@@ -6,8 +6,10 @@ unchanged: same method names, argument meaning and error behaviour as
 ``CheddarLibrary`` (orion/backend/cheddar/bindings.py:135-1342) and
 ``LattigoLibrary`` (orion/backend/lattigo/bindings.py:99-797).  Every call
 goes through the C ABI of ``libhelrm_b200.so`` (include/helrm_b200.h) into
-sm_100a kernels; nothing here computes on the CPU except the canonical
-embedding encode/decode, which the native library also does on the host.
+sm_100a kernels (the canonical-embedding encoding and decoding included);
+no ciphertext or plaintext arithmetic runs on the CPU.  Compile-time
+tables (the composite-sign fit, the bootstrapping matrices) are formed
+with numpy on the host.
 """
 from __future__ import annotations
 

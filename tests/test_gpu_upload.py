@@ -176,3 +176,24 @@ def test_unpack_errors(pair):
         pair.lib.UnpackLanes([a, b], 4)
     with pytest.raises(ValueError):
         pair.lib.UnpackLanes([a], 3)
+
+
+@pytest.mark.parametrize("level,scale_bits", [(0, 30), (1, 60), (3, 100), (4, 120)])
+def test_device_decode_multilimb(pair, level, scale_bits):
+    """Decoding runs on the device: Garner's CRT over the first min(l+1, 4)
+    limbs, centred, then the special FFT.  Large scales put the
+    coefficients beyond the first limbs (40- and 36-bit primes here), so
+    the mixed radix and its sign decision are exercised; negative and
+    complex values too."""
+    rng = np.random.default_rng(scale_bits)
+    z = rng.uniform(-3, 3, pair.slots) + 1j * rng.uniform(-3, 3, pair.slots)
+    scale = 2.0 ** scale_bits
+    # the coefficients round(scale * values) through the oracle's encoder,
+    # which handles any scale exactly (integer arithmetic)
+    want = pair.o.encode(z, level + 1, scale)
+    pt = pair.lib.NewPlaintextFromData(want, level, False, scale)
+    got = np.array(pair.lib.DecodeComplex(pt))
+    got = got[0::2] + 1j * got[1::2]
+    assert np.abs(got - z).max() < 1e-8
+    real = np.array(pair.lib.Decode(pt))
+    assert np.abs(real - z.real).max() < 1e-8
