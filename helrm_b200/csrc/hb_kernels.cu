@@ -2864,12 +2864,15 @@ void decode_slots(double *out, const u64 *limbs, const DecCrt &c, double scale, 
                   const EncTables &t, cudaStream_t s) {
     if (c.n < 1 || c.n > HB_DEC_MAX) throw std::invalid_argument("decode: 1 to 4 limbs");
     const unsigned N = 1u << t.logN, n = N >> 1;
-    ProfScope ps(KC_ELEMENTWISE, (double)N * (8.0 * c.n + 8.0) + (double)n * 48.0, 0.0, s, 3);
-    k_dec_crt<<<grid1d(N, 256), 256, 0, s>>>(coef, limbs, c, 1.0 / scale, t.logN);
-    check_launch("dec_crt");
-    k_dec_twist<<<grid1d(n, 256), 256, 0, s>>>(z, coef, t.logN);
-    check_launch("dec_twist");
+    {
+        ProfScope ps(KC_ELEMENTWISE, (double)N * (8.0 * c.n + 16.0) + (double)n * 16.0, 0.0, s, 2);
+        k_dec_crt<<<grid1d(N, 256), 256, 0, s>>>(coef, limbs, c, 1.0 / scale, t.logN);
+        check_launch("dec_crt");
+        k_dec_twist<<<grid1d(n, 256), 256, 0, s>>>(z, coef, t.logN);
+        check_launch("dec_twist");
+    }
     enc_ifft(z, 1, t, s);
+    ProfScope ps(KC_ELEMENTWISE, (double)n * (16.0 + 4.0 + 8.0 * (cplx ? 2 : 1)), 0.0, s, 1);
     k_dec_gather<<<grid1d(n, 256), 256, 0, s>>>(out, z, t.perm, cplx, t.logN - 1);
     check_launch("dec_gather");
 }

@@ -194,6 +194,9 @@ def test_device_decode_multilimb(pair, level, scale_bits):
     pt = pair.lib.NewPlaintextFromData(want, level, False, scale)
     got = np.array(pair.lib.DecodeComplex(pt))
     got = got[0::2] + 1j * got[1::2]
-    assert np.abs(got - z).max() < 1e-8
+    # the encoding's own rounding (half a unit per coefficient, about
+    # sqrt(N) / 2 / scale in a slot) plus the FP64 transform's error
+    tol = 256.0 / scale + 1e-12
+    assert np.abs(got - z).max() < tol
     real = np.array(pair.lib.Decode(pt))
-    assert np.abs(real - z.real).max() < 1e-8
+    assert np.abs(real - z.real).max() < tol
