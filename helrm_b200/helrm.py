@@ -124,7 +124,7 @@ class HELRM:
 
     def __init__(self, lib, *, vocab=None, base: int = 64, bottom=BOTTOM, top_hidden=TOP_HIDDEN, seed: int = 0,
                  fit_queries: int = 256, ratio: float | None = None, emb_ratio: float | None = None,
-                 boot_chunk: int = 16,
+                 boot_chunk: int = 32,
                  build: bool = True):
         self.lib = lib
         info = lib.scheme_info()
