@@ -414,6 +414,48 @@ def run_boot(slot_counts=(512,), reps=3, device=0) -> list[dict]:
     return out
 
 
+def run_mac_mixed(reps=3, batch=8, device=0) -> dict:
+    """Profiling case of the fused MAC over mixed prime sizes (the
+    bootstrapping chain's shape, kept to a few GB): LogN 16, q0 of 50 bits,
+    five 36-bit and three 60-bit q primes, three 60-bit special primes at
+    dnum 5 (five digits at the top level), one 64-diagonal transform at
+    bsgs_ratio 16 (a full chunk of 32 babies, two giant slots), `batch`
+    ciphertexts, `reps` evaluations; CUDA events on the library stream."""
+    from helrm_b200 import B200Library, CKKSConfig, _capi
+
+    cfg = CKKSConfig(logn=16, logq=[50] + [36] * 5 + [60] * 3, logp=[60] * 3, logscale=36, h=192)
+    lib = B200Library(dnum=5, seed=5, device=device)
+    lib.setup_bindings(cfg)
+    try:
+        lib.GenerateSecretKey()
+        S = lib.scheme_info()["slots"]
+        ks = list(range(64))
+        rng = np.random.default_rng(1)
+        level = len(cfg.logq) - 1
+        lt = lib.GenerateLinearTransform(ks, rng.uniform(-0.5, 0.5, (len(ks), S)).ravel(), level, 16.0, "none")
+        for k in lib.GetLinearTransformRotationKeys(lt):
+            lib.GenerateLinearTransformRotationKey(k)
+        cts = []
+        for _ in range(batch):
+            pt = lib.Encode(list(rng.uniform(-1, 1, S)), level, float(1 << 36))
+            cts.append(lib.Encrypt(pt))
+            lib.DeletePlaintext(pt)
+        for o in lib.EvaluateLinearTransformBatch(lt, cts):  # warm-up
+            lib.DeleteCiphertext(o)
+        capi = _capi.load()
+        lib.Synchronize()
+        _capi.check(capi.helrm_TimerStart())
+        for _ in range(reps):
+            for o in lib.EvaluateLinearTransformBatch(lt, cts):
+                lib.DeleteCiphertext(o)
+        ms = ctypes.c_double(0)
+        _capi.check(capi.helrm_TimerStop(ctypes.byref(ms)))
+        return {"op": "lt_mixed_primes", "logN": 16, "digits": 5, "diagonals": 64, "bs": 32, "batch": batch,
+                "ms": ms.value / reps, "peak_device_mb": lib.GetPeakDeviceMemoryMB()}
+    finally:
+        lib.DeleteScheme()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batches", default="1,16,128")
@@ -424,7 +466,12 @@ def main():
     ap.add_argument("--relu", action="store_true", help="also Orion's composite ReLU through EvaluatePolynomial")
     ap.add_argument("--upload", action="store_true", help="also the selector upload (device encode, lane split)")
     ap.add_argument("--boot", action="store_true", help="also bootstrapping at LogN 16 (256 and 512 slots)")
+    ap.add_argument("--mac-mixed", action="store_true",
+                    help="only the mixed-prime fused-MAC profiling case (a few GB on the device)")
     args = ap.parse_args()
+    if args.mac_mixed:
+        print(json.dumps(run_mac_mixed()), flush=True)
+        return
     run([int(b) for b in args.batches.split(",")], args.reps, args.ops, args.rotations,
         emit=lambda line: print(json.dumps(line), flush=True))
     if args.table:
