@@ -75,6 +75,7 @@ SIGNATURES = {
     "helrm_GetLinearTransformInfo": [c_int, P(c_int), P(c_int), P(c_int), P(c_int)],
     "helrm_HybridFoldBatch": [P(c_int), c_int, c_int],
     "helrm_RescaleBatch": [P(c_int), c_int],
+    "helrm_MulRelinCiphertextBatchNew": [P(c_int), P(c_int), c_int, P(c_int)],
     "helrm_DeleteCiphertext": [c_int],
     "helrm_DeletePlaintext": [c_int],
     "helrm_GetCiphertextLevel": [c_int, P(c_int)],

@@ -256,15 +256,15 @@ def bootstrap_batch(lib, ctx: BootContext, cts) -> list[int]:
     ys = lib.EvaluatePolynomialBatch(us, ctx.poly_cos, ctx.s_cos)
     for u in us:
         lib.DeleteCiphertext(u)
-    for i, y in enumerate(ys):
-        for _ in range(DOUBLE_ANGLES):
-            sq = lib.MulRelinCiphertextNew(y, y)
+    for _ in range(DOUBLE_ANGLES):  # y <- 2 y^2 - 1
+        sqs = lib.MulRelinCiphertextBatchNew(ys, ys)
+        for y in ys:
             lib.DeleteCiphertext(y)
-            lib.Rescale(sq)
+        lib.RescaleBatch(sqs)
+        for sq in sqs:
             lib.AddCiphertext(sq, sq)
             lib.AddScalar(sq, -1.0)
-            y = sq
-        ys[i] = y
+        ys = sqs
     if ctx.asin:
         zs = lib.EvaluatePolynomialBatch(ys, ctx.poly_asin, ctx.s_evalmod)
         for y in ys:

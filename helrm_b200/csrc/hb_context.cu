@@ -2198,6 +2198,56 @@ static int mul_relin(Context &c, int a, int b) {
 }
 NEW_AND_INPLACE2(MulRelinCiphertext, mul_relin(c, a, b))
 
+// the pairs of one level (the lower of the two operands') gathered into one
+// batch: one batched tensor product and one batched relinearisation, the
+// same arithmetic as mul_relin per pair
+HB_API int helrm_MulRelinCiphertextBatchNew(const int *a, const int *b, int n, int *out) {
+    return guard([&] {
+        Context &c = C();
+        if (n < 0 || (n > 0 && (!a || !b || !out))) HB_THROW(HB_EINVAL, "MulRelinCiphertextBatchNew: bad arguments");
+        if (!c.d_rlk) c.gen_relin();
+        std::map<int, std::vector<int>> groups;
+        for (int i = 0; i < n; i++) {
+            const Ct &ca = c.ct(a[i]), &cb = c.ct(b[i]);
+            if (ca.npoly != 2 || cb.npoly != 2) HB_THROW(HB_ESTATE, "MulRelinCiphertext: operand is degree-2");
+            groups[std::min(ca.nq, cb.nq)].push_back(i);
+        }
+        for (auto &kv : groups) {
+            const int nq = kv.first;
+            const auto &idx = kv.second;
+            const int nb = (int)idx.size();
+            const size_t w2 = (size_t)2 * nq * c.N;
+            std::vector<const Ct *> va(nb), vb(nb);
+            for (int k = 0; k < nb; k++) {
+                va[k] = &c.ct(a[idx[k]]);
+                vb[k] = &c.ct(b[idx[k]]);
+            }
+            u64 *A = c.alloc((size_t)nb * w2), *B = c.alloc((size_t)nb * w2);
+            c.gather_cts(A, va, nq);  // the first nq rows of each polynomial
+            c.gather_cts(B, vb, nq);
+            u64 *t3 = c.alloc((size_t)nb * 3 * nq * c.N);
+            ew_tensor_batch(t3, A, B, nq, nq, nq, nb, w2, w2, c.logN, c.stream);
+            c.release(A);
+            c.release(B);
+            u64 *R = c.alloc((size_t)nb * w2);
+            c.relinearize_batch(R, t3, nq, nb);
+            c.release(t3);
+            std::vector<u64 *> dst(nb);
+            std::vector<int> fresh(nb);
+            for (int k = 0; k < nb; k++) {
+                const Ct &ca = *va[k], &cb = *vb[k];
+                Ct o = c.new_ct(nq, 2, ca.scale * cb.scale);
+                o.slots = std::max(ca.slots, cb.slots);
+                dst[k] = o.d;
+                fresh[k] = c.put_ct(o);
+            }
+            c.scatter_words(dst, R, w2);
+            c.release(R);
+            for (int k = 0; k < nb; k++) out[idx[k]] = fresh[k];
+        }
+    });
+}
+
 // ---- polynomial evaluation ----------------------------------------------------
 static PolyPlan &poly_plan(Context &c, bool cheb, int nq0, double s1, const std::vector<double> &co, double S) {
     std::string key;

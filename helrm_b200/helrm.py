@@ -349,7 +349,7 @@ class HELRM:
             if cur is not xs:
                 self._free(cur)
             cur = nxt
-        res = [lib.MulRelinCiphertextNew(x, s) for x, s in zip(xs, cur)]
+        res = lib.MulRelinCiphertextBatchNew(xs, cur)
         lib.RescaleBatch(res)
         self._free(cur)
         self._free(xs)

@@ -290,6 +290,17 @@ class B200Library:
     def MulRelinCiphertextNew(self, a, b):
         return self._new2("helrm_MulRelinCiphertextNew", a, b)
 
+    def MulRelinCiphertextBatchNew(self, a_ids: Sequence[int], b_ids: Sequence[int]) -> list[int]:
+        """[MulRelinCiphertextNew(a, b) for a, b in pairs], the pairs of one
+        level computed in batched kernels (residue-identical)."""
+        if len(a_ids) != len(b_ids):
+            raise ValueError("MulRelinCiphertextBatchNew: a_ids and b_ids differ in length")
+        aa, ap = _int_array(a_ids)
+        ba, bp = _int_array(b_ids)
+        outs = np.zeros(len(aa), dtype=np.int32)
+        call("helrm_MulRelinCiphertextBatchNew", ap, bp, len(aa), outs.ctypes.data_as(P(c_int)))
+        return outs.tolist()
+
     def MulRelinCiphertext(self, a, b):
         call("helrm_MulRelinCiphertext", int(a), int(b))
         return int(a)

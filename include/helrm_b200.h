@@ -158,6 +158,10 @@ int helrm_GetLinearTransformInfo(int lt, int *bs, int *ndiag, int *ngiant, int *
 int helrm_HybridFoldBatch(const int *cts, int n, int rotations);
 /* Rescale n ciphertexts in place. */
 int helrm_RescaleBatch(const int *cts, int n);
+/* out[i] = MulRelinCiphertextNew(a[i], b[i]) for n pairs, the pairs of one
+ * level computed together (batch form of the per-pair call above; the
+ * reference's evaluators multiply one pair per call). */
+int helrm_MulRelinCiphertextBatchNew(const int *a, const int *b, int n, int *out);
 
 /* ---- broadcast constants and the one-pass table products of the IVE lookup
  * (cheddar bindings.py:621-706; cheddar_pybind.cu:1044-1569).  A constant is

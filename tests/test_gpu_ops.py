@@ -248,3 +248,28 @@ def test_live_counts_and_memory(s):
     assert s.backend.GetLiveCiphertexts() == n0
     assert s.backend.GetKeyMemoryMB() > 0
     assert s.backend.GetPeakLiveMemoryMB() >= s.backend.GetLiveMemoryMB()
+
+
+def test_mul_relin_batch_equals_per_pair(s):
+    """MulRelinCiphertextBatchNew: the pairs of each level in one batched
+    tensor product and relinearisation, residue for residue what
+    MulRelinCiphertextNew gives pair by pair (mixed levels, a squaring,
+    operands at different levels)."""
+    lib = s.backend
+    rng = np.random.default_rng(31)
+    top = s.max_level
+    cts = [s.enc(rng.uniform(-1, 1, s.slots), lvl) for lvl in (top, top, top - 1, top, top - 1)]
+    a_ids = [cts[0], cts[1], cts[2], cts[3], cts[0]]
+    b_ids = [cts[1], cts[1], cts[4], cts[2], cts[0]]
+    got = lib.MulRelinCiphertextBatchNew(a_ids, b_ids)
+    assert len(set(got)) == len(got)
+    for a, b, g in zip(a_ids, b_ids, got):
+        want = lib.MulRelinCiphertextNew(a, b)
+        assert np.array_equal(lib.GetCiphertextData(g), lib.GetCiphertextData(want))
+        assert lib.GetCiphertextScale(g) == lib.GetCiphertextScale(want)
+        assert lib.GetCiphertextLevel(g) == lib.GetCiphertextLevel(want)
+        lib.DeleteCiphertext(want)
+        lib.DeleteCiphertext(g)
+    assert lib.MulRelinCiphertextBatchNew([], []) == []
+    with pytest.raises(ValueError):
+        lib.MulRelinCiphertextBatchNew([cts[0]], [])
