@@ -1602,10 +1602,14 @@ public:
     // ---------------------------------------------------------- linear transforms
     int generate_lt(const int *idxs, int n, const double *data, int width, int level, double ratio,
                     bool cplx = false, double pscale = 0.0) {
-        if (!(pscale > 0)) pscale = default_scale;
         if (n <= 0) HB_THROW(HB_EINVAL, "GenerateLinearTransform: no diagonals");
         if (width <= 0 || width > slots) HB_THROW(HB_EINVAL, "GenerateLinearTransform: bad diagonal width");
         if (level < 0 || level >= L) HB_THROW(HB_EINVAL, "GenerateLinearTransform: level out of range");
+        // the diagonals at the level's prime, as the reference's Lattigo
+        // backend encodes them (lineartransform.go:65): the rescale after
+        // the transform divides that prime back out, so the output keeps
+        // the input's scale exactly
+        if (!(pscale > 0)) pscale = (double)primes[level];
         auto t = std::make_unique<LinTrans>();
         t->level = level;
         t->scale = pscale;

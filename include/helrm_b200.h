@@ -142,7 +142,9 @@ int helrm_Conjugate(int ct);
 
 /* ---- linear transforms (lineartransform.go:37-211; cheddar bindings.py:833-1066) -- */
 /* GenerateLinearTransform: n diagonals, each `width` values, row-major in
- * `data`; bsgs_ratio <= 0 means "none" (one giant group). */
+ * `data`; bsgs_ratio <= 0 means "none" (one giant group).  The diagonals are
+ * encoded at the level's prime (lineartransform.go:65), so the rescaled
+ * output keeps the input's scale. */
 int helrm_GenerateLinearTransform(const int *diag_idxs, int n, const double *data, int width, int level,
                                   double bsgs_ratio, int *out_lt);
 int helrm_EvaluateLinearTransform(int lt, int ct, int *out);

@@ -3,8 +3,10 @@
     python tests/golden/make_orion_trace.py <reference checkout>
 
 Runs the reference's own flow (orion/core/orion.py: init_scheme, fit,
-compile, encode, encrypt, the encrypted forward, decrypt, decode) for two
-small networks, an ``on.Linear`` layer and an ``on.Embedding`` layer, with
+compile, encode, encrypt, the encrypted forward, decrypt, decode) for small
+networks (an ``on.Linear`` layer, an ``on.Embedding`` layer, ReLU MLPs with
+and without placed bootstraps, and the reference's HELRM model of
+examples/criteo/dlrm.py with its widths narrowed), with
 ``helrm_b200.orion_adapter.install()`` registering ``backend: b200``.  The
 backend object handed to Orion here is a recording stand-in with the
 B200Library's method names and its level, scale and slot rules (this
@@ -309,7 +311,7 @@ class Recorder:
     def EvaluateLinearTransform(self, lt, ct):
         m = dict(self.cts[ct])
         m["level"] = min(m["level"], self.lts[lt]["level"])
-        m["scale"] *= self._default_scale
+        m["scale"] *= float(self.primes[self.lts[lt]["level"]])  # diagonals at the level's prime
         i = self._ct_new(m)
         return self._log("EvaluateLinearTransform", [{"lt": lt}, {"ct": ct}], {"ct": i})["ct"]
 
@@ -450,6 +452,40 @@ def record(net_kind: str, ref_root: str, config=None):
             h = net.fc1(inp).detach().abs()
             if float(h.min()) >= 0.05 * float(h.max()):
                 break
+    elif net_kind == "helrm":
+        # the reference's own encrypted model (examples/criteo/dlrm.py:181-229),
+        # its module-level widths narrowed to fit LogN 13: two tables (50 and
+        # 300 categories, radix-4 digits above 20), embedding dim 4, bottom
+        # MLP 13-16-4, top MLP 12-8-1
+        sys.path.insert(0, os.path.join(ref_root, "examples", "criteo"))
+        import dlrm
+        dlrm.sparse_fields, dlrm.embedding_features = 2, 4
+        dlrm.bottom_widths = [dlrm.dense_features, 16, 4]
+        dlrm.top_widths = [4 * 3, 8, 1]
+        net = dlrm.HELRM([50, 300], compress_threshold=20, base=4)
+        # dense features log1p(lognormal) and indices whose ReLU inputs stay
+        # clear of the composite sign's gap (|h| >= 0.05 max|h| per layer)
+        for seed in range(2000):
+            g = torch.Generator().manual_seed(seed)
+            dense = torch.log1p(torch.exp(torch.randn(1, 13, generator=g)))
+            sparse = torch.tensor([int(torch.randint(0, 50, (1,), generator=g)),
+                                   int(torch.randint(0, 300, (1,), generator=g))])
+            d_in, s_in = net.fhe_input(dense, sparse)
+            hs = []
+            x = d_in
+            for layer in net.bottom:
+                x = layer(x)
+                if isinstance(layer, on.Linear):
+                    hs.append(x.detach())
+            top_in = net.bottom_to_top(x) + net.sparse_to_top(net.sparse(s_in))
+            x = top_in
+            for layer in net.top:
+                x = layer(x)
+                if isinstance(layer, on.Linear):
+                    hs.append(x.detach())
+            if all(float(h.abs().min()) >= 0.05 * float(h.abs().max()) for h in hs[:-1]):
+                break
+        inp = [d_in, s_in]
     else:
         class Net(on.Module):
             def __init__(self):
@@ -464,13 +500,13 @@ def record(net_kind: str, ref_root: str, config=None):
     scheme = orion.init_scheme(config)
     rec = holder["rec"]
     net.eval()
-    out_clear = net(inp).detach().numpy().ravel()
+    inputs = inp if isinstance(inp, list) else [inp]
+    out_clear = net(*inputs).detach().numpy().ravel()
     orion.fit(net, inp)
     level = orion.compile(net)
-    ptxt = orion.encode(inp, level)
-    ctxt = orion.encrypt(ptxt)
+    ctxts = [orion.encrypt(orion.encode(x, level)) for x in inputs]
     net.he()
-    out_ct = net(ctxt)
+    out_ct = net(*ctxts)
     mark = len(rec.calls)
     out_pt = out_ct.decrypt()
     out_pt.decode()
@@ -484,8 +520,8 @@ def main():
     if not ref or not os.path.isdir(ref):
         raise SystemExit("usage: make_orion_trace.py <reference checkout>")
     traces, arrays = {}, {}
-    configs = {"mlp_relu": CONFIG_DEEP, "mlp_boot": CONFIG_BOOT}
-    for kind in ("linear", "embedding", "mlp_relu", "mlp_boot"):
+    configs = {"mlp_relu": CONFIG_DEEP, "mlp_boot": CONFIG_BOOT, "helrm": CONFIG_BOOT}
+    for kind in ("linear", "embedding", "mlp_relu", "mlp_boot", "helrm"):
         rec, out_clear, decodes, level = record(kind, ref, configs.get(kind, CONFIG))
         traces[kind] = {"params": rec.params, "calls": rec.calls, "output_decode_calls": decodes,
                         "input_level": int(level), "cleartext_output": [float(v) for v in out_clear]}

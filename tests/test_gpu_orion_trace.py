@@ -10,7 +10,11 @@ coefficients from GenerateMinimaxSignCoeffs, three EvaluatePolynomial
 stages at the levels Orion's compiler placed, x * step(x)), and of a
 network with two ReLUs over a chain too short for both, where Orion's own
 bootstrap placement (orion/core/auto_bootstrap.py) inserted two
-NewBootstrapper / Bootstrap calls (orion/nn/operations.py:38-115)
+NewBootstrapper / Bootstrap calls (orion/nn/operations.py:38-115), and
+of the reference's own HE-LRM model (examples/criteo/dlrm.py:181-229:
+bottom MLP with ReLUs, the block-diagonal embedding, the two copy-into
+layers, the add, the top MLP; module widths narrowed to fit LogN 13),
+two encrypted inputs and three Orion-placed bootstraps,
 with ``backend: b200`` registered through helrm_b200.orion_adapter and
 recorded every backend call, in order, with its arguments.  The reference
 cannot travel to the GPU box, so the calls are replayed here on the real
@@ -77,7 +81,7 @@ def _replay(kind):
         lib.DeleteScheme()
 
 
-@pytest.mark.parametrize("kind", ["linear", "embedding", "mlp_relu", "mlp_boot"])
+@pytest.mark.parametrize("kind", ["linear", "embedding", "mlp_relu", "mlp_boot", "helrm"])
 def test_orion_flow_replayed_on_b200(kind):
     out, clear = _replay(kind)
     n = len(clear)
