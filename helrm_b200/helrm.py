@@ -250,13 +250,13 @@ class HELRM:
     def _compile(self, ratio: float, emb_ratio: float):
         lib = self.lib
         nb = len(self.bottom_w)
-        self.bottom = [LinearLayer(lib, w, b, lvl, ratio=ratio, narrow=False, exact=True)
+        self.bottom = [LinearLayer(lib, w, b, lvl, ratio=ratio, narrow=False)
                        for (w, b), lvl in zip(self.bottom_w, self.bottom_levels)]
-        self.b2t_layer = LinearLayer(lib, self.b2t, None, self.level_b2t, ratio=ratio, narrow=False, exact=True)
-        self.emb_layer = LinearLayer(lib, self.emb, None, self.level_sel, ratio=emb_ratio, narrow=False, exact=True)
-        self.s2t_layer = LinearLayer(lib, self.s2t, None, self.level_sel - 1, ratio=ratio, narrow=False, exact=True)
+        self.b2t_layer = LinearLayer(lib, self.b2t, None, self.level_b2t, ratio=ratio, narrow=False)
+        self.emb_layer = LinearLayer(lib, self.emb, None, self.level_sel, ratio=emb_ratio, narrow=False)
+        self.s2t_layer = LinearLayer(lib, self.s2t, None, self.level_sel - 1, ratio=ratio, narrow=False)
         nt = len(self.top_w)
-        self.top = [LinearLayer(lib, w, b, lvl, last=(i == nt - 1), ratio=ratio, narrow=False, exact=True)
+        self.top = [LinearLayer(lib, w, b, lvl, last=(i == nt - 1), ratio=ratio, narrow=False)
                     for i, ((w, b), lvl) in enumerate(zip(self.top_w, self.top_levels))]
         self.polys = [lib.GenerateChebyshev(list(c)) for c in self.stages]
         if sum(lib.GetPolyDepth(p) for p in self.polys) != SIGN_DEPTH:

@@ -19,7 +19,7 @@ The backend works on full-width ciphertexts: after the fold the output is
 periodic with period bh (the block height), and the bias is tiled with
 the same period, so the full-width and the narrowed views agree.  The
 bias plaintext is encoded at the exact scale the rescaled output carries
-(input scale x plaintext scale / the dropped prime), so the add needs no
+(the input's: the diagonals sit at the dropped prime), so the add needs no
 scale-drift absorption.
 """
 from __future__ import annotations
@@ -34,12 +34,11 @@ class LinearLayer:
     B200Library scheme, evaluated on a batch of ciphertexts that each hold
     one input vector in slots 0..in-1 (any period-replicated copies beyond
     are ignored: the diagonals read only the first copy).  narrow retags
-    the folded output to its period; exact encodes the diagonals at the
-    level's prime instead of the default scale; ratio None picks the BSGS
-    split with 32 baby steps (64 above 512 diagonals)."""
+    the folded output to its period; ratio None picks the BSGS split with
+    32 baby steps (64 above 512 diagonals)."""
 
     def __init__(self, lib, weight: np.ndarray, bias, level: int, last: bool = False, ratio: float | None = 2.0,
-                 narrow: bool = True, exact: bool = False):
+                 narrow: bool = True):
         self.lib = lib
         info = lib.scheme_info()
         self.slots = info["slots"]
@@ -57,11 +56,9 @@ class LinearLayer:
         if ratio is None:  # 32 baby steps (64 above 512 diagonals): the fused MAC's full chunks
             bs = 64 if len(self.ks) > 512 else 32
             ratio = bs * bs / float(len(self.ks))
-        if exact:  # diagonals at q_level: the rescaled output keeps the input's scale exactly
-            q = float(lib.GetModuliChain()[level])
-            self.lt = lib.GenerateLinearTransformEx(self.ks, data, self.slots, level, ratio, False, q)
-        else:
-            self.lt = lib.GenerateLinearTransform(self.ks, data, level, ratio, "none")
+        # the diagonals at q_level (GenerateLinearTransform's rule): the
+        # rescaled output keeps the input's scale exactly
+        self.lt = lib.GenerateLinearTransform(self.ks, data, level, ratio, "none")
         for k in lib.GetLinearTransformRotationKeys(self.lt):
             lib.GenerateLinearTransformRotationKey(k)
         for i in range(1, self.rot + 1):
