@@ -1365,22 +1365,18 @@ public:
         else res = const_residues(value * (long double)c.scale);
         if (kind == 1)
             for (int p = 0; p < P; p++) res[p] = res[p] ? primes[p] - res[p] : 0;
-        u64 *dc = alloc((size_t)2 * P);
-        std::vector<u64> hc(2 * P);
+        ConstWords cw{};
         for (int p = 0; p < P; p++) {
-            hc[p] = res[p];
-            hc[P + p] = h_shoup(res[p], primes[p]);
+            cw.v[p] = res[p];
+            cw.vp[p] = h_shoup(res[p], primes[p]);
         }
-        cuda_check(cudaMemcpyAsync(dc, hc.data(), hc.size() * 8, cudaMemcpyHostToDevice, stream), "const");
         if (kind <= 1) {
-            ew_add_const(o.d, c.d, dc, c.nq, qmap(c.nq), logN, stream);
+            ew_add_const(o.d, c.d, cw, c.nq, qmap(c.nq), logN, stream);
             if (c.npoly > 1) d2d(o.d + (size_t)c.nq * N, c.d + (size_t)c.nq * N, (size_t)(c.npoly - 1) * c.nq * N);
         } else {
-            ew_mul_const(o.d, c.d, dc, dc + P, c.npoly * c.nq, qmap(c.nq), logN, stream);
+            ew_mul_const(o.d, c.d, cw, c.npoly * c.nq, qmap(c.nq), logN, stream);
             if (kind == 3) o.scale = c.scale * c.scale;
         }
-        sync();  // host constant buffer
-        release(dc);
         return put_ct(o);
     }
 

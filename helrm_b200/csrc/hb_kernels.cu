@@ -1265,34 +1265,35 @@ void ew_mul_bcast(u64 *out, const u64 *a, const u64 *b, int npoly, int nq, int, 
     check_launch("mul_bcast");
 }
 
-__global__ void k_mul_const(u64 *out, const u64 *a, const u64 *c, const u64 *cp, size_t n, RowMap map, int logN) {
+// the constant's residues travel as a kernel parameter: no device buffer,
+// no host copy to wait for
+__global__ void k_mul_const(u64 *out, const u64 *a, const ConstWords cw, size_t n, RowMap map, int logN) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int p = map.prime((int)(i >> logN));
-        out[i] = mul_shoup(a[i], c[p], cp[p], c_pc[p].q);
+        out[i] = mul_shoup(a[i], cw.v[p], cw.vp[p], c_pc[p].q);
     }
 }
-void ew_mul_const(u64 *out, const u64 *a, const u64 *c, const u64 *cp, int nrows, RowMap map, int logN,
-                  cudaStream_t s) {
+void ew_mul_const(u64 *out, const u64 *a, const ConstWords &cw, int nrows, RowMap map, int logN, cudaStream_t s) {
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
     ProfScope ps(KC_ELEMENTWISE, 16.0 * n, (double)n, s, 1);
-    k_mul_const<<<g, 256, 0, s>>>(out, a, c, cp, n, map, logN);
+    k_mul_const<<<g, 256, 0, s>>>(out, a, cw, n, map, logN);
     check_launch("mul_const");
 }
 
-__global__ void k_add_const(u64 *out, const u64 *a, const u64 *c, size_t n, RowMap map, int logN) {
+__global__ void k_add_const(u64 *out, const u64 *a, const ConstWords cw, size_t n, RowMap map, int logN) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int p = map.prime((int)(i >> logN));
-        out[i] = add_mod(a[i], c[p], c_pc[p].q);
+        out[i] = add_mod(a[i], cw.v[p], c_pc[p].q);
     }
 }
-void ew_add_const(u64 *out, const u64 *a, const u64 *c, int nrows, RowMap map, int logN, cudaStream_t s) {
+void ew_add_const(u64 *out, const u64 *a, const ConstWords &cw, int nrows, RowMap map, int logN, cudaStream_t s) {
     size_t n = (size_t)nrows << logN;
     unsigned g = grid1d(n, 256);
     if (g > 148u * 64u) g = 148u * 64u;
     ProfScope ps(KC_ELEMENTWISE, 16.0 * n, 0, s, 1);
-    k_add_const<<<g, 256, 0, s>>>(out, a, c, n, map, logN);
+    k_add_const<<<g, 256, 0, s>>>(out, a, cw, n, map, logN);
     check_launch("add_const");
 }
 

@@ -90,9 +90,13 @@ void ew_reduce_rows(u64 *out, const u64 *a, int nrows, RowMap map, int logN, cud
 void ew_mul_bcast(u64 *out, const u64 *a, const u64 *b, int npoly, int nq, int b_rows_stride_nq,
                   int logN, cudaStream_t s);
 // out[r] = a[r] * c[prime(r)] (+ add[prime(r)] if add != null), constants per prime with Shoup
-void ew_mul_const(u64 *out, const u64 *a, const u64 *c, const u64 *cp, int nrows, RowMap map, int logN,
-                  cudaStream_t s);
-void ew_add_const(u64 *out, const u64 *a, const u64 *c, int nrows, RowMap map, int logN, cudaStream_t s);
+// one word per prime (and its Shoup companion), passed by value
+struct ConstWords {
+    u64 v[HB_MAX_PRIMES];
+    u64 vp[HB_MAX_PRIMES];
+};
+void ew_mul_const(u64 *out, const u64 *a, const ConstWords &cw, int nrows, RowMap map, int logN, cudaStream_t s);
+void ew_add_const(u64 *out, const u64 *a, const ConstWords &cw, int nrows, RowMap map, int logN, cudaStream_t s);
 // ct x ct tensor: out[0]=a0b0, out[1]=a0b1+a1b0, out[2]=a1b1 (nq rows each)
 void ew_tensor(u64 *out, const u64 *a, const u64 *b, int nq, int logN, cudaStream_t s);
 // out = c0 + c1 * sk (nq rows)
