@@ -4,13 +4,18 @@
 One step = one batch of 64 encrypted Criteo-shaped queries through the
 embedding layer, the reference's hot path (examples/criteo/dlrm.py:226-229
 -> orion/nn/linear.py:99-140): the BSGS diagonal linear transform of the
-26-table block-diagonal 416 x 4224 matrix (512 diagonals, bs 32, 16 giant
-groups) on ciphertexts at LogN 16 with 24 limbs + 4 special primes
-(dnum 4), then the rescale and the 6 hybrid-fold rotations.  Inputs are
-seeded synthetic data with the reference's shapes (the Criteo dataset is
-not available), weights N(0, 0.05), queries Zipf(1.05).
+26-table block-diagonal 416 x 4224 matrix (512 diagonals; `--bsgs-ratio`,
+default 8: bs 64, 8 giant groups) on ciphertexts at LogN 16 with 24 limbs
++ 4 special primes (dnum 4), then the rescale and the 6 hybrid-fold
+rotations.  Inputs are seeded synthetic data with the reference's shapes
+(the Criteo dataset is not available), weights N(0, 0.05), queries
+Zipf(1.05).  On one GPU the line also carries the config-3 primitive
+microbenchmark, a compact config-4 forward (the whole bootstrapped HE-LRM
+network), the CPU baseline and a level-4 secondary.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python bench.py --mode tables        # the 26 tables sharded over the ranks
+    python bench.py --mode helrm         # config 4: the end-to-end forward
 
 Under torchrun each rank runs its own batch (query-batch data parallelism,
 keys and diagonals replicated, no data-path collective): weak scaling.
