@@ -152,6 +152,24 @@ def test_bootstrap_keeps_a_drifted_scale(pair):
     assert np.abs(_decrypt_c(pair, out) - vals).max() < 1e-5
 
 
+def test_bootstrap_batch_equals_single(pair):
+    """BootstrapBatch runs the circuit through the batched entry points
+    (folds, transforms, rescales, polynomials, products); each output must
+    equal Bootstrap of that input residue for residue, mixed sparse and
+    zero-padded inputs included."""
+    n = 16
+    rng = np.random.default_rng(21)
+    cts = []
+    for i in range(3):
+        z = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)) * 0.6
+        cts.append(_encrypt_sparse(pair, z, n, 0, padded=(i == 1)))
+    batch = pair.lib.BootstrapBatch(cts, n)
+    for c, b in zip(cts, batch):
+        one = pair.lib.Bootstrap(c, n)
+        assert np.array_equal(pair.ct_data(b), pair.ct_data(one))
+        assert pair.lib.GetCiphertextScale(b) == pair.lib.GetCiphertextScale(one)
+
+
 def test_message_ratio_is_checked(pair):
     n = 16
     pt = pair.lib.Encode(list(np.zeros(pair.slots)), 0, 2.0 ** 48)
