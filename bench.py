@@ -686,21 +686,6 @@ def run_b200_tables(args, dist):
     dist.barrier()
     t = dist.max(e0.elapsed_time(e1) / 1000.0)
     value = args.batch * args.steps / t
-    # ---- config 4 (the whole HE-LRM forward), compact: three warm-up steps
-    # (the first one checked against the cleartext), one timed step
-    # (bench.py --mode helrm for the full line with the kernel breakdown
-    # and e2e)
-    cfg4 = None
-    if dist.world == 1 and not args.small and not args.no_cfg4:
-        try:
-            cfg4 = helrm_measure(dist, args.batch, 1, 3, profile=False, e2e=False)
-            cfg4["config"] = helrm_config(args)
-            cfg4["note"] = ("config 4 end to end: HE-LRM inferences/s (the headline value above is the config-2 "
-                            "embedding PCMM, one query per ciphertext)")
-            correct = correct and cfg4["correct"]
-        except Exception as ex:  # the PCMM line must not be lost with it
-            cfg4 = {"value": None, "error": f"{type(ex).__name__}: {ex}"}
-
     if dist.rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
