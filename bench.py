@@ -571,7 +571,7 @@ def run_b200(args, dist):
             if r["op"] == "hoisted_keyswitch_R32" and r["batch"] == 16:
                 keyswitch = {"GBps": r["GBps"], "frac_hbm": r["frac_hbm"], "batch": 16, "rotations": 32,
                              "ms": r["ms"], "what": "whole hoisted key switch (ModUp + KeyMult + ModDown, NTTs "
-                                                    "included), SURVEY 8(d) algorithmic bytes"}
+                                                    "included), algorithmic bytes: each operand read or written once"}
 
     # ---- config 4 (the whole HE-LRM forward), compact: three warm-up steps
     # (the first one checked against the cleartext), one timed step

@@ -11,8 +11,8 @@ after warm-up, with inputs larger than L2.
     python -m helrm_b200.microbench [--batches 1,16,128] [--reps 5] [--ops ntt,ks]
 
 Prints one JSON line per (primitive, batch): milliseconds per launch,
-algorithmic GB/s (each operand read or written once, SURVEY's per-ciphertext
-byte counts) and its fraction of the measured HBM copy bandwidth.
+algorithmic GB/s (each operand read or written once per ciphertext) and
+its fraction of the measured HBM copy bandwidth.
 """
 from __future__ import annotations
 
@@ -149,8 +149,8 @@ def run(batches=(1, 16, 128), reps=5, ops="ntt,intt,aut,mac,rescale,ks", rotatio
                             _capi.check(capi.helrm_kernel_rotate_hoisted(ptr(xs), nq, nb, ks, R, ptr(outs), sp))
                     ms = timed(ks_batch)
                     ne = nq + K
-                    # SURVEY-style algorithmic bytes of ModUp + KeyMult + ModDown,
-                    # their NTTs included (each operand read or written once)
+                    # algorithmic bytes of ModUp + KeyMult + ModDown, their
+                    # NTTs included (each operand read or written once)
                     modup = nq * limb + beta * ne * limb
                     per_rot = beta * ne * limb + 2 * ne * limb + (2 * ne + 2 * nq) * limb + nq * limb
                     evk = 2 * beta * ne * limb * R * ((B + sub - 1) // sub)
