@@ -2330,7 +2330,9 @@ void bsgs_baby_mac(u64 *inner, const u64 *ct, const u64 *D, const BsgsChunk &ch,
     const bool pair = split && full && ch.gcount <= HB_GCH / 2 && nbatch > 1;
     // full chunks of 2 to 7 digits over mixed rows (primes on both sides of
     // 2^40, e.g. a 50-bit q0 or 60-bit bootstrapping primes): the fixed-shape
-    // kernel with the product form chosen per row
+    // kernel with the product form chosen per row.  Not one digit: the
+    // fixed shape runs the identity baby as a rotated one whose key tile
+    // holds P at digit 0 (for c0) and digit 1 (for c1)
     const bool fixed_mixed = !split && full && beta >= 2 && beta <= 7;
     const size_t smem = bsgs_smem_words(beta, pair ? 2 : 1, (split && full) || fixed_mixed) * 8;
     if (smem > 227 * 1024 || beta > HB_MAX_BETA)
