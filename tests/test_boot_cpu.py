@@ -64,6 +64,22 @@ def test_arcsine_only_below_ratio_2_10():
     assert BT.boot_prime_bits(36, 45) == [60] * 14
 
 
+@pytest.mark.parametrize("logq0", [50, 44])
+def test_level_plan_spends_exactly_the_reserved_primes(logq0):
+    """CtS, the cosine, the double angles, the arcsine when taken and StC
+    use every reserved prime once: StC's output sits at the top of the
+    usable chain, and each double angle keeps the cosine's scale when it
+    squares at a prime of that size."""
+    usable_top, logscale = 23, 36
+    nboot = BT.boot_levels(logq0, logscale)
+    q = [2.0 ** 50] + [2.0 ** 36] * usable_top + [2.0 ** 60] * nboot
+    top = len(q) - 1
+    plan = BT.level_plan(q, top, BT.uses_arcsin(logq0, logscale))
+    assert plan["lvl_stc"] - 1 == usable_top
+    assert plan["s_u"] == q[top - 1] and plan["s_cos"] == q[top - 7]
+    assert plan["s_dbl"] == plan["s_cos"] and plan["s_evalmod"] == q[plan["lvl_stc"]]
+
+
 @pytest.mark.parametrize("padded,asin", [(False, False), (True, False), (False, True)])
 def test_oracle_bootstrap_precision(request, padded, asin):
     from oracle import boot as OB
